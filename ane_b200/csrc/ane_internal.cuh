@@ -1,0 +1,113 @@
+// ane_internal.cuh -- shared host/device helpers of libane_b200 (not installed).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <string>
+
+#include "../../include/ane_b200.h"
+
+namespace ane_b200 {
+
+// ------------------------------------------------------------- status plumbing
+// Thread-local last status + message (stream_exec returns void, like the reference).
+void set_status(int code, const std::string& msg);
+int ok();  // records ANE_OK and returns it
+
+// Every kernel launch goes through this counter so tests and bench can prove
+// that the CUDA path (not some fallback) ran.
+extern std::atomic<uint64_t> g_launches;
+inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+#define ANE_CUDA_TRY(expr)                                                              \
+    do {                                                                                \
+        cudaError_t _e = (expr);                                                        \
+        if (_e != cudaSuccess) {                                                        \
+            ::ane_b200::set_status(ANE_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
+            return ANE_ERR_CUDA;                                                        \
+        }                                                                               \
+    } while (0)
+
+#define ANE_CHECK_LAUNCH()                                                              \
+    do {                                                                                \
+        cudaError_t _e = cudaGetLastError();                                            \
+        ::ane_b200::count_launch();                                                     \
+        if (_e != cudaSuccess) {                                                        \
+            ::ane_b200::set_status(ANE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(_e)); \
+            return ANE_ERR_CUDA;                                                        \
+        }                                                                               \
+    } while (0)
+
+#define ANE_ARG_CHECK(cond, msg)                                                        \
+    do {                                                                                \
+        if (!(cond)) {                                                                  \
+            ::ane_b200::set_status(ANE_ERR_INVALID_ARGUMENT, msg);                      \
+            return ANE_ERR_INVALID_ARGUMENT;                                            \
+        }                                                                               \
+    } while (0)
+
+// Device properties of the current device (cached per device).
+int num_sms();
+// Verifies that the current device is sm_100 (the only target of this library).
+int require_sm100();
+
+// Device-side bounded-wait failure counter (incremented by kernels that give up).
+int read_and_reset_device_timeouts(cudaStream_t s);
+int* device_timeout_flag();  // device address of the counter
+
+// ------------------------------------------------------- small math helpers
+__host__ __device__ inline size_t ceil_div(size_t a, size_t b) { return (a + b - 1) / b; }
+__host__ __device__ inline size_t round_up(size_t a, size_t b) { return ceil_div(a, b) * b; }
+
+// ARM FMAX semantics (the reference's relu / -FLT_MAX floor): a NaN operand
+// yields NaN, max(-0, +0) = +0.
+__device__ __forceinline__ float arm_fmax(float y, float floor_v) {
+    if (y != y) return y;
+    if (y == floor_v) return (__float_as_uint(y) >> 31) ? floor_v : y;
+    return y > floor_v ? y : floor_v;
+}
+
+// ------------------------------------------------------------ kernel launchers
+// (definitions in the .cu files; all asynchronous on `s`)
+int launch_absmax_partials(const float* a, size_t na, const float* b, size_t nb, float* partials,
+                           int blocks_a, int blocks_b, cudaStream_t s);
+int absmax_blocks_for(size_t n);
+int launch_reduce_partials(const float* partials, int pblocks_a, int pblocks_b, float* absmax2, cudaStream_t s);
+int launch_quantize_pair(uint32_t M, uint32_t N, uint32_t K, uint32_t K16, const float* A,
+                         const float* B, int8_t* Aq, int8_t* Bt, float* scales, const float* partials,
+                         int blocks_a, int blocks_b, cudaStream_t s);
+int launch_quantize_flat(size_t count, const float* src, int8_t* dst, float* scale_out,
+                         float* partials, int blocks, cudaStream_t s);
+int launch_quantize_channelwise(uint32_t rows, uint32_t cols, const float* src, int8_t* dst,
+                                float* scales, cudaStream_t s);
+int launch_dequantize(size_t count, float scale, const int8_t* src, float* dst, cudaStream_t s);
+int launch_pack_b(uint32_t K, uint32_t N, const int8_t* src, int8_t* dst, cudaStream_t s);
+int launch_unpack_b_to_kmajor(uint32_t K64, uint32_t N, const int8_t* Bp, int8_t* Bt,
+                              cudaStream_t s);
+
+// GEMM epilogue selector.
+enum GemmOut : int {
+    kOutFusedF32 = 0,  // y = float(acc)*(sa*sb); y = y*scale; relu ? fmax(y,0) : y
+    kOutRawI32 = 1,    // int32 accumulators
+    kOutDenseI8 = 2,   // y = float(acc)*(sa*sb); y = y + bias[n]; fmax(y, relu ? 0 : -FLT_MAX)
+};
+struct GemmEpilogue {
+    int mode;
+    const float* scales;  // device float[2] (sa, sb) or NULL -> sa_imm, sb_imm
+    float sa_imm, sb_imm;
+    float scale;          // fused mode multiplier
+    int relu;
+    const float* bias;    // dense_i8 mode, device pointer (>= N floats)
+};
+// C[M x ldc] += epilogue(Aq[M x K] * Bt[N x K]^T); K multiple of 16, both K-major
+// with row stride K.
+int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const int8_t* Bt,
+                      void* C, size_t ldc, const GemmEpilogue& ep, cudaStream_t s);
+int launch_fill_epilogue_zero_k(uint32_t M, uint32_t N, void* C, size_t ldc, const GemmEpilogue& ep,
+                                cudaStream_t s);
+
+int launch_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out,
+                     cudaStream_t s);
+
+}  // namespace ane_b200

@@ -1,0 +1,489 @@
+// capi.cu -- C-ABI entry points of libane_b200: status plumbing, per-thread
+// streams, host-pointer staging, and the device (`*_dev`) operations.
+//
+// The reference's calling contract (include/ane/ane.hpp:206-220, dispatch ->
+// stream_exec) is synchronous on caller-owned host memory and reentrant across
+// threads (tests/test_mnist_i8.cpp:437-449 runs Hogwild workers).  Here every
+// calling thread gets its own CUDA stream and its own device staging arena, so
+// concurrent callers never share mutable state; device-resident buffers are
+// used in place (zero copy), host buffers are copied in and out.
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "ane_internal.cuh"
+
+namespace ane_b200 {
+
+std::atomic<uint64_t> g_launches{0};
+
+namespace {
+thread_local int t_status = ANE_OK;
+thread_local std::string t_msg;
+
+constexpr int kMaxDevices = 64;
+struct DeviceInfo {
+    std::once_flag once;
+    int sms = 0;
+    int major = 0;
+    int* timeout_flag = nullptr;
+};
+DeviceInfo g_dev[kMaxDevices];
+
+DeviceInfo& device_info() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDevices) dev = 0;
+    DeviceInfo& d = g_dev[dev];
+    std::call_once(d.once, [&d, dev] {
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, dev) == cudaSuccess) {
+            d.sms = prop.multiProcessorCount;
+            d.major = prop.major;
+        }
+        if (cudaMalloc(&d.timeout_flag, sizeof(int)) == cudaSuccess) cudaMemset(d.timeout_flag, 0, sizeof(int));
+    });
+    return d;
+}
+
+// Per-thread execution context for the synchronous, host-facing entry points.
+struct ThreadCtx {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    void* arena = nullptr;
+    size_t arena_bytes = 0;
+    void* ws = nullptr;  // default workspace for *_dev calls given workspace == NULL
+    size_t ws_bytes = 0;
+};
+thread_local ThreadCtx t_ctx;
+
+int ensure_thread_ctx() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        set_status(ANE_ERR_NO_DEVICE, "no CUDA device");
+        return ANE_ERR_NO_DEVICE;
+    }
+    if (t_ctx.device != dev) {
+        // a thread that switched devices gets fresh per-device resources
+        t_ctx = ThreadCtx();
+        t_ctx.device = dev;
+        ANE_CUDA_TRY(cudaStreamCreateWithFlags(&t_ctx.stream, cudaStreamNonBlocking));
+    }
+    return ANE_OK;
+}
+
+int ensure_buffer(void** buf, size_t* have, size_t need) {
+    if (*have >= need) return ANE_OK;
+    if (*buf) {
+        cudaFree(*buf);  // synchronises the device; the arena is idle between calls anyway
+        *buf = nullptr;
+        *have = 0;
+    }
+    size_t sz = need < ((size_t)1 << 20) ? ((size_t)1 << 20) : need + need / 4;
+    if (cudaMalloc(buf, sz) != cudaSuccess) {
+        cudaGetLastError();
+        set_status(ANE_ERR_OUT_OF_MEMORY, "cudaMalloc of " + std::to_string(sz) + " bytes failed");
+        return ANE_ERR_OUT_OF_MEMORY;
+    }
+    *have = sz;
+    return ANE_OK;
+}
+
+bool device_accessible(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// One caller buffer of a host-facing call.
+struct Arg {
+    const void* user;
+    size_t bytes;
+    bool in, out;
+    void* dev = nullptr;
+    bool staged = false;
+};
+
+// Resolves every argument to a device address (staging host memory through the
+// thread's arena), runs `body` on the thread stream, copies outputs back, syncs.
+template <class Body>
+int run_staged(std::vector<Arg>& args, size_t extra_bytes, Body body) {
+    int rc = ensure_thread_ctx();
+    if (rc) return rc;
+    size_t need = extra_bytes;
+    for (auto& a : args) {
+        if (a.bytes == 0 || a.user == nullptr) continue;
+        if (device_accessible(a.user)) {
+            a.dev = const_cast<void*>(a.user);
+        } else {
+            a.staged = true;
+            need += round_up(a.bytes, 256);
+        }
+    }
+    rc = ensure_buffer(&t_ctx.arena, &t_ctx.arena_bytes, need);
+    if (rc) return rc;
+    uint8_t* cur = static_cast<uint8_t*>(t_ctx.arena);
+    void* extra = cur;
+    cur += round_up(extra_bytes, 256);
+    cudaStream_t s = t_ctx.stream;
+    for (auto& a : args) {
+        if (!a.staged) continue;
+        a.dev = cur;
+        cur += round_up(a.bytes, 256);
+        if (a.in) ANE_CUDA_TRY(cudaMemcpyAsync(a.dev, a.user, a.bytes, cudaMemcpyHostToDevice, s));
+    }
+    rc = body(s, extra);
+    if (rc) {
+        cudaStreamSynchronize(s);
+        return rc;
+    }
+    for (auto& a : args)
+        if (a.staged && a.out) ANE_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(a.user), a.dev, a.bytes,
+                                                            cudaMemcpyDeviceToHost, s));
+    ANE_CUDA_TRY(cudaStreamSynchronize(s));
+    int timeouts = read_and_reset_device_timeouts(s);
+    if (timeouts) {
+        set_status(ANE_ERR_DEVICE_TIMEOUT, "a device-side bounded wait timed out");
+        return ANE_ERR_DEVICE_TIMEOUT;
+    }
+    return ok();
+}
+
+inline size_t a256(size_t n) { return round_up(n, 256); }
+
+struct FusedWs {
+    int8_t* Aq;
+    int8_t* Bt;
+    float* scales;
+    float* partials;
+};
+size_t fused_ws_layout(uint32_t M, uint32_t N, uint32_t K, FusedWs* w, void* base) {
+    const size_t K16 = round_up(K, 16);
+    const size_t pcount = ane_absmax_partials_count((size_t)M * K, (size_t)K * N);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += a256(bytes);
+        return o;
+    };
+    size_t oa = take((size_t)M * K16), ob = take((size_t)N * K16), os = take(2 * sizeof(float)),
+           op = take(pcount * sizeof(float));
+    if (w && base) {
+        uint8_t* b = static_cast<uint8_t*>(base);
+        w->Aq = reinterpret_cast<int8_t*>(b + oa);
+        w->Bt = reinterpret_cast<int8_t*>(b + ob);
+        w->scales = reinterpret_cast<float*>(b + os);
+        w->partials = reinterpret_cast<float*>(b + op);
+    }
+    return off;
+}
+
+int dense_fused_on_stream(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t relu, const float* A,
+                          const float* B, float* C, void* ws, cudaStream_t s) {
+    FusedWs w{};
+    fused_ws_layout(M, N, K, &w, ws);
+    const uint32_t K16 = (uint32_t)round_up(K, 16);
+    const size_t na = (size_t)M * K, nb = (size_t)K * N;
+    const int pa = absmax_blocks_for(na), pb = absmax_blocks_for(nb);
+    int rc = launch_absmax_partials(A, na, B, nb, w.partials, pa, pb, s);
+    if (rc) return rc;
+    rc = launch_quantize_pair(M, N, K, K16, A, B, w.Aq, w.Bt, w.scales, w.partials, pa, pb, s);
+    if (rc) return rc;
+    GemmEpilogue ep{kOutFusedF32, w.scales, 0.f, 0.f, scale, relu ? 1 : 0, nullptr};
+    return launch_gemm_s8_tc(M, N, K16, w.Aq, w.Bt, C, N, ep, s);
+}
+
+}  // namespace
+
+// --------------------------------------------------------------- status API
+void set_status(int code, const std::string& msg) {
+    t_status = code;
+    t_msg = msg;
+    if (code != ANE_OK && getenv("ANE_ABORT_ON_ERROR")) {
+        fprintf(stderr, "libane_b200: %s\n", msg.c_str());
+        abort();
+    }
+}
+int ok() {
+    t_status = ANE_OK;
+    t_msg.clear();
+    return ANE_OK;
+}
+int num_sms() {
+    int s = device_info().sms;
+    return s > 0 ? s : 148;
+}
+int require_sm100() {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        set_status(ANE_ERR_NO_DEVICE, "no CUDA device visible");
+        return ANE_ERR_NO_DEVICE;
+    }
+    if (device_info().major != 10) {
+        set_status(ANE_ERR_NO_DEVICE, "libane_b200 needs an sm_100 (B200) device");
+        return ANE_ERR_NO_DEVICE;
+    }
+    return ANE_OK;
+}
+int* device_timeout_flag() { return device_info().timeout_flag; }
+int read_and_reset_device_timeouts(cudaStream_t s) {
+    int* f = device_timeout_flag();
+    if (!f) return 0;
+    int v = 0;
+    if (cudaMemcpyAsync(&v, f, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return 0;
+    cudaStreamSynchronize(s);
+    if (v) cudaMemsetAsync(f, 0, sizeof(int), s);
+    return v;
+}
+
+}  // namespace ane_b200
+
+using namespace ane_b200;
+
+#define ANE_REQUIRE_GPU()                 \
+    do {                                  \
+        int _rc = require_sm100();        \
+        if (_rc) return _rc;              \
+    } while (0)
+
+extern "C" {
+
+int ane_last_error(void) { return t_status; }
+const char* ane_last_error_string(void) { return t_msg.c_str(); }
+void ane_clear_error(void) { ok(); }
+const char* ane_version(void) { return "ane_b200 0.1 (sm_100a)"; }
+uint64_t ane_kernel_launch_count(void) { return g_launches.load(); }
+int ane_device_timeouts(void) {
+    if (require_sm100()) return 0;
+    return read_and_reset_device_timeouts(nullptr);
+}
+
+size_t ane_absmax_partials_count(size_t count_a, size_t count_b) {
+    // absmax_blocks_for() never returns more than 1024 blocks per tensor
+    (void)count_a;
+    (void)count_b;
+    return 2 * 1024;
+}
+
+size_t ane_dense_fused_i8_workspace_size(uint32_t M, uint32_t N, uint32_t K) {
+    return fused_ws_layout(M, N, K, nullptr, nullptr);
+}
+
+// ------------------------------------------------------------- device ops
+int ane_dense_fused_i8_dev(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t relu, const float* A,
+                           const float* B, float* C, void* workspace, size_t workspace_bytes, void* stream) {
+    ANE_REQUIRE_GPU();
+    if (M == 0 || N == 0) return ok();
+    ANE_ARG_CHECK(A && B && C, "dense_fused_i8: NULL pointer");
+    const size_t need = ane_dense_fused_i8_workspace_size(M, N, K);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!workspace) {
+        int rc = ensure_thread_ctx();
+        if (rc) return rc;
+        if (t_ctx.ws_bytes < need) cudaStreamSynchronize(s);  // old workspace may be in use on s
+        rc = ensure_buffer(&t_ctx.ws, &t_ctx.ws_bytes, need);
+        if (rc) return rc;
+        workspace = t_ctx.ws;
+    } else {
+        ANE_ARG_CHECK(workspace_bytes >= need, "dense_fused_i8: workspace too small");
+        ANE_ARG_CHECK(((uintptr_t)workspace & 255) == 0, "dense_fused_i8: workspace must be 256-byte aligned");
+    }
+    int rc = dense_fused_on_stream(M, N, K, scale, relu, A, B, C, workspace, s);
+    return rc ? rc : ok();
+}
+
+int ane_quantize_pair_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
+                          int8_t* Bt, float* scales, float* partials, void* stream) {
+    ANE_REQUIRE_GPU();
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const uint32_t K16 = (uint32_t)round_up(K, 16);
+    const size_t na = (size_t)M * K, nb = (size_t)K * N;
+    const int pa = absmax_blocks_for(na), pb = absmax_blocks_for(nb);
+    int rc = launch_absmax_partials(A, na, B, nb, partials, pa, pb, s);
+    if (rc) return rc;
+    rc = launch_quantize_pair(M, N, K, K16, A, B, Aq, Bt, scales, partials, pa, pb, s);
+    return rc ? rc : ok();
+}
+
+int ane_absmax_pair_dev(const float* A, size_t count_a, const float* B, size_t count_b, float* absmax2,
+                        float* partials, void* stream) {
+    ANE_REQUIRE_GPU();
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int pa = absmax_blocks_for(count_a), pb = absmax_blocks_for(count_b);
+    int rc = launch_absmax_partials(A, count_a, B, count_b, partials, pa, pb, s);
+    if (rc) return rc;
+    rc = launch_reduce_partials(partials, pa, pb, absmax2, s);
+    return rc ? rc : ok();
+}
+
+int ane_quantize_pair_absmax_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
+                                 int8_t* Bt, const float* absmax2, float* scales, void* stream) {
+    ANE_REQUIRE_GPU();
+    // absmax2 stands in for a one-entry partials list per tensor
+    int rc = launch_quantize_pair(M, N, K, (uint32_t)round_up(K, 16), A, B, Aq, Bt, scales, absmax2, 1, 1,
+                                  static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+int ane_gemm_s8_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* Aq, const int8_t* Bt, const float* scales,
+                    float scale, uint8_t relu, int out_mode, void* C, void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(out_mode == 0 || out_mode == 1, "gemm_s8: out_mode must be 0 (fp32) or 1 (int32)");
+    GemmEpilogue ep{out_mode == 0 ? kOutFusedF32 : kOutRawI32, scales, 1.f, 1.f, scale, relu ? 1 : 0, nullptr};
+    int rc = launch_gemm_s8_tc(M, N, K16, Aq, Bt, C, N, ep, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+int ane_quantize_fp32_i8_dev(uint32_t count, const float* src, int8_t* dst, float* scale_out, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = ensure_thread_ctx();
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t need = ane_absmax_partials_count(count, 0) * sizeof(float);
+    if (t_ctx.ws_bytes < need) cudaStreamSynchronize(s);
+    rc = ensure_buffer(&t_ctx.ws, &t_ctx.ws_bytes, need);
+    if (rc) return rc;
+    rc = launch_quantize_flat(count, src, dst, scale_out, static_cast<float*>(t_ctx.ws), absmax_blocks_for(count), s);
+    return rc ? rc : ok();
+}
+
+int ane_pack_b_i8_dev(uint32_t K, uint32_t N, const int8_t* src, int8_t* dst, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = launch_pack_b(K, N, src, dst, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+int ane_dense_i8_dev(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags, const int8_t* A,
+                     const int8_t* B_packed, const float* bias, float* C, void* stream) {
+    ANE_REQUIRE_GPU();
+    if (M == 0 || N == 0) return ok();
+    const uint32_t M16 = (uint32_t)round_up(M, 16), K64 = (uint32_t)round_up(K, 64);
+    int rc = ensure_thread_ctx();
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t need = (size_t)N * K64;
+    if (t_ctx.ws_bytes < need) cudaStreamSynchronize(s);
+    rc = ensure_buffer(&t_ctx.ws, &t_ctx.ws_bytes, need > 0 ? need : 1);
+    if (rc) return rc;
+    int8_t* Bt = static_cast<int8_t*>(t_ctx.ws);
+    rc = launch_unpack_b_to_kmajor(K64, N, B_packed, Bt, s);
+    if (rc) return rc;
+    GemmEpilogue ep{kOutDenseI8, nullptr, sa, sb, 1.f, (flags & 1) ? 1 : 0, bias};
+    rc = launch_gemm_s8_tc(M16, N, K64, A, Bt, C, N, ep, s);
+    return rc ? rc : ok();
+}
+
+int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = launch_q8_0_gemv(M, K, in, static_cast<const uint8_t*>(W), out, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+// ------------------------------------------------- host-facing (synchronous)
+int ane_quantize_fp32_i8(uint32_t count, const float* src, int8_t* dst, float* scale_out) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(scale_out != nullptr, "quantize_fp32_i8: NULL scale_out");
+    ANE_ARG_CHECK(count == 0 || (src && dst), "quantize_fp32_i8: NULL pointer");
+    std::vector<Arg> args = {{src, (size_t)count * 4, true, false},
+                             {dst, (size_t)count, false, true},
+                             {scale_out, 4, false, true}};
+    const size_t pbytes = ane_absmax_partials_count(count, 0) * sizeof(float);
+    return run_staged(args, pbytes, [&](cudaStream_t s, void* extra) {
+        return launch_quantize_flat(count, (const float*)args[0].dev, (int8_t*)args[1].dev, (float*)args[2].dev,
+                                    (float*)extra, absmax_blocks_for(count), s);
+    });
+}
+
+int ane_dequantize_i8_fp32(uint32_t count, float scale, const int8_t* src, float* dst) {
+    ANE_REQUIRE_GPU();
+    if (count == 0) return ok();
+    ANE_ARG_CHECK(src && dst, "dequantize_i8_fp32: NULL pointer");
+    std::vector<Arg> args = {{src, (size_t)count, true, false}, {dst, (size_t)count * 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_dequantize(count, scale, (const int8_t*)args[0].dev, (float*)args[1].dev, s);
+    });
+}
+
+int ane_pack_b_i8(uint32_t K, uint32_t N, const int8_t* src, int8_t* dst) {
+    ANE_REQUIRE_GPU();
+    const size_t out_bytes = (size_t)((N + 15) / 16) * ((K + 3) / 4) * 64;
+    if (out_bytes == 0) return ok();
+    ANE_ARG_CHECK(dst && (src || (size_t)K * N == 0), "pack_b_i8: NULL pointer");
+    std::vector<Arg> args = {{src, (size_t)K * N, true, false}, {dst, out_bytes, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_pack_b(K, N, (const int8_t*)args[0].dev, (int8_t*)args[1].dev, s);
+    });
+}
+
+int ane_quantize_fp32_i8_channelwise(uint32_t rows, uint32_t cols, const float* src, int8_t* dst, float* scales) {
+    ANE_REQUIRE_GPU();
+    if (rows == 0) return ok();
+    ANE_ARG_CHECK(src && dst && scales, "quantize_fp32_i8_channelwise: NULL pointer");
+    std::vector<Arg> args = {{src, (size_t)rows * cols * 4, true, false},
+                             {dst, (size_t)rows * cols, false, true},
+                             {scales, (size_t)rows * 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_quantize_channelwise(rows, cols, (const float*)args[0].dev, (int8_t*)args[1].dev,
+                                           (float*)args[2].dev, s);
+    });
+}
+
+int ane_dense_i8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags, const int8_t* A,
+                 const int8_t* B_packed, const float* bias, float* C) {
+    ANE_REQUIRE_GPU();
+    if (M == 0 || N == 0) return ok();
+    ANE_ARG_CHECK(A && B_packed && bias && C, "dense_i8: NULL pointer");
+    const size_t M16 = round_up(M, 16), K64 = round_up(K, 64);
+    const size_t bp_bytes = ceil_div(N, 16) * (K64 / 4) * 64;
+    std::vector<Arg> args = {{A, M16 * K64, true, false},
+                             {B_packed, bp_bytes, true, false},
+                             {bias, (size_t)N * 4, true, false},
+                             {C, M16 * N * 4, false, true}};
+    const size_t bt_bytes = (size_t)N * K64;
+    return run_staged(args, bt_bytes, [&](cudaStream_t s, void* extra) {
+        int8_t* Bt = static_cast<int8_t*>(extra);
+        int rc = launch_unpack_b_to_kmajor((uint32_t)K64, N, (const int8_t*)args[1].dev, Bt, s);
+        if (rc) return rc;
+        GemmEpilogue ep{kOutDenseI8, nullptr, sa, sb, 1.f, (flags & 1) ? 1 : 0, (const float*)args[2].dev};
+        return launch_gemm_s8_tc((uint32_t)M16, N, (uint32_t)K64, (const int8_t*)args[0].dev, Bt, args[3].dev, N,
+                                 ep, s);
+    });
+}
+
+int ane_dense_fused_i8(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t relu, const float* A,
+                       const float* B, float* C) {
+    ANE_REQUIRE_GPU();
+    if (M == 0 || N == 0) return ok();
+    ANE_ARG_CHECK(C && (K == 0 || (A && B)), "dense_fused_i8: NULL pointer");
+    std::vector<Arg> args = {{A, (size_t)M * K * 4, true, false},
+                             {B, (size_t)K * N * 4, true, false},
+                             {C, (size_t)M * N * 4, false, true}};
+    const size_t ws = ane_dense_fused_i8_workspace_size(M, N, K);
+    return run_staged(args, ws, [&](cudaStream_t s, void* extra) {
+        return dense_fused_on_stream(M, N, K, scale, relu, (const float*)args[0].dev, (const float*)args[1].dev,
+                                     (float*)args[2].dev, extra, s);
+    });
+}
+
+int ane_q8_0_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out) {
+    ANE_REQUIRE_GPU();
+    if (M == 0) return ok();
+    ANE_ARG_CHECK(K % 32 == 0, "q8_0_gemv: K must be a multiple of 32");
+    ANE_ARG_CHECK(in && W && out, "q8_0_gemv: NULL pointer");
+    std::vector<Arg> args = {{in, (size_t)K * 4, true, false},
+                             {W, (size_t)M * (K / 32) * 34, true, false},
+                             {out, (size_t)M * 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_q8_0_gemv(M, K, (const float*)args[0].dev, (const uint8_t*)args[1].dev, (float*)args[2].dev, s);
+    });
+}
+
+}  // extern "C"

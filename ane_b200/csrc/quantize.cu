@@ -1,0 +1,322 @@
+// quantize.cu -- per-tensor absmax int8 quantization kernels (HBM-bound).
+//
+// Semantics follow the reference handler quantize_fp32_i8
+// (src/bytecode_interpreter.s:1876-1950), bit for bit:
+//   absmax = max|x| (NaN propagates); absmax == 0 -> scale 1, inv 127;
+//   else scale = absmax/127, inv = 127/absmax (IEEE RN divisions);
+//   q = rint_even(min(max(x*inv, -127), 127)), NaN -> 0.
+// The reduction is a two-kernel scheme with no atomics and no zero-init:
+// kernel 1 writes one partial max per block, kernel 2 re-reduces the partials
+// (a few hundred floats, L2-resident) in every block before quantizing.
+#include <float.h>
+
+#include "ane_internal.cuh"
+
+namespace ane_b200 {
+
+static constexpr int kThreads = 256;
+
+// ------------------------------------------------------------------ helpers
+__device__ __forceinline__ uint32_t absbits(float v) { return __float_as_uint(v) & 0x7fffffffu; }
+
+// Max of |x| as an unsigned compare of the magnitude bits: NaN > inf > finite,
+// so a NaN anywhere wins, exactly like the reference's propagating fmax.
+__device__ __forceinline__ uint32_t block_max_u32(uint32_t v) {
+    __shared__ uint32_t red[kThreads / 32];
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    v = l < (int)(blockDim.x >> 5) ? red[l] : 0u;
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;  // valid in every warp
+}
+
+__device__ __forceinline__ void scale_from_absmax(float absmax, float* scale, float* inv) {
+    if (absmax == 0.0f) {
+        *scale = 1.0f;
+        *inv = 127.0f;
+    } else {  // NaN is unordered and takes this path, as fcmp/b.eq does
+        *scale = __fdiv_rn(absmax, 127.0f);
+        *inv = __fdiv_rn(127.0f, absmax);
+    }
+}
+
+__device__ __forceinline__ int8_t quantize_one(float x, float inv) {
+    float y = __fmul_rn(x, inv);
+    if (y != y) return 0;  // fmax/fmin keep NaN, fcvtzs(NaN) = 0
+    y = fminf(fmaxf(y, -127.0f), 127.0f);
+    return (int8_t)__float2int_rn(y);  // frintn (ties to even) + fcvtzs
+}
+
+__device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d, float inv) {
+    uint32_t r = (uint32_t)(uint8_t)quantize_one(a, inv);
+    r |= (uint32_t)(uint8_t)quantize_one(b, inv) << 8;
+    r |= (uint32_t)(uint8_t)quantize_one(c, inv) << 16;
+    r |= (uint32_t)(uint8_t)quantize_one(d, inv) << 24;
+    return r;
+}
+
+// ------------------------------------------------------- absmax partials
+// Blocks [0, blocks_a) reduce a[0..na), blocks [blocks_a, +blocks_b) reduce b.
+__global__ void __launch_bounds__(kThreads) absmax_partials_kernel(const float* __restrict__ a, size_t na,
+                                                                   const float* __restrict__ b, size_t nb,
+                                                                   float* __restrict__ partials,
+                                                                   int blocks_a) {
+    const bool seg_b = (int)blockIdx.x >= blocks_a;
+    const float* x = seg_b ? b : a;
+    const size_t n = seg_b ? nb : na;
+    const int nblk = seg_b ? (int)gridDim.x - blocks_a : blocks_a;
+    const int bid = seg_b ? (int)blockIdx.x - blocks_a : (int)blockIdx.x;
+    uint32_t m = 0;
+    const size_t tid = (size_t)bid * kThreads + threadIdx.x;
+    const size_t stride = (size_t)nblk * kThreads;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        const size_t n4 = n / 4;
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        size_t i = tid;
+        // two independent loads in flight per iteration
+        for (; i + stride < n4; i += 2 * stride) {
+            float4 v = __ldcs(x4 + i);
+            float4 u = __ldcs(x4 + i + stride);
+            m = max(m, max(max(absbits(v.x), absbits(v.y)), max(absbits(v.z), absbits(v.w))));
+            m = max(m, max(max(absbits(u.x), absbits(u.y)), max(absbits(u.z), absbits(u.w))));
+        }
+        for (; i < n4; i += stride) {
+            float4 v = __ldcs(x4 + i);
+            m = max(m, max(max(absbits(v.x), absbits(v.y)), max(absbits(v.z), absbits(v.w))));
+        }
+        for (size_t j = n4 * 4 + tid; j < n; j += stride) m = max(m, absbits(x[j]));
+    } else {
+        for (size_t j = tid; j < n; j += stride) m = max(m, absbits(x[j]));
+    }
+    m = block_max_u32(m);
+    if (threadIdx.x == 0) partials[blockIdx.x] = __uint_as_float(m);
+}
+
+__device__ __forceinline__ float reduce_partials(const float* __restrict__ p, int n) {
+    uint32_t m = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) m = max(m, __float_as_uint(p[i]));
+    return __uint_as_float(block_max_u32(m));
+}
+
+// ---------------------------------------------------- row-major quantize
+// dst[r*ld + k] = q(src[r*K + k]) for k < K, 0 for K <= k < ld.
+__device__ void quantize_rows(const float* __restrict__ src, int8_t* __restrict__ dst, uint32_t rows,
+                              uint32_t K, uint32_t ld, float inv, int bid, int nblk) {
+    const size_t tid = (size_t)bid * blockDim.x + threadIdx.x;
+    const size_t stride = (size_t)nblk * blockDim.x;
+    const bool vec = (K % 16 == 0) && (ld == K) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+    if (vec) {
+        const size_t chunks = (size_t)rows * K / 16;
+        const float4* s4 = reinterpret_cast<const float4*>(src);
+        uint4* d16 = reinterpret_cast<uint4*>(dst);
+        for (size_t c = tid; c < chunks; c += stride) {
+            float4 v0 = __ldcs(s4 + 4 * c + 0), v1 = __ldcs(s4 + 4 * c + 1);
+            float4 v2 = __ldcs(s4 + 4 * c + 2), v3 = __ldcs(s4 + 4 * c + 3);
+            uint4 o;
+            o.x = pack4(v0.x, v0.y, v0.z, v0.w, inv);
+            o.y = pack4(v1.x, v1.y, v1.z, v1.w, inv);
+            o.z = pack4(v2.x, v2.y, v2.z, v2.w, inv);
+            o.w = pack4(v3.x, v3.y, v3.z, v3.w, inv);
+            d16[c] = o;
+        }
+    } else {
+        const size_t total = (size_t)rows * ld;
+        for (size_t i = tid; i < total; i += stride) {
+            size_t r = i / ld, k = i % ld;
+            dst[i] = k < K ? quantize_one(src[r * K + k], inv) : (int8_t)0;
+        }
+    }
+}
+
+// ------------------------------------------------ transposing quantize of B
+// B is K x N fp32 row-major; Bt is N x ld int8 (ld = K16), Bt[n][k] = q(B[k][n]),
+// zero for K <= k < ld.  64x64 tiles through shared memory: coalesced 128-B
+// fp32 reads along n, 16-B int8 writes along k.
+static constexpr int kTT = 64;
+static constexpr int kTPitch = kTT + 4;  // bytes; 17 words -> conflict-free column writes
+
+__device__ void quantize_transpose(const float* __restrict__ B, int8_t* __restrict__ Bt, uint32_t K,
+                                   uint32_t N, uint32_t ld, float inv, int bid, int nblk) {
+    __shared__ __align__(16) uint8_t tile[kTT * kTPitch];
+    const uint32_t tiles_k = (ld + kTT - 1) / kTT, tiles_n = (N + kTT - 1) / kTT;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (uint32_t t = bid; t < tiles_k * tiles_n; t += nblk) {
+        const uint32_t k0 = (t / tiles_n) * kTT, n0 = (t % tiles_n) * kTT;
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < kTT / 8; i++) {
+            const uint32_t kl = warp + 8 * i, k = k0 + kl;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t nl = lane + 32 * h, n = n0 + nl;
+                int8_t q = 0;
+                if (k < K && n < N) q = quantize_one(__ldcs(B + (size_t)k * N + n), inv);
+                tile[nl * kTPitch + kl] = (uint8_t)q;
+            }
+        }
+        __syncthreads();
+        const uint32_t nl = threadIdx.x >> 2, kc = (threadIdx.x & 3) * 16;
+        const uint32_t n = n0 + nl, k = k0 + kc;
+        if (n < N && k < ld) {
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(tile + nl * kTPitch + kc);
+            uint4 o = make_uint4(src[0], src[1], src[2], src[3]);
+            if (k + 16 <= ld) {
+                *reinterpret_cast<uint4*>(Bt + (size_t)n * ld + k) = o;
+            } else {  // ld is a multiple of 16, so this only guards odd callers
+                const uint8_t* ob = reinterpret_cast<const uint8_t*>(&o);
+                for (uint32_t j = 0; k + j < ld; j++) Bt[(size_t)n * ld + k + j] = (int8_t)ob[j];
+            }
+        }
+    }
+}
+
+// Quantize A (row-major -> Aq, row stride ld) and B (-> Bt transposed, row stride
+// ld) in one launch: blocks [0, blocks_a) take A, the rest take B.
+__global__ void __launch_bounds__(kThreads) quantize_pair_kernel(
+    const float* __restrict__ A, const float* __restrict__ B, int8_t* __restrict__ Aq,
+    int8_t* __restrict__ Bt, float* __restrict__ scales, const float* __restrict__ partials,
+    uint32_t M, uint32_t N, uint32_t K, uint32_t ld, int pblocks_a, int pblocks_b, int blocks_a) {
+    const bool seg_b = (int)blockIdx.x >= blocks_a;
+    const float absmax = seg_b ? reduce_partials(partials + pblocks_a, pblocks_b)
+                               : reduce_partials(partials, pblocks_a);
+    float scale, inv;
+    scale_from_absmax(absmax, &scale, &inv);
+    const int bid = seg_b ? (int)blockIdx.x - blocks_a : (int)blockIdx.x;
+    const int nblk = seg_b ? (int)gridDim.x - blocks_a : blocks_a;
+    if (bid == 0 && threadIdx.x == 0) scales[seg_b ? 1 : 0] = scale;
+    if (!seg_b)
+        quantize_rows(A, Aq, M, K, ld, inv, bid, nblk);
+    else
+        quantize_transpose(B, Bt, K, N, ld, inv, bid, nblk);
+}
+
+// Flat quantize of one tensor (opcode 0x19).
+__global__ void __launch_bounds__(kThreads) quantize_flat_kernel(const float* __restrict__ src,
+                                                                 int8_t* __restrict__ dst, size_t count,
+                                                                 float* __restrict__ scale_out,
+                                                                 const float* __restrict__ partials,
+                                                                 int pblocks) {
+    const float absmax = reduce_partials(partials, pblocks);
+    float scale, inv;
+    scale_from_absmax(absmax, &scale, &inv);
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
+    // treat as rows of 16 when possible so the vector path applies
+    if (count % 16 == 0)
+        quantize_rows(src, dst, (uint32_t)(count / 16), 16, 16, inv, blockIdx.x, gridDim.x);
+    else {
+        const size_t stride = (size_t)gridDim.x * blockDim.x;
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride)
+            dst[i] = quantize_one(src[i], inv);
+    }
+}
+
+// Per-row quantize (opcode 0x1C): one block per row.
+__global__ void __launch_bounds__(kThreads) quantize_channelwise_kernel(const float* __restrict__ src,
+                                                                        int8_t* __restrict__ dst,
+                                                                        float* __restrict__ scales,
+                                                                        uint32_t rows, uint32_t cols) {
+    for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float* x = src + (size_t)r * cols;
+        uint32_t m = 0;
+        for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) m = max(m, absbits(x[i]));
+        float scale, inv;
+        scale_from_absmax(__uint_as_float(block_max_u32(m)), &scale, &inv);
+        if (threadIdx.x == 0) scales[r] = scale;
+        for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) dst[(size_t)r * cols + i] = quantize_one(x[i], inv);
+    }
+}
+
+// Opcode 0x1A: out = float(q) * scale (scvtf then fmul).
+__global__ void dequantize_kernel(const int8_t* __restrict__ src, float* __restrict__ dst, size_t count,
+                                  float scale) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride)
+        dst[i] = __fmul_rn(__int2float_rn(src[i]), scale);
+}
+
+// Final reduction of the partials of two tensors into absmax2[0..1] (one block each).
+__global__ void __launch_bounds__(kThreads) reduce_partials_kernel(const float* __restrict__ partials,
+                                                                   int pblocks_a, int pblocks_b,
+                                                                   float* __restrict__ absmax2) {
+    const float m = blockIdx.x == 0 ? reduce_partials(partials, pblocks_a)
+                                    : reduce_partials(partials + pblocks_a, pblocks_b);
+    if (threadIdx.x == 0) absmax2[blockIdx.x] = m;
+}
+
+// ------------------------------------------------------------------ launchers
+int launch_reduce_partials(const float* partials, int pblocks_a, int pblocks_b, float* absmax2, cudaStream_t s) {
+    reduce_partials_kernel<<<2, kThreads, 0, s>>>(partials, pblocks_a, pblocks_b, absmax2);
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
+
+int absmax_blocks_for(size_t n) {
+    size_t want = ceil_div(n, (size_t)kThreads * 32);  // >= 32 elements per thread
+    size_t cap = (size_t)num_sms() * 4;
+    if (cap > 1024) cap = 1024;  // ane_absmax_partials_count() reserves 2 x 1024 slots
+    if (want < 1) want = 1;
+    return (int)(want < cap ? want : cap);
+}
+
+int launch_absmax_partials(const float* a, size_t na, const float* b, size_t nb, float* partials,
+                           int blocks_a, int blocks_b, cudaStream_t s) {
+    absmax_partials_kernel<<<blocks_a + blocks_b, kThreads, 0, s>>>(a, na, b, nb, partials, blocks_a);
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
+
+int launch_quantize_pair(uint32_t M, uint32_t N, uint32_t K, uint32_t K16, const float* A,
+                         const float* B, int8_t* Aq, int8_t* Bt, float* scales, const float* partials,
+                         int pblocks_a, int pblocks_b, cudaStream_t s) {
+    const size_t work_a = (size_t)M * K16, work_b = (size_t)N * K16;
+    const int sms = num_sms();
+    // split ~4 waves of blocks between the two tensors in proportion to their size
+    int total = sms * 4;
+    int ba = (int)((double)total * (double)work_a / (double)(work_a + work_b + 1));
+    if (ba < 1) ba = 1;
+    int bb = total - ba;
+    if (bb < 1) bb = 1;
+    size_t tiles_b = ceil_div(K16, kTT) * ceil_div(N, kTT);
+    if ((size_t)bb > tiles_b) bb = (int)tiles_b;
+    if (bb < 1) bb = 1;
+    quantize_pair_kernel<<<ba + bb, kThreads, 0, s>>>(A, B, Aq, Bt, scales, partials, M, N, K, K16,
+                                                      pblocks_a, pblocks_b, ba);
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
+
+int launch_quantize_flat(size_t count, const float* src, int8_t* dst, float* scale_out, float* partials,
+                         int blocks, cudaStream_t s) {
+    int rc = launch_absmax_partials(src, count, nullptr, 0, partials, blocks, 0, s);
+    if (rc) return rc;
+    int qb = (int)ceil_div(count, (size_t)kThreads * 16);
+    if (qb > num_sms() * 4) qb = num_sms() * 4;
+    if (qb < 1) qb = 1;
+    quantize_flat_kernel<<<qb, kThreads, 0, s>>>(src, dst, count, scale_out, partials, blocks);
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
+
+int launch_quantize_channelwise(uint32_t rows, uint32_t cols, const float* src, int8_t* dst,
+                                float* scales, cudaStream_t s) {
+    int g = (int)(rows < 65535u ? rows : 65535u);
+    if (g < 1) return ANE_OK;
+    quantize_channelwise_kernel<<<g, kThreads, 0, s>>>(src, dst, scales, rows, cols);
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
+
+int launch_dequantize(size_t count, float scale, const int8_t* src, float* dst, cudaStream_t s) {
+    if (count == 0) return ANE_OK;
+    int g = (int)ceil_div(count, (size_t)kThreads * 8);
+    if (g > num_sms() * 8) g = num_sms() * 8;
+    dequantize_kernel<<<g, kThreads, 0, s>>>(src, dst, count, scale);
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
+
+}  // namespace ane_b200

@@ -1,0 +1,153 @@
+// stream_exec.cpp -- host decoder of the reference bytecode stream.
+//
+// Replaces the AArch64 dispatch loop of the reference interpreter
+// (src/bytecode_interpreter.s:12-40 fetch / jump table, :174-185 exit).  The
+// encoding is the one ane::dispatch produces (include/ane/ane.hpp:206-220): one
+// opcode byte, then every argument memcpy'd back to back by sizeof, no padding,
+// little-endian.  Hot-path opcodes run on the GPU through the synchronous C
+// entry points; any other opcode stops the stream with
+// ANE_ERR_UNSUPPORTED_OPCODE (the reference has no bounds check at all).
+#include <string.h>
+
+#include <string>
+
+#include "../../include/ane_b200.h"
+
+namespace ane_b200 {
+void set_status(int code, const std::string& msg);
+int ok();
+}  // namespace ane_b200
+
+namespace {
+
+struct Reader {
+    const uint8_t* p;
+    size_t left;
+    template <class T>
+    T get() {
+        T v;
+        memcpy(&v, p, sizeof(T));
+        p += sizeof(T);
+        left -= sizeof(T);
+        return v;
+    }
+    template <class T>
+    T* ptr() {
+        return reinterpret_cast<T*>(static_cast<uintptr_t>(get<uint64_t>()));
+    }
+};
+
+// Payload sizes (bytes after the opcode) of the executed opcodes.
+int payload_size(uint8_t op) {
+    switch (op) {
+        case 0x18: return 12 + 8 + 1 + 32;  // dense_i8: M N K sa sb flags A Bp bias C
+        case 0x19: return 4 + 24;           // quantize_fp32_i8: count src dst scale_out
+        case 0x1A: return 4 + 4 + 16;       // dequantize_i8_fp32: count scale src dst
+        case 0x1B: return 8 + 16;           // pack_b_i8: K N src dst
+        case 0x1C: return 8 + 24;           // quantize_fp32_i8_channelwise: rows cols src dst scales
+        case 0x57: return 8 + 24;           // q8_0_gemv: M K in W out
+        case 0x80: return 12 + 4 + 1 + 24;  // dense_fused_i8: M N K scale relu A B C
+        default: return -1;
+    }
+}
+
+inline uint32_t round16(uint32_t v) { return (v + 15u) & ~15u; }
+
+int exec_one(uint8_t op, Reader& r) {
+    switch (op) {
+        case 0x18: {
+            uint32_t M = r.get<uint32_t>(), N = r.get<uint32_t>(), K = r.get<uint32_t>();
+            float sa = r.get<float>(), sb = r.get<float>();
+            uint8_t flags = r.get<uint8_t>();
+            const int8_t* A = r.ptr<const int8_t>();
+            const int8_t* Bp = r.ptr<const int8_t>();
+            const float* bias = r.ptr<const float>();
+            float* C = r.ptr<float>();
+            return ane_dense_i8(M, N, K, sa, sb, flags, A, Bp, bias, C);
+        }
+        case 0x19: {
+            // The handler works on whole 16-lane vectors: ceil(count/16)*16 elements
+            // (callers pad buffers to 16 elements, README.md:79).
+            uint32_t count = r.get<uint32_t>();
+            const float* src = r.ptr<const float>();
+            int8_t* dst = r.ptr<int8_t>();
+            float* scale_out = r.ptr<float>();
+            return ane_quantize_fp32_i8(round16(count), src, dst, scale_out);
+        }
+        case 0x1A: {
+            uint32_t count = r.get<uint32_t>();
+            float scale = r.get<float>();
+            const int8_t* src = r.ptr<const int8_t>();
+            float* dst = r.ptr<float>();
+            return ane_dequantize_i8_fp32(count, scale, src, dst);
+        }
+        case 0x1B: {
+            uint32_t K = r.get<uint32_t>(), N = r.get<uint32_t>();
+            const int8_t* src = r.ptr<const int8_t>();
+            int8_t* dst = r.ptr<int8_t>();
+            return ane_pack_b_i8(K, N, src, dst);
+        }
+        case 0x1C: {
+            // rows are walked contiguously in whole 16-element vectors
+            uint32_t rows = r.get<uint32_t>(), cols = r.get<uint32_t>();
+            const float* src = r.ptr<const float>();
+            int8_t* dst = r.ptr<int8_t>();
+            float* scales = r.ptr<float>();
+            return ane_quantize_fp32_i8_channelwise(rows, round16(cols), src, dst, scales);
+        }
+        case 0x57: {
+            uint32_t M = r.get<uint32_t>(), K = r.get<uint32_t>();
+            const float* in = r.ptr<const float>();
+            const void* W = r.ptr<const void>();
+            float* out = r.ptr<float>();
+            return ane_q8_0_gemv(M, K & ~31u, in, W, out);  // num_blocks = K/32
+        }
+        case 0x80: {
+            uint32_t M = r.get<uint32_t>(), N = r.get<uint32_t>(), K = r.get<uint32_t>();
+            float scale = r.get<float>();
+            uint8_t relu = r.get<uint8_t>();
+            const float* A = r.ptr<const float>();
+            const float* B = r.ptr<const float>();
+            float* C = r.ptr<float>();
+            return ane_dense_fused_i8(M, N, K, scale, relu ? 1 : 0, A, B, C);
+        }
+        default:
+            return ANE_ERR_UNSUPPORTED_OPCODE;
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int ane_opcode_payload_size(uint8_t op) { return payload_size(op); }
+int ane_opcode_supported(uint8_t op) { return payload_size(op) >= 0 ? 1 : 0; }
+
+void stream_exec(const uint8_t* data, size_t size) {
+    using namespace ane_b200;
+    if (size && !data) {
+        set_status(ANE_ERR_INVALID_ARGUMENT, "stream_exec: NULL stream");
+        return;
+    }
+    Reader r{data, size};
+    while (r.left > 0) {
+        const uint8_t op = r.get<uint8_t>();
+        if (op == 0x00) break;  // reserved slot 0 = exit (jump table entry 0)
+        const int need = payload_size(op);
+        if (need < 0) {
+            set_status(ANE_ERR_UNSUPPORTED_OPCODE,
+                       "stream_exec: opcode 0x" + std::to_string(op) + " is outside the B200 hot path");
+            return;
+        }
+        if ((size_t)need > r.left) {
+            set_status(ANE_ERR_TRUNCATED_STREAM, "stream_exec: payload of opcode " + std::to_string(op) +
+                                                     " runs past the end of the stream");
+            return;
+        }
+        const int rc = exec_one(op, r);
+        if (rc != ANE_OK) return;  // the entry point recorded the detail
+    }
+    ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,371 @@
+"""Benchmark of ane's quantized dense hot path on B200 (one JSON line on rank 0).
+
+Headline workload (the metric's first half):
+dense_fused_i8 with M = N = K = 4096, scale 1.0, ReLU off, fp32 N(0,1) inputs
+resident in HBM.  One step = one dense_fused_i8 call = absmax pass, quantize
+pass, tcgen05 int8 GEMM with fused fp32 epilogue.  value = 2*M*N*K / step time
+(int8 TOPS, whole job).  Inputs (A+B fp32 = 128 MiB, plus Aq/Bt/C) exceed the
+126 MB L2, so no extra flush is needed between steps.
+
+Also reported on the same line:
+* roofline of the dominant kernel (the GEMM), timed alone with CUDA events on
+  its stream, against the int8 dense peak = 2 x measured bf16 burst peak;
+* e2e: the same op through the reference-facing C ABI (ane_dense_fused_i8)
+  with pinned HOST buffers, H2D + D2H inside the timed region;
+* q8_0_gemv GB/s (the metric's second half) with rotated
+  weight copies (> L2) so every call streams from HBM;
+* cpu_baseline: the oracle's OpenMP restatement on the host cores, on a
+  bounded sample of the same workload.
+
+Multi-GPU (torchrun, N > 1): every rank holds A and a 4096-column shard of B
+(weak scaling, per-rank work fixed); the global absmax is an NCCL all-reduce
+(MAX) of two floats, each rank runs the GEMM on its shard and the M x N output
+shards are NCCL all-gathered -- bit-identical to the 1-GPU result.
+
+`--impl reference` times the reference's CPU semantics (the oracle, kind
+"port": the reference's SME2 assembly cannot run on x86) on the same config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "int8 GEMM TOPS (4096³) & Q8_0 matvec GB/s at 1/2/4/8 B200"
+M = N = K = 4096
+SCALE, RELU = 1.0, False
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", default="ane_b200", choices=["ane_b200", "reference"])
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-q8", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sms, maxs, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxs.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxs) if maxs else None,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    import numpy as np
+
+    import oracle
+
+    threads = oracle.max_threads()
+    rows = 256  # bounded sample: first 256 rows of A against the full 4096 x 4096 B
+    rng = np.random.default_rng(1234)
+    A = rng.standard_normal((rows, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    for _ in range(max(1, min(args.warmup, 1))):
+        oracle.dense_fused_i8_omp(A[:16], B, SCALE, RELU, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.dense_fused_i8_omp(A, B, SCALE, RELU, threads)
+    dt = (time.perf_counter() - t0) / args.steps
+    tops = 2.0 * rows * N * K / dt / 1e12
+    sample = f"rows 0..{rows - 1} of A (of {M}) x full B {K}x{N} per step, quantize of full B included"
+    line = {"impl": "reference", "metric": METRIC, "value": tops, "unit": "TOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "dense_fused_i8 M=N=K=4096 scale=1.0 relu=off (CPU sample)", "sample": sample},
+            "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- our arm
+def cpu_baseline_sample():
+    import numpy as np
+
+    import oracle
+
+    threads = oracle.max_threads()
+    rows = 256
+    rng = np.random.default_rng(1234)
+    A = rng.standard_normal((rows, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    oracle.dense_fused_i8_omp(A[:16], B, SCALE, RELU, threads)
+    reps = 3
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        oracle.dense_fused_i8_omp(A, B, SCALE, RELU, threads)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": 2.0 * rows * N * K / dt / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"oracle OpenMP dense_fused_i8, rows 0..{rows - 1} of A x full 4096x4096 B, {reps} reps"}
+
+
+def time_events(fn, steps, stream):
+    import torch
+
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record(stream)
+    for _ in range(steps):
+        fn()
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps  # ms
+
+
+def q8_bench(ane, torch, dev, steps=50):
+    """Q8_0 matvec GB/s on the 7B shapes, rotating >= 4 weight copies (> L2)."""
+    import numpy as np
+
+    out = {}
+    stream = torch.cuda.current_stream()
+    for (rows, cols) in [(4096, 4096), (11008, 4096), (4096, 11008)]:
+        wbytes = rows * (cols // 32) * 34
+        copies = max(4, int(np.ceil(512e6 / wbytes)))
+        g = torch.Generator(device=dev).manual_seed(rows + cols)
+        Ws = [torch.randint(0, 256, (wbytes,), dtype=torch.uint8, device=dev, generator=g) for _ in range(copies)]
+        for W in Ws:  # valid fp16 scales (d in [2^-8, 2^-7)) so no block takes the non-finite path
+            Wv = W.view(rows * (cols // 32), 34)
+            Wv[:, 0] = torch.randint(0, 256, (Wv.shape[0],), dtype=torch.uint8, device=dev, generator=g)
+            Wv[:, 1] = 0x1C
+        x = torch.randn(cols, device=dev, generator=g)
+        y = torch.empty(rows, device=dev)
+        for i in range(3):
+            ane.q8_0_gemv(Ws[i % copies], x, rows, cols, out=y)
+        it = [0]
+
+        def step():
+            ane.q8_0_gemv(Ws[it[0] % copies], x, rows, cols, out=y)
+            it[0] += 1
+
+        ms = time_events(step, steps, stream)
+        nbytes = wbytes + 4 * cols + 4 * rows
+        out[f"{rows}x{cols}"] = {"gbs": nbytes / (ms * 1e-3) / 1e9, "us": ms * 1e3, "bytes": nbytes,
+                                 "weight_copies_rotated": copies}
+        del Ws
+    return out
+
+
+def run_ours(args):
+    import torch
+
+    import ane_b200 as ane
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist.group.WORLD
+    peaks = load_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    stream = torch.cuda.current_stream()
+
+    g = torch.Generator(device=dev).manual_seed(1234)
+    A = torch.randn((M, K), device=dev, generator=g)
+    g2 = torch.Generator(device=dev).manual_seed(5678 + rank)
+    B = torch.randn((K, N), device=dev, generator=g2)  # this rank's column shard of B when world > 1
+    C = torch.empty((M, N), device=dev)
+    ws = ane.dense_fused_i8_workspace(M, N, K, dev)
+
+    if world == 1:
+        def step():
+            ane.dense_fused_i8(A, B, SCALE, RELU, out=C, workspace=ws)
+    else:
+        from ane_b200 import sharded
+
+        ctx = sharded.ShardedDense(M, N, K, world, dev, pg)
+
+        def step():
+            ctx.forward(A, B, SCALE, RELU)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if pg is not None:
+        torch.distributed.barrier()
+
+    launches0 = ane.launch_count()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)  # let the sampler start before the timed region
+    t_s = torch.cuda.Event(enable_timing=True)
+    t_e = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if pg is not None:
+        torch.distributed.barrier()
+    t_s.record(stream)
+    for _ in range(args.steps):
+        step()
+    t_e.record(stream)
+    torch.cuda.synchronize()
+    if pg is not None:
+        torch.distributed.barrier()
+    ms = t_s.elapsed_time(t_e) / args.steps
+    # keep the clock sampler fed for at least ~1 s of the same load
+    soak_until = time.perf_counter() + 1.0
+    while time.perf_counter() < soak_until:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
+    clocks = sampler.stop()
+    launches = ane.launch_count() - launches0
+
+    if pg is not None:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ops_per_rank = 2.0 * M * N * K
+    value = world * ops_per_rank / (ms * 1e-3) / 1e12
+    launches_per_step = launches / float(args.steps) if args.steps else 0
+
+    # ---- dominant kernel alone: tcgen05 GEMM on resident quantized operands
+    Aq, Bt, scales = ane.quantize_pair(A, B)
+    for _ in range(3):
+        ane.gemm_s8(Aq, Bt, scales, SCALE, RELU, out=C)
+    gemm_steps = max(20, args.steps)
+    gemm_ms = time_events(lambda: ane.gemm_s8(Aq, Bt, scales, SCALE, RELU, out=C), gemm_steps, stream)
+    gemm_tops = ops_per_rank / (gemm_ms * 1e-3) / 1e12
+    q_ms = time_events(lambda: ane.quantize_pair(A, B), max(10, args.steps // 4), stream)
+
+    # ---- e2e through the reference-facing C ABI with pinned host buffers
+    e2e = None
+    if rank == 0 or world > 1:
+        Ah = A.cpu().pin_memory()
+        Bh = B.cpu().pin_memory()
+        Ch = torch.empty((M, N), dtype=torch.float32).pin_memory()
+        ane.check(ane.lib.ane_dense_fused_i8(M, N, K, SCALE, int(RELU), Ah.data_ptr(), Bh.data_ptr(), Ch.data_ptr()))
+        e2e_steps = max(3, min(args.steps, 20))
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            ane.check(ane.lib.ane_dense_fused_i8(M, N, K, SCALE, int(RELU), Ah.data_ptr(), Bh.data_ptr(),
+                                                 Ch.data_ptr()))
+        e2e_s = (time.perf_counter() - t0) / e2e_steps
+        e2e = {"value": world * ops_per_rank / e2e_s / 1e12, "unit": "TOPS",
+               "h2d_bytes_per_step": 4 * (M * K + K * N), "d2h_bytes_per_step": 4 * M * N,
+               "ms_per_step": e2e_s * 1e3, "path": "ane_dense_fused_i8 (C ABI, pinned host buffers)"}
+
+    q8 = None
+    if not args.no_q8 and rank == 0:
+        q8 = q8_bench(ane, torch, dev)
+
+    if rank != 0:
+        if pg is not None:
+            torch.distributed.destroy_process_group()
+        return
+    cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline_sample()
+    line = {
+        "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "dense_fused_i8 M=N=K=4096 scale=1.0 relu=off, fp32 N(0,1) A and B in HBM"
+                               + ("" if world == 1 else f"; B/C column-sharded, {N} columns per rank, "
+                                  "NCCL all-reduce(max) of absmax + all-gather of C"),
+                   "M": M, "N_per_rank": N, "K": K,
+                   "l2": "inputs larger than L2 (A+B fp32 = 128 MiB > 126 MB L2), no flush",
+                   "parallelism": f"n-shard{world}" if world > 1 else "single"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_s8_tc_kernel (tcgen05 kind::i8)",
+                     "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS", "frac": gemm_tops / int8_peak,
+                     "peak_source": f"2 x {peaks['source']} bf16 burst ({peaks['bf16_tflops']} TFLOP/s)",
+                     "traffic": None, "gemm_ms": gemm_ms},
+        "stages_ms": {"quantize_pair": q_ms, "gemm": gemm_ms, "step": ms},
+        "e2e": e2e, "gpu_launches": int(launches), "gpu_launches_per_step": launches_per_step,
+        "clocks": clocks, "q8_0_gemv": q8, "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    if pg is not None:
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

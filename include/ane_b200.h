@@ -1,0 +1,130 @@
+/*
+ * ane_b200.h -- C ABI of the B200 (sm_100a) implementation of ane's quantized
+ * dense hot path.  Plain pointers and sizes only.
+ *
+ * Two families of entry points:
+ *   1. Reference-facing, synchronous, any pointer kind (pageable / pinned host,
+ *      device, managed).  They keep the reference's calling contract: results
+ *      are in caller memory on return, buffers are caller-owned.  Host buffers
+ *      are copied to the device and back inside the call.
+ *   2. `*_dev` entry points: device pointers, asynchronous on a caller stream
+ *      (`stream` is a cudaStream_t passed as void*; NULL = legacy default).
+ *
+ * Every entry point returns an ane_status (0 = OK) and also records it in a
+ * thread-local slot readable with ane_last_error(), because stream_exec keeps
+ * the reference's `void` signature.
+ */
+#ifndef ANE_B200_H
+#define ANE_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum ane_status {
+    ANE_OK = 0,
+    ANE_ERR_INVALID_ARGUMENT = 1,   /* bad size, NULL pointer, misaligned K, ... */
+    ANE_ERR_UNSUPPORTED_OPCODE = 2, /* stream_exec met an opcode outside the hot path */
+    ANE_ERR_TRUNCATED_STREAM = 3,   /* stream_exec payload runs past the end */
+    ANE_ERR_CUDA = 4,               /* a CUDA runtime/driver call failed */
+    ANE_ERR_NO_DEVICE = 5,          /* no sm_100 device visible */
+    ANE_ERR_OUT_OF_MEMORY = 6,
+    ANE_ERR_DEVICE_TIMEOUT = 7      /* a bounded device-side wait gave up */
+} ane_status;
+
+/* ------------------------------------------------------------------ status */
+int ane_last_error(void);                 /* status of this thread's last call */
+const char* ane_last_error_string(void);  /* human-readable detail of it */
+void ane_clear_error(void);
+const char* ane_version(void);
+/* Number of opcodes stream_exec executes, and whether `op` is one of them. */
+int ane_opcode_supported(uint8_t op);
+/* Payload bytes that follow opcode `op` in a stream (reference encoding), or -1. */
+int ane_opcode_payload_size(uint8_t op);
+
+/* ---------------------------------------------------------- drop-in boundary
+ * Replaces `ane::interpreter::stream_exec` (reference include/ane/ane.hpp:37-39,
+ * src/bytecode_interpreter.s:11-40,174-185).  Decodes the reference byte
+ * stream `[u8 op][args packed by sizeof, little-endian]...` and executes the
+ * hot-path opcodes on the GPU.  Stops at the first unsupported opcode or
+ * truncated payload and records the status (ane_last_error). */
+void stream_exec(const uint8_t* data, size_t size);
+
+/* ------------------------------------------ reference-facing synchronous ops
+ * Each mirrors one opcode; argument order = the reference's encoding order. */
+
+/* quantize_fp32_i8 (0x19; bytecode_interpreter.s:1876-1950).  `count` elements
+ * exactly (the reference rounds up to a multiple of 16 inside stream_exec). */
+int ane_quantize_fp32_i8(uint32_t count, const float* src, int8_t* dst, float* scale_out);
+/* dequantize_i8_fp32 (0x1A; :1951-1977). */
+int ane_dequantize_i8_fp32(uint32_t count, float scale, const int8_t* src, float* dst);
+/* pack_b_i8 (0x1B; :2447-2582).  dst holds ceil(N/16)*ceil(K/4)*64 bytes. */
+int ane_pack_b_i8(uint32_t K, uint32_t N, const int8_t* src, int8_t* dst);
+/* quantize_fp32_i8_channelwise (0x1C; :2583-2662). */
+int ane_quantize_fp32_i8_channelwise(uint32_t rows, uint32_t cols, const float* src, int8_t* dst,
+                                     float* scales);
+/* dense_i8 (0x18; :1978-2446).  Reference memory contract: A is M16 x K64
+ * (row stride K64), B_packed from pack_b_i8 with K64 rows, bias N32 floats,
+ * C receives M16 rows of N floats (padded rows included). */
+int ane_dense_i8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags,
+                 const int8_t* A, const int8_t* B_packed, const float* bias, float* C);
+/* dense_fused_i8 (0x80, new; README.md:87-97 usage).  fp32 A (M x K, stride K)
+ * and B (K x N, stride N) quantized per tensor to int8 (absmax/127), int8 x int8
+ * -> exact int32, y = float(acc)*(sa*sb), y = y*scale, optional ReLU; C is
+ * M x N fp32 (stride N).  Only the M*N outputs are written. */
+int ane_dense_fused_i8(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t relu,
+                       const float* A, const float* B, float* C);
+/* q8_0_gemv (0x57; :7010-7063, docs/API.md:592-604).  W = M rows of K/32
+ * Q8_0 blocks {fp16 d; int8 qs[32]} (34 B, unpadded); fp32 in[K]; out[M].
+ * Bit-exact with the reference's 16-lane FMA order and FADDV tree. */
+int ane_q8_0_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out);
+
+/* ------------------------------------------------------------ device ops
+ * Device pointers; asynchronous on `stream`.  Workspace-taking ops accept a
+ * caller buffer of at least the size reported by the matching *_workspace_size
+ * (NULL -> the library uses a cached per-device allocation). */
+size_t ane_dense_fused_i8_workspace_size(uint32_t M, uint32_t N, uint32_t K);
+int ane_dense_fused_i8_dev(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t relu,
+                           const float* A, const float* B, float* C, void* workspace,
+                           size_t workspace_bytes, void* stream);
+/* Quantize-only stages of dense_fused_i8 (for staged timing and tests):
+ * Aq = M x K16 int8 (row stride K16 = ceil(K/16)*16, pad columns zero),
+ * Bt = N x K16 int8 (B quantized AND transposed, pad zero), scales[0]=sa,
+ * scales[1]=sb.  `partials` holds ane_absmax_partials_count(M*K, K*N) floats. */
+size_t ane_absmax_partials_count(size_t count_a, size_t count_b);
+int ane_quantize_pair_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B,
+                          int8_t* Aq, int8_t* Bt, float* scales, float* partials, void* stream);
+/* Multi-GPU building blocks (N-sharded dense_fused_i8): absmax of both tensors
+ * into device absmax2[2] (reduce across ranks with MAX, then quantize with the
+ * global values, so every shard uses the single-GPU scales). */
+int ane_absmax_pair_dev(const float* A, size_t count_a, const float* B, size_t count_b, float* absmax2,
+                        float* partials, void* stream);
+int ane_quantize_pair_absmax_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
+                                 int8_t* Bt, const float* absmax2, float* scales, void* stream);
+/* int8 tensor-core GEMM with the dense_fused_i8 epilogue, operands resident:
+ * Aq M x K16 (K-major), Bt N x K16 (K-major), scales device float[2].
+ * out_mode 0: fp32 C = relu?(float(acc)*(s0*s1)*scale);  1: raw int32 acc. */
+int ane_gemm_s8_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* Aq, const int8_t* Bt,
+                    const float* scales, float scale, uint8_t relu, int out_mode, void* C,
+                    void* stream);
+int ane_quantize_fp32_i8_dev(uint32_t count, const float* src, int8_t* dst, float* scale_out,
+                             void* stream);
+int ane_pack_b_i8_dev(uint32_t K, uint32_t N, const int8_t* src, int8_t* dst, void* stream);
+int ane_dense_i8_dev(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags,
+                     const int8_t* A, const int8_t* B_packed, const float* bias, float* C,
+                     void* stream);
+int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out,
+                      void* stream);
+
+/* ------------------------------------------------------------ diagnostics */
+/* Device-side bounded-wait failures since the last call (and reset). */
+int ane_device_timeouts(void);
+/* Kernel launches this library issued since process start (all threads). */
+uint64_t ane_kernel_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,414 @@
+/*
+ * ane_oracle.c -- CPU restatement of the reference's quantized dense hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY (parity checker and timed CPU baseline); never part
+ * of the product.  See ane_oracle.h for the reference file:line each function
+ * follows.  Build with -ffp-contract=off and without -ffast-math: every fp32
+ * operation here is one IEEE round-to-nearest-even operation, as in the asm.
+ */
+#include "ane_oracle.h"
+
+#include <float.h>
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ------------------------------------------------------------------ scalars */
+
+float ane_ref_fp16_to_fp32(uint16_t h) {
+    /* fcvt s,h (bytecode_interpreter.s:7034): exact widening. */
+    uint32_t sign = (uint32_t)(h >> 15) << 31;
+    uint32_t e = (h >> 10) & 0x1f;
+    uint32_t m = h & 0x3ff;
+    uint32_t bits;
+    if (e == 0) {
+        if (m == 0) {
+            bits = sign;
+        } else { /* subnormal half -> normal float */
+            int shift = 0;
+            while ((m & 0x400) == 0) { m <<= 1; shift++; }
+            m &= 0x3ff;
+            bits = sign | ((uint32_t)(127 - 15 + 1 - shift) << 23) | (m << 13);
+        }
+    } else if (e == 31) {
+        bits = sign | 0x7f800000u | (m << 13);
+    } else {
+        bits = sign | ((e - 15 + 127) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+uint16_t ane_ref_fp32_to_fp16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t absx = x & 0x7fffffffu;
+    if (absx >= 0x7f800000u) { /* inf / nan */
+        return (uint16_t)(sign | 0x7c00u | (absx > 0x7f800000u ? (0x200u | ((absx >> 13) & 0x3ffu)) : 0));
+    }
+    if (absx >= 0x477ff000u) /* rounds to >= 65520 -> inf */
+        return (uint16_t)(sign | 0x7c00u);
+    int e = (int)(absx >> 23) - 127;
+    uint32_t mant = (absx & 0x7fffffu) | 0x800000u;
+    if (e < -25) return (uint16_t)sign; /* below half of the smallest subnormal */
+    if (e < -14) {                      /* subnormal half */
+        int shift = -14 - e + 13;       /* bits dropped from the 24-bit mantissa */
+        uint32_t q = mant >> shift;
+        uint32_t rem = mant & ((1u << shift) - 1);
+        uint32_t halfway = 1u << (shift - 1);
+        if (rem > halfway || (rem == halfway && (q & 1))) q++;
+        return (uint16_t)(sign | q);
+    }
+    uint32_t q = mant >> 13;
+    uint32_t rem = mant & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (q & 1))) q++;
+    uint32_t he = (uint32_t)(e + 15);
+    if (q == 0x800u) { q = 0x400u; he++; }
+    return (uint16_t)(sign | (he << 10) | (q & 0x3ffu));
+}
+
+float ane_ref_relu_max(float y, float floor_v) {
+    /* ARM FMAX (not FMAXNM): a NaN operand yields NaN; max(-0, +0) = +0. */
+    if (isnan(y)) return y;
+    if (isnan(floor_v)) return floor_v;
+    if (y == floor_v) return signbit(y) ? floor_v : y;
+    return y > floor_v ? y : floor_v;
+}
+
+static inline float arm_fmin(float a, float b) {
+    if (isnan(a)) return a;
+    if (isnan(b)) return b;
+    if (a == b) return signbit(a) ? a : b;
+    return a < b ? a : b;
+}
+
+/* --------------------------------------------------------- quantize_fp32_i8 */
+
+float ane_ref_absmax(const float* src, size_t count) {
+    /* bytecode_interpreter.s:1893-1900: fabs + fmax into 16 lanes, then fmaxv.
+     * max is order-independent except for NaN, which propagates either way. */
+    float m = 0.0f;
+    for (size_t i = 0; i < count; i++) m = ane_ref_relu_max(m, fabsf(src[i]));
+    return m;
+}
+
+float ane_ref_scale_from_absmax(float absmax, float* inv_out) {
+    /* bytecode_interpreter.s:1902-1914.  fcmp #0.0 / b.eq: NaN is unordered,
+     * so a NaN absmax takes the division path. */
+    float scale, inv;
+    if (absmax == 0.0f) {
+        scale = 1.0f;
+        inv = 127.0f;
+    } else {
+        scale = absmax / 127.0f;
+        inv = 127.0f / absmax;
+    }
+    if (inv_out) *inv_out = inv;
+    return scale;
+}
+
+int8_t ane_ref_quantize_one(float x, float inv) {
+    /* bytecode_interpreter.s:1929-1941: fmul, fmax -127, fmin 127, frintn,
+     * fcvtzs (NaN -> 0), st1b truncating narrow. */
+    float y = x * inv;
+    y = ane_ref_relu_max(y, -127.0f);
+    y = arm_fmin(y, 127.0f);
+    if (isnan(y)) return 0;
+    y = rintf(y); /* default rounding mode: nearest, ties to even */
+    return (int8_t)(int32_t)y;
+}
+
+float ane_ref_quantize_fp32_i8(const float* src, int8_t* dst, size_t count, float* scale_out) {
+    float inv;
+    float scale = ane_ref_scale_from_absmax(ane_ref_absmax(src, count), &inv);
+    if (scale_out) *scale_out = scale;
+    for (size_t i = 0; i < count; i++) dst[i] = ane_ref_quantize_one(src[i], inv);
+    return scale;
+}
+
+void ane_ref_quantize_fp32_i8_channelwise(uint32_t rows, uint32_t cols, const float* src,
+                                          int8_t* dst, float* scales) {
+    /* bytecode_interpreter.s:2583-2662: the per-tensor rule applied per row. */
+    for (uint32_t r = 0; r < rows; r++)
+        ane_ref_quantize_fp32_i8(src + (size_t)r * cols, dst + (size_t)r * cols, cols, &scales[r]);
+}
+
+void ane_ref_dequantize_i8_fp32(size_t count, float scale, const int8_t* src, float* dst) {
+    /* bytecode_interpreter.s:1966-1975: scvtf then fmul. */
+    for (size_t i = 0; i < count; i++) dst[i] = (float)src[i] * scale;
+}
+
+/* ---------------------------------------------------------------- pack_b_i8 */
+
+size_t ane_ref_packed_b_size(uint32_t K, uint32_t N) {
+    size_t groups = ((size_t)K + 3) / 4;
+    size_t panels = ((size_t)N + 15) / 16;
+    return panels * groups * 64;
+}
+
+void ane_ref_pack_b_i8(uint32_t K, uint32_t N, const int8_t* src, int8_t* dst) {
+    /* bytecode_interpreter.s:2466-2580:
+     * dst[(p*G + g)*64 + c*4 + d] = B[(4g+d)*N + 16p+c], zero outside K x N. */
+    size_t G = ((size_t)K + 3) / 4;
+    size_t P = ((size_t)N + 15) / 16;
+    for (size_t p = 0; p < P; p++)
+        for (size_t g = 0; g < G; g++)
+            for (size_t c = 0; c < 16; c++)
+                for (size_t d = 0; d < 4; d++) {
+                    size_t k = 4 * g + d, n = 16 * p + c;
+                    dst[(p * G + g) * 64 + c * 4 + d] = (k < K && n < N) ? src[k * N + n] : 0;
+                }
+}
+
+/* --------------------------------------------------------------- int8 GEMM */
+
+void ane_ref_gemm_s8_s32(uint32_t M, uint32_t N, uint32_t K, const int8_t* A, size_t lda,
+                         const int8_t* B, size_t ldb, int32_t* acc) {
+    for (uint32_t m = 0; m < M; m++) {
+        int32_t* row = acc + (size_t)m * N;
+        for (uint32_t n = 0; n < N; n++) row[n] = 0;
+        for (uint32_t k = 0; k < K; k++) {
+            int32_t a = A[(size_t)m * lda + k];
+            const int8_t* b = B + (size_t)k * ldb;
+            for (uint32_t n = 0; n < N; n++) row[n] += a * (int32_t)b[n];
+        }
+    }
+}
+
+void ane_ref_dense_i8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags,
+                      const int8_t* A, const int8_t* B_packed, const float* bias, float* C) {
+    /* bytecode_interpreter.s:1995-2446.  M16 x N32 tiles, K padded to K64,
+     * A row stride K64, B panel stride K64/4*64 bytes, C rows not predicated. */
+    uint32_t M16 = (M + 15) & ~15u;
+    uint32_t N32 = (N + 31) & ~31u;
+    uint32_t K64 = (K + 63) & ~63u;
+    size_t G = K64 / 4;
+    float comb = sa * sb;                           /* :2017 fmul s20,s20,s22 */
+    float floor_v = (flags & 1) ? 0.0f : -FLT_MAX;  /* :2022-2029 */
+    for (uint32_t r = 0; r < M16; r++) {
+        for (uint32_t n = 0; n < N32 && n < N; n++) {
+            size_t p = n / 16, c = n % 16;
+            int32_t acc = 0;
+            for (uint32_t k = 0; k < K64; k++) {
+                size_t g = k / 4, d = k % 4;
+                acc += (int32_t)A[(size_t)r * K64 + k] *
+                       (int32_t)B_packed[(p * G + g) * 64 + c * 4 + d];
+            }
+            float y = (float)acc;                 /* scvtf */
+            y = y * comb;                         /* fmul */
+            y = y + bias[n];                      /* fadd */
+            C[(size_t)r * N + n] = ane_ref_relu_max(y, floor_v); /* fmax */
+        }
+    }
+}
+
+/* ---------------------------------------------------------- dense_fused_i8 */
+
+void ane_ref_dense_fused_epilogue(uint32_t M, uint32_t N, const int32_t* acc, float sa, float sb,
+                                  float scale, int relu, float* C) {
+    float comb = sa * sb;
+    for (size_t i = 0; i < (size_t)M * N; i++) {
+        float y = (float)acc[i];
+        y = y * comb;
+        y = y * scale;
+        C[i] = relu ? ane_ref_relu_max(y, 0.0f) : y;
+    }
+}
+
+void ane_ref_dense_fused_i8(uint32_t M, uint32_t N, uint32_t K, float scale, int relu,
+                            const float* A, const float* B, float* C, int8_t* Aq_out,
+                            int8_t* Bq_out, int32_t* acc_out, float* sa_out, float* sb_out) {
+    size_t MK = (size_t)M * K, KN = (size_t)K * N, MN = (size_t)M * N;
+    int8_t* Aq = Aq_out ? Aq_out : (int8_t*)malloc(MK ? MK : 1);
+    int8_t* Bq = Bq_out ? Bq_out : (int8_t*)malloc(KN ? KN : 1);
+    int32_t* acc = acc_out ? acc_out : (int32_t*)malloc((MN ? MN : 1) * sizeof(int32_t));
+    float sa = ane_ref_quantize_fp32_i8(A, Aq, MK, NULL);
+    float sb = ane_ref_quantize_fp32_i8(B, Bq, KN, NULL);
+    ane_ref_gemm_s8_s32(M, N, K, Aq, K, Bq, N, acc);
+    ane_ref_dense_fused_epilogue(M, N, acc, sa, sb, scale, relu, C);
+    if (sa_out) *sa_out = sa;
+    if (sb_out) *sb_out = sb;
+    if (!Aq_out) free(Aq);
+    if (!Bq_out) free(Bq);
+    if (!acc_out) free(acc);
+}
+
+/* --------------------------------------------------------------- q8_0_gemv */
+
+static inline float faddv16(const float* a) {
+    /* SVE FADDV over 16 fp32 lanes: Reduce() splits into low/high halves
+     * recursively, so the tree is ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)) ... */
+    float s8[8], s4[4], s2[2];
+    for (int i = 0; i < 8; i++) s8[i] = a[2 * i] + a[2 * i + 1];
+    for (int i = 0; i < 4; i++) s4[i] = s8[2 * i] + s8[2 * i + 1];
+    for (int i = 0; i < 2; i++) s2[i] = s4[2 * i] + s4[2 * i + 1];
+    return s2[0] + s2[1];
+}
+
+static void q8_0_gemv_rows(uint32_t m0, uint32_t m1, uint32_t K, const float* x,
+                           const uint8_t* W, float* out) {
+    uint32_t nb = K / 32;
+    for (uint32_t m = m0; m < m1; m++) {
+        const uint8_t* row = W + (size_t)m * nb * 34;
+        float acc[16] = {0};
+        for (uint32_t b = 0; b < nb; b++) {
+            const uint8_t* blk = row + (size_t)b * 34;
+            uint16_t hb = (uint16_t)(blk[0] | (blk[1] << 8));
+            float d = ane_ref_fp16_to_fp32(hb);      /* ldr h0 ; fcvt */
+            const int8_t* qs = (const int8_t*)(blk + 2);
+            const float* xb = x + (size_t)b * 32;
+            for (int l = 0; l < 16; l++) {             /* first half, :7042-7047 */
+                float dq = (float)qs[l] * d;           /* scvtf ; fmul */
+                acc[l] = fmaf(dq, xb[l], acc[l]);      /* fmla */
+            }
+            for (int l = 0; l < 16; l++) {             /* second half, :7049-7055 */
+                float dq = (float)qs[16 + l] * d;
+                acc[l] = fmaf(dq, xb[16 + l], acc[l]);
+            }
+        }
+        out[m] = faddv16(acc);                         /* faddv ; str */
+    }
+}
+
+void ane_ref_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out) {
+    q8_0_gemv_rows(0, M, K, x, W, out);
+}
+
+void ane_ref_quantize_q8_0(const float* x, uint8_t* blocks, size_t n_rows, size_t K) {
+    size_t nb = K / 32;
+    for (size_t r = 0; r < n_rows; r++)
+        for (size_t b = 0; b < nb; b++) {
+            const float* xb = x + r * K + b * 32;
+            uint8_t* blk = blocks + (r * nb + b) * 34;
+            float amax = 0.0f;
+            for (int j = 0; j < 32; j++) {
+                float v = fabsf(xb[j]);
+                amax = amax > v ? amax : v;
+            }
+            float d = amax / 127.0f;
+            float id = d != 0.0f ? 1.0f / d : 0.0f;
+            uint16_t hd = ane_ref_fp32_to_fp16(d);
+            blk[0] = (uint8_t)(hd & 0xff);
+            blk[1] = (uint8_t)(hd >> 8);
+            for (int j = 0; j < 32; j++) blk[2 + j] = (uint8_t)(int8_t)roundf(xb[j] * id);
+        }
+}
+
+void ane_ref_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8_t* W,
+                          float* out, int32_t* block_dots) {
+    uint32_t nb = K / 32;
+    for (uint32_t m = 0; m < M; m++) {
+        float sumf = 0.0f;
+        for (uint32_t b = 0; b < nb; b++) {
+            const uint8_t* wb = W + ((size_t)m * nb + b) * 34;
+            const uint8_t* xb = xq + (size_t)b * 34;
+            int32_t sumi = 0;
+            for (int j = 0; j < 32; j++) sumi += (int32_t)(int8_t)wb[2 + j] * (int32_t)(int8_t)xb[2 + j];
+            if (block_dots) block_dots[(size_t)m * nb + b] = sumi;
+            float dw = ane_ref_fp16_to_fp32((uint16_t)(wb[0] | (wb[1] << 8)));
+            float dx = ane_ref_fp16_to_fp32((uint16_t)(xb[0] | (xb[1] << 8)));
+            sumf += (float)sumi * (dw * dx);
+        }
+        out[m] = sumf;
+    }
+}
+
+void ane_ref_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const uint8_t* table,
+                           const uint32_t* indices, float* out) {
+    /* bytecode_interpreter.s:12365-12405. */
+    uint32_t nb = dim / 32;
+    for (uint32_t r = 0; r < n_rows; r++) {
+        const uint8_t* row = table + (size_t)indices[r] * nb * 34;
+        for (uint32_t b = 0; b < nb; b++) {
+            const uint8_t* blk = row + (size_t)b * 34;
+            float d = ane_ref_fp16_to_fp32((uint16_t)(blk[0] | (blk[1] << 8)));
+            for (int j = 0; j < 32; j++)
+                out[(size_t)r * dim + b * 32 + j] = (float)(int8_t)blk[2 + j] * d;
+        }
+    }
+}
+
+/* ------------------------------------------------------- OpenMP baselines */
+
+int ane_ref_max_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+static float absmax_omp(const float* src, size_t n, int nt) {
+    float m = 0.0f;
+    int saw_nan = 0;
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(nt) reduction(max : m) reduction(| : saw_nan)
+#endif
+    for (size_t i = 0; i < n; i++) {
+        float v = fabsf(src[i]);
+        if (isnan(v)) saw_nan = 1;
+        m = v > m ? v : m;
+    }
+    (void)nt;
+    return saw_nan ? NAN : m;
+}
+
+void ane_ref_dense_fused_i8_omp(uint32_t M, uint32_t N, uint32_t K, float scale, int relu,
+                                const float* A, const float* B, float* C, int n_threads) {
+    size_t MK = (size_t)M * K, KN = (size_t)K * N;
+    int nt = n_threads > 0 ? n_threads : ane_ref_max_threads();
+    int8_t* Aq = (int8_t*)malloc(MK ? MK : 1);
+    int8_t* Bt = (int8_t*)malloc(KN ? KN : 1); /* quantized B, transposed N x K */
+    float inv_a, inv_b;
+    float sa = ane_ref_scale_from_absmax(absmax_omp(A, MK, nt), &inv_a);
+    float sb = ane_ref_scale_from_absmax(absmax_omp(B, KN, nt), &inv_b);
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(nt)
+#endif
+    for (size_t i = 0; i < MK; i++) Aq[i] = ane_ref_quantize_one(A[i], inv_a);
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(nt)
+#endif
+    for (uint32_t k = 0; k < K; k++)
+        for (uint32_t n = 0; n < N; n++) Bt[(size_t)n * K + k] = ane_ref_quantize_one(B[(size_t)k * N + n], inv_b);
+    float comb = sa * sb;
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(nt) schedule(dynamic, 1)
+#endif
+    for (uint32_t m = 0; m < M; m++) {
+        const int8_t* a = Aq + (size_t)m * K;
+        for (uint32_t n = 0; n < N; n++) {
+            const int8_t* b = Bt + (size_t)n * K;
+            int32_t s = 0;
+            for (uint32_t k = 0; k < K; k++) s += (int32_t)a[k] * (int32_t)b[k];
+            float y = (float)s;
+            y = y * comb;
+            y = y * scale;
+            C[(size_t)m * N + n] = relu ? ane_ref_relu_max(y, 0.0f) : y;
+        }
+    }
+    free(Aq);
+    free(Bt);
+}
+
+void ane_ref_q8_0_gemv_omp(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out,
+                           int n_threads) {
+    int nt = n_threads > 0 ? n_threads : ane_ref_max_threads();
+#ifdef _OPENMP
+#pragma omp parallel num_threads(nt)
+    {
+        int t = omp_get_thread_num(), T = omp_get_num_threads();
+        uint32_t per = (M + T - 1) / T;
+        uint32_t m0 = per * t, m1 = m0 + per > M ? M : m0 + per;
+        if (m0 < m1) q8_0_gemv_rows(m0, m1, K, x, W, out);
+    }
+#else
+    (void)nt;
+    q8_0_gemv_rows(0, M, K, x, W, out);
+#endif
+}
