@@ -36,7 +36,7 @@ __global__ void pack_b_kernel(const int8_t* __restrict__ src, int8_t* __restrict
 __global__ void unpack_b_kernel(const int8_t* __restrict__ Bp, int8_t* __restrict__ Bt, uint32_t K64,
                                 uint32_t N) {
     const uint32_t G = K64 / 4, J = K64 / 16;
-    const size_t items = (size_t)N * J;
+    const size_t items = ceil_div(N, 16) * 16 * J;  // whole panels; columns >= N are skipped below
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     const uint32_t* Bw = reinterpret_cast<const uint32_t*>(Bp);
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < items; i += stride) {

@@ -52,6 +52,8 @@ def parse():
     p.add_argument("--impl", default="ane_b200", choices=["ane_b200", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-q8", action="store_true")
+    p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (profiling runs)")
+    p.add_argument("--no-clocks", action="store_true", help="skip nvidia-smi sampling and its soak (profiling runs)")
     return p.parse_args()
 
 
@@ -269,8 +271,9 @@ def run_ours(args):
 
     launches0 = ane.launch_count()
     sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)  # let the sampler start before the timed region
+    if not args.no_clocks:
+        sampler.start()
+        time.sleep(0.3)  # let the sampler start before the timed region
     t_s = torch.cuda.Event(enable_timing=True)
     t_e = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -284,14 +287,16 @@ def run_ours(args):
     if pg is not None:
         torch.distributed.barrier()
     ms = t_s.elapsed_time(t_e) / args.steps
-    # keep the clock sampler fed for at least ~1 s of the same load
-    soak_until = time.perf_counter() + 1.0
-    while time.perf_counter() < soak_until:
-        for _ in range(20):
-            step()
-        torch.cuda.synchronize()
-    clocks = sampler.stop()
     launches = ane.launch_count() - launches0
+    clocks = None
+    if not args.no_clocks:
+        # keep the clock sampler fed for at least ~1 s of the same load
+        soak_until = time.perf_counter() + 1.0
+        while time.perf_counter() < soak_until:
+            for _ in range(20):
+                step()
+            torch.cuda.synchronize()
+        clocks = sampler.stop()
 
     if pg is not None:
         t = torch.tensor([ms], device=dev)
@@ -308,11 +313,20 @@ def run_ours(args):
     gemm_steps = max(20, args.steps)
     gemm_ms = time_events(lambda: ane.gemm_s8(Aq, Bt, scales, SCALE, RELU, out=C), gemm_steps, stream)
     gemm_tops = ops_per_rank / (gemm_ms * 1e-3) / 1e12
-    q_ms = time_events(lambda: ane.quantize_pair(A, B), max(10, args.steps // 4), stream)
+    qbufs = ane.quantize_pair(A, B)
+    partials = torch.empty(int(ane.lib.ane_absmax_partials_count(M * K, K * N)), dtype=torch.float32, device=dev)
+    sptr = ane._stream_ptr()
+
+    def quant_only():
+        ane.check(ane.lib.ane_quantize_pair_dev(M, N, K, A.data_ptr(), B.data_ptr(), qbufs[0].data_ptr(),
+                                                qbufs[1].data_ptr(), qbufs[2].data_ptr(), partials.data_ptr(), sptr))
+
+    quant_only()
+    q_ms = time_events(quant_only, max(10, args.steps // 4), stream)
 
     # ---- e2e through the reference-facing C ABI with pinned host buffers
     e2e = None
-    if rank == 0 or world > 1:
+    if not args.no_e2e:
         Ah = A.cpu().pin_memory()
         Bh = B.cpu().pin_memory()
         Ch = torch.empty((M, N), dtype=torch.float32).pin_memory()

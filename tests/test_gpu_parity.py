@@ -32,7 +32,17 @@ def bits_equal(a, b):
     a = np.ascontiguousarray(a, F32)
     b = np.ascontiguousarray(b, F32)
     nan = np.isnan(a) | np.isnan(b)
-    return np.array_equal(np.isnan(a), np.isnan(b)) and np.array_equal(a[~nan].view(np.uint32), b[~nan].view(np.uint32))
+    ok = np.array_equal(np.isnan(a), np.isnan(b)) and np.array_equal(a[~nan].view(np.uint32),
+                                                                     b[~nan].view(np.uint32))
+    if not ok and a.shape == b.shape:
+        diff = (a.view(np.uint32) != b.view(np.uint32)) & ~(np.isnan(a) & np.isnan(b))
+        idx = np.argwhere(diff)
+        print(f"bits_equal: {len(idx)} of {a.size} differ; first {idx[:8].tolist()}; "
+              f"got {a[diff][:8].tolist()} want {b[diff][:8].tolist()}")
+        if a.ndim == 2:
+            rows, cols = np.unique(idx[:, 0]), np.unique(idx[:, 1])
+            print(f"  rows {rows.min()}..{rows.max()} ({rows.size}), cols {cols.min()}..{cols.max()} ({cols.size})")
+    return ok
 
 
 def assert_close_rel(got, ref, rtol=REL_TOL):
