@@ -7,19 +7,27 @@
 //   y = float_rn(acc); y = y * (sa*sb); [y = y*scale | y = y + bias[n]]; fmax(...)
 // with every fp32 op a separate IEEE RN operation (no FMA contraction).
 //
-// Structure (one persistent CTA per SM, 192 threads, warp-specialised):
-//   warp 0      TMA producer: 128x128 A tile + 256x128 B tile (int8, SWIZZLE_128B)
-//               per stage into a 4-stage shared-memory ring, mbarrier complete_tx.
-//   warp 1      TMEM allocator + MMA issuer: one elected thread issues
-//               tcgen05.mma.cta_group::1.kind::i8 (M=128, N=256, K=32) x4 per
-//               stage into a TMEM accumulator; tcgen05.commit frees the stage.
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from their TMEM lane
-//               quarter, fp32 epilogue, stores.  Two TMEM accumulators (2x256
-//               columns) let the epilogue of tile i overlap the MMAs of tile i+1.
-// No TMA multicast anywhere (this code also runs in multi-GPU jobs).
+// Two kernels, both persistent and warp-specialised (192 threads per CTA):
+//   warp 0      TMA producer into a shared-memory ring (SWIZZLE_128B, K-major).
+//   warp 1      TMEM allocator + MMA issuer (one thread issues tcgen05.mma).
+//   warps 2..5  epilogue: tcgen05.ld from the TMEM lane quarter the warp may
+//               access, fp32 epilogue, then a 32x32 shared-memory transpose
+//               (XOR-swizzled 16-byte chunks) so every global store instruction
+//               writes four full 128-byte rows.
+// * gemm_s8_pair_kernel: CTA pairs (cluster of 2, tcgen05 cta_group::2), tile
+//   256 x 256.  Each CTA loads 128 rows of A and 128 rows of B^T per stage;
+//   the even CTA issues M=256,N=256,K=32 MMAs that read both CTAs' shared
+//   memory and write 128 accumulator rows into each CTA's TMEM.  Half the
+//   operand bytes per SM of a 1-CTA 128x256 tile.
+// * gemm_s8_single_kernel: one CTA, tile 128 x 256 (used when M <= 128).
+// Two TMEM accumulators (2 x 256 int32 columns) per CTA let the epilogue of
+// tile i overlap the MMAs of tile i+1.  No TMA multicast anywhere.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <float.h>
+
+#include <stdlib.h>
+#include <string.h>
 
 #include <mutex>
 
@@ -29,18 +37,22 @@
 namespace ane_b200 {
 namespace {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BK = 128;  // bytes = int8 elements = one 128-B swizzle row
 constexpr int UMMA_K = 32;
-constexpr int STAGES = 4;
-constexpr int A_STAGE = BM * BK;
-constexpr int B_STAGE = BN * BK;
-constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
-constexpr int ACC_COLS = BN;  // int32 accumulator columns per buffer
+constexpr int ACC_COLS = 256;
 constexpr int TMEM_COLS = 2 * ACC_COLS;
 constexpr int NUM_THREADS = 192;
+constexpr int EPI_STAGE_WORDS = 32 * 32;  // per epilogue warp
+constexpr int EPI_BYTES = 4 * EPI_STAGE_WORDS * 4;
 
+// single-CTA configuration
+constexpr int S_BM = 128, S_BN = 256, S_STAGES = 4;
+constexpr int S_A = S_BM * BK, S_B = S_BN * BK, S_STAGE = S_A + S_B;
+// CTA-pair configuration (per-CTA halves)
+constexpr int P_BM = 256, P_BN = 256, P_HM = 128, P_HN = 128, P_STAGES = 6;
+constexpr int P_A = P_HM * BK, P_B = P_HN * BK, P_STAGE = P_A + P_B;
+
+template <int STAGES>
 struct Barriers {
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
@@ -48,48 +60,139 @@ struct Barriers {
     uint64_t tmem_empty[2];
     uint32_t tmem_base;
 };
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + sizeof(Barriers) + 1024;
+constexpr size_t S_SMEM = (size_t)S_STAGES * S_STAGE + EPI_BYTES + sizeof(Barriers<S_STAGES>) + 1024;
+constexpr size_t P_SMEM = (size_t)P_STAGES * P_STAGE + EPI_BYTES + sizeof(Barriers<P_STAGES>) + 1024;
+static_assert(S_SMEM <= 232448 && P_SMEM <= 232448, "shared memory budget");
 
 struct Params {
     uint32_t M, N, K;
     uint32_t tiles_m, tiles_n, num_kb;
     void* C;
     size_t ldc;
+    int vec_ok;  // C rows allow 16-byte stores
     GemmEpilogue ep;
     int* err;
 };
 
-__device__ __forceinline__ float epi_f32(int32_t acc, float comb, const Params& p, uint32_t n) {
-    float y = __int2float_rn(acc);
-    y = __fmul_rn(y, comb);
-    if (p.ep.mode == kOutDenseI8) {
-        y = __fadd_rn(y, p.ep.bias[n]);
-        return arm_fmax(y, p.ep.relu ? 0.0f : -FLT_MAX);
-    }
-    y = __fmul_rn(y, p.ep.scale);
-    return p.ep.relu ? arm_fmax(y, 0.0f) : y;
+// max that propagates NaN (ARM FMAX, not IEEE maxNum); one instruction.
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+// ReLU with the reference's FMAX semantics: NaN stays NaN, and the "+ 0.0f"
+// turns a -0 result into +0 (FMAX(-0, +0) = +0) without changing anything else.
+__device__ __forceinline__ float relu_arm(float y) { return __fadd_rn(max_nan(y, 0.0f), 0.0f); }
+
+__device__ __forceinline__ float tile_comb(const Params& p) {
+    if (p.ep.mode == kOutRawI32) return 0.0f;
+    const float s0 = p.ep.scales ? p.ep.scales[0] : p.ep.sa_imm;
+    const float s1 = p.ep.scales ? p.ep.scales[1] : p.ep.sb_imm;
+    return __fmul_rn(s0, s1);
 }
 
+// One warp stores a 32 x 32 block: lane i holds row (row0 + i), columns nc..nc+31
+// as raw accumulators in r[].  Rows are transposed through this warp's
+// shared-memory stage so global stores are row-contiguous.
+__device__ __forceinline__ void store_block(const Params& p, float comb, const uint32_t (&r)[32], uint32_t* stage,
+                                            uint32_t row0, uint32_t nc, int lane) {
+    if (row0 >= p.M || nc >= p.N) return;  // warp-uniform
+    uint32_t v[32];
+    // The mode / relu branches are warp-uniform and hoisted out of the element
+    // loops; each loop is straight-line RN arithmetic.
+    if (p.ep.mode == kOutRawI32) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = r[j];
+    } else if (p.ep.mode == kOutFusedF32) {
+        const float scale = p.ep.scale;
+        if (p.ep.relu) {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                v[j] = __float_as_uint(relu_arm(__fmul_rn(__fmul_rn(__int2float_rn((int32_t)r[j]), comb), scale)));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                v[j] = __float_as_uint(__fmul_rn(__fmul_rn(__int2float_rn((int32_t)r[j]), comb), scale));
+        }
+    } else {
+        const float floor_v = p.ep.relu ? 0.0f : -FLT_MAX;
+        const float* bias = p.ep.bias + nc;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const float y = __fadd_rn(__fmul_rn(__int2float_rn((int32_t)r[j]), comb), nc + j < p.N ? bias[j] : 0.0f);
+            v[j] = __float_as_uint(p.ep.relu ? relu_arm(y) : max_nan(y, floor_v));
+        }
+    }
+    uint32_t* my_row = stage + lane * 32;
+#pragma unroll
+    for (int c = 0; c < 8; c++)
+        *reinterpret_cast<uint4*>(my_row + ((c ^ (lane & 7)) * 4)) =
+            make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    __syncwarp();
+    const uint32_t cc = lane & 7;
+    const uint32_t n = nc + 4 * cc;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint32_t rr = 4 * i + (lane >> 3);
+        const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * 32 + ((cc ^ (rr & 7)) * 4));
+        const uint32_t m = row0 + rr;
+        if (m < p.M && n < p.N) {
+            uint32_t* out = reinterpret_cast<uint32_t*>(p.C) + (size_t)m * p.ldc + n;
+            if (p.vec_ok && n + 4 <= p.N) {
+                *reinterpret_cast<uint4*>(out) = val;
+            } else {
+                out[0] = val.x;
+                if (n + 1 < p.N) out[1] = val.y;
+                if (n + 2 < p.N) out[2] = val.z;
+                if (n + 3 < p.N) out[3] = val.w;
+            }
+        }
+    }
+    __syncwarp();
+}
+
+// Drains one 128-row x 256-column TMEM accumulator of this CTA (warp = one lane
+// quarter) and stores it.  Calls `release()` right after the last TMEM read.
+template <class Release>
+__device__ __forceinline__ void drain_accumulator(const Params& p, uint32_t taddr, uint32_t row0, uint32_t n0,
+                                                  uint32_t* stage, int lane, Release release) {
+    const float comb = tile_comb(p);
+#pragma unroll 1
+    for (int c = 0; c < ACC_COLS / 32; c++) {
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(taddr + c * 32, r);
+        ptx::tmem_ld_wait();
+        if (c == ACC_COLS / 32 - 1) {
+            ptx::tc_fence_before();
+            __syncwarp();
+            release();
+        }
+        store_block(p, comb, r, stage, row0, n0 + c * 32, lane);
+    }
+}
+
+// ------------------------------------------------------------ 1-CTA kernel
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_s8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                      const Params p) {
+    gemm_s8_single_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                          const Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sa = smem;                              // STAGES x 16 KB
-    uint8_t* sb = smem + (size_t)STAGES * A_STAGE;   // STAGES x 32 KB
-    Barriers* bars = reinterpret_cast<Barriers*>(smem + (size_t)STAGES * STAGE_BYTES);
+    uint8_t* sa = smem;
+    uint8_t* sb = smem + (size_t)S_STAGES * S_A;
+    uint32_t* epi = reinterpret_cast<uint32_t*>(smem + (size_t)S_STAGES * S_STAGE);
+    auto* bars = reinterpret_cast<Barriers<S_STAGES>*>(smem + (size_t)S_STAGES * S_STAGE + EPI_BYTES);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t num_tiles = p.tiles_m * p.tiles_n;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; s++) {
+        for (int s = 0; s < S_STAGES; s++) {
             ptx::mbar_init(&bars->full[s], 1);
             ptx::mbar_init(&bars->empty[s], 1);
         }
         for (int a = 0; a < 2; a++) {
             ptx::mbar_init(&bars->tmem_full[a], 1);
-            ptx::mbar_init(&bars->tmem_empty[a], 4);  // one arrive per epilogue warp
+            ptx::mbar_init(&bars->tmem_empty[a], 4);
         }
         ptx::fence_mbarrier_init();
         ptx::prefetch_tmap(&tmap_a);
@@ -105,25 +208,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t tmem_base = bars->tmem_base;
 
     if (warp == 0) {
-        // ------------------------------------------------------------ producer
         if (lane == 0) {
             uint32_t stage = 0, phase = 0;
             bool alive = true;
             for (uint32_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
-                const int m0 = (int)((t / p.tiles_n) * BM), n0 = (int)((t % p.tiles_n) * BN);
+                const int m0 = (int)((t / p.tiles_n) * S_BM), n0 = (int)((t % p.tiles_n) * S_BN);
                 for (uint32_t kb = 0; kb < p.num_kb; kb++) {
                     if (!ptx::mbar_wait(&bars->empty[stage], phase ^ 1, p.err)) { alive = false; break; }
-                    ptx::mbar_arrive_expect_tx(&bars->full[stage], STAGE_BYTES);
-                    ptx::tma_load_2d(sa + (size_t)stage * A_STAGE, &tmap_a, &bars->full[stage], (int)(kb * BK), m0);
-                    ptx::tma_load_2d(sb + (size_t)stage * B_STAGE, &tmap_b, &bars->full[stage], (int)(kb * BK), n0);
-                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                    ptx::mbar_arrive_expect_tx(&bars->full[stage], S_STAGE);
+                    ptx::tma_load_2d(sa + (size_t)stage * S_A, &tmap_a, &bars->full[stage], (int)(kb * BK), m0);
+                    ptx::tma_load_2d(sb + (size_t)stage * S_B, &tmap_b, &bars->full[stage], (int)(kb * BK), n0);
+                    if (++stage == S_STAGES) { stage = 0; phase ^= 1; }
                 }
             }
         }
     } else if (warp == 1) {
-        // ---------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = ptx::idesc_s8s8s32(BM, BN);
+            constexpr uint32_t idesc = ptx::idesc_s8s8s32(S_BM, S_BN);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool alive = true;
             for (uint32_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
@@ -133,83 +234,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (uint32_t kb = 0; kb < p.num_kb; kb++) {
                     if (!ptx::mbar_wait(&bars->full[stage], phase, p.err)) { alive = false; break; }
                     ptx::tc_fence_after();
-                    const uint32_t a_addr = ptx::smem_u32(sa + (size_t)stage * A_STAGE);
-                    const uint32_t b_addr = ptx::smem_u32(sb + (size_t)stage * B_STAGE);
+                    const uint32_t a_addr = ptx::smem_u32(sa + (size_t)stage * S_A);
+                    const uint32_t b_addr = ptx::smem_u32(sb + (size_t)stage * S_B);
 #pragma unroll
-                    for (int k = 0; k < BK / UMMA_K; k++) {
-                        const uint64_t ad = ptx::sdesc_kmajor_sw128(a_addr + k * UMMA_K);
-                        const uint64_t bd = ptx::sdesc_kmajor_sw128(b_addr + k * UMMA_K);
-                        ptx::umma_i8(d_tmem, ad, bd, idesc, (kb | k) != 0);
-                    }
-                    ptx::umma_commit(&bars->empty[stage]);  // frees the smem stage when done
-                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                    for (int k = 0; k < BK / UMMA_K; k++)
+                        ptx::umma_i8(d_tmem, ptx::sdesc_kmajor_sw128(a_addr + k * UMMA_K),
+                                     ptx::sdesc_kmajor_sw128(b_addr + k * UMMA_K), idesc, (kb | k) != 0);
+                    ptx::umma_commit(&bars->empty[stage]);
+                    if (++stage == S_STAGES) { stage = 0; phase ^= 1; }
                 }
                 if (!alive) break;
-                ptx::umma_commit(&bars->tmem_full[acc]);  // accumulator ready for the epilogue
+                ptx::umma_commit(&bars->tmem_full[acc]);
                 acc ^= 1;
                 if (acc == 0) acc_phase ^= 1;
             }
         }
     } else {
-        // ------------------------------------------------------------ epilogue
-        const uint32_t quarter = (uint32_t)(warp & 3);  // TMEM lanes this warp may access
-        const uint32_t row_in_tile = quarter * 32 + lane;
+        const uint32_t quarter = (uint32_t)(warp & 3);
+        uint32_t* stage = epi + (warp - 2) * EPI_STAGE_WORDS;
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-            const uint32_t m0 = (t / p.tiles_n) * BM, n0 = (t % p.tiles_n) * BN;
+            const uint32_t m0 = (t / p.tiles_n) * S_BM, n0 = (t % p.tiles_n) * S_BN;
             if (!ptx::mbar_wait(&bars->tmem_full[acc], acc_phase, p.err)) break;
             ptx::tc_fence_after();
-            float comb = 0.0f;
-            if (p.ep.mode != kOutRawI32) {
-                const float s0 = p.ep.scales ? p.ep.scales[0] : p.ep.sa_imm;
-                const float s1 = p.ep.scales ? p.ep.scales[1] : p.ep.sb_imm;
-                comb = __fmul_rn(s0, s1);
-            }
-            const uint32_t m = m0 + row_in_tile;
             const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + acc * ACC_COLS;
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; c++) {
-                uint32_t r[32];
-                ptx::tmem_ld_32x32b_x32(taddr + c * 32, r);
-                ptx::tmem_ld_wait();
-                if (c == BN / 32 - 1) {
-                    // all TMEM reads of this accumulator are done: hand it back
-                    ptx::tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) ptx::mbar_arrive(&bars->tmem_empty[acc]);
-                }
-                const uint32_t nc = n0 + c * 32;
-                if (m >= p.M || nc >= p.N) continue;
-                if (p.ep.mode == kOutRawI32) {
-                    int32_t* out = reinterpret_cast<int32_t*>(p.C) + (size_t)m * p.ldc + nc;
-                    if (nc + 32 <= p.N && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<int4*>(out + j) = make_int4(r[j], r[j + 1], r[j + 2], r[j + 3]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (nc + j < p.N) out[j] = (int32_t)r[j];
-                    }
-                } else {
-                    float* out = reinterpret_cast<float*>(p.C) + (size_t)m * p.ldc + nc;
-                    if (nc + 32 <= p.N && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 v;
-                            v.x = epi_f32((int32_t)r[j + 0], comb, p, nc + j + 0);
-                            v.y = epi_f32((int32_t)r[j + 1], comb, p, nc + j + 1);
-                            v.z = epi_f32((int32_t)r[j + 2], comb, p, nc + j + 2);
-                            v.w = epi_f32((int32_t)r[j + 3], comb, p, nc + j + 3);
-                            *reinterpret_cast<float4*>(out + j) = v;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (nc + j < p.N) out[j] = epi_f32((int32_t)r[j], comb, p, nc + j);
-                    }
-                }
-            }
+            uint64_t* empty_bar = &bars->tmem_empty[acc];
+            drain_accumulator(p, taddr, m0 + quarter * 32, n0, stage, lane, [&] {
+                if (lane == 0) ptx::mbar_arrive(empty_bar);
+            });
             acc ^= 1;
             if (acc == 0) acc_phase ^= 1;
         }
@@ -220,6 +272,116 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// --------------------------------------------------------- CTA-pair kernel
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_s8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                        const Params p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sa = smem;
+    uint8_t* sb = smem + (size_t)P_STAGES * P_A;
+    uint32_t* epi = reinterpret_cast<uint32_t*>(smem + (size_t)P_STAGES * P_STAGE);
+    auto* bars = reinterpret_cast<Barriers<P_STAGES>*>(smem + (size_t)P_STAGES * P_STAGE + EPI_BYTES);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = ptx::cluster_ctarank();  // 0 = leader (issues the MMAs)
+    const uint32_t pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+    const uint32_t num_tiles = p.tiles_m * p.tiles_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; s++) {
+            ptx::mbar_init(&bars->full[s], 1);   // leader's producer arrive (+ tx of both CTAs)
+            ptx::mbar_init(&bars->empty[s], 1);  // one multicast commit per CTA
+        }
+        for (int a = 0; a < 2; a++) {
+            ptx::mbar_init(&bars->tmem_full[a], 1);
+            ptx::mbar_init(&bars->tmem_empty[a], 8);  // 4 epilogue warps x 2 CTAs (leader's copy is used)
+        }
+        ptx::fence_mbarrier_init();
+        ptx::prefetch_tmap(&tmap_a);
+        ptx::prefetch_tmap(&tmap_b);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc_cg2(&bars->tmem_base, TMEM_COLS);
+        ptx::tmem_relinquish_cg2();
+    }
+    ptx::tc_fence_before();
+    ptx::cluster_sync();
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = bars->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            bool alive = true;
+            for (uint32_t t = pair; t < num_tiles && alive; t += num_pairs) {
+                const int m0 = (int)((t / p.tiles_n) * P_BM + rank * P_HM);
+                const int n0 = (int)((t % p.tiles_n) * P_BN + rank * P_HN);
+                for (uint32_t kb = 0; kb < p.num_kb; kb++) {
+                    if (!ptx::mbar_wait(&bars->empty[stage], phase ^ 1, p.err)) { alive = false; break; }
+                    if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->full[stage], 2 * P_STAGE);
+                    const uint32_t full_leader = ptx::mapa_shared(ptx::smem_u32(&bars->full[stage]), 0);
+                    ptx::tma_load_2d_cg2(sa + (size_t)stage * P_A, &tmap_a, full_leader, (int)(kb * BK), m0);
+                    ptx::tma_load_2d_cg2(sb + (size_t)stage * P_B, &tmap_b, full_leader, (int)(kb * BK), n0);
+                    if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = ptx::idesc_s8s8s32(P_BM, P_BN);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool alive = true;
+            for (uint32_t t = pair; t < num_tiles && alive; t += num_pairs) {
+                if (!ptx::mbar_wait(&bars->tmem_empty[acc], acc_phase ^ 1, p.err)) break;
+                ptx::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+                for (uint32_t kb = 0; kb < p.num_kb; kb++) {
+                    if (!ptx::mbar_wait(&bars->full[stage], phase, p.err)) { alive = false; break; }
+                    ptx::tc_fence_after();
+                    const uint32_t a_addr = ptx::smem_u32(sa + (size_t)stage * P_A);
+                    const uint32_t b_addr = ptx::smem_u32(sb + (size_t)stage * P_B);
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; k++)
+                        ptx::umma_i8_cg2(d_tmem, ptx::sdesc_kmajor_sw128(a_addr + k * UMMA_K),
+                                         ptx::sdesc_kmajor_sw128(b_addr + k * UMMA_K), idesc, (kb | k) != 0);
+                    ptx::umma_commit_cg2_mc(&bars->empty[stage], 0x3);  // frees the stage in both CTAs
+                    if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+                }
+                if (!alive) break;
+                ptx::umma_commit_cg2_mc(&bars->tmem_full[acc], 0x3);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1;
+            }
+        }
+    } else {
+        const uint32_t quarter = (uint32_t)(warp & 3);
+        uint32_t* stage = epi + (warp - 2) * EPI_STAGE_WORDS;
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t t = pair; t < num_tiles; t += num_pairs) {
+            const uint32_t m0 = (t / p.tiles_n) * P_BM + rank * P_HM, n0 = (t % p.tiles_n) * P_BN;
+            if (!ptx::mbar_wait(&bars->tmem_full[acc], acc_phase, p.err)) break;
+            ptx::tc_fence_after();
+            const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + acc * ACC_COLS;
+            const uint32_t empty_leader = ptx::mapa_shared(ptx::smem_u32(&bars->tmem_empty[acc]), 0);
+            drain_accumulator(p, taddr, m0 + quarter * 32, n0, stage, lane, [&] {
+                if (lane == 0) ptx::mbar_arrive_cluster(empty_leader);
+            });
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1;
+        }
+    }
+
+    // Both CTAs are done with TMEM and with each other's shared memory only when
+    // every role of both has finished.
+    ptx::tc_fence_before();
+    ptx::cluster_sync();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc_cg2(tmem_base, TMEM_COLS);
     }
 }
 
@@ -283,47 +445,82 @@ int make_kmajor_map(CUtensorMap* map, const int8_t* base, uint32_t rows, uint32_
     return ANE_OK;
 }
 
+int set_smem_attr_once(const void* fn, size_t bytes, std::once_flag& flag, cudaError_t& err) {
+    std::call_once(flag, [&] { err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes); });
+    ANE_CUDA_TRY(err);
+    return ANE_OK;
+}
+
 }  // namespace
 
-int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const int8_t* Bt, void* C,
-                      size_t ldc, const GemmEpilogue& ep, cudaStream_t s) {
+int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const int8_t* Bt, void* C, size_t ldc,
+                      const GemmEpilogue& ep, cudaStream_t s) {
     if (M == 0 || N == 0) return ANE_OK;
     if (K == 0) return launch_fill_epilogue_zero_k(M, N, C, ldc, ep, s);
     ANE_ARG_CHECK(K % 16 == 0, "gemm: K must be a multiple of 16 (TMA row stride)");
     ANE_ARG_CHECK((reinterpret_cast<uintptr_t>(Aq) & 15) == 0 && (reinterpret_cast<uintptr_t>(Bt) & 15) == 0,
                   "gemm: int8 operands must be 16-byte aligned");
-    CUtensorMap ta, tb;
-    int rc = make_kmajor_map(&ta, Aq, M, K, BM);
-    if (rc) return rc;
-    rc = make_kmajor_map(&tb, Bt, N, K, BN);
-    if (rc) return rc;
-    static std::once_flag attr_once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(attr_once, [] {
-        attr_err = cudaFuncSetAttribute(gemm_s8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)SMEM_BYTES);
-    });
-    ANE_CUDA_TRY(attr_err);
     Params p;
     p.M = M;
     p.N = N;
     p.K = K;
-    p.tiles_m = (M + BM - 1) / BM;
-    p.tiles_n = (N + BN - 1) / BN;
     p.num_kb = (K + BK - 1) / BK;
     p.C = C;
     p.ldc = ldc;
+    p.vec_ok = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
     p.ep = ep;
     p.err = device_timeout_flag();
+    const int sms = num_sms();
+    // ANE_GEMM_KERNEL=single|pair overrides the shape-based choice (tuning aid).
+    static const char* force = getenv("ANE_GEMM_KERNEL");
+    bool pair = M > (uint32_t)S_BM;
+    if (force && !strcmp(force, "single")) pair = false;
+    if (force && !strcmp(force, "pair")) pair = true;
+    CUtensorMap ta, tb;
+    int rc = make_kmajor_map(&ta, Aq, M, K, pair ? P_HM : S_BM);
+    if (rc) return rc;
+    rc = make_kmajor_map(&tb, Bt, N, K, pair ? P_HN : S_BN);
+    if (rc) return rc;
+    if (!pair) {
+        static std::once_flag f;
+        static cudaError_t e;
+        rc = set_smem_attr_once((const void*)gemm_s8_single_kernel, S_SMEM, f, e);
+        if (rc) return rc;
+        p.tiles_m = (M + S_BM - 1) / S_BM;
+        p.tiles_n = (N + S_BN - 1) / S_BN;
+        const uint32_t tiles = p.tiles_m * p.tiles_n;
+        const uint32_t grid = tiles < (uint32_t)sms ? tiles : (uint32_t)sms;
+        gemm_s8_single_kernel<<<grid, NUM_THREADS, S_SMEM, s>>>(ta, tb, p);
+        ANE_CHECK_LAUNCH();
+        return ANE_OK;
+    }
+    static std::once_flag f2;
+    static cudaError_t e2;
+    rc = set_smem_attr_once((const void*)gemm_s8_pair_kernel, P_SMEM, f2, e2);
+    if (rc) return rc;
+    p.tiles_m = (M + P_BM - 1) / P_BM;
+    p.tiles_n = (N + P_BN - 1) / P_BN;
     const uint32_t tiles = p.tiles_m * p.tiles_n;
-    const uint32_t grid = tiles < (uint32_t)num_sms() ? tiles : (uint32_t)num_sms();
-    gemm_s8_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(ta, tb, p);
+    uint32_t pairs = (uint32_t)sms / 2;
+    if (pairs > tiles) pairs = tiles;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = P_SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_s8_pair_kernel, ta, tb, p));
     ANE_CHECK_LAUNCH();
     return ANE_OK;
 }
 
-int launch_fill_epilogue_zero_k(uint32_t M, uint32_t N, void* C, size_t ldc, const GemmEpilogue& ep,
-                                cudaStream_t s) {
+int launch_fill_epilogue_zero_k(uint32_t M, uint32_t N, void* C, size_t ldc, const GemmEpilogue& ep, cudaStream_t s) {
     const size_t total = (size_t)M * N;
     if (total == 0) return ANE_OK;
     int g = (int)ceil_div(total, 256 * 4);

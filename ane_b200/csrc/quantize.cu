@@ -76,15 +76,17 @@ __global__ void __launch_bounds__(kThreads) absmax_partials_kernel(const float* 
         const size_t n4 = n / 4;
         const float4* x4 = reinterpret_cast<const float4*>(x);
         size_t i = tid;
-        // two independent loads in flight per iteration
+        // Two independent loads in flight per iteration.  Plain (L2-allocating)
+        // loads: the quantize pass re-reads these tensors back to front, so the
+        // tail of this pass is still L2-resident when it starts.
         for (; i + stride < n4; i += 2 * stride) {
-            float4 v = __ldcs(x4 + i);
-            float4 u = __ldcs(x4 + i + stride);
+            float4 v = __ldg(x4 + i);
+            float4 u = __ldg(x4 + i + stride);
             m = max(m, max(max(absbits(v.x), absbits(v.y)), max(absbits(v.z), absbits(v.w))));
             m = max(m, max(max(absbits(u.x), absbits(u.y)), max(absbits(u.z), absbits(u.w))));
         }
         for (; i < n4; i += stride) {
-            float4 v = __ldcs(x4 + i);
+            float4 v = __ldg(x4 + i);
             m = max(m, max(max(absbits(v.x), absbits(v.y)), max(absbits(v.z), absbits(v.w))));
         }
         for (size_t j = n4 * 4 + tid; j < n; j += stride) m = max(m, absbits(x[j]));
@@ -110,18 +112,35 @@ __device__ void quantize_rows(const float* __restrict__ src, int8_t* __restrict_
     const bool vec = (K % 16 == 0) && (ld == K) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
     if (vec) {
+        // 16 elements -> one 16-byte store per chunk; walked from the end so the
+        // first chunks read are the ones the absmax pass left in L2; two chunks
+        // (eight 16-byte loads) in flight per thread.
         const size_t chunks = (size_t)rows * K / 16;
         const float4* s4 = reinterpret_cast<const float4*>(src);
         uint4* d16 = reinterpret_cast<uint4*>(dst);
-        for (size_t c = tid; c < chunks; c += stride) {
-            float4 v0 = __ldcs(s4 + 4 * c + 0), v1 = __ldcs(s4 + 4 * c + 1);
-            float4 v2 = __ldcs(s4 + 4 * c + 2), v3 = __ldcs(s4 + 4 * c + 3);
+        auto quant16 = [&](size_t c, const float4& v0, const float4& v1, const float4& v2, const float4& v3) {
             uint4 o;
             o.x = pack4(v0.x, v0.y, v0.z, v0.w, inv);
             o.y = pack4(v1.x, v1.y, v1.z, v1.w, inv);
             o.z = pack4(v2.x, v2.y, v2.z, v2.w, inv);
             o.w = pack4(v3.x, v3.y, v3.z, v3.w, inv);
             d16[c] = o;
+        };
+        size_t j = tid;
+        for (; j + stride < chunks; j += 2 * stride) {
+            const size_t c0 = chunks - 1 - j, c1 = chunks - 1 - (j + stride);
+            float4 a0 = __ldcs(s4 + 4 * c0 + 0), a1 = __ldcs(s4 + 4 * c0 + 1);
+            float4 a2 = __ldcs(s4 + 4 * c0 + 2), a3 = __ldcs(s4 + 4 * c0 + 3);
+            float4 b0 = __ldcs(s4 + 4 * c1 + 0), b1 = __ldcs(s4 + 4 * c1 + 1);
+            float4 b2 = __ldcs(s4 + 4 * c1 + 2), b3 = __ldcs(s4 + 4 * c1 + 3);
+            quant16(c0, a0, a1, a2, a3);
+            quant16(c1, b0, b1, b2, b3);
+        }
+        for (; j < chunks; j += stride) {
+            const size_t c0 = chunks - 1 - j;
+            float4 a0 = __ldcs(s4 + 4 * c0 + 0), a1 = __ldcs(s4 + 4 * c0 + 1);
+            float4 a2 = __ldcs(s4 + 4 * c0 + 2), a3 = __ldcs(s4 + 4 * c0 + 3);
+            quant16(c0, a0, a1, a2, a3);
         }
     } else {
         const size_t total = (size_t)rows * ld;
@@ -134,42 +153,62 @@ __device__ void quantize_rows(const float* __restrict__ src, int8_t* __restrict_
 
 // ------------------------------------------------ transposing quantize of B
 // B is K x N fp32 row-major; Bt is N x ld int8 (ld = K16), Bt[n][k] = q(B[k][n]),
-// zero for K <= k < ld.  64x64 tiles through shared memory: coalesced 128-B
-// fp32 reads along n, 16-B int8 writes along k.
-static constexpr int kTT = 64;
-static constexpr int kTPitch = kTT + 4;  // bytes; 17 words -> conflict-free column writes
+// zero for K <= k < ld.  Tiles of 128 (k) x 32 (n) through shared memory:
+// each thread issues its four 16-byte loads (rows k, k+32, k+64, k+96; 4-column
+// group) back to back, quantizes, scatters the bytes into a transposed tile
+// (pitch 132 B = 33 words: conflict-free both ways), then each n-row of the tile
+// leaves as one full 128-byte line.  Tiles are walked from the highest k down,
+// the reverse of the absmax pass, to hit its L2-resident tail first.
+static constexpr int kTK = 128, kTN = 32;
+static constexpr int kTPitch = kTK + 4;
 
 __device__ void quantize_transpose(const float* __restrict__ B, int8_t* __restrict__ Bt, uint32_t K,
                                    uint32_t N, uint32_t ld, float inv, int bid, int nblk) {
-    __shared__ __align__(16) uint8_t tile[kTT * kTPitch];
-    const uint32_t tiles_k = (ld + kTT - 1) / kTT, tiles_n = (N + kTT - 1) / kTT;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (uint32_t t = bid; t < tiles_k * tiles_n; t += nblk) {
-        const uint32_t k0 = (t / tiles_n) * kTT, n0 = (t % tiles_n) * kTT;
-        __syncthreads();
+    __shared__ __align__(16) uint8_t tile[kTN * kTPitch];
+    const uint32_t tiles_k = (ld + kTK - 1) / kTK, tiles_n = (N + kTN - 1) / kTN;
+    const uint32_t num_tiles = tiles_k * tiles_n;
+    const uint32_t t8 = threadIdx.x & 7, r0 = threadIdx.x >> 3;  // 4-column group, first row
+    const bool vec = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(B) & 15) == 0);
+    for (uint32_t it = bid; it < num_tiles; it += nblk) {
+        const uint32_t t = num_tiles - 1 - it;
+        const uint32_t k0 = (t / tiles_n) * kTK, n0 = (t % tiles_n) * kTN;
+        const uint32_t n = n0 + 4 * t8;
+        float4 v[4];
 #pragma unroll
-        for (int i = 0; i < kTT / 8; i++) {
-            const uint32_t kl = warp + 8 * i, k = k0 + kl;
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const uint32_t nl = lane + 32 * h, n = n0 + nl;
-                int8_t q = 0;
-                if (k < K && n < N) q = quantize_one(__ldcs(B + (size_t)k * N + n), inv);
-                tile[nl * kTPitch + kl] = (uint8_t)q;
+        for (int i = 0; i < 4; i++) {
+            const uint32_t k = k0 + r0 + 32 * i;
+            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k < K) {
+                const float* src = B + (size_t)k * N + n;
+                if (vec && n + 4 <= N) {
+                    v[i] = __ldcs(reinterpret_cast<const float4*>(src));
+                } else {
+                    if (n + 0 < N) v[i].x = __ldcs(src + 0);
+                    if (n + 1 < N) v[i].y = __ldcs(src + 1);
+                    if (n + 2 < N) v[i].z = __ldcs(src + 2);
+                    if (n + 3 < N) v[i].w = __ldcs(src + 3);
+                }
             }
         }
+        __syncthreads();  // previous tile's reads of `tile` are done
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t kl = r0 + 32 * i;
+            const bool kin = k0 + kl < K;  // zero padding K <= k < ld
+            uint8_t* col = tile + (4 * t8) * kTPitch + kl;
+            col[0 * kTPitch] = kin ? (uint8_t)quantize_one(v[i].x, inv) : 0;
+            col[1 * kTPitch] = kin ? (uint8_t)quantize_one(v[i].y, inv) : 0;
+            col[2 * kTPitch] = kin ? (uint8_t)quantize_one(v[i].z, inv) : 0;
+            col[3 * kTPitch] = kin ? (uint8_t)quantize_one(v[i].w, inv) : 0;
+        }
         __syncthreads();
-        const uint32_t nl = threadIdx.x >> 2, kc = (threadIdx.x & 3) * 16;
-        const uint32_t n = n0 + nl, k = k0 + kc;
-        if (n < N && k < ld) {
+        const uint32_t nl = threadIdx.x >> 3, kc = (threadIdx.x & 7) * 16;
+        const uint32_t nn = n0 + nl, k = k0 + kc;
+        if (nn < N && k < ld) {
             const uint32_t* src = reinterpret_cast<const uint32_t*>(tile + nl * kTPitch + kc);
-            uint4 o = make_uint4(src[0], src[1], src[2], src[3]);
-            if (k + 16 <= ld) {
-                *reinterpret_cast<uint4*>(Bt + (size_t)n * ld + k) = o;
-            } else {  // ld is a multiple of 16, so this only guards odd callers
-                const uint8_t* ob = reinterpret_cast<const uint8_t*>(&o);
-                for (uint32_t j = 0; k + j < ld; j++) Bt[(size_t)n * ld + k + j] = (int8_t)ob[j];
-            }
+            const uint4 o = make_uint4(src[0], src[1], src[2], src[3]);
+            // ld is a multiple of 16, so a 16-byte chunk is either all in or all out
+            *reinterpret_cast<uint4*>(Bt + (size_t)nn * ld + k) = o;
         }
     }
 }
@@ -275,12 +314,12 @@ int launch_quantize_pair(uint32_t M, uint32_t N, uint32_t K, uint32_t K16, const
     const size_t work_a = (size_t)M * K16, work_b = (size_t)N * K16;
     const int sms = num_sms();
     // split ~4 waves of blocks between the two tensors in proportion to their size
-    int total = sms * 4;
+    int total = sms * 8;  // 8 resident 256-thread blocks per SM
     int ba = (int)((double)total * (double)work_a / (double)(work_a + work_b + 1));
     if (ba < 1) ba = 1;
     int bb = total - ba;
     if (bb < 1) bb = 1;
-    size_t tiles_b = ceil_div(K16, kTT) * ceil_div(N, kTT);
+    size_t tiles_b = ceil_div(K16, kTK) * ceil_div(N, kTN);
     if ((size_t)bb > tiles_b) bb = (int)tiles_b;
     if (bb < 1) bb = 1;
     quantize_pair_kernel<<<ba + bb, kThreads, 0, s>>>(A, B, Aq, Bt, scales, partials, M, N, K, K16,
