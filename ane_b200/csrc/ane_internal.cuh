@@ -1,5 +1,6 @@
 // ane_internal.cuh -- shared host/device helpers of libane_b200 (not installed).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -55,6 +56,12 @@ int require_sm100();
 // Device-side bounded-wait failure counter (incremented by kernels that give up).
 int read_and_reset_device_timeouts(cudaStream_t s);
 int* device_timeout_flag();  // device address of the counter
+
+// 2-D TMA tensor map: `outer` rows of `inner` elements, row stride in bytes
+// (multiple of 16), box of box_inner x box_outer elements, zero OOB fill.
+int encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+                         uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                         CUtensorMapSwizzle swizzle);
 
 // ------------------------------------------------------- small math helpers
 __host__ __device__ inline size_t ceil_div(size_t a, size_t b) { return (a + b - 1) / b; }

@@ -411,38 +411,10 @@ __global__ void fill_zero_k_kernel(uint32_t M, uint32_t N, void* C, size_t ldc, 
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
 // K-major int8 operand: `rows` x K (row stride K bytes), box = box_rows x BK.
 int make_kmajor_map(CUtensorMap* map, const int8_t* base, uint32_t rows, uint32_t K, uint32_t box_rows) {
-    auto enc = tensor_map_encoder();
-    if (!enc) {
-        set_status(ANE_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
-        return ANE_ERR_CUDA;
-    }
-    cuuint64_t dims[2] = {K, rows};
-    cuuint64_t strides[1] = {K};
-    cuuint32_t box[2] = {BK, box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-        set_status(ANE_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
-        return ANE_ERR_CUDA;
-    }
-    return ANE_OK;
+    return encode_tensor_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, K, rows, K, BK, box_rows,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 int set_smem_attr_once(const void* fn, size_t bytes, std::once_flag& flag, cudaError_t& err) {
