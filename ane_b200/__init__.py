@@ -54,6 +54,7 @@ SIGNATURES = {
     "ane_q8_0_gemv": (_i32, [_u32, _u32, _vp, _vp, _vp]),
     "ane_dense_fused_i8_workspace_size": (_sz, [_u32, _u32, _u32]),
     "ane_dense_fused_i8_dev": (_i32, [_u32, _u32, _u32, _f, _u8, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "ane_dense_fused_i8_noalloc_dev": (_i32, [_u32, _u32, _u32, _f, _u8, _vp, _vp, _vp, _vp]),
     "ane_absmax_partials_count": (_sz, [_sz, _sz]),
     "ane_quantize_pair_dev": (_i32, [_u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ane_absmax_pair_dev": (_i32, [_vp, _sz, _vp, _sz, _vp, _vp, _vp]),

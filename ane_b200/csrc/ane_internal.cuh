@@ -57,6 +57,33 @@ int require_sm100();
 int read_and_reset_device_timeouts(cudaStream_t s);
 int* device_timeout_flag();  // device address of the counter
 
+// While a ScopedLaunchOverride is alive on a thread, num_sms() and
+// device_timeout_flag() return its values instead of touching the lazily
+// initialised per-device state (which allocates on first use).
+struct LaunchOverride {
+    int sms;
+    int* err;
+};
+class ScopedLaunchOverride {
+public:
+    explicit ScopedLaunchOverride(const LaunchOverride* o);
+    ~ScopedLaunchOverride();
+
+private:
+    const LaunchOverride* prev_;
+};
+
+// dense_fused_i8 on a stream with a caller-provided workspace (layout below).
+struct FusedWs {
+    int8_t* Aq;
+    int8_t* Bt;
+    float* scales;
+    float* partials;
+};
+size_t fused_ws_layout(uint32_t M, uint32_t N, uint32_t K, FusedWs* w, void* base);
+int dense_fused_on_stream(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t relu, const float* A,
+                          const float* B, float* C, void* ws, cudaStream_t s);
+
 // 2-D TMA tensor map: `outer` rows of `inner` elements, row stride in bytes
 // (multiple of 16), box of box_inner x box_outer elements, zero OOB fill.
 int encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,

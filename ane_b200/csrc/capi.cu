@@ -158,12 +158,8 @@ int run_staged(std::vector<Arg>& args, size_t extra_bytes, Body body) {
 
 inline size_t a256(size_t n) { return round_up(n, 256); }
 
-struct FusedWs {
-    int8_t* Aq;
-    int8_t* Bt;
-    float* scales;
-    float* partials;
-};
+}  // namespace
+
 size_t fused_ws_layout(uint32_t M, uint32_t N, uint32_t K, FusedWs* w, void* base) {
     const size_t K16 = round_up(K, 16);
     const size_t pcount = ane_absmax_partials_count((size_t)M * K, (size_t)K * N);
@@ -200,7 +196,11 @@ int dense_fused_on_stream(uint32_t M, uint32_t N, uint32_t K, float scale, uint8
     return launch_gemm_s8_tc(M, N, K16, w.Aq, w.Bt, C, N, ep, s);
 }
 
+namespace {
+thread_local const LaunchOverride* t_override = nullptr;
 }  // namespace
+ScopedLaunchOverride::ScopedLaunchOverride(const LaunchOverride* o) : prev_(t_override) { t_override = o; }
+ScopedLaunchOverride::~ScopedLaunchOverride() { t_override = prev_; }
 
 // --------------------------------------------------------------- status API
 void set_status(int code, const std::string& msg) {
@@ -217,6 +217,7 @@ int ok() {
     return ANE_OK;
 }
 int num_sms() {
+    if (t_override) return t_override->sms;
     int s = device_info().sms;
     return s > 0 ? s : 148;
 }
@@ -233,7 +234,10 @@ int require_sm100() {
     }
     return ANE_OK;
 }
-int* device_timeout_flag() { return device_info().timeout_flag; }
+int* device_timeout_flag() {
+    if (t_override) return t_override->err;
+    return device_info().timeout_flag;
+}
 int read_and_reset_device_timeouts(cudaStream_t s) {
     int* f = device_timeout_flag();
     if (!f) return 0;

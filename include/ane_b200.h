@@ -118,6 +118,21 @@ int ane_dense_i8_dev(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uin
 int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out,
                       void* stream);
 
+/* dense_fused_i8 without any allocation.  No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory when they run the op
+ * (a framework that already reserved nearly all GPU memory for its own pool, a
+ * ggml-style backend inside graph_compute, latency-critical loops where
+ * cudaMalloc/cudaFree would synchronise).  Same arguments and results as
+ * ane_dense_fused_i8_dev, but the scratch is one fixed 40 MiB device array
+ * inside the library (enough for M = N = K = 4096); a problem whose
+ * ane_dense_fused_i8_workspace_size exceeds it returns ANE_ERR_INVALID_ARGUMENT.
+ * Every GPU that loads this part of the library keeps the 40 MiB until exit.
+ * All calls on a device share the array: calls whose kernels overlap on the
+ * GPU race, so serialise them.  The first call on each device looks the array
+ * up (cudaGetSymbolAddress); make it before any stream capture. */
+int ane_dense_fused_i8_noalloc_dev(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t relu,
+                                   const float* A, const float* B, float* C, void* stream);
+
 /* ------------------------------------------------------------ diagnostics */
 /* Device-side bounded-wait failures since the last call (and reset). */
 int ane_device_timeouts(void);
