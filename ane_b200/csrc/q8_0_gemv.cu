@@ -116,6 +116,9 @@ static constexpr int kChunkBlocks = 16;
 static constexpr int kChunkBytes = kChunkBlocks * 34;  // 544 = 34 x 16
 static constexpr int kChunkXBytes = kChunkBlocks * 32 * 4;
 static constexpr int kSlots = 4;
+// TMA shared-memory destinations must be 128-byte aligned: every slot is
+// rows*544 + 2048 bytes with rows a multiple of 4 (4*544 = 17*128).
+static_assert((4 * kChunkBytes) % 128 == 0 && kChunkXBytes % 128 == 0, "slot alignment");
 
 // q as fp32 from the biased byte: 0x4700_uu00 = 32768 + u = 32896 + q, minus
 // 32896 (exact).  Then q*d is one RN multiply, exact for finite d and the same
