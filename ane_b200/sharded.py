@@ -5,28 +5,92 @@ Partitioning: every rank holds the full A (M x K) and a column shard of B
 The only cross-rank dependencies are
 
 1. the per-tensor absmax: each rank reduces its local absmax of A and B into
-   two floats (ane_absmax_pair_dev) and the ranks all-reduce them with MAX, so
-   every shard is quantized with exactly the scales a single GPU would use;
-2. the output: the M x N_local shards are all-gathered and interleaved into the
-   row-major M x (world*N_local) result.
+   two floats and the ranks all-reduce them with MAX, so every shard is
+   quantized with exactly the scales one GPU would compute;
+2. the output (optional): the M x N_local shards are all-gathered and
+   interleaved into the row-major M x (world*N_local) result.
 
 Because the global scales are identical and all per-element arithmetic is
 unchanged, the sharded result is bit-identical to the 1-GPU dense_fused_i8.
-The collectives go through torch.distributed (NCCL); the compute is
-libane_b200's kernels.
+
+`ShardPlan` holds the collective orchestration and is independent of where
+the compute runs (the CPU tests drive it with gloo ranks and the oracle);
+`ShardedDense` binds it to libane_b200's kernels and NCCL.
 """
 from __future__ import annotations
+
+from typing import Callable
 
 import torch
 import torch.distributed as dist
 
-import ane_b200 as ane
+
+def global_absmax(local_absmax2: torch.Tensor, group=None) -> torch.Tensor:
+    """All-reduce (MAX) the per-rank absmax of A and of B, in place.
+
+    The values are non-negative floats or NaN, whose bit patterns order as
+    integers exactly like the reference's propagating max (NaN > inf >
+    finite); reducing the int32 view keeps a NaN on any rank, which a float
+    MAX collective may drop."""
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(local_absmax2.view(torch.int32), op=dist.ReduceOp.MAX, group=group)
+    return local_absmax2
+
+
+def interleave_shards(gathered: torch.Tensor) -> torch.Tensor:
+    """[world, M, N_local] -> [M, world * N_local] (column shards side by side)."""
+    world, M, n_local = gathered.shape
+    return gathered.permute(1, 0, 2).reshape(M, world * n_local)
+
+
+class ShardPlan:
+    """Collective steps of the sharded op around two compute callables:
+    absmax2(A_part, B_part) -> float[2] (local absmax of the two operands) and
+    quantize_gemm(A_part, B_part, absmax2) -> C_part.
+
+    shard="cols": every rank has all of A and a column block of B; C blocks are
+    interleaved after the gather.  shard="rows": every rank has a row block of
+    A and all of B; the gathered row blocks are already the row-major C."""
+
+    def __init__(self, world: int, group=None, shard: str = "cols"):
+        assert shard in ("cols", "rows")
+        self.world = world
+        self.group = group
+        self.shard = shard
+
+    def run(self, A, B, absmax2_fn: Callable, quantize_gemm_fn: Callable, gather: bool = True,
+            gathered_out: torch.Tensor | None = None):
+        absmax2 = global_absmax(absmax2_fn(A, B), self.group)
+        C_local = quantize_gemm_fn(A, B, absmax2)
+        if not gather:
+            return C_local
+        if self.world > 1:
+            if gathered_out is None:
+                gathered_out = torch.empty((self.world,) + tuple(C_local.shape), dtype=C_local.dtype,
+                                           device=C_local.device)
+            if gathered_out.is_cuda:
+                dist.all_gather_into_tensor(gathered_out, C_local, group=self.group)
+            else:  # gloo has no all_gather_into_tensor
+                dist.all_gather(list(gathered_out.unbind(0)), C_local, group=self.group)
+            if self.shard == "rows":
+                return gathered_out.view(self.world * C_local.shape[0], C_local.shape[1])
+            return interleave_shards(gathered_out)
+        return C_local
 
 
 class ShardedDense:
-    def __init__(self, M: int, N_local: int, K: int, world: int, device, group=None):
+    """dense_fused_i8 over this rank's part on its GPU.
+
+    shard="cols": operands A (M x K) and a column block of B (K x N_local).
+    shard="rows": operands a row block of A (M x K, M = rows per rank) and all
+    of B (K x N_local, N_local = N)."""
+
+    def __init__(self, M: int, N_local: int, K: int, world: int, device, group=None, shard: str = "cols"):
+        import ane_b200 as ane
+
+        self.ane = ane
         self.M, self.N_local, self.K, self.world = M, N_local, K, world
-        self.group = group
+        self.plan = ShardPlan(world, group, shard)
         K16 = (K + 15) // 16 * 16
         self.absmax2 = torch.empty(2, dtype=torch.float32, device=device)
         self.partials = torch.empty(int(ane.lib.ane_absmax_partials_count(M * K, K * N_local)),
@@ -37,22 +101,21 @@ class ShardedDense:
         self.C_local = torch.empty((M, N_local), dtype=torch.float32, device=device)
         self.gathered = torch.empty((world, M, N_local), dtype=torch.float32, device=device)
 
+    def _absmax2(self, A, B_local):
+        ane = self.ane
+        ane.check(ane.lib.ane_absmax_pair_dev(A.data_ptr(), self.M * self.K, B_local.data_ptr(),
+                                              self.K * self.N_local, self.absmax2.data_ptr(),
+                                              self.partials.data_ptr(), ane._stream_ptr()))
+        return self.absmax2
+
     def forward(self, A, B_local, scale: float = 1.0, relu: bool = False, gather: bool = True):
-        M, N_local, K = self.M, self.N_local, self.K
-        s = ane._stream_ptr()
-        ane.check(ane.lib.ane_absmax_pair_dev(A.data_ptr(), M * K, B_local.data_ptr(), K * N_local,
-                                              self.absmax2.data_ptr(), self.partials.data_ptr(), s))
-        if self.world > 1:
-            dist.all_reduce(self.absmax2, op=dist.ReduceOp.MAX, group=self.group)
-        ane.check(ane.lib.ane_quantize_pair_absmax_dev(M, N_local, K, A.data_ptr(), B_local.data_ptr(),
-                                                       self.Aq.data_ptr(), self.Bt.data_ptr(),
-                                                       self.absmax2.data_ptr(), self.scales.data_ptr(), s))
-        ane.gemm_s8(self.Aq, self.Bt, self.scales, scale, relu, out=self.C_local)
-        if not gather:
-            return self.C_local
-        if self.world > 1:
-            dist.all_gather_into_tensor(self.gathered, self.C_local, group=self.group)
-        else:
-            self.gathered[0].copy_(self.C_local)
-        # [world, M, N_local] -> [M, world * N_local]
-        return self.gathered.permute(1, 0, 2).reshape(M, self.world * N_local)
+        ane = self.ane
+
+        def quantize_gemm(A, B_local, absmax2):
+            ane.check(ane.lib.ane_quantize_pair_absmax_dev(self.M, self.N_local, self.K, A.data_ptr(),
+                                                           B_local.data_ptr(), self.Aq.data_ptr(),
+                                                           self.Bt.data_ptr(), absmax2.data_ptr(),
+                                                           self.scales.data_ptr(), ane._stream_ptr()))
+            return ane.gemm_s8(self.Aq, self.Bt, self.scales, scale, relu, out=self.C_local)
+
+        return self.plan.run(A, B_local, self._absmax2, quantize_gemm, gather, self.gathered)

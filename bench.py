@@ -17,10 +17,11 @@ Also reported on the same line:
 * cpu_baseline: the oracle's OpenMP restatement on the host cores, on a
   bounded sample of the same workload.
 
-Multi-GPU (torchrun, N > 1): every rank holds A and a 4096-column shard of B
-(weak scaling, per-rank work fixed); the global absmax is an NCCL all-reduce
-(MAX) of two floats, each rank runs the GEMM on its shard and the M x N output
-shards are NCCL all-gathered -- bit-identical to the 1-GPU result.
+Multi-GPU (torchrun, N > 1): every rank holds a 4096-row block of A and all of
+B (weak scaling, per-rank work = the 1-GPU step); the global absmax is an NCCL
+all-reduce (MAX) of the two absmax bit patterns, each rank runs the GEMM on its
+rows and the row blocks of C are NCCL all-gathered (already row-major) --
+bit-identical to one GPU running the (N*4096) x 4096 x 4096 problem.
 
 `--impl reference` times the reference's CPU semantics (the oracle, kind
 "port": the reference's SME2 assembly cannot run on x86) on the same config.
@@ -42,6 +43,9 @@ sys.path.insert(0, ROOT)
 METRIC = "int8 GEMM TOPS (4096³) & Q8_0 matvec GB/s at 1/2/4/8 B200"
 M = N = K = 4096
 SCALE, RELU = 1.0, False
+# DRAM read + write of one gemm_s8_pair_kernel launch at 4096^3, from the ncu
+# capture summarised in profiles/gemm_s8_pair_dense_fused_4096.md
+GEMM_TRAFFIC_BYTES = 34_202_880 + 18_851_584
 
 
 def parse():
@@ -245,10 +249,11 @@ def run_ours(args):
     int8_peak = 2.0 * peaks["bf16_tflops"]
     stream = torch.cuda.current_stream()
 
-    g = torch.Generator(device=dev).manual_seed(1234)
+    # world > 1: this rank's row block of A (its own seed) and the full B (same seed everywhere)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
     A = torch.randn((M, K), device=dev, generator=g)
-    g2 = torch.Generator(device=dev).manual_seed(5678 + rank)
-    B = torch.randn((K, N), device=dev, generator=g2)  # this rank's column shard of B when world > 1
+    g2 = torch.Generator(device=dev).manual_seed(5678)
+    B = torch.randn((K, N), device=dev, generator=g2)
     C = torch.empty((M, N), device=dev)
     ws = ane.dense_fused_i8_workspace(M, N, K, dev)
 
@@ -258,7 +263,7 @@ def run_ours(args):
     else:
         from ane_b200 import sharded
 
-        ctx = sharded.ShardedDense(M, N, K, world, dev, pg)
+        ctx = sharded.ShardedDense(M, N, K, world, dev, pg, shard="rows")
 
         def step():
             ctx.forward(A, B, SCALE, RELU)
@@ -288,23 +293,27 @@ def run_ours(args):
         torch.distributed.barrier()
     ms = t_s.elapsed_time(t_e) / args.steps
     launches = ane.launch_count() - launches0
-    clocks = None
-    if not args.no_clocks:
-        # keep the clock sampler fed for at least ~1 s of the same load
-        soak_until = time.perf_counter() + 1.0
-        while time.perf_counter() < soak_until:
-            for _ in range(20):
-                step()
-            torch.cuda.synchronize()
-        clocks = sampler.stop()
-
     if pg is not None:
         t = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
+    clocks = None
+    if not args.no_clocks:
+        # keep the clock sampler fed for ~1 s of the same load; a fixed count, so
+        # every rank issues the same collectives
+        for _ in range(max(20, int(1000.0 / max(ms, 1e-3)))):
+            step()
+        torch.cuda.synchronize()
+        clocks = sampler.stop()
     ops_per_rank = 2.0 * M * N * K
     value = world * ops_per_rank / (ms * 1e-3) / 1e12
     launches_per_step = launches / float(args.steps) if args.steps else 0
+    no_gather_ms = None
+    if world > 1:
+        no_gather_ms = time_events(lambda: ctx.forward(A, B, SCALE, RELU, gather=False), args.steps, stream)
+        t = torch.tensor([no_gather_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        no_gather_ms = float(t.item())
 
     # ---- dominant kernel alone: tcgen05 GEMM on resident quantized operands
     Aq, Bt, scales = ane.quantize_pair(A, B)
@@ -324,22 +333,45 @@ def run_ours(args):
     quant_only()
     q_ms = time_events(quant_only, max(10, args.steps // 4), stream)
 
-    # ---- e2e through the reference-facing C ABI with pinned host buffers
+    # ---- e2e with pinned HOST buffers, host<->device copies inside the timed region
     e2e = None
     if not args.no_e2e:
         Ah = A.cpu().pin_memory()
         Bh = B.cpu().pin_memory()
-        Ch = torch.empty((M, N), dtype=torch.float32).pin_memory()
-        ane.check(ane.lib.ane_dense_fused_i8(M, N, K, SCALE, int(RELU), Ah.data_ptr(), Bh.data_ptr(), Ch.data_ptr()))
         e2e_steps = max(3, min(args.steps, 20))
+        if world == 1:
+            # the reference-facing C entry point (what stream_exec calls for opcode 0x80)
+            Ch = torch.empty((M, N), dtype=torch.float32).pin_memory()
+
+            def e2e_step():
+                ane.check(ane.lib.ane_dense_fused_i8(M, N, K, SCALE, int(RELU), Ah.data_ptr(), Bh.data_ptr(),
+                                                     Ch.data_ptr()))
+            path = "ane_dense_fused_i8 (C ABI, pinned host buffers)"
+            d2h = 4 * M * N
+        else:
+            Ch = torch.empty((world * M, N), dtype=torch.float32).pin_memory()
+
+            def e2e_step():
+                A.copy_(Ah, non_blocking=True)
+                B.copy_(Bh, non_blocking=True)
+                Ch.copy_(ctx.forward(A, B, SCALE, RELU), non_blocking=True)
+                torch.cuda.synchronize()
+            path = "ShardedDense.forward (rows) with host A block / B in, gathered C out (pinned)"
+            d2h = 4 * M * N * world
+        e2e_step()
+        if pg is not None:
+            torch.distributed.barrier()
         t0 = time.perf_counter()
         for _ in range(e2e_steps):
-            ane.check(ane.lib.ane_dense_fused_i8(M, N, K, SCALE, int(RELU), Ah.data_ptr(), Bh.data_ptr(),
-                                                 Ch.data_ptr()))
+            e2e_step()
         e2e_s = (time.perf_counter() - t0) / e2e_steps
+        if pg is not None:
+            t = torch.tensor([e2e_s], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e2e_s = float(t.item())
         e2e = {"value": world * ops_per_rank / e2e_s / 1e12, "unit": "TOPS",
-               "h2d_bytes_per_step": 4 * (M * K + K * N), "d2h_bytes_per_step": 4 * M * N,
-               "ms_per_step": e2e_s * 1e3, "path": "ane_dense_fused_i8 (C ABI, pinned host buffers)"}
+               "h2d_bytes_per_step": 4 * (M * K + K * N), "d2h_bytes_per_step": d2h,
+               "ms_per_step": e2e_s * 1e3, "path": path}
 
     q8 = None
     if not args.no_q8 and rank == 0:
@@ -355,16 +387,18 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": "dense_fused_i8 M=N=K=4096 scale=1.0 relu=off, fp32 N(0,1) A and B in HBM"
-                               + ("" if world == 1 else f"; B/C column-sharded, {N} columns per rank, "
-                                  "NCCL all-reduce(max) of absmax + all-gather of C"),
-                   "M": M, "N_per_rank": N, "K": K,
+                               + ("" if world == 1 else f"; A/C row-sharded, {M} rows per rank, B replicated, "
+                                  "NCCL all-reduce(max) of the absmax bits + all-gather of C"),
+                   "M_per_rank": M, "N": N, "K": K,
                    "l2": "inputs larger than L2 (A+B fp32 = 128 MiB > 126 MB L2), no flush",
                    "parallelism": f"n-shard{world}" if world > 1 else "single"},
-        "roofline": {"bound": "tensor", "kernel": "gemm_s8_tc_kernel (tcgen05 kind::i8)",
+        "roofline": {"bound": "tensor", "kernel": "gemm_s8_pair_kernel (tcgen05 kind::i8, cta_group::2)",
                      "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS", "frac": gemm_tops / int8_peak,
                      "peak_source": f"2 x {peaks['source']} bf16 burst ({peaks['bf16_tflops']} TFLOP/s)",
-                     "traffic": None, "gemm_ms": gemm_ms},
-        "stages_ms": {"quantize_pair": q_ms, "gemm": gemm_ms, "step": ms},
+                     "traffic": GEMM_TRAFFIC_BYTES, "traffic_unit": "bytes per launch (DRAM read + write)",
+                     "traffic_source": "ncu capture, profiles/gemm_s8_pair_dense_fused_4096.md",
+                     "algorithmic_bytes": M * K + N * K + 4 * M * N, "gemm_ms": gemm_ms},
+        "stages_ms": {"quantize_pair": q_ms, "gemm": gemm_ms, "step": ms, "step_without_all_gather": no_gather_ms},
         "e2e": e2e, "gpu_launches": int(launches), "gpu_launches_per_step": launches_per_step,
         "clocks": clocks, "q8_0_gemv": q8, "cpu_baseline": cpu,
     }

@@ -48,6 +48,7 @@ def lib():
             "ane_ref_relu_max": (_f, [_f, _f]),
             "ane_ref_quantize_fp32_i8": (_f, [_f32p, _i8p, _sz, _vp]),
             "ane_ref_absmax": (_f, [_f32p, _sz]),
+            "ane_ref_quantize_with_absmax": (_f, [_f32p, _i8p, _sz, _f]),
             "ane_ref_quantize_fp32_i8_channelwise": (None, [_u32, _u32, _f32p, _i8p, _f32p]),
             "ane_ref_dequantize_i8_fp32": (None, [_sz, _f, _i8p, _f32p]),
             "ane_ref_packed_b_size": (_sz, [_u32, _u32]),
@@ -102,6 +103,14 @@ def quantize_fp32_i8(x):
 def absmax(x) -> np.float32:
     x = _c(x, np.float32).ravel()
     return np.float32(lib().ane_ref_absmax(x, x.size))
+
+
+def quantize_with_absmax(x, absmax):
+    """Quantize with an absmax reduced elsewhere; returns (codes, scale)."""
+    x = _c(x, np.float32).ravel()
+    q = np.empty(x.size, np.int8)
+    s = lib().ane_ref_quantize_with_absmax(x, q, x.size, float(absmax))
+    return q, np.float32(s)
 
 
 def quantize_fp32_i8_channelwise(x):

@@ -131,6 +131,15 @@ float ane_ref_quantize_fp32_i8(const float* src, int8_t* dst, size_t count, floa
     return scale;
 }
 
+float ane_ref_quantize_with_absmax(const float* src, int8_t* dst, size_t count, float absmax) {
+    /* second pass of the handler alone, given an absmax reduced elsewhere
+     * (the N-sharded op reduces it across ranks). */
+    float inv;
+    float scale = ane_ref_scale_from_absmax(absmax, &inv);
+    for (size_t i = 0; i < count; i++) dst[i] = ane_ref_quantize_one(src[i], inv);
+    return scale;
+}
+
 void ane_ref_quantize_fp32_i8_channelwise(uint32_t rows, uint32_t cols, const float* src,
                                           int8_t* dst, float* scales) {
     /* bytecode_interpreter.s:2583-2662: the per-tensor rule applied per row. */

@@ -51,6 +51,8 @@ float ane_ref_absmax(const float* src, size_t count);
 /* second pass alone, given the absmax from the first. */
 float ane_ref_scale_from_absmax(float absmax, float* inv_out);
 int8_t ane_ref_quantize_one(float x, float inv);
+/* second pass alone with a given absmax; returns the scale. */
+float ane_ref_quantize_with_absmax(const float* src, int8_t* dst, size_t count, float absmax);
 
 /* ---- quantize_fp32_i8_channelwise (0x1C) ------------------------------------ */
 void ane_ref_quantize_fp32_i8_channelwise(uint32_t rows, uint32_t cols, const float* src,
