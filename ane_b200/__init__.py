@@ -64,6 +64,8 @@ SIGNATURES = {
     "ane_pack_b_i8_dev": (_i32, [_u32, _u32, _vp, _vp, _vp]),
     "ane_dense_i8_dev": (_i32, [_u32, _u32, _u32, _f, _f, _u8, _vp, _vp, _vp, _vp, _vp]),
     "ane_q8_0_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
+    "ane_quantize_q8_0_dev": (_i32, [_u32, _vp, _vp, _vp]),
+    "ane_q8_0_gemv_q8_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _vp]),
     "ane_device_timeouts": (_i32, []),
     "ane_kernel_launch_count": (_u64, []),
 }
@@ -253,6 +255,26 @@ def gemm_s8(Aq, Bt, scales=None, scale: float = 1.0, relu: bool = False, raw_i32
     check(_lib.ane_gemm_s8_dev(M, N, K16, Aq.data_ptr(), Bt.data_ptr(),
                                scales.data_ptr() if scales is not None else None, float(scale), int(bool(relu)),
                                1 if raw_i32 else 0, out.data_ptr(), _stream_ptr(stream)))
+    return out
+
+
+def quantize_q8_0(x, out=None, stream=None):
+    """fp32 x[K] -> K/32 Q8_0 blocks (uint8 tensor of K/32*34 bytes)."""
+    torch = _torch()
+    K = x.numel()
+    if out is None:
+        out = torch.empty(K // 32 * 34, dtype=torch.uint8, device=x.device)
+    check(_lib.ane_quantize_q8_0_dev(K, x.data_ptr(), out.data_ptr(), _stream_ptr(stream)))
+    return out
+
+
+def q8_0_gemv_q8(W, xq, M: int, K: int, out=None, block_dots=None, stream=None):
+    """Q8_0 weights x Q8_0 activation blocks -> fp32 out[M] (optionally the int32 block dots)."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty(M, dtype=torch.float32, device=W.device)
+    check(_lib.ane_q8_0_gemv_q8_dev(M, K, xq.data_ptr(), W.data_ptr(), out.data_ptr(),
+                                    block_dots.data_ptr() if block_dots is not None else None, _stream_ptr(stream)))
     return out
 
 

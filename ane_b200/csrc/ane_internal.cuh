@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <cstdlib>
 
 #include <atomic>
 #include <string>
@@ -50,6 +51,12 @@ inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_o
 
 // Device properties of the current device (cached per device).
 int num_sms();
+
+// Integer tuning override from the environment (0 / unset = automatic choice).
+inline int env_int(const char* name) {
+    const char* v = getenv(name);
+    return v ? atoi(v) : 0;
+}
 // Verifies that the current device is sm_100 (the only target of this library).
 int require_sm100();
 
@@ -143,5 +150,8 @@ int launch_fill_epilogue_zero_k(uint32_t M, uint32_t N, void* C, size_t ldc, con
 
 int launch_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out,
                      cudaStream_t s);
+int launch_quantize_q8_0(uint32_t K, const float* x, uint8_t* out, cudaStream_t s);
+int launch_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8_t* W, float* out, int32_t* block_dots,
+                        cudaStream_t s);
 
 }  // namespace ane_b200

@@ -391,6 +391,20 @@ int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, fl
     return rc ? rc : ok();
 }
 
+int ane_quantize_q8_0_dev(uint32_t K, const float* x, void* xq_blocks, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = launch_quantize_q8_0(K, x, static_cast<uint8_t*>(xq_blocks), static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+int ane_q8_0_gemv_q8_dev(uint32_t M, uint32_t K, const void* xq_blocks, const void* W, float* out,
+                         int32_t* block_dots, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = launch_q8_0_gemv_q8(M, K, static_cast<const uint8_t*>(xq_blocks), static_cast<const uint8_t*>(W), out,
+                                 block_dots, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
 // ------------------------------------------------- host-facing (synchronous)
 int ane_quantize_fp32_i8(uint32_t count, const float* src, int8_t* dst, float* scale_out) {
     ANE_REQUIRE_GPU();

@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(kQThreads) q8_0_gemv_kernel(const float* __res
 static constexpr int kChunkBlocks = 16;
 static constexpr int kChunkBytes = kChunkBlocks * 34;  // 544 = 34 x 16
 static constexpr int kChunkXBytes = kChunkBlocks * 32 * 4;
-static constexpr int kSlots = 4;
+static constexpr int kMaxSlots = 8;  // full[8] + empty[8] fill the 128-byte barrier area
 // TMA shared-memory destinations must be 128-byte aligned: every slot is
 // rows*544 + 2048 bytes with rows a multiple of 4 (4*544 = 17*128).
 static_assert((4 * kChunkBytes) % 128 == 0 && kChunkXBytes % 128 == 0, "slot alignment");
@@ -163,7 +163,8 @@ __device__ __forceinline__ void q8_fma2(float& acc0, float& acc1, uint32_t w, fl
 // wait on each other.  Compute warps w = 1..NW each own 4 rows.
 __global__ void q8_0_gemv_stream_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ W,
                                         const float* __restrict__ x,
-                                        float* __restrict__ out, uint32_t M, uint32_t K, int* err) {
+                                        float* __restrict__ out, uint32_t M, uint32_t K, uint32_t nslots,
+                                        int* err) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t nw = blockDim.x / 32 - 1;  // compute warps
     const uint32_t rows_per_cta = 4 * nw;
@@ -172,15 +173,15 @@ __global__ void q8_0_gemv_stream_kernel(const __grid_constant__ CUtensorMap wmap
     const uint32_t w_bytes = rows_per_cta * kChunkBytes;  // weight part of a slot
     const uint32_t slot_bytes = w_bytes + kChunkXBytes;   // + the chunk's slice of x
     auto chunk_blocks = [&](uint32_t c) { return min((uint32_t)kChunkBlocks, nb - c * kChunkBlocks); };
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // kSlots
-    uint64_t* empty = full + kSlots;                     // kSlots
-    uint8_t* ring = smem + 128;                          // kSlots x slot_bytes
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // nslots
+    uint64_t* empty = full + nslots;                     // nslots
+    uint8_t* ring = smem + 128;                          // nslots x slot_bytes
     const uint32_t r0 = blockIdx.x * rows_per_cta;
     const uint32_t nrows = min(rows_per_cta, M - r0);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kSlots; s++) {
+        for (int s = 0; s < nslots; s++) {
             ptx::mbar_init(&full[s], 1);
             ptx::mbar_init(&empty[s], nw);
         }
@@ -197,8 +198,8 @@ __global__ void q8_0_gemv_stream_kernel(const __grid_constant__ CUtensorMap wmap
         if (lane == 0) {
             ptx::prefetch_tmap(&wmap);
             for (uint32_t c = 0; c < nchunks; c++) {
-                const uint32_t slot = c % kSlots;
-                if (!ptx::mbar_wait(&empty[slot], ((c / kSlots) & 1) ^ 1, err)) break;
+                const uint32_t slot = c % nslots;
+                if (!ptx::mbar_wait(&empty[slot], ((c / nslots) & 1) ^ 1, err)) break;
                 const uint32_t xbytes = chunk_blocks(c) * 32 * 4;
                 uint8_t* dst = ring + (size_t)slot * slot_bytes;
                 ptx::mbar_arrive_expect_tx(&full[slot], w_bytes + xbytes);
@@ -214,8 +215,8 @@ __global__ void q8_0_gemv_stream_kernel(const __grid_constant__ CUtensorMap wmap
     float acc0 = 0.f, acc1 = 0.f;
     bool alive = true;
     for (uint32_t c = 0; c < nchunks && alive; c++) {
-        const uint32_t slot = c % kSlots;
-        if (!ptx::mbar_wait(&full[slot], (c / kSlots) & 1, err)) { alive = false; break; }
+        const uint32_t slot = c % nslots;
+        if (!ptx::mbar_wait(&full[slot], (c / nslots) & 1, err)) { alive = false; break; }
         if (active) {
             const uint8_t* rp = ring + (size_t)slot * slot_bytes + row * kChunkBytes;
             const float* xc = reinterpret_cast<const float*>(ring + (size_t)slot * slot_bytes + w_bytes) + 2 * j;
@@ -283,10 +284,24 @@ int launch_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, f
     if (K % 256 == 0 && ((uintptr_t)W & 15) == 0 && ((uintptr_t)x & 15) == 0) {
         // ~6 resident CTAs per SM, each 1 producer warp + nw compute warps (4 rows each)
         const uint32_t sms = (uint32_t)num_sms();
-        uint32_t nw = (M + 4 * 6 * sms - 1) / (4 * 6 * sms);
+        // ANE_Q8_WARPS (1..8 compute warps) and ANE_Q8_SLOTS (2..8) override the
+        // shape-based choice (tuning aids)
+        static const int force_warps = env_int("ANE_Q8_WARPS"), force_slots = env_int("ANE_Q8_SLOTS");
+        uint32_t nw = force_warps > 0 ? (uint32_t)force_warps : (M + 4 * 6 * sms - 1) / (4 * 6 * sms);
         nw = nw < 1 ? 1 : (nw > 8 ? 8 : nw);
         const uint32_t rows = 4 * nw;
-        const size_t smem = 128 + (size_t)kSlots * (rows * kChunkBytes + kChunkXBytes);
+        // as many ring slots as fit a fair share of the SM's shared memory (up to
+        // every chunk of the CTA): more bytes in flight per CTA from the start
+        const uint32_t blocks_per_sm = (((M + rows - 1) / rows) + sms - 1) / sms;
+        const size_t slot = (size_t)rows * kChunkBytes + kChunkXBytes;
+        const uint32_t nchunks = (K / 32 + kChunkBlocks - 1) / kChunkBlocks;
+        // (228 KB per SM, 1 KB of it reserved per resident CTA)
+        const size_t share = 227 * 1024 / (blocks_per_sm ? blocks_per_sm : 1) - 1024;
+        uint32_t nslots = share > 128 ? (uint32_t)((share - 128) / slot) : 2;
+        nslots = nslots < 2 ? 2 : (nslots > (uint32_t)kMaxSlots ? (uint32_t)kMaxSlots : nslots);
+        if (nslots > nchunks) nslots = nchunks < 2 ? 2 : nchunks;
+        if (force_slots > 0) nslots = force_slots < 2 ? 2 : (force_slots > kMaxSlots ? kMaxSlots : force_slots);
+        const size_t smem = 128 + (size_t)nslots * slot;
         static const cudaError_t attr_err = cudaFuncSetAttribute(
             q8_0_gemv_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         ANE_CUDA_TRY(attr_err);
@@ -296,7 +311,8 @@ int launch_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, f
         int rc = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, row_bytes / 4, M, row_bytes,
                                       kChunkBytes / 4, rows, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
-        q8_0_gemv_stream_kernel<<<blocks, 32 * (nw + 1), smem, s>>>(wmap, W, x, out, M, K, device_timeout_flag());
+        q8_0_gemv_stream_kernel<<<blocks, 32 * (nw + 1), smem, s>>>(wmap, W, x, out, M, K, nslots,
+                                                                    device_timeout_flag());
         ANE_CHECK_LAUNCH();
         return ANE_OK;
     }

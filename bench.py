@@ -196,6 +196,30 @@ def time_events(fn, steps, stream):
     return s.elapsed_time(e) / steps  # ms
 
 
+def time_graph(fn, steps, stream):
+    """Per-call ms of `steps` calls of fn captured into one CUDA graph and replayed.
+
+    A Q8_0 matvec runs for ~3-15 us, below the host's per-call launch cost from
+    Python, so eager timing would measure the host; a replayed graph keeps the
+    GPU fed back to back and times the kernels."""
+    import torch
+
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(steps):
+            fn()
+    g.replay()  # warm
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    g.replay()
+    e.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return s.elapsed_time(e) / steps  # ms
+
+
 def q8_bench(ane, torch, dev, steps=50):
     """Q8_0 matvec GB/s on the 7B shapes, rotating >= 4 weight copies (> L2)."""
     import numpy as np
@@ -221,9 +245,24 @@ def q8_bench(ane, torch, dev, steps=50):
             ane.q8_0_gemv(Ws[it[0] % copies], x, rows, cols, out=y)
             it[0] += 1
 
-        ms = time_events(step, steps, stream)
+        eager_ms = time_events(step, steps, stream)
+        ms = time_graph(step, steps, stream)
         nbytes = wbytes + 4 * cols + 4 * rows
+        # mode Q: activation quantized to Q8_0 (ggml convention), exact int32 block dots
+        xq = ane.quantize_q8_0(x)
+        for i in range(3):
+            ane.q8_0_gemv_q8(Ws[i % copies], xq, rows, cols, out=y)
+        itq = [0]
+
+        def step_q():
+            ane.q8_0_gemv_q8(Ws[itq[0] % copies], xq, rows, cols, out=y)
+            itq[0] += 1
+
+        ms_q = time_graph(step_q, steps, stream)
+        nbytes_q = wbytes + (cols // 32) * 34 + 4 * rows
         out[f"{rows}x{cols}"] = {"gbs": nbytes / (ms * 1e-3) / 1e9, "us": ms * 1e3, "bytes": nbytes,
+                                 "mode_q_gbs": nbytes_q / (ms_q * 1e-3) / 1e9, "mode_q_us": ms_q * 1e3,
+                                 "eager_us": eager_ms * 1e3, "timing": "CUDA graph of back-to-back calls",
                                  "weight_copies_rotated": copies}
         del Ws
     return out

@@ -117,6 +117,15 @@ int ane_dense_i8_dev(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uin
                      void* stream);
 int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out,
                       void* stream);
+/* Q8_0 x Q8_0 matvec (the ggml / llama.cpp activation convention; the
+ * reference's q8_0_gemv keeps x in fp32, see ane_q8_0_gemv).  x[K] is first
+ * quantized to K/32 Q8_0 blocks (d = fp16(amax/127), q = roundf(x/d)); the
+ * matvec computes exact int32 block dot products (dp4a) and
+ * out[m] = sum_b float(sumi_b) * (dw_b * dx_b).  block_dots (NULL to skip)
+ * receives the M x K/32 int32 block dots.  K % 256 == 0, W 16-byte aligned. */
+int ane_quantize_q8_0_dev(uint32_t K, const float* x, void* xq_blocks, void* stream);
+int ane_q8_0_gemv_q8_dev(uint32_t M, uint32_t K, const void* xq_blocks, const void* W, float* out,
+                         int32_t* block_dots, void* stream);
 
 /* dense_fused_i8 without any allocation.  No counterpart in the reference: it
  * exists for callers that cannot allocate device memory when they run the op

@@ -383,3 +383,31 @@ def test_threads_are_independent(ane):
     assert not errs
     for (A, B), o in zip(cases, outs):
         assert bits_equal(o, oracle.dense_fused_i8(A, B, 1.0, True))
+
+
+# ------------------------------------------------------- Q8_0 x Q8_0 (mode Q)
+@pytest.mark.parametrize("M,K", [(4096, 4096), (11008, 4096), (4096, 11008), (40, 256)])
+def test_q8_0_gemv_q8_mode(ane, M, K):
+    """Activation quantizer bytes exact; int32 block dots exact; fp32 out within
+    1e-5 of the sum of |block terms| (its own fp32 order)."""
+    import torch
+
+    rng = np.random.default_rng(M * 3 + K)
+    W = oracle.quantize_q8_0((rng.standard_normal((M, K)) * 0.02).astype(F32), M, K)
+    x = rng.standard_normal(K).astype(F32)
+    x[64:96] = 0.0  # an all-zero block (d = 0, id = 0)
+    xq_ref = oracle.quantize_q8_0(x, 1, K)
+    xg = torch.from_numpy(x).cuda()
+    xq = ane.quantize_q8_0(xg)
+    assert np.array_equal(xq.cpu().numpy(), xq_ref)
+    Wg = torch.from_numpy(W).cuda()
+    dots = torch.empty((M, K // 32), dtype=torch.int32, device="cuda")
+    out = ane.q8_0_gemv_q8(Wg, xq, M, K, block_dots=dots)
+    ref, ref_dots = oracle.q8_0_gemv_q8(W, xq_ref, M, K, with_dots=True)
+    assert np.array_equal(dots.cpu().numpy(), ref_dots)
+    Wb = W.reshape(M, K // 32, 34)
+    dw = Wb[:, :, 0:2].copy().view(np.float16)[..., 0].astype(np.float64)
+    dx = xq_ref.reshape(K // 32, 34)[:, 0:2].copy().view(np.float16)[:, 0].astype(np.float64)
+    bound = np.abs(ref_dots.astype(np.float64) * dw * dx[None, :]).sum(axis=1)
+    got = out.cpu().numpy().astype(np.float64)
+    assert np.all(np.abs(got - ref.astype(np.float64)) <= 1e-5 * bound + 1e-30)
