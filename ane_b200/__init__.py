@@ -66,6 +66,8 @@ SIGNATURES = {
     "ane_q8_0_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
     "ane_quantize_q8_0_dev": (_i32, [_u32, _vp, _vp, _vp]),
     "ane_q8_0_gemv_q8_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _vp]),
+    "ane_q8_0_gemv_ex_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _u32, _vp]),
+    "ane_q8_0_gemv_q8_ex_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _u32, _vp]),
     "ane_device_timeouts": (_i32, []),
     "ane_kernel_launch_count": (_u64, []),
 }
@@ -268,20 +270,28 @@ def quantize_q8_0(x, out=None, stream=None):
     return out
 
 
-def q8_0_gemv_q8(W, xq, M: int, K: int, out=None, block_dots=None, stream=None):
-    """Q8_0 weights x Q8_0 activation blocks -> fp32 out[M] (optionally the int32 block dots)."""
+WEIGHTS_STATIC = 1  # ANE_Q8_WEIGHTS_STATIC: W is not written by the kernel just before the call
+
+
+def q8_0_gemv_q8(W, xq, M: int, K: int, out=None, block_dots=None, stream=None, static_weights=False):
+    """Q8_0 weights x Q8_0 activation blocks -> fp32 out[M] (optionally the int32 block dots).
+
+    static_weights promises that W was not written by the kernel queued just
+    before this call, so the kernel may start streaming W early."""
     torch = _torch()
     if out is None:
         out = torch.empty(M, dtype=torch.float32, device=W.device)
-    check(_lib.ane_q8_0_gemv_q8_dev(M, K, xq.data_ptr(), W.data_ptr(), out.data_ptr(),
-                                    block_dots.data_ptr() if block_dots is not None else None, _stream_ptr(stream)))
+    check(_lib.ane_q8_0_gemv_q8_ex_dev(M, K, xq.data_ptr(), W.data_ptr(), out.data_ptr(),
+                                       block_dots.data_ptr() if block_dots is not None else None,
+                                       WEIGHTS_STATIC if static_weights else 0, _stream_ptr(stream)))
     return out
 
 
-def q8_0_gemv(W, x, M: int, K: int, out=None, stream=None):
+def q8_0_gemv(W, x, M: int, K: int, out=None, stream=None, static_weights=False):
     """out[M] = Q8_0 matrix W (M rows of K/32 34-byte blocks, uint8 tensor) times fp32 x[K]."""
     torch = _torch()
     if out is None:
         out = torch.empty(M, dtype=torch.float32, device=x.device)
-    check(_lib.ane_q8_0_gemv_dev(M, K, x.data_ptr(), W.data_ptr(), out.data_ptr(), _stream_ptr(stream)))
+    check(_lib.ane_q8_0_gemv_ex_dev(M, K, x.data_ptr(), W.data_ptr(), out.data_ptr(),
+                                    WEIGHTS_STATIC if static_weights else 0, _stream_ptr(stream)))
     return out

@@ -148,10 +148,12 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
 int launch_fill_epilogue_zero_k(uint32_t M, uint32_t N, void* C, size_t ldc, const GemmEpilogue& ep,
                                 cudaStream_t s);
 
-int launch_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out,
+// flags: ANE_Q8_WEIGHTS_STATIC lets the streamed kernels read W before the
+// previous kernel on the stream has finished.
+int launch_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, uint32_t flags,
                      cudaStream_t s);
 int launch_quantize_q8_0(uint32_t K, const float* x, uint8_t* out, cudaStream_t s);
 int launch_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8_t* W, float* out, int32_t* block_dots,
-                        cudaStream_t s);
+                        uint32_t flags, cudaStream_t s);
 
 }  // namespace ane_b200

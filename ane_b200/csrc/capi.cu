@@ -386,8 +386,14 @@ int ane_dense_i8_dev(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uin
 }
 
 int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
+    return ane_q8_0_gemv_ex_dev(M, K, in, W, out, 0, stream);
+}
+
+int ane_q8_0_gemv_ex_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, uint32_t flags,
+                         void* stream) {
     ANE_REQUIRE_GPU();
-    int rc = launch_q8_0_gemv(M, K, in, static_cast<const uint8_t*>(W), out, static_cast<cudaStream_t>(stream));
+    ANE_ARG_CHECK((flags & ~ANE_Q8_WEIGHTS_STATIC) == 0, "q8_0_gemv: unknown flag bits");
+    int rc = launch_q8_0_gemv(M, K, in, static_cast<const uint8_t*>(W), out, flags, static_cast<cudaStream_t>(stream));
     return rc ? rc : ok();
 }
 
@@ -399,9 +405,15 @@ int ane_quantize_q8_0_dev(uint32_t K, const float* x, void* xq_blocks, void* str
 
 int ane_q8_0_gemv_q8_dev(uint32_t M, uint32_t K, const void* xq_blocks, const void* W, float* out,
                          int32_t* block_dots, void* stream) {
+    return ane_q8_0_gemv_q8_ex_dev(M, K, xq_blocks, W, out, block_dots, 0, stream);
+}
+
+int ane_q8_0_gemv_q8_ex_dev(uint32_t M, uint32_t K, const void* xq_blocks, const void* W, float* out,
+                            int32_t* block_dots, uint32_t flags, void* stream) {
     ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK((flags & ~ANE_Q8_WEIGHTS_STATIC) == 0, "q8_0_gemv_q8: unknown flag bits");
     int rc = launch_q8_0_gemv_q8(M, K, static_cast<const uint8_t*>(xq_blocks), static_cast<const uint8_t*>(W), out,
-                                 block_dots, static_cast<cudaStream_t>(stream));
+                                 block_dots, flags, static_cast<cudaStream_t>(stream));
     return rc ? rc : ok();
 }
 
@@ -500,7 +512,7 @@ int ane_q8_0_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float*
                              {W, (size_t)M * (K / 32) * 34, true, false},
                              {out, (size_t)M * 4, false, true}};
     return run_staged(args, 0, [&](cudaStream_t s, void*) {
-        return launch_q8_0_gemv(M, K, (const float*)args[0].dev, (const uint8_t*)args[1].dev, (float*)args[2].dev, s);
+        return launch_q8_0_gemv(M, K, (const float*)args[0].dev, (const uint8_t*)args[1].dev, (float*)args[2].dev, 0, s);
     });
 }
 

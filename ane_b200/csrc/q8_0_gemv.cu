@@ -22,6 +22,7 @@
 #include <cuda_fp16.h>
 
 #include "ane_internal.cuh"
+#include "q8_stream.cuh"
 #include "sm100_ptx.cuh"
 
 namespace ane_b200 {
@@ -104,21 +105,15 @@ __global__ void __launch_bounds__(kQThreads) q8_0_gemv_kernel(const float* __res
 }
 
 // ----------------------------------------------------------- streamed kernel
-// For K % 256 == 0 and 16-byte-aligned W (every row starts 16-byte aligned):
-// each CTA owns `rows` consecutive output rows; 8 threads per row, thread j
-// owning lanes 2j and 2j+1 (bytes q[2j..2j+1] and q[16+2j..16+2j+1] of every
-// block).  Weight rows stream through a ring of kSlots shared-memory slots in
-// chunks of kChunkBlocks blocks (272 B per row) with cp.async.bulk, so HBM
-// reads run up to kSlots-1 chunks ahead of the FMA chains; x sits in shared
-// memory for the whole kernel.  FADDV: level 1 in-thread, levels 2-4 by xor
-// shuffles 1, 2, 4 across the 8 threads of the row.
-static constexpr int kChunkBlocks = 16;
-static constexpr int kChunkBytes = kChunkBlocks * 34;  // 544 = 34 x 16
-static constexpr int kChunkXBytes = kChunkBlocks * 32 * 4;
-static constexpr int kMaxSlots = 8;  // full[8] + empty[8] fill the 128-byte barrier area
-// TMA shared-memory destinations must be 128-byte aligned: every slot is
-// rows*544 + 2048 bytes with rows a multiple of 4 (4*544 = 17*128).
-static_assert((4 * kChunkBytes) % 128 == 0 && kChunkXBytes % 128 == 0, "slot alignment");
+// For K % 256 == 0 and 16-byte-aligned W and x (every row starts 16-byte
+// aligned).  Work split, ring and launch: q8_stream.cuh.  A compute warp owns 4
+// rows, 8 threads per row, thread j owning lanes 2j and 2j+1 (bytes
+// q[2j..2j+1] and q[16+2j..16+2j+1] of every block).  Each ring stage carries,
+// next to the 4-row weight tiles of every compute warp, the chunk's 512-float
+// slice of x.  FADDV: level 1 in-thread, levels 2-4 by xor shuffles 1, 2, 4
+// across the 8 threads of the row.
+static constexpr int kChunkXBytes = kQ8ChunkBlocks * 32 * 4;
+static_assert(kChunkXBytes % 128 == 0, "slot alignment");
 
 // q as fp32 from the biased byte: 0x4700_uu00 = 32768 + u = 32896 + q, minus
 // 32896 (exact).  Then q*d is one RN multiply, exact for finite d and the same
@@ -136,185 +131,183 @@ __device__ __forceinline__ void q8_fma2_exact(float& acc0, float& acc1, uint32_t
     acc1 = __fmaf_rn(__fmul_rn(q_to_f32(u, 0x7434u), d), xhi.y, acc1);  // lane 2j+1, second half
 }
 
-__device__ __forceinline__ void q8_fma2(float& acc0, float& acc1, uint32_t w, float d, float negcd, bool finite,
-                                        float2 xlo, float2 xhi) {
-    // w bytes: {q[2j], q[2j+1], q[16+2j], q[16+2j+1]}
-    float dq0, dq1, dq2, dq3;
-    if (finite) {
-        const uint32_t u = w ^ 0x80808080u;
-        dq0 = dq_fast(u, 0x7404u, d, negcd);
-        dq1 = dq_fast(u, 0x7414u, d, negcd);
-        dq2 = dq_fast(u, 0x7424u, d, negcd);
-        dq3 = dq_fast(u, 0x7434u, d, negcd);
-    } else {
-        dq0 = __fmul_rn((float)(int8_t)(w & 0xff), d);
-        dq1 = __fmul_rn((float)(int8_t)((w >> 8) & 0xff), d);
-        dq2 = __fmul_rn((float)(int8_t)((w >> 16) & 0xff), d);
-        dq3 = __fmul_rn((float)(int8_t)(w >> 24), d);
-    }
-    acc0 = __fmaf_rn(dq0, xlo.x, acc0);  // lane 2j,   first half
-    acc1 = __fmaf_rn(dq1, xlo.y, acc1);  // lane 2j+1, first half
-    acc0 = __fmaf_rn(dq2, xhi.x, acc0);  // lane 2j,   second half
-    acc1 = __fmaf_rn(dq3, xhi.y, acc1);  // lane 2j+1, second half
+// One block for lanes {2j, 2j+1}, finite d: the four products q*d come from two
+// packed FMAs fma(f, d, -32896*d) (exact), the two accumulate steps are packed
+// FMAs on {acc[2j], acc[2j+1]} -- per lane the same roundings, in the same
+// order, as the reference's fmul + fmla.
+__device__ __forceinline__ float2 q8_block_fast(float2 acc, uint32_t w, float d, float2 xlo, float2 xhi) {
+    const uint32_t u = w ^ 0x80808080u;
+    const float2 dd = make_float2(d, d);
+    const float ncd = __fmul_rn(-32896.0f, d);
+    const float2 nc = make_float2(ncd, ncd);
+    const float2 f01 = make_float2(__uint_as_float(__byte_perm(u, 0x47000000u, 0x7404u)),
+                                   __uint_as_float(__byte_perm(u, 0x47000000u, 0x7414u)));
+    const float2 f23 = make_float2(__uint_as_float(__byte_perm(u, 0x47000000u, 0x7424u)),
+                                   __uint_as_float(__byte_perm(u, 0x47000000u, 0x7434u)));
+    const float2 dq01 = ptx::ffma2(f01, dd, nc);
+    const float2 dq23 = ptx::ffma2(f23, dd, nc);
+    acc = ptx::ffma2(dq01, xlo, acc);
+    return ptx::ffma2(dq23, xhi, acc);
 }
 
-// Warp 0 of every CTA is the producer: it refills a slot as soon as all compute
-// warps have released it (per-slot `empty` mbarrier), so compute warps never
-// wait on each other.  Compute warps w = 1..NW each own 4 rows.
-__global__ void q8_0_gemv_stream_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ W,
-                                        const float* __restrict__ x,
-                                        float* __restrict__ out, uint32_t M, uint32_t K, uint32_t nslots,
-                                        int* err) {
+// Warp 0 of every CTA is the producer (one elected lane): per stage it issues
+// one 4-row x 544-byte TMA box per compute warp with rows in the pass and one
+// bulk copy of the x slice, after the consumers have released the stage.
+// (The launch bound lets ptxas keep a whole 8-block load phase in registers.)
+__global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
+    q8_0_gemv_stream_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ W,
+                            const float* __restrict__ x, float* __restrict__ out, uint32_t M, uint32_t K,
+                            uint32_t groups, uint32_t nw, uint32_t nslots, uint32_t flags, int* err) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t nw = blockDim.x / 32 - 1;  // compute warps
-    const uint32_t rows_per_cta = 4 * nw;
-    // the last chunk may hold fewer than kChunkBlocks blocks (the TMA zero-fills the rest)
-    const uint32_t nb = K / 32, nchunks = (nb + kChunkBlocks - 1) / kChunkBlocks;
-    const uint32_t w_bytes = rows_per_cta * kChunkBytes;  // weight part of a slot
-    const uint32_t slot_bytes = w_bytes + kChunkXBytes;   // + the chunk's slice of x
-    auto chunk_blocks = [&](uint32_t c) { return min((uint32_t)kChunkBlocks, nb - c * kChunkBlocks); };
+    // the last chunk may hold 8 blocks (K % 512 == 256): the TMA box then runs
+    // past the row end and zero-fills, and the transaction counts the full box
+    const uint32_t nb = K / 32, nchunks = (nb + kQ8ChunkBlocks - 1) / kQ8ChunkBlocks;
+    const uint32_t w_bytes = nw * kQ8WarpTileBytes;  // weight part of a stage
+    const uint32_t slot_bytes = w_bytes + kChunkXBytes;
+    auto chunk_blocks = [&](uint32_t c) { return min((uint32_t)kQ8ChunkBlocks, nb - c * kQ8ChunkBlocks); };
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // nslots
     uint64_t* empty = full + nslots;                     // nslots
     uint8_t* ring = smem + 128;                          // nslots x slot_bytes
-    const uint32_t r0 = blockIdx.x * rows_per_cta;
-    const uint32_t nrows = min(rows_per_cta, M - r0);
+    const uint32_t g0 = (uint32_t)((uint64_t)groups * blockIdx.x / gridDim.x);
+    const uint32_t g1 = (uint32_t)((uint64_t)groups * (blockIdx.x + 1) / gridDim.x);
+    const uint32_t npass = (g1 - g0 + nw - 1) / nw, ntiles = npass * nchunks;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < nslots; s++) {
+        for (uint32_t s = 0; s < nslots; s++) {
             ptx::mbar_init(&full[s], 1);
             ptx::mbar_init(&empty[s], nw);
         }
         ptx::fence_mbarrier_init();
     }
     __syncthreads();
+    ptx::griddep_launch_dependents();
 
     if (warp == 0) {
-        // ---------------------------------------------------------- producer
-        // Per chunk: one 2-D TMA for rows r0.. of the CTA x 544 bytes (136 uint32;
-        // rows past M and bytes past the row end of a half last chunk read as
-        // zero, the transaction counts the full box) and one 1-D bulk copy of
-        // the chunk's x slice (512 or 256 floats).
         if (lane == 0) {
             ptx::prefetch_tmap(&wmap);
-            for (uint32_t c = 0; c < nchunks; c++) {
-                const uint32_t slot = c % nslots;
-                if (!ptx::mbar_wait(&empty[slot], ((c / nslots) & 1) ^ 1, err)) break;
-                const uint32_t xbytes = chunk_blocks(c) * 32 * 4;
+            auto issue_weights = [&](uint32_t t, uint32_t slot) {
+                const uint32_t pass = t / nchunks, c = t - pass * nchunks;
+                const uint32_t gp = g0 + pass * nw, nwp = min(nw, g1 - gp);
                 uint8_t* dst = ring + (size_t)slot * slot_bytes;
-                ptx::mbar_arrive_expect_tx(&full[slot], w_bytes + xbytes);
-                ptx::tma_load_2d(dst, &wmap, &full[slot], (int)(c * (kChunkBytes / 4)), (int)r0);
-                ptx::bulk_load(dst + w_bytes, x + (size_t)c * kChunkBlocks * 32, xbytes, &full[slot]);
+                ptx::mbar_arrive_expect_tx(&full[slot], nwp * kQ8WarpTileBytes + chunk_blocks(c) * 32 * 4);
+                for (uint32_t w = 0; w < nwp; w++)
+                    ptx::tma_load_2d(dst + w * kQ8WarpTileBytes, &wmap, &full[slot], (int)(c * (kQ8ChunkBytes / 4)),
+                                     (int)((gp + w) * kQ8RowsPerWarp));
+            };
+            auto issue_x = [&](uint32_t t, uint32_t slot) {
+                const uint32_t c = t % nchunks;
+                ptx::bulk_load(ring + (size_t)slot * slot_bytes + w_bytes, x + (size_t)c * kQ8ChunkBlocks * 32,
+                               chunk_blocks(c) * 32 * 4, &full[slot]);
+            };
+            // static weights: the first stages' weight tiles are requested before
+            // the previous kernel on the stream has finished
+            const uint32_t pre = (flags & ANE_Q8_WEIGHTS_STATIC) ? min(nslots, ntiles) : 0;
+            for (uint32_t t = 0; t < pre; t++) issue_weights(t, t);
+            ptx::griddep_wait();  // x may be written by the previous kernel
+            for (uint32_t t = 0; t < pre; t++) issue_x(t, t);
+            for (uint32_t t = pre; t < ntiles; t++) {
+                const uint32_t slot = t % nslots;
+                if (!ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err)) break;
+                issue_weights(t, slot);
+                issue_x(t, slot);
             }
         }
         return;
     }
     // ------------------------------------------------------------ compute
-    const uint32_t row = (warp - 1) * 4 + (lane >> 3), j = lane & 7;
-    const bool active = row < nrows;
-    float acc0 = 0.f, acc1 = 0.f;
+    ptx::griddep_wait();  // out (and x, on the replay path) may belong to the previous kernel
+    const uint32_t cw = warp - 1, rr = lane >> 3, j = lane & 7;
     bool alive = true;
-    for (uint32_t c = 0; c < nchunks && alive; c++) {
-        const uint32_t slot = c % nslots;
-        if (!ptx::mbar_wait(&full[slot], (c / nslots) & 1, err)) { alive = false; break; }
-        if (active) {
-            const uint8_t* rp = ring + (size_t)slot * slot_bytes + row * kChunkBytes;
-            const float* xc = reinterpret_cast<const float*>(ring + (size_t)slot * slot_bytes + w_bytes) + 2 * j;
-            const int cb = (int)chunk_blocks(c);  // 16, or 8 for the half last chunk
-            for (int b0 = 0; b0 < cb; b0 += 8) {
-                // load phase: all shared-memory reads of 8 blocks issue back to back
-                uint32_t dbits[8], w[8];
-                float2 xl[8], xh[8];
+    for (uint32_t pass = 0; pass < npass && alive; pass++) {
+        const uint32_t gp = g0 + pass * nw;
+        const uint32_t row = (gp + cw) * kQ8RowsPerWarp + rr;
+        const bool active = gp + cw < g1 && row < M;
+        float2 acc = make_float2(0.f, 0.f);
+        for (uint32_t c = 0; c < nchunks; c++) {
+            const uint32_t t = pass * nchunks + c, slot = t % nslots;
+            if (!ptx::mbar_wait(&full[slot], (t / nslots) & 1, err)) { alive = false; break; }
+            if (active) {
+                const uint8_t* st = ring + (size_t)slot * slot_bytes;
+                const uint8_t* rp = st + cw * kQ8WarpTileBytes + rr * kQ8ChunkBytes;
+                const float* xc = reinterpret_cast<const float*>(st + w_bytes) + 2 * j;
+                const int cb = (int)chunk_blocks(c);  // 16, or 8 for the half last chunk
+                for (int b0 = 0; b0 < cb; b0 += 8) {
+                    // load phase: all shared-memory reads of 8 blocks issue back to back
+                    uint32_t dbits[8], w[8];
+                    float2 xl[8], xh[8];
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const uint8_t* blk = rp + (b0 + i) * 34;
-                    dbits[i] = *reinterpret_cast<const unsigned short*>(blk);
-                    w[i] = *reinterpret_cast<const unsigned short*>(blk + 2 + 2 * j) |
-                           ((uint32_t)*reinterpret_cast<const unsigned short*>(blk + 18 + 2 * j) << 16);
-                    xl[i] = *reinterpret_cast<const float2*>(xc + (b0 + i) * 32);
-                    xh[i] = *reinterpret_cast<const float2*>(xc + (b0 + i) * 32 + 16);
-                }
-                // compute phase: blocks in order, two FMA chains.  fma(f, d, -32896*d)
-                // equals q*d exactly for every finite d; an inf/NaN d makes the row
-                // result non-finite, and such rows are recomputed below.
+                    for (int i = 0; i < 8; i++) {
+                        const uint8_t* blk = rp + (b0 + i) * 34;
+                        dbits[i] = *reinterpret_cast<const unsigned short*>(blk);
+                        w[i] = *reinterpret_cast<const unsigned short*>(blk + 2 + 2 * j) |
+                               ((uint32_t)*reinterpret_cast<const unsigned short*>(blk + 18 + 2 * j) << 16);
+                        xl[i] = *reinterpret_cast<const float2*>(xc + (b0 + i) * 32);
+                        xh[i] = *reinterpret_cast<const float2*>(xc + (b0 + i) * 32 + 16);
+                    }
+                    // compute phase: blocks in order.  The fast dequant equals q*d
+                    // exactly for every finite d; an inf/NaN d makes the row result
+                    // non-finite, and such rows are recomputed below.
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const float d = __half2float(__ushort_as_half((unsigned short)dbits[i]));
-                    q8_fma2(acc0, acc1, w[i], d, __fmul_rn(-32896.0f, d), true, xl[i], xh[i]);
+                    for (int i = 0; i < 8; i++) {
+                        const float d = __half2float(__ushort_as_half((unsigned short)dbits[i]));
+                        acc = q8_block_fast(acc, w[i], d, xl[i], xh[i]);
+                    }
                 }
             }
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&empty[slot]);  // this warp is done with the stage
         }
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&empty[slot]);  // this warp is done with the slot
-    }
-    auto faddv = [](float a0, float a1) {  // level 1 in-thread, levels 2-4 across the row's 8 threads
-        float t = __fadd_rn(a0, a1);
-        t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
-        t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
-        return __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 4));
-    };
-    float s = faddv(acc0, acc1);
-    // Rare path: a non-finite row result may come from an inf/NaN block scale, for
-    // which the fma shortcut differs from the reference's scvtf + fmul; replay
-    // such rows (row-uniform decision) from global memory with the direct product.
-    const bool redo = active && alive && !isfinite(s);
-    if (__any_sync(0xffffffffu, redo)) {
-        float a0 = 0.f, a1 = 0.f;
-        if (redo) {
-            const uint8_t* rp = W + (size_t)(r0 + row) * ((size_t)nb * 34);
-            for (uint32_t b = 0; b < nb; b++) {
-                const uint8_t* blk = rp + (size_t)b * 34;
-                const uint32_t w = (uint32_t)*reinterpret_cast<const unsigned short*>(blk + 2 + 2 * j) |
-                                   ((uint32_t)*reinterpret_cast<const unsigned short*>(blk + 18 + 2 * j) << 16);
-                const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(blk)));
-                q8_fma2_exact(a0, a1, w, d, *reinterpret_cast<const float2*>(x + 32 * b + 2 * j),
-                              *reinterpret_cast<const float2*>(x + 32 * b + 16 + 2 * j));
+        auto faddv = [](float a0, float a1) {  // level 1 in-thread, levels 2-4 across the row's 8 threads
+            float t = __fadd_rn(a0, a1);
+            t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
+            t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+            return __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 4));
+        };
+        float s = faddv(acc.x, acc.y);
+        // Rare path: a non-finite row result may come from an inf/NaN block scale,
+        // for which the fma shortcut differs from the reference's scvtf + fmul;
+        // replay such rows (row-uniform decision) from global memory with the
+        // direct product.
+        const bool redo = active && alive && !isfinite(s);
+        if (__any_sync(0xffffffffu, redo)) {
+            float a0 = 0.f, a1 = 0.f;
+            if (redo) {
+                const uint8_t* rp = W + (size_t)row * ((size_t)nb * 34);
+                for (uint32_t b = 0; b < nb; b++) {
+                    const uint8_t* blk = rp + (size_t)b * 34;
+                    const uint32_t w = (uint32_t)*reinterpret_cast<const unsigned short*>(blk + 2 + 2 * j) |
+                                       ((uint32_t)*reinterpret_cast<const unsigned short*>(blk + 18 + 2 * j) << 16);
+                    const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(blk)));
+                    q8_fma2_exact(a0, a1, w, d, *reinterpret_cast<const float2*>(x + 32 * b + 2 * j),
+                                  *reinterpret_cast<const float2*>(x + 32 * b + 16 + 2 * j));
+                }
             }
+            const float t = faddv(a0, a1);
+            if (redo) s = t;
         }
-        const float t = faddv(a0, a1);
-        if (redo) s = t;
+        if (active && j == 0 && alive) out[row] = s;
     }
-    if (active && j == 0 && alive) out[r0 + row] = s;
 }
 
-int launch_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, cudaStream_t s) {
+int launch_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, uint32_t flags,
+                     cudaStream_t s) {
     if (M == 0) return ANE_OK;
     ANE_ARG_CHECK(K % 32 == 0, "q8_0_gemv: K must be a multiple of 32");
     ANE_ARG_CHECK(((uintptr_t)W & 1) == 0, "q8_0_gemv: W must be 2-byte aligned");
     if (K % 256 == 0 && ((uintptr_t)W & 15) == 0 && ((uintptr_t)x & 15) == 0) {
-        // ~6 resident CTAs per SM, each 1 producer warp + nw compute warps (4 rows each)
-        const uint32_t sms = (uint32_t)num_sms();
-        // ANE_Q8_WARPS (1..8 compute warps) and ANE_Q8_SLOTS (2..8) override the
-        // shape-based choice (tuning aids)
-        static const int force_warps = env_int("ANE_Q8_WARPS"), force_slots = env_int("ANE_Q8_SLOTS");
-        uint32_t nw = force_warps > 0 ? (uint32_t)force_warps : (M + 4 * 6 * sms - 1) / (4 * 6 * sms);
-        nw = nw < 1 ? 1 : (nw > 8 ? 8 : nw);
-        const uint32_t rows = 4 * nw;
-        // as many ring slots as fit a fair share of the SM's shared memory (up to
-        // every chunk of the CTA): more bytes in flight per CTA from the start
-        const uint32_t blocks_per_sm = (((M + rows - 1) / rows) + sms - 1) / sms;
-        const size_t slot = (size_t)rows * kChunkBytes + kChunkXBytes;
-        const uint32_t nchunks = (K / 32 + kChunkBlocks - 1) / kChunkBlocks;
-        // (228 KB per SM, 1 KB of it reserved per resident CTA)
-        const size_t share = 227 * 1024 / (blocks_per_sm ? blocks_per_sm : 1) - 1024;
-        uint32_t nslots = share > 128 ? (uint32_t)((share - 128) / slot) : 2;
-        nslots = nslots < 2 ? 2 : (nslots > (uint32_t)kMaxSlots ? (uint32_t)kMaxSlots : nslots);
-        if (nslots > nchunks) nslots = nchunks < 2 ? 2 : nchunks;
-        if (force_slots > 0) nslots = force_slots < 2 ? 2 : (force_slots > kMaxSlots ? kMaxSlots : force_slots);
-        const size_t smem = 128 + (size_t)nslots * slot;
+        const Q8Plan p = plan_q8_stream(M, K, kChunkXBytes, 128);
         static const cudaError_t attr_err = cudaFuncSetAttribute(
             q8_0_gemv_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         ANE_CUDA_TRY(attr_err);
-        const uint32_t blocks = (M + rows - 1) / rows;
+        ANE_ARG_CHECK(p.smem <= 200 * 1024, "q8_0_gemv: shared-memory plan too large");
         const uint64_t row_bytes = (uint64_t)(K / 32) * 34;
         CUtensorMap wmap;
         int rc = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, row_bytes / 4, M, row_bytes,
-                                      kChunkBytes / 4, rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+                                      kQ8ChunkBytes / 4, kQ8RowsPerWarp, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
-        q8_0_gemv_stream_kernel<<<blocks, 32 * (nw + 1), smem, s>>>(wmap, W, x, out, M, K, nslots,
-                                                                    device_timeout_flag());
-        ANE_CHECK_LAUNCH();
-        return ANE_OK;
+        return launch_q8_stream(q8_0_gemv_stream_kernel, p, s, wmap, W, x, out, M, K, p.groups, p.warps, p.slots,
+                                flags, device_timeout_flag());
     }
     const size_t smem = (size_t)K * sizeof(float);
     ANE_ARG_CHECK(smem <= 200 * 1024, "q8_0_gemv: K too large for the shared activation buffer");

@@ -14,21 +14,18 @@
 // checked against the sequential CPU restatement within a tolerance).
 //
 // Memory: the weights stream through the same TMA ring as the fp32-activation
-// kernel (one producer warp, 16-block chunks per row); the activation blocks are
-// re-laid-out once per CTA into shared memory as an aligned int8 array + fp32
-// scales so each dp4a operand is one aligned 32-bit load.
+// kernel (q8_stream.cuh); the activation blocks arrive in shared memory by one
+// bulk copy and are re-laid-out once per CTA as an aligned int8 array + fp32
+// scales, so each dp4a operand is one aligned 32-bit load.
 #include <cuda_fp16.h>
 
 #include "ane_internal.cuh"
+#include "q8_stream.cuh"
 #include "sm100_ptx.cuh"
 
 namespace ane_b200 {
 namespace {
 
-constexpr int kCB = 16;             // blocks per chunk
-constexpr int kCBytes = kCB * 34;   // 544
-constexpr int kMaxSlotsQ = 8;  // full[8] + empty[8] fill the 128-byte barrier area
-static_assert((4 * kCBytes) % 128 == 0, "TMA destinations stay 128-byte aligned");
 
 // One warp per 32 blocks of x: thread j quantizes block (warp*32 + j)... one
 // thread per block keeps ggml's sequential amax (NaN behaviour included).
@@ -64,101 +61,133 @@ __global__ void quantize_q8_0_kernel(const float* __restrict__ x, uint8_t* __res
     }
 }
 
+// Work split, ring and launch: q8_stream.cuh.  A compute warp owns 4 rows; lane
+// = 4*pp + r takes block pair pp (blocks 2pp, 2pp+1 of the chunk) of row r.  A
+// pair is 68 bytes, so it starts 4-byte aligned in the stage and is read as 17
+// aligned words: the odd block's codes are words 9..16, the even block's codes
+// straddle words 0..8 (one funnel shift per word).  Per lane the block terms
+// are summed in block order, then across the 8 pairs by xor shuffles 4, 8, 16.
 __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ xq,
                                     float* __restrict__ out, int32_t* __restrict__ block_dots, uint32_t M, uint32_t K,
-                                    uint32_t nslots, int* err) {
+                                    uint32_t groups, uint32_t nw, uint32_t nslots, uint32_t flags, int* err) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t nw = blockDim.x / 32 - 1;
-    const uint32_t rows_per_cta = 4 * nw;
-    const uint32_t nb = K / 32, nchunks = (nb + kCB - 1) / kCB;
-    const uint32_t slot_bytes = rows_per_cta * kCBytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + nslots;
-    float* xd = reinterpret_cast<float*>(smem + 128);                       // nb scales
-    int8_t* xs = reinterpret_cast<int8_t*>(smem + 128 + round_up(nb * 4, 128));  // K codes
-    uint8_t* ring = smem + 128 + round_up(nb * 4, 128) + round_up(K, 128);
-    const uint32_t r0 = blockIdx.x * rows_per_cta;
-    const uint32_t nrows = min(rows_per_cta, M - r0);
+    const uint32_t nb = K / 32, nchunks = (nb + kQ8ChunkBlocks - 1) / kQ8ChunkBlocks;
+    const uint32_t slot_bytes = nw * kQ8WarpTileBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // nslots
+    uint64_t* empty = full + nslots;                     // nslots
+    uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + 128);
+    uint8_t* xraw = smem + 256;                                                // nb x 34 bytes, as in HBM
+    float* xd = reinterpret_cast<float*>(xraw + round_up(nb * 34, 128));       // nb scales
+    int8_t* xs = reinterpret_cast<int8_t*>(xraw + round_up(nb * 34, 128) + round_up(nb * 4, 128));  // K codes
+    uint8_t* ring = reinterpret_cast<uint8_t*>(xs) + round_up(K, 128);
+    const uint32_t g0 = (uint32_t)((uint64_t)groups * blockIdx.x / gridDim.x);
+    const uint32_t g1 = (uint32_t)((uint64_t)groups * (blockIdx.x + 1) / gridDim.x);
+    const uint32_t npass = (g1 - g0 + nw - 1) / nw, ntiles = npass * nchunks;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < nslots; s++) {
+        for (uint32_t s = 0; s < nslots; s++) {
             ptx::mbar_init(&full[s], 1);
             ptx::mbar_init(&empty[s], nw);
         }
+        ptx::mbar_init(xbar, 1);
         ptx::fence_mbarrier_init();
     }
-    // activation blocks -> aligned codes + scales (all threads)
-    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
-        const uint8_t* blk = xq + (size_t)b * 34;
-        xd[b] = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
-    }
-    for (uint32_t i = threadIdx.x; i < nb * 8; i += blockDim.x) {
-        const uint8_t* src = xq + (size_t)(i >> 3) * 34 + 2 + (i & 7) * 4;
-        const uint32_t w = (uint32_t)src[0] | ((uint32_t)src[1] << 8) | ((uint32_t)src[2] << 16) |
-                           ((uint32_t)src[3] << 24);
-        reinterpret_cast<uint32_t*>(xs)[i] = w;
-    }
     __syncthreads();
+    ptx::griddep_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
             ptx::prefetch_tmap(&wmap);
-            for (uint32_t c = 0; c < nchunks; c++) {
-                const uint32_t slot = c % nslots;
-                if (!ptx::mbar_wait(&empty[slot], ((c / nslots) & 1) ^ 1, err)) break;
-                ptx::mbar_arrive_expect_tx(&full[slot], slot_bytes);
-                ptx::tma_load_2d(ring + (size_t)slot * slot_bytes, &wmap, &full[slot], (int)(c * (kCBytes / 4)),
-                                 (int)r0);
+            auto issue_weights = [&](uint32_t t, uint32_t slot) {
+                const uint32_t pass = t / nchunks, c = t - pass * nchunks;
+                const uint32_t gp = g0 + pass * nw, nwp = min(nw, g1 - gp);
+                uint8_t* dst = ring + (size_t)slot * slot_bytes;
+                ptx::mbar_arrive_expect_tx(&full[slot], nwp * kQ8WarpTileBytes);
+                for (uint32_t w = 0; w < nwp; w++)
+                    ptx::tma_load_2d(dst + w * kQ8WarpTileBytes, &wmap, &full[slot], (int)(c * (kQ8ChunkBytes / 4)),
+                                     (int)((gp + w) * kQ8RowsPerWarp));
+            };
+            // static weights: the first stages' weight tiles are requested before
+            // the previous kernel on the stream has finished
+            const uint32_t pre = (flags & ANE_Q8_WEIGHTS_STATIC) ? min(nslots, ntiles) : 0;
+            for (uint32_t t = 0; t < pre; t++) issue_weights(t, t);
+            ptx::griddep_wait();  // xq may be written by the previous kernel
+            ptx::mbar_arrive_expect_tx(xbar, nb * 34);
+            ptx::bulk_load(xraw, xq, nb * 34, xbar);
+            for (uint32_t t = pre; t < ntiles; t++) {
+                const uint32_t slot = t % nslots;
+                if (!ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err)) break;
+                issue_weights(t, slot);
             }
         }
         return;
     }
-    // compute warp: 4 rows; per chunk, (row, block) pairs p = lane and lane + 32,
-    // row = p / 16, block = p % 16 -> each lane feeds two rows
-    const uint32_t wrow0 = (warp - 1) * 4;
-    const uint32_t ra = wrow0 + (lane >> 4), rb = wrow0 + 2 + (lane >> 4), bl = lane & 15;
-    float suma = 0.f, sumb = 0.f;
-    bool alive = true;
-    for (uint32_t c = 0; c < nchunks && alive; c++) {
-        const uint32_t slot = c % nslots;
-        if (!ptx::mbar_wait(&full[slot], (c / nslots) & 1, err)) { alive = false; break; }
-        const uint32_t b = c * kCB + bl;
-        if (b < nb) {
-            const int32_t* xw = reinterpret_cast<const int32_t*>(xs + (size_t)b * 32);
-            int4 x0 = *reinterpret_cast<const int4*>(xw), x1 = *reinterpret_cast<const int4*>(xw + 4);
-            const int32_t xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-            const float dx = xd[b];
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const uint32_t r = h ? rb : ra;
-                if (r >= nrows) continue;
-                const uint8_t* blk = ring + (size_t)slot * slot_bytes + r * kCBytes + bl * 34;
-                // qs starts 2 bytes into the block: 9 halfword-pair loads, byte-aligned words by permute
-                const unsigned short* hw = reinterpret_cast<const unsigned short*>(blk);
-                const float dw = __half2float(__ushort_as_half(hw[0]));
-                int32_t sumi = 0;
-#pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    const int32_t w = (int32_t)((uint32_t)hw[1 + 2 * k] | ((uint32_t)hw[2 + 2 * k] << 16));
-                    sumi = __dp4a(w, xv[k], sumi);
-                }
-                if (block_dots) block_dots[(size_t)(r0 + r) * nb + b] = sumi;
-                const float t = __fmul_rn(__int2float_rn(sumi), __fmul_rn(dw, dx));
-                if (h) sumb = __fadd_rn(sumb, t); else suma = __fadd_rn(suma, t);
-            }
+    // ------------------------------------------------------------ compute
+    ptx::griddep_wait();  // out / block_dots may belong to the previous kernel
+    const uint32_t cw = warp - 1;
+    bool alive = ptx::mbar_wait(xbar, 0, err);
+    if (alive) {  // activation blocks -> aligned codes + fp32 scales (compute warps only)
+        for (uint32_t i = cw * 32 + lane; i < nb * 8; i += nw * 32) {
+            const unsigned short* src = reinterpret_cast<const unsigned short*>(xraw + (i >> 3) * 34 + 2 + (i & 7) * 4);
+            reinterpret_cast<uint32_t*>(xs)[i] = (uint32_t)src[0] | ((uint32_t)src[1] << 16);
         }
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&empty[slot]);
+        for (uint32_t b = cw * 32 + lane; b < nb; b += nw * 32)
+            xd[b] = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(xraw + b * 34)));
     }
+    ptx::named_barrier_sync(1, nw * 32);
+    const uint32_t r = lane & 3, pp = lane >> 2;
+    for (uint32_t pass = 0; pass < npass && alive; pass++) {
+        const uint32_t gp = g0 + pass * nw;
+        const uint32_t row = (gp + cw) * kQ8RowsPerWarp + r;
+        const bool active = gp + cw < g1 && row < M;
+        float sum = 0.f;
+        for (uint32_t c = 0; c < nchunks; c++) {
+            const uint32_t t = pass * nchunks + c, slot = t % nslots;
+            if (!ptx::mbar_wait(&full[slot], (t / nslots) & 1, err)) { alive = false; break; }
+            const uint32_t b = c * kQ8ChunkBlocks + 2 * pp;  // first block of the pair
+            if (active && b < nb) {
+                const uint32_t* pw = reinterpret_cast<const uint32_t*>(ring + (size_t)slot * slot_bytes +
+                                                                        cw * kQ8WarpTileBytes + r * kQ8ChunkBytes +
+                                                                        pp * 68);
+                uint32_t w[17];
 #pragma unroll
-    for (int o = 1; o < 16; o <<= 1) {
-        suma = __fadd_rn(suma, __shfl_xor_sync(0xffffffffu, suma, o));
-        sumb = __fadd_rn(sumb, __shfl_xor_sync(0xffffffffu, sumb, o));
-    }
-    if (alive && bl == 0) {
-        if (ra < nrows) out[r0 + ra] = suma;
-        if (rb < nrows) out[r0 + rb] = sumb;
+                for (int k = 0; k < 17; k++) w[k] = pw[k];
+                const int4* x0 = reinterpret_cast<const int4*>(xs + (size_t)b * 32);
+                const int4 xa0 = x0[0], xa1 = x0[1], xb0 = x0[2], xb1 = x0[3];
+                const float dx0 = xd[b], dx1 = xd[b + 1];
+                int32_t s0 = 0, s1 = 0;
+                s0 = __dp4a((int)__funnelshift_r(w[0], w[1], 16), xa0.x, s0);
+                s0 = __dp4a((int)__funnelshift_r(w[1], w[2], 16), xa0.y, s0);
+                s0 = __dp4a((int)__funnelshift_r(w[2], w[3], 16), xa0.z, s0);
+                s0 = __dp4a((int)__funnelshift_r(w[3], w[4], 16), xa0.w, s0);
+                s0 = __dp4a((int)__funnelshift_r(w[4], w[5], 16), xa1.x, s0);
+                s0 = __dp4a((int)__funnelshift_r(w[5], w[6], 16), xa1.y, s0);
+                s0 = __dp4a((int)__funnelshift_r(w[6], w[7], 16), xa1.z, s0);
+                s0 = __dp4a((int)__funnelshift_r(w[7], w[8], 16), xa1.w, s0);
+                s1 = __dp4a((int)w[9], xb0.x, s1);
+                s1 = __dp4a((int)w[10], xb0.y, s1);
+                s1 = __dp4a((int)w[11], xb0.z, s1);
+                s1 = __dp4a((int)w[12], xb0.w, s1);
+                s1 = __dp4a((int)w[13], xb1.x, s1);
+                s1 = __dp4a((int)w[14], xb1.y, s1);
+                s1 = __dp4a((int)w[15], xb1.z, s1);
+                s1 = __dp4a((int)w[16], xb1.w, s1);
+                const float dw0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xffffu)));
+                const float dw1 = __half2float(__ushort_as_half((unsigned short)(w[8] >> 16)));
+                if (block_dots) {
+                    block_dots[(size_t)row * nb + b] = s0;
+                    block_dots[(size_t)row * nb + b + 1] = s1;
+                }
+                sum = __fadd_rn(sum, __fmul_rn(__int2float_rn(s0), __fmul_rn(dw0, dx0)));
+                sum = __fadd_rn(sum, __fmul_rn(__int2float_rn(s1), __fmul_rn(dw1, dx1)));
+            }
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&empty[slot]);
+        }
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+        if (active && alive && pp == 0) out[row] = sum;
     }
 }
 
@@ -175,38 +204,26 @@ int launch_quantize_q8_0(uint32_t K, const float* x, uint8_t* out, cudaStream_t 
 }
 
 int launch_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8_t* W, float* out, int32_t* block_dots,
-                        cudaStream_t s) {
+                        uint32_t flags, cudaStream_t s) {
     if (M == 0) return ANE_OK;
     ANE_ARG_CHECK(K % 256 == 0, "q8_0_gemv_q8: K must be a multiple of 256");
     ANE_ARG_CHECK(((uintptr_t)W & 15) == 0, "q8_0_gemv_q8: W must be 16-byte aligned");
-    const uint32_t sms = (uint32_t)num_sms();
-    static const int force_warps = env_int("ANE_Q8_WARPS"), force_slots = env_int("ANE_Q8_SLOTS");
-    uint32_t nw = force_warps > 0 ? (uint32_t)force_warps : (M + 4 * 6 * sms - 1) / (4 * 6 * sms);
-    nw = nw < 1 ? 1 : (nw > 8 ? 8 : nw);
-    const uint32_t rows = 4 * nw, nb = K / 32;
-    const size_t fixed = 128 + round_up((size_t)nb * 4, 128) + round_up(K, 128);
-    const uint32_t blocks = (M + rows - 1) / rows, blocks_per_sm = (blocks + sms - 1) / sms;
-    const uint32_t nchunks = (nb + kCB - 1) / kCB;
-    const size_t slot = (size_t)rows * kCBytes;
-    const size_t share = 227 * 1024 / (blocks_per_sm ? blocks_per_sm : 1) - 1024;  // 1 KB reserved per CTA
-    uint32_t nslots = share > fixed ? (uint32_t)((share - fixed) / slot) : 2;
-    nslots = nslots < 2 ? 2 : (nslots > (uint32_t)kMaxSlotsQ ? (uint32_t)kMaxSlotsQ : nslots);
-    if (nslots > nchunks) nslots = nchunks < 2 ? 2 : nchunks;
-    if (force_slots > 0) nslots = force_slots < 2 ? 2 : (force_slots > kMaxSlotsQ ? kMaxSlotsQ : force_slots);
-    const size_t smem = fixed + (size_t)nslots * slot;
-    ANE_ARG_CHECK(smem <= 200 * 1024, "q8_0_gemv_q8: K too large");
+    ANE_ARG_CHECK(((uintptr_t)xq & 15) == 0, "q8_0_gemv_q8: xq must be 16-byte aligned");
+    const uint32_t nb = K / 32;
+    // barriers (256) + the raw activation blocks + scales + aligned codes
+    const size_t fixed = 256 + round_up((size_t)nb * 34, 128) + round_up((size_t)nb * 4, 128) + round_up(K, 128);
+    const Q8Plan p = plan_q8_stream(M, K, 0, fixed);
+    ANE_ARG_CHECK(p.smem <= 200 * 1024, "q8_0_gemv_q8: K too large for the shared activation buffer");
     static const cudaError_t attr_err =
         cudaFuncSetAttribute(q8_0_gemv_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     ANE_CUDA_TRY(attr_err);
     const uint64_t row_bytes = (uint64_t)nb * 34;
     CUtensorMap wmap;
-    int rc = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, row_bytes / 4, M, row_bytes, kCBytes / 4,
-                                  rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    int rc = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, row_bytes / 4, M, row_bytes,
+                                  kQ8ChunkBytes / 4, kQ8RowsPerWarp, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    q8_0_gemv_q8_kernel<<<blocks, 32 * (nw + 1), smem, s>>>(wmap, xq, out, block_dots, M, K, nslots,
-                                                           device_timeout_flag());
-    ANE_CHECK_LAUNCH();
-    return ANE_OK;
+    return launch_q8_stream(q8_0_gemv_q8_kernel, p, s, wmap, xq, out, block_dots, M, K, p.groups, p.warps, p.slots,
+                            flags, device_timeout_flag());
 }
 
 }  // namespace ane_b200

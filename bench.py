@@ -221,7 +221,13 @@ def time_graph(fn, steps, stream):
 
 
 def q8_bench(ane, torch, dev, steps=50):
-    """Q8_0 matvec GB/s on the 7B shapes, rotating >= 4 weight copies (> L2)."""
+    """Q8_0 matvec GB/s on the 7B shapes, rotating >= 4 weight copies (> L2).
+
+    Legs per shape: mode R (fp32 activation, the reference's q8_0_gemv) and
+    mode Q (Q8_0 activation, config 3's ggml convention), each through the
+    plain entry point and with the static-weights flag (W is never written
+    between calls, so each call may start streaming W while the previous one
+    drains)."""
     import numpy as np
 
     out = {}
@@ -236,34 +242,29 @@ def q8_bench(ane, torch, dev, steps=50):
             Wv[:, 0] = torch.randint(0, 256, (Wv.shape[0],), dtype=torch.uint8, device=dev, generator=g)
             Wv[:, 1] = 0x1C
         x = torch.randn(cols, device=dev, generator=g)
-        y = torch.empty(rows, device=dev)
-        for i in range(3):
-            ane.q8_0_gemv(Ws[i % copies], x, rows, cols, out=y)
-        it = [0]
-
-        def step():
-            ane.q8_0_gemv(Ws[it[0] % copies], x, rows, cols, out=y)
-            it[0] += 1
-
-        eager_ms = time_events(step, steps, stream)
-        ms = time_graph(step, steps, stream)
-        nbytes = wbytes + 4 * cols + 4 * rows
-        # mode Q: activation quantized to Q8_0 (ggml convention), exact int32 block dots
         xq = ane.quantize_q8_0(x)
-        for i in range(3):
-            ane.q8_0_gemv_q8(Ws[i % copies], xq, rows, cols, out=y)
-        itq = [0]
+        y = torch.empty(rows, device=dev)
+        res = {"bytes": wbytes + 4 * cols + 4 * rows, "mode_q_bytes": wbytes + (cols // 32) * 34 + 4 * rows}
+        for name, fn, nbytes in [("mode_r", lambda W, st: ane.q8_0_gemv(W, x, rows, cols, out=y, static_weights=st),
+                                  res["bytes"]),
+                                 ("mode_q", lambda W, st: ane.q8_0_gemv_q8(W, xq, rows, cols, out=y, static_weights=st),
+                                  res["mode_q_bytes"])]:
+            for st in (False, True):
+                for i in range(3):
+                    fn(Ws[i % copies], st)
+                it = [0]
 
-        def step_q():
-            ane.q8_0_gemv_q8(Ws[itq[0] % copies], xq, rows, cols, out=y)
-            itq[0] += 1
+                def step():
+                    fn(Ws[it[0] % copies], st)
+                    it[0] += 1
 
-        ms_q = time_graph(step_q, steps, stream)
-        nbytes_q = wbytes + (cols // 32) * 34 + 4 * rows
-        out[f"{rows}x{cols}"] = {"gbs": nbytes / (ms * 1e-3) / 1e9, "us": ms * 1e3, "bytes": nbytes,
-                                 "mode_q_gbs": nbytes_q / (ms_q * 1e-3) / 1e9, "mode_q_us": ms_q * 1e3,
-                                 "eager_us": eager_ms * 1e3, "timing": "CUDA graph of back-to-back calls",
-                                 "weight_copies_rotated": copies}
+                ms = time_graph(step, steps, stream)
+                key = name + ("_static" if st else "")
+                res[key + "_gbs"] = nbytes / (ms * 1e-3) / 1e9
+                res[key + "_us"] = ms * 1e3
+        res["timing"] = "CUDA graph of back-to-back calls"
+        res["weight_copies_rotated"] = copies
+        out[f"{rows}x{cols}"] = res
         del Ws
     return out
 

@@ -127,6 +127,20 @@ int ane_quantize_q8_0_dev(uint32_t K, const float* x, void* xq_blocks, void* str
 int ane_q8_0_gemv_q8_dev(uint32_t M, uint32_t K, const void* xq_blocks, const void* W, float* out,
                          int32_t* block_dots, void* stream);
 
+/* The two matvecs above with a flags word.  The streamed kernels always start
+ * early (programmatic dependent launch) and read x / write out only once the
+ * previous kernel on the stream has finished.  ANE_Q8_WEIGHTS_STATIC promises
+ * that W is not written by the kernel that precedes this call on the stream
+ * (weights loaded once, then many matvecs), which lets the kernel start
+ * streaming W into shared memory while that kernel is still running.  Without
+ * the promise such a read could see W before the preceding kernel's writes.
+ * No counterpart in the reference (its calls are synchronous). */
+#define ANE_Q8_WEIGHTS_STATIC 1u
+int ane_q8_0_gemv_ex_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out,
+                         uint32_t flags, void* stream);
+int ane_q8_0_gemv_q8_ex_dev(uint32_t M, uint32_t K, const void* xq_blocks, const void* W, float* out,
+                            int32_t* block_dots, uint32_t flags, void* stream);
+
 /* dense_fused_i8 without any allocation.  No counterpart in the reference: it
  * exists for callers that cannot allocate device memory when they run the op
  * (a framework that already reserved nearly all GPU memory for its own pool, a

@@ -411,3 +411,70 @@ def test_q8_0_gemv_q8_mode(ane, M, K):
     bound = np.abs(ref_dots.astype(np.float64) * dw * dx[None, :]).sum(axis=1)
     got = out.cpu().numpy().astype(np.float64)
     assert np.all(np.abs(got - ref.astype(np.float64)) <= 1e-5 * bound + 1e-30)
+
+
+# ------------------------------------- back-to-back matvecs (early launch, PDL)
+@pytest.mark.parametrize("static_weights", [False, True])
+def test_q8_chain_reads_previous_output(ane, static_weights):
+    """Each matvec reads the vector the previous kernel just wrote and writes the
+    buffer the previous kernel read (ping-pong), with no host sync in between:
+    the streamed kernels start early but must see x only after the previous
+    kernel has finished, and must not overwrite its input while it runs."""
+    import torch
+
+    M = K = 4096
+    rng = np.random.default_rng(404)
+    Ws = [oracle.quantize_q8_0((rng.standard_normal((M, K)) * 0.02).astype(F32), M, K) for _ in range(2)]
+    x0 = rng.standard_normal(K).astype(F32)
+    Wg = [torch.from_numpy(w).cuda() for w in Ws]
+    bufs = [torch.from_numpy(x0).cuda(), torch.empty(K, device="cuda")]
+    steps = 6
+    snaps = []
+    for i in range(steps):  # mode R chain, no synchronisation inside
+        ane.q8_0_gemv(Wg[i % 2], bufs[i % 2], M, K, out=bufs[(i + 1) % 2], static_weights=static_weights)
+        snaps.append(bufs[(i + 1) % 2].clone())
+    x = x0
+    for i in range(steps):
+        y = oracle.q8_0_gemv(Ws[i % 2], x, M, K)
+        assert bits_equal(snaps[i].cpu().numpy(), y), f"step {i}"
+        x = y
+    # mode Q chain: quantize -> matvec -> quantize -> ..., again without syncs
+    xg = torch.from_numpy(x0).cuda()
+    outs = []
+    for i in range(steps):
+        xq = ane.quantize_q8_0(xg)
+        xg = ane.q8_0_gemv_q8(Wg[i % 2], xq, M, K, static_weights=static_weights)
+        outs.append(xg)
+    x = x0
+    for i in range(steps):
+        xq_ref = oracle.quantize_q8_0(x, 1, K)
+        ref = oracle.q8_0_gemv_q8(Ws[i % 2], xq_ref, M, K)
+        got = outs[i].cpu().numpy()
+        assert np.allclose(got, ref, rtol=1e-4, atol=1e-4), f"step {i}"
+        x = got  # continue from the GPU's own vector so rounding differences do not compound
+
+
+def test_q8_chain_in_cuda_graph(ane):
+    """The same early-launching kernels captured back to back in a CUDA graph."""
+    import torch
+
+    M, K = 11008, 4096
+    rng = np.random.default_rng(405)
+    W = oracle.quantize_q8_0((rng.standard_normal((M, K)) * 0.02).astype(F32), M, K)
+    x = rng.standard_normal(K).astype(F32)
+    Wg, xg = torch.from_numpy(W).cuda(), torch.from_numpy(x).cuda()
+    outs = [torch.empty(M, device="cuda") for _ in range(4)]
+    ane.q8_0_gemv(Wg, xg, M, K, out=outs[0], static_weights=True)  # first call outside capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for o in outs:
+            ane.q8_0_gemv(Wg, xg, M, K, out=o, static_weights=True)
+    for o in outs:
+        o.fill_(float("nan"))
+    g.replay()
+    torch.cuda.synchronize()
+    ref = oracle.q8_0_gemv(W, x, M, K)
+    for o in outs:
+        assert bits_equal(o.cpu().numpy(), ref)
+    del g
