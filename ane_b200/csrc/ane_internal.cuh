@@ -57,6 +57,37 @@ inline int env_int(const char* name) {
     const char* v = getenv(name);
     return v ? atoi(v) : 0;
 }
+
+// Programmatic dependent launch (on unless ANE_PDL=0).
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("ANE_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+// Launches `kernel` with programmatic stream serialization: its CTAs may start
+// (barrier setup, descriptor prefetch) while the previous kernel on the stream
+// is still running.  Every kernel launched this way executes
+// griddepcontrol.wait before it touches global memory that an earlier kernel
+// may write, and griddepcontrol.launch_dependents to let the next one start.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, args...));
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
 // Verifies that the current device is sm_100 (the only target of this library).
 int require_sm100();
 
@@ -115,6 +146,17 @@ int launch_absmax_partials(const float* a, size_t na, const float* b, size_t nb,
                            int blocks_a, int blocks_b, cudaStream_t s);
 int absmax_blocks_for(size_t n);
 int launch_reduce_partials(const float* partials, int pblocks_a, int pblocks_b, float* absmax2, cudaStream_t s);
+// dense_fused_i8 prologue as one cooperative kernel reading A and B from HBM
+// once (prologue_coop.cu); partials must hold 2 x num_sms() floats.
+bool prologue_coop_supported(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, const int8_t* Aq,
+                             const int8_t* Bt);
+int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq, int8_t* Bt,
+                         float* scales, float* partials, cudaStream_t s);
+// dense_fused_i8 prologue in three programmatic-dependent launches with each fp32
+// tensor kept L2-resident between its absmax read and its quantize read;
+// partials must hold 2 x 1024 floats.
+int launch_quantize_staged(uint32_t M, uint32_t N, uint32_t K, uint32_t K16, const float* A, const float* B,
+                           int8_t* Aq, int8_t* Bt, float* scales, float* partials, cudaStream_t s);
 int launch_quantize_pair(uint32_t M, uint32_t N, uint32_t K, uint32_t K16, const float* A,
                          const float* B, int8_t* Aq, int8_t* Bt, float* scales, const float* partials,
                          int blocks_a, int blocks_b, cudaStream_t s);

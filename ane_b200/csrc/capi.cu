@@ -181,16 +181,24 @@ size_t fused_ws_layout(uint32_t M, uint32_t N, uint32_t K, FusedWs* w, void* bas
     return off;
 }
 
+// The quantize prologue: one cooperative kernel when the shape allows it
+// (prologue_coop.cu), else three programmatic-dependent launches.
+// ANE_PROLOGUE=staged forces the latter (tuning aid).
+static int launch_prologue(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
+                           int8_t* Bt, float* scales, float* partials, cudaStream_t s) {
+    static const char* force = getenv("ANE_PROLOGUE");
+    const bool staged = force && !strcmp(force, "staged");
+    if (!staged && prologue_coop_supported(M, N, K, A, B, Aq, Bt))
+        return launch_prologue_coop(M, N, K, A, B, Aq, Bt, scales, partials, s);
+    return launch_quantize_staged(M, N, K, (uint32_t)round_up(K, 16), A, B, Aq, Bt, scales, partials, s);
+}
+
 int dense_fused_on_stream(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t relu, const float* A,
                           const float* B, float* C, void* ws, cudaStream_t s) {
     FusedWs w{};
     fused_ws_layout(M, N, K, &w, ws);
     const uint32_t K16 = (uint32_t)round_up(K, 16);
-    const size_t na = (size_t)M * K, nb = (size_t)K * N;
-    const int pa = absmax_blocks_for(na), pb = absmax_blocks_for(nb);
-    int rc = launch_absmax_partials(A, na, B, nb, w.partials, pa, pb, s);
-    if (rc) return rc;
-    rc = launch_quantize_pair(M, N, K, K16, A, B, w.Aq, w.Bt, w.scales, w.partials, pa, pb, s);
+    int rc = launch_prologue(M, N, K, A, B, w.Aq, w.Bt, w.scales, w.partials, s);
     if (rc) return rc;
     GemmEpilogue ep{kOutFusedF32, w.scales, 0.f, 0.f, scale, relu ? 1 : 0, nullptr};
     return launch_gemm_s8_tc(M, N, K16, w.Aq, w.Bt, C, N, ep, s);
@@ -308,12 +316,7 @@ int ane_quantize_pair_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, co
                           int8_t* Bt, float* scales, float* partials, void* stream) {
     ANE_REQUIRE_GPU();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const uint32_t K16 = (uint32_t)round_up(K, 16);
-    const size_t na = (size_t)M * K, nb = (size_t)K * N;
-    const int pa = absmax_blocks_for(na), pb = absmax_blocks_for(nb);
-    int rc = launch_absmax_partials(A, na, B, nb, partials, pa, pb, s);
-    if (rc) return rc;
-    rc = launch_quantize_pair(M, N, K, K16, A, B, Aq, Bt, scales, partials, pa, pb, s);
+    int rc = launch_prologue(M, N, K, A, B, Aq, Bt, scales, partials, s);
     return rc ? rc : ok();
 }
 

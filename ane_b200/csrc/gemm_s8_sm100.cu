@@ -206,6 +206,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem_base = bars->tmem_base;
+    // programmatic dependent launch: the prologue above may overlap the previous
+    // kernel on the stream; operands, scales and C are touched only after it ends
+    ptx::griddep_launch_dependents();
+    ptx::griddep_wait();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -312,6 +316,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     ptx::cluster_sync();
     ptx::tc_fence_after();
     const uint32_t tmem_base = bars->tmem_base;
+    // programmatic dependent launch: the prologue above may overlap the previous
+    // kernel on the stream; operands, scales and C are touched only after it ends
+    ptx::griddep_launch_dependents();
+    ptx::griddep_wait();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -462,9 +470,7 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
         p.tiles_n = (N + S_BN - 1) / S_BN;
         const uint32_t tiles = p.tiles_m * p.tiles_n;
         const uint32_t grid = tiles < (uint32_t)sms ? tiles : (uint32_t)sms;
-        gemm_s8_single_kernel<<<grid, NUM_THREADS, S_SMEM, s>>>(ta, tb, p);
-        ANE_CHECK_LAUNCH();
-        return ANE_OK;
+        return launch_pdl(gemm_s8_single_kernel, dim3(grid), dim3(NUM_THREADS), S_SMEM, s, ta, tb, p);
     }
     static std::once_flag f2;
     static cudaError_t e2;
@@ -480,13 +486,15 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
     cfg.blockDim = dim3(NUM_THREADS, 1, 1);
     cfg.dynamicSmemBytes = P_SMEM;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_s8_pair_kernel, ta, tb, p));
     ANE_CHECK_LAUNCH();
     return ANE_OK;

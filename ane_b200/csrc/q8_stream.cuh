@@ -75,34 +75,12 @@ inline Q8Plan plan_q8_stream(uint32_t M, uint32_t K, size_t extra_slot_bytes, si
     return p;
 }
 
-inline bool q8_pdl_enabled() {
-    static const bool on = [] {
-        const char* v = getenv("ANE_PDL");
-        return !(v && v[0] == '0');
-    }();
-    return on;
-}
-
-// Launches a streamed Q8_0 kernel with programmatic stream serialization, so
-// that its CTAs may start (barrier setup, descriptor prefetch) before the
-// previous kernel on the stream has finished; the kernels read x and write out
-// only after griddepcontrol.wait, and W too unless the caller passed
-// ANE_Q8_WEIGHTS_STATIC.
+// Launches a streamed Q8_0 kernel with programmatic stream serialization; the
+// kernels read x and write out only after griddepcontrol.wait, and W too unless
+// the caller passed ANE_Q8_WEIGHTS_STATIC.
 template <typename... KArgs, typename... Args>
 int launch_q8_stream(void (*kernel)(KArgs...), const Q8Plan& p, cudaStream_t s, Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.ctas, 1, 1);
-    cfg.blockDim = dim3(32 * (p.warps + 1), 1, 1);
-    cfg.dynamicSmemBytes = p.smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = q8_pdl_enabled() ? 1 : 0;
-    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, args...));
-    ANE_CHECK_LAUNCH();
-    return ANE_OK;
+    return launch_pdl(kernel, dim3(p.ctas, 1, 1), dim3(32 * (p.warps + 1), 1, 1), p.smem, s, args...);
 }
 
 }  // namespace ane_b200

@@ -81,6 +81,13 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     return d;
 }
 
+// max that propagates NaN (IEEE maximum), on magnitudes: the absmax step.
+__device__ __forceinline__ float absmax_nan(float m, float a) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(m), "f"(fabsf(a)));
+    return d;
+}
+
 // 2-D tiled TMA load (no multicast) completing on an mbarrier.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
     asm volatile(

@@ -478,3 +478,30 @@ def test_q8_chain_in_cuda_graph(ane):
     for o in outs:
         assert bits_equal(o.cpu().numpy(), ref)
     del g
+
+
+# ------------------------------------- cooperative single-read quantize prologue
+@pytest.mark.parametrize("M,N,K,special", [
+    (2048, 2052, 2048, None),       # smallest shapes that take the cooperative prologue
+    (4100, 1024, 4096, "inf"),      # ragged per-CTA slices; +-inf in A
+    (1024, 4096, 4112, "nan"),      # K not a multiple of 64; NaN in B
+])
+def test_quantize_prologue_single_read(ane, M, N, K, special):
+    """Aq, Bt and both scales from the one-kernel prologue, each bit-exact."""
+    import torch
+
+    rng = np.random.default_rng(M + 3 * N + 7 * K)
+    A = rng.standard_normal((M, K)).astype(F32)
+    B = rng.standard_normal((K, N)).astype(F32)
+    A[rng.random((M, K)) < 0.001] *= 50
+    if special == "inf":
+        A[3, 5], A[M - 1, K - 1] = np.inf, -np.inf
+    if special == "nan":
+        B[K // 2, N - 3] = np.nan
+    Aq, Bt, scales = ane.quantize_pair(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
+    qa, sa = oracle.quantize_fp32_i8(A)
+    qb, sb = oracle.quantize_fp32_i8(B)
+    s = scales.cpu().numpy()
+    assert bits_equal(s, np.array([sa, sb], F32))
+    assert np.array_equal(Aq.cpu().numpy(), qa.reshape(M, K))
+    assert np.array_equal(Bt.cpu().numpy(), qb.reshape(K, N).T)
