@@ -68,6 +68,7 @@ SIGNATURES = {
     "ane_q8_0_gemv_q8_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _vp]),
     "ane_q8_0_gemv_ex_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _u32, _vp]),
     "ane_q8_0_gemv_q8_ex_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _u32, _vp]),
+    "ane_mul_mat_q8_0_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _u32, _vp]),
     "ane_device_timeouts": (_i32, []),
     "ane_kernel_launch_count": (_u64, []),
 }
@@ -284,6 +285,17 @@ def q8_0_gemv_q8(W, xq, M: int, K: int, out=None, block_dots=None, stream=None, 
     check(_lib.ane_q8_0_gemv_q8_ex_dev(M, K, xq.data_ptr(), W.data_ptr(), out.data_ptr(),
                                        block_dots.data_ptr() if block_dots is not None else None,
                                        WEIGHTS_STATIC if static_weights else 0, _stream_ptr(stream)))
+    return out
+
+
+def mul_mat_q8_0(W, x, M: int, K: int, out=None, block_dots=None, stream=None, static_weights=False):
+    """ggml MUL_MAT at batch 1: fp32 x[K] quantized to Q8_0 inside the Q8_0 x Q8_0 matvec."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty(M, dtype=torch.float32, device=W.device)
+    check(_lib.ane_mul_mat_q8_0_dev(M, K, x.data_ptr(), W.data_ptr(), out.data_ptr(),
+                                    block_dots.data_ptr() if block_dots is not None else None,
+                                    WEIGHTS_STATIC if static_weights else 0, _stream_ptr(stream)))
     return out
 
 

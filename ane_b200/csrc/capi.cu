@@ -420,6 +420,15 @@ int ane_q8_0_gemv_q8_ex_dev(uint32_t M, uint32_t K, const void* xq_blocks, const
     return rc ? rc : ok();
 }
 
+int ane_mul_mat_q8_0_dev(uint32_t M, uint32_t K, const float* x, const void* W, float* out, int32_t* block_dots,
+                         uint32_t flags, void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK((flags & ~ANE_Q8_WEIGHTS_STATIC) == 0, "mul_mat_q8_0: unknown flag bits");
+    int rc = launch_mul_mat_q8_0(M, K, x, static_cast<const uint8_t*>(W), out, block_dots, flags,
+                                 static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
 // ------------------------------------------------- host-facing (synchronous)
 int ane_quantize_fp32_i8(uint32_t count, const float* src, int8_t* dst, float* scale_out) {
     ANE_REQUIRE_GPU();

@@ -67,18 +67,28 @@ __global__ void quantize_q8_0_kernel(const float* __restrict__ x, uint8_t* __res
 // aligned words: the odd block's codes are words 9..16, the even block's codes
 // straddle words 0..8 (one funnel shift per word).  Per lane the block terms
 // are summed in block order, then across the 8 pairs by xor shuffles 4, 8, 16.
+// Bytes of the activation as it arrives in shared memory: Q8_0 blocks, or fp32
+// when the kernel quantizes the activation itself (XF32).
+__host__ __device__ constexpr uint32_t x_raw_bytes(bool xf32, uint32_t K) { return xf32 ? K * 4 : K / 32 * 34; }
+
+// XF32 = false: xq holds K/32 Q8_0 blocks.  XF32 = true: xq holds fp32 x[K] and
+// every CTA quantizes it with the ggml rule (the quantize_q8_0_kernel
+// arithmetic above, block by block) into the same shared-memory codes + scales,
+// so the result equals quantize_q8_0 followed by the XF32 = false kernel.
+template <bool XF32>
 __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ xq,
                                     float* __restrict__ out, int32_t* __restrict__ block_dots, uint32_t M, uint32_t K,
                                     uint32_t groups, uint32_t nw, uint32_t nslots, uint32_t flags, int* err) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t nb = K / 32, nchunks = (nb + kQ8ChunkBlocks - 1) / kQ8ChunkBlocks;
     const uint32_t slot_bytes = nw * kQ8WarpTileBytes;
+    const uint32_t xbytes = x_raw_bytes(XF32, K);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // nslots
     uint64_t* empty = full + nslots;                     // nslots
     uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + 128);
-    uint8_t* xraw = smem + 256;                                                // nb x 34 bytes, as in HBM
-    float* xd = reinterpret_cast<float*>(xraw + round_up(nb * 34, 128));       // nb scales
-    int8_t* xs = reinterpret_cast<int8_t*>(xraw + round_up(nb * 34, 128) + round_up(nb * 4, 128));  // K codes
+    uint8_t* xraw = smem + 256;                                                // the activation as in HBM
+    float* xd = reinterpret_cast<float*>(xraw + round_up(xbytes, 128));        // nb scales
+    int8_t* xs = reinterpret_cast<int8_t*>(xraw + round_up(xbytes, 128) + round_up(nb * 4, 128));  // K codes
     uint8_t* ring = reinterpret_cast<uint8_t*>(xs) + round_up(K, 128);
     const uint32_t g0 = (uint32_t)((uint64_t)groups * blockIdx.x / gridDim.x);
     const uint32_t g1 = (uint32_t)((uint64_t)groups * (blockIdx.x + 1) / gridDim.x);
@@ -113,8 +123,8 @@ __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, co
             const uint32_t pre = (flags & ANE_Q8_WEIGHTS_STATIC) ? min(nslots, ntiles) : 0;
             for (uint32_t t = 0; t < pre; t++) issue_weights(t, t);
             ptx::griddep_wait();  // xq may be written by the previous kernel
-            ptx::mbar_arrive_expect_tx(xbar, nb * 34);
-            ptx::bulk_load(xraw, xq, nb * 34, xbar);
+            ptx::mbar_arrive_expect_tx(xbar, xbytes);
+            ptx::bulk_load(xraw, xq, xbytes, xbar);
             for (uint32_t t = pre; t < ntiles; t++) {
                 const uint32_t slot = t % nslots;
                 if (!ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err)) break;
@@ -127,7 +137,38 @@ __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, co
     ptx::griddep_wait();  // out / block_dots may belong to the previous kernel
     const uint32_t cw = warp - 1;
     bool alive = ptx::mbar_wait(xbar, 0, err);
-    if (alive) {  // activation blocks -> aligned codes + fp32 scales (compute warps only)
+    if (alive && XF32) {  // quantize: one thread per 32-element block
+        for (uint32_t b = cw * 32 + lane; b < nb; b += nw * 32) {
+            const float4* xb = reinterpret_cast<const float4*>(xraw) + b * 8;
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const float4 t = xb[j];
+                v[4 * j] = t.x;
+                v[4 * j + 1] = t.y;
+                v[4 * j + 2] = t.z;
+                v[4 * j + 3] = t.w;
+            }
+            float amax = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                const float a = fabsf(v[j]);
+                amax = amax > a ? amax : a;
+            }
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            xd[b] = __half2float(__float2half_rn(d));
+            uint32_t* dst = reinterpret_cast<uint32_t*>(xs + (size_t)b * 32);
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                uint32_t w = 0;
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    w |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[j + i], id)) << (8 * i);
+                dst[j / 4] = w;
+            }
+        }
+    } else if (alive) {  // activation blocks -> aligned codes + fp32 scales (compute warps only)
         for (uint32_t i = cw * 32 + lane; i < nb * 8; i += nw * 32) {
             const unsigned short* src = reinterpret_cast<const unsigned short*>(xraw + (i >> 3) * 34 + 2 + (i & 7) * 4);
             reinterpret_cast<uint32_t*>(xs)[i] = (uint32_t)src[0] | ((uint32_t)src[1] << 16);
@@ -203,27 +244,39 @@ int launch_quantize_q8_0(uint32_t K, const float* x, uint8_t* out, cudaStream_t 
     return ANE_OK;
 }
 
-int launch_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8_t* W, float* out, int32_t* block_dots,
-                        uint32_t flags, cudaStream_t s) {
+template <bool XF32>
+static int launch_gemv_q8(uint32_t M, uint32_t K, const uint8_t* x, const uint8_t* W, float* out, int32_t* block_dots,
+                          uint32_t flags, cudaStream_t s) {
     if (M == 0) return ANE_OK;
     ANE_ARG_CHECK(K % 256 == 0, "q8_0_gemv_q8: K must be a multiple of 256");
     ANE_ARG_CHECK(((uintptr_t)W & 15) == 0, "q8_0_gemv_q8: W must be 16-byte aligned");
-    ANE_ARG_CHECK(((uintptr_t)xq & 15) == 0, "q8_0_gemv_q8: xq must be 16-byte aligned");
+    ANE_ARG_CHECK(((uintptr_t)x & 15) == 0, "q8_0_gemv_q8: the activation must be 16-byte aligned");
     const uint32_t nb = K / 32;
-    // barriers (256) + the raw activation blocks + scales + aligned codes
-    const size_t fixed = 256 + round_up((size_t)nb * 34, 128) + round_up((size_t)nb * 4, 128) + round_up(K, 128);
+    // barriers (256) + the raw activation + scales + aligned codes
+    const size_t fixed = 256 + round_up((size_t)x_raw_bytes(XF32, K), 128) + round_up((size_t)nb * 4, 128) +
+                         round_up(K, 128);
     const Q8Plan p = plan_q8_stream(M, K, 0, fixed);
     ANE_ARG_CHECK(p.smem <= 200 * 1024, "q8_0_gemv_q8: K too large for the shared activation buffer");
     static const cudaError_t attr_err =
-        cudaFuncSetAttribute(q8_0_gemv_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(q8_0_gemv_q8_kernel<XF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     ANE_CUDA_TRY(attr_err);
     const uint64_t row_bytes = (uint64_t)nb * 34;
     CUtensorMap wmap;
     int rc = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, row_bytes / 4, M, row_bytes,
                                   kQ8ChunkBytes / 4, kQ8RowsPerWarp, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    return launch_q8_stream(q8_0_gemv_q8_kernel, p, s, wmap, xq, out, block_dots, M, K, p.groups, p.warps, p.slots,
-                            flags, device_timeout_flag());
+    return launch_q8_stream(q8_0_gemv_q8_kernel<XF32>, p, s, wmap, x, out, block_dots, M, K, p.groups, p.warps,
+                            p.slots, flags, device_timeout_flag());
+}
+
+int launch_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8_t* W, float* out, int32_t* block_dots,
+                        uint32_t flags, cudaStream_t s) {
+    return launch_gemv_q8<false>(M, K, xq, W, out, block_dots, flags, s);
+}
+
+int launch_mul_mat_q8_0(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, int32_t* block_dots,
+                        uint32_t flags, cudaStream_t s) {
+    return launch_gemv_q8<true>(M, K, reinterpret_cast<const uint8_t*>(x), W, out, block_dots, flags, s);
 }
 
 }  // namespace ane_b200

@@ -1,0 +1,145 @@
+"""Q8_0 decode stack: a 7B-shaped stack of Q8_0 matvecs, N-sharded by rows.
+
+Per layer four projections run back to back (ggml MUL_MAT at batch 1 with
+Q8_0 weights, src/ggml-backend/ggml-ane.cpp:142-177; the activation of each
+matvec is first quantized to Q8_0, the ggml CPU convention for Q8_0 weights):
+
+    QKV      12288 x 4096
+    O         4096 x 4096
+    gate+up  22016 x 4096
+    down      4096 x 11008
+
+Attention, norms and the SwiGLU product are outside the quantized hot path.
+Every layer starts from its own seeded fp32 activation vector (norms would keep
+a real stack's scale bounded; a raw chain of N(0, 0.02) projections grows ~4x
+per layer and would overflow the fp16 block scales after ~10 layers); inside a
+layer each projection consumes the first K entries of the previous one's output
+(QKV -> O takes q, gate+up -> down takes the gate half), so the stack exercises
+exactly the quantize / matvec / all-gather path with its true dependencies.
+
+Sharding: every rank owns rows [r*M/world, (r+1)*M/world) of every weight
+matrix and computes that slice of every output; the slices are all-gathered
+into the full vector before the next projection.  Weight rows are generated
+from per-64-row-block seeds, so the logical matrices -- and, since each output
+row is computed the same way on any rank, the outputs -- do not depend on the
+number of ranks.
+
+`DecodeStack` takes its three steps (quantize, matvec, all-gather) as
+callables: the GPU path binds them to libane_b200 and NCCL, the CPU tests bind
+them to the oracle and gloo ranks.
+"""
+from __future__ import annotations
+
+from typing import Callable, Sequence
+
+import torch
+import torch.distributed as dist
+
+LAYER_SHAPES = (("qkv", 12288, 4096), ("o", 4096, 4096), ("gate_up", 22016, 4096), ("down", 4096, 11008))
+ROW_BLOCK = 64
+BLOCK_BYTES = 34  # Q8_0: fp16 d + 32 int8
+
+
+def q8_row_bytes(K: int) -> int:
+    return K // 32 * BLOCK_BYTES
+
+
+def stack_weight_bytes(layers: int, shapes=LAYER_SHAPES) -> int:
+    return layers * sum(M * q8_row_bytes(K) for _, M, K in shapes)
+
+
+def shard_rows(M: int, world: int, rank: int) -> tuple[int, int]:
+    if M % world or (M // world) % ROW_BLOCK:
+        raise ValueError(f"{M} rows do not split into {world} shards of whole {ROW_BLOCK}-row blocks")
+    m = M // world
+    return rank * m, (rank + 1) * m
+
+
+def block_seed(seed: int, layer: int, proj: int, block: int) -> int:
+    return (seed * 1_000_003 + layer * 10_007 + proj * 101 + block) & 0x7FFFFFFF
+
+
+class DecodeStack:
+    """Row-sharded stack of Q8_0 projections.
+
+    quantize(x_fp32[K]) -> xq (K/32 Q8_0 blocks, uint8)
+    matvec(W_local, xq, rows, K, out) -> out fp32[rows]
+    gather(y_local, y_full) -> y_full fp32[M]  (not called when world == 1: the
+        matvec then writes the full output directly)
+    make_rows(layer, proj, block, K) -> uint8 [ROW_BLOCK * row_bytes]  (one block of weight rows)
+    """
+
+    def __init__(self, layers: int, world: int, rank: int, make_rows: Callable, quantize: Callable,
+                 matvec: Callable, gather: Callable, shapes: Sequence = LAYER_SHAPES, alloc=None,
+                 make_inputs: Callable | None = None):
+        self.layers, self.world, self.rank = layers, world, rank
+        self.shapes = tuple(shapes)
+        for (_, M_prev, _), (name, _, K) in zip(self.shapes, self.shapes[1:]):
+            if K > M_prev:
+                raise ValueError(f"projection {name} reads {K} entries of a {M_prev}-entry vector")
+        self.quantize, self.matvec, self.gather = quantize, matvec, gather
+        alloc = alloc or (lambda n, dtype: torch.empty(n, dtype=dtype))
+        self.weights = []
+        for layer in range(layers):
+            ws = []
+            for p, (_, M, K) in enumerate(self.shapes):
+                r0, r1 = shard_rows(M, world, rank)
+                rb = q8_row_bytes(K)
+                W = alloc((r1 - r0) * rb, torch.uint8)
+                for i, blk in enumerate(range(r0 // ROW_BLOCK, r1 // ROW_BLOCK)):
+                    W[i * ROW_BLOCK * rb:(i + 1) * ROW_BLOCK * rb] = make_rows(layer, p, blk, K)
+                ws.append(W)
+            self.weights.append(ws)
+        width = max(max(M, K) for _, M, K in self.shapes)
+        self.h = [alloc(width, torch.float32), alloc(width, torch.float32)]
+        k0 = self.shapes[0][2]
+        self.inputs = make_inputs(layers, k0) if make_inputs else torch.randn(layers, k0)  # per-layer x
+        self.y_local = {M: alloc(M // world, torch.float32) for _, M, _ in self.shapes} if world > 1 else {}
+
+    def forward(self, trace: list | None = None) -> torch.Tensor:
+        """One token through every layer; returns the last projection's full output."""
+        cur = 0
+        for layer in range(self.layers):
+            for p, (_, M, K) in enumerate(self.shapes):
+                xin = self.inputs[layer] if p == 0 else self.h[cur][:K]
+                xq = self.quantize(xin)
+                out = self.h[1 - cur][:M]
+                if self.world == 1:
+                    self.matvec(self.weights[layer][p], xq, M, K, out)
+                else:
+                    y_loc = self.matvec(self.weights[layer][p], xq, M // self.world, K, self.y_local[M])
+                    self.gather(y_loc, out)
+                if trace is not None:
+                    trace.append((layer, p, xin.clone(), out.clone()))
+                cur = 1 - cur
+        return self.h[cur][:self.shapes[-1][1]]
+
+
+# ------------------------------------------------------------------ GPU binding
+def gpu_stack(layers: int, device, world: int = 1, rank: int = 0, group=None, seed: int = 5,
+              shapes: Sequence = LAYER_SHAPES, static_weights: bool = True) -> DecodeStack:
+    """DecodeStack on libane_b200 (one launch per projection: Q8_0 activation
+    quantization fused into the Q8_0 x Q8_0 matvec) with an NCCL all-gather."""
+    import ane_b200 as ane
+
+    def make_rows(layer, p, blk, K):
+        g = torch.Generator(device=device).manual_seed(block_seed(seed, layer, p, blk))
+        w = torch.randn(ROW_BLOCK * K, device=device, generator=g) * 0.02
+        return ane.quantize_q8_0(w)
+
+    # the activation's Q8_0 quantization runs inside the matvec (ggml MUL_MAT at batch 1)
+    def quantize(x):
+        return x
+
+    def matvec(W, x, rows, K, out):
+        return ane.mul_mat_q8_0(W, x, rows, K, out=out, static_weights=static_weights)
+
+    def gather(y_loc, y_full):
+        dist.all_gather_into_tensor(y_full, y_loc, group=group)
+
+    def make_inputs(n, K):
+        g = torch.Generator(device=device).manual_seed(seed + 17)
+        return torch.randn(n, K, device=device, generator=g)
+
+    alloc = lambda n, dtype: torch.empty(n, dtype=dtype, device=device)  # noqa: E731
+    return DecodeStack(layers, world, rank, make_rows, quantize, matvec, gather, shapes, alloc, make_inputs)

@@ -56,6 +56,7 @@ def parse():
     p.add_argument("--impl", default="ane_b200", choices=["ane_b200", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-q8", action="store_true")
+    p.add_argument("--no-decode", action="store_true", help="skip the 32-layer Q8_0 decode-stack leg")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (profiling runs)")
     p.add_argument("--no-clocks", action="store_true", help="skip nvidia-smi sampling and its soak (profiling runs)")
     return p.parse_args()
@@ -269,6 +270,56 @@ def q8_bench(ane, torch, dev, steps=50):
     return out
 
 
+def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
+    """Config 5: 32-layer 7B-shaped Q8_0 decode stack at batch 1 (QKV, O, gate+up,
+    down per layer; 6.88 GB of Q8_0 weights, far above L2), rows sharded over
+    the ranks with an NCCL all-gather after every projection.  One token = one
+    pass over every layer.  1 GPU: the token is a CUDA graph of 256 launches."""
+    from ane_b200 import decode
+
+    t0 = time.perf_counter()
+    stack = decode.gpu_stack(layers, dev, world=world, rank=rank, group=group)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    stack.forward()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    g = None
+    if world == 1:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            stack.forward()
+        run = g.replay
+    else:
+        run = stack.forward
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    if group is not None:
+        torch.distributed.barrier(group)
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record(stream)
+    for _ in range(reps):
+        run()
+    e_ev.record(stream)
+    torch.cuda.synchronize()
+    ms = s_ev.elapsed_time(e_ev) / reps
+    if group is not None:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=group)
+        ms = float(t.item())
+    del g
+    wbytes = decode.stack_weight_bytes(layers)
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    peaks = load_peaks()
+    return {"layers": layers, "batch": 1, "n_gpus": world, "weight_bytes": wbytes, "ms_per_token": ms,
+            "gbs": gbs, "per_gpu_hbm_frac": gbs / world / peaks["hbm_gbs"],
+            "launches_per_token": 4 * layers, "activation": "Q8_0 (ggml convention), static weights",
+            "timing": ("CUDA graph replay of one token" if world == 1 else "eager, NCCL all-gather per projection")
+                      + f", {reps} tokens, CUDA events" + ("" if world == 1 else ", max over ranks"),
+            "build_s": build_s}
+
+
 def run_ours(args):
     import torch
 
@@ -424,6 +475,10 @@ def run_ours(args):
                "ms_per_step": e2e_s * 1e3, "path": path}
 
     q8 = None
+    dec = None
+    if not args.no_decode:
+        dec = decode_bench(torch, dev, world=world, rank=rank, group=pg)
+
     if not args.no_q8 and rank == 0:
         q8 = q8_bench(ane, torch, dev)
 
@@ -452,7 +507,7 @@ def run_ours(args):
                      "algorithmic_bytes": M * K + N * K + 4 * M * N, "gemm_ms": gemm_ms},
         "stages_ms": {"quantize_pair": q_ms, "gemm": gemm_ms, "step": ms, "step_without_all_gather": no_gather_ms},
         "e2e": e2e, "gpu_launches": int(launches), "gpu_launches_per_step": launches_per_step,
-        "clocks": clocks, "q8_0_gemv": q8, "cpu_baseline": cpu,
+        "clocks": clocks, "q8_0_gemv": q8, "decode_stack": dec, "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
     if pg is not None:

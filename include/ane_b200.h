@@ -136,6 +136,15 @@ int ane_q8_0_gemv_q8_dev(uint32_t M, uint32_t K, const void* xq_blocks, const vo
  * the promise such a read could see W before the preceding kernel's writes.
  * No counterpart in the reference (its calls are synchronous). */
 #define ANE_Q8_WEIGHTS_STATIC 1u
+/* ggml MUL_MAT at batch 1 with Q8_0 weights and an fp32 activation
+ * (src/ggml-backend/ggml-ane.cpp:142-177 hands the fp32 src1 to q8_0_gemv;
+ * ggml's own CPU path first quantizes src1 to Q8_0): x[K] is quantized to
+ * Q8_0 with the ggml rule inside the matvec, then the Q8_0 x Q8_0 matvec runs.
+ * out (and block_dots, NULL to skip) equal ane_quantize_q8_0_dev followed by
+ * ane_q8_0_gemv_q8_ex_dev bit for bit, in one launch.  K % 256 == 0, W and x
+ * 16-byte aligned, flags as above. */
+int ane_mul_mat_q8_0_dev(uint32_t M, uint32_t K, const float* x, const void* W, float* out, int32_t* block_dots,
+                         uint32_t flags, void* stream);
 int ane_q8_0_gemv_ex_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out,
                          uint32_t flags, void* stream);
 int ane_q8_0_gemv_q8_ex_dev(uint32_t M, uint32_t K, const void* xq_blocks, const void* W, float* out,

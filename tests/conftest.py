@@ -17,3 +17,14 @@ def kats():
     import numpy as np
 
     return np.load(os.path.join(ROOT, "tests", "golden", "reference_kats.npz"))
+
+
+@pytest.fixture(scope="session")
+def ane():
+    """libane_b200 on a CUDA device (GPU tests only)."""
+    import torch
+
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import ane_b200
+
+    return ane_b200

@@ -1,0 +1,56 @@
+"""The Q8_0 decode stack on the GPU (config 5 shapes, 1 GPU), step by step
+against the oracle: each projection's fp32 output must lie within 1e-5 of the
+sum of |block terms| of the oracle's Q8_0 x Q8_0 matvec of the same input."""
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _check_step(W, x, M, K, y):
+    xq = oracle.quantize_q8_0(x, 1, K)
+    ref, dots = oracle.q8_0_gemv_q8(W, xq, M, K, with_dots=True)
+    dw = W.reshape(M, K // 32, 34)[:, :, 0:2].copy().view(np.float16)[..., 0].astype(np.float64)
+    dx = xq.reshape(K // 32, 34)[:, 0:2].copy().view(np.float16)[:, 0].astype(np.float64)
+    bound = np.abs(dots.astype(np.float64) * dw * dx[None, :]).sum(axis=1)
+    assert np.all(np.abs(y.astype(np.float64) - ref.astype(np.float64)) <= 1e-5 * bound + 1e-30)
+
+
+@pytest.mark.parametrize("shapes", ["small", "config5"])
+def test_decode_stack_steps(ane, shapes):
+    import torch
+
+    from ane_b200.decode import LAYER_SHAPES, gpu_stack
+
+    sh = LAYER_SHAPES if shapes == "config5" else (("qkv", 512, 256), ("o", 256, 256), ("gate_up", 512, 256),
+                                                   ("down", 256, 256))
+    layers = 1 if shapes == "config5" else 2
+    stack = gpu_stack(layers, torch.device("cuda", 0), shapes=sh, seed=9)
+    trace = []
+    out = stack.forward(trace)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    for (l, p, x, y) in trace:
+        _, M, K = sh[p]
+        _check_step(stack.weights[l][p].cpu().numpy(), x.cpu().numpy(), M, K, y.cpu().numpy())
+
+
+def test_decode_stack_graph_replay_matches_eager(ane):
+    import torch
+
+    from ane_b200.decode import gpu_stack
+
+    sh = (("qkv", 512, 256), ("o", 256, 256), ("gate_up", 512, 256), ("down", 256, 256))
+    stack = gpu_stack(3, torch.device("cuda", 0), shapes=sh, seed=4)
+    eager = stack.forward().clone()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        res = stack.forward()
+    res.fill_(float("nan"))
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(res, eager)
+    del g

@@ -18,16 +18,6 @@ F32 = np.float32
 REL_TOL = 1e-5  # north_star: fp32 outputs within 1e-5 relative
 
 
-@pytest.fixture(scope="module")
-def ane():
-    import torch
-
-    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
-    import ane_b200
-
-    return ane_b200
-
-
 def bits_equal(a, b):
     a = np.ascontiguousarray(a, F32)
     b = np.ascontiguousarray(b, F32)
@@ -505,3 +495,26 @@ def test_quantize_prologue_single_read(ane, M, N, K, special):
     assert bits_equal(s, np.array([sa, sb], F32))
     assert np.array_equal(Aq.cpu().numpy(), qa.reshape(M, K))
     assert np.array_equal(Bt.cpu().numpy(), qb.reshape(K, N).T)
+
+
+# ----------------------------------- ggml MUL_MAT: activation quantized in-kernel
+@pytest.mark.parametrize("M,K", [(4096, 4096), (22016, 4096), (4096, 11008), (40, 256)])
+def test_mul_mat_q8_0_equals_quantize_then_gemv(ane, M, K):
+    """One-launch MUL_MAT (fp32 x) == quantize_q8_0 + Q8_0 x Q8_0 matvec, bit for
+    bit, block dots included; the block dots also match the oracle."""
+    import torch
+
+    rng = np.random.default_rng(M + 5 * K)
+    W = oracle.quantize_q8_0((rng.standard_normal((M, K)) * 0.02).astype(F32), M, K)
+    x = rng.standard_normal(K).astype(F32)
+    x[32:64] = 0.0         # d = 0 block
+    x[96] = 3e-39          # subnormal input
+    Wg, xg = torch.from_numpy(W).cuda(), torch.from_numpy(x).cuda()
+    d1 = torch.empty((M, K // 32), dtype=torch.int32, device="cuda")
+    d2 = torch.empty_like(d1)
+    y1 = ane.mul_mat_q8_0(Wg, xg, M, K, block_dots=d1)
+    y2 = ane.q8_0_gemv_q8(Wg, ane.quantize_q8_0(xg), M, K, block_dots=d2)
+    assert torch.equal(d1, d2)
+    assert torch.equal(y1.view(torch.int32), y2.view(torch.int32))
+    _, ref_dots = oracle.q8_0_gemv_q8(W, oracle.quantize_q8_0(x, 1, K), M, K, with_dots=True)
+    assert np.array_equal(d1.cpu().numpy(), ref_dots)
