@@ -69,6 +69,12 @@ SIGNATURES = {
     "ane_q8_0_gemv_ex_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _u32, _vp]),
     "ane_q8_0_gemv_q8_ex_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _u32, _vp]),
     "ane_mul_mat_q8_0_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _u32, _vp]),
+    "ane_q8_stack_plan_create": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp]),
+    "ane_q8_stack_run": (_i32, [_vp, _vp]),
+    "ane_q8_stack_plan_free": (None, [_vp]),
+    "ane_ipc_get_handle": (_i32, [_vp, _vp, _vp]),
+    "ane_ipc_open_handle": (_i32, [_vp, _vp]),
+    "ane_ipc_close_handle": (_i32, [_vp]),
     "ane_device_timeouts": (_i32, []),
     "ane_kernel_launch_count": (_u64, []),
 }
@@ -272,6 +278,13 @@ def quantize_q8_0(x, out=None, stream=None):
 
 
 WEIGHTS_STATIC = 1  # ANE_Q8_WEIGHTS_STATIC: W is not written by the kernel just before the call
+
+
+class Q8StackProj(ctypes.Structure):
+    """ane_q8_stack_proj (include/ane_b200.h)."""
+    _fields_ = [("W", ctypes.c_void_p), ("rows_local", ctypes.c_uint32), ("K", ctypes.c_uint32),
+                ("x", ctypes.c_void_p), ("x_tagged", ctypes.c_uint32), ("out", ctypes.c_void_p * 8),
+                ("out_all", ctypes.c_void_p)]
 
 
 def q8_0_gemv_q8(W, xq, M: int, K: int, out=None, block_dots=None, stream=None, static_weights=False):

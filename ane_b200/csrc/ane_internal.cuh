@@ -197,6 +197,11 @@ int launch_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, f
 int launch_quantize_q8_0(uint32_t K, const float* x, uint8_t* out, cudaStream_t s);
 int launch_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8_t* W, float* out, int32_t* block_dots,
                         uint32_t flags, cudaStream_t s);
+// Persistent decode-stack kernel (decode_stack.cu).
+int stack_plan_create(const ane_q8_stack_proj* projs, uint32_t nproj, uint32_t world, uint32_t rank, uint32_t* ctl,
+                      void** plan_out);
+int stack_plan_run(void* plan, cudaStream_t s);
+void stack_plan_free(void* plan);
 // ggml MUL_MAT at batch 1: fp32 x quantized to Q8_0 inside the matvec.
 int launch_mul_mat_q8_0(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, int32_t* block_dots,
                         uint32_t flags, cudaStream_t s);

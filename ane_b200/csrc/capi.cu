@@ -429,6 +429,74 @@ int ane_mul_mat_q8_0_dev(uint32_t M, uint32_t K, const float* x, const void* W, 
     return rc ? rc : ok();
 }
 
+int ane_q8_stack_plan_create(const ane_q8_stack_proj* projs, uint32_t nproj, uint32_t world, uint32_t rank,
+                             uint32_t* ctl, void** plan) {
+    ANE_REQUIRE_GPU();
+    int rc = stack_plan_create(projs, nproj, world, rank, ctl, plan);
+    return rc ? rc : ok();
+}
+
+int ane_q8_stack_run(void* plan, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = stack_plan_run(plan, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+void ane_q8_stack_plan_free(void* plan) { stack_plan_free(plan); }
+
+namespace {
+// cuMemGetAddressRange through the runtime's driver entry point (no -lcuda).
+using MemGetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+MemGetAddressRangeFn address_range_fn() {
+    static MemGetAddressRangeFn fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (MemGetAddressRangeFn) nullptr;
+        return reinterpret_cast<MemGetAddressRangeFn>(f);
+    }();
+    return fn;
+}
+}  // namespace
+
+int ane_ipc_get_handle(const void* dev_ptr, void* handle64, uint64_t* offset) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(dev_ptr && handle64 && offset, "ipc: NULL argument");
+    auto fn = address_range_fn();
+    if (!fn) {
+        set_status(ANE_ERR_CUDA, "ipc: cuMemGetAddressRange unavailable");
+        return ANE_ERR_CUDA;
+    }
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (fn(&base, &size, (CUdeviceptr)dev_ptr) != CUDA_SUCCESS) {
+        set_status(ANE_ERR_INVALID_ARGUMENT, "ipc: pointer is not device memory");
+        return ANE_ERR_INVALID_ARGUMENT;
+    }
+    cudaIpcMemHandle_t h;
+    ANE_CUDA_TRY(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+    static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+    memcpy(handle64, &h, sizeof(h));
+    *offset = (uint64_t)((CUdeviceptr)dev_ptr - base);
+    return ok();
+}
+
+int ane_ipc_open_handle(const void* handle64, void** base) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(handle64 && base, "ipc: NULL argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    ANE_CUDA_TRY(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess));
+    return ok();
+}
+
+int ane_ipc_close_handle(void* base) {
+    ANE_REQUIRE_GPU();
+    ANE_CUDA_TRY(cudaIpcCloseMemHandle(base));
+    return ok();
+}
+
 // ------------------------------------------------- host-facing (synchronous)
 int ane_quantize_fp32_i8(uint32_t count, const float* src, int8_t* dst, float* scale_out) {
     ANE_REQUIRE_GPU();

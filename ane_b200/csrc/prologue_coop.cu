@@ -108,6 +108,7 @@ __device__ bool grid_barrier(unsigned int nblocks, int* err) {
         }
         ok_s = ok;
     }
+    __syncwarp();  // warp 0 reconverges after lane 0's spin
     __syncthreads();
     return ok_s != 0;
 }

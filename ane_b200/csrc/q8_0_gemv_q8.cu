@@ -20,6 +20,7 @@
 #include <cuda_fp16.h>
 
 #include "ane_internal.cuh"
+#include "q8_mmq.cuh"
 #include "q8_stream.cuh"
 #include "sm100_ptx.cuh"
 
@@ -138,36 +139,8 @@ __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, co
     const uint32_t cw = warp - 1;
     bool alive = ptx::mbar_wait(xbar, 0, err);
     if (alive && XF32) {  // quantize: one thread per 32-element block
-        for (uint32_t b = cw * 32 + lane; b < nb; b += nw * 32) {
-            const float4* xb = reinterpret_cast<const float4*>(xraw) + b * 8;
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const float4 t = xb[j];
-                v[4 * j] = t.x;
-                v[4 * j + 1] = t.y;
-                v[4 * j + 2] = t.z;
-                v[4 * j + 3] = t.w;
-            }
-            float amax = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const float a = fabsf(v[j]);
-                amax = amax > a ? amax : a;
-            }
-            const float d = __fdiv_rn(amax, 127.0f);
-            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-            xd[b] = __half2float(__float2half_rn(d));
-            uint32_t* dst = reinterpret_cast<uint32_t*>(xs + (size_t)b * 32);
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                uint32_t w = 0;
-#pragma unroll
-                for (int i = 0; i < 4; i++)
-                    w |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[j + i], id)) << (8 * i);
-                dst[j / 4] = w;
-            }
-        }
+        for (uint32_t b = cw * 32 + lane; b < nb; b += nw * 32)
+            q8_quantize_block<false>(reinterpret_cast<const float*>(xraw) + (size_t)b * 32, xs, xd, b);
     } else if (alive) {  // activation blocks -> aligned codes + fp32 scales (compute warps only)
         for (uint32_t i = cw * 32 + lane; i < nb * 8; i += nw * 32) {
             const unsigned short* src = reinterpret_cast<const unsigned short*>(xraw + (i >> 3) * 34 + 2 + (i & 7) * 4);
@@ -176,6 +149,7 @@ __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, co
         for (uint32_t b = cw * 32 + lane; b < nb; b += nw * 32)
             xd[b] = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(xraw + b * 34)));
     }
+    __syncwarp();
     ptx::named_barrier_sync(1, nw * 32);
     const uint32_t r = lane & 3, pp = lane >> 2;
     for (uint32_t pass = 0; pass < npass && alive; pass++) {
@@ -191,43 +165,17 @@ __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, co
                 const uint32_t* pw = reinterpret_cast<const uint32_t*>(ring + (size_t)slot * slot_bytes +
                                                                         cw * kQ8WarpTileBytes + r * kQ8ChunkBytes +
                                                                         pp * 68);
-                uint32_t w[17];
-#pragma unroll
-                for (int k = 0; k < 17; k++) w[k] = pw[k];
-                const int4* x0 = reinterpret_cast<const int4*>(xs + (size_t)b * 32);
-                const int4 xa0 = x0[0], xa1 = x0[1], xb0 = x0[2], xb1 = x0[3];
-                const float dx0 = xd[b], dx1 = xd[b + 1];
-                int32_t s0 = 0, s1 = 0;
-                s0 = __dp4a((int)__funnelshift_r(w[0], w[1], 16), xa0.x, s0);
-                s0 = __dp4a((int)__funnelshift_r(w[1], w[2], 16), xa0.y, s0);
-                s0 = __dp4a((int)__funnelshift_r(w[2], w[3], 16), xa0.z, s0);
-                s0 = __dp4a((int)__funnelshift_r(w[3], w[4], 16), xa0.w, s0);
-                s0 = __dp4a((int)__funnelshift_r(w[4], w[5], 16), xa1.x, s0);
-                s0 = __dp4a((int)__funnelshift_r(w[5], w[6], 16), xa1.y, s0);
-                s0 = __dp4a((int)__funnelshift_r(w[6], w[7], 16), xa1.z, s0);
-                s0 = __dp4a((int)__funnelshift_r(w[7], w[8], 16), xa1.w, s0);
-                s1 = __dp4a((int)w[9], xb0.x, s1);
-                s1 = __dp4a((int)w[10], xb0.y, s1);
-                s1 = __dp4a((int)w[11], xb0.z, s1);
-                s1 = __dp4a((int)w[12], xb0.w, s1);
-                s1 = __dp4a((int)w[13], xb1.x, s1);
-                s1 = __dp4a((int)w[14], xb1.y, s1);
-                s1 = __dp4a((int)w[15], xb1.z, s1);
-                s1 = __dp4a((int)w[16], xb1.w, s1);
-                const float dw0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xffffu)));
-                const float dw1 = __half2float(__ushort_as_half((unsigned short)(w[8] >> 16)));
+                int32_t s0, s1;
+                q8_pair(pw, xs, xd, b, s0, s1, sum);
                 if (block_dots) {
                     block_dots[(size_t)row * nb + b] = s0;
                     block_dots[(size_t)row * nb + b + 1] = s1;
                 }
-                sum = __fadd_rn(sum, __fmul_rn(__int2float_rn(s0), __fmul_rn(dw0, dx0)));
-                sum = __fadd_rn(sum, __fmul_rn(__int2float_rn(s1), __fmul_rn(dw1, dx1)));
             }
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&empty[slot]);
         }
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+        sum = q8_row_total(sum);
         if (active && alive && pp == 0) out[row] = sum;
     }
 }

@@ -61,9 +61,12 @@ __device__ __forceinline__ void griddep_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Named barrier over `nthreads` threads (a multiple of 32) of the CTA.
+// Named barrier over `nthreads` threads (a multiple of 32) of the CTA.  The
+// non-.aligned form: lanes of a warp may arrive at different times (one lane
+// spinning on a flag while the others already wait), which the .aligned form
+// (`bar.sync`) does not allow.
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Two IEEE fp32 fused multiply-adds (round to nearest even, no flush to zero)

@@ -143,3 +143,82 @@ def gpu_stack(layers: int, device, world: int = 1, rank: int = 0, group=None, se
 
     alloc = lambda n, dtype: torch.empty(n, dtype=dtype, device=device)  # noqa: E731
     return DecodeStack(layers, world, rank, make_rows, quantize, matvec, gather, shapes, alloc, make_inputs)
+
+
+# ------------------------------------------------- one persistent launch per token
+class FusedDecodeStack:
+    """The weights and inputs of a DecodeStack run as ONE persistent kernel per
+    token (ane_q8_stack_*): weight streaming never stops between projections,
+    and with world > 1 every CTA stores its output rows straight into every
+    rank's activation vector (CUDA-IPC peer pointers over NVLink) -- the
+    all-gather is part of the matvec.
+
+    Activations are two ping-pong TAGGED vectors per rank (projection j writes
+    vector j % 2; element = 8-byte {fp32 value, u32 tag} word) followed by two
+    control words, all zero at creation and never reset.
+    """
+
+    def __init__(self, stack: DecodeStack, device, group=None):
+        import ctypes
+
+        import ane_b200 as ane
+
+        self._ane = ane
+        world, rank = stack.world, stack.rank
+        self.nproj = stack.layers * len(stack.shapes)
+        width = stack.h[0].numel()
+        vec_bytes = width * 8
+        ctl_off = 2 * vec_bytes
+        self.block = torch.zeros(ctl_off + 64, dtype=torch.uint8, device=device)
+        base = self.block.data_ptr()
+        self._opened = []
+        peer = [0] * world
+        peer[rank] = base
+        if world > 1:
+            handle = (ctypes.c_uint8 * 64)()
+            off = ctypes.c_uint64()
+            ane.check(ane.lib.ane_ipc_get_handle(base, handle, ctypes.byref(off)))
+            everyone = [None] * world
+            dist.all_gather_object(everyone, (bytes(handle), off.value), group=group)
+            for r in range(world):
+                if r == rank:
+                    continue
+                h = (ctypes.c_uint8 * 64).from_buffer_copy(everyone[r][0])
+                b = ctypes.c_void_p()
+                ane.check(ane.lib.ane_ipc_open_handle(h, ctypes.byref(b)))
+                self._opened.append(b.value)
+                peer[r] = b.value + everyone[r][1]
+        projs = (ane.Q8StackProj * self.nproj)()
+        j = 0
+        for layer in range(stack.layers):
+            for p, (_, M, K) in enumerate(stack.shapes):
+                rows = M // world
+                pr = projs[j]
+                pr.W = stack.weights[layer][p].data_ptr()
+                pr.rows_local = rows
+                pr.K = K
+                if p == 0:
+                    pr.x, pr.x_tagged = stack.inputs[layer].data_ptr(), 0
+                else:
+                    pr.x, pr.x_tagged = base + ((j - 1) % 2) * vec_bytes, 1
+                for r in range(world):
+                    pr.out[r] = peer[r] + (j % 2) * vec_bytes + 8 * rank * rows
+                pr.out_all = base + (j % 2) * vec_bytes
+                j += 1
+        self.plan = ctypes.c_void_p()
+        ane.check(ane.lib.ane_q8_stack_plan_create(projs, self.nproj, world, rank, base + ctl_off,
+                                                   ctypes.byref(self.plan)))
+        words = self.block[:ctl_off].view(torch.float32).view(2, width, 2)
+        self.out = words[(self.nproj - 1) % 2, :stack.shapes[-1][1], 0]  # values of the last output
+
+    def forward(self, stream=None) -> torch.Tensor:
+        self._ane.check(self._ane.lib.ane_q8_stack_run(self.plan, self._ane._stream_ptr(stream)))
+        return self.out
+
+    def close(self):
+        if self.plan:
+            self._ane.lib.ane_q8_stack_plan_free(self.plan)
+            self.plan = None
+        for b in self._opened:
+            self._ane.lib.ane_ipc_close_handle(b)
+        self._opened = []

@@ -273,50 +273,70 @@ def q8_bench(ane, torch, dev, steps=50):
 def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
     """Config 5: 32-layer 7B-shaped Q8_0 decode stack at batch 1 (QKV, O, gate+up,
     down per layer; 6.88 GB of Q8_0 weights, far above L2), rows sharded over
-    the ranks with an NCCL all-gather after every projection.  One token = one
-    pass over every layer.  1 GPU: the token is a CUDA graph of 256 launches."""
+    the ranks.  One token = one pass over every layer.  Two paths:
+      fused     -- ONE persistent launch per token (ane_q8_stack_run); with N > 1
+                   each rank's rows go to every rank by NVLink peer stores;
+      chain     -- one MUL_MAT launch per projection (a CUDA graph on 1 GPU), NCCL
+                   all-gather per projection with N > 1."""
     from ane_b200 import decode
 
     t0 = time.perf_counter()
     stack = decode.gpu_stack(layers, dev, world=world, rank=rank, group=group)
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
+    stream = torch.cuda.current_stream()
+
+    def timed(run):
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        if group is not None:
+            torch.distributed.barrier(group)
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record(stream)
+        for _ in range(reps):
+            run()
+        e_ev.record(stream)
+        torch.cuda.synchronize()
+        ms = s_ev.elapsed_time(e_ev) / reps
+        if group is not None:
+            t = torch.tensor([ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=group)
+            ms = float(t.item())
+        return ms
+
     stack.forward()
     torch.cuda.synchronize()
-    stream = torch.cuda.current_stream()
     g = None
     if world == 1:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             stack.forward()
-        run = g.replay
+        chain_ms = timed(g.replay)
     else:
-        run = stack.forward
-    for _ in range(3):
-        run()
-    torch.cuda.synchronize()
-    if group is not None:
-        torch.distributed.barrier(group)
-    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s_ev.record(stream)
-    for _ in range(reps):
-        run()
-    e_ev.record(stream)
-    torch.cuda.synchronize()
-    ms = s_ev.elapsed_time(e_ev) / reps
-    if group is not None:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=group)
-        ms = float(t.item())
+        chain_ms = timed(stack.forward)
     del g
+    fused = decode.FusedDecodeStack(stack, dev, group=group)
+    try:
+        fused_ms = timed(fused.forward)
+        torch.cuda.synchronize()
+        if group is not None:
+            torch.distributed.barrier(group)
+    finally:
+        fused.close()
     wbytes = decode.stack_weight_bytes(layers)
-    gbs = wbytes / (ms * 1e-3) / 1e9
     peaks = load_peaks()
-    return {"layers": layers, "batch": 1, "n_gpus": world, "weight_bytes": wbytes, "ms_per_token": ms,
-            "gbs": gbs, "per_gpu_hbm_frac": gbs / world / peaks["hbm_gbs"],
-            "launches_per_token": 4 * layers, "activation": "Q8_0 (ggml convention), static weights",
-            "timing": ("CUDA graph replay of one token" if world == 1 else "eager, NCCL all-gather per projection")
-                      + f", {reps} tokens, CUDA events" + ("" if world == 1 else ", max over ranks"),
+    fused_path = "one persistent launch per token" + (", all-gather by NVLink peer stores" if world > 1 else "")
+    chain_path = (f"{4 * layers} MUL_MAT launches in a CUDA graph" if world == 1
+                  else f"{4 * layers} MUL_MAT launches + NCCL all-gather each")
+    best_ms, best_path = (fused_ms, fused_path) if fused_ms <= chain_ms else (chain_ms, chain_path)
+    gbs = wbytes / (best_ms * 1e-3) / 1e9
+    return {"layers": layers, "batch": 1, "n_gpus": world, "weight_bytes": wbytes, "ms_per_token": best_ms,
+            "gbs": gbs, "per_gpu_hbm_frac": gbs / world / peaks["hbm_gbs"], "path": best_path,
+            "fused_ms_per_token": fused_ms, "fused_gbs": wbytes / (fused_ms * 1e-3) / 1e9, "fused_path": fused_path,
+            "chain_ms_per_token": chain_ms, "chain_gbs": wbytes / (chain_ms * 1e-3) / 1e9, "chain_path": chain_path,
+            "activation": "Q8_0 (ggml convention), static weights",
+            "timing": f"{reps} tokens each path, CUDA events" + ("" if world == 1 else ", max over ranks"),
             "build_s": build_s}
 
 

@@ -150,6 +150,40 @@ int ane_q8_0_gemv_ex_dev(uint32_t M, uint32_t K, const float* in, const void* W,
 int ane_q8_0_gemv_q8_ex_dev(uint32_t M, uint32_t K, const void* xq_blocks, const void* W, float* out,
                             int32_t* block_dots, uint32_t flags, void* stream);
 
+/* ------------------------------------------------ decode stack (config 5)
+ * A chain of Q8_0 MUL_MATs (batch 1, Q8_0 activation, as ane_mul_mat_q8_0_dev)
+ * in ONE persistent cooperative launch, row-sharded over `world` GPUs.
+ * Outputs are TAGGED vectors: element i is one 8-byte word {fp32 value, u32
+ * tag}, written with a single store, so a reader that sees the expected tag
+ * has the value (no fence or flag).  Projection j reads x -- a plain fp32
+ * vector, or (x_tagged) the tagged output of projection j-1 -- and writes its
+ * rows_local results to out[r] on every rank r < world (CUDA-IPC mapped peer
+ * pointers; out[rank] is local); out_all is this rank's whole output vector
+ * of projection j (word 0).  ctl = this rank's 2 uint32 control words, zero
+ * before the first run and never reset; tagged vectors start zeroed.  Every
+ * rank runs the same plan shape the same number of times.  No counterpart in
+ * the reference (its ggml backend issues one synchronous q8_0_gemv per
+ * MUL_MAT). */
+typedef struct ane_q8_stack_proj {
+    const void* W;        /* this rank's rows_local x K/32 Q8_0 blocks, 16-byte aligned */
+    uint32_t rows_local;  /* rows of this rank */
+    uint32_t K;           /* multiple of 256 */
+    const void* x;        /* fp32[K] or K tagged words, this GPU's memory, 16-byte aligned */
+    uint32_t x_tagged;    /* 1: x is projection j-1's tagged output */
+    void* out[8];         /* per rank: where this rank's first output word goes on that rank */
+    const void* out_all;  /* this rank's tagged output vector of this projection */
+} ane_q8_stack_proj;
+int ane_q8_stack_plan_create(const ane_q8_stack_proj* projs, uint32_t nproj, uint32_t world, uint32_t rank,
+                             uint32_t* ctl, void** plan);
+int ane_q8_stack_run(void* plan, void* stream);
+void ane_q8_stack_plan_free(void* plan);
+/* CUDA IPC for the peer pointers above: a 64-byte handle of the allocation that
+ * holds dev_ptr plus dev_ptr's offset in it; open maps a peer's allocation
+ * (NVLink peer access enabled lazily) and returns its base. */
+int ane_ipc_get_handle(const void* dev_ptr, void* handle64, uint64_t* offset);
+int ane_ipc_open_handle(const void* handle64, void** base);
+int ane_ipc_close_handle(void* base);
+
 /* dense_fused_i8 without any allocation.  No counterpart in the reference: it
  * exists for callers that cannot allocate device memory when they run the op
  * (a framework that already reserved nearly all GPU memory for its own pool, a

@@ -54,3 +54,35 @@ def test_decode_stack_graph_replay_matches_eager(ane):
     torch.cuda.synchronize()
     assert torch.equal(res, eager)
     del g
+
+
+@pytest.mark.parametrize("shapes,layers", [("small", 3), ("config5", 2)])
+def test_fused_stack_equals_per_projection_chain(ane, shapes, layers):
+    """One persistent launch per token == the chain of MUL_MAT launches, bit for
+    bit, on repeated tokens (the counters only grow) and under graph replay."""
+    import torch
+
+    from ane_b200.decode import LAYER_SHAPES, FusedDecodeStack, gpu_stack
+
+    sh = LAYER_SHAPES if shapes == "config5" else (("qkv", 512, 256), ("o", 256, 256), ("gate_up", 512, 256),
+                                                   ("down", 256, 256))
+    stack = gpu_stack(layers, torch.device("cuda", 0), shapes=sh, seed=21)
+    ref = stack.forward().clone()
+    fused = FusedDecodeStack(stack, torch.device("cuda", 0))
+    try:
+        for _ in range(3):
+            out = fused.forward()
+            torch.cuda.synchronize()
+            assert torch.equal(out.view(torch.int32), ref.view(torch.int32))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fused.forward()
+        for _ in range(2):
+            fused.out.fill_(float("nan"))
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(fused.out.view(torch.int32), ref.view(torch.int32))
+        del g
+        assert ane.lib.ane_device_timeouts() == 0
+    finally:
+        fused.close()

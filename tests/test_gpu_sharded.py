@@ -78,3 +78,62 @@ def test_sharded_dense_fused_two_gpus_bit_exact(M, N, K, scale, relu, shard):
         p.join(timeout=300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert q.get(timeout=5) == 1
+
+
+def _stack_worker(rank, world, port, layers, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    fused = None
+    try:
+        import ane_b200 as ane
+        from ane_b200.decode import FusedDecodeStack, gpu_stack
+
+        sharded = gpu_stack(layers, dev, world=world, rank=rank, seed=33)
+        nccl_out = sharded.forward().clone()            # NCCL all-gather per projection
+        fused = FusedDecodeStack(sharded, dev)           # peer stores + counters, one launch
+        outs = [fused.forward().clone() for _ in range(3)]
+        single = gpu_stack(layers, dev, world=1, rank=0, seed=33).forward()  # one GPU, all rows
+        torch.cuda.synchronize()
+        ok = torch.equal(nccl_out.view(torch.int32), single.view(torch.int32)) and all(
+            torch.equal(o.view(torch.int32), single.view(torch.int32)) for o in outs)
+        ok = ok and ane.lib.ane_device_timeouts() == 0
+        flags = torch.tensor([1 if ok else 0], device=dev)
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+        if rank == 0:
+            result_q.put(int(flags.item()))
+    finally:
+        if fused is not None:
+            torch.cuda.synchronize()
+            dist.barrier()  # no rank unmaps a peer buffer while a peer still writes it
+            fused.close()
+        dist.destroy_process_group()
+
+
+def test_decode_stack_two_gpus_fused_and_nccl_equal_one_gpu():
+    """Config-5 decode stack (2 layers) row-sharded over 2 GPUs: the NCCL
+    all-gather version and the one-launch peer-store version both give the
+    1-GPU vector bit for bit, on repeated tokens."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_stack_worker, args=(r, 2, port, 2, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert q.get(timeout=5) == 1
