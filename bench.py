@@ -57,6 +57,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-q8", action="store_true")
     p.add_argument("--no-decode", action="store_true", help="skip the 32-layer Q8_0 decode-stack leg")
+    p.add_argument("--no-configs", action="store_true", help="skip the config 1 / 2-sweep / 4 legs")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (profiling runs)")
     p.add_argument("--no-clocks", action="store_true", help="skip nvidia-smi sampling and its soak (profiling runs)")
     return p.parse_args()
@@ -340,6 +341,102 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
             "build_s": build_s}
 
 
+def timed_steps_flushed(torch, fn, steps, stream, flush):
+    """Mean device ms of fn() with the L2 flushed (a 256 MiB write) before every
+    step; only fn() sits between the events."""
+    total = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record(stream)
+        fn()
+        e_ev.record(stream)
+        torch.cuda.synchronize()
+        total += s_ev.elapsed_time(e_ev)
+    return total / steps
+
+
+def config_legs(ane, torch, dev, steps=20):
+    """Configs 1, 2 (size sweep) and 4 of BASELINE.json at 1 GPU, each step with
+    the L2 flushed first (small inputs would otherwise be served from L2)."""
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    out = {}
+    # ---- config 1: MNIST-MLP forward (784 -> 128 ReLU -> 10), batch 50
+    g = torch.Generator(device=dev).manual_seed(1)
+    A = torch.rand((50, 784), device=dev, generator=g)
+    W1 = torch.randn((784, 128), device=dev, generator=g) * (2.0 / 784) ** 0.5
+    W2 = torch.randn((128, 10), device=dev, generator=g) * (2.0 / 128) ** 0.5
+    h = torch.empty((50, 128), device=dev)
+    y = torch.empty((50, 10), device=dev)
+
+    def mnist():
+        ane.dense_fused_i8(A, W1, 1.0, True, out=h)
+        ane.dense_fused_i8(h, W2, 1.0, False, out=y)
+
+    for _ in range(3):
+        mnist()
+    ms = timed_steps_flushed(torch, mnist, steps, stream, flush)
+    ops = 2 * 50 * 128 * 784 + 2 * 50 * 10 * 128
+    An, W1n, W2n = A.cpu().numpy(), W1.cpu().numpy(), W2.cpu().numpy()
+    Ah = torch.from_numpy(An).pin_memory()
+    hh = torch.empty((50, 128)).pin_memory()
+    yh = torch.empty((50, 10)).pin_memory()
+    W1h, W2h = torch.from_numpy(W1n).pin_memory(), torch.from_numpy(W2n).pin_memory()
+
+    def mnist_host():  # the reference-facing synchronous C entry point on host buffers
+        ane.check(ane.lib.ane_dense_fused_i8(50, 128, 784, 1.0, 1, Ah.data_ptr(), W1h.data_ptr(), hh.data_ptr()))
+        ane.check(ane.lib.ane_dense_fused_i8(50, 10, 128, 1.0, 0, hh.data_ptr(), W2h.data_ptr(), yh.data_ptr()))
+
+    for _ in range(3):
+        mnist_host()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        mnist_host()
+    host_ms = (time.perf_counter() - t0) * 1e3 / steps
+    out["config1_mnist_forward"] = {"us_device": ms * 1e3, "samples_per_s_device": 50 / (ms * 1e-3),
+                                    "us_host_entry": host_ms * 1e3, "ops": ops,
+                                    "timing": "two dense_fused_i8 calls per forward, L2 flushed before each "
+                                              "forward; host entry = wall clock of the synchronous C calls on pinned "
+                                              "host buffers"}
+    del A, W1, W2, h, y
+    # ---- config 2 sweep: M = N = K
+    sweep = {}
+    for n in (512, 1024, 2048, 8192):
+        g = torch.Generator(device=dev).manual_seed(n)
+        A = torch.randn((n, n), device=dev, generator=g)
+        B = torch.randn((n, n), device=dev, generator=g)
+        C = torch.empty((n, n), device=dev)
+        ws = ane.dense_fused_i8_workspace(n, n, n, dev)
+        f = lambda: ane.dense_fused_i8(A, B, 1.0, False, out=C, workspace=ws)  # noqa: E731
+        for _ in range(3):
+            f()
+        ms = timed_steps_flushed(torch, f, max(5, steps // 2), stream, flush)
+        sweep[str(n)] = {"tops": 2.0 * n ** 3 / (ms * 1e-3) / 1e12, "ms": ms}
+        del A, B, C, ws
+    out["config2_sweep"] = sweep
+    # ---- config 4: batched-token projection, N = 14336, K = 4096, ReLU, scale 0.125, 1% outliers x20
+    cfg4 = {}
+    g = torch.Generator(device=dev).manual_seed(4)
+    B = torch.randn((4096, 14336), device=dev, generator=g)
+    for m in (1, 8, 64, 512):
+        A = torch.randn((m, 4096), device=dev, generator=g)
+        A = torch.where(torch.rand(A.shape, device=dev, generator=g) < 0.01, A * 20, A)
+        C = torch.empty((m, 14336), device=dev)
+        ws = ane.dense_fused_i8_workspace(m, 14336, 4096, dev)
+        f = lambda: ane.dense_fused_i8(A, B, 0.125, True, out=C, workspace=ws)  # noqa: E731
+        for _ in range(3):
+            f()
+        ms = timed_steps_flushed(torch, f, steps, stream, flush)
+        nbytes = 9 * (4096 * m + 4096 * 14336) + 4 * m * 14336
+        cfg4[str(m)] = {"tops": 2.0 * m * 14336 * 4096 / (ms * 1e-3) / 1e12, "ms": ms,
+                        "gbs": nbytes / (ms * 1e-3) / 1e9, "bytes": nbytes}
+        del A, C, ws
+    out["config4_projection"] = cfg4
+    del B, flush
+    return out
+
+
 def run_ours(args):
     import torch
 
@@ -495,6 +592,10 @@ def run_ours(args):
                "ms_per_step": e2e_s * 1e3, "path": path}
 
     q8 = None
+    legs = None
+    if not args.no_configs and world == 1:
+        legs = config_legs(ane, torch, dev)
+
     dec = None
     if not args.no_decode:
         dec = decode_bench(torch, dev, world=world, rank=rank, group=pg)
@@ -527,7 +628,7 @@ def run_ours(args):
                      "algorithmic_bytes": M * K + N * K + 4 * M * N, "gemm_ms": gemm_ms},
         "stages_ms": {"quantize_pair": q_ms, "gemm": gemm_ms, "step": ms, "step_without_all_gather": no_gather_ms},
         "e2e": e2e, "gpu_launches": int(launches), "gpu_launches_per_step": launches_per_step,
-        "clocks": clocks, "q8_0_gemv": q8, "decode_stack": dec, "cpu_baseline": cpu,
+        "clocks": clocks, "q8_0_gemv": q8, "decode_stack": dec, "configs": legs, "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
     if pg is not None:
