@@ -185,8 +185,16 @@ struct GemmEpilogue {
 };
 // C[M x ldc] += epilogue(Aq[M x K] * Bt[N x K]^T); K multiple of 16, both K-major
 // with row stride K.
-int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const int8_t* Bt,
-                      void* C, size_t ldc, const GemmEpilogue& ep, cudaStream_t s);
+// Fused all-gather of the GEMM output (see Params in gemm_s8_sm100.cu).
+struct GatherArgs {
+    uint32_t world;
+    void* C_rank[8];
+    uint32_t* ctr_rank[8];
+};
+int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const int8_t* Bt, void* C, size_t ldc,
+                      const GemmEpilogue& ep, cudaStream_t s, const GatherArgs* gather = nullptr,
+                      uint32_t* grid_out = nullptr);
+int launch_gather_wait(const uint32_t* ctr, uint32_t* epoch, uint32_t per_call, cudaStream_t s);
 int launch_fill_epilogue_zero_k(uint32_t M, uint32_t N, void* C, size_t ldc, const GemmEpilogue& ep,
                                 cudaStream_t s);
 

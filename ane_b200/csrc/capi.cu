@@ -429,6 +429,29 @@ int ane_mul_mat_q8_0_dev(uint32_t M, uint32_t K, const float* x, const void* W, 
     return rc ? rc : ok();
 }
 
+int ane_gemm_s8_gather_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* Aq, const int8_t* Bt,
+                           const float* scales, float scale, uint8_t relu, uint32_t world, uint32_t rank,
+                           void* const* C_ranks, uint32_t ldc, uint32_t* const* ctr_ranks, uint32_t* epoch,
+                           void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(world >= 2 && world <= 8 && rank < world, "gemm gather: world must be 2..8, rank < world");
+    ANE_ARG_CHECK(C_ranks && ctr_ranks && epoch && scales, "gemm gather: NULL argument");
+    ANE_ARG_CHECK(M > 0 && N > 0 && K16 > 0, "gemm gather: empty problem");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    GatherArgs g{};
+    g.world = world;
+    for (uint32_t q = 0; q < world; q++) {
+        g.C_rank[q] = C_ranks[q];
+        g.ctr_rank[q] = ctr_ranks[q];
+    }
+    GemmEpilogue ep{kOutFusedF32, scales, 0.f, 0.f, scale, relu ? 1 : 0, nullptr};
+    uint32_t grid = 0;
+    int rc = launch_gemm_s8_tc(M, N, K16, Aq, Bt, C_ranks[rank], ldc, ep, s, &g, &grid);
+    if (rc) return rc;
+    rc = launch_gather_wait(ctr_ranks[rank], epoch, world * grid, s);
+    return rc ? rc : ok();
+}
+
 int ane_q8_stack_plan_create(const ane_q8_stack_proj* projs, uint32_t nproj, uint32_t world, uint32_t rank,
                              uint32_t* ctl, void** plan) {
     ANE_REQUIRE_GPU();

@@ -64,6 +64,8 @@ constexpr size_t S_SMEM = (size_t)S_STAGES * S_STAGE + EPI_BYTES + sizeof(Barrie
 constexpr size_t P_SMEM = (size_t)P_STAGES * P_STAGE + EPI_BYTES + sizeof(Barriers<P_STAGES>) + 1024;
 static_assert(S_SMEM <= 232448 && P_SMEM <= 232448, "shared memory budget");
 
+constexpr uint32_t kGatherMaxRanks = 8;
+
 struct Params {
     uint32_t M, N, K;
     uint32_t tiles_m, tiles_n, num_kb;
@@ -72,6 +74,12 @@ struct Params {
     int vec_ok;  // C rows allow 16-byte stores
     GemmEpilogue ep;
     int* err;
+    // fused all-gather (world > 1): every tile is also stored into each rank's
+    // gathered C (C_rank[q] = that rank's buffer at this rank's first row), and
+    // each CTA adds 1 to every rank's counter once its stores are issued
+    uint32_t world;
+    void* C_rank[kGatherMaxRanks];
+    uint32_t* ctr_rank[kGatherMaxRanks];
 };
 
 // max that propagates NaN (ARM FMAX, not IEEE maxNum); one instruction.
@@ -83,6 +91,16 @@ __device__ __forceinline__ float max_nan(float a, float b) {
 // ReLU with the reference's FMAX semantics: NaN stays NaN, and the "+ 0.0f"
 // turns a -0 result into +0 (FMAX(-0, +0) = +0) without changing anything else.
 __device__ __forceinline__ float relu_arm(float y) { return __fadd_rn(max_nan(y, 0.0f), 0.0f); }
+
+// Fused all-gather: after the CTA's last epilogue store, publish to every rank
+// (release at system scope: the peers read these rows over NVLink).
+__device__ __forceinline__ void gather_signal(const Params& p) {
+    if (p.world > 1 && threadIdx.x == 0) {
+        __threadfence_system();
+        for (uint32_t q = 0; q < p.world; q++)
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.ctr_rank[q]) : "memory");
+    }
+}
 
 __device__ __forceinline__ float tile_comb(const Params& p) {
     if (p.ep.mode == kOutRawI32) return 0.0f;
@@ -137,14 +155,16 @@ __device__ __forceinline__ void store_block(const Params& p, float comb, const u
         const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * 32 + ((cc ^ (rr & 7)) * 4));
         const uint32_t m = row0 + rr;
         if (m < p.M && n < p.N) {
-            uint32_t* out = reinterpret_cast<uint32_t*>(p.C) + (size_t)m * p.ldc + n;
-            if (p.vec_ok && n + 4 <= p.N) {
-                *reinterpret_cast<uint4*>(out) = val;
-            } else {
-                out[0] = val.x;
-                if (n + 1 < p.N) out[1] = val.y;
-                if (n + 2 < p.N) out[2] = val.z;
-                if (n + 3 < p.N) out[3] = val.w;
+            for (uint32_t q = 0; q < (p.world > 1 ? p.world : 1u); q++) {
+                uint32_t* out = reinterpret_cast<uint32_t*>(p.world > 1 ? p.C_rank[q] : p.C) + (size_t)m * p.ldc + n;
+                if (p.vec_ok && n + 4 <= p.N) {
+                    *reinterpret_cast<uint4*>(out) = val;
+                } else {
+                    out[0] = val.x;
+                    if (n + 1 < p.N) out[1] = val.y;
+                    if (n + 2 < p.N) out[2] = val.z;
+                    if (n + 3 < p.N) out[3] = val.w;
+                }
             }
         }
     }
@@ -273,6 +293,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     ptx::tc_fence_before();
     __syncthreads();
+    gather_signal(p);
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem_base, TMEM_COLS);
@@ -387,6 +408,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // every role of both has finished.
     ptx::tc_fence_before();
     ptx::cluster_sync();
+    gather_signal(p);
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc_cg2(tmem_base, TMEM_COLS);
@@ -434,7 +456,7 @@ int set_smem_attr_once(const void* fn, size_t bytes, std::once_flag& flag, cudaE
 }  // namespace
 
 int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const int8_t* Bt, void* C, size_t ldc,
-                      const GemmEpilogue& ep, cudaStream_t s) {
+                      const GemmEpilogue& ep, cudaStream_t s, const GatherArgs* gather, uint32_t* grid_out) {
     if (M == 0 || N == 0) return ANE_OK;
     if (K == 0) return launch_fill_epilogue_zero_k(M, N, C, ldc, ep, s);
     ANE_ARG_CHECK(K % 16 == 0, "gemm: K must be a multiple of 16 (TMA row stride)");
@@ -450,6 +472,19 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
     p.vec_ok = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
     p.ep = ep;
     p.err = device_timeout_flag();
+    p.world = 1;
+    if (gather && gather->world > 1) {
+        ANE_ARG_CHECK(gather->world <= kGatherMaxRanks, "gemm gather: at most 8 ranks");
+        p.world = gather->world;
+        bool aligned = (ldc % 4 == 0);
+        for (uint32_t q = 0; q < p.world; q++) {
+            ANE_ARG_CHECK(gather->C_rank[q] && gather->ctr_rank[q], "gemm gather: NULL peer pointer");
+            p.C_rank[q] = gather->C_rank[q];
+            p.ctr_rank[q] = gather->ctr_rank[q];
+            aligned = aligned && ((reinterpret_cast<uintptr_t>(gather->C_rank[q]) & 15) == 0);
+        }
+        p.vec_ok = aligned;
+    }
     const int sms = num_sms();
     // ANE_GEMM_KERNEL=single|pair overrides the shape-based choice (tuning aid).
     static const char* force = getenv("ANE_GEMM_KERNEL");
@@ -470,6 +505,7 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
         p.tiles_n = (N + S_BN - 1) / S_BN;
         const uint32_t tiles = p.tiles_m * p.tiles_n;
         const uint32_t grid = tiles < (uint32_t)sms ? tiles : (uint32_t)sms;
+        if (grid_out) *grid_out = grid;
         return launch_pdl(gemm_s8_single_kernel, dim3(grid), dim3(NUM_THREADS), S_SMEM, s, ta, tb, p);
     }
     static std::once_flag f2;
@@ -481,6 +517,7 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
     const uint32_t tiles = p.tiles_m * p.tiles_n;
     uint32_t pairs = (uint32_t)sms / 2;
     if (pairs > tiles) pairs = tiles;
+    if (grid_out) *grid_out = 2 * pairs;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
     cfg.blockDim = dim3(NUM_THREADS, 1, 1);
@@ -496,6 +533,32 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
     ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_s8_pair_kernel, ta, tb, p));
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
+
+// Fused all-gather, receiving side: one thread waits (bounded) until every CTA
+// of every rank has published this call's rows to this GPU, then bumps the
+// call count.  Counters only grow: call e needs (e + 1) x per_call arrivals.
+__global__ void gather_wait_kernel(const uint32_t* ctr, uint32_t* epoch, uint32_t per_call, int* err) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const uint32_t target = (*reinterpret_cast<volatile uint32_t*>(epoch) + 1u) * per_call;
+    const long long t0 = clock64();
+    while (true) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+        if ((int32_t)(v - target) >= 0) break;
+        if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
+            atomicAdd(err, 1);
+            break;
+        }
+        __nanosleep(100);
+    }
+    *epoch += 1u;
+}
+
+int launch_gather_wait(const uint32_t* ctr, uint32_t* epoch, uint32_t per_call, cudaStream_t s) {
+    gather_wait_kernel<<<1, 32, 0, s>>>(ctr, epoch, per_call, device_timeout_flag());
     ANE_CHECK_LAUNCH();
     return ANE_OK;
 }

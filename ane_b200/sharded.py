@@ -78,6 +78,43 @@ class ShardPlan:
         return C_local
 
 
+class PeerBuffers:
+    """A device tensor of this rank, opened on every rank through CUDA IPC:
+    ptrs[q] is rank q's copy of the same-shaped buffer as seen from this GPU
+    (ptrs[rank] is local).  Collective: every rank constructs it together."""
+
+    def __init__(self, nbytes: int, device, group=None):
+        import ctypes
+
+        import ane_b200 as ane
+
+        self._ane = ane
+        self.tensor = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        base = self.tensor.data_ptr()
+        handle = (ctypes.c_uint8 * 64)()
+        off = ctypes.c_uint64()
+        ane.check(ane.lib.ane_ipc_get_handle(base, handle, ctypes.byref(off)))
+        everyone = [None] * world
+        dist.all_gather_object(everyone, (bytes(handle), off.value), group=group)
+        self._opened = []
+        self.ptrs = []
+        for q in range(world):
+            if q == rank:
+                self.ptrs.append(base)
+                continue
+            h = (ctypes.c_uint8 * 64).from_buffer_copy(everyone[q][0])
+            b = ctypes.c_void_p()
+            ane.check(ane.lib.ane_ipc_open_handle(h, ctypes.byref(b)))
+            self._opened.append(b.value)
+            self.ptrs.append(b.value + everyone[q][1])
+
+    def close(self):
+        for b in self._opened:
+            self._ane.lib.ane_ipc_close_handle(b)
+        self._opened = []
+
+
 class ShardedDense:
     """dense_fused_i8 over this rank's part on its GPU.
 
@@ -85,10 +122,12 @@ class ShardedDense:
     shard="rows": operands a row block of A (M x K, M = rows per rank) and all
     of B (K x N_local, N_local = N)."""
 
-    def __init__(self, M: int, N_local: int, K: int, world: int, device, group=None, shard: str = "cols"):
+    def __init__(self, M: int, N_local: int, K: int, world: int, device, group=None, shard: str = "cols",
+                 fused_gather: bool = False):
         import ane_b200 as ane
 
         self.ane = ane
+        self.group, self.shard = group, shard
         self.M, self.N_local, self.K, self.world = M, N_local, K, world
         self.plan = ShardPlan(world, group, shard)
         K16 = (K + 15) // 16 * 16
@@ -100,6 +139,27 @@ class ShardedDense:
         self.scales = torch.empty(2, dtype=torch.float32, device=device)
         self.C_local = torch.empty((M, N_local), dtype=torch.float32, device=device)
         self.gathered = torch.empty((world, M, N_local), dtype=torch.float32, device=device)
+        # fused gather: the GEMM epilogue stores each tile into every rank's
+        # gathered C (one IPC-shared buffer per rank: C, then a counter and the
+        # call count); rows -> [world*M, N_local], cols -> [M, world*N_local]
+        self.fused = None
+        if fused_gather and world > 1:
+            import ctypes
+
+            c_bytes = world * M * N_local * 4
+            self.fused = PeerBuffers(c_bytes + 256, device, group)
+            rank = dist.get_rank(group)
+            if shard == "rows":
+                off, self.ldc = rank * M * N_local * 4, N_local
+                shape = (world * M, N_local)
+            else:
+                off, self.ldc = rank * N_local * 4, world * N_local
+                shape = (M, world * N_local)
+            self._c_ranks = (ctypes.c_void_p * world)(*[b + off for b in self.fused.ptrs])
+            self._ctr_ranks = (ctypes.c_void_p * world)(*[b + c_bytes for b in self.fused.ptrs])
+            self._epoch = self.fused.ptrs[rank] + c_bytes + 128
+            self._rank = rank
+            self.C_gathered = self.fused.tensor[:c_bytes].view(torch.float32).view(*shape)
 
     def _absmax2(self, A, B_local):
         ane = self.ane
@@ -110,6 +170,20 @@ class ShardedDense:
 
     def forward(self, A, B_local, scale: float = 1.0, relu: bool = False, gather: bool = True):
         ane = self.ane
+        if self.fused is not None and gather:
+            # the absmax all-reduce is also the handshake: every rank has entered
+            # this call (its earlier readers of C_gathered are done) before any
+            # GEMM epilogue stores into peers
+            absmax2 = global_absmax(self._absmax2(A, B_local), self.group)
+            ane.check(ane.lib.ane_quantize_pair_absmax_dev(self.M, self.N_local, self.K, A.data_ptr(),
+                                                           B_local.data_ptr(), self.Aq.data_ptr(),
+                                                           self.Bt.data_ptr(), absmax2.data_ptr(),
+                                                           self.scales.data_ptr(), ane._stream_ptr()))
+            ane.check(ane.lib.ane_gemm_s8_gather_dev(self.M, self.N_local, self.Aq.shape[1], self.Aq.data_ptr(),
+                                                     self.Bt.data_ptr(), self.scales.data_ptr(), float(scale),
+                                                     int(bool(relu)), self.world, self._rank, self._c_ranks,
+                                                     self.ldc, self._ctr_ranks, self._epoch, ane._stream_ptr()))
+            return self.C_gathered
 
         def quantize_gemm(A, B_local, absmax2):
             ane.check(ane.lib.ane_quantize_pair_absmax_dev(self.M, self.N_local, self.K, A.data_ptr(),
@@ -119,3 +193,8 @@ class ShardedDense:
             return ane.gemm_s8(self.Aq, self.Bt, self.scales, scale, relu, out=self.C_local)
 
         return self.plan.run(A, B_local, self._absmax2, quantize_gemm, gather, self.gathered)
+
+    def close(self):
+        if self.fused is not None:
+            self.fused.close()
+            self.fused = None

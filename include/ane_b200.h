@@ -177,6 +177,20 @@ int ane_q8_stack_plan_create(const ane_q8_stack_proj* projs, uint32_t nproj, uin
                              uint32_t* ctl, void** plan);
 int ane_q8_stack_run(void* plan, void* stream);
 void ane_q8_stack_plan_free(void* plan);
+/* int8 GEMM (as ane_gemm_s8_dev, out_mode 0) fused with an all-gather of C over
+ * `world` GPUs: every C tile is stored into each rank's gathered output from the
+ * epilogue (C_ranks[q] = rank q's buffer at this rank's first element, row
+ * stride ldc floats; CUDA-IPC peer pointers, C_ranks[rank] local), then every
+ * CTA bumps every rank's counter (ctr_ranks[q]); a final one-thread kernel
+ * waits (bounded) until this GPU has all ranks' tiles and bumps *epoch.
+ * Counters and epoch start at zero and only grow; every rank makes the same
+ * calls.  A stream-ordered collective before the call (the absmax all-reduce
+ * of the sharded dense_fused_i8) must separate it from the previous call's
+ * readers.  No counterpart in the reference. */
+int ane_gemm_s8_gather_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* Aq, const int8_t* Bt,
+                           const float* scales, float scale, uint8_t relu, uint32_t world, uint32_t rank,
+                           void* const* C_ranks, uint32_t ldc, uint32_t* const* ctr_ranks, uint32_t* epoch,
+                           void* stream);
 /* CUDA IPC for the peer pointers above: a 64-byte handle of the allocation that
  * holds dev_ptr plus dev_ptr's offset in it; open maps a peer's allocation
  * (NVLink peer access enabled lazily) and returns its base. */

@@ -21,7 +21,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, M, N, K, scale, relu, shard, result_q):
+def _worker(rank, world, port, M, N, K, scale, relu, shard, fused, result_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
 
@@ -39,17 +39,24 @@ def _worker(rank, world, port, M, N, K, scale, relu, shard, result_q):
         g = torch.Generator(device=dev).manual_seed(11)
         A = torch.randn((M, K), device=dev, generator=g)
         B = torch.randn((K, N), device=dev, generator=g)  # same full B on every rank
+        ref = ane.dense_fused_i8(A, B, scale, relu)  # single-GPU result on the same inputs
         if shard == "cols":
             n_local = N // world
-            part = ShardedDense(M, n_local, K, world, dev, shard="cols")
-            C = part.forward(A, B[:, rank * n_local:(rank + 1) * n_local].contiguous(), scale, relu)
+            part = ShardedDense(M, n_local, K, world, dev, shard="cols", fused_gather=fused)
+            args = (A, B[:, rank * n_local:(rank + 1) * n_local].contiguous())
         else:
             m_local = M // world
-            part = ShardedDense(m_local, N, K, world, dev, shard="rows")
-            C = part.forward(A[rank * m_local:(rank + 1) * m_local].contiguous(), B, scale, relu)
-        ref = ane.dense_fused_i8(A, B, scale, relu)  # single-GPU result on the same inputs
+            part = ShardedDense(m_local, N, K, world, dev, shard="rows", fused_gather=fused)
+            args = (A[rank * m_local:(rank + 1) * m_local].contiguous(), B)
+        same = True
+        for _ in range(3):  # repeated calls: the fused gather's counters only grow
+            C = part.forward(*args, scale, relu).clone()
+            torch.cuda.synchronize()
+            same = same and torch.equal(C.view(torch.int32), ref.view(torch.int32))
+        same = same and ane.lib.ane_device_timeouts() == 0
         torch.cuda.synchronize()
-        same = torch.equal(C.view(torch.int32), ref.view(torch.int32))
+        dist.barrier()  # no rank unmaps a peer buffer while a peer still writes it
+        part.close()
         flags = torch.tensor([1 if same else 0], device=dev)
         dist.all_reduce(flags, op=dist.ReduceOp.MIN)
         if rank == 0:
@@ -58,10 +65,14 @@ def _worker(rank, world, port, M, N, K, scale, relu, shard, result_q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("M,N,K,scale,relu,shard", [(512, 1024, 512, 1.0, False, "cols"),
                                                     (64, 14336, 4096, 0.125, True, "cols"),
-                                                    (1024, 768, 4096, 1.0, True, "rows")])
-def test_sharded_dense_fused_two_gpus_bit_exact(M, N, K, scale, relu, shard):
+                                                    (1024, 768, 4096, 1.0, True, "rows"),
+                                                    (4096, 4096, 4096, 1.0, False, "rows")])
+def test_sharded_dense_fused_two_gpus_bit_exact(M, N, K, scale, relu, shard, fused):
+    """NCCL all-gather (fused=False) or the gather fused into the GEMM epilogue
+    (peer stores, fused=True): either way the gathered C equals one GPU's."""
     import torch
 
     if torch.cuda.device_count() < 2:
@@ -71,7 +82,8 @@ def test_sharded_dense_fused_two_gpus_bit_exact(M, N, K, scale, relu, shard):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, M, N, K, scale, relu, shard, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, M, N, K, scale, relu, shard, fused, q))
+             for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
