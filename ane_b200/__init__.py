@@ -72,6 +72,8 @@ SIGNATURES = {
     "ane_q8_stack_plan_create": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp]),
     "ane_q8_stack_run": (_i32, [_vp, _vp]),
     "ane_q8_stack_plan_free": (None, [_vp]),
+    "ane_quantize_pair_xrank_dev": (_i32, [_u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _vp, _vp,
+                                           _vp, _vp]),
     "ane_gemm_s8_gather_dev": (_i32, [_u32, _u32, _u32, _vp, _vp, _vp, _f, _u8, _u32, _u32, _vp, _u32, _vp, _vp,
                                       _vp]),
     "ane_ipc_get_handle": (_i32, [_vp, _vp, _vp]),

@@ -150,8 +150,15 @@ int launch_reduce_partials(const float* partials, int pblocks_a, int pblocks_b, 
 // once (prologue_coop.cu); partials must hold 2 x num_sms() floats.
 bool prologue_coop_supported(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, const int8_t* Aq,
                              const int8_t* Bt);
+// Cross-GPU absmax exchange of the cooperative prologue (N-sharded dense_fused_i8).
+struct CoopXRank {
+    uint32_t world, rank;
+    void* slot_peer[8];  // per rank q: this rank's two 64-bit words in q's exchange area
+    const void* slots;   // this GPU's exchange area (2 words per rank)
+    uint32_t* ctl;       // this GPU's 2 control words
+};
 int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq, int8_t* Bt,
-                         float* scales, float* partials, cudaStream_t s);
+                         float* scales, float* partials, cudaStream_t s, const CoopXRank* x = nullptr);
 // dense_fused_i8 prologue in three programmatic-dependent launches with each fp32
 // tensor kept L2-resident between its absmax read and its quantize read;
 // partials must hold 2 x 1024 floats.

@@ -429,6 +429,24 @@ int ane_mul_mat_q8_0_dev(uint32_t M, uint32_t K, const float* x, const void* W, 
     return rc ? rc : ok();
 }
 
+int ane_quantize_pair_xrank_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
+                                int8_t* Bt, float* scales, float* partials, uint32_t world, uint32_t rank,
+                                void* const* slot_peer, const void* slots, uint32_t* ctl, void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(world >= 1 && world <= 8 && rank < world, "quantize xrank: world must be 1..8, rank < world");
+    ANE_ARG_CHECK(prologue_coop_supported(M, N, K, A, B, Aq, Bt),
+                  "quantize xrank: needs K % 16 == 0, N % 4 == 0, 16-byte alignment and M*K, K*N >= 2^22");
+    ANE_ARG_CHECK(world == 1 || (slot_peer && slots && ctl), "quantize xrank: NULL exchange pointer");
+    CoopXRank x{};
+    x.world = world;
+    x.rank = rank;
+    for (uint32_t q = 0; q < world && world > 1; q++) x.slot_peer[q] = slot_peer[q];
+    x.slots = slots;
+    x.ctl = ctl;
+    int rc = launch_prologue_coop(M, N, K, A, B, Aq, Bt, scales, partials, static_cast<cudaStream_t>(stream), &x);
+    return rc ? rc : ok();
+}
+
 int ane_gemm_s8_gather_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* Aq, const int8_t* Bt,
                            const float* scales, float scale, uint8_t relu, uint32_t world, uint32_t rank,
                            void* const* C_ranks, uint32_t ldc, uint32_t* const* ctr_ranks, uint32_t* epoch,

@@ -306,13 +306,75 @@ __device__ float global_absmax(const float* __restrict__ partials, unsigned int 
     return __uint_as_float(block_max(m));
 }
 
+// Cross-GPU absmax (N-sharded dense_fused_i8): every rank publishes its
+// tensor-wide absmax of A and of B to every rank as 64-bit {bits, tag} words
+// (one store each, through CUDA-IPC peer pointers) and takes the max of all
+// ranks' words carrying this call's tag, so each shard is quantized with the
+// scales one GPU would compute.  tag = this GPU's call count + 1, bumped by its
+// last CTA.  The exchange is also the entry handshake of a call: a rank leaves
+// it only after every rank has entered the same call.
+struct CoopRanks {
+    uint32_t world, rank;
+    uint64_t* slot_peer[8];  // on rank q: this rank's words {A, B} in q's exchange area
+    const uint64_t* slots;   // this GPU's exchange area: words {A, B} of every rank
+    uint32_t* ctl;           // this GPU's {calls, CTAs done}
+};
+
+__device__ __forceinline__ uint32_t exchange_absmax(const CoopRanks& xr, uint32_t which, uint32_t local_bits,
+                                                    uint32_t tag, int* err, bool* ok) {
+    __shared__ uint32_t m_s;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        const uint64_t w = (uint64_t)local_bits | ((uint64_t)tag << 32);
+        for (uint32_t q = 0; q < xr.world; q++)
+            asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(xr.slot_peer[q] + which), "l"(w) : "memory");
+    }
+    if (threadIdx.x == 0) m_s = local_bits;
+    __syncthreads();
+    if (threadIdx.x < xr.world) {
+        const uint64_t* p = xr.slots + 2 * threadIdx.x + which;
+        const long long t0 = clock64();
+        while (true) {
+            uint64_t v;
+            asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+            if ((uint32_t)(v >> 32) == tag) {
+                atomicMax(&m_s, (uint32_t)v);  // magnitude bits: NaN > inf > finite, like the reference's max
+                break;
+            }
+            if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
+                atomicAdd(err, 1);
+                *ok = false;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    __syncwarp();
+    __syncthreads();
+    return m_s;
+}
+
 __global__ void __launch_bounds__(kCoopThreads, 1)
     prologue_coop_kernel(const float* __restrict__ A, const float* __restrict__ B, int8_t* __restrict__ Aq,
                          int8_t* __restrict__ Bt, uint32_t M, uint32_t N, uint32_t K, float* __restrict__ scales,
-                         float* __restrict__ partials, int* err) {
+                         float* __restrict__ partials, CoopRanks xr, int* err) {
     extern __shared__ __align__(16) float4 cache[];
     __shared__ __align__(16) uint32_t stage[kUnitRows / 4 * kStageRow];
+    __shared__ uint32_t tag_s;
+    __shared__ int fail_s;
     const unsigned int G = gridDim.x, c = blockIdx.x;
+    if (threadIdx.x == 0) {
+        tag_s = xr.world > 1 ? *reinterpret_cast<volatile uint32_t*>(xr.ctl) + 1u : 0u;
+        fail_s = 0;
+    }
+    __syncthreads();
+    const uint32_t tag = tag_s;
+    auto rank_absmax = [&](uint32_t which, float local) -> float {
+        if (xr.world <= 1) return local;
+        bool ok = true;
+        const uint32_t m = exchange_absmax(xr, which, __float_as_uint(local), tag, err, &ok);
+        if (!ok) fail_s = 1;
+        return __uint_as_float(m);
+    };
 
     // ------------------------------------------------------------------ A
     const size_t na4 = (size_t)M * K / 4;
@@ -323,7 +385,9 @@ __global__ void __launch_bounds__(kCoopThreads, 1)
     if (threadIdx.x == 0) partials[c] = __uint_as_float(m);
     if (!grid_barrier(G, err)) return;
     float scale, inv;
-    scale_from_absmax(global_absmax(partials, G), &scale, &inv);
+    scale_from_absmax(rank_absmax(0, global_absmax(partials, G)), &scale, &inv);
+    __syncthreads();
+    if (fail_s) return;
     if (c == 0 && threadIdx.x == 0) scales[0] = scale;
     uint32_t* outA = reinterpret_cast<uint32_t*>(Aq) + a0;  // K % 16 == 0: Aq row stride is K
     if (fast_inv(inv))
@@ -377,12 +441,23 @@ __global__ void __launch_bounds__(kCoopThreads, 1)
     }
     if (threadIdx.x == 0) partials[G + c] = __uint_as_float(m);
     if (!grid_barrier(G, err)) return;
-    scale_from_absmax(global_absmax(partials + G, G), &scale, &inv);
+    scale_from_absmax(rank_absmax(1, global_absmax(partials + G, G)), &scale, &inv);
+    __syncthreads();
+    if (fail_s) return;
     if (c == 0 && threadIdx.x == 0) scales[1] = scale;
     if (fast_inv(inv))
         quantize_units_transposed<true>(B4, N4, K, N, nch, ub0, ub1, cache, stage, Bt, inv);
     else
         quantize_units_transposed<false>(B4, N4, K, N, nch, ub0, ub1, cache, stage, Bt, inv);
+    // this call is finished on this CTA; the last CTA of this GPU bumps the call count
+    if (xr.world > 1 && threadIdx.x == 0) {
+        const uint32_t prev = atomicAdd(xr.ctl + 1, 1u);
+        if (prev == G - 1) {
+            xr.ctl[1] = 0;
+            __threadfence();
+            atomicAdd(xr.ctl, 1u);
+        }
+    }
 }
 
 }  // namespace
@@ -397,7 +472,20 @@ bool prologue_coop_supported(uint32_t M, uint32_t N, uint32_t K, const float* A,
 }
 
 int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq, int8_t* Bt,
-                         float* scales, float* partials, cudaStream_t s) {
+                         float* scales, float* partials, cudaStream_t s, const CoopXRank* x) {
+    CoopRanks xr{};
+    xr.world = 1;
+    if (x && x->world > 1) {
+        ANE_ARG_CHECK(x->world <= 8 && x->rank < x->world && x->slots && x->ctl, "prologue: bad rank exchange");
+        xr.world = x->world;
+        xr.rank = x->rank;
+        for (uint32_t q = 0; q < x->world; q++) {
+            ANE_ARG_CHECK(x->slot_peer[q] && ((uintptr_t)x->slot_peer[q] & 7) == 0, "prologue: bad peer slot");
+            xr.slot_peer[q] = static_cast<uint64_t*>(x->slot_peer[q]);
+        }
+        xr.slots = static_cast<const uint64_t*>(x->slots);
+        xr.ctl = x->ctl;
+    }
     static const cudaError_t attr_err = cudaFuncSetAttribute(
         prologue_coop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCoopSmem);
     ANE_CUDA_TRY(attr_err);
@@ -411,7 +499,7 @@ int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, con
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, prologue_coop_kernel, A, B, Aq, Bt, M, N, K, scales, partials,
+    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, prologue_coop_kernel, A, B, Aq, Bt, M, N, K, scales, partials, xr,
                                     device_timeout_flag()));
     ANE_CHECK_LAUNCH();
     return ANE_OK;

@@ -147,7 +147,10 @@ class ShardedDense:
             import ctypes
 
             c_bytes = world * M * N_local * 4
-            self.fused = PeerBuffers(c_bytes + 256, device, group)
+            # after C: gather counter (+0), gather call count (+128), the
+            # prologue's absmax exchange area (+256, 2 words per rank), its
+            # control words (+512)
+            self.fused = PeerBuffers(c_bytes + 1024, device, group)
             rank = dist.get_rank(group)
             if shard == "rows":
                 off, self.ldc = rank * M * N_local * 4, N_local
@@ -158,6 +161,12 @@ class ShardedDense:
             self._c_ranks = (ctypes.c_void_p * world)(*[b + off for b in self.fused.ptrs])
             self._ctr_ranks = (ctypes.c_void_p * world)(*[b + c_bytes for b in self.fused.ptrs])
             self._epoch = self.fused.ptrs[rank] + c_bytes + 128
+            self._slot_peer = (ctypes.c_void_p * world)(*[b + c_bytes + 256 + 16 * rank for b in self.fused.ptrs])
+            self._slots = self.fused.ptrs[rank] + c_bytes + 256
+            self._xctl = self.fused.ptrs[rank] + c_bytes + 512
+            K16 = (K + 15) // 16 * 16
+            self._coop = (K % 16 == 0 and N_local % 4 == 0 and M * K >= (1 << 22) and K * N_local >= (1 << 22)
+                          and K16 == K)
             self._rank = rank
             self.C_gathered = self.fused.tensor[:c_bytes].view(torch.float32).view(*shape)
 
@@ -171,14 +180,23 @@ class ShardedDense:
     def forward(self, A, B_local, scale: float = 1.0, relu: bool = False, gather: bool = True):
         ane = self.ane
         if self.fused is not None and gather:
-            # the absmax all-reduce is also the handshake: every rank has entered
-            # this call (its earlier readers of C_gathered are done) before any
-            # GEMM epilogue stores into peers
-            absmax2 = global_absmax(self._absmax2(A, B_local), self.group)
-            ane.check(ane.lib.ane_quantize_pair_absmax_dev(self.M, self.N_local, self.K, A.data_ptr(),
-                                                           B_local.data_ptr(), self.Aq.data_ptr(),
-                                                           self.Bt.data_ptr(), absmax2.data_ptr(),
-                                                           self.scales.data_ptr(), ane._stream_ptr()))
+            # the absmax exchange (tagged peer words, or the NCCL all-reduce) is
+            # also the handshake: every rank has entered this call (its earlier
+            # readers of C_gathered are done) before any GEMM epilogue stores
+            # into peers
+            if self._coop and A.data_ptr() % 16 == 0 and B_local.data_ptr() % 16 == 0:
+                # one cooperative launch: A and B read once, absmax exchanged
+                # with the peers through tagged words (also the handshake)
+                ane.check(ane.lib.ane_quantize_pair_xrank_dev(
+                    self.M, self.N_local, self.K, A.data_ptr(), B_local.data_ptr(), self.Aq.data_ptr(),
+                    self.Bt.data_ptr(), self.scales.data_ptr(), self.partials.data_ptr(), self.world, self._rank,
+                    self._slot_peer, self._slots, self._xctl, ane._stream_ptr()))
+            else:
+                absmax2 = global_absmax(self._absmax2(A, B_local), self.group)
+                ane.check(ane.lib.ane_quantize_pair_absmax_dev(self.M, self.N_local, self.K, A.data_ptr(),
+                                                               B_local.data_ptr(), self.Aq.data_ptr(),
+                                                               self.Bt.data_ptr(), absmax2.data_ptr(),
+                                                               self.scales.data_ptr(), ane._stream_ptr()))
             ane.check(ane.lib.ane_gemm_s8_gather_dev(self.M, self.N_local, self.Aq.shape[1], self.Aq.data_ptr(),
                                                      self.Bt.data_ptr(), self.scales.data_ptr(), float(scale),
                                                      int(bool(relu)), self.world, self._rank, self._c_ranks,

@@ -629,8 +629,9 @@ def run_ours(args):
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": "dense_fused_i8 M=N=K=4096 scale=1.0 relu=off, fp32 N(0,1) A and B in HBM"
                                + ("" if world == 1 else f"; A/C row-sharded, {M} rows per rank, B replicated, "
-                                  "NCCL all-reduce(max) of the absmax bits, all-gather of C fused into the GEMM "
-                                  "epilogue (NVLink peer stores)"),
+                                  "absmax exchanged between GPUs inside the cooperative prologue (tagged NVLink "
+                                  "peer words), all-gather of C fused into the GEMM epilogue (NVLink peer stores); "
+                                  "no NCCL call in the step"),
                    "M_per_rank": M, "N": N, "K": K,
                    "l2": ("inputs larger than L2: two (A, B) fp32 pairs of 128 MiB alternate between steps, no flush; "
                           "within a step each fp32 tensor's second read (quantize after absmax) is served from "
@@ -642,7 +643,7 @@ def run_ours(args):
                      "traffic": GEMM_TRAFFIC_BYTES, "traffic_unit": "bytes per launch (DRAM read + write)",
                      "traffic_source": "ncu capture, profiles/gemm_s8_pair_dense_fused_4096.md",
                      "algorithmic_bytes": M * K + N * K + 4 * M * N, "gemm_ms": gemm_ms},
-        "stages_ms": {"quantize_pair": q_ms, "gemm": gemm_ms, "step": ms, "step_without_all_gather": no_gather_ms,
+        "stages_ms": {"quantize_pair": q_ms, "gemm": gemm_ms, "step": ms, "step_nccl_path_without_all_gather": no_gather_ms,
                       "step_with_nccl_all_gather": nccl_gather_ms},
         "e2e": e2e, "gpu_launches": int(launches), "gpu_launches_per_step": launches_per_step,
         "clocks": clocks, "q8_0_gemv": q8, "decode_stack": dec, "configs": legs, "cpu_baseline": cpu,

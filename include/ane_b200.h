@@ -177,6 +177,21 @@ int ane_q8_stack_plan_create(const ane_q8_stack_proj* projs, uint32_t nproj, uin
                              uint32_t* ctl, void** plan);
 int ane_q8_stack_run(void* plan, void* stream);
 void ane_q8_stack_plan_free(void* plan);
+/* Quantize stage of the N-sharded dense_fused_i8 in one cooperative launch
+ * (A and B read from HBM once, as in ane_dense_fused_i8_dev) with the tensor-
+ * wide absmax of A and B taken over all `world` ranks: each rank stores its
+ * two absmax words to every rank's exchange area (slot_peer[q] = this rank's
+ * two 64-bit words on rank q, CUDA-IPC peer pointers; slots = this GPU's area
+ * of 2*world words) and waits (bounded) for every rank's words of this call.
+ * ctl = this GPU's 2 control words.  Exchange area and ctl start zeroed and
+ * are never reset; every rank makes the same calls.  The exchange also acts as
+ * the call's entry handshake (a rank leaves it only after all ranks entered).
+ * Needs K % 16 == 0, N % 4 == 0, 16-byte aligned A, B, Aq, Bt, and
+ * M*K, K*N >= 2^22 (else ANE_ERR_INVALID_ARGUMENT).  Aq is M x K, Bt N x K.
+ * No counterpart in the reference. */
+int ane_quantize_pair_xrank_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
+                                int8_t* Bt, float* scales, float* partials, uint32_t world, uint32_t rank,
+                                void* const* slot_peer, const void* slots, uint32_t* ctl, void* stream);
 /* int8 GEMM (as ane_gemm_s8_dev, out_mode 0) fused with an all-gather of C over
  * `world` GPUs: every C tile is stored into each rank's gathered output from the
  * epilogue (C_ranks[q] = rank q's buffer at this rank's first element, row
