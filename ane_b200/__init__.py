@@ -69,6 +69,8 @@ SIGNATURES = {
     "ane_q8_0_gemv_ex_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _u32, _vp]),
     "ane_q8_0_gemv_q8_ex_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _u32, _vp]),
     "ane_mul_mat_q8_0_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _u32, _vp]),
+    "ane_mul_mat_q8_0_batch_workspace_size": (_sz, [_u32, _u32]),
+    "ane_mul_mat_q8_0_batch_dev": (_i32, [_u32, _u32, _u32, _vp, _sz, _vp, _vp, _sz, _vp, _u32, _vp]),
     "ane_q8_stack_plan_create": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp]),
     "ane_q8_stack_run": (_i32, [_vp, _vp]),
     "ane_q8_stack_plan_free": (None, [_vp]),
@@ -313,6 +315,30 @@ def mul_mat_q8_0(W, x, M: int, K: int, out=None, block_dots=None, stream=None, s
     check(_lib.ane_mul_mat_q8_0_dev(M, K, x.data_ptr(), W.data_ptr(), out.data_ptr(),
                                     block_dots.data_ptr() if block_dots is not None else None,
                                     WEIGHTS_STATIC if static_weights else 0, _stream_ptr(stream)))
+    return out
+
+
+def mul_mat_q8_0_batch_workspace(M: int, K: int, device):
+    """Zeroed workspace for mul_mat_q8_0_batch (reusable by calls on one stream)."""
+    torch = _torch()
+    n = int(_lib.ane_mul_mat_q8_0_batch_workspace_size(M, K))
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def mul_mat_q8_0_batch(W, x, M: int, K: int, out=None, workspace=None, stream=None, static_weights=False):
+    """ggml MUL_MAT for NT <= 16 fp32 activation rows x [NT, K] (row stride
+    x.stride(0)) against Q8_0 weights W: out [NT, M] (row stride out.stride(0))."""
+    torch = _torch()
+    NT = x.shape[0]
+    assert x.dim() == 2 and x.shape[1] == K and x.stride(1) == 1
+    if out is None:
+        out = torch.empty((NT, M), dtype=torch.float32, device=W.device)
+    assert out.dim() == 2 and out.shape == (NT, M) and out.stride(1) == 1
+    if workspace is None:
+        workspace = mul_mat_q8_0_batch_workspace(M, K, W.device)
+    check(_lib.ane_mul_mat_q8_0_batch_dev(M, K, NT, x.data_ptr(), x.stride(0), W.data_ptr(), out.data_ptr(),
+                                          out.stride(0), workspace.data_ptr(), WEIGHTS_STATIC if static_weights else 0,
+                                          _stream_ptr(stream)))
     return out
 
 

@@ -429,6 +429,19 @@ int ane_mul_mat_q8_0_dev(uint32_t M, uint32_t K, const float* x, const void* W, 
     return rc ? rc : ok();
 }
 
+size_t ane_mul_mat_q8_0_batch_workspace_size(uint32_t M, uint32_t K) {
+    return mul_mat_q8_0_batch_workspace_size(M, K);
+}
+
+int ane_mul_mat_q8_0_batch_dev(uint32_t M, uint32_t K, uint32_t NT, const float* x, size_t ldx, const void* W,
+                               float* y, size_t ldy, void* workspace, uint32_t flags, void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK((flags & ~ANE_Q8_WEIGHTS_STATIC) == 0, "mul_mat_q8_0_batch: unknown flag bits");
+    int rc = launch_mul_mat_q8_0_batch(M, K, NT, x, ldx, static_cast<const uint8_t*>(W), y, ldy, workspace, flags,
+                                       static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
 int ane_quantize_pair_xrank_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
                                 int8_t* Bt, float* scales, float* partials, uint32_t world, uint32_t rank,
                                 void* const* slot_peer, const void* slots, uint32_t* ctl, void* stream) {

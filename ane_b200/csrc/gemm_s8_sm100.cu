@@ -65,6 +65,7 @@ constexpr size_t P_SMEM = (size_t)P_STAGES * P_STAGE + EPI_BYTES + sizeof(Barrie
 static_assert(S_SMEM <= 232448 && P_SMEM <= 232448, "shared memory budget");
 
 constexpr uint32_t kGatherMaxRanks = 8;
+constexpr uint32_t P_BN_COLS = 256;  // pair tile width (= P_BN)
 
 struct Params {
     uint32_t M, N, K;
@@ -80,7 +81,26 @@ struct Params {
     uint32_t world;
     void* C_rank[kGatherMaxRanks];
     uint32_t* ctr_rank[kGatherMaxRanks];
+    // pair kernel, last partial wave: tiles tail_start.. are cut along N into
+    // `split` parts (1, 2 or 4) of 256/split columns, each over the full K, so
+    // the leftover tiles spread over all CTA pairs instead of a few
+    uint32_t tail_start, split, num_units;
 };
+
+// One work unit of the pair kernel: a 256-row tile, columns n0 .. n0+ncols-1.
+struct PairUnit {
+    uint32_t m0, n0, ncols;
+};
+__device__ __forceinline__ PairUnit pair_unit(const Params& p, uint32_t u) {
+    uint32_t t = u, j = 0, ncols = P_BN_COLS;
+    if (u >= p.tail_start) {
+        const uint32_t v = u - p.tail_start;
+        t = p.tail_start + v / p.split;
+        j = v % p.split;
+        ncols = P_BN_COLS / p.split;
+    }
+    return {(t / p.tiles_n) * 256u, (t % p.tiles_n) * P_BN_COLS + j * ncols, ncols};
+}
 
 // max that propagates NaN (ARM FMAX, not IEEE maxNum); one instruction.
 __device__ __forceinline__ float max_nan(float a, float b) {
@@ -171,18 +191,19 @@ __device__ __forceinline__ void store_block(const Params& p, float comb, const u
     __syncwarp();
 }
 
-// Drains one 128-row x 256-column TMEM accumulator of this CTA (warp = one lane
+// Drains one 128-row x `ncols`-column TMEM accumulator of this CTA (warp = one lane
 // quarter) and stores it.  Calls `release()` right after the last TMEM read.
 template <class Release>
 __device__ __forceinline__ void drain_accumulator(const Params& p, uint32_t taddr, uint32_t row0, uint32_t n0,
-                                                  uint32_t* stage, int lane, Release release) {
+                                                  uint32_t ncols, uint32_t* stage, int lane, Release release) {
     const float comb = tile_comb(p);
+    const int chunks = (int)(ncols / 32);
 #pragma unroll 1
-    for (int c = 0; c < ACC_COLS / 32; c++) {
+    for (int c = 0; c < chunks; c++) {
         uint32_t r[32];
         ptx::tmem_ld_32x32b_x32(taddr + c * 32, r);
         ptx::tmem_ld_wait();
-        if (c == ACC_COLS / 32 - 1) {
+        if (c == chunks - 1) {
             ptx::tc_fence_before();
             __syncwarp();
             release();
@@ -283,7 +304,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ptx::tc_fence_after();
             const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + acc * ACC_COLS;
             uint64_t* empty_bar = &bars->tmem_empty[acc];
-            drain_accumulator(p, taddr, m0 + quarter * 32, n0, stage, lane, [&] {
+            drain_accumulator(p, taddr, m0 + quarter * 32, n0, ACC_COLS, stage, lane, [&] {
                 if (lane == 0) ptx::mbar_arrive(empty_bar);
             });
             acc ^= 1;
@@ -303,7 +324,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // --------------------------------------------------------- CTA-pair kernel
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_s8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                        const Params p) {
+                        const __grid_constant__ CUtensorMap tmap_b32, const Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sa = smem;
@@ -314,7 +335,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = ptx::cluster_ctarank();  // 0 = leader (issues the MMAs)
     const uint32_t pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
-    const uint32_t num_tiles = p.tiles_m * p.tiles_n;
+    const uint32_t num_units = p.num_units;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < P_STAGES; s++) {
@@ -328,6 +349,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ptx::fence_mbarrier_init();
         ptx::prefetch_tmap(&tmap_a);
         ptx::prefetch_tmap(&tmap_b);
+        if (p.split > 1) ptx::prefetch_tmap(&tmap_b32);
     }
     if (warp == 1) {
         ptx::tmem_alloc_cg2(&bars->tmem_base, TMEM_COLS);
@@ -346,25 +368,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) {
             uint32_t stage = 0, phase = 0;
             bool alive = true;
-            for (uint32_t t = pair; t < num_tiles && alive; t += num_pairs) {
-                const int m0 = (int)((t / p.tiles_n) * P_BM + rank * P_HM);
-                const int n0 = (int)((t % p.tiles_n) * P_BN + rank * P_HN);
+            for (uint32_t u = pair; u < num_units && alive; u += num_pairs) {
+                const PairUnit un = pair_unit(p, u);
+                if (un.n0 >= p.N) continue;  // a split part entirely right of N (all roles skip it)
+                const uint32_t half = un.ncols / 2;  // B rows this CTA supplies
+                const int m0 = (int)(un.m0 + rank * P_HM);
+                const int n0 = (int)(un.n0 + rank * half);
+                const uint32_t tx = 2 * (P_A + half * BK);
                 for (uint32_t kb = 0; kb < p.num_kb; kb++) {
                     if (!ptx::mbar_wait(&bars->empty[stage], phase ^ 1, p.err)) { alive = false; break; }
-                    if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->full[stage], 2 * P_STAGE);
+                    if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->full[stage], tx);
                     const uint32_t full_leader = ptx::mapa_shared(ptx::smem_u32(&bars->full[stage]), 0);
                     ptx::tma_load_2d_cg2(sa + (size_t)stage * P_A, &tmap_a, full_leader, (int)(kb * BK), m0);
-                    ptx::tma_load_2d_cg2(sb + (size_t)stage * P_B, &tmap_b, full_leader, (int)(kb * BK), n0);
+                    if (half == P_HN) {
+                        ptx::tma_load_2d_cg2(sb + (size_t)stage * P_B, &tmap_b, full_leader, (int)(kb * BK), n0);
+                    } else {
+                        // 32-row boxes, each 4 KB apart: the same SWIZZLE_128B image as one taller box
+                        for (uint32_t r = 0; r < half; r += 32)
+                            ptx::tma_load_2d_cg2(sb + (size_t)stage * P_B + r * BK, &tmap_b32, full_leader,
+                                                 (int)(kb * BK), n0 + (int)r);
+                    }
                     if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
-            constexpr uint32_t idesc = ptx::idesc_s8s8s32(P_BM, P_BN);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool alive = true;
-            for (uint32_t t = pair; t < num_tiles && alive; t += num_pairs) {
+            for (uint32_t u = pair; u < num_units && alive; u += num_pairs) {
+                const PairUnit un = pair_unit(p, u);
+                if (un.n0 >= p.N) continue;
+                const uint32_t idesc = ptx::idesc_s8s8s32(P_BM, (int)un.ncols);
                 if (!ptx::mbar_wait(&bars->tmem_empty[acc], acc_phase ^ 1, p.err)) break;
                 ptx::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
@@ -390,13 +425,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t quarter = (uint32_t)(warp & 3);
         uint32_t* stage = epi + (warp - 2) * EPI_STAGE_WORDS;
         uint32_t acc = 0, acc_phase = 0;
-        for (uint32_t t = pair; t < num_tiles; t += num_pairs) {
-            const uint32_t m0 = (t / p.tiles_n) * P_BM + rank * P_HM, n0 = (t % p.tiles_n) * P_BN;
+        for (uint32_t u = pair; u < num_units; u += num_pairs) {
+            const PairUnit un = pair_unit(p, u);
+            if (un.n0 >= p.N) continue;
+            const uint32_t m0 = un.m0 + rank * P_HM;
             if (!ptx::mbar_wait(&bars->tmem_full[acc], acc_phase, p.err)) break;
             ptx::tc_fence_after();
             const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + acc * ACC_COLS;
             const uint32_t empty_leader = ptx::mapa_shared(ptx::smem_u32(&bars->tmem_empty[acc]), 0);
-            drain_accumulator(p, taddr, m0 + quarter * 32, n0, stage, lane, [&] {
+            drain_accumulator(p, taddr, m0 + quarter * 32, un.n0, un.ncols, stage, lane, [&] {
                 if (lane == 0) ptx::mbar_arrive_cluster(empty_leader);
             });
             acc ^= 1;
@@ -473,6 +510,7 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
     p.ep = ep;
     p.err = device_timeout_flag();
     p.world = 1;
+    p.tail_start = p.split = p.num_units = 0;
     if (gather && gather->world > 1) {
         ANE_ARG_CHECK(gather->world <= kGatherMaxRanks, "gemm gather: at most 8 ranks");
         p.world = gather->world;
@@ -516,8 +554,34 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
     p.tiles_n = (N + P_BN - 1) / P_BN;
     const uint32_t tiles = p.tiles_m * p.tiles_n;
     uint32_t pairs = (uint32_t)sms / 2;
-    if (pairs > tiles) pairs = tiles;
+    // Last partial wave: r leftover tiles would keep r pairs busy for a whole
+    // tile while the rest idle.  Cutting each into s = 2 or 4 column parts
+    // (s*r <= pairs) ends that wave after 1/s of a tile.  Every part runs the
+    // full K, so no partial sums are combined.  ANE_GEMM_TAIL_SPLIT=0 turns it off.
+    p.tail_start = tiles;
+    p.split = 1;
+    static const bool tail_split = [] {
+        const char* v = getenv("ANE_GEMM_TAIL_SPLIT");
+        return !(v && v[0] == '0');
+    }();
+    const uint32_t r = tiles % pairs;
+    if (tail_split && r != 0) {
+        const uint32_t sp = pairs / r >= 4 ? 4u : pairs / r >= 2 ? 2u : 1u;
+        if (sp > 1) {
+            p.tail_start = tiles - r;
+            p.split = sp;
+        }
+    }
+    p.num_units = p.tail_start + p.split * (tiles - p.tail_start);
+    if (pairs > p.num_units) pairs = p.num_units;
     if (grid_out) *grid_out = 2 * pairs;
+    CUtensorMap tb32;
+    if (p.split > 1) {
+        rc = make_kmajor_map(&tb32, Bt, N, K, 32);
+        if (rc) return rc;
+    } else {
+        tb32 = tb;  // unused
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
     cfg.blockDim = dim3(NUM_THREADS, 1, 1);
@@ -532,7 +596,7 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_s8_pair_kernel, ta, tb, p));
+    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_s8_pair_kernel, ta, tb, tb32, p));
     ANE_CHECK_LAUNCH();
     return ANE_OK;
 }

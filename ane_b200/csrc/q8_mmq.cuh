@@ -14,8 +14,9 @@
 
 namespace ane_b200 {
 
-// Quantizes one 32-element block held in registers into xs[32b..32b+31], xd[b].
-__device__ __forceinline__ void q8_quantize_regs(const float (&v)[32], int8_t* xs, float* xd, uint32_t b) {
+// One 32-element block in registers -> its 32 codes as 8 little-endian words;
+// returns the block scale as stored (fp16(d), widened).
+__device__ __forceinline__ float q8_quantize_words(const float (&v)[32], uint32_t (&w)[8]) {
     float amax = 0.0f;
 #pragma unroll
     for (int j = 0; j < 32; j++) {
@@ -24,15 +25,23 @@ __device__ __forceinline__ void q8_quantize_regs(const float (&v)[32], int8_t* x
     }
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    xd[b] = __half2float(__float2half_rn(d));
-    uint32_t* dst = reinterpret_cast<uint32_t*>(xs + (size_t)b * 32);
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
-        uint32_t w = 0;
+        uint32_t x = 0;
 #pragma unroll
-        for (int i = 0; i < 4; i++) w |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[j + i], id)) << (8 * i);
-        dst[j / 4] = w;
+        for (int i = 0; i < 4; i++) x |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[j + i], id)) << (8 * i);
+        w[j / 4] = x;
     }
+    return __half2float(__float2half_rn(d));
+}
+
+// Quantizes one 32-element block held in registers into xs[32b..32b+31], xd[b].
+__device__ __forceinline__ void q8_quantize_regs(const float (&v)[32], int8_t* xs, float* xd, uint32_t b) {
+    uint32_t w[8];
+    xd[b] = q8_quantize_words(v, w);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(xs + (size_t)b * 32);
+#pragma unroll
+    for (int j = 0; j < 8; j++) dst[j] = w[j];
 }
 
 // Quantizes block b of x (32 floats at xb) into xs[32b..32b+31] and xd[b].

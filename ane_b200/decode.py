@@ -71,16 +71,16 @@ class DecodeStack:
 
     def __init__(self, layers: int, world: int, rank: int, make_rows: Callable, quantize: Callable,
                  matvec: Callable, gather: Callable, shapes: Sequence = LAYER_SHAPES, alloc=None,
-                 make_inputs: Callable | None = None):
-        self.layers, self.world, self.rank = layers, world, rank
+                 make_inputs: Callable | None = None, batch: int = 1, weights: list | None = None):
+        self.layers, self.world, self.rank, self.batch = layers, world, rank, batch
         self.shapes = tuple(shapes)
         for (_, M_prev, _), (name, _, K) in zip(self.shapes, self.shapes[1:]):
             if K > M_prev:
                 raise ValueError(f"projection {name} reads {K} entries of a {M_prev}-entry vector")
         self.quantize, self.matvec, self.gather = quantize, matvec, gather
         alloc = alloc or (lambda n, dtype: torch.empty(n, dtype=dtype))
-        self.weights = []
-        for layer in range(layers):
+        self.weights = weights if weights is not None else []  # reuse another stack's shards
+        for layer in range(layers if weights is None else 0):
             ws = []
             for p, (_, M, K) in enumerate(self.shapes):
                 r0, r1 = shard_rows(M, world, rank)
@@ -91,19 +91,28 @@ class DecodeStack:
                 ws.append(W)
             self.weights.append(ws)
         width = max(max(M, K) for _, M, K in self.shapes)
-        self.h = [alloc(width, torch.float32), alloc(width, torch.float32)]
         k0 = self.shapes[0][2]
-        self.inputs = make_inputs(layers, k0) if make_inputs else torch.randn(layers, k0)  # per-layer x
-        self.y_local = {M: alloc(M // world, torch.float32) for _, M, _ in self.shapes} if world > 1 else {}
+        if batch == 1:
+            self.h = [alloc(width, torch.float32), alloc(width, torch.float32)]
+            self.inputs = make_inputs(layers, k0) if make_inputs else torch.randn(layers, k0)  # per-layer x
+            self.y_local = {M: alloc(M // world, torch.float32) for _, M, _ in self.shapes} if world > 1 else {}
+        else:
+            # token t is row t of every activation: h[i] is [batch, width], inputs [layers, batch, K]
+            self.h = [alloc(batch * width, torch.float32).view(batch, width) for _ in range(2)]
+            self.inputs = (make_inputs(layers * batch, k0) if make_inputs
+                           else torch.randn(layers * batch, k0)).view(layers, batch, k0)
+            self.y_local = ({M: alloc(batch * (M // world), torch.float32).view(batch, M // world)
+                             for _, M, _ in self.shapes} if world > 1 else {})
 
     def forward(self, trace: list | None = None) -> torch.Tensor:
-        """One token through every layer; returns the last projection's full output."""
+        """One step (one token, or `batch` tokens as rows) through every layer;
+        returns the last projection's full output."""
         cur = 0
         for layer in range(self.layers):
             for p, (_, M, K) in enumerate(self.shapes):
-                xin = self.inputs[layer] if p == 0 else self.h[cur][:K]
+                xin = self.inputs[layer] if p == 0 else self.h[cur][..., :K]
                 xq = self.quantize(xin)
-                out = self.h[1 - cur][:M]
+                out = self.h[1 - cur][..., :M]
                 if self.world == 1:
                     self.matvec(self.weights[layer][p], xq, M, K, out)
                 else:
@@ -112,15 +121,19 @@ class DecodeStack:
                 if trace is not None:
                     trace.append((layer, p, xin.clone(), out.clone()))
                 cur = 1 - cur
-        return self.h[cur][:self.shapes[-1][1]]
+        return self.h[cur][..., :self.shapes[-1][1]]
 
 
 # ------------------------------------------------------------------ GPU binding
 def gpu_stack(layers: int, device, world: int = 1, rank: int = 0, group=None, seed: int = 5,
-              shapes: Sequence = LAYER_SHAPES, static_weights: bool = True) -> DecodeStack:
-    """DecodeStack on libane_b200 (one launch per projection: Q8_0 activation
-    quantization fused into the Q8_0 x Q8_0 matvec) with an NCCL all-gather."""
+              shapes: Sequence = LAYER_SHAPES, static_weights: bool = True, batch: int = 1,
+              weights: list | None = None) -> DecodeStack:
+    """DecodeStack on libane_b200 with an NCCL all-gather.  batch 1: one launch
+    per projection (Q8_0 activation quantization fused into the Q8_0 x Q8_0
+    matvec); batch > 1: the batched MUL_MAT (weights read once for all tokens)."""
     import ane_b200 as ane
+
+    workspaces, gather_bufs = {}, {}
 
     def make_rows(layer, p, blk, K):
         g = torch.Generator(device=device).manual_seed(block_seed(seed, layer, p, blk))
@@ -132,17 +145,32 @@ def gpu_stack(layers: int, device, world: int = 1, rank: int = 0, group=None, se
         return x
 
     def matvec(W, x, rows, K, out):
-        return ane.mul_mat_q8_0(W, x, rows, K, out=out, static_weights=static_weights)
+        if batch == 1:
+            return ane.mul_mat_q8_0(W, x, rows, K, out=out, static_weights=static_weights)
+        if (rows, K) not in workspaces:
+            workspaces[(rows, K)] = ane.mul_mat_q8_0_batch_workspace(rows, K, device)
+        return ane.mul_mat_q8_0_batch(W, x, rows, K, out=out, workspace=workspaces[(rows, K)],
+                                      static_weights=static_weights)
 
     def gather(y_loc, y_full):
-        dist.all_gather_into_tensor(y_full, y_loc, group=group)
+        if batch == 1:
+            dist.all_gather_into_tensor(y_full, y_loc, group=group)
+            return
+        # [batch, m] slices -> [world, batch, m] -> token rows of [batch, world * m]
+        m = y_loc.shape[1]
+        if m not in gather_bufs:
+            gather_bufs[m] = torch.empty(world * batch * m, dtype=torch.float32, device=device)
+        buf = gather_bufs[m]
+        dist.all_gather_into_tensor(buf, y_loc, group=group)
+        y_full.copy_(buf.view(world, batch, m).permute(1, 0, 2).reshape(batch, world * m))
 
     def make_inputs(n, K):
         g = torch.Generator(device=device).manual_seed(seed + 17)
         return torch.randn(n, K, device=device, generator=g)
 
     alloc = lambda n, dtype: torch.empty(n, dtype=dtype, device=device)  # noqa: E731
-    return DecodeStack(layers, world, rank, make_rows, quantize, matvec, gather, shapes, alloc, make_inputs)
+    return DecodeStack(layers, world, rank, make_rows, quantize, matvec, gather, shapes, alloc, make_inputs, batch,
+                       weights)
 
 
 # ------------------------------------------------- one persistent launch per token

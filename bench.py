@@ -325,6 +325,21 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
             torch.distributed.barrier(group)
     finally:
         fused.close()
+    # batch 16: the same weights, 16 tokens per step through the batched MUL_MAT
+    batch = 16
+    stack16 = decode.gpu_stack(layers, dev, world=world, rank=rank, group=group, batch=batch,
+                               weights=stack.weights)
+    stack16.forward()
+    torch.cuda.synchronize()
+    g16 = None
+    if world == 1:
+        g16 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g16):
+            stack16.forward()
+        b16_ms = timed(g16.replay)
+    else:
+        b16_ms = timed(stack16.forward)
+    del g16, stack16
     wbytes = decode.stack_weight_bytes(layers)
     peaks = load_peaks()
     fused_path = "one persistent launch per token" + (", all-gather by NVLink peer stores" if world > 1 else "")
@@ -336,6 +351,11 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
             "gbs": gbs, "per_gpu_hbm_frac": gbs / world / peaks["hbm_gbs"], "path": best_path,
             "fused_ms_per_token": fused_ms, "fused_gbs": wbytes / (fused_ms * 1e-3) / 1e9, "fused_path": fused_path,
             "chain_ms_per_token": chain_ms, "chain_gbs": wbytes / (chain_ms * 1e-3) / 1e9, "chain_path": chain_path,
+            "batch16": {"ms_per_step": b16_ms, "tokens_per_s": batch / (b16_ms * 1e-3),
+                        "weight_gbs": wbytes / (b16_ms * 1e-3) / 1e9,
+                        "per_gpu_hbm_frac": wbytes / (b16_ms * 1e-3) / 1e9 / world / peaks["hbm_gbs"],
+                        "path": (f"{4 * layers} x (activation quantize + batched MUL_MAT) launches"
+                                 + (" in a CUDA graph" if world == 1 else " + NCCL all-gather each"))},
             "activation": "Q8_0 (ggml convention), static weights",
             "timing": f"{reps} tokens each path, CUDA events" + ("" if world == 1 else ", max over ranks"),
             "build_s": build_s}
@@ -435,6 +455,43 @@ def config_legs(ane, torch, dev, steps=20):
     out["config4_projection"] = cfg4
     del B, flush
     return out
+
+
+def config4_sharded(ane, torch, dev, world, group, steps=20):
+    """Config 4 on N GPUs: the 14336 output columns N-sharded (each rank holds A
+    and a K x 14336/N block of B), the global absmax exchanged and C all-gathered
+    by the fused path (the all-gather of C inside the GEMM epilogue).  Device
+    time per step, L2 flushed before every step, max over ranks."""
+    from ane_b200 import sharded
+
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    rank = torch.distributed.get_rank(group)
+    n_local = 14336 // world
+    g = torch.Generator(device=dev).manual_seed(4)
+    B = torch.randn((4096, 14336), device=dev, generator=g)
+    B_local = B[:, rank * n_local:(rank + 1) * n_local].contiguous()
+    del B
+    out = {}
+    for m in (1, 8, 64, 512):
+        A = torch.randn((m, 4096), device=dev, generator=g)
+        A = torch.where(torch.rand(A.shape, device=dev, generator=g) < 0.01, A * 20, A)
+        ctx = sharded.ShardedDense(m, n_local, 4096, world, dev, group, shard="cols", fused_gather=True)
+        f = lambda: ctx.forward(A, B_local, 0.125, True)  # noqa: E731
+        for _ in range(3):
+            f()
+        torch.cuda.synchronize()
+        torch.distributed.barrier(group)
+        ms = timed_steps_flushed(torch, f, steps, stream, flush)
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=group)
+        ms = float(t.item())
+        torch.cuda.synchronize()
+        torch.distributed.barrier(group)
+        ctx.close()
+        out[str(m)] = {"tops": 2.0 * m * 14336 * 4096 / (ms * 1e-3) / 1e12, "ms": ms}
+    del flush, B_local
+    return {"config4_projection_sharded": {"n_gpus": world, "shard": f"cols, 14336/{world} per rank", **out}}
 
 
 def run_ours(args):
@@ -606,6 +663,8 @@ def run_ours(args):
     legs = None
     if not args.no_configs and world == 1:
         legs = config_legs(ane, torch, dev)
+    elif not args.no_configs:
+        legs = config4_sharded(ane, torch, dev, world, pg)
 
     dec = None
     if not args.no_decode:

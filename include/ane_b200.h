@@ -150,6 +150,22 @@ int ane_q8_0_gemv_ex_dev(uint32_t M, uint32_t K, const float* in, const void* W,
 int ane_q8_0_gemv_q8_ex_dev(uint32_t M, uint32_t K, const void* xq_blocks, const void* W, float* out,
                             int32_t* block_dots, uint32_t flags, void* stream);
 
+/* ggml MUL_MAT with Q8_0 weights W[M rows x K] and NT (1..16) fp32 activation
+ * rows x[t * ldx + k] (a decode step over NT tokens): y[t * ldy + m].  The
+ * reference runs MUL_MAT Q8_0 as one q8_0_gemv (src/ggml-backend/ggml-ane.cpp:
+ * 137-143); here the weights cross HBM once for all NT rows.  Each activation
+ * row is quantized to Q8_0 with the ggml rule; per (t, m) the batch-1 terms
+ * float(sumi) * (dw * dx) are summed in block order within segments of 32
+ * blocks, then the segment sums in order (each sum from +0) -- an order fixed by
+ * K alone.  K % 256 == 0; W and x 16-byte aligned, ldx % 4 == 0; `workspace`
+ * holds ane_mul_mat_q8_0_batch_workspace_size(M, K) bytes, 256-byte aligned,
+ * zero before its first use (every call leaves it so); calls sharing a
+ * workspace must be ordered on one stream.  flags: ANE_Q8_WEIGHTS_STATIC.
+ * No counterpart in the reference. */
+size_t ane_mul_mat_q8_0_batch_workspace_size(uint32_t M, uint32_t K);
+int ane_mul_mat_q8_0_batch_dev(uint32_t M, uint32_t K, uint32_t NT, const float* x, size_t ldx, const void* W,
+                               float* y, size_t ldy, void* workspace, uint32_t flags, void* stream);
+
 /* ------------------------------------------------ decode stack (config 5)
  * A chain of Q8_0 MUL_MATs (batch 1, Q8_0 activation, as ane_mul_mat_q8_0_dev)
  * in ONE persistent cooperative launch, row-sharded over `world` GPUs.

@@ -62,6 +62,7 @@ def lib():
             "ane_ref_quantize_q8_0": (None, [_f32p, _u8p, _sz, _sz]),
             "ane_ref_q8_0_gemv_q8": (None, [_u32, _u32, _u8p, _u8p, _f32p, _vp]),
             "ane_ref_get_rows_q8_0": (None, [_u32, _u32, _u8p, _u32p, _f32p]),
+            "ane_ref_mul_mat_q8_0_batch": (None, [_u32, _u32, _u32, _u8p, _u8p, _f32p, _sz]),
             "ane_ref_dense_fused_i8_omp": (None, [_u32, _u32, _u32, _f, ctypes.c_int, _f32p, _f32p, _f32p,
                                                   ctypes.c_int]),
             "ane_ref_q8_0_gemv_omp": (None, [_u32, _u32, _f32p, _u8p, _f32p, ctypes.c_int]),
@@ -225,6 +226,14 @@ def q8_0_gemv_q8(W_blocks, xq_blocks, M: int, K: int, with_dots=False):
     lib().ane_ref_q8_0_gemv_q8(M, K, _c(xq_blocks, np.uint8).ravel(), _c(W_blocks, np.uint8).ravel(), out,
                                _ptr(dots) if with_dots else None)
     return (out, dots.reshape(M, K // 32)) if with_dots else out
+
+
+def mul_mat_q8_0_batch(W_blocks, xq_blocks, M: int, K: int, NT: int):
+    """[NT, M] fp32: Q8_0 weights against NT Q8_0 activation rows, segment order."""
+    out = np.empty((NT, M), np.float32)
+    lib().ane_ref_mul_mat_q8_0_batch(M, K, NT, _c(xq_blocks, np.uint8).ravel(), _c(W_blocks, np.uint8).ravel(),
+                                     out, M)
+    return out
 
 
 def get_rows_q8_0(table, indices, dim: int):

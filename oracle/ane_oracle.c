@@ -327,6 +327,35 @@ void ane_ref_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8
     }
 }
 
+/* Q8_0 x Q8_0 product for NT activation rows (ggml MUL_MAT with ne1 = NT):
+ * the batch-1 formula above per (weight row, activation row), with the fp32
+ * terms grouped into segments of ANE_Q8_SEG_BLOCKS blocks: each segment is
+ * summed from +0 in block order, then the segment sums are added from +0 in
+ * segment order.  out[t * ldo + m]; xq holds NT rows of K/32 blocks. */
+void ane_ref_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const uint8_t* xq, const uint8_t* W,
+                                float* out, size_t ldo) {
+    uint32_t nb = K / 32;
+    for (uint32_t t = 0; t < NT; t++)
+        for (uint32_t m = 0; m < M; m++) {
+            float total = 0.0f;
+            for (uint32_t s0 = 0; s0 < nb; s0 += ANE_Q8_SEG_BLOCKS) {
+                float part = 0.0f;
+                uint32_t s1 = s0 + ANE_Q8_SEG_BLOCKS < nb ? s0 + ANE_Q8_SEG_BLOCKS : nb;
+                for (uint32_t b = s0; b < s1; b++) {
+                    const uint8_t* wb = W + ((size_t)m * nb + b) * 34;
+                    const uint8_t* xb = xq + ((size_t)t * nb + b) * 34;
+                    int32_t sumi = 0;
+                    for (int j = 0; j < 32; j++) sumi += (int32_t)(int8_t)wb[2 + j] * (int32_t)(int8_t)xb[2 + j];
+                    float dw = ane_ref_fp16_to_fp32((uint16_t)(wb[0] | (wb[1] << 8)));
+                    float dx = ane_ref_fp16_to_fp32((uint16_t)(xb[0] | (xb[1] << 8)));
+                    part += (float)sumi * (dw * dx);
+                }
+                total += part;
+            }
+            out[(size_t)t * ldo + m] = total;
+        }
+}
+
 void ane_ref_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const uint8_t* table,
                            const uint32_t* indices, float* out) {
     /* bytecode_interpreter.s:12365-12405. */

@@ -105,6 +105,16 @@ void ane_ref_quantize_q8_0(const float* x, uint8_t* blocks, size_t n_rows, size_
 void ane_ref_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8_t* W,
                           float* out, int32_t* block_dots);
 
+/* ---- Q8_0 MUL_MAT for NT activation rows (config 5 at batch 16) --------------------
+ * No reference handler: the reference's ggml backend runs MUL_MAT Q8_0 as one
+ * q8_0_gemv (src/ggml-backend/ggml-ane.cpp:137-143).  Per (activation row t,
+ * weight row m) the batch-1 mode-Q terms, summed per segment of
+ * ANE_Q8_SEG_BLOCKS blocks in block order, then over segments in order; every
+ * sum starts from +0.  out[t * ldo + m]. */
+#define ANE_Q8_SEG_BLOCKS 32
+void ane_ref_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const uint8_t* xq, const uint8_t* W,
+                                float* out, size_t ldo);
+
 /* ---- get_rows_q8_0 (0x7C) -------------------------------------------------------- */
 void ane_ref_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const uint8_t* table,
                            const uint32_t* indices, float* out);

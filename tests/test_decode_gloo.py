@@ -24,7 +24,7 @@ def _free_port():
     return p
 
 
-def _oracle_stack(layers, world, rank, gather):
+def _oracle_stack(layers, world, rank, gather, batch=1):
     import oracle
     from ane_b200.decode import ROW_BLOCK, DecodeStack, block_seed
 
@@ -34,19 +34,24 @@ def _oracle_stack(layers, world, rank, gather):
         return torch.from_numpy(oracle.quantize_q8_0(w, ROW_BLOCK, K))
 
     def quantize(x):
+        if batch > 1:  # [batch, K] rows -> batch rows of Q8_0 blocks
+            return torch.from_numpy(oracle.quantize_q8_0(x.contiguous().numpy(), x.shape[0], x.shape[1]))
         return torch.from_numpy(oracle.quantize_q8_0(x.numpy(), 1, x.numel()))
 
     def matvec(W, xq, rows, K, out):
-        out.copy_(torch.from_numpy(oracle.q8_0_gemv_q8(W.numpy(), xq.numpy(), rows, K)))
+        if batch > 1:
+            out.copy_(torch.from_numpy(oracle.mul_mat_q8_0_batch(W.numpy(), xq.numpy(), rows, K, batch)))
+        else:
+            out.copy_(torch.from_numpy(oracle.q8_0_gemv_q8(W.numpy(), xq.numpy(), rows, K)))
         return out
 
     def make_inputs(n, K):
         return torch.from_numpy(np.random.default_rng(11).standard_normal((n, K)).astype(np.float32))
 
-    return DecodeStack(layers, world, rank, make_rows, quantize, matvec, gather, SHAPES, None, make_inputs)
+    return DecodeStack(layers, world, rank, make_rows, quantize, matvec, gather, SHAPES, None, make_inputs, batch)
 
 
-def _worker(rank, world, port, layers, result_q):
+def _worker(rank, world, port, layers, result_q, batch=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
@@ -56,24 +61,32 @@ def _worker(rank, world, port, layers, result_q):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         def gather(y_loc, y_full):
-            dist.all_gather(list(y_full.view(world, -1).unbind(0)), y_loc)
+            if batch == 1:
+                dist.all_gather(list(y_full.view(world, -1).unbind(0)), y_loc)
+                return
+            parts = [torch.empty_like(y_loc) for _ in range(world)]
+            dist.all_gather(parts, y_loc)
+            m = y_loc.shape[1]
+            for r, part in enumerate(parts):
+                y_full[:, r * m:(r + 1) * m] = part
 
         trace = []
-        out = _oracle_stack(layers, world, rank, gather).forward(trace)
+        out = _oracle_stack(layers, world, rank, gather, batch).forward(trace)
         if rank == 0:
             result_q.put((out.numpy().copy(), [(l, p, x.numpy(), y.numpy()) for l, p, x, y in trace]))
     finally:
         dist.destroy_process_group()
 
 
-def test_decode_stack_sharded_equals_single():
+@pytest.mark.parametrize("batch", [1, 3])
+def test_decode_stack_sharded_equals_single(batch):
     import oracle
 
     layers, world = 2, 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, layers, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, layers, q, batch)) for r in range(world)]
     for p in procs:
         p.start()
     out2, trace2 = q.get(timeout=120)
@@ -82,17 +95,22 @@ def test_decode_stack_sharded_equals_single():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
 
     trace1 = []
-    out1 = _oracle_stack(layers, 1, 0, None).forward(trace1).numpy()
+    out1 = _oracle_stack(layers, 1, 0, None, batch).forward(trace1).numpy()
     assert np.array_equal(out1.view(np.uint32), out2.view(np.uint32))
     assert len(trace1) == len(trace2) == layers * len(SHAPES)
     for (l, p, x, y), (_, _, x2, y2) in zip(trace1, trace2):
         assert np.array_equal(x.numpy().view(np.uint32), x2.view(np.uint32))
         assert np.array_equal(y.numpy().view(np.uint32), y2.view(np.uint32))
-    # each step is the oracle's matvec of that step's quantized input
-    stack = _oracle_stack(layers, 1, 0, None)
+    # each step is the oracle's product of that step's quantized input
+    stack = _oracle_stack(layers, 1, 0, None, batch)
     for (l, p, x, y) in trace1:
         _, M, K = SHAPES[p]
-        ref = oracle.q8_0_gemv_q8(stack.weights[l][p].numpy(), oracle.quantize_q8_0(x.numpy(), 1, K), M, K)
+        W = stack.weights[l][p].numpy()
+        if batch == 1:
+            ref = oracle.q8_0_gemv_q8(W, oracle.quantize_q8_0(x.numpy(), 1, K), M, K)
+        else:
+            xq = oracle.quantize_q8_0(x.contiguous().numpy(), batch, K)
+            ref = oracle.mul_mat_q8_0_batch(W, xq, M, K, batch)
         assert np.array_equal(ref.view(np.uint32), y.numpy().view(np.uint32))
 
 

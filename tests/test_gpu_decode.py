@@ -37,6 +37,28 @@ def test_decode_stack_steps(ane, shapes):
         _check_step(stack.weights[l][p].cpu().numpy(), x.cpu().numpy(), M, K, y.cpu().numpy())
 
 
+@pytest.mark.parametrize("shapes,batch", [("small", 16), ("config5", 16), ("small", 5)])
+def test_decode_stack_batch_steps_exact(ane, shapes, batch):
+    """Config 5 at batch > 1: every projection of the stack equals the
+    oracle's batched Q8_0 product of that step's input rows, bit for bit."""
+    import torch
+
+    from ane_b200.decode import LAYER_SHAPES, gpu_stack
+
+    sh = LAYER_SHAPES if shapes == "config5" else (("qkv", 512, 256), ("o", 256, 256), ("gate_up", 512, 256),
+                                                   ("down", 256, 256))
+    stack = gpu_stack(1 if shapes == "config5" else 2, torch.device("cuda", 0), shapes=sh, seed=9, batch=batch)
+    trace = []
+    out = stack.forward(trace)
+    torch.cuda.synchronize()
+    assert out.shape == (batch, sh[-1][1]) and torch.isfinite(out).all()
+    for (l, p, x, y) in trace:
+        _, M, K = sh[p]
+        xq = oracle.quantize_q8_0(x.contiguous().cpu().numpy(), batch, K)
+        ref = oracle.mul_mat_q8_0_batch(stack.weights[l][p].cpu().numpy(), xq, M, K, batch)
+        assert np.array_equal(ref.view(np.uint32), y.contiguous().cpu().numpy().view(np.uint32)), (l, p)
+
+
 def test_decode_stack_graph_replay_matches_eager(ane):
     import torch
 

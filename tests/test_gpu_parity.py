@@ -175,6 +175,24 @@ def test_gemm_s8_int32_exact(ane, M, N, K):
     assert np.array_equal(acc.cpu().numpy(), ref.astype(np.int32))
 
 
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 256),   # 256 tiles on 74 pairs: last 34 cut in 2
+                                   (1000, 1000, 256),   # 16 tiles: every tile cut in 4 (64 columns)
+                                   (4096, 1100, 512),   # 80 tiles: last 6 cut in 4, ragged N, parts past N
+                                   (3000, 2000, 384),   # 96 tiles: last 22 cut in 2, ragged M
+                                   (2304, 2304, 128)])  # 81 tiles: last 7 cut in 4
+def test_gemm_s8_tail_split_exact(ane, M, N, K):
+    """The pair kernel's last partial wave runs as column parts of 128 or 64;
+    every part is exact against an fp64 product (exact for these integers)."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N * 3 + K)
+    Aq = torch.randint(-127, 128, (M, K), generator=g, device="cuda", dtype=torch.int8)
+    Bt = torch.randint(-127, 128, (N, K), generator=g, device="cuda", dtype=torch.int8)
+    acc = ane.gemm_s8(Aq, Bt, raw_i32=True)
+    ref = (Aq.double() @ Bt.double().T).to(torch.int32)
+    assert torch.equal(acc, ref)
+
+
 def test_gemm_s8_extreme_values(ane):
     """All -127 / +127 operands: the largest |acc| K allows, exact."""
     import torch
