@@ -319,7 +319,7 @@ def mul_mat_q8_0(W, x, M: int, K: int, out=None, block_dots=None, stream=None, s
 
 
 def mul_mat_q8_0_batch_workspace(M: int, K: int, device):
-    """Zeroed workspace for mul_mat_q8_0_batch (reusable by calls on one stream)."""
+    """Workspace for mul_mat_q8_0_batch: the quantized activation (reusable by calls on one stream)."""
     torch = _torch()
     n = int(_lib.ane_mul_mat_q8_0_batch_workspace_size(M, K))
     return torch.zeros(n, dtype=torch.uint8, device=device)

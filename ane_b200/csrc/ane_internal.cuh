@@ -221,8 +221,8 @@ void stack_plan_free(void* plan);
 int launch_mul_mat_q8_0(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, int32_t* block_dots,
                         uint32_t flags, cudaStream_t s);
 // ggml MUL_MAT for NT <= 16 activation rows (q8_0_gemm_q8.cu); the workspace
-// (mul_mat_q8_0_batch_workspace_size bytes, 256-byte aligned) is zero before
-// the first call and left zero by every call.
+// (mul_mat_q8_0_batch_workspace_size bytes, 256-byte aligned) receives the
+// quantized activation.
 size_t mul_mat_q8_0_batch_workspace_size(uint32_t M, uint32_t K);
 int launch_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const float* x, size_t ldx, const uint8_t* W,
                               float* y, size_t ldy, void* workspace, uint32_t flags, cudaStream_t s);

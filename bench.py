@@ -264,6 +264,22 @@ def q8_bench(ane, torch, dev, steps=50):
                 key = name + ("_static" if st else "")
                 res[key + "_gbs"] = nbytes / (ms * 1e-3) / 1e9
                 res[key + "_us"] = ms * 1e3
+        # decode at batch 16: ggml MUL_MAT over 16 fp32 activation rows, weights read once
+        xb = torch.randn((16, cols), device=dev, generator=g)
+        yb = torch.empty((16, rows), device=dev)
+        ws = ane.mul_mat_q8_0_batch_workspace(rows, cols, dev)
+        for i in range(3):
+            ane.mul_mat_q8_0_batch(Ws[i % copies], xb, rows, cols, out=yb, workspace=ws, static_weights=True)
+        itb = [0]
+
+        def step_b():
+            ane.mul_mat_q8_0_batch(Ws[itb[0] % copies], xb, rows, cols, out=yb, workspace=ws, static_weights=True)
+            itb[0] += 1
+
+        ms = time_graph(step_b, steps, stream)
+        res["batch16_static_us"] = ms * 1e3
+        res["batch16_static_gbs"] = (wbytes + 16 * 4 * (cols + rows)) / (ms * 1e-3) / 1e9
+        res["batch16_tokens_per_s"] = 16 / (ms * 1e-3)
         res["timing"] = "CUDA graph of back-to-back calls"
         res["weight_copies_rotated"] = copies
         out[f"{rows}x{cols}"] = res

@@ -158,9 +158,9 @@ int ane_q8_0_gemv_q8_ex_dev(uint32_t M, uint32_t K, const void* xq_blocks, const
  * float(sumi) * (dw * dx) are summed in block order within segments of 32
  * blocks, then the segment sums in order (each sum from +0) -- an order fixed by
  * K alone.  K % 256 == 0; W and x 16-byte aligned, ldx % 4 == 0; `workspace`
- * holds ane_mul_mat_q8_0_batch_workspace_size(M, K) bytes, 256-byte aligned,
- * zero before its first use (every call leaves it so); calls sharing a
- * workspace must be ordered on one stream.  flags: ANE_Q8_WEIGHTS_STATIC.
+ * holds ane_mul_mat_q8_0_batch_workspace_size(M, K) bytes (the quantized
+ * activation), 256-byte aligned, any contents; calls sharing a workspace must
+ * be ordered on one stream.  flags: ANE_Q8_WEIGHTS_STATIC.
  * No counterpart in the reference. */
 size_t ane_mul_mat_q8_0_batch_workspace_size(uint32_t M, uint32_t K);
 int ane_mul_mat_q8_0_batch_dev(uint32_t M, uint32_t K, uint32_t NT, const float* x, size_t ldx, const void* W,

@@ -47,7 +47,7 @@ def test_mul_mat_q8_0_batch_exact(ane, M, K, NT):
 
 def test_mul_mat_q8_0_batch_strided_repeat_graph(ane):
     """Strided activation / output rows (a view into wider buffers), a reused
-    workspace (its counters return to zero), static weights, graph replay."""
+    workspace, static weights, graph replay."""
     import torch
 
     M, K, NT = 1024, 2048, 16
