@@ -322,16 +322,29 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
             ms = float(t.item())
         return ms
 
+    def capture(fn):
+        """fn captured in a CUDA graph (its NCCL all-gathers included when N > 1),
+        or None if any rank could not capture it (every rank then runs eagerly)."""
+        g = torch.cuda.CUDAGraph()
+        ok = 1
+        try:
+            with torch.cuda.graph(g):
+                fn()
+        except Exception:
+            g, ok = None, 0
+        torch.cuda.synchronize()
+        if group is not None:
+            t = torch.tensor([ok], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN, group=group)
+            if int(t.item()) == 0:
+                g = None
+        return g
+
     stack.forward()
     torch.cuda.synchronize()
-    g = None
-    if world == 1:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            stack.forward()
-        chain_ms = timed(g.replay)
-    else:
-        chain_ms = timed(stack.forward)
+    g = capture(stack.forward)
+    chain_graph = g is not None
+    chain_ms = timed(g.replay if chain_graph else stack.forward)
     del g
     fused = decode.FusedDecodeStack(stack, dev, group=group)
     try:
@@ -347,20 +360,15 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
                                weights=stack.weights)
     stack16.forward()
     torch.cuda.synchronize()
-    g16 = None
-    if world == 1:
-        g16 = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g16):
-            stack16.forward()
-        b16_ms = timed(g16.replay)
-    else:
-        b16_ms = timed(stack16.forward)
+    g16 = capture(stack16.forward)
+    b16_graph = g16 is not None
+    b16_ms = timed(g16.replay if b16_graph else stack16.forward)
     del g16, stack16
     wbytes = decode.stack_weight_bytes(layers)
     peaks = load_peaks()
     fused_path = "one persistent launch per token" + (", all-gather by NVLink peer stores" if world > 1 else "")
-    chain_path = (f"{4 * layers} MUL_MAT launches in a CUDA graph" if world == 1
-                  else f"{4 * layers} MUL_MAT launches + NCCL all-gather each")
+    chain_path = (f"{4 * layers} MUL_MAT launches" + ("" if world == 1 else " + NCCL all-gather each")
+                  + (" in a CUDA graph" if chain_graph else " (eager)"))
     best_ms, best_path = (fused_ms, fused_path) if fused_ms <= chain_ms else (chain_ms, chain_path)
     gbs = wbytes / (best_ms * 1e-3) / 1e9
     return {"layers": layers, "batch": 1, "n_gpus": world, "weight_bytes": wbytes, "ms_per_token": best_ms,
@@ -371,7 +379,8 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
                         "weight_gbs": wbytes / (b16_ms * 1e-3) / 1e9,
                         "per_gpu_hbm_frac": wbytes / (b16_ms * 1e-3) / 1e9 / world / peaks["hbm_gbs"],
                         "path": (f"{4 * layers} x (activation quantize + batched MUL_MAT) launches"
-                                 + (" in a CUDA graph" if world == 1 else " + NCCL all-gather each"))},
+                                 + ("" if world == 1 else " + NCCL all-gather each")
+                                 + (" in a CUDA graph" if b16_graph else " (eager)"))},
             "activation": "Q8_0 (ggml convention), static weights",
             "timing": f"{reps} tokens each path, CUDA events" + ("" if world == 1 else ", max over ranks"),
             "build_s": build_s}
