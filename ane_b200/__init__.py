@@ -50,6 +50,10 @@ SIGNATURES = {
     "ane_pack_b_i8": (_i32, [_u32, _u32, _vp, _vp]),
     "ane_quantize_fp32_i8_channelwise": (_i32, [_u32, _u32, _vp, _vp, _vp]),
     "ane_dense_i8": (_i32, [_u32, _u32, _u32, _f, _f, _u8, _vp, _vp, _vp, _vp]),
+    "ane_dense_u8s8": (_i32, [_u32, _u32, _u32, _f, _f, _u8, _vp, _vp, _vp, _vp]),
+    "ane_cblas_igemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
+    "ane_cblas_ugemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
+    "ane_cblas_usgemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
     "ane_dense_fused_i8": (_i32, [_u32, _u32, _u32, _f, _u8, _vp, _vp, _vp]),
     "ane_q8_0_gemv": (_i32, [_u32, _u32, _vp, _vp, _vp]),
     "ane_dense_fused_i8_workspace_size": (_sz, [_u32, _u32, _u32]),
@@ -63,6 +67,8 @@ SIGNATURES = {
     "ane_quantize_fp32_i8_dev": (_i32, [_u32, _vp, _vp, _vp, _vp]),
     "ane_pack_b_i8_dev": (_i32, [_u32, _u32, _vp, _vp, _vp]),
     "ane_dense_i8_dev": (_i32, [_u32, _u32, _u32, _f, _f, _u8, _vp, _vp, _vp, _vp, _vp]),
+    "ane_dense_u8s8_dev": (_i32, [_u32, _u32, _u32, _f, _f, _u8, _vp, _vp, _vp, _vp, _vp]),
+    "ane_cblas_int_gemm_dev": (_i32, [_i32, _u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp, _vp]),
     "ane_q8_0_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
     "ane_quantize_q8_0_dev": (_i32, [_u32, _vp, _vp, _vp]),
     "ane_q8_0_gemv_q8_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _vp]),
@@ -133,6 +139,8 @@ class Op(enum.IntEnum):
     q8_0_gemv = 0x57
     q4_0_gemv = 0x58
     cblas_igemm = 0x61
+    cblas_ugemm = 0x62
+    cblas_usgemm = 0x63
     get_rows_q8_0 = 0x7C
     dense_fused_i8 = 0x80
 
@@ -257,6 +265,19 @@ def quantize_pair(A, B, stream=None):
     check(_lib.ane_quantize_pair_dev(M, N, K, A.contiguous().data_ptr(), B.contiguous().data_ptr(), Aq.data_ptr(),
                                      Bt.data_ptr(), scales.data_ptr(), partials.data_ptr(), _stream_ptr(stream)))
     return Aq, Bt, scales
+
+
+INT_GEMM_KINDS = {"igemm": 0, "ugemm": 1, "usgemm": 2}
+
+
+def cblas_int_gemm(kind: str, A, B, C, M: int, N: int, K: int, lda: int, ldb: int, ldc: int, alpha: float = 1.0,
+                   beta: float = 0.0, trans_a: bool = False, trans_b: bool = False, stream=None):
+    """cblas_igemm / ugemm / usgemm on device tensors (byte strides lda / ldb, ldc
+    in floats): C = alpha * cvt(op(A) @ op(B)) [beta: see ane_cblas_igemm]."""
+    flags = (1 if trans_a else 0) | (2 if trans_b else 0)
+    check(_lib.ane_cblas_int_gemm_dev(INT_GEMM_KINDS[kind], flags, M, N, K, lda, ldb, ldc, float(alpha), float(beta),
+                                      A.data_ptr(), B.data_ptr(), C.data_ptr(), _stream_ptr(stream)))
+    return C
 
 
 def gemm_s8(Aq, Bt, scales=None, scale: float = 1.0, relu: bool = False, raw_i32: bool = False, out=None,

@@ -175,12 +175,16 @@ int launch_dequantize(size_t count, float scale, const int8_t* src, float* dst, 
 int launch_pack_b(uint32_t K, uint32_t N, const int8_t* src, int8_t* dst, cudaStream_t s);
 int launch_unpack_b_to_kmajor(uint32_t K64, uint32_t N, const int8_t* Bp, int8_t* Bt,
                               cudaStream_t s);
+// Strided (optionally transposed) int8 operand -> `rows` x K16 K-major, pad 0.
+int launch_kmajor_i8(const void* src, size_t ld, bool trans, uint32_t rows, uint32_t K, uint32_t K16, void* dst,
+                     cudaStream_t s);
 
 // GEMM epilogue selector.
 enum GemmOut : int {
     kOutFusedF32 = 0,  // y = float(acc)*(sa*sb); y = y*scale; relu ? fmax(y,0) : y
     kOutRawI32 = 1,    // int32 accumulators
     kOutDenseI8 = 2,   // y = float(acc)*(sa*sb); y = y + bias[n]; fmax(y, relu ? 0 : -FLT_MAX)
+    kOutIntGemm = 3,   // integer CBLAS GEMM: y = cvt(acc [+ bits(beta*C) if beta != 0]) * alpha
 };
 struct GemmEpilogue {
     int mode;
@@ -189,6 +193,12 @@ struct GemmEpilogue {
     float scale;          // fused mode multiplier
     int relu;
     const float* bias;    // dense_i8 mode, device pointer (>= N floats)
+    // operand signedness (tcgen05 kind::i8 takes each as s8 or u8)
+    int a_unsigned = 0, b_unsigned = 0;
+    // kOutIntGemm: alpha, beta, C read in place (row stride = ldc of the launch);
+    // acc_unsigned: the accumulator converts as uint32 (ucvtf), else int32 (scvtf)
+    float alpha = 1.0f, beta = 0.0f;
+    int acc_unsigned = 0;
 };
 // C[M x ldc] += epilogue(Aq[M x K] * Bt[N x K]^T); K multiple of 16, both K-major
 // with row stride K.

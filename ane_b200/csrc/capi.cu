@@ -368,14 +368,13 @@ int ane_pack_b_i8_dev(uint32_t K, uint32_t N, const int8_t* src, int8_t* dst, vo
     return rc ? rc : ok();
 }
 
-int ane_dense_i8_dev(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags, const int8_t* A,
-                     const int8_t* B_packed, const float* bias, float* C, void* stream) {
-    ANE_REQUIRE_GPU();
-    if (M == 0 || N == 0) return ok();
+// dense_i8 (A signed) and dense_u8s8 (A unsigned) on device pointers.
+static int dense8_dev(bool a_unsigned, uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags,
+                      const void* A, const int8_t* B_packed, const float* bias, float* C, cudaStream_t s) {
+    if (M == 0 || N == 0) return ANE_OK;
     const uint32_t M16 = (uint32_t)round_up(M, 16), K64 = (uint32_t)round_up(K, 64);
     int rc = ensure_thread_ctx();
     if (rc) return rc;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t need = (size_t)N * K64;
     if (t_ctx.ws_bytes < need) cudaStreamSynchronize(s);
     rc = ensure_buffer(&t_ctx.ws, &t_ctx.ws_bytes, need > 0 ? need : 1);
@@ -384,7 +383,79 @@ int ane_dense_i8_dev(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uin
     rc = launch_unpack_b_to_kmajor(K64, N, B_packed, Bt, s);
     if (rc) return rc;
     GemmEpilogue ep{kOutDenseI8, nullptr, sa, sb, 1.f, (flags & 1) ? 1 : 0, bias};
-    rc = launch_gemm_s8_tc(M16, N, K64, A, Bt, C, N, ep, s);
+    ep.a_unsigned = a_unsigned ? 1 : 0;
+    return launch_gemm_s8_tc(M16, N, K64, static_cast<const int8_t*>(A), Bt, C, N, ep, s);
+}
+
+int ane_dense_i8_dev(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags, const int8_t* A,
+                     const int8_t* B_packed, const float* bias, float* C, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = dense8_dev(false, M, N, K, sa, sb, flags, A, B_packed, bias, C, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+int ane_dense_u8s8_dev(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags, const uint8_t* A,
+                       const int8_t* B_packed, const float* bias, float* C, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = dense8_dev(true, M, N, K, sa, sb, flags, A, B_packed, bias, C, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+// Integer CBLAS GEMMs: operands to K-major rows (transposing where the layout
+// asks for it), then the tensor-core GEMM with per-operand signedness and the
+// cvt * alpha epilogue.  kind: 0 igemm, 1 ugemm, 2 usgemm.
+static size_t int_gemm_ws(uint32_t M, uint32_t N, uint32_t K) {
+    const size_t K16 = round_up(K, 16);
+    return round_up((size_t)M * K16, 256) + round_up((size_t)N * K16, 256);
+}
+
+static int int_gemm_check(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
+                          uint32_t ldc, const void* A, const void* B, const float* C) {
+    ANE_ARG_CHECK((flags & ~3u) == 0, "integer gemm: unknown flag bits");
+    ANE_ARG_CHECK(K % 64 == 0, "integer gemm: K must be a multiple of 64");
+    ANE_ARG_CHECK(lda >= ((flags & 1) ? M : K) && ldb >= ((flags & 2) ? K : N) && ldc >= N,
+                  "integer gemm: leading dimension smaller than the matrix");
+    ANE_ARG_CHECK(M == 0 || N == 0 || (C && (K == 0 || (A && B))), "integer gemm: NULL pointer");
+    return ANE_OK;
+}
+
+static int int_gemm_on_stream(int kind, uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda,
+                              uint32_t ldb, uint32_t ldc, float alpha, float beta, const void* A, const void* B,
+                              float* C, void* ws, cudaStream_t s) {
+    if (M == 0 || N == 0) return ANE_OK;
+    const uint32_t K16 = (uint32_t)round_up(K, 16);
+    uint8_t* Akm = static_cast<uint8_t*>(ws);
+    uint8_t* Bkm = Akm + round_up((size_t)M * K16, 256);
+    int rc = launch_kmajor_i8(A, lda, (flags & 1) != 0, M, K, K16, Akm, s);  // transA: A is K x M
+    if (rc) return rc;
+    rc = launch_kmajor_i8(B, ldb, (flags & 2) == 0, N, K, K16, Bkm, s);     // B is K x N unless transB
+    if (rc) return rc;
+    GemmEpilogue ep{kOutIntGemm, nullptr, 1.f, 1.f, 1.f, 0, nullptr};
+    ep.a_unsigned = kind != 0;
+    ep.b_unsigned = kind == 1;
+    ep.acc_unsigned = kind == 1;
+    ep.alpha = alpha;
+    ep.beta = beta;
+    return launch_gemm_s8_tc(M, N, K16, reinterpret_cast<const int8_t*>(Akm), reinterpret_cast<const int8_t*>(Bkm),
+                             C, ldc, ep, s);
+}
+
+int ane_cblas_int_gemm_dev(int kind, uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
+                           uint32_t ldc, float alpha, float beta, const void* A, const void* B, float* C,
+                           void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(kind >= 0 && kind <= 2, "integer gemm: kind must be 0 (igemm), 1 (ugemm) or 2 (usgemm)");
+    int rc = int_gemm_check(flags, M, N, K, lda, ldb, ldc, A, B, C);
+    if (rc) return rc;
+    if (M == 0 || N == 0) return ok();
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    rc = ensure_thread_ctx();
+    if (rc) return rc;
+    const size_t need = int_gemm_ws(M, N, K);
+    if (t_ctx.ws_bytes < need) cudaStreamSynchronize(s);
+    rc = ensure_buffer(&t_ctx.ws, &t_ctx.ws_bytes, need > 0 ? need : 1);
+    if (rc) return rc;
+    rc = int_gemm_on_stream(kind, flags, M, N, K, lda, ldb, ldc, alpha, beta, A, B, C, t_ctx.ws, s);
     return rc ? rc : ok();
 }
 
@@ -600,8 +671,9 @@ int ane_quantize_fp32_i8_channelwise(uint32_t rows, uint32_t cols, const float* 
     });
 }
 
-int ane_dense_i8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags, const int8_t* A,
-                 const int8_t* B_packed, const float* bias, float* C) {
+// dense_i8 / dense_u8s8 on any pointer kind (the reference's synchronous contract).
+static int dense8_host(bool a_unsigned, uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags,
+                       const void* A, const int8_t* B_packed, const float* bias, float* C) {
     ANE_REQUIRE_GPU();
     if (M == 0 || N == 0) return ok();
     ANE_ARG_CHECK(A && B_packed && bias && C, "dense_i8: NULL pointer");
@@ -617,9 +689,51 @@ int ane_dense_i8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t
         int rc = launch_unpack_b_to_kmajor((uint32_t)K64, N, (const int8_t*)args[1].dev, Bt, s);
         if (rc) return rc;
         GemmEpilogue ep{kOutDenseI8, nullptr, sa, sb, 1.f, (flags & 1) ? 1 : 0, (const float*)args[2].dev};
+        ep.a_unsigned = a_unsigned ? 1 : 0;
         return launch_gemm_s8_tc((uint32_t)M16, N, (uint32_t)K64, (const int8_t*)args[0].dev, Bt, args[3].dev, N,
                                  ep, s);
     });
+}
+
+int ane_dense_i8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags, const int8_t* A,
+                 const int8_t* B_packed, const float* bias, float* C) {
+    return dense8_host(false, M, N, K, sa, sb, flags, A, B_packed, bias, C);
+}
+
+int ane_dense_u8s8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags, const uint8_t* A,
+                   const int8_t* B_packed, const float* bias, float* C) {
+    return dense8_host(true, M, N, K, sa, sb, flags, A, B_packed, bias, C);
+}
+
+static int int_gemm_host(int kind, uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
+                         uint32_t ldc, float alpha, float beta, const void* A, const void* B, float* C) {
+    ANE_REQUIRE_GPU();
+    int rc = int_gemm_check(flags, M, N, K, lda, ldb, ldc, A, B, C);
+    if (rc) return rc;
+    if (M == 0 || N == 0) return ok();
+    // bytes each strided operand spans
+    const bool ta = flags & 1, tb = flags & 2;
+    const size_t a_bytes = K == 0 ? 0 : ta ? (size_t)(K - 1) * lda + M : (size_t)(M - 1) * lda + K;
+    const size_t b_bytes = K == 0 ? 0 : tb ? (size_t)(N - 1) * ldb + K : (size_t)(K - 1) * ldb + N;
+    const size_t c_bytes = ((size_t)(M - 1) * ldc + N) * 4;
+    std::vector<Arg> args = {{A, a_bytes, true, false}, {B, b_bytes, true, false}, {C, c_bytes, true, true}};
+    return run_staged(args, int_gemm_ws(M, N, K), [&](cudaStream_t s, void* extra) {
+        return int_gemm_on_stream(kind, flags, M, N, K, lda, ldb, ldc, alpha, beta, args[0].dev, args[1].dev,
+                                  (float*)args[2].dev, extra, s);
+    });
+}
+
+int ane_cblas_igemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
+                    float alpha, float beta, const void* A, const void* B, float* C) {
+    return int_gemm_host(0, flags, M, N, K, lda, ldb, ldc, alpha, beta, A, B, C);
+}
+int ane_cblas_ugemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
+                    float alpha, float beta, const void* A, const void* B, float* C) {
+    return int_gemm_host(1, flags, M, N, K, lda, ldb, ldc, alpha, beta, A, B, C);
+}
+int ane_cblas_usgemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
+                     float alpha, float beta, const void* A, const void* B, float* C) {
+    return int_gemm_host(2, flags, M, N, K, lda, ldb, ldc, alpha, beta, A, B, C);
 }
 
 int ane_dense_fused_i8(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t relu, const float* A,

@@ -152,6 +152,20 @@ __device__ __forceinline__ void store_block(const Params& p, float comb, const u
             for (int j = 0; j < 32; j++)
                 v[j] = __float_as_uint(__fmul_rn(__fmul_rn(__int2float_rn((int32_t)r[j]), comb), scale));
         }
+    } else if (p.ep.mode == kOutIntGemm) {
+        // the reference seeds its int32 accumulator with the fp32 bits of beta*C
+        // when beta != 0 (cblas integer GEMM macro, bytecode_interpreter.s:8411-8489)
+        const float alpha = p.ep.alpha, beta = p.ep.beta;
+        const bool fold = __float_as_uint(beta) != 0u;
+        const uint32_t m = row0 + lane;
+        const float* crow = reinterpret_cast<const float*>(p.C) + (size_t)m * p.ldc + nc;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            uint32_t a = r[j];
+            if (fold && m < p.M && nc + j < p.N) a += __float_as_uint(__fmul_rn(crow[j], beta));
+            const float f = p.ep.acc_unsigned ? __uint2float_rn(a) : __int2float_rn((int32_t)a);
+            v[j] = __float_as_uint(__fmul_rn(f, alpha));
+        }
     } else {
         const float floor_v = p.ep.relu ? 0.0f : -FLT_MAX;
         const float* bias = p.ep.bias + nc;
@@ -269,7 +283,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = ptx::idesc_s8s8s32(S_BM, S_BN);
+            const uint32_t idesc = ptx::idesc_i8(S_BM, S_BN, !p.ep.a_unsigned, !p.ep.b_unsigned);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool alive = true;
             for (uint32_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
@@ -399,7 +413,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (uint32_t u = pair; u < num_units && alive; u += num_pairs) {
                 const PairUnit un = pair_unit(p, u);
                 if (un.n0 >= p.N) continue;
-                const uint32_t idesc = ptx::idesc_s8s8s32(P_BM, (int)un.ncols);
+                const uint32_t idesc = ptx::idesc_i8(P_BM, (int)un.ncols, !p.ep.a_unsigned, !p.ep.b_unsigned);
                 if (!ptx::mbar_wait(&bars->tmem_empty[acc], acc_phase ^ 1, p.err)) break;
                 ptx::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
@@ -465,6 +479,13 @@ __global__ void fill_zero_k_kernel(uint32_t M, uint32_t N, void* C, size_t ldc, 
         const uint32_t m = (uint32_t)(i / N), n = (uint32_t)(i % N);
         if (ep.mode == kOutRawI32) {
             reinterpret_cast<int32_t*>(C)[(size_t)m * ldc + n] = 0;
+            continue;
+        }
+        if (ep.mode == kOutIntGemm) {
+            float* c = reinterpret_cast<float*>(C) + (size_t)m * ldc + n;
+            const uint32_t a = __float_as_uint(ep.beta) != 0u ? __float_as_uint(__fmul_rn(*c, ep.beta)) : 0u;
+            const float f = ep.acc_unsigned ? __uint2float_rn(a) : __int2float_rn((int32_t)a);
+            *c = __fmul_rn(f, ep.alpha);
             continue;
         }
         float y = __fmul_rn(0.0f, comb);

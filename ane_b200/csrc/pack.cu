@@ -78,4 +78,44 @@ int launch_unpack_b_to_kmajor(uint32_t K64, uint32_t N, const int8_t* Bp, int8_t
     return ANE_OK;
 }
 
+// Strided int8 operand -> K-major rows for the tensor-core GEMM (integer CBLAS
+// GEMMs, cblas_igemm / ugemm / usgemm, src/bytecode_interpreter.s:8329-9139):
+//   dst[r][k] = k < K ? (trans ? src[k * ld + r] : src[r * ld + k]) : 0,
+// r < rows, k < K16 (row stride K16).  32 x 32 byte tiles through shared memory
+// so both the reads and the writes run along contiguous bytes.
+__global__ void kmajor_i8_kernel(const uint8_t* __restrict__ src, size_t ld, int trans, uint32_t rows, uint32_t K,
+                                 uint32_t K16, uint8_t* __restrict__ dst) {
+    __shared__ uint8_t tile[32][33];
+    const uint32_t k0 = blockIdx.x * 32, r0 = blockIdx.y * 32, tx = threadIdx.x, ty = threadIdx.y;
+    if (trans) {  // src is K x rows: read along r, write along k
+#pragma unroll
+        for (uint32_t i = 0; i < 32; i += 8) {
+            const uint32_t k = k0 + ty + i, r = r0 + tx;
+            tile[ty + i][tx] = (k < K && r < rows) ? src[(size_t)k * ld + r] : (uint8_t)0;
+        }
+        __syncthreads();
+#pragma unroll
+        for (uint32_t i = 0; i < 32; i += 8) {
+            const uint32_t r = r0 + ty + i, k = k0 + tx;
+            if (r < rows && k < K16) dst[(size_t)r * K16 + k] = tile[tx][ty + i];
+        }
+    } else {  // src is rows x K
+#pragma unroll
+        for (uint32_t i = 0; i < 32; i += 8) {
+            const uint32_t r = r0 + ty + i, k = k0 + tx;
+            if (r < rows && k < K16) dst[(size_t)r * K16 + k] = k < K ? src[(size_t)r * ld + k] : (uint8_t)0;
+        }
+    }
+}
+
+int launch_kmajor_i8(const void* src, size_t ld, bool trans, uint32_t rows, uint32_t K, uint32_t K16, void* dst,
+                     cudaStream_t s) {
+    if (rows == 0 || K16 == 0) return ANE_OK;
+    const dim3 grid((K16 + 31) / 32, (rows + 31) / 32), block(32, 8);
+    kmajor_i8_kernel<<<grid, block, 0, s>>>(static_cast<const uint8_t*>(src), ld, trans ? 1 : 0, rows, K, K16,
+                                            static_cast<uint8_t*>(dst));
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
+
 }  // namespace ane_b200

@@ -249,6 +249,11 @@ __host__ __device__ constexpr uint32_t idesc_s8s8s32(int M, int N) {
            | ((uint32_t)(N >> 3) << 17)  // N / 8
            | ((uint32_t)(M >> 4) << 24); // M / 16
 }
+// kind::i8 with each operand signed (1) or unsigned (0) 8-bit; S32 accumulator.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N, bool a_signed, bool b_signed) {
+    return (2u << 4) | ((a_signed ? 1u : 0u) << 7) | ((b_signed ? 1u : 0u) << 10) |
+           ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
 
 }  // namespace ptx
 }  // namespace ane_b200

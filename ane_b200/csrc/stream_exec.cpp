@@ -45,6 +45,10 @@ int payload_size(uint8_t op) {
         case 0x1A: return 4 + 4 + 16;       // dequantize_i8_fp32: count scale src dst
         case 0x1B: return 8 + 16;           // pack_b_i8: K N src dst
         case 0x1C: return 8 + 24;           // quantize_fp32_i8_channelwise: rows cols src dst scales
+        case 0x1E: return 12 + 8 + 1 + 32;  // dense_u8s8: as dense_i8, A unsigned
+        case 0x61:                          // cblas_igemm / ugemm / usgemm:
+        case 0x62:                          //   flags M N K lda ldb ldc alpha beta A B C
+        case 0x63: return 1 + 12 + 12 + 8 + 24;
         case 0x57: return 8 + 24;           // q8_0_gemv: M K in W out
         case 0x80: return 12 + 4 + 1 + 24;  // dense_fused_i8: M N K scale relu A B C
         default: return -1;
@@ -64,6 +68,30 @@ int exec_one(uint8_t op, Reader& r) {
             const float* bias = r.ptr<const float>();
             float* C = r.ptr<float>();
             return ane_dense_i8(M, N, K, sa, sb, flags, A, Bp, bias, C);
+        }
+        case 0x1E: {
+            uint32_t M = r.get<uint32_t>(), N = r.get<uint32_t>(), K = r.get<uint32_t>();
+            float sa = r.get<float>(), sb = r.get<float>();
+            uint8_t flags = r.get<uint8_t>();
+            const uint8_t* A = r.ptr<const uint8_t>();
+            const int8_t* Bp = r.ptr<const int8_t>();
+            const float* bias = r.ptr<const float>();
+            float* C = r.ptr<float>();
+            return ane_dense_u8s8(M, N, K, sa, sb, flags, A, Bp, bias, C);
+        }
+        case 0x61:
+        case 0x62:
+        case 0x63: {
+            uint8_t flags = r.get<uint8_t>();
+            uint32_t M = r.get<uint32_t>(), N = r.get<uint32_t>(), K = r.get<uint32_t>();
+            uint32_t lda = r.get<uint32_t>(), ldb = r.get<uint32_t>(), ldc = r.get<uint32_t>();
+            float alpha = r.get<float>(), beta = r.get<float>();
+            const void* A = r.ptr<const void>();
+            const void* B = r.ptr<const void>();
+            float* C = r.ptr<float>();
+            if (op == 0x61) return ane_cblas_igemm(flags, M, N, K, lda, ldb, ldc, alpha, beta, A, B, C);
+            if (op == 0x62) return ane_cblas_ugemm(flags, M, N, K, lda, ldb, ldc, alpha, beta, A, B, C);
+            return ane_cblas_usgemm(flags, M, N, K, lda, ldb, ldc, alpha, beta, A, B, C);
         }
         case 0x19: {
             // The handler works on whole 16-lane vectors: ceil(count/16)*16 elements

@@ -62,7 +62,7 @@ enum class Op : uint8_t {
     pack_b_i8 = 0x1B,                     // executed on the GPU
     quantize_fp32_i8_channelwise = 0x1C,  // executed on the GPU
     transpose_i8 = 0x1D,
-    dense_u8s8 = 0x1E,
+    dense_u8s8 = 0x1E,                    // executed on the GPU
     load = 0x1F,
     store = 0x20,
     l2_squared_fp32 = 0x21,
@@ -129,9 +129,9 @@ enum class Op : uint8_t {
     load_wide_param = 0x5E,
     store_wide_param = 0x5F,
     cblas_bfgemm = 0x60,
-    cblas_igemm = 0x61,
-    cblas_ugemm = 0x62,
-    cblas_usgemm = 0x63,
+    cblas_igemm = 0x61,                   // executed on the GPU
+    cblas_ugemm = 0x62,                   // executed on the GPU
+    cblas_usgemm = 0x63,                  // executed on the GPU
     gemm_tile_fp32 = 0x64,
     softmax_partial_fp32 = 0x65,
     softmax_correct_fp32 = 0x66,

@@ -70,6 +70,24 @@ int ane_quantize_fp32_i8_channelwise(uint32_t rows, uint32_t cols, const float* 
  * C receives M16 rows of N floats (padded rows included). */
 int ane_dense_i8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags,
                  const int8_t* A, const int8_t* B_packed, const float* bias, float* C);
+/* dense_u8s8 (0x1E; :2841-3305): dense_i8 with an unsigned A (u8 x s8 products),
+ * same memory contract, scales, bias and ReLU. */
+int ane_dense_u8s8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags,
+                   const uint8_t* A, const int8_t* B_packed, const float* bias, float* C);
+/* Integer CBLAS GEMMs (0x61 cblas_igemm s8 x s8, 0x62 cblas_ugemm u8 x u8,
+ * 0x63 cblas_usgemm u8 x s8; :8329-9139, docs/API.md:356-370):
+ * C = alpha * cvt(op(A) @ op(B)), flags bit 0 = transpose A (A stored K x M),
+ * bit 1 = transpose B (B stored N x K); lda / ldb in bytes, ldc in floats;
+ * K % 64 == 0.  cvt = int32 -> fp32 (uint32 -> fp32 for ugemm), then one RN
+ * multiply by alpha.  beta != 0 reproduces the reference: its int32
+ * accumulator starts from the fp32 bit pattern of RN(beta * C) (the ZA tiles
+ * are seeded with beta*C, :8411-8489) instead of adding beta*C in fp32. */
+int ane_cblas_igemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
+                    float alpha, float beta, const void* A, const void* B, float* C);
+int ane_cblas_ugemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
+                    float alpha, float beta, const void* A, const void* B, float* C);
+int ane_cblas_usgemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
+                     float alpha, float beta, const void* A, const void* B, float* C);
 /* dense_fused_i8 (0x80, new; README.md:87-97 usage).  fp32 A (M x K, stride K)
  * and B (K x N, stride N) quantized per tensor to int8 (absmax/127), int8 x int8
  * -> exact int32, y = float(acc)*(sa*sb), y = y*scale, optional ReLU; C is
@@ -115,6 +133,13 @@ int ane_pack_b_i8_dev(uint32_t K, uint32_t N, const int8_t* src, int8_t* dst, vo
 int ane_dense_i8_dev(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags,
                      const int8_t* A, const int8_t* B_packed, const float* bias, float* C,
                      void* stream);
+int ane_dense_u8s8_dev(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags,
+                       const uint8_t* A, const int8_t* B_packed, const float* bias, float* C,
+                       void* stream);
+/* kind: 0 = igemm (s8 x s8), 1 = ugemm (u8 x u8), 2 = usgemm (u8 x s8). */
+int ane_cblas_int_gemm_dev(int kind, uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda,
+                           uint32_t ldb, uint32_t ldc, float alpha, float beta, const void* A, const void* B,
+                           float* C, void* stream);
 int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out,
                       void* stream);
 /* Q8_0 x Q8_0 matvec (the ggml / llama.cpp activation convention; the

@@ -63,6 +63,9 @@ def lib():
             "ane_ref_q8_0_gemv_q8": (None, [_u32, _u32, _u8p, _u8p, _f32p, _vp]),
             "ane_ref_get_rows_q8_0": (None, [_u32, _u32, _u8p, _u32p, _f32p]),
             "ane_ref_mul_mat_q8_0_batch": (None, [_u32, _u32, _u32, _u8p, _u8p, _f32p, _sz]),
+            "ane_ref_dense_u8s8": (None, [_u32, _u32, _u32, _f, _f, ctypes.c_uint8, _u8p, _i8p, _f32p, _f32p]),
+            "ane_ref_int_gemm": (None, [ctypes.c_int, ctypes.c_uint8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f,
+                                        _u8p, _u8p, _f32p]),
             "ane_ref_dense_fused_i8_omp": (None, [_u32, _u32, _u32, _f, ctypes.c_int, _f32p, _f32p, _f32p,
                                                   ctypes.c_int]),
             "ane_ref_q8_0_gemv_omp": (None, [_u32, _u32, _f32p, _u8p, _f32p, ctypes.c_int]),
@@ -226,6 +229,27 @@ def q8_0_gemv_q8(W_blocks, xq_blocks, M: int, K: int, with_dots=False):
     lib().ane_ref_q8_0_gemv_q8(M, K, _c(xq_blocks, np.uint8).ravel(), _c(W_blocks, np.uint8).ravel(), out,
                                _ptr(dots) if with_dots else None)
     return (out, dots.reshape(M, K // 32)) if with_dots else out
+
+
+def dense_u8s8(M, N, K, sa, sb, flags, A_pad, B_packed, bias, C_rows=None):
+    """Reference dense_u8s8 on padded buffers: A uint8 [M16 x K64], B packed (pack_b_i8
+    with K64), bias [>= N]; returns C [M16 x N] (padded rows included)."""
+    M16 = (M + 15) // 16 * 16
+    C = np.empty(M16 * N, np.float32)
+    lib().ane_ref_dense_u8s8(M, N, K, sa, sb, flags, _c(A_pad, np.uint8).ravel(), _c(B_packed, np.int8).ravel(),
+                             _c(bias, np.float32).ravel(), C)
+    return C.reshape(M16, N)
+
+
+INT_GEMM_KINDS = {"igemm": 0, "ugemm": 1, "usgemm": 2}
+
+
+def int_gemm(kind, flags, M, N, K, lda, ldb, ldc, alpha, beta, A_bytes, B_bytes, C):
+    """Reference integer CBLAS GEMM; C (float32, >= (M-1)*ldc+N) is updated in place."""
+    assert C.dtype == np.float32 and C.flags["C_CONTIGUOUS"]
+    lib().ane_ref_int_gemm(INT_GEMM_KINDS[kind], flags, M, N, K, lda, ldb, ldc, alpha, beta,
+                           _c(A_bytes, np.uint8).ravel(), _c(B_bytes, np.uint8).ravel(), C.ravel())
+    return C
 
 
 def mul_mat_q8_0_batch(W_blocks, xq_blocks, M: int, K: int, NT: int):

@@ -216,6 +216,63 @@ void ane_ref_dense_i8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, ui
     }
 }
 
+/* dense_u8s8 (bytecode_interpreter.s:2841-3305): dense_i8 with an unsigned A
+ * (usmopa), the same padding, epilogue and ReLU floor. */
+void ane_ref_dense_u8s8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags,
+                        const uint8_t* A, const int8_t* B_packed, const float* bias, float* C) {
+    uint32_t M16 = (M + 15) & ~15u;
+    uint32_t N32 = (N + 31) & ~31u;
+    uint32_t K64 = (K + 63) & ~63u;
+    size_t G = K64 / 4;
+    float comb = sa * sb;
+    float floor_v = (flags & 1) ? 0.0f : -FLT_MAX;
+    for (uint32_t r = 0; r < M16; r++) {
+        for (uint32_t n = 0; n < N32 && n < N; n++) {
+            size_t p = n / 16, c = n % 16;
+            int32_t acc = 0;
+            for (uint32_t k = 0; k < K64; k++) {
+                size_t g = k / 4, d = k % 4;
+                acc += (int32_t)A[(size_t)r * K64 + k] * (int32_t)B_packed[(p * G + g) * 64 + c * 4 + d];
+            }
+            float y = (float)acc;
+            y = y * comb;
+            y = y + bias[n];
+            C[(size_t)r * N + n] = ane_ref_relu_max(y, floor_v);
+        }
+    }
+}
+
+/* Integer CBLAS GEMMs (bytecode_interpreter.s:8329-9139, macro CBLAS_INTEGER_GEMM):
+ * kind 0 igemm (s8 x s8, scvtf), 1 ugemm (u8 x u8, ucvtf), 2 usgemm (u8 x s8, scvtf).
+ * op(A)[m][k] = flags&1 ? A[k*lda+m] : A[m*lda+k]; op(B)[k][n] = flags&2 ? B[n*ldb+k]
+ * : B[k*ldb+n].  The 32-bit accumulator starts at 0, or -- when beta's bits are
+ * not zero -- at the bit pattern of RN(beta * C[m][n]) (the ZA tile is loaded
+ * with fmul(C, beta), :8411-8489); products are added modulo 2^32; then
+ * C = RN(cvt(acc) * alpha). */
+void ane_ref_int_gemm(int kind, uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
+                      uint32_t ldc, float alpha, float beta, const uint8_t* A, const uint8_t* B, float* C) {
+    uint32_t beta_bits;
+    memcpy(&beta_bits, &beta, 4);
+    for (uint32_t m = 0; m < M; m++)
+        for (uint32_t n = 0; n < N; n++) {
+            float* c = C + (size_t)m * ldc + n;
+            uint32_t acc = 0;
+            if (beta_bits != 0) {
+                float bc = *c * beta;
+                memcpy(&acc, &bc, 4);
+            }
+            for (uint32_t k = 0; k < K; k++) {
+                uint8_t a = (flags & 1) ? A[(size_t)k * lda + m] : A[(size_t)m * lda + k];
+                uint8_t b = (flags & 2) ? B[(size_t)n * ldb + k] : B[(size_t)k * ldb + n];
+                int32_t av = kind == 0 ? (int32_t)(int8_t)a : (int32_t)a;
+                int32_t bv = kind == 1 ? (int32_t)b : (int32_t)(int8_t)b;
+                acc += (uint32_t)(av * bv);
+            }
+            float f = kind == 1 ? (float)acc : (float)(int32_t)acc;
+            *c = f * alpha;
+        }
+}
+
 /* ---------------------------------------------------------- dense_fused_i8 */
 
 void ane_ref_dense_fused_epilogue(uint32_t M, uint32_t N, const int32_t* acc, float sa, float sb,

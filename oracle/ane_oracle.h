@@ -105,6 +105,16 @@ void ane_ref_quantize_q8_0(const float* x, uint8_t* blocks, size_t n_rows, size_
 void ane_ref_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8_t* W,
                           float* out, int32_t* block_dots);
 
+/* ---- dense_u8s8 (0x1E; :2841-3305): dense_i8 with unsigned A ----------------------- */
+void ane_ref_dense_u8s8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags,
+                        const uint8_t* A, const int8_t* B_packed, const float* bias, float* C);
+
+/* ---- integer CBLAS GEMMs (0x61-0x63; :8329-9139) ------------------------------------
+ * kind 0 = igemm (s8 x s8), 1 = ugemm (u8 x u8), 2 = usgemm (u8 x s8);
+ * C = RN(cvt(acc) * alpha), acc seeded with the bits of RN(beta*C) when beta != 0. */
+void ane_ref_int_gemm(int kind, uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
+                      uint32_t ldc, float alpha, float beta, const uint8_t* A, const uint8_t* B, float* C);
+
 /* ---- Q8_0 MUL_MAT for NT activation rows (config 5 at batch 16) --------------------
  * No reference handler: the reference's ggml backend runs MUL_MAT Q8_0 as one
  * q8_0_gemv (src/ggml-backend/ggml-ane.cpp:137-143).  Per (activation row t,

@@ -1,0 +1,101 @@
+"""dense_u8s8 (0x1E) and the integer CBLAS GEMMs (0x61 cblas_igemm, 0x62
+cblas_ugemm, 0x63 cblas_usgemm) on the GPU, bit-exact against the oracle,
+through the device entry point, the host entry point and stream_exec."""
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+F32 = np.float32
+
+
+def _layout(M, N, K, ta, tb, pad, rng):
+    lda = (M if ta else K) + pad
+    ldb = (K if tb else N) + pad
+    A = rng.integers(0, 256, ((K if ta else M) * lda,), dtype=np.uint8)
+    B = rng.integers(0, 256, ((N if tb else K) * ldb,), dtype=np.uint8)
+    return A, B, lda, ldb
+
+
+@pytest.mark.parametrize("kind", ["igemm", "ugemm", "usgemm"])
+@pytest.mark.parametrize("M,N,K", [(16, 32, 64), (100, 77, 192), (300, 260, 256), (129, 513, 1024)])
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
+def test_int_gemm_device_exact(ane, kind, M, N, K, ta, tb):
+    import torch
+
+    rng = np.random.default_rng(M * 7 + N + K + ta * 2 + tb)
+    A, B, lda, ldb = _layout(M, N, K, ta, tb, 16, rng)
+    ldc = N + 3
+    for beta in (0.0, 0.75):
+        C0 = rng.standard_normal(M * ldc).astype(F32)
+        ref = C0.copy()
+        oracle.int_gemm(kind, ta | (tb << 1), M, N, K, lda, ldb, ldc, np.float32(1.25), np.float32(beta), A, B, ref)
+        Cd = torch.from_numpy(C0.copy()).cuda()
+        ane.cblas_int_gemm(kind, torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), Cd, M, N, K, lda, ldb, ldc,
+                           1.25, beta, bool(ta), bool(tb))
+        torch.cuda.synchronize()
+        assert np.array_equal(Cd.cpu().numpy().view(np.uint32), ref.view(np.uint32)), (kind, beta)
+
+
+def test_int_gemm_host_and_stream_exec(ane, kats):
+    """The reference KAT (test_remaining_ops.cpp:131-184) through the synchronous
+    host entry point and an ane::dispatch byte stream."""
+    A, B = kats["igemm_A"], kats["igemm_B"]
+    M, K = A.shape
+    N = B.shape[1]
+    C = np.zeros((M, N), F32)
+    ane.check(ane.lib.ane_cblas_igemm(0, M, N, K, K, N, N, 0.5, 0.0, A.ctypes.data, B.ctypes.data, C.ctypes.data))
+    assert np.array_equal(C, kats["igemm_ref_alpha05"])
+    C2 = np.zeros((M, N), F32)
+    ane.dispatch(ane.Op.cblas_igemm, ane.U8(0), ane.U32(M), ane.U32(N), ane.U32(K), ane.U32(K), ane.U32(N),
+                 ane.U32(N), ane.F32(1.0), ane.F32(0.0), ane.Ptr(A.ctypes.data), ane.Ptr(B.ctypes.data),
+                 ane.Ptr(C2.ctypes.data))
+    assert ane.lib.ane_last_error() == 0
+    assert np.array_equal(C2, kats["igemm_ref_alpha1"])
+    # ugemm / usgemm through stream_exec with transposes
+    rng = np.random.default_rng(3)
+    for op, kind in ((ane.Op.cblas_ugemm, "ugemm"), (ane.Op.cblas_usgemm, "usgemm")):
+        Au, Bu, lda, ldb = _layout(40, 24, 128, 1, 1, 0, rng)
+        Cu = np.zeros(40 * 24, F32)
+        ref = Cu.copy()
+        oracle.int_gemm(kind, 3, 40, 24, 128, lda, ldb, 24, np.float32(2.0), np.float32(0.0), Au, Bu, ref)
+        ane.dispatch(op, ane.U8(3), ane.U32(40), ane.U32(24), ane.U32(128), ane.U32(lda), ane.U32(ldb), ane.U32(24),
+                     ane.F32(2.0), ane.F32(0.0), ane.Ptr(Au.ctypes.data), ane.Ptr(Bu.ctypes.data),
+                     ane.Ptr(Cu.ctypes.data))
+        assert ane.lib.ane_last_error() == 0
+        assert np.array_equal(Cu, ref), kind
+
+
+def test_int_gemm_rejects_k_not_multiple_of_64(ane):
+    A = np.zeros(16 * 48, np.uint8)
+    B = np.zeros(48 * 16, np.uint8)
+    C = np.zeros(16 * 16, F32)
+    rc = ane.lib.ane_cblas_igemm(0, 16, 16, 48, 48, 16, 16, 1.0, 0.0, A.ctypes.data, B.ctypes.data, C.ctypes.data)
+    assert rc == 1  # ANE_ERR_INVALID_ARGUMENT (the reference requires K % 64 == 0)
+
+
+@pytest.mark.parametrize("M,N,K,relu", [(50, 128, 784, True), (300, 200, 1000, False), (16, 16, 64, True)])
+def test_dense_u8s8_exact(ane, M, N, K, relu):
+    """MNIST layer 1 (test_mnist_i8.cpp:304-307 runs it as dense_u8s8) and ragged
+    shapes: host entry point and stream_exec, padded rows included."""
+    rng = np.random.default_rng(M + N + K)
+    K64 = (K + 63) // 64 * 64
+    M16 = (M + 15) // 16 * 16
+    A = np.zeros((M16, K64), np.uint8)
+    A[:M, :K] = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(-127, 128, (K64, N)).astype(np.int8)
+    B[K:] = 0
+    bias = rng.standard_normal((N + 31) // 32 * 32).astype(F32)
+    Bp = oracle.pack_b_i8(B, K64, N)
+    ref = oracle.dense_u8s8(M, N, K, 0.013, 0.021, int(relu), A, Bp, bias)
+    C = np.empty((M16, N), F32)
+    ane.check(ane.lib.ane_dense_u8s8(M, N, K, 0.013, 0.021, int(relu), A.ctypes.data, Bp.ctypes.data,
+                                     bias.ctypes.data, C.ctypes.data))
+    assert np.array_equal(C.view(np.uint32), ref.view(np.uint32))
+    C2 = np.empty((M16, N), F32)
+    ane.dispatch(ane.Op.dense_u8s8, ane.U32(M), ane.U32(N), ane.U32(K), ane.F32(0.013), ane.F32(0.021),
+                 ane.U8(int(relu)), ane.Ptr(A.ctypes.data), ane.Ptr(Bp.ctypes.data), ane.Ptr(bias.ctypes.data),
+                 ane.Ptr(C2.ctypes.data))
+    assert ane.lib.ane_last_error() == 0
+    assert np.array_equal(C2.view(np.uint32), ref.view(np.uint32))

@@ -22,6 +22,68 @@ def test_igemm_exact_kat(kats):
     assert np.array_equal(acc, ref)
 
 
+def test_cblas_igemm_oracle_kat(kats):
+    """The KAT through the integer CBLAS GEMM (opcode 0x61) in all four transpose
+    layouts, alpha 1 and 0.5 (test_remaining_ops.cpp:131-184)."""
+    A, B = kats["igemm_A"], kats["igemm_B"]
+    M, K = A.shape
+    N = B.shape[1]
+    for alpha, ref in ((1.0, kats["igemm_ref_alpha1"]), (0.5, kats["igemm_ref_alpha05"])):
+        for ta in (0, 1):
+            for tb in (0, 1):
+                Aop = np.ascontiguousarray(A.T if ta else A)
+                Bop = np.ascontiguousarray(B.T if tb else B)
+                C = np.full(M * N, 7.0, F32)
+                oracle.int_gemm("igemm", ta | (tb << 1), M, N, K, Aop.shape[1], Bop.shape[1], N, alpha, 0.0,
+                                Aop.view(np.uint8), Bop.view(np.uint8), C)
+                assert np.array_equal(C.reshape(M, N), ref), (alpha, ta, tb)
+
+
+def test_int_gemm_oracle_numpy_restatement():
+    """ugemm / usgemm (uint32 / int32 conversion) and the beta != 0 accumulator
+    seeding, against an independent numpy restatement; strided ldc."""
+    rng = np.random.default_rng(5)
+    M, N, K, ldc = 20, 37, 128, 40
+    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(0, 256, (K, N), dtype=np.uint8)
+    for kind in ("igemm", "ugemm", "usgemm"):
+        for beta in (0.0, 0.75):
+            C0 = rng.standard_normal(M * ldc).astype(F32)
+            C = C0.copy()
+            oracle.int_gemm(kind, 0, M, N, K, K, N, ldc, np.float32(1.25), np.float32(beta), A, B, C)
+            a = A.astype(np.int64) if kind != "igemm" else A.view(np.int8).astype(np.int64)
+            b = B.astype(np.int64) if kind == "ugemm" else B.view(np.int8).astype(np.int64)
+            acc = (a @ b) & 0xFFFFFFFF
+            cin = C0.reshape(M, ldc)[:, :N]
+            if beta != 0.0:
+                seed = (cin * np.float32(beta)).astype(F32).view(np.uint32).astype(np.int64)
+                acc = (acc + seed) & 0xFFFFFFFF
+            acc = acc.astype(np.uint32)
+            f = acc.astype(np.float32) if kind == "ugemm" else acc.view(np.int32).astype(np.float32)
+            ref = (f * np.float32(1.25)).astype(F32)
+            got = C.reshape(M, ldc)
+            assert np.array_equal(got[:, :N], ref), (kind, beta)
+            assert np.array_equal(got[:, N:], C0.reshape(M, ldc)[:, N:])  # columns past N untouched
+
+
+def test_dense_u8s8_oracle_matches_widened_dense_i8():
+    """dense_u8s8 = dense_i8 with unsigned A: exact int sums, same epilogue."""
+    rng = np.random.default_rng(6)
+    M, N, K = 50, 128, 784
+    K64 = (K + 63) // 64 * 64
+    M16 = (M + 15) // 16 * 16
+    A = np.zeros((M16, K64), np.uint8)
+    A[:M, :K] = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(-127, 128, (K64, N)).astype(np.int8)
+    B[K:] = 0
+    bias = rng.standard_normal(N).astype(F32)
+    Bp = oracle.pack_b_i8(B, K64, N)
+    C = oracle.dense_u8s8(M, N, K, 0.01, 0.02, 1, A, Bp, bias)
+    acc = (A.astype(np.int64) @ B.astype(np.int64)).astype(np.float32)
+    y = (acc * np.float32(np.float32(0.01) * np.float32(0.02))).astype(F32) + bias
+    assert np.array_equal(C, np.maximum(y, F32(0)) + F32(0))
+
+
 def test_igemm_via_pack_and_dense_i8(kats):
     """The same KAT through pack_b_i8 + dense_i8 (sa=sb=1, zero bias)."""
     A, B, ref = kats["igemm_A"], kats["igemm_B"], kats["igemm_ref_alpha1"]
