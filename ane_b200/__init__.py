@@ -51,6 +51,8 @@ SIGNATURES = {
     "ane_quantize_fp32_i8_channelwise": (_i32, [_u32, _u32, _vp, _vp, _vp]),
     "ane_dense_i8": (_i32, [_u32, _u32, _u32, _f, _f, _u8, _vp, _vp, _vp, _vp]),
     "ane_dense_u8s8": (_i32, [_u32, _u32, _u32, _f, _f, _u8, _vp, _vp, _vp, _vp]),
+    "ane_get_rows_q8_0": (_i32, [_u32, _u32, _vp, _vp, _vp]),
+    "ane_get_rows_q8_0_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
     "ane_cblas_igemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
     "ane_cblas_ugemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
     "ane_cblas_usgemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),

@@ -459,6 +459,15 @@ int ane_cblas_int_gemm_dev(int kind, uint8_t flags, uint32_t M, uint32_t N, uint
     return rc ? rc : ok();
 }
 
+int ane_get_rows_q8_0_dev(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out,
+                          void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(n_rows == 0 || dim == 0 || (table && indices && out), "get_rows_q8_0: NULL pointer");
+    int rc = launch_get_rows_q8_0(n_rows, dim, static_cast<const uint8_t*>(table), indices, out,
+                                  static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
 int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
     return ane_q8_0_gemv_ex_dev(M, K, in, W, out, 0, stream);
 }
@@ -734,6 +743,29 @@ int ane_cblas_ugemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t 
 int ane_cblas_usgemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
                      float alpha, float beta, const void* A, const void* B, float* C) {
     return int_gemm_host(2, flags, M, N, K, lda, ldb, ldc, alpha, beta, A, B, C);
+}
+
+int ane_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(dim % 32 == 0, "get_rows_q8_0: dim must be a multiple of 32");
+    if (n_rows == 0 || dim == 0) return ok();
+    ANE_ARG_CHECK(table && indices && out, "get_rows_q8_0: NULL pointer");
+    // the table has no size in the reference's encoding: copy rows up to the largest index
+    uint32_t max_idx = 0;
+    if (device_accessible(indices) && !device_accessible(table)) {
+        set_status(ANE_ERR_INVALID_ARGUMENT, "get_rows_q8_0: host table with device indices");
+        return ANE_ERR_INVALID_ARGUMENT;
+    }
+    if (!device_accessible(table))
+        for (uint32_t r = 0; r < n_rows; r++) max_idx = indices[r] > max_idx ? indices[r] : max_idx;
+    const size_t row_bytes = (size_t)(dim / 32) * 34;
+    std::vector<Arg> args = {{table, device_accessible(table) ? 1 : ((size_t)max_idx + 1) * row_bytes, true, false},
+                             {indices, (size_t)n_rows * 4, true, false},
+                             {out, (size_t)n_rows * dim * 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_get_rows_q8_0(n_rows, dim, (const uint8_t*)args[0].dev, (const uint32_t*)args[1].dev,
+                                    (float*)args[2].dev, s);
+    });
 }
 
 int ane_dense_fused_i8(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t relu, const float* A,

@@ -182,6 +182,30 @@ __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, co
 
 }  // namespace
 
+// get_rows_q8_0 (0x7C; src/bytecode_interpreter.s:12355-12408): out[r][32b+j] =
+// float(q_j) * float(d) of block b of table row indices[r] (one RN multiply).
+// One warp per 32-element block, lane j = element j.
+__global__ void get_rows_q8_0_kernel(uint32_t n_rows, uint32_t nb, const uint8_t* __restrict__ table,
+                                     const uint32_t* __restrict__ indices, float* __restrict__ out) {
+    const size_t w = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    if (w >= (size_t)n_rows * nb) return;
+    const uint32_t r = (uint32_t)(w / nb), b = (uint32_t)(w % nb);
+    const uint8_t* blk = table + ((size_t)indices[r] * nb + b) * 34;
+    const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+    out[(size_t)r * nb * 32 + (size_t)b * 32 + lane] = __fmul_rn((float)(int8_t)blk[2 + lane], d);
+}
+
+int launch_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const uint8_t* table, const uint32_t* indices, float* out,
+                         cudaStream_t s) {
+    ANE_ARG_CHECK(dim % 32 == 0, "get_rows_q8_0: dim must be a multiple of 32");
+    const size_t warps = (size_t)n_rows * (dim / 32);
+    if (warps == 0) return ANE_OK;
+    get_rows_q8_0_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(n_rows, dim / 32, table, indices, out);
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
+
 int launch_quantize_q8_0(uint32_t K, const float* x, uint8_t* out, cudaStream_t s) {
     ANE_ARG_CHECK(K % 32 == 0, "quantize_q8_0: K must be a multiple of 32");
     ANE_ARG_CHECK(((uintptr_t)x & 15) == 0, "quantize_q8_0: x must be 16-byte aligned");

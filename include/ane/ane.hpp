@@ -156,7 +156,7 @@ enum class Op : uint8_t {
     q6_k_gemv = 0x79,
     flash_attention_fp32 = 0x7A,
     get_rows_fp32 = 0x7B,
-    get_rows_q8_0 = 0x7C,
+    get_rows_q8_0 = 0x7C,                 // executed on the GPU
     get_rows_q4_0 = 0x7D,
     dense_strided_fp32 = 0x7E,
     advance_param_stride = 0x7F,

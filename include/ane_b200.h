@@ -88,6 +88,10 @@ int ane_cblas_ugemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t 
                     float alpha, float beta, const void* A, const void* B, float* C);
 int ane_cblas_usgemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
                      float alpha, float beta, const void* A, const void* B, float* C);
+/* get_rows_q8_0 (0x7C; :12355-12408): out[r][32b+j] = float(q) * float(d) of
+ * block b of table row indices[r] (u32 indices; dim % 32 == 0).  With a host
+ * table the rows up to the largest index are copied to the device. */
+int ane_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out);
 /* dense_fused_i8 (0x80, new; README.md:87-97 usage).  fp32 A (M x K, stride K)
  * and B (K x N, stride N) quantized per tensor to int8 (absmax/127), int8 x int8
  * -> exact int32, y = float(acc)*(sa*sb), y = y*scale, optional ReLU; C is
@@ -142,6 +146,8 @@ int ane_cblas_int_gemm_dev(int kind, uint8_t flags, uint32_t M, uint32_t N, uint
                            float* C, void* stream);
 int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out,
                       void* stream);
+int ane_get_rows_q8_0_dev(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out,
+                          void* stream);
 /* Q8_0 x Q8_0 matvec (the ggml / llama.cpp activation convention; the
  * reference's q8_0_gemv keeps x in fp32, see ane_q8_0_gemv).  x[K] is first
  * quantized to K/32 Q8_0 blocks (d = fp16(amax/127), q = roundf(x/d)); the

@@ -1,6 +1,7 @@
-"""dense_u8s8 (0x1E) and the integer CBLAS GEMMs (0x61 cblas_igemm, 0x62
-cblas_ugemm, 0x63 cblas_usgemm) on the GPU, bit-exact against the oracle,
-through the device entry point, the host entry point and stream_exec."""
+"""dense_u8s8 (0x1E), the integer CBLAS GEMMs (0x61 cblas_igemm, 0x62
+cblas_ugemm, 0x63 cblas_usgemm) and get_rows_q8_0 (0x7C) on the GPU, bit-exact
+against the oracle, through the device entry point, the host entry point and
+stream_exec."""
 import numpy as np
 import pytest
 
@@ -99,3 +100,40 @@ def test_dense_u8s8_exact(ane, M, N, K, relu):
                  ane.Ptr(C2.ctypes.data))
     assert ane.lib.ane_last_error() == 0
     assert np.array_equal(C2.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("dim", [32, 64])
+def test_get_rows_q8_0_kat(ane, kats, dim):
+    """get_rows_q8_0 (0x7C) on the reference's Q8_0 tables
+    (test_remaining_ops.cpp:230-325): host entry point and stream_exec equal the
+    oracle bit for bit and the reference's expected values within its bound."""
+    table = np.ascontiguousarray(kats[f"q8rows{dim}_table"]).astype(np.uint8)
+    idx = np.ascontiguousarray(kats["q8rows_idx"]).astype(np.uint32)
+    ref = oracle.get_rows_q8_0(table, idx, dim)
+    out = np.empty(idx.size * dim, F32)
+    ane.check(ane.lib.ane_get_rows_q8_0(idx.size, dim, table.ctypes.data, idx.ctypes.data, out.ctypes.data))
+    assert np.array_equal(out.view(np.uint32), np.asarray(ref, F32).ravel().view(np.uint32))
+    assert np.max(np.abs(out.reshape(idx.size, dim) - kats[f"q8rows{dim}_ref"])) <= kats["q8rows_tol"]
+    out2 = np.empty_like(out)
+    ane.dispatch(ane.Op.get_rows_q8_0, ane.U32(idx.size), ane.U32(dim), ane.Ptr(table.ctypes.data),
+                 ane.Ptr(idx.ctypes.data), ane.Ptr(out2.ctypes.data))
+    assert ane.lib.ane_last_error() == 0
+    assert np.array_equal(out2, out)
+
+
+def test_get_rows_q8_0_device_large(ane):
+    """Device entry point: 4096 random row lookups from a 32000 x 4096 Q8_0 table
+    (a 7B embedding shape), repeated and out-of-order indices."""
+    import torch
+
+    rows, dim, n = 32000, 4096, 4096
+    g = torch.Generator(device="cuda").manual_seed(9)
+    table = torch.randint(0, 256, (rows * (dim // 32) * 34,), dtype=torch.uint8, device="cuda", generator=g)
+    table.view(-1, 34)[:, 1] = 0x1C  # finite fp16 scales
+    idx = torch.randint(0, rows, (n,), dtype=torch.int32, device="cuda", generator=g)
+    idx[:8] = idx[0]
+    out = torch.empty(n * dim, dtype=torch.float32, device="cuda")
+    ane.check(ane.lib.ane_get_rows_q8_0_dev(n, dim, table.data_ptr(), idx.data_ptr(), out.data_ptr(), None))
+    torch.cuda.synchronize()
+    ref = oracle.get_rows_q8_0(table.cpu().numpy(), idx.cpu().numpy().astype(np.uint32), dim)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), np.asarray(ref, F32).ravel().view(np.uint32))
