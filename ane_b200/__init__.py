@@ -52,6 +52,9 @@ SIGNATURES = {
     "ane_dense_i8": (_i32, [_u32, _u32, _u32, _f, _f, _u8, _vp, _vp, _vp, _vp]),
     "ane_dense_u8s8": (_i32, [_u32, _u32, _u32, _f, _f, _u8, _vp, _vp, _vp, _vp]),
     "ane_get_rows_q8_0": (_i32, [_u32, _u32, _vp, _vp, _vp]),
+    "ane_q4_0_gemv": (_i32, [_u32, _u32, _vp, _vp, _vp]),
+    "ane_q4_0_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
+    "ane_q4_0_gemv_ex_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _u32, _vp]),
     "ane_get_rows_q8_0_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
     "ane_cblas_igemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
     "ane_cblas_ugemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
@@ -362,6 +365,16 @@ def mul_mat_q8_0_batch(W, x, M: int, K: int, out=None, workspace=None, stream=No
     check(_lib.ane_mul_mat_q8_0_batch_dev(M, K, NT, x.data_ptr(), x.stride(0), W.data_ptr(), out.data_ptr(),
                                           out.stride(0), workspace.data_ptr(), WEIGHTS_STATIC if static_weights else 0,
                                           _stream_ptr(stream)))
+    return out
+
+
+def q4_0_gemv(W, x, M: int, K: int, out=None, stream=None, static_weights=False):
+    """out[M] = Q4_0 matrix W (M rows of K/32 18-byte blocks, uint8 tensor) times fp32 x[K]."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty(M, dtype=torch.float32, device=x.device)
+    check(_lib.ane_q4_0_gemv_ex_dev(M, K, x.data_ptr(), W.data_ptr(), out.data_ptr(),
+                                    WEIGHTS_STATIC if static_weights else 0, _stream_ptr(stream)))
     return out
 
 

@@ -230,6 +230,8 @@ void stack_plan_free(void* plan);
 // ggml MUL_MAT at batch 1: fp32 x quantized to Q8_0 inside the matvec.
 int launch_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const uint8_t* table, const uint32_t* indices, float* out,
                          cudaStream_t s);
+int launch_q4_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, uint32_t flags,
+                     cudaStream_t s);
 int launch_mul_mat_q8_0(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, int32_t* block_dots,
                         uint32_t flags, cudaStream_t s);
 // ggml MUL_MAT for NT <= 16 activation rows (q8_0_gemm_q8.cu); the workspace

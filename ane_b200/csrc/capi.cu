@@ -468,6 +468,18 @@ int ane_get_rows_q8_0_dev(uint32_t n_rows, uint32_t dim, const void* table, cons
     return rc ? rc : ok();
 }
 
+int ane_q4_0_gemv_ex_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, uint32_t flags,
+                         void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK((flags & ~ANE_Q8_WEIGHTS_STATIC) == 0, "q4_0_gemv: unknown flag bits");
+    int rc = launch_q4_0_gemv(M, K, in, static_cast<const uint8_t*>(W), out, flags, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+int ane_q4_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
+    return ane_q4_0_gemv_ex_dev(M, K, in, W, out, 0, stream);
+}
+
 int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
     return ane_q8_0_gemv_ex_dev(M, K, in, W, out, 0, stream);
 }
@@ -743,6 +755,19 @@ int ane_cblas_ugemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t 
 int ane_cblas_usgemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
                      float alpha, float beta, const void* A, const void* B, float* C) {
     return int_gemm_host(2, flags, M, N, K, lda, ldb, ldc, alpha, beta, A, B, C);
+}
+
+int ane_q4_0_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out) {
+    ANE_REQUIRE_GPU();
+    if (M == 0) return ok();
+    ANE_ARG_CHECK(K % 32 == 0, "q4_0_gemv: K must be a multiple of 32");
+    ANE_ARG_CHECK(in && W && out, "q4_0_gemv: NULL pointer");
+    std::vector<Arg> args = {{in, (size_t)K * 4, true, false},
+                             {W, (size_t)M * (K / 32) * 18, true, false},
+                             {out, (size_t)M * 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_q4_0_gemv(M, K, (const float*)args[0].dev, (const uint8_t*)args[1].dev, (float*)args[2].dev, 0, s);
+    });
 }
 
 int ane_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out) {

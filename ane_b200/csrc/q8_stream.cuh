@@ -37,7 +37,10 @@ struct Q8Plan {
 // With programmatic dependent launch the next matvec's CTAs start their
 // prologue while this grid drains (see the budget below).  ANE_Q8_WARPS /
 // ANE_Q8_SLOTS / ANE_Q8_CPS (CTAs per SM) override the choice (tuning aids).
-inline Q8Plan plan_q8_stream(uint32_t M, uint32_t K, size_t extra_slot_bytes, size_t fixed_bytes) {
+// block_bytes / warp_tile_bytes: 34 / 2176 for Q8_0; 18 / 1152 for Q4_0 (same
+// 4 rows x 16 blocks per warp tile).
+inline Q8Plan plan_q8_stream(uint32_t M, uint32_t K, size_t extra_slot_bytes, size_t fixed_bytes,
+                             uint32_t block_bytes = 34, uint32_t warp_tile_bytes = kQ8WarpTileBytes) {
     static const int force_warps = env_int("ANE_Q8_WARPS"), force_slots = env_int("ANE_Q8_SLOTS"),
                      force_cps = env_int("ANE_Q8_CPS");
     const uint32_t sms = (uint32_t)num_sms();
@@ -48,7 +51,7 @@ inline Q8Plan plan_q8_stream(uint32_t M, uint32_t K, size_t extra_slot_bytes, si
     // the next grid's CTA beside it.  Larger ones: at least two CTAs per SM
     // (finer-grained hand-over between grids) and the whole shared memory for
     // the rings (more bytes in flight per SM).
-    const double sm_bytes = (double)M * (K / 32) * 34 / sms;
+    const double sm_bytes = (double)M * (K / 32) * block_bytes / sms;
     uint32_t cps = (per_sm + kQ8MaxWarps - 1) / kQ8MaxWarps;
     if (sm_bytes > 160.0 * 1024 && cps < 2 && per_sm >= 2) cps = 2;
     if (force_cps > 0) cps = (uint32_t)force_cps;
@@ -62,7 +65,7 @@ inline Q8Plan plan_q8_stream(uint32_t M, uint32_t K, size_t extra_slot_bytes, si
     if (p.ctas == 0) p.ctas = 1;
     p.warps = (p.groups + p.ctas - 1) / p.ctas;
     if (p.warps > kQ8MaxWarps) p.warps = kQ8MaxWarps;  // the CTA then streams several passes
-    p.slot_bytes = (size_t)p.warps * kQ8WarpTileBytes + extra_slot_bytes;
+    p.slot_bytes = (size_t)p.warps * warp_tile_bytes + extra_slot_bytes;
     // With one CTA per SM, the next grid's CTAs fit beside this grid's, one per
     // SM, so they are placed evenly; with more, a reserved spare would be filled
     // unevenly as CTAs finish, so the rings take the whole share instead.

@@ -50,6 +50,7 @@ int payload_size(uint8_t op) {
         case 0x62:                          //   flags M N K lda ldb ldc alpha beta A B C
         case 0x63: return 1 + 12 + 12 + 8 + 24;
         case 0x57: return 8 + 24;           // q8_0_gemv: M K in W out
+        case 0x58: return 8 + 24;           // q4_0_gemv: M K in W out
         case 0x7C: return 8 + 24;           // get_rows_q8_0: n_rows dim table indices out
         case 0x80: return 12 + 4 + 1 + 24;  // dense_fused_i8: M N K scale relu A B C
         default: return -1;
@@ -79,6 +80,13 @@ int exec_one(uint8_t op, Reader& r) {
             const float* bias = r.ptr<const float>();
             float* C = r.ptr<float>();
             return ane_dense_u8s8(M, N, K, sa, sb, flags, A, Bp, bias, C);
+        }
+        case 0x58: {
+            uint32_t M = r.get<uint32_t>(), K = r.get<uint32_t>();
+            const float* in = r.ptr<const float>();
+            const void* W = r.ptr<const void>();
+            float* out = r.ptr<float>();
+            return ane_q4_0_gemv(M, K, in, W, out);
         }
         case 0x7C: {
             uint32_t n_rows = r.get<uint32_t>(), dim = r.get<uint32_t>();

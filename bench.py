@@ -264,6 +264,24 @@ def q8_bench(ane, torch, dev, steps=50):
                 key = name + ("_static" if st else "")
                 res[key + "_gbs"] = nbytes / (ms * 1e-3) / 1e9
                 res[key + "_us"] = ms * 1e3
+        # Q4_0 (q4_0_gemv, 0x58) on the same shape: 18 B per 32 weights, static weights
+        q4bytes = rows * (cols // 32) * 18
+        q4copies = max(4, int(np.ceil(512e6 / q4bytes)))
+        W4s = [torch.randint(0, 256, (q4bytes,), dtype=torch.uint8, device=dev, generator=g) for _ in range(q4copies)]
+        for W4 in W4s:
+            W4.view(-1, 18)[:, 1] = 0x1C
+        for i in range(3):
+            ane.q4_0_gemv(W4s[i % q4copies], x, rows, cols, out=y, static_weights=True)
+        it4 = [0]
+
+        def step_q4():
+            ane.q4_0_gemv(W4s[it4[0] % q4copies], x, rows, cols, out=y, static_weights=True)
+            it4[0] += 1
+
+        ms = time_graph(step_q4, steps, stream)
+        res["q4_0_static_us"] = ms * 1e3
+        res["q4_0_static_gbs"] = (q4bytes + 4 * cols + 4 * rows) / (ms * 1e-3) / 1e9
+        del W4s
         # decode at batch 16: ggml MUL_MAT over 16 fp32 activation rows, weights read once
         xb = torch.randn((16, cols), device=dev, generator=g)
         yb = torch.empty((16, rows), device=dev)

@@ -120,7 +120,7 @@ enum class Op : uint8_t {
     rope_fp32 = 0x55,
     softmax_fp32 = 0x56,
     q8_0_gemv = 0x57,  // executed on the GPU
-    q4_0_gemv = 0x58,
+    q4_0_gemv = 0x58,                     // executed on the GPU
     fdot_zreg = 0x59,
     fmla_wide_zreg = 0x5A,
     fadd_wide_zreg = 0x5B,

@@ -88,6 +88,11 @@ int ane_cblas_ugemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t 
                     float alpha, float beta, const void* A, const void* B, float* C);
 int ane_cblas_usgemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
                      float alpha, float beta, const void* A, const void* B, float* C);
+/* q4_0_gemv (0x58; :7064-7126): W = M rows of K/32 Q4_0 blocks {fp16 d; 16
+ * bytes} (18 B, unpadded); element i < 16 = low nibble of byte i, 16+i = its
+ * high nibble, value (nibble - 8) * d; out[M].  Bit-exact with the reference's
+ * 16-lane FMA order and FADDV tree (the q8_0_gemv scheme). */
+int ane_q4_0_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out);
 /* get_rows_q8_0 (0x7C; :12355-12408): out[r][32b+j] = float(q) * float(d) of
  * block b of table row indices[r] (u32 indices; dim % 32 == 0).  With a host
  * table the rows up to the largest index are copied to the device. */
@@ -148,6 +153,10 @@ int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, fl
                       void* stream);
 int ane_get_rows_q8_0_dev(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out,
                           void* stream);
+int ane_q4_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream);
+/* flags: ANE_Q8_WEIGHTS_STATIC (W not written by the preceding kernel). */
+int ane_q4_0_gemv_ex_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, uint32_t flags,
+                         void* stream);
 /* Q8_0 x Q8_0 matvec (the ggml / llama.cpp activation convention; the
  * reference's q8_0_gemv keeps x in fp32, see ane_q8_0_gemv).  x[K] is first
  * quantized to K/32 Q8_0 blocks (d = fp16(amax/127), q = roundf(x/d)); the

@@ -59,6 +59,7 @@ def lib():
                                               _vp, _vp, _vp, _vp, _vp]),
             "ane_ref_dense_fused_epilogue": (None, [_u32, _u32, _i32p, _f, _f, _f, ctypes.c_int, _f32p]),
             "ane_ref_q8_0_gemv": (None, [_u32, _u32, _f32p, _u8p, _f32p]),
+            "ane_ref_q4_0_gemv": (None, [_u32, _u32, _f32p, _u8p, _f32p]),
             "ane_ref_quantize_q8_0": (None, [_f32p, _u8p, _sz, _sz]),
             "ane_ref_q8_0_gemv_q8": (None, [_u32, _u32, _u8p, _u8p, _f32p, _vp]),
             "ane_ref_get_rows_q8_0": (None, [_u32, _u32, _u8p, _u32p, _f32p]),
@@ -207,6 +208,12 @@ def dense_fused_i8_omp(A, B, scale=1.0, relu=False, threads=0):
 def q8_0_gemv(W_blocks, x, M: int, K: int):
     out = np.empty(M, np.float32)
     lib().ane_ref_q8_0_gemv(M, K, _c(x, np.float32).ravel(), _c(W_blocks, np.uint8).ravel(), out)
+    return out
+
+
+def q4_0_gemv(W_blocks, x, M: int, K: int):
+    out = np.empty(M, np.float32)
+    lib().ane_ref_q4_0_gemv(M, K, _c(x, np.float32).ravel(), _c(W_blocks, np.uint8).ravel(), out)
     return out
 
 

@@ -345,6 +345,33 @@ void ane_ref_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W,
     q8_0_gemv_rows(0, M, K, x, W, out);
 }
 
+/* q4_0_gemv (bytecode_interpreter.s:7064-7126): 18-byte blocks {fp16 d; 16 bytes},
+ * element i < 16 = low nibble of byte i, element 16+i = its high nibble, value
+ * (nibble - 8) * d; lane l accumulates element l then 16+l of every block, then
+ * the FADDV tree -- the q8_0_gemv scheme with another block decoder. */
+void ane_ref_q4_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out) {
+    uint32_t nb = K / 32;
+    for (uint32_t m = 0; m < M; m++) {
+        const uint8_t* row = W + (size_t)m * nb * 18;
+        float acc[16] = {0};
+        for (uint32_t b = 0; b < nb; b++) {
+            const uint8_t* blk = row + (size_t)b * 18;
+            float d = ane_ref_fp16_to_fp32((uint16_t)(blk[0] | (blk[1] << 8)));  /* ldr h0 ; fcvt */
+            const uint8_t* qs = blk + 2;
+            const float* xb = x + (size_t)b * 32;
+            for (int l = 0; l < 16; l++) {  /* low nibbles: and #0x0F ; sub 8 ; scvtf ; fmul ; fmla */
+                float dq = (float)((int32_t)(qs[l] & 0x0F) - 8) * d;
+                acc[l] = fmaf(dq, xb[l], acc[l]);
+            }
+            for (int l = 0; l < 16; l++) {  /* high nibbles: lsr #4 ; ... */
+                float dq = (float)((int32_t)(qs[l] >> 4) - 8) * d;
+                acc[l] = fmaf(dq, xb[16 + l], acc[l]);
+            }
+        }
+        out[m] = faddv16(acc);
+    }
+}
+
 void ane_ref_quantize_q8_0(const float* x, uint8_t* blocks, size_t n_rows, size_t K) {
     size_t nb = K / 32;
     for (size_t r = 0; r < n_rows; r++)

@@ -94,6 +94,11 @@ void ane_ref_dense_fused_epilogue(uint32_t M, uint32_t N, const int32_t* acc, fl
  * out[m] = FADDV(acc) (pairwise halves tree).  K % 32 == 0. */
 void ane_ref_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out);
 
+/* ---- q4_0_gemv (0x58; :7064-7126): 18-byte blocks, element i = low nibble of
+ * byte i, element 16+i = high nibble, value (nibble - 8) * d; q8_0_gemv's lane
+ * order and FADDV tree. */
+void ane_ref_q4_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out);
+
 /* ---- Q8_0 helpers ---------------------------------------------------------------
  * Quantize fp32 rows into Q8_0 blocks with the ggml rule: d = absmax/127,
  * stored as fp16(d); q = round-half-away(x * (1/d)) (0 when d == 0). */

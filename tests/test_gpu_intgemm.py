@@ -1,7 +1,7 @@
 """dense_u8s8 (0x1E), the integer CBLAS GEMMs (0x61 cblas_igemm, 0x62
-cblas_ugemm, 0x63 cblas_usgemm) and get_rows_q8_0 (0x7C) on the GPU, bit-exact
-against the oracle, through the device entry point, the host entry point and
-stream_exec."""
+cblas_ugemm, 0x63 cblas_usgemm), get_rows_q8_0 (0x7C) and q4_0_gemv (0x58) on
+the GPU, bit-exact against the oracle, through the device entry point, the host
+entry point and stream_exec."""
 import numpy as np
 import pytest
 
@@ -137,3 +137,51 @@ def test_get_rows_q8_0_device_large(ane):
     torch.cuda.synchronize()
     ref = oracle.get_rows_q8_0(table.cpu().numpy(), idx.cpu().numpy().astype(np.uint32), dim)
     assert np.array_equal(out.cpu().numpy().view(np.uint32), np.asarray(ref, F32).ravel().view(np.uint32))
+
+
+def _q4_weights(M, K, rng):
+    W = rng.integers(0, 256, (M * (K // 32), 18), dtype=np.uint8)
+    W[:, 0:2] = np.frombuffer((rng.standard_normal(M * (K // 32)) * 0.01).astype(np.float16).tobytes(),
+                              np.uint8).reshape(-1, 2)
+    return W
+
+
+@pytest.mark.parametrize("M,K", [(4096, 4096), (11008, 4096), (4096, 11008), (333, 768), (64, 96), (5, 32)])
+def test_q4_0_gemv_exact(ane, M, K):
+    """q4_0_gemv (0x58): the streamed kernel (K % 256 == 0; K = 768 and 11008 end
+    on a half chunk) and the generic kernel (K = 96, 32), bit-exact."""
+    import torch
+
+    rng = np.random.default_rng(M + K)
+    W = _q4_weights(M, K, rng)
+    x = rng.standard_normal(K).astype(F32)
+    ref = oracle.q4_0_gemv(W, x, M, K)
+    Wd, xd = torch.from_numpy(W.ravel()).cuda(), torch.from_numpy(x).cuda()
+    for st in (False, True):
+        y = ane.q4_0_gemv(Wd, xd, M, K, static_weights=st)
+        assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32)), st
+
+
+def test_q4_0_gemv_special_scales_host_and_stream_exec(ane):
+    """inf / NaN / zero / subnormal fp16 scales (the non-finite rows take the
+    replay path) through the host entry point and an ane::dispatch stream."""
+    rng = np.random.default_rng(4)
+    M, K = 96, 512
+    W = _q4_weights(M, K, rng).reshape(M, K // 32, 18)
+    for row, blk, val in ((1, 0, np.inf), (2, 3, -np.inf), (3, 5, np.nan), (4, 1, 0.0), (5, 2, 6e-8)):
+        W[row, blk, 0:2] = np.frombuffer(np.float16(val).tobytes(), np.uint8)
+    W[6, 4, 2:] = 0x88  # every nibble 8: value 0, times inf below
+    W[6, 4, 0:2] = np.frombuffer(np.float16(np.inf).tobytes(), np.uint8)
+    W = np.ascontiguousarray(W.ravel())
+    x = rng.standard_normal(K).astype(F32)
+    ref = oracle.q4_0_gemv(W, x, M, K)
+    out = np.empty(M, F32)
+    ane.check(ane.lib.ane_q4_0_gemv(M, K, x.ctypes.data, W.ctypes.data, out.ctypes.data))
+    nan = np.isnan(ref)
+    assert np.array_equal(np.isnan(out), nan) and np.array_equal(out[~nan].view(np.uint32), ref[~nan].view(np.uint32))
+    out2 = np.empty(M, F32)
+    ane.dispatch(ane.Op.q4_0_gemv, ane.U32(M), ane.U32(K), ane.Ptr(x.ctypes.data), ane.Ptr(W.ctypes.data),
+                 ane.Ptr(out2.ctypes.data))
+    assert ane.lib.ane_last_error() == 0
+    assert np.array_equal(np.isnan(out2), nan) and np.array_equal(out2[~nan].view(np.uint32),
+                                                                   ref[~nan].view(np.uint32))
