@@ -53,6 +53,18 @@ SIGNATURES = {
     "ane_dense_u8s8": (_i32, [_u32, _u32, _u32, _f, _f, _u8, _vp, _vp, _vp, _vp]),
     "ane_get_rows_q8_0": (_i32, [_u32, _u32, _vp, _vp, _vp]),
     "ane_q4_0_gemv": (_i32, [_u32, _u32, _vp, _vp, _vp]),
+    "ane_elementwise_scaled_add_fp32": (_i32, [_u32, _f, _vp, _vp, _vp]),
+    "ane_relu_backward_fp32": (_i32, [_u32, _vp, _vp, _vp]),
+    "ane_transpose_fp32": (_i32, [_u32, _u32, _vp, _vp]),
+    "ane_softmax_argmax_fp32": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _vp]),
+    "ane_dense_fp32": (_i32, [_u32, _u32, _u32, _f, _u8, _vp, _vp, _vp, _vp]),
+    "ane_count_matches": (_i32, [_u32, _vp, _vp, _vp]),
+    "ane_elementwise_scaled_add_fp32_dev": (_i32, [_u32, _f, _vp, _vp, _vp, _vp]),
+    "ane_relu_backward_fp32_dev": (_i32, [_u32, _vp, _vp, _vp, _vp]),
+    "ane_transpose_fp32_dev": (_i32, [_u32, _u32, _vp, _vp, _vp]),
+    "ane_count_matches_dev": (_i32, [_u32, _vp, _vp, _vp, _vp]),
+    "ane_dense_fp32_dev": (_i32, [_u32, _u32, _u32, _f, _u8, _vp, _vp, _vp, _vp, _vp]),
+    "ane_softmax_argmax_fp32_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ane_q4_0_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
     "ane_q4_0_gemv_ex_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _u32, _vp]),
     "ane_get_rows_q8_0_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
@@ -134,6 +146,12 @@ def launch_count() -> int:
 class Op(enum.IntEnum):
     """Opcode values of the reference (include/ane/ane.hpp:47-177) + dense_fused_i8."""
     reserved_0x00 = 0x00
+    elementwise_scaled_add_fp32 = 0x0D
+    relu_backward_fp32 = 0x0F
+    transpose_fp32 = 0x11
+    softmax_argmax_fp32 = 0x12
+    dense_fp32 = 0x15
+    count_matches = 0x16
     dense_i8 = 0x18
     quantize_fp32_i8 = 0x19
     dequantize_i8_fp32 = 0x1A

@@ -232,6 +232,15 @@ int launch_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const uint8_t* table, co
                          cudaStream_t s);
 int launch_q4_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, uint32_t flags,
                      cudaStream_t s);
+// MNIST-i8 training opcodes (mnist_ops.cu)
+int launch_scaled_add_f32(uint32_t n, float scale, const float* a, const float* b, float* out, cudaStream_t s);
+int launch_relu_backward_f32(uint32_t n, const float* act, const float* grad, float* out, cudaStream_t s);
+int launch_transpose_f32(uint32_t M, uint32_t N, const float* src, float* dst, cudaStream_t s);
+int launch_count_matches(uint32_t n, const int32_t* pred, const uint8_t* labels, int32_t* out, cudaStream_t s);
+int launch_dense_f32(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t flags, const float* A, const float* B,
+                     const float* bias, float* C, cudaStream_t s);
+int launch_softmax_argmax_f32(uint32_t batch, uint32_t cols, const float* logits, float* probs,
+                              const uint8_t* labels, float* g_out, int32_t* argmax, cudaStream_t s);
 int launch_mul_mat_q8_0(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, int32_t* block_dots,
                         uint32_t flags, cudaStream_t s);
 // ggml MUL_MAT for NT <= 16 activation rows (q8_0_gemm_q8.cu); the workspace

@@ -757,6 +757,126 @@ int ane_cblas_usgemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t
     return int_gemm_host(2, flags, M, N, K, lda, ldb, ldc, alpha, beta, A, B, C);
 }
 
+// ---- MNIST-i8 training opcodes on any pointer kind
+int ane_elementwise_scaled_add_fp32(uint32_t count, float scale, const float* a, const float* b, float* out) {
+    ANE_REQUIRE_GPU();
+    if (count == 0) return ok();
+    ANE_ARG_CHECK(a && b && out, "elementwise_scaled_add_fp32: NULL pointer");
+    std::vector<Arg> args = {{a, (size_t)count * 4, true, false},
+                             {b, (size_t)count * 4, true, false},
+                             {out, (size_t)count * 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_scaled_add_f32(count, scale, (const float*)args[0].dev, (const float*)args[1].dev,
+                                     (float*)args[2].dev, s);
+    });
+}
+
+int ane_relu_backward_fp32(uint32_t count, const float* act, const float* grad, float* out) {
+    ANE_REQUIRE_GPU();
+    if (count == 0) return ok();
+    ANE_ARG_CHECK(act && grad && out, "relu_backward_fp32: NULL pointer");
+    std::vector<Arg> args = {{act, (size_t)count * 4, true, false},
+                             {grad, (size_t)count * 4, true, false},
+                             {out, (size_t)count * 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_relu_backward_f32(count, (const float*)args[0].dev, (const float*)args[1].dev,
+                                        (float*)args[2].dev, s);
+    });
+}
+
+int ane_transpose_fp32(uint32_t M, uint32_t N, const float* src, float* dst) {
+    ANE_REQUIRE_GPU();
+    if (M == 0 || N == 0) return ok();
+    ANE_ARG_CHECK(src && dst, "transpose_fp32: NULL pointer");
+    std::vector<Arg> args = {{src, (size_t)M * N * 4, true, false}, {dst, (size_t)M * N * 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_transpose_f32(M, N, (const float*)args[0].dev, (float*)args[1].dev, s);
+    });
+}
+
+int ane_count_matches(uint32_t count, const int32_t* pred, const uint8_t* labels, int32_t* out) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(out && (count == 0 || (pred && labels)), "count_matches: NULL pointer");
+    std::vector<Arg> args = {{pred, (size_t)count * 4, true, false},
+                             {labels, (size_t)count, true, false},
+                             {out, 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_count_matches(count, (const int32_t*)args[0].dev, (const uint8_t*)args[1].dev,
+                                    (int32_t*)args[2].dev, s);
+    });
+}
+
+int ane_dense_fp32(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t flags, const float* A, const float* B,
+                   const float* bias, float* C) {
+    ANE_REQUIRE_GPU();
+    if (M == 0 || N == 0) return ok();
+    ANE_ARG_CHECK(A && B && bias && C, "dense_fp32: NULL pointer");
+    const size_t M16 = round_up(M, 16);
+    std::vector<Arg> args = {{A, M16 * K * 4, true, false},
+                             {B, (size_t)K * N * 4, true, false},
+                             {bias, (size_t)N * 4, true, false},
+                             {C, M16 * N * 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_dense_f32(M, N, K, scale, flags, (const float*)args[0].dev, (const float*)args[1].dev,
+                                (const float*)args[2].dev, (float*)args[3].dev, s);
+    });
+}
+
+int ane_softmax_argmax_fp32(uint32_t batch, uint32_t cols, const float* logits, float* probs, const uint8_t* labels,
+                            float* g_out, int32_t* argmax) {
+    ANE_REQUIRE_GPU();
+    if (batch == 0) return ok();
+    ANE_ARG_CHECK(cols >= 16 && cols % 16 == 0, "softmax_argmax_fp32: cols must be a positive multiple of 16");
+    ANE_ARG_CHECK(logits && probs && labels && g_out && argmax, "softmax_argmax_fp32: NULL pointer");
+    const size_t bytes = (size_t)batch * cols * 4;
+    // only the first 16 columns of each g_out row are written: copy it in too
+    std::vector<Arg> args = {{logits, bytes, true, false},
+                             {probs, bytes, false, true},
+                             {labels, batch, true, false},
+                             {g_out, bytes, true, true},
+                             {argmax, (size_t)batch * 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_softmax_argmax_f32(batch, cols, (const float*)args[0].dev, (float*)args[1].dev,
+                                         (const uint8_t*)args[2].dev, (float*)args[3].dev, (int32_t*)args[4].dev, s);
+    });
+}
+
+// device-pointer forms, asynchronous on `stream`
+int ane_elementwise_scaled_add_fp32_dev(uint32_t count, float scale, const float* a, const float* b, float* out,
+                                        void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = launch_scaled_add_f32(count, scale, a, b, out, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+int ane_relu_backward_fp32_dev(uint32_t count, const float* act, const float* grad, float* out, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = launch_relu_backward_f32(count, act, grad, out, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+int ane_transpose_fp32_dev(uint32_t M, uint32_t N, const float* src, float* dst, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = launch_transpose_f32(M, N, src, dst, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+int ane_count_matches_dev(uint32_t count, const int32_t* pred, const uint8_t* labels, int32_t* out, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = launch_count_matches(count, pred, labels, out, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+int ane_dense_fp32_dev(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t flags, const float* A, const float* B,
+                       const float* bias, float* C, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = launch_dense_f32(M, N, K, scale, flags, A, B, bias, C, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+int ane_softmax_argmax_fp32_dev(uint32_t batch, uint32_t cols, const float* logits, float* probs,
+                                const uint8_t* labels, float* g_out, int32_t* argmax, void* stream) {
+    ANE_REQUIRE_GPU();
+    int rc = launch_softmax_argmax_f32(batch, cols, logits, probs, labels, g_out, argmax,
+                                       static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
 int ane_q4_0_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out) {
     ANE_REQUIRE_GPU();
     if (M == 0) return ok();

@@ -40,6 +40,12 @@ struct Reader {
 // Payload sizes (bytes after the opcode) of the executed opcodes.
 int payload_size(uint8_t op) {
     switch (op) {
+        case 0x0D: return 4 + 4 + 24;       // elementwise_scaled_add_fp32: count scale a b out
+        case 0x0F: return 4 + 24;           // relu_backward_fp32: count act grad out
+        case 0x11: return 8 + 16;           // transpose_fp32: M N src dst
+        case 0x12: return 8 + 40;           // softmax_argmax_fp32: batch cols logits probs labels g_out argmax
+        case 0x15: return 12 + 4 + 1 + 32;  // dense_fp32: M N K scale flags A B bias C
+        case 0x16: return 4 + 24;           // count_matches: count pred labels out
         case 0x18: return 12 + 8 + 1 + 32;  // dense_i8: M N K sa sb flags A Bp bias C
         case 0x19: return 4 + 24;           // quantize_fp32_i8: count src dst scale_out
         case 0x1A: return 4 + 4 + 16;       // dequantize_i8_fp32: count scale src dst
@@ -61,6 +67,53 @@ inline uint32_t round16(uint32_t v) { return (v + 15u) & ~15u; }
 
 int exec_one(uint8_t op, Reader& r) {
     switch (op) {
+        case 0x0D: {
+            uint32_t count = r.get<uint32_t>();
+            float scale = r.get<float>();
+            const float* a = r.ptr<const float>();
+            const float* b = r.ptr<const float>();
+            float* out = r.ptr<float>();
+            return ane_elementwise_scaled_add_fp32(count, scale, a, b, out);
+        }
+        case 0x0F: {
+            uint32_t count = r.get<uint32_t>();
+            const float* act = r.ptr<const float>();
+            const float* grad = r.ptr<const float>();
+            float* out = r.ptr<float>();
+            return ane_relu_backward_fp32(count, act, grad, out);
+        }
+        case 0x11: {
+            uint32_t M = r.get<uint32_t>(), N = r.get<uint32_t>();
+            const float* src = r.ptr<const float>();
+            float* dst = r.ptr<float>();
+            return ane_transpose_fp32(M, N, src, dst);
+        }
+        case 0x12: {
+            uint32_t batch = r.get<uint32_t>(), cols = r.get<uint32_t>();
+            const float* logits = r.ptr<const float>();
+            float* probs = r.ptr<float>();
+            const uint8_t* labels = r.ptr<const uint8_t>();
+            float* g_out = r.ptr<float>();
+            int32_t* argmax = r.ptr<int32_t>();
+            return ane_softmax_argmax_fp32(batch, cols, logits, probs, labels, g_out, argmax);
+        }
+        case 0x15: {
+            uint32_t M = r.get<uint32_t>(), N = r.get<uint32_t>(), K = r.get<uint32_t>();
+            float scale = r.get<float>();
+            uint8_t flags = r.get<uint8_t>();
+            const float* A = r.ptr<const float>();
+            const float* B = r.ptr<const float>();
+            const float* bias = r.ptr<const float>();
+            float* C = r.ptr<float>();
+            return ane_dense_fp32(M, N, K, scale, flags, A, B, bias, C);
+        }
+        case 0x16: {
+            uint32_t count = r.get<uint32_t>();
+            const int32_t* pred = r.ptr<const int32_t>();
+            const uint8_t* labels = r.ptr<const uint8_t>();
+            int32_t* out = r.ptr<int32_t>();
+            return ane_count_matches(count, pred, labels, out);
+        }
         case 0x18: {
             uint32_t M = r.get<uint32_t>(), N = r.get<uint32_t>(), K = r.get<uint32_t>();
             float sa = r.get<float>(), sb = r.get<float>();

@@ -45,16 +45,16 @@ enum class Op : uint8_t {
     load_bias = 0x0A,
     scale_store = 0x0B,
     elementwise_add_fp32 = 0x0C,
-    elementwise_scaled_add_fp32 = 0x0D,
+    elementwise_scaled_add_fp32 = 0x0D,   // executed on the GPU
     elementwise_mul_fp32 = 0x0E,
-    relu_backward_fp32 = 0x0F,
+    relu_backward_fp32 = 0x0F,            // executed on the GPU
     scatter_tile_fp32 = 0x10,
-    transpose_fp32 = 0x11,
-    softmax_argmax_fp32 = 0x12,
+    transpose_fp32 = 0x11,                // executed on the GPU
+    softmax_argmax_fp32 = 0x12,           // executed on the GPU
     luti4_op = 0x13,
     luti2_op = 0x14,
-    dense_fp32 = 0x15,
-    count_matches = 0x16,
+    dense_fp32 = 0x15,                    // executed on the GPU
+    count_matches = 0x16,                 // executed on the GPU
     reduce_sum_fp32 = 0x17,
     dense_i8 = 0x18,                      // executed on the GPU
     quantize_fp32_i8 = 0x19,              // executed on the GPU

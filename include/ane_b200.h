@@ -88,6 +88,29 @@ int ane_cblas_ugemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t 
                     float alpha, float beta, const void* A, const void* B, float* C);
 int ane_cblas_usgemm(uint8_t flags, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
                      float alpha, float beta, const void* A, const void* B, float* C);
+/* ---- the fp32 opcodes of the reference's MNIST-i8 training step
+ * (tests/test_mnist_i8.cpp:304-346), each bit-identical with its handler: */
+/* elementwise_scaled_add_fp32 (0x0D; :585-605): out = fma(b, scale, a). */
+int ane_elementwise_scaled_add_fp32(uint32_t count, float scale, const float* a, const float* b, float* out);
+/* relu_backward_fp32 (0x0F; :639-661): out = act > 0 ? grad : +0. */
+int ane_relu_backward_fp32(uint32_t count, const float* act, const float* grad, float* out);
+/* transpose_fp32 (0x11; :705-741): dst (N x M) = src (M x N)^T. */
+int ane_transpose_fp32(uint32_t M, uint32_t N, const float* src, float* dst);
+/* softmax_argmax_fp32 (0x12; :742-1007): per row of cols (a multiple of 16):
+ * probs = the handler's polynomial softmax (exp via 2^n times a degree-4
+ * polynomial, 16-lane sums, one RN division), g_out[0..15] = probs - one_hot
+ * (only the first 16 columns of a g_out row are written), argmax = first
+ * index of the maximum of the first 16 probs (15 if none compares equal). */
+int ane_softmax_argmax_fp32(uint32_t batch, uint32_t cols, const float* logits, float* probs, const uint8_t* labels,
+                            float* g_out, int32_t* argmax);
+/* dense_fp32 (0x15; :1008-1826): C = fmax(RN((bias + A @ B) * scale), relu ? 0 :
+ * -FLT_MAX), each element one fused multiply-add per k in order from bias;
+ * A is M16 x K (rows written up to M16, like dense_i8).  As in the reference,
+ * only k < (K & ~15) contribute (it runs K/16 whole blocks; row stride K). */
+int ane_dense_fp32(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t flags, const float* A, const float* B,
+                   const float* bias, float* C);
+/* count_matches (0x16; :1827-1850): *out = #{i : pred[i] == labels[i]}. */
+int ane_count_matches(uint32_t count, const int32_t* pred, const uint8_t* labels, int32_t* out);
 /* q4_0_gemv (0x58; :7064-7126): W = M rows of K/32 Q4_0 blocks {fp16 d; 16
  * bytes} (18 B, unpadded); element i < 16 = low nibble of byte i, 16+i = its
  * high nibble, value (nibble - 8) * d; out[M].  Bit-exact with the reference's
@@ -154,6 +177,15 @@ int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, fl
 int ane_get_rows_q8_0_dev(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out,
                           void* stream);
 int ane_q4_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream);
+int ane_elementwise_scaled_add_fp32_dev(uint32_t count, float scale, const float* a, const float* b, float* out,
+                                        void* stream);
+int ane_relu_backward_fp32_dev(uint32_t count, const float* act, const float* grad, float* out, void* stream);
+int ane_transpose_fp32_dev(uint32_t M, uint32_t N, const float* src, float* dst, void* stream);
+int ane_count_matches_dev(uint32_t count, const int32_t* pred, const uint8_t* labels, int32_t* out, void* stream);
+int ane_dense_fp32_dev(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t flags, const float* A, const float* B,
+                       const float* bias, float* C, void* stream);
+int ane_softmax_argmax_fp32_dev(uint32_t batch, uint32_t cols, const float* logits, float* probs,
+                                const uint8_t* labels, float* g_out, int32_t* argmax, void* stream);
 /* flags: ANE_Q8_WEIGHTS_STATIC (W not written by the preceding kernel). */
 int ane_q4_0_gemv_ex_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, uint32_t flags,
                          void* stream);

@@ -65,6 +65,12 @@ def lib():
             "ane_ref_get_rows_q8_0": (None, [_u32, _u32, _u8p, _u32p, _f32p]),
             "ane_ref_mul_mat_q8_0_batch": (None, [_u32, _u32, _u32, _u8p, _u8p, _f32p, _sz]),
             "ane_ref_dense_u8s8": (None, [_u32, _u32, _u32, _f, _f, ctypes.c_uint8, _u8p, _i8p, _f32p, _f32p]),
+            "ane_ref_elementwise_scaled_add_fp32": (None, [_u32, _f, _f32p, _f32p, _f32p]),
+            "ane_ref_relu_backward_fp32": (None, [_u32, _f32p, _f32p, _f32p]),
+            "ane_ref_transpose_fp32": (None, [_u32, _u32, _f32p, _f32p]),
+            "ane_ref_count_matches": (None, [_u32, _i32p, _u8p, _i32p]),
+            "ane_ref_dense_fp32": (None, [_u32, _u32, _u32, _f, ctypes.c_uint8, _f32p, _f32p, _f32p, _f32p]),
+            "ane_ref_softmax_argmax_fp32": (None, [_u32, _u32, _f32p, _f32p, _u8p, _f32p, _i32p]),
             "ane_ref_int_gemm": (None, [ctypes.c_int, ctypes.c_uint8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f,
                                         _u8p, _u8p, _f32p]),
             "ane_ref_dense_fused_i8_omp": (None, [_u32, _u32, _u32, _f, ctypes.c_int, _f32p, _f32p, _f32p,
@@ -257,6 +263,57 @@ def int_gemm(kind, flags, M, N, K, lda, ldb, ldc, alpha, beta, A_bytes, B_bytes,
     lib().ane_ref_int_gemm(INT_GEMM_KINDS[kind], flags, M, N, K, lda, ldb, ldc, alpha, beta,
                            _c(A_bytes, np.uint8).ravel(), _c(B_bytes, np.uint8).ravel(), C.ravel())
     return C
+
+
+def elementwise_scaled_add_fp32(scale, a, b):
+    a, b = _c(a, np.float32).ravel(), _c(b, np.float32).ravel()
+    out = np.empty_like(a)
+    lib().ane_ref_elementwise_scaled_add_fp32(a.size, scale, a, b, out)
+    return out
+
+
+def relu_backward_fp32(act, grad):
+    act, grad = _c(act, np.float32).ravel(), _c(grad, np.float32).ravel()
+    out = np.empty_like(act)
+    lib().ane_ref_relu_backward_fp32(act.size, act, grad, out)
+    return out
+
+
+def transpose_fp32(src):
+    src = _c(src, np.float32)
+    M, N = src.shape
+    dst = np.empty((N, M), np.float32)
+    lib().ane_ref_transpose_fp32(M, N, src.ravel(), dst.ravel())
+    return dst
+
+
+def count_matches(pred, labels):
+    out = np.zeros(1, np.int32)
+    pred, labels = _c(pred, np.int32).ravel(), _c(labels, np.uint8).ravel()
+    lib().ane_ref_count_matches(pred.size, pred, labels, out)
+    return int(out[0])
+
+
+def dense_fp32(M, N, K, scale, flags, A_pad, B, bias):
+    """A [M16 x K], B [K x N], bias [>= N]: C [M16 x N] (padded rows included)."""
+    M16 = (M + 15) // 16 * 16
+    C = np.empty((M16, N), np.float32)
+    lib().ane_ref_dense_fp32(M, N, K, scale, flags, _c(A_pad, np.float32).ravel(), _c(B, np.float32).ravel(),
+                             _c(bias, np.float32).ravel(), C.ravel())
+    return C
+
+
+def softmax_argmax_fp32(logits, labels, g_out=None):
+    """logits [batch x cols]; returns probs, g_out (only its first 16 columns are
+    written: pass the previous contents), argmax."""
+    logits = _c(logits, np.float32)
+    batch, cols = logits.shape
+    probs = np.empty_like(logits)
+    g = np.zeros_like(logits) if g_out is None else np.array(g_out, np.float32, copy=True)
+    am = np.empty(batch, np.int32)
+    lib().ane_ref_softmax_argmax_fp32(batch, cols, logits.ravel(), probs.ravel(), _c(labels, np.uint8).ravel(),
+                                      g.ravel(), am)
+    return probs, g, am
 
 
 def mul_mat_q8_0_batch(W_blocks, xq_blocks, M: int, K: int, NT: int):

@@ -273,6 +273,121 @@ void ane_ref_int_gemm(int kind, uint8_t flags, uint32_t M, uint32_t N, uint32_t 
         }
 }
 
+/* ------------------------------------------- MNIST-i8 training opcodes */
+
+static inline float faddv16(const float* a);
+static inline float f32_bits(uint32_t u) {
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* elementwise_scaled_add_fp32 (0x0D; :585-605): out = fma(b, scale, a) (fmla). */
+void ane_ref_elementwise_scaled_add_fp32(uint32_t count, float scale, const float* a, const float* b, float* out) {
+    for (uint32_t i = 0; i < count; i++) out[i] = fmaf(b[i], scale, a[i]);
+}
+
+/* relu_backward_fp32 (0x0F; :639-661): out = act > 0 ? grad : +0 (fcmgt; NaN -> 0). */
+void ane_ref_relu_backward_fp32(uint32_t count, const float* act, const float* grad, float* out) {
+    for (uint32_t i = 0; i < count; i++) out[i] = act[i] > 0.0f ? grad[i] : 0.0f;
+}
+
+/* transpose_fp32 (0x11; :705-741): dst[N x M] = src[M x N]^T. */
+void ane_ref_transpose_fp32(uint32_t M, uint32_t N, const float* src, float* dst) {
+    for (uint32_t i = 0; i < M; i++)
+        for (uint32_t j = 0; j < N; j++) dst[(size_t)j * M + i] = src[(size_t)i * N + j];
+}
+
+/* count_matches (0x16; :1827-1850): number of i with pred[i] == (int32)labels[i]. */
+void ane_ref_count_matches(uint32_t count, const int32_t* pred, const uint8_t* labels, int32_t* out) {
+    int32_t n = 0;
+    for (uint32_t i = 0; i < count; i++) n += pred[i] == (int32_t)labels[i];
+    *out = n;
+}
+
+/* dense_fp32 (0x15; :1008-1826): C[r][c] = fmax(RN((bias[c] + sum_k A[r][k]*B[k][c]) * scale),
+ * relu ? 0 : -FLT_MAX), the accumulator starting at bias[c] and taking one fused
+ * multiply-add per k in order (FMOPA); rows r < M16 written (not predicated),
+ * columns c < N; A row stride K, B and C row stride N.  The handler runs K/16
+ * whole k-blocks (lsr w15, w2, #4): only k < (K & ~15) contribute. */
+void ane_ref_dense_fp32(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t flags, const float* A,
+                        const float* B, const float* bias, float* C) {
+    uint32_t M16 = (M + 15) & ~15u;
+    float floor_v = (flags & 1) ? 0.0f : -FLT_MAX;
+    for (uint32_t r = 0; r < M16; r++)
+        for (uint32_t c = 0; c < N; c++) {
+            float acc = bias[c];
+            for (uint32_t k = 0; k < (K & ~15u); k++) acc = fmaf(A[(size_t)r * K + k], B[(size_t)k * N + c], acc);
+            C[(size_t)r * N + c] = ane_ref_relu_max(acc * scale, floor_v);
+        }
+}
+
+/* softmax_argmax_fp32 (0x12; :742-1007), per row of `cols` (a multiple of 16):
+ *   m = max over the row (fmax, NaN wins)
+ *   e_i = 2^n * p(f): t = RN((x_i - m) * log2e), n = floor(t), f = RN(t - n),
+ *         p = ((((c4*f + c3)*f + c2)*f + ln2)*f + 1) with every * and + rounded,
+ *         2^n built from the exponent bits of max(trunc(n), -127) (+127 << 23)
+ *   probs_i = RN(e_i * RN(1 / S)), S = FADDV over 16 lanes of the lane sums
+ *             (lane l adds e_l, e_{l+16}, ... in order)
+ *   g_out[0..15] = probs[0..15], g_out[label] -= 1 (first 16 columns only)
+ *   argmax = first index of max(probs[0..15]) among the first 16 (15 if none). */
+static float smx_exp(float x, float m) {
+    const float log2e = f32_bits(0x3FB8AA3Bu);  /* the handler's movz/movk constants */
+    const float c4 = f32_bits(0x3C1D955Au);
+    const float c3 = f32_bits(0x3D635847u);
+    const float c2 = f32_bits(0x3E75FDF0u);
+    const float c1 = f32_bits(0x3F317218u);
+    float xm = x - m;
+    float t = xm * log2e;
+    float n = floorf(t);
+    float f = t - n;
+    float p = c4 * f;
+    p = p + c3;
+    p = p * f;
+    p = p + c2;
+    p = p * f;
+    p = p + c1;
+    p = p * f;
+    p = p + 1.0f;
+    int32_t e;
+    if (n != n) e = 0;                                  /* fcvtzs: NaN -> 0 */
+    else if (n >= 2147483648.0f) e = INT32_MAX;         /* saturating */
+    else if (n < -2147483648.0f) e = INT32_MIN;
+    else e = (int32_t)n;
+    if (e < -127) e = -127;
+    uint32_t bits = (uint32_t)(e + 127) << 23;
+    float two_n;
+    memcpy(&two_n, &bits, 4);
+    return p * two_n;
+}
+
+void ane_ref_softmax_argmax_fp32(uint32_t batch, uint32_t cols, const float* logits, float* probs,
+                                 const uint8_t* labels, float* g_out, int32_t* argmax) {
+    for (uint32_t r = 0; r < batch; r++) {
+        const float* x = logits + (size_t)r * cols;
+        float* pr = probs + (size_t)r * cols;
+        float m = -INFINITY;
+        for (uint32_t i = 0; i < cols; i++) m = ane_ref_relu_max(m, x[i]) ;  /* fmax (NaN wins) */
+        float lane[16] = {0};
+        for (uint32_t i = 0; i < cols; i++) {
+            float e = smx_exp(x[i], m);
+            pr[i] = e;
+            lane[i % 16] = lane[i % 16] + e;
+        }
+        float S = faddv16(lane);
+        float inv = 1.0f / S;
+        for (uint32_t i = 0; i < cols; i++) pr[i] = pr[i] * inv;
+        float* g = g_out + (size_t)r * cols;
+        for (uint32_t i = 0; i < 16; i++) g[i] = (i == labels[r]) ? pr[i] - 1.0f : pr[i];
+        float mx = -INFINITY;
+        for (uint32_t i = 0; i < 16; i++) mx = ane_ref_relu_max(mx, i < cols ? pr[i] : -INFINITY);
+        int32_t idx = 15;
+        for (int32_t i = 15; i >= 0; i--)
+            if ((i < (int32_t)cols ? pr[i] : -INFINITY) == mx) idx = i;
+        argmax[r] = idx;
+    }
+}
+
 /* ---------------------------------------------------------- dense_fused_i8 */
 
 void ane_ref_dense_fused_epilogue(uint32_t M, uint32_t N, const int32_t* acc, float sa, float sb,

@@ -110,6 +110,16 @@ void ane_ref_quantize_q8_0(const float* x, uint8_t* blocks, size_t n_rows, size_
 void ane_ref_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8_t* W,
                           float* out, int32_t* block_dots);
 
+/* ---- MNIST-i8 training opcodes (tests/test_mnist_i8.cpp:304-346) ---------------------- */
+void ane_ref_elementwise_scaled_add_fp32(uint32_t count, float scale, const float* a, const float* b, float* out);
+void ane_ref_relu_backward_fp32(uint32_t count, const float* act, const float* grad, float* out);
+void ane_ref_transpose_fp32(uint32_t M, uint32_t N, const float* src, float* dst);
+void ane_ref_count_matches(uint32_t count, const int32_t* pred, const uint8_t* labels, int32_t* out);
+void ane_ref_dense_fp32(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t flags, const float* A,
+                        const float* B, const float* bias, float* C);
+void ane_ref_softmax_argmax_fp32(uint32_t batch, uint32_t cols, const float* logits, float* probs,
+                                 const uint8_t* labels, float* g_out, int32_t* argmax);
+
 /* ---- dense_u8s8 (0x1E; :2841-3305): dense_i8 with unsigned A ----------------------- */
 void ane_ref_dense_u8s8(uint32_t M, uint32_t N, uint32_t K, float sa, float sb, uint8_t flags,
                         const uint8_t* A, const int8_t* B_packed, const float* bias, float* C);

@@ -53,10 +53,12 @@ def test_payload_size_table_matches_encoding():
     import ane_b200
 
     L = ane_b200.lib
-    for op, n in [(0x18, 53), (0x19, 28), (0x1A, 24), (0x1B, 24), (0x1C, 32), (0x57, 32), (0x80, 41)]:
-        assert L.ane_opcode_payload_size(op) == n
+    for op, n in [(0x18, 53), (0x19, 28), (0x1A, 24), (0x1B, 24), (0x1C, 32), (0x57, 32), (0x80, 41),
+                  (0x1E, 53), (0x58, 32), (0x61, 57), (0x62, 57), (0x63, 57), (0x7C, 32),
+                  (0x0D, 32), (0x0F, 28), (0x11, 24), (0x12, 48), (0x15, 49), (0x16, 28)]:
+        assert L.ane_opcode_payload_size(op) == n, hex(op)
         assert L.ane_opcode_supported(op) == 1
-    for op in (0x01, 0x15, 0x4D, 0x7A, 0x7F, 0xFF):
+    for op in (0x01, 0x14, 0x4D, 0x7A, 0x7F, 0xFF):
         assert L.ane_opcode_supported(op) == 0
         assert L.ane_opcode_payload_size(op) == -1
 
@@ -66,14 +68,14 @@ def test_stream_exec_rejects_unsupported_and_truncated():
     from ane_b200 import U32, Op, Ptr, encode
 
     with pytest.raises(ane_b200.AneError) as e:
-        ane_b200.stream_exec(bytes([0x15]) + bytes(40))  # dense_fp32: outside the hot path
+        ane_b200.stream_exec(bytes([0x14]) + bytes(40))  # luti2_op: not executed here
     assert e.value.code == 2
     full = encode(Op.q8_0_gemv, U32(32), U32(32), Ptr(1), Ptr(2), Ptr(3))
     with pytest.raises(ane_b200.AneError) as e:
         ane_b200.stream_exec(full[:-1])
     assert e.value.code == 3
     # 0x00 ends the stream (jump-table slot 0 = exit) and an empty stream is a no-op
-    ane_b200.stream_exec(bytes([0x00]) + bytes([0x15]))
+    ane_b200.stream_exec(bytes([0x00]) + bytes([0x14]))
     ane_b200.stream_exec(b"")
 
 

@@ -314,3 +314,33 @@ def test_q8_0_gemv_lane_order_and_modes():
     assert np.array_equal(dots, ref_dots.astype(np.int32))
     del acc
     assert np.allclose(outq, out, rtol=0.05, atol=0.05)
+
+
+def test_mnist_fp32_ops_oracle_sanity():
+    """The MNIST-i8 training opcodes' restatements against numpy: exact for the
+    data movement ops, within the reference polynomial's accuracy for softmax."""
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((50, 128)).astype(F32)
+    assert np.array_equal(oracle.transpose_fp32(x), x.T)
+    g = rng.standard_normal(x.size).astype(F32)
+    assert np.array_equal(oracle.relu_backward_fp32(x, g), np.where(x.ravel() > 0, g, F32(0)))
+    pred = rng.integers(0, 10, 50).astype(np.int32)
+    lab = rng.integers(0, 10, 50).astype(np.uint8)
+    assert oracle.count_matches(pred, lab) == int((pred == lab).sum())
+    # dense_fp32: K = 50 uses only the first 48 k (the handler's whole 16-blocks)
+    A = rng.standard_normal((128, 50)).astype(F32)
+    B = rng.standard_normal((50, 16)).astype(F32)
+    bias = rng.standard_normal(16).astype(F32)
+    C = oracle.dense_fp32(128, 16, 50, 0.5, 0, A, B, bias)
+    ref = (bias.astype(np.float64) + A[:, :48].astype(np.float64) @ B[:48].astype(np.float64)) * 0.5
+    assert np.max(np.abs(C - ref)) < 1e-4
+    logits = (rng.standard_normal((50, 16)) * 4).astype(F32)
+    labels = rng.integers(0, 10, 50).astype(np.uint8)
+    probs, gout, am = oracle.softmax_argmax_fp32(logits, labels)
+    sm = np.exp(logits.astype(np.float64) - logits.max(1, keepdims=True))
+    sm /= sm.sum(1, keepdims=True)
+    assert np.max(np.abs(probs - sm)) < 2e-4
+    assert np.array_equal(am, probs.argmax(1))
+    onehot = np.zeros_like(probs)
+    onehot[np.arange(50), labels] = 1
+    assert np.array_equal(gout, (probs - onehot).astype(F32))
