@@ -10,21 +10,27 @@
 // segment sums are added from +0 in segment order.  The grouping depends on K
 // only, so results do not change with M, the row shard or the GPU count.
 //
-// Launch 1 (quantize_x_chunks_kernel): the activation rows, quantized with the
-// ggml Q8_0 rule, into one record per chunk of kChunk blocks:
-//     codes  [kChunk][16 tokens][8 words]   words of a block stored as 0,4,1,5,2,6,3,7
-//     scales [kChunk][8][2] fp32            token t at (t % 8) * 2 + t / 8
+// Launch 1 (quantize_x_segments_kernel): the activation rows, quantized with the
+// ggml Q8_0 rule, into one record per K segment of 32 blocks:
+//     codes  [32 blocks][16 tokens][8 words]   words of a block stored as 0,4,1,5,2,6,3,7
+//     scales [32 blocks][8][2] fp32            token t at (t % 8) * 2 + t / 8
 // (zero past NT) -- the layout the MMA fragments load with one 64-bit
 // shared-memory load per token and block.
-// Launch 2 (q8_0_gemm_q8_kernel): the structure of the batch-1 streaming matvec.
-// Rows are dealt to the CTAs in balanced runs of 4; a compute warp owns 8 rows
-// (or the run's last 4) over the whole of K.  One producer warp per CTA feeds a
-// ring whose stage t holds chunk t of K: the activation record (one bulk copy)
-// and every compute warp's 8 x 272 B weight tile (2-D TMA).  Per block a warp
-// runs one mma.sync m16n8k32 (s8 x s8 -> s32) -- the 16 tokens as M, its 8
-// weight rows as N -- issuing a chunk's eight products before their fp32 scale
-// math; the int32 dots become floats by an exact magic-number add.  Segment
-// sums stay in registers; nothing crosses warps or CTAs.
+// Launch 2 (q8_0_gemm_q8_kernel): rows are dealt to one CTA per SM in balanced
+// runs of 4; the CTA's rows form tiles of 8 (the run's last tile may hold 4).
+// One producer warp feeds a ring whose stage holds one K segment: the
+// activation record (one bulk copy) and each tile's 8 rows as one 2-D TMA box
+// of 138 x 8 int64 elements from the segment start (long box rows keep the TMA
+// engine at HBM rate -- 272-byte rows held it near 2 TB/s -- and the 1104-byte
+// row pitch keeps the fragment loads free of bank conflicts).  Two groups of
+// compute warps
+// take alternate segments, one warp per tile in each group.  Per block a warp
+// runs one mma.sync m16n8k32 (s8 x s8 -> s32) -- the 16 tokens as M, the tile's
+// 8 rows as N -- eight products ahead of their fp32 scale math; the int32 dots
+// become floats by an exact magic-number add.  A warp's segment sum joins the
+// row total in segment order through a per-tile shared-memory baton (one
+// mbarrier phase per segment), so the fp32 order is the contract's whatever
+// the group timing.
 #include <cuda.h>
 
 #include "ane_internal.cuh"
@@ -34,34 +40,40 @@
 namespace ane_b200 {
 namespace {
 
-constexpr uint32_t kRows = 8;                             // weight rows per compute warp (MMA N)
+constexpr uint32_t kRows = 8;                             // weight rows per tile (MMA N)
 constexpr uint32_t kSegBlocks = 32;                       // blocks per K segment (the sum grouping)
-constexpr uint32_t kChunk = 8;                            // blocks per ring stage
-constexpr uint32_t kChunkBytes = kChunk * 34;             // 272 B of a row
-constexpr uint32_t kTileBytes = kRows * kChunkBytes;      // 2176 = 17 x 128
-constexpr uint32_t kChunksPerSeg = kSegBlocks / kChunk;   // 4
+constexpr uint32_t kSegBytes = kSegBlocks * 34;           // 1088 B of a row per segment
+constexpr uint32_t kRowPitch = kSegBytes + 16;            // 276 words: rows g = 0..7 start in distinct 4-bank groups
+constexpr uint32_t kTileBytes = kRows * kRowPitch;        // 8832 = 69 x 128
 constexpr uint32_t kTok = 16;                             // activation rows per record (MMA M)
-constexpr uint32_t kXCodes = kChunk * kTok * 32;          // 4096
-constexpr uint32_t kXChunkBytes = kXCodes + kChunk * kTok * 4;  // + scales = 4608 = 36 x 128
-constexpr uint32_t kMaxWarps = 16;
+constexpr uint32_t kXCodes = kSegBlocks * kTok * 32;      // 16384
+constexpr uint32_t kXSegBytes = kXCodes + kSegBlocks * kTok * 4;  // + scales = 18432 = 144 x 128
+constexpr uint32_t kMaxTiles = 8;                         // tiles per pass (compute warps per group)
+constexpr uint32_t kMaxGroups = 2;
 constexpr uint32_t kMaxSlots = 8;
-static_assert(kTileBytes % 128 == 0 && kXChunkBytes % 128 == 0, "TMA / bulk destinations stay 128-byte aligned");
-static_assert(kSegBlocks % kChunk == 0, "a stage never straddles two segments");
+constexpr uint32_t kTotBytes = 32 * 4 * 4;                // one tile's running totals: 32 lanes x 4 floats
+constexpr uint32_t kRingOffset = 256 + kMaxTiles * kTotBytes;  // 4352 = 34 x 128
+static_assert(kTileBytes % 128 == 0 && kXSegBytes % 128 == 0 && kRingOffset % 128 == 0,
+              "TMA / bulk destinations stay 128-byte aligned");
+static_assert(kSegBytes % 16 == 0 && kRowPitch / 8 <= 256 && (kRowPitch / 4) % 8 == 4,
+              "a segment start is a 16-byte aligned TMA x; one box row of int64 elements; a row pitch of 4 mod 8 "
+              "words keeps the fragment loads free of bank conflicts");
 
 __host__ __device__ constexpr size_t round_up256(size_t v) { return (v + 255) / 256 * 256; }
 
 // ------------------------------------------------------- activation records
 // Thread i = (block b, token t): ggml Q8_0 quantization of x[t][32b..32b+31]
 // (q8_quantize_words, the arithmetic of every other Q8_0 activation path here).
-__global__ void quantize_x_chunks_kernel(const float* __restrict__ x, size_t ldx, uint32_t NT, uint32_t nb,
-                                         uint8_t* __restrict__ chunks) {
+// Blocks past nb in the last segment's record are never written nor read.
+__global__ void quantize_x_segments_kernel(const float* __restrict__ x, size_t ldx, uint32_t NT, uint32_t nb,
+                                           uint8_t* __restrict__ records) {
     ptx::griddep_launch_dependents();
     ptx::griddep_wait();  // x may come from the previous kernel; the records may still be read by it
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= nb * kTok) return;
     const uint32_t b = i / kTok, t = i % kTok;
-    const uint32_t c = b / kChunk, j = b % kChunk;
-    uint8_t* rec = chunks + (size_t)c * kXChunkBytes;
+    const uint32_t s = b / kSegBlocks, j = b % kSegBlocks;
+    uint8_t* rec = records + (size_t)s * kXSegBytes;
     uint4* codes = reinterpret_cast<uint4*>(rec + ((size_t)j * kTok + t) * 32);
     float* scale = reinterpret_cast<float*>(rec + kXCodes) + j * kTok + (t % 8) * 2 + t / 8;
     if (t >= NT) {
@@ -95,8 +107,10 @@ __device__ __forceinline__ void mma_s8_16832(const uint32_t (&a)[4], uint32_t b0
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
 }
 
-// Two IEEE fp32 products (round to nearest even) in one packed instruction.
-// Only ever followed by another multiply, so nothing can fuse it into an FMA.
+// Packed IEEE fp32 operations, round to nearest even, subnormals kept: two
+// lanes per instruction, each lane exactly the scalar operation.  Used only
+// where no product feeds a sum (products of products, sums of exact values),
+// since the assembler may contract a packed multiply and add into an FMA.
 __device__ __forceinline__ float2 fmul2_rn(float2 a, float2 b) {
     float2 d;
     asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
@@ -108,16 +122,24 @@ __device__ __forceinline__ float2 fmul2_rn(float2 a, float2 b) {
         : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
     return d;
 }
-
-// float(s) for |s| < 2^22, exactly: the bits of 1.5 * 2^23 + s, minus 1.5 * 2^23
-// (|sumi| <= 32 * 128 * 127 < 2^19).  Integer add + fp32 add, both full rate.
-__device__ __forceinline__ float i2f_exact(int32_t s) {
-    return __fsub_rn(__int_as_float(0x4B400000 + s), 12582912.0f);
+__device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
 }
 
-// acc + float(sumi) * p with p = RN(dw * dx): separate RN operations, never fused
-__device__ __forceinline__ float q8_term_add(float acc, int32_t sumi, float p) {
-    return __fadd_rn(acc, __fmul_rn(i2f_exact(sumi), p));
+// float(s0), float(s1) for |s| < 2^22, exactly: the bits of 1.5 * 2^23 + s,
+// plus -1.5 * 2^23 (|sumi| <= 32 * 128 * 127 < 2^19).  Integer adds + one
+// packed fp32 add, all full rate.
+__device__ __forceinline__ float2 i2f2_exact(int32_t s0, int32_t s1) {
+    return fadd2_rn(make_float2(__int_as_float(0x4B400000 + s0), __int_as_float(0x4B400000 + s1)),
+                    make_float2(-12582912.0f, -12582912.0f));
 }
 
 // Codes 4q..4q+3 and 16+4q..16+4q+3 of the 34-byte Q8_0 block at `blk` in the
@@ -136,82 +158,136 @@ __device__ __forceinline__ void block_words(const uint8_t* blk, uint32_t q, uint
     }
 }
 
+// One K segment of one tile: the sum from +0, in block order, of the terms of
+// blocks [0, nblk) (nblk a multiple of 8).  Thread (g, q) holds tokens g, g+8 x
+// tile rows 2q, 2q+1: seg01 = (tok g, row 2q | 2q+1), seg23 = (tok g+8, ...).
+__device__ __forceinline__ void segment_sums(const uint8_t* xs, const uint8_t* tile, uint32_t nblk, uint32_t rows,
+                                             uint32_t g, uint32_t q, float2& seg01, float2& seg23) {
+    const float* xd = reinterpret_cast<const float*>(xs + kXCodes);
+    const uint8_t* rb = tile + g * kRowPitch;         // B fragment: tile row g
+    const uint8_t* rd0 = tile + (2 * q) * kRowPitch;  // scales of rows 2q, 2q+1
+    const uint8_t* rd1 = rd0 + kRowPitch;
+    seg01 = make_float2(0.0f, 0.0f);
+    seg23 = make_float2(0.0f, 0.0f);
+    for (uint32_t j0 = 0; j0 < nblk; j0 += 8) {
+        int32_t d[8][4];
+#pragma unroll
+        for (uint32_t u = 0; u < 8; u++) {  // eight products first
+            const uint32_t j = j0 + u;
+            uint32_t b0 = 0, b1 = 0;
+            if (g < rows) {
+                if (u & 1)
+                    block_words<true>(rb + j * 34, q, b0, b1);
+                else
+                    block_words<false>(rb + j * 34, q, b0, b1);
+            }
+            const uint2 x0 = *reinterpret_cast<const uint2*>(xs + ((size_t)j * kTok + g) * 32 + 8 * q);
+            const uint2 x1 = *reinterpret_cast<const uint2*>(xs + ((size_t)j * kTok + g + 8) * 32 + 8 * q);
+            const uint32_t fa[4] = {x0.x, x1.x, x0.y, x1.y};
+            mma_s8_16832(fa, b0, b1, d[u]);
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < 8; u++) {  // then their terms, in block order
+            const uint32_t j = j0 + u;
+            const float2 dw = make_float2(__half2float(*reinterpret_cast<const __half*>(rd0 + j * 34)),
+                                          __half2float(*reinterpret_cast<const __half*>(rd1 + j * 34)));
+            const float2 dx = *reinterpret_cast<const float2*>(xd + j * kTok + 2 * g);  // tokens g, g+8
+            const float2 p0 = fmul2_rn(make_float2(dx.x, dx.x), dw);  // token g   x rows 2q, 2q+1
+            const float2 p1 = fmul2_rn(make_float2(dx.y, dx.y), dw);  // token g+8 x rows 2q, 2q+1
+            // the term products and the sums stay scalar: a packed product feeding a
+            // packed sum is contracted into an FMA by the assembler
+            const float2 f01 = i2f2_exact(d[u][0], d[u][1]), f23 = i2f2_exact(d[u][2], d[u][3]);
+            seg01.x = __fadd_rn(seg01.x, __fmul_rn(f01.x, p0.x));
+            seg01.y = __fadd_rn(seg01.y, __fmul_rn(f01.y, p0.y));
+            seg23.x = __fadd_rn(seg23.x, __fmul_rn(f23.x, p1.x));
+            seg23.y = __fadd_rn(seg23.y, __fmul_rn(f23.y, p1.y));
+        }
+    }
+}
+
 // ------------------------------------------------------------- the product
 struct GemmQ8Args {
     float* y;
     size_t ldy;
-    uint32_t M, nb, NT, quads, nw, nslots, flags;
+    uint32_t M, nb, NT, quads;
+    uint32_t ntiles;  // tiles per pass (compute warps per group)
+    uint32_t ngroups, nslots, flags;
 };
 
-__global__ void __launch_bounds__(32 * (kMaxWarps + 1), 1)
+__global__ void __launch_bounds__(32 * (kMaxTiles * kMaxGroups + 1), 1)
     q8_0_gemm_q8_kernel(const __grid_constant__ CUtensorMap wmap8, const __grid_constant__ CUtensorMap wmap4,
-                        const uint8_t* __restrict__ xchunks, const GemmQ8Args a, int* err) {
+                        const uint8_t* __restrict__ records, const GemmQ8Args a, int* err) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t nw = a.nw, nslots = a.nslots, nchunks = a.nb / kChunk;
-    const uint32_t slot_bytes = kXChunkBytes + nw * kTileBytes;
+    const uint32_t T = a.ntiles, nslots = a.nslots, nseg = (a.nb + kSegBlocks - 1) / kSegBlocks;
+    const uint32_t slot_bytes = kXSegBytes + T * kTileBytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // nslots
-    uint64_t* empty = full + kMaxSlots;                  // nslots
-    uint8_t* ring = smem + 256;
-    // this CTA's rows: quads [q0, q1) (balanced); warp unit i = quads q0+2i, q0+2i+1
+    uint64_t* empty = full + kMaxSlots;                  // nslots: T arrivals (the stage's group)
+    uint64_t* baton = empty + kMaxSlots;                 // T: one phase per segment of the tile
+    float* totals = reinterpret_cast<float*>(smem + 256);
+    uint8_t* ring = smem + kRingOffset;
+    // this CTA's rows: quads [q0, q1) (balanced); tile i of pass p = quads q0+2(pT+i), +1
     const uint32_t q0 = (uint32_t)((uint64_t)a.quads * blockIdx.x / gridDim.x);
     const uint32_t q1 = (uint32_t)((uint64_t)a.quads * (blockIdx.x + 1) / gridDim.x);
-    const uint32_t units = (q1 - q0 + 1) / 2, npass = (units + nw - 1) / nw, ntiles = npass * nchunks;
+    const uint32_t tiles = (q1 - q0 + 1) / 2, npass = (tiles + T - 1) / T, nstages = npass * nseg;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < nslots; s++) {
             ptx::mbar_init(&full[s], 1);
-            ptx::mbar_init(&empty[s], nw);
+            ptx::mbar_init(&empty[s], T);
         }
+        for (uint32_t i = 0; i < T; i++) ptx::mbar_init(&baton[i], 1);
         ptx::fence_mbarrier_init();
     }
     __syncthreads();
     ptx::griddep_launch_dependents();
 
     if (warp == 0) {
-        if (lane == 0 && units > 0) {
+        if (lane == 0 && tiles > 0) {
             ptx::prefetch_tmap(&wmap8);
             ptx::prefetch_tmap(&wmap4);
-            // stage t = chunk t % nchunks of pass t / nchunks: the activation record, then the weight tiles
-            auto stage_bytes = [&](uint32_t t) {
-                const uint32_t pass = t / nchunks;
-                uint32_t bytes = kXChunkBytes;
-                for (uint32_t w = 0; w < nw; w++) {
-                    const uint32_t qa = q0 + 2 * (pass * nw + w);
+            // stage t = segment t % nseg of pass t / nseg: the activation record, then
+            // one TMA box per tile (full boxes: rows past M and bytes past the row end
+            // arrive as zero fill and are never stored)
+            auto weight_bytes = [&](uint32_t t) {
+                const uint32_t pass = t / nseg;
+                uint32_t bytes = 0;
+                for (uint32_t i = 0; i < T; i++) {
+                    const uint32_t qa = q0 + 2 * (pass * T + i);
                     if (qa >= q1) break;
                     bytes += (qa + 1 < q1 ? 2u : 1u) * (kTileBytes / 2);
                 }
                 return bytes;
             };
             auto issue_weights = [&](uint32_t t, uint32_t slot) {
-                const uint32_t pass = t / nchunks, c = t - pass * nchunks;
-                uint8_t* dst = ring + (size_t)slot * slot_bytes + kXChunkBytes;
-                for (uint32_t w = 0; w < nw; w++) {
-                    const uint32_t qa = q0 + 2 * (pass * nw + w);
+                const uint32_t pass = t / nseg, s = t - pass * nseg;
+                uint8_t* dst = ring + (size_t)slot * slot_bytes + kXSegBytes;
+                for (uint32_t i = 0; i < T; i++) {
+                    const uint32_t qa = q0 + 2 * (pass * T + i);
                     if (qa >= q1) break;
-                    // x in 32-bit words: c * 272 / 4 = 68 c (a multiple of 4 words)
-                    ptx::tma_load_2d(dst + (size_t)w * kTileBytes, qa + 1 < q1 ? &wmap8 : &wmap4, &full[slot],
-                                     (int)(c * (kChunkBytes / 4)), (int)(qa * 4));
+                    // x in int64 elements: s * 1088 / 8 = 136 s (16-byte aligned)
+                    ptx::tma_load_2d(dst + (size_t)i * kTileBytes, qa + 1 < q1 ? &wmap8 : &wmap4, &full[slot],
+                                     (int)(s * (kSegBytes / 8)), (int)(qa * 4));
                 }
             };
             auto issue_x = [&](uint32_t t, uint32_t slot) {
-                const uint32_t c = t % nchunks;
-                ptx::bulk_load(ring + (size_t)slot * slot_bytes, xchunks + (size_t)c * kXChunkBytes, kXChunkBytes,
+                const uint32_t s = t % nseg;
+                ptx::bulk_load(ring + (size_t)slot * slot_bytes, records + (size_t)s * kXSegBytes, kXSegBytes,
                                &full[slot]);
             };
             // static weights: the first stages' weight tiles are requested before the
             // previous kernel ends; their activation records only after it
-            const uint32_t pre = (a.flags & ANE_Q8_WEIGHTS_STATIC) ? min(nslots, ntiles) : 0;
+            const uint32_t pre = (a.flags & ANE_Q8_WEIGHTS_STATIC) ? min(nslots, nstages) : 0;
             for (uint32_t t = 0; t < pre; t++) {
-                ptx::mbar_arrive_expect_tx(&full[t], stage_bytes(t));
+                ptx::mbar_arrive_expect_tx(&full[t], kXSegBytes + weight_bytes(t));
                 issue_weights(t, t);
             }
             ptx::griddep_wait();  // the activation records come from the quantize kernel
             for (uint32_t t = 0; t < pre; t++) issue_x(t, t);
-            for (uint32_t t = pre; t < ntiles; t++) {
+            for (uint32_t t = pre; t < nstages; t++) {
                 const uint32_t slot = t % nslots;
                 if (!ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err)) break;
-                ptx::mbar_arrive_expect_tx(&full[slot], stage_bytes(t));
+                ptx::mbar_arrive_expect_tx(&full[slot], kXSegBytes + weight_bytes(t));
                 issue_x(t, slot);
                 issue_weights(t, slot);
             }
@@ -220,83 +296,57 @@ __global__ void __launch_bounds__(32 * (kMaxWarps + 1), 1)
     }
     // ------------------------------------------------------------ compute
     ptx::griddep_wait();  // y may still be read by the kernel before this one
-    const uint32_t cw = warp - 1;
-    if (units == 0) return;
+    const uint32_t cw = warp - 1, grp = cw / T, ti = cw % T;
+    if (tiles == 0 || grp >= a.ngroups) return;
     const uint32_t g = lane >> 2, q = lane & 3;
-    bool alive = true;
-    for (uint32_t pass = 0; pass < npass && alive; pass++) {
-        const uint32_t qa = q0 + 2 * (pass * nw + cw);
-        const bool active = qa < q1;
-        const uint32_t rows = active ? (qa + 1 < q1 ? 8u : 4u) : 0u;  // real rows of this warp's tile
-        // thread (g, q): tokens g, g+8 x weight rows 2q, 2q+1 of the tile
-        float seg[4] = {0.0f, 0.0f, 0.0f, 0.0f}, total[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (uint32_t c = 0; c < nchunks; c++) {
-            const uint32_t t = pass * nchunks + c, slot = t % nslots;
-            if (!ptx::mbar_wait(&full[slot], (t / nslots) & 1, err)) {
-                alive = false;
-                break;
-            }
-            if (active) {
-                const uint8_t* xs = ring + (size_t)slot * slot_bytes;
-                const float* xd = reinterpret_cast<const float*>(xs + kXCodes);
-                const uint8_t* tile = xs + kXChunkBytes + (size_t)cw * kTileBytes;
-                const uint8_t* rb = tile + g * kChunkBytes;         // B fragment: weight row g
-                const uint8_t* rd0 = tile + (2 * q) * kChunkBytes;  // scales of rows 2q, 2q+1
-                const uint8_t* rd1 = rd0 + kChunkBytes;
-                int32_t d[kChunk][4];
-#pragma unroll
-                for (uint32_t j = 0; j < kChunk; j++) {  // the chunk's eight products first
-                    uint32_t b0 = 0, b1 = 0;
-                    if (g < rows) {
-                        if (j & 1)
-                            block_words<true>(rb + j * 34, q, b0, b1);
-                        else
-                            block_words<false>(rb + j * 34, q, b0, b1);
-                    }
-                    const uint2 x0 = *reinterpret_cast<const uint2*>(xs + ((size_t)j * kTok + g) * 32 + 8 * q);
-                    const uint2 x1 = *reinterpret_cast<const uint2*>(xs + ((size_t)j * kTok + g + 8) * 32 + 8 * q);
-                    const uint32_t fa[4] = {x0.x, x1.x, x0.y, x1.y};
-                    mma_s8_16832(fa, b0, b1, d[j]);
-                }
-#pragma unroll
-                for (uint32_t j = 0; j < kChunk; j++) {  // then their terms, in block order
-                    const float2 dw = make_float2(__half2float(*reinterpret_cast<const __half*>(rd0 + j * 34)),
-                                                  __half2float(*reinterpret_cast<const __half*>(rd1 + j * 34)));
-                    const float2 dx = *reinterpret_cast<const float2*>(xd + j * kTok + 2 * g);  // tokens g, g+8
-                    const float2 p0 = fmul2_rn(make_float2(dx.x, dx.x), dw);  // token g   x rows 2q, 2q+1
-                    const float2 p1 = fmul2_rn(make_float2(dx.y, dx.y), dw);  // token g+8 x rows 2q, 2q+1
-                    seg[0] = q8_term_add(seg[0], d[j][0], p0.x);
-                    seg[1] = q8_term_add(seg[1], d[j][1], p0.y);
-                    seg[2] = q8_term_add(seg[2], d[j][2], p1.x);
-                    seg[3] = q8_term_add(seg[3], d[j][3], p1.y);
-                }
-                if ((c + 1) % kChunksPerSeg == 0 || c + 1 == nchunks) {  // segment complete
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        total[k] = __fadd_rn(total[k], seg[k]);
-                        seg[k] = 0.0f;
-                    }
-                }
-            }
+    float* tot = totals + ti * (kTotBytes / 4) + lane * 4;
+    // stage t goes to group t % ngroups, so with two groups stage t - 2 is always
+    // this warp's own: when it waits on phase t - 1 of the baton, phase t - 2 is
+    // complete and the parity test is exact
+    for (uint32_t t = grp; t < nstages; t += a.ngroups) {
+        const uint32_t pass = t / nseg, s = t - pass * nseg, slot = t % nslots;
+        const uint32_t qa = q0 + 2 * (pass * T + ti);
+        const bool active = qa < q1;  // once false, false for every later pass
+        if (!ptx::mbar_wait(&full[slot], (t / nslots) & 1, err)) break;
+        if (!active) {
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&empty[slot]);
+            continue;
         }
-        if (!alive || !active) continue;
-        const uint32_t row0 = qa * 4 + 2 * q;  // rows 2q, 2q+1 of the tile
+        const uint32_t rows = qa + 1 < q1 ? 8u : 4u;  // real rows of this tile
+        const uint8_t* xs = ring + (size_t)slot * slot_bytes;
+        const uint32_t nblk = min(kSegBlocks, a.nb - s * kSegBlocks);
+        float2 seg01, seg23;
+        segment_sums(xs, xs + kXSegBytes + (size_t)ti * kTileBytes, nblk, rows, g, q, seg01, seg23);
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&empty[slot]);
+        // the row totals, in segment order: wait for stage t - 1's phase of this
+        // tile's baton, add this segment, pass the baton on
+        if (t > 0 && !ptx::mbar_wait(&baton[ti], (t - 1) & 1, err)) break;
+        float4 acc = s == 0 ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : *reinterpret_cast<const float4*>(tot);
+        const float2 lo = fadd2_rn(make_float2(acc.x, acc.y), seg01);
+        const float2 hi = fadd2_rn(make_float2(acc.z, acc.w), seg23);
+        if (s + 1 < nseg) {
+            *reinterpret_cast<float4*>(tot) = make_float4(lo.x, lo.y, hi.x, hi.y);
+        } else {
+            const uint32_t row0 = qa * 4 + 2 * q;  // rows 2q, 2q+1 of the tile
+            const float v[4] = {lo.x, lo.y, hi.x, hi.y};
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const uint32_t row = row0 + (k & 1), tok = g + 8 * (k >> 1);
-            if (2 * q + (k & 1) < rows && row < a.M && tok < a.NT) a.y[(size_t)tok * a.ldy + row] = total[k];
+            for (int k = 0; k < 4; k++) {
+                const uint32_t row = row0 + (k & 1), tok = g + 8 * (k >> 1);
+                if (2 * q + (k & 1) < rows && row < a.M && tok < a.NT) a.y[(size_t)tok * a.ldy + row] = v[k];
+            }
         }
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&baton[ti]);
     }
 }
 
 }  // namespace
-
-// Workspace: the activation records, nb / kChunk of kXChunkBytes.
+// Workspace: the activation records, one of kXSegBytes per K segment.
 size_t mul_mat_q8_0_batch_workspace_size(uint32_t M, uint32_t K) {
     (void)M;
-    return round_up256((size_t)(K / 32 / kChunk) * kXChunkBytes);
+    return round_up256((size_t)((K / 32 + kSegBlocks - 1) / kSegBlocks) * kXSegBytes);
 }
 
 int launch_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const float* x, size_t ldx, const uint8_t* W,
@@ -309,7 +359,7 @@ int launch_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const float* 
                   "mul_mat_q8_0_batch: x rows must be 16-byte aligned (ldx % 4 == 0, ldx >= K)");
     ANE_ARG_CHECK(ldy >= M || NT == 1, "mul_mat_q8_0_batch: ldy < M");
     ANE_ARG_CHECK(workspace && ((uintptr_t)workspace & 255) == 0, "mul_mat_q8_0_batch: workspace must be 256-byte aligned");
-    const uint32_t sms = (uint32_t)num_sms(), nb = K / 32;
+    const uint32_t sms = (uint32_t)num_sms(), nb = K / 32, nseg = (nb + kSegBlocks - 1) / kSegBlocks;
     GemmQ8Args a;
     a.y = y;
     a.ldy = ldy;
@@ -318,43 +368,46 @@ int launch_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const float* 
     a.NT = NT;
     a.quads = (M + 3) / 4;
     a.flags = flags;
-    // balanced runs of quads per CTA; one or more CTAs per SM so that a CTA
-    // needs at most kMaxWarps compute warps (8 rows each)
-    const uint32_t units_per_sm = (a.quads + 2 * sms - 1) / (2 * sms);
-    uint32_t cps = (units_per_sm + kMaxWarps - 1) / kMaxWarps;
-    if (cps == 0) cps = 1;
-    uint32_t ctas = sms * cps;
-    if (ctas > a.quads) ctas = a.quads;
-    const uint32_t max_quads = (a.quads + ctas - 1) / ctas;
-    a.nw = (max_quads + 1) / 2;
-    if (a.nw > kMaxWarps) a.nw = kMaxWarps;
-    const size_t slot_bytes = kXChunkBytes + (size_t)a.nw * kTileBytes;
-    // with one CTA per SM, room for the next kernel's CTA beside it
-    const size_t budget = (cps == 1 ? 227 * 1024 / 2 : 227 * 1024 / cps) - 1024;
-    uint32_t slots = budget > 256 + 2 * slot_bytes ? (uint32_t)((budget - 256) / slot_bytes) : 2;
-    static const int force_slots = env_int("ANE_Q8B_SLOTS");
+    // balanced runs of quads, one CTA per SM; a CTA's tiles in as few balanced
+    // passes as the tile cap allows; two warp groups unless K is one segment
+    static const int force_tiles = env_int("ANE_Q8B_TILES"), force_slots = env_int("ANE_Q8B_SLOTS"),
+                     force_groups = env_int("ANE_Q8B_GROUPS"), force_budget_kb = env_int("ANE_Q8B_SMEM_KB");
+    const uint32_t ctas = a.quads < sms ? a.quads : sms;
+    const uint32_t max_quads = (a.quads + ctas - 1) / ctas, max_tiles = (max_quads + 1) / 2;
+    uint32_t tcap = force_tiles > 0 ? (uint32_t)force_tiles : 4u;
+    if (tcap > kMaxTiles) tcap = kMaxTiles;
+    const uint32_t npass = (max_tiles + tcap - 1) / tcap;
+    a.ntiles = (max_tiles + npass - 1) / npass;
+    a.ngroups = nseg >= 2 ? kMaxGroups : 1u;
+    if (force_groups == 1) a.ngroups = 1;
+    const size_t slot_bytes = kXSegBytes + (size_t)a.ntiles * kTileBytes;
+    const size_t budget = force_budget_kb > 0 ? (size_t)force_budget_kb * 1024 : 227 * 1024;
+    uint32_t slots = budget > kRingOffset + 2 * slot_bytes ? (uint32_t)((budget - kRingOffset) / slot_bytes) : 2;
     if (force_slots > 0) slots = (uint32_t)force_slots;
     a.nslots = slots < 2 ? 2 : (slots > kMaxSlots ? kMaxSlots : slots);
-    const size_t smem = 256 + a.nslots * slot_bytes;
+    const size_t smem = kRingOffset + a.nslots * slot_bytes;
     ANE_ARG_CHECK(smem <= 227 * 1024, "mul_mat_q8_0_batch: shared memory plan too large");
 
-    const uint64_t row_bytes = (uint64_t)nb * 34;
+    // box rows of kRowPitch bytes from each segment start: the pitch the box lands
+    // in shared memory with; the 16 bytes past the segment are the next one's (or
+    // zero fill past the row end) and are never read
+    const uint64_t row_bytes = (uint64_t)nb * 34;  // a multiple of 272, so of 8 and 16
     CUtensorMap wmap8, wmap4;
-    int rc = encode_tensor_map_2d(&wmap8, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, row_bytes / 4, M, row_bytes,
-                                  kChunkBytes / 4, kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    int rc = encode_tensor_map_2d(&wmap8, CU_TENSOR_MAP_DATA_TYPE_INT64, W, row_bytes / 8, M, row_bytes,
+                                  kRowPitch / 8, kRows, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    rc = encode_tensor_map_2d(&wmap4, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, row_bytes / 4, M, row_bytes,
-                              kChunkBytes / 4, kRows / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+    rc = encode_tensor_map_2d(&wmap4, CU_TENSOR_MAP_DATA_TYPE_INT64, W, row_bytes / 8, M, row_bytes, kRowPitch / 8,
+                              kRows / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    uint8_t* chunks = static_cast<uint8_t*>(workspace);
+    uint8_t* records = static_cast<uint8_t*>(workspace);
     const uint32_t nthreads = nb * kTok;
-    rc = launch_pdl(quantize_x_chunks_kernel, dim3((nthreads + 255) / 256), dim3(256), 0, s, x, ldx, NT, nb, chunks);
+    rc = launch_pdl(quantize_x_segments_kernel, dim3((nthreads + 255) / 256), dim3(256), 0, s, x, ldx, NT, nb, records);
     if (rc) return rc;
     static const cudaError_t attr_err =
         cudaFuncSetAttribute(q8_0_gemm_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     ANE_CUDA_TRY(attr_err);
-    return launch_pdl(q8_0_gemm_q8_kernel, dim3(ctas), dim3(32 * (a.nw + 1)), smem, s, wmap8, wmap4,
-                      (const uint8_t*)chunks, a, device_timeout_flag());
+    return launch_pdl(q8_0_gemm_q8_kernel, dim3(ctas), dim3(32 * (1 + a.ntiles * a.ngroups)), smem, s, wmap8, wmap4,
+                      (const uint8_t*)records, a, device_timeout_flag());
 }
 
 }  // namespace ane_b200

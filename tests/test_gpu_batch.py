@@ -35,6 +35,8 @@ def _case(M, K, NT, seed):
     (300, 11008, 9),
     (64, 512, 16),
     (2000, 1024, 12),
+    (37, 512, 3),        # M % 4 != 0: the last tile's missing rows are never copied
+    (1001, 4352, 16),    # K = 17 x 256: a last segment of 8 blocks
 ])
 def test_mul_mat_q8_0_batch_exact(ane, M, K, NT):
     import torch
