@@ -12,10 +12,11 @@
 //
 // Launch 1 (quantize_x_segments_kernel): the activation rows, quantized with the
 // ggml Q8_0 rule, into one record per K segment of 32 blocks:
-//     codes  [32 blocks][16 tokens][8 words]   words of a block stored as 0,4,1,5,2,6,3,7
+//     codes  [32 blocks][8 g][4 q][4 words]   lane (g, q) of an MMA A fragment: words q of
+//                                              tokens g, g+8, then words q+4 of tokens g, g+8
 //     scales [32 blocks][8][2] fp32            token t at (t % 8) * 2 + t / 8
-// (zero past NT) -- the layout the MMA fragments load with one 64-bit
-// shared-memory load per token and block.
+// (zero past NT) -- the layout the MMA A fragments load with one 128-bit
+// shared-memory load per lane and block.
 // Launch 2 (q8_0_gemm_q8_kernel): rows are dealt to one CTA per SM in balanced
 // runs of 4; the CTA's rows form tiles of 8 (the run's last tile may hold 4).
 // One producer warp feeds a ring whose stage holds one K segment: the
@@ -23,11 +24,11 @@
 // of 138 x 8 int64 elements from the segment start (long box rows keep the TMA
 // engine at HBM rate -- 272-byte rows held it near 2 TB/s -- and the 1104-byte
 // row pitch keeps the fragment loads free of bank conflicts).  Two groups of
-// compute warps
-// take alternate segments, one warp per tile in each group.  Per block a warp
-// runs one mma.sync m16n8k32 (s8 x s8 -> s32) -- the 16 tokens as M, the tile's
-// 8 rows as N -- eight products ahead of their fp32 scale math; the int32 dots
-// become floats by an exact magic-number add.  A warp's segment sum joins the
+// compute warps take alternate segments, one warp per tile in each group.  Per
+// block a warp runs one mma.sync m16n8k32 (s8 x s8 -> s32) -- the 16 tokens as
+// M, the tile's 8 rows as N -- the next eight products ahead of the current
+// eight blocks' fp32 scale math; the int32 dots become floats exactly through
+// a magic number the MMA adds as its C operand.  A warp's segment sum joins the
 // row total in segment order through a per-tile shared-memory baton (one
 // mbarrier phase per segment), so the fp32 order is the contract's whatever
 // the group timing.
@@ -48,11 +49,11 @@ constexpr uint32_t kTileBytes = kRows * kRowPitch;        // 8832 = 69 x 128
 constexpr uint32_t kTok = 16;                             // activation rows per record (MMA M)
 constexpr uint32_t kXCodes = kSegBlocks * kTok * 32;      // 16384
 constexpr uint32_t kXSegBytes = kXCodes + kSegBlocks * kTok * 4;  // + scales = 18432 = 144 x 128
-constexpr uint32_t kMaxTiles = 8;                         // tiles per pass (compute warps per group)
+constexpr uint32_t kMaxTiles = 6;                         // tiles per pass (compute warps per group)
 constexpr uint32_t kMaxGroups = 2;
 constexpr uint32_t kMaxSlots = 8;
 constexpr uint32_t kTotBytes = 32 * 4 * 4;                // one tile's running totals: 32 lanes x 4 floats
-constexpr uint32_t kRingOffset = 256 + kMaxTiles * kTotBytes;  // 4352 = 34 x 128
+constexpr uint32_t kRingOffset = 256 + kMaxTiles * kTotBytes;  // 3328 = 26 x 128
 static_assert(kTileBytes % 128 == 0 && kXSegBytes % 128 == 0 && kRingOffset % 128 == 0,
               "TMA / bulk destinations stay 128-byte aligned");
 static_assert(kSegBytes % 16 == 0 && kRowPitch / 8 <= 256 && (kRowPitch / 4) % 8 == 4,
@@ -74,11 +75,12 @@ __global__ void quantize_x_segments_kernel(const float* __restrict__ x, size_t l
     const uint32_t b = i / kTok, t = i % kTok;
     const uint32_t s = b / kSegBlocks, j = b % kSegBlocks;
     uint8_t* rec = records + (size_t)s * kXSegBytes;
-    uint4* codes = reinterpret_cast<uint4*>(rec + ((size_t)j * kTok + t) * 32);
+    // token t = g + 8h: word q at lane (g, q) word h, word q+4 at lane (g, q) word 2+h
+    uint32_t* codes = reinterpret_cast<uint32_t*>(rec + (size_t)j * kTok * 32 + (t % 8) * 64) + t / 8;
     float* scale = reinterpret_cast<float*>(rec + kXCodes) + j * kTok + (t % 8) * 2 + t / 8;
     if (t >= NT) {
-        codes[0] = make_uint4(0, 0, 0, 0);
-        codes[1] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int q = 0; q < 4; q++) codes[4 * q] = codes[4 * q + 2] = 0u;
         *scale = 0.0f;
         return;
     }
@@ -94,17 +96,20 @@ __global__ void quantize_x_segments_kernel(const float* __restrict__ x, size_t l
     }
     uint32_t w[8];
     *scale = q8_quantize_words(v, w);
-    // lane q of an MMA fragment reads words (q, q+4) = codes 4q..4q+3 and 16+4q..16+4q+3
-    codes[0] = make_uint4(w[0], w[4], w[1], w[5]);
-    codes[1] = make_uint4(w[2], w[6], w[3], w[7]);
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        codes[4 * q] = w[q];
+        codes[4 * q + 2] = w[q + 4];
+    }
 }
 
-__device__ __forceinline__ void mma_s8_16832(const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int32_t (&d)[4]) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+// d = a x b + c (s8 x s8 -> s32, exact; the int32 add wraps)
+__device__ __forceinline__ void mma_s8_16832(const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int32_t c,
+                                             int32_t (&d)[4]) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
         "{%10, %10, %10, %10};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c));
 }
 
 // Packed IEEE fp32 operations, round to nearest even, subnormals kept: two
@@ -134,12 +139,13 @@ __device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
     return d;
 }
 
-// float(s0), float(s1) for |s| < 2^22, exactly: the bits of 1.5 * 2^23 + s,
-// plus -1.5 * 2^23 (|sumi| <= 32 * 128 * 127 < 2^19).  Integer adds + one
-// packed fp32 add, all full rate.
-__device__ __forceinline__ float2 i2f2_exact(int32_t s0, int32_t s1) {
-    return fadd2_rn(make_float2(__int_as_float(0x4B400000 + s0), __int_as_float(0x4B400000 + s1)),
-                    make_float2(-12582912.0f, -12582912.0f));
+// The products carry the magic number 1.5 * 2^23 (0x4B400000) added by the
+// tensor core (the MMA's C operand): for |sumi| < 2^22 the bits 0x4B400000 +
+// sumi are the float 1.5 * 2^23 + sumi, so one packed fp32 add of -1.5 * 2^23
+// gives float(sumi) exactly (|sumi| <= 32 * 128 * 127 < 2^19).
+constexpr int32_t kMagic = 0x4B400000;
+__device__ __forceinline__ float2 magic2_to_float(int32_t m0, int32_t m1) {
+    return fadd2_rn(make_float2(__int_as_float(m0), __int_as_float(m1)), make_float2(-12582912.0f, -12582912.0f));
 }
 
 // Codes 4q..4q+3 and 16+4q..16+4q+3 of the 34-byte Q8_0 block at `blk` in the
@@ -158,9 +164,52 @@ __device__ __forceinline__ void block_words(const uint8_t* blk, uint32_t q, uint
     }
 }
 
+// The products of blocks j0..j0+7 of one tile: d[u] = kMagic + the int32 dots
+// of block j0+u for (token g | g+8) x (tile row 2q | 2q+1).
+__device__ __forceinline__ void block_products(const uint8_t* xs, const uint8_t* rb, uint32_t j0, uint32_t rows,
+                                               uint32_t g, uint32_t q, int32_t (&d)[8][4]) {
+#pragma unroll
+    for (uint32_t u = 0; u < 8; u++) {
+        const uint32_t j = j0 + u;
+        uint32_t b0 = 0, b1 = 0;
+        if (g < rows) {
+            if (u & 1)
+                block_words<true>(rb + j * 34, q, b0, b1);
+            else
+                block_words<false>(rb + j * 34, q, b0, b1);
+        }
+        const uint4 xa = *reinterpret_cast<const uint4*>(xs + (size_t)j * kTok * 32 + (g * 4 + q) * 16);
+        const uint32_t fa[4] = {xa.x, xa.y, xa.z, xa.w};
+        mma_s8_16832(fa, b0, b1, kMagic, d[u]);
+    }
+}
+
+// The terms of blocks j0..j0+7, added in block order.
+__device__ __forceinline__ void block_terms(const float* xd, const uint8_t* rd0, const uint8_t* rd1, uint32_t j0,
+                                            uint32_t g, const int32_t (&d)[8][4], float2& seg01, float2& seg23) {
+#pragma unroll
+    for (uint32_t u = 0; u < 8; u++) {
+        const uint32_t j = j0 + u;
+        const float2 dw = make_float2(__half2float(*reinterpret_cast<const __half*>(rd0 + j * 34)),
+                                      __half2float(*reinterpret_cast<const __half*>(rd1 + j * 34)));
+        const float2 dx = *reinterpret_cast<const float2*>(xd + j * kTok + 2 * g);  // tokens g, g+8
+        const float2 p0 = fmul2_rn(make_float2(dx.x, dx.x), dw);  // token g   x rows 2q, 2q+1
+        const float2 p1 = fmul2_rn(make_float2(dx.y, dx.y), dw);  // token g+8 x rows 2q, 2q+1
+        // the term products and the sums stay scalar: a packed product feeding a
+        // packed sum is contracted into an FMA by the assembler
+        const float2 f01 = magic2_to_float(d[u][0], d[u][1]), f23 = magic2_to_float(d[u][2], d[u][3]);
+        seg01.x = __fadd_rn(seg01.x, __fmul_rn(f01.x, p0.x));
+        seg01.y = __fadd_rn(seg01.y, __fmul_rn(f01.y, p0.y));
+        seg23.x = __fadd_rn(seg23.x, __fmul_rn(f23.x, p1.x));
+        seg23.y = __fadd_rn(seg23.y, __fmul_rn(f23.y, p1.y));
+    }
+}
+
 // One K segment of one tile: the sum from +0, in block order, of the terms of
 // blocks [0, nblk) (nblk a multiple of 8).  Thread (g, q) holds tokens g, g+8 x
 // tile rows 2q, 2q+1: seg01 = (tok g, row 2q | 2q+1), seg23 = (tok g+8, ...).
+// Software-pipelined: the next eight products are issued before the current
+// eight blocks' terms, so the tensor-core latency hides behind the fp32 work.
 __device__ __forceinline__ void segment_sums(const uint8_t* xs, const uint8_t* tile, uint32_t nblk, uint32_t rows,
                                              uint32_t g, uint32_t q, float2& seg01, float2& seg23) {
     const float* xd = reinterpret_cast<const float*>(xs + kXCodes);
@@ -169,39 +218,15 @@ __device__ __forceinline__ void segment_sums(const uint8_t* xs, const uint8_t* t
     const uint8_t* rd1 = rd0 + kRowPitch;
     seg01 = make_float2(0.0f, 0.0f);
     seg23 = make_float2(0.0f, 0.0f);
-    for (uint32_t j0 = 0; j0 < nblk; j0 += 8) {
-        int32_t d[8][4];
-#pragma unroll
-        for (uint32_t u = 0; u < 8; u++) {  // eight products first
-            const uint32_t j = j0 + u;
-            uint32_t b0 = 0, b1 = 0;
-            if (g < rows) {
-                if (u & 1)
-                    block_words<true>(rb + j * 34, q, b0, b1);
-                else
-                    block_words<false>(rb + j * 34, q, b0, b1);
-            }
-            const uint2 x0 = *reinterpret_cast<const uint2*>(xs + ((size_t)j * kTok + g) * 32 + 8 * q);
-            const uint2 x1 = *reinterpret_cast<const uint2*>(xs + ((size_t)j * kTok + g + 8) * 32 + 8 * q);
-            const uint32_t fa[4] = {x0.x, x1.x, x0.y, x1.y};
-            mma_s8_16832(fa, b0, b1, d[u]);
-        }
-#pragma unroll
-        for (uint32_t u = 0; u < 8; u++) {  // then their terms, in block order
-            const uint32_t j = j0 + u;
-            const float2 dw = make_float2(__half2float(*reinterpret_cast<const __half*>(rd0 + j * 34)),
-                                          __half2float(*reinterpret_cast<const __half*>(rd1 + j * 34)));
-            const float2 dx = *reinterpret_cast<const float2*>(xd + j * kTok + 2 * g);  // tokens g, g+8
-            const float2 p0 = fmul2_rn(make_float2(dx.x, dx.x), dw);  // token g   x rows 2q, 2q+1
-            const float2 p1 = fmul2_rn(make_float2(dx.y, dx.y), dw);  // token g+8 x rows 2q, 2q+1
-            // the term products and the sums stay scalar: a packed product feeding a
-            // packed sum is contracted into an FMA by the assembler
-            const float2 f01 = i2f2_exact(d[u][0], d[u][1]), f23 = i2f2_exact(d[u][2], d[u][3]);
-            seg01.x = __fadd_rn(seg01.x, __fmul_rn(f01.x, p0.x));
-            seg01.y = __fadd_rn(seg01.y, __fmul_rn(f01.y, p0.y));
-            seg23.x = __fadd_rn(seg23.x, __fmul_rn(f23.x, p1.x));
-            seg23.y = __fadd_rn(seg23.y, __fmul_rn(f23.y, p1.y));
-        }
+    int32_t da[8][4], db[8][4];
+    block_products(xs, rb, 0, rows, g, q, da);
+    for (uint32_t j0 = 0; j0 < nblk; j0 += 16) {
+        const bool more = j0 + 8 < nblk;
+        if (more) block_products(xs, rb, j0 + 8, rows, g, q, db);
+        block_terms(xd, rd0, rd1, j0, g, da, seg01, seg23);
+        if (!more) break;
+        if (j0 + 16 < nblk) block_products(xs, rb, j0 + 16, rows, g, q, da);
+        block_terms(xd, rd0, rd1, j0 + 8, g, db, seg01, seg23);
     }
 }
 
@@ -374,15 +399,17 @@ int launch_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const float* 
                      force_groups = env_int("ANE_Q8B_GROUPS"), force_budget_kb = env_int("ANE_Q8B_SMEM_KB");
     const uint32_t ctas = a.quads < sms ? a.quads : sms;
     const uint32_t max_quads = (a.quads + ctas - 1) / ctas, max_tiles = (max_quads + 1) / 2;
-    uint32_t tcap = force_tiles > 0 ? (uint32_t)force_tiles : 4u;
+    uint32_t tcap = force_tiles > 0 ? (uint32_t)force_tiles : 5u;
     if (tcap > kMaxTiles) tcap = kMaxTiles;
     const uint32_t npass = (max_tiles + tcap - 1) / tcap;
     a.ntiles = (max_tiles + npass - 1) / npass;
     a.ngroups = nseg >= 2 ? kMaxGroups : 1u;
     if (force_groups == 1) a.ngroups = 1;
     const size_t slot_bytes = kXSegBytes + (size_t)a.ntiles * kTileBytes;
+    // three stages (measured on B200: 2 starve one group, 4 were slower than 3)
     const size_t budget = force_budget_kb > 0 ? (size_t)force_budget_kb * 1024 : 227 * 1024;
     uint32_t slots = budget > kRingOffset + 2 * slot_bytes ? (uint32_t)((budget - kRingOffset) / slot_bytes) : 2;
+    if (slots > 3 && force_budget_kb <= 0) slots = 3;
     if (force_slots > 0) slots = (uint32_t)force_slots;
     a.nslots = slots < 2 ? 2 : (slots > kMaxSlots ? kMaxSlots : slots);
     const size_t smem = kRingOffset + a.nslots * slot_bytes;
