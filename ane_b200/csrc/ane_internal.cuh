@@ -128,6 +128,12 @@ int encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void
                          uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                          CUtensorMapSwizzle swizzle);
 
+// 3-D TMA tensor map: dims[0] innermost (elements), strides of dims 1 and 2 in
+// bytes (multiples of 16), box box[0] x box[1] x box[2] elements, zero OOB fill,
+// no swizzle.
+int encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t (&dims)[3],
+                         const uint64_t (&stride_bytes)[2], const uint32_t (&box)[3]);
+
 // ------------------------------------------------------- small math helpers
 __host__ __device__ inline size_t ceil_div(size_t a, size_t b) { return (a + b - 1) / b; }
 __host__ __device__ inline size_t round_up(size_t a, size_t b) { return ceil_div(a, b) * b; }

@@ -24,6 +24,9 @@
 // record a device timeout instead of hanging.  Two launches of this kernel can
 // never be resident at once (each CTA takes more than half of an SM's shared
 // memory), so one barrier per device suffices.
+#include <cuda.h>
+#include <string.h>
+
 #include "ane_internal.cuh"
 #include "sm100_ptx.cuh"
 
@@ -230,20 +233,106 @@ __device__ __forceinline__ BUnit b_unit(uint32_t u, uint32_t nch, uint32_t K, ui
     return g;
 }
 
-// Codes of B units [ub0, ub1), transposed: thread (c4 = t % 128, rg = t / 128)
-// takes 4-row groups g = rg, rg + 4 of column quad c4; a 4x4 block of codes is
-// transposed in registers (8 byte permutes) and staged as Bt rows.  The next
-// unit's eight float4 are requested before the current unit is processed.
+// Pack, transpose and write one unit of B codes from the thread's eight float4
+// (two 4-row groups of column quad c4): a 4x4 block of codes is transposed in
+// registers (8 byte permutes) and staged as Bt rows; then every Bt row of the
+// unit receives one aligned 32-byte run.
 template <bool FAST>
-__device__ void quantize_units_transposed(const float4* __restrict__ B4, uint32_t N4, uint32_t K, uint32_t N,
-                                          uint32_t nch, uint32_t ub0, uint32_t ub1, const float4* cache,
-                                          uint32_t* stage, int8_t* __restrict__ Bt, float inv) {
+__device__ __forceinline__ void unit_codes_out(const float4 (&cur)[2][4], const BUnit& g, uint32_t c4, uint32_t rg,
+                                               uint32_t* stage, int8_t* __restrict__ Bt, uint32_t K, float inv) {
+    const uint32_t groups = g.rows / 4;
+    if (c4 < g.cols4) {
+#pragma unroll
+        for (uint32_t h = 0; h < 2; h++) {
+            const uint32_t gi = rg + 4 * h;
+            if (gi >= groups) break;
+            uint32_t P[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) P[i] = pack4<FAST>(cur[h][i], inv);  // row 4gi+i, columns 4c4..+3
+            const uint32_t t0 = __byte_perm(P[0], P[1], 0x5140), t1 = __byte_perm(P[0], P[1], 0x7362);
+            const uint32_t t2 = __byte_perm(P[2], P[3], 0x5140), t3 = __byte_perm(P[2], P[3], 0x7362);
+            uint4 cols;  // word j: rows 4gi..4gi+3 of column 4c4+j
+            cols.x = __byte_perm(t0, t2, 0x5410);
+            cols.y = __byte_perm(t0, t2, 0x7632);
+            cols.z = __byte_perm(t1, t3, 0x5410);
+            cols.w = __byte_perm(t1, t3, 0x7632);
+            *reinterpret_cast<uint4*>(stage + gi * kStageRow + 4 * c4) = cols;
+        }
+    }
+    __syncthreads();
+    // Bt row c0 + n receives `groups` (8 or 4) consecutive words at column r0,
+    // written as 16-byte pieces: piece q = (n, half), words 4*half..4*half+3
+    const uint32_t cols = 4 * g.cols4, hshift = groups == 8 ? 1 : 0;
+    for (uint32_t q = threadIdx.x; q < (cols << hshift); q += kCoopThreads) {
+        const uint32_t n = q >> hshift, half = q & hshift;
+        const uint32_t* sp = stage + 4 * half * kStageRow + n;
+        const uint4 o = make_uint4(sp[0], sp[kStageRow], sp[2 * kStageRow], sp[3 * kStageRow]);
+        *reinterpret_cast<uint4*>(Bt + (size_t)(g.c0 + n) * K + g.r0 + 16 * half) = o;
+    }
+    __syncthreads();  // stage is rewritten by the next unit
+}
+
+// The thread's eight float4 of unit g from a shared-memory copy of the unit
+// (32 rows x 512 columns, row pitch 128 float4); zero outside the unit.
+__device__ __forceinline__ void unit_from_smem(float4 (&v)[2][4], const float4* cu, const BUnit& g, uint32_t c4,
+                                               uint32_t rg) {
+    const uint32_t groups = g.rows / 4;
+#pragma unroll
+    for (uint32_t h = 0; h < 2; h++) {
+        const uint32_t gi = rg + 4 * h;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            v[h][i] = (c4 >= g.cols4 || gi >= groups) ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                                       : cu[(4 * gi + i) * (kUnitCols / 4) + c4];
+    }
+}
+
+// Codes of B units [ub0, ub1), transposed: thread (c4 = t % 128, rg = t / 128)
+// takes 4-row groups g = rg, rg + 4 of column quad c4.
+// With a tensor map (bmap): unit k of the CTA is read from shared-memory slot
+// k % kCacheSlots -- units 0..2 are still there from the absmax phase; unit
+// k + 3 is brought into slot k % 3 by one 3-D TMA box (from L2, where the
+// absmax phase left it) as soon as unit k's values are in registers, so the
+// copies run two units ahead of the arithmetic.  Returns false if a copy did
+// not arrive in time (device timeout recorded).
+// Without: the next unit's eight float4 are requested (shared memory or L2)
+// before the current unit is processed.
+template <bool FAST>
+__device__ bool quantize_units_transposed(const float4* __restrict__ B4, uint32_t N4, uint32_t K, uint32_t N,
+                                          uint32_t nch, uint32_t ub0, uint32_t ub1, float4* cache,
+                                          uint32_t* stage, int8_t* __restrict__ Bt, float inv,
+                                          const CUtensorMap* bmap, uint64_t* tbar, int* err) {
     const uint64_t once = policy_evict_first();
     const uint32_t c4 = threadIdx.x % (kUnitCols / 4), rg = threadIdx.x / (kUnitCols / 4);
+    if (bmap) {
+        const uint32_t n = ub1 - ub0;
+        for (uint32_t k = 0; k < n; k++) {
+            const uint32_t slot = k % kCacheSlots;
+            if (k >= kCacheSlots) {
+                const bool ok = ptx::mbar_wait(&tbar[slot], (k / kCacheSlots - 1) & 1, err);
+                if (__syncthreads_or(!ok)) return false;
+            }
+            const BUnit g = b_unit(ub0 + k, nch, K, N);
+            float4 cur[2][4];
+            unit_from_smem(cur, cache + slot * kUnitF4, g, c4, rg);
+            __syncthreads();  // every thread holds its values: the slot may be refilled
+            if (threadIdx.x == 0 && k + kCacheSlots < n) {
+                const BUnit gn = b_unit(ub0 + k + kCacheSlots, nch, K, N);
+                ptx::fence_proxy_async_smem();  // the slot's generic accesses before the async-proxy write
+                ptx::mbar_arrive_expect_tx(&tbar[slot], kUnitF4 * 16);
+                ptx::tma_load_3d(cache + slot * kUnitF4, bmap, &tbar[slot], 0, (int)(gn.c0 / 256), (int)gn.r0);
+            }
+            unit_codes_out<FAST>(cur, g, c4, rg, stage, Bt, K, inv);
+        }
+        return true;
+    }
     auto load_unit = [&](float4 (&v)[2][4], uint32_t u) {
         const BUnit g = b_unit(u, nch, K, N);
         const uint32_t slot = u - ub0, groups = g.rows / 4;
-        const float4* cu = slot < kCacheSlots ? cache + slot * kUnitF4 : nullptr;
+        if (slot < kCacheSlots) {
+            unit_from_smem(v, cache + slot * kUnitF4, g, c4, rg);
+            return;
+        }
 #pragma unroll
         for (uint32_t h = 0; h < 2; h++) {
             const uint32_t gi = rg + 4 * h;
@@ -252,8 +341,7 @@ __device__ void quantize_units_transposed(const float4* __restrict__ B4, uint32_
                 const uint32_t r = 4 * gi + i;
                 v[h][i] = (c4 >= g.cols4 || gi >= groups)
                               ? make_float4(0.f, 0.f, 0.f, 0.f)
-                              : (cu ? cu[r * (kUnitCols / 4) + c4]
-                                    : ld4(B4 + (size_t)(g.r0 + r) * N4 + g.c0 / 4 + c4, once));
+                              : ld4(B4 + (size_t)(g.r0 + r) * N4 + g.c0 / 4 + c4, once);
             }
         }
     };
@@ -261,42 +349,13 @@ __device__ void quantize_units_transposed(const float4* __restrict__ B4, uint32_
     if (ub0 < ub1) load_unit(cur, ub0);
     for (uint32_t u = ub0; u < ub1; u++) {
         if (u + 1 < ub1) load_unit(nxt, u + 1);
-        const BUnit g = b_unit(u, nch, K, N);
-        const uint32_t groups = g.rows / 4;
-        if (c4 < g.cols4) {
-#pragma unroll
-            for (uint32_t h = 0; h < 2; h++) {
-                const uint32_t gi = rg + 4 * h;
-                if (gi >= groups) break;
-                uint32_t P[4];
-#pragma unroll
-                for (int i = 0; i < 4; i++) P[i] = pack4<FAST>(cur[h][i], inv);  // row 4gi+i, columns 4c4..+3
-                const uint32_t t0 = __byte_perm(P[0], P[1], 0x5140), t1 = __byte_perm(P[0], P[1], 0x7362);
-                const uint32_t t2 = __byte_perm(P[2], P[3], 0x5140), t3 = __byte_perm(P[2], P[3], 0x7362);
-                uint4 cols;  // word j: rows 4gi..4gi+3 of column 4c4+j
-                cols.x = __byte_perm(t0, t2, 0x5410);
-                cols.y = __byte_perm(t0, t2, 0x7632);
-                cols.z = __byte_perm(t1, t3, 0x5410);
-                cols.w = __byte_perm(t1, t3, 0x7632);
-                *reinterpret_cast<uint4*>(stage + gi * kStageRow + 4 * c4) = cols;
-            }
-        }
-        __syncthreads();
-        // Bt row c0 + n receives `groups` (8 or 4) consecutive words at column r0,
-        // written as 16-byte pieces: piece q = (n, half), words 4*half..4*half+3
-        const uint32_t cols = 4 * g.cols4, hshift = groups == 8 ? 1 : 0;
-        for (uint32_t q = threadIdx.x; q < (cols << hshift); q += kCoopThreads) {
-            const uint32_t n = q >> hshift, half = q & hshift;
-            const uint32_t* sp = stage + 4 * half * kStageRow + n;
-            const uint4 o = make_uint4(sp[0], sp[kStageRow], sp[2 * kStageRow], sp[3 * kStageRow]);
-            *reinterpret_cast<uint4*>(Bt + (size_t)(g.c0 + n) * K + g.r0 + 16 * half) = o;
-        }
-        __syncthreads();  // stage is rewritten by the next unit
+        unit_codes_out<FAST>(cur, b_unit(u, nch, K, N), c4, rg, stage, Bt, K, inv);
 #pragma unroll
         for (int h = 0; h < 2; h++)
 #pragma unroll
             for (int i = 0; i < 4; i++) cur[h][i] = nxt[h][i];
     }
+    return true;
 }
 
 __device__ float global_absmax(const float* __restrict__ partials, unsigned int n) {
@@ -356,15 +415,19 @@ __device__ __forceinline__ uint32_t exchange_absmax(const CoopRanks& xr, uint32_
 __global__ void __launch_bounds__(kCoopThreads, 1)
     prologue_coop_kernel(const float* __restrict__ A, const float* __restrict__ B, int8_t* __restrict__ Aq,
                          int8_t* __restrict__ Bt, uint32_t M, uint32_t N, uint32_t K, float* __restrict__ scales,
-                         float* __restrict__ partials, CoopRanks xr, int* err) {
-    extern __shared__ __align__(16) float4 cache[];
+                         float* __restrict__ partials, CoopRanks xr, const __grid_constant__ CUtensorMap bmap,
+                         uint32_t use_tma, int* err) {
+    extern __shared__ __align__(128) float4 cache[];  // 128-byte aligned: TMA destination
     __shared__ __align__(16) uint32_t stage[kUnitRows / 4 * kStageRow];
+    __shared__ uint64_t tbar[kCacheSlots];  // B units refilled into the cache slots
     __shared__ uint32_t tag_s;
     __shared__ int fail_s;
     const unsigned int G = gridDim.x, c = blockIdx.x;
     if (threadIdx.x == 0) {
         tag_s = xr.world > 1 ? *reinterpret_cast<volatile uint32_t*>(xr.ctl) + 1u : 0u;
         fail_s = 0;
+        for (uint32_t i = 0; i < kCacheSlots; i++) ptx::mbar_init(&tbar[i], 1);
+        ptx::fence_mbarrier_init();
     }
     __syncthreads();
     const uint32_t tag = tag_s;
@@ -445,10 +508,11 @@ __global__ void __launch_bounds__(kCoopThreads, 1)
     __syncthreads();
     if (fail_s) return;
     if (c == 0 && threadIdx.x == 0) scales[1] = scale;
-    if (fast_inv(inv))
-        quantize_units_transposed<true>(B4, N4, K, N, nch, ub0, ub1, cache, stage, Bt, inv);
-    else
-        quantize_units_transposed<false>(B4, N4, K, N, nch, ub0, ub1, cache, stage, Bt, inv);
+    const CUtensorMap* bm = use_tma ? &bmap : nullptr;
+    const bool done = fast_inv(inv)
+                          ? quantize_units_transposed<true>(B4, N4, K, N, nch, ub0, ub1, cache, stage, Bt, inv, bm, tbar, err)
+                          : quantize_units_transposed<false>(B4, N4, K, N, nch, ub0, ub1, cache, stage, Bt, inv, bm, tbar, err);
+    if (!done) return;
     // this call is finished on this CTA; the last CTA of this GPU bumps the call count
     if (xr.world > 1 && threadIdx.x == 0) {
         const uint32_t prev = atomicAdd(xr.ctl + 1, 1u);
@@ -499,8 +563,20 @@ int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, con
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, prologue_coop_kernel, A, B, Aq, Bt, M, N, K, scales, partials, xr,
-                                    device_timeout_flag()));
+    // B as (256 columns, N / 256 column halves, K rows): one 256 x 2 x 32 box is a
+    // whole B unit (32 rows x 512 columns) in the shared-memory layout of the cache
+    CUtensorMap bmap;
+    memset(&bmap, 0, sizeof(bmap));
+    uint32_t use_tma = 0;
+    if (N % 256 == 0) {
+        const uint64_t dims[3] = {256, N / 256, K}, strides[2] = {1024, (uint64_t)N * 4};
+        const uint32_t box[3] = {256, 2, kUnitRows};
+        int rc = encode_tensor_map_3d(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, B, dims, strides, box);
+        if (rc) return rc;
+        use_tma = 1;
+    }
+    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, prologue_coop_kernel, A, B, Aq, Bt, M, N, K, scales, partials, xr, bmap,
+                                    use_tma, device_timeout_flag()));
     ANE_CHECK_LAUNCH();
     return ANE_OK;
 }
