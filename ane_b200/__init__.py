@@ -53,6 +53,12 @@ SIGNATURES = {
     "ane_dense_u8s8": (_i32, [_u32, _u32, _u32, _f, _f, _u8, _vp, _vp, _vp, _vp]),
     "ane_get_rows_q8_0": (_i32, [_u32, _u32, _vp, _vp, _vp]),
     "ane_q4_0_gemv": (_i32, [_u32, _u32, _vp, _vp, _vp]),
+    "ane_get_rows_q4_0": (_i32, [_u32, _u32, _vp, _vp, _vp]),
+    "ane_q4_k_gemv": (_i32, [_u32, _u32, _vp, _vp, _vp]),
+    "ane_q2_k_gemv": (_i32, [_u32, _u32, _vp, _vp, _vp]),
+    "ane_q3_k_gemv": (_i32, [_u32, _u32, _vp, _vp, _vp]),
+    "ane_q5_k_gemv": (_i32, [_u32, _u32, _vp, _vp, _vp]),
+    "ane_q6_k_gemv": (_i32, [_u32, _u32, _vp, _vp, _vp]),
     "ane_elementwise_scaled_add_fp32": (_i32, [_u32, _f, _vp, _vp, _vp]),
     "ane_relu_backward_fp32": (_i32, [_u32, _vp, _vp, _vp]),
     "ane_transpose_fp32": (_i32, [_u32, _u32, _vp, _vp]),
@@ -68,6 +74,12 @@ SIGNATURES = {
     "ane_q4_0_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
     "ane_q4_0_gemv_ex_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _u32, _vp]),
     "ane_get_rows_q8_0_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
+    "ane_get_rows_q4_0_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
+    "ane_q4_k_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
+    "ane_q2_k_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
+    "ane_q3_k_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
+    "ane_q5_k_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
+    "ane_q6_k_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
     "ane_cblas_igemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
     "ane_cblas_ugemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
     "ane_cblas_usgemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
@@ -164,7 +176,13 @@ class Op(enum.IntEnum):
     cblas_igemm = 0x61
     cblas_ugemm = 0x62
     cblas_usgemm = 0x63
+    q4_k_gemv = 0x75
+    q2_k_gemv = 0x76
+    q3_k_gemv = 0x77
+    q5_k_gemv = 0x78
+    q6_k_gemv = 0x79
     get_rows_q8_0 = 0x7C
+    get_rows_q4_0 = 0x7D
     dense_fused_i8 = 0x80
 
 
@@ -393,6 +411,34 @@ def q4_0_gemv(W, x, M: int, K: int, out=None, stream=None, static_weights=False)
         out = torch.empty(M, dtype=torch.float32, device=x.device)
     check(_lib.ane_q4_0_gemv_ex_dev(M, K, x.data_ptr(), W.data_ptr(), out.data_ptr(),
                                     WEIGHTS_STATIC if static_weights else 0, _stream_ptr(stream)))
+    return out
+
+
+# K-quant super-block sizes (bytes per 256 weights), by format name
+KQUANT_BLOCK_BYTES = {"q2_k": 84, "q3_k": 110, "q4_k": 144, "q5_k": 176, "q6_k": 210}
+
+
+def kquant_gemv(fmt: str, W, x, M: int, K: int, out=None, stream=None):
+    """out[M] = K-quant matrix W (M rows of K/256 super-blocks of format `fmt`,
+    a key of KQUANT_BLOCK_BYTES; uint8 tensor) times fp32 x[K]."""
+    torch = _torch()
+    if fmt not in KQUANT_BLOCK_BYTES:
+        raise ValueError("unknown K-quant format %r" % (fmt,))
+    if out is None:
+        out = torch.empty(M, dtype=torch.float32, device=x.device)
+    fn = getattr(_lib, "ane_%s_gemv_dev" % fmt)
+    check(fn(M, K, x.data_ptr(), W.data_ptr(), out.data_ptr(), _stream_ptr(stream)))
+    return out
+
+
+def get_rows_q4_0(table, indices, dim: int, out=None, stream=None):
+    """Rows `indices` (uint32/int32 tensor) of a Q4_0 table, dequantized: out [n, dim]."""
+    torch = _torch()
+    n = indices.numel()
+    if out is None:
+        out = torch.empty((n, dim), dtype=torch.float32, device=table.device)
+    check(_lib.ane_get_rows_q4_0_dev(n, dim, table.data_ptr(), indices.data_ptr(), out.data_ptr(),
+                                     _stream_ptr(stream)))
     return out
 
 

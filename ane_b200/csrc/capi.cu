@@ -468,6 +468,38 @@ int ane_get_rows_q8_0_dev(uint32_t n_rows, uint32_t dim, const void* table, cons
     return rc ? rc : ok();
 }
 
+static int kquant_dev(uint32_t fmt, uint32_t M, uint32_t K, const float* in, const void* W, float* out,
+                      void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(M == 0 || (in && W && out), "k-quant gemv: NULL pointer");
+    int rc = launch_kquant_gemv(fmt, M, K, in, static_cast<const uint8_t*>(W), out, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+int ane_q4_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
+    return kquant_dev(0, M, K, in, W, out, stream);
+}
+int ane_q2_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
+    return kquant_dev(1, M, K, in, W, out, stream);
+}
+int ane_q3_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
+    return kquant_dev(2, M, K, in, W, out, stream);
+}
+int ane_q5_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
+    return kquant_dev(3, M, K, in, W, out, stream);
+}
+int ane_q6_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
+    return kquant_dev(4, M, K, in, W, out, stream);
+}
+
+int ane_get_rows_q4_0_dev(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out,
+                          void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(n_rows == 0 || dim == 0 || (table && indices && out), "get_rows_q4_0: NULL pointer");
+    int rc = launch_get_rows_q4_0(n_rows, dim, static_cast<const uint8_t*>(table), indices, out,
+                                  static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
 int ane_q4_0_gemv_ex_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, uint32_t flags,
                          void* stream) {
     ANE_REQUIRE_GPU();
@@ -887,6 +919,58 @@ int ane_q4_0_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float*
                              {out, (size_t)M * 4, false, true}};
     return run_staged(args, 0, [&](cudaStream_t s, void*) {
         return launch_q4_0_gemv(M, K, (const float*)args[0].dev, (const uint8_t*)args[1].dev, (float*)args[2].dev, 0, s);
+    });
+}
+
+static int kquant_host(uint32_t fmt, uint32_t M, uint32_t K, const float* in, const void* W, float* out) {
+    ANE_REQUIRE_GPU();
+    if (M == 0) return ok();
+    ANE_ARG_CHECK(in && W && out, "k-quant gemv: NULL pointer");
+    const size_t nsb = K / 256;
+    std::vector<Arg> args = {{in, nsb > 0 ? nsb * 256 * 4 : 4, true, false},
+                             {W, nsb > 0 ? (size_t)M * nsb * kquant_block_bytes(fmt) : 4, true, false},
+                             {out, (size_t)M * 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_kquant_gemv(fmt, M, K, (const float*)args[0].dev, (const uint8_t*)args[1].dev,
+                                  (float*)args[2].dev, s);
+    });
+}
+int ane_q4_k_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out) {
+    return kquant_host(0, M, K, in, W, out);
+}
+int ane_q2_k_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out) {
+    return kquant_host(1, M, K, in, W, out);
+}
+int ane_q3_k_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out) {
+    return kquant_host(2, M, K, in, W, out);
+}
+int ane_q5_k_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out) {
+    return kquant_host(3, M, K, in, W, out);
+}
+int ane_q6_k_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out) {
+    return kquant_host(4, M, K, in, W, out);
+}
+
+int ane_get_rows_q4_0(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(dim % 32 == 0, "get_rows_q4_0: dim must be a multiple of 32");
+    if (n_rows == 0 || dim == 0) return ok();
+    ANE_ARG_CHECK(table && indices && out, "get_rows_q4_0: NULL pointer");
+    // the table has no size in the reference's encoding: copy rows up to the largest index
+    uint32_t max_idx = 0;
+    if (device_accessible(indices) && !device_accessible(table)) {
+        set_status(ANE_ERR_INVALID_ARGUMENT, "get_rows_q4_0: host table with device indices");
+        return ANE_ERR_INVALID_ARGUMENT;
+    }
+    if (!device_accessible(table))
+        for (uint32_t r = 0; r < n_rows; r++) max_idx = indices[r] > max_idx ? indices[r] : max_idx;
+    const size_t row_bytes = (size_t)(dim / 32) * 18;
+    std::vector<Arg> args = {{table, device_accessible(table) ? 1 : ((size_t)max_idx + 1) * row_bytes, true, false},
+                             {indices, (size_t)n_rows * 4, true, false},
+                             {out, (size_t)n_rows * dim * 4, false, true}};
+    return run_staged(args, 0, [&](cudaStream_t s, void*) {
+        return launch_get_rows_q4_0(n_rows, dim, (const uint8_t*)args[0].dev, (const uint32_t*)args[1].dev,
+                                    (float*)args[2].dev, s);
     });
 }
 

@@ -1,0 +1,274 @@
+// kquant_gemv.cu -- the K-quant matvecs q4_k_gemv (0x75), q2_k_gemv (0x76),
+// q3_k_gemv (0x77), q5_k_gemv (0x78), q6_k_gemv (0x79)
+// (src/bytecode_interpreter.s:11024-11620) and get_rows_q4_0 (0x7D, :12419-12466).
+//
+// Arithmetic of every matvec handler: rows of K/256 super-blocks; 16
+// accumulator lanes, lane l taking element l of every 16-element chunk of the
+// row in order with one fused multiply-add; the row result is the FADDV tree
+// ((a0+a1)+(a2+a3))+... over the 16 lanes.  Element values are computed with the
+// handler's separately rounded operations (integer -> float exact, one multiply
+// by the sub-block scale, one add of the sub-block min where the format has
+// one).  The byte layouts are the handlers' own, including q3_k's stale shift
+// vector: its second 16 elements of every 32-element sub-block shift the packed
+// 2-bit codes right first by the bit pattern of the x values the first half
+// loaded (shifts >= 32 give 0, as SVE LSR does), then by 2l.
+//
+// Threads: 8 per row, thread t holding lanes 2t and 2t+1 (the first FADDV level
+// in-thread, the other three by xor shuffles 1, 2, 4) -- the q4_0 / q8_0 mode-R
+// lane mapping; 4 rows per warp.  Loads follow each format's alignment (144-
+// and 176-byte super-blocks keep 16-byte alignment, 84-byte ones 4-byte,
+// 110- and 210-byte ones only 2-byte).
+#include <cuda_fp16.h>
+
+#include "ane_internal.cuh"
+#include "sm100_ptx.cuh"
+
+namespace ane_b200 {
+namespace {
+
+enum KFormat { kQ4K = 0, kQ2K = 1, kQ3K = 2, kQ5K = 3, kQ6K = 4 };
+
+template <int F>
+struct KBlock;
+template <>
+struct KBlock<kQ4K> {
+    static constexpr uint32_t bytes = 144;
+};
+template <>
+struct KBlock<kQ2K> {
+    static constexpr uint32_t bytes = 84;
+};
+template <>
+struct KBlock<kQ3K> {
+    static constexpr uint32_t bytes = 110;
+};
+template <>
+struct KBlock<kQ5K> {
+    static constexpr uint32_t bytes = 176;
+};
+template <>
+struct KBlock<kQ6K> {
+    static constexpr uint32_t bytes = 210;
+};
+
+__device__ __forceinline__ float h2f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }
+__device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) { return *reinterpret_cast<const unsigned short*>(p); }
+__device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t* p) { return ld_u16(p) | (ld_u16(p + 2) << 16); }
+
+// 6-bit scale and min of sub-block j from the 12 packed bytes s (q4_k / q5_k)
+__device__ __forceinline__ void k_scale_min(const uint8_t* s, uint32_t j, uint32_t& sc, uint32_t& m) {
+    if (j < 4) {
+        sc = s[j] & 0x3Fu;
+        m = s[j + 4] & 0x3Fu;
+    } else {
+        sc = (s[j + 4] & 0x0Fu) | ((uint32_t)(s[j - 4] >> 6) << 4);
+        m = (uint32_t)(s[j + 4] >> 4) | ((uint32_t)(s[j] >> 6) << 4);
+    }
+}
+
+// value = RN(RN(q * dsc) + dmm), accumulated with one fma
+__device__ __forceinline__ float kq_min_term(float acc, uint32_t q, float dsc, float dmm, float x) {
+    return __fmaf_rn(__fadd_rn(__fmul_rn((float)q, dsc), dmm), x, acc);
+}
+// value = RN(q * dsc) (signed q), accumulated with one fma
+__device__ __forceinline__ float kq_term(float acc, int32_t q, float dsc, float x) {
+    return __fmaf_rn(__fmul_rn((float)q, dsc), x, acc);
+}
+
+// One super-block of a row for thread t's lanes 2t (a0) and 2t+1 (a1).
+template <int F>
+__device__ __forceinline__ void kq_superblock(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
+                                              uint32_t t, float& a0, float& a1);
+
+template <>
+__device__ __forceinline__ void kq_superblock<kQ4K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
+                                                    uint32_t t, float& a0, float& a1) {
+    const float d = h2f(ld_u16(blk)), nd = -h2f(ld_u16(blk + 2));
+    const uint8_t* qs = blk + 16;
+#pragma unroll
+    for (uint32_t j = 0; j < 8; j++) {
+        uint32_t sc, mn;
+        k_scale_min(blk + 4, j, sc, mn);
+        const float dsc = __fmul_rn(d, (float)sc), dmm = __fmul_rn(nd, (float)mn);
+        const uint32_t b = ld_u16(qs + 16 * j + 2 * t);  // bytes of lanes 2t, 2t+1
+        const float2 xl = *reinterpret_cast<const float2*>(xb + 32 * j + 2 * t);
+        const float2 xh = *reinterpret_cast<const float2*>(xb + 32 * j + 16 + 2 * t);
+        a0 = kq_min_term(a0, b & 0x0Fu, dsc, dmm, xl.x);
+        a1 = kq_min_term(a1, (b >> 8) & 0x0Fu, dsc, dmm, xl.y);
+        a0 = kq_min_term(a0, (b >> 4) & 0x0Fu, dsc, dmm, xh.x);
+        a1 = kq_min_term(a1, (b >> 12) & 0x0Fu, dsc, dmm, xh.y);
+    }
+}
+
+template <>
+__device__ __forceinline__ void kq_superblock<kQ2K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
+                                                    uint32_t t, float& a0, float& a1) {
+    const uint32_t dd = *reinterpret_cast<const uint32_t*>(blk + 80);
+    const float d = h2f(dd & 0xFFFFu), nd = -h2f(dd >> 16);
+#pragma unroll
+    for (uint32_t j = 0; j < 16; j++) {
+        const uint32_t s = blk[j];
+        const float dsc = __fmul_rn(d, (float)(s & 0x0Fu)), dmm = __fmul_rn(nd, (float)(s >> 4));
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(blk + 16 + 4 * j);
+        const float2 xv = *reinterpret_cast<const float2*>(xb + 16 * j + 2 * t);
+        a0 = kq_min_term(a0, (w >> (4 * t)) & 3u, dsc, dmm, xv.x);
+        a1 = kq_min_term(a1, (w >> (4 * t + 2)) & 3u, dsc, dmm, xv.y);
+    }
+}
+
+template <>
+__device__ __forceinline__ void kq_superblock<kQ3K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
+                                                    uint32_t t, float& a0, float& a1) {
+    const uint8_t *hm = blk, *qs = blk + 32, *sc = blk + 96;
+    const float d = h2f(ld_u16(blk + 108));
+    const uint32_t l0 = 2 * t, l1 = 2 * t + 1;
+#pragma unroll
+    for (uint32_t j = 0; j < 8; j++) {
+        const uint32_t s6 = j < 4 ? (sc[j] & 0x3Fu) : ((sc[j + 4] & 0x0Fu) | ((uint32_t)(sc[j - 4] >> 6) << 4));
+        const float dsc = __fmul_rn(d, (float)((int32_t)s6 - 32));
+        const uint32_t w0 = ld_u32_a2(qs + 8 * j), h0 = ld_u16(hm + 4 * j);
+        const float2 xl = *reinterpret_cast<const float2*>(xb + 32 * j + 2 * t);
+        const float2 xh = *reinterpret_cast<const float2*>(xb + 32 * j + 16 + 2 * t);
+        const uint32_t q00 = ((w0 >> (2 * l0)) & 3u) | (((h0 >> l0) & 1u) << 2);
+        const uint32_t q01 = ((w0 >> (2 * l1)) & 3u) | (((h0 >> l1) & 1u) << 2);
+        a0 = kq_term(a0, (int32_t)q00 - 4, dsc, xl.x);
+        a1 = kq_term(a1, (int32_t)q01 - 4, dsc, xl.y);
+        // second half: the stale shift by the first half's x bits, then by 2l
+        const uint32_t w1 = ld_u32_a2(qs + 8 * j + 4), h1 = ld_u16(hm + 4 * j + 2);
+        const uint32_t s0 = __float_as_uint(xl.x), s1 = __float_as_uint(xl.y);
+        const uint32_t t0 = s0 >= 32u ? 0u : (w1 >> s0), t1 = s1 >= 32u ? 0u : (w1 >> s1);
+        const uint32_t q10 = ((t0 >> (2 * l0)) & 3u) | (((h1 >> l0) & 1u) << 2);
+        const uint32_t q11 = ((t1 >> (2 * l1)) & 3u) | (((h1 >> l1) & 1u) << 2);
+        a0 = kq_term(a0, (int32_t)q10 - 4, dsc, xh.x);
+        a1 = kq_term(a1, (int32_t)q11 - 4, dsc, xh.y);
+    }
+}
+
+template <>
+__device__ __forceinline__ void kq_superblock<kQ5K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
+                                                    uint32_t t, float& a0, float& a1) {
+    const float d = h2f(ld_u16(blk)), nd = -h2f(ld_u16(blk + 2));
+    const uint8_t *qh = blk + 16, *qs = blk + 48;
+    const uint32_t l0 = 2 * t, l1 = 2 * t + 1;
+#pragma unroll
+    for (uint32_t j = 0; j < 8; j++) {
+        uint32_t sc, mn;
+        k_scale_min(blk + 4, j, sc, mn);
+        const float dsc = __fmul_rn(d, (float)sc), dmm = __fmul_rn(nd, (float)mn);
+        const uint32_t h = *reinterpret_cast<const uint32_t*>(qh + 4 * j);
+        const uint32_t b = ld_u16(qs + 16 * j + 2 * t);
+        const float2 xl = *reinterpret_cast<const float2*>(xb + 32 * j + 2 * t);
+        const float2 xh = *reinterpret_cast<const float2*>(xb + 32 * j + 16 + 2 * t);
+        a0 = kq_min_term(a0, (b & 0x0Fu) | (((h >> l0) & 1u) << 4), dsc, dmm, xl.x);
+        a1 = kq_min_term(a1, ((b >> 8) & 0x0Fu) | (((h >> l1) & 1u) << 4), dsc, dmm, xl.y);
+        a0 = kq_min_term(a0, ((b >> 4) & 0x0Fu) | (((h >> (16 + l0)) & 1u) << 4), dsc, dmm, xh.x);
+        a1 = kq_min_term(a1, ((b >> 12) & 0x0Fu) | (((h >> (16 + l1)) & 1u) << 4), dsc, dmm, xh.y);
+    }
+}
+
+template <>
+__device__ __forceinline__ void kq_superblock<kQ6K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
+                                                    uint32_t t, float& a0, float& a1) {
+    const uint8_t *ql = blk, *qh = blk + 128;
+    const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
+    const float d = h2f(ld_u16(blk + 208));
+#pragma unroll
+    for (uint32_t j = 0; j < 16; j++) {
+        const float dsc = __fmul_rn(d, (float)sc[j]);
+        const uint32_t h = ld_u32_a2(qh + 4 * j);
+        const uint32_t b = ql[8 * j + t];  // element 2t: low nibble, 2t+1: high nibble
+        const float2 xv = *reinterpret_cast<const float2*>(xb + 16 * j + 2 * t);
+        const uint32_t q0 = (b & 0x0Fu) | (((h >> (4 * t)) & 3u) << 4);
+        const uint32_t q1 = (b >> 4) | (((h >> (4 * t + 2)) & 3u) << 4);
+        a0 = kq_term(a0, (int32_t)q0 - 32, dsc, xv.x);
+        a1 = kq_term(a1, (int32_t)q1 - 32, dsc, xv.y);
+    }
+}
+
+template <int F>
+__global__ void __launch_bounds__(256) kquant_gemv_kernel(const float* __restrict__ x, const uint8_t* __restrict__ W,
+                                                          float* __restrict__ out, uint32_t M, uint32_t nsb) {
+    const uint32_t row = blockIdx.x * (blockDim.x / 8) + threadIdx.x / 8, t = threadIdx.x % 8;
+    float a0 = 0.0f, a1 = 0.0f;
+    if (row < M) {
+        const uint8_t* rp = W + (size_t)row * nsb * KBlock<F>::bytes;
+        for (uint32_t b = 0; b < nsb; b++) kq_superblock<F>(rp + (size_t)b * KBlock<F>::bytes, x + 256 * b, t, a0, a1);
+    }
+    // FADDV: level 1 in-thread (lanes 2t, 2t+1), levels 2-4 across the row's 8 threads
+    float s = __fadd_rn(a0, a1);
+    s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
+    s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 2));
+    s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 4));
+    if (row < M && t == 0) out[row] = s;
+}
+
+// get_rows_q4_0: one thread per (row, block, i < 16): elements i and 16 + i.
+__global__ void get_rows_q4_0_kernel(uint32_t n_rows, uint32_t nb, const uint8_t* __restrict__ table,
+                                     const uint32_t* __restrict__ idx, float* __restrict__ out) {
+    const size_t n = (size_t)n_rows * nb * 16;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t e = (uint32_t)(i % 16);
+        const size_t rb = i / 16;
+        const uint32_t r = (uint32_t)(rb / nb), b = (uint32_t)(rb % nb);
+        const uint8_t* blk = table + ((size_t)idx[r] * nb + b) * 18;
+        const float d = h2f(ld_u16(blk));
+        const uint32_t q = blk[2 + e];
+        float* o = out + (size_t)r * nb * 32 + (size_t)b * 32;
+        o[e] = __fmul_rn((float)((int32_t)(q & 0x0Fu) - 8), d);
+        o[16 + e] = __fmul_rn((float)((int32_t)(q >> 4) - 8), d);
+    }
+}
+
+}  // namespace
+
+uint32_t kquant_block_bytes(uint32_t fmt) {
+    switch (fmt) {
+        case kQ4K: return KBlock<kQ4K>::bytes;
+        case kQ2K: return KBlock<kQ2K>::bytes;
+        case kQ3K: return KBlock<kQ3K>::bytes;
+        case kQ5K: return KBlock<kQ5K>::bytes;
+        case kQ6K: return KBlock<kQ6K>::bytes;
+        default: return 0;
+    }
+}
+
+int launch_kquant_gemv(uint32_t fmt, uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out,
+                       cudaStream_t s) {
+    ANE_ARG_CHECK(fmt <= kQ6K, "kquant_gemv: unknown format");
+    if (M == 0) return ANE_OK;
+    // float2 loads of x; the widest aligned weight load per format (16-byte
+    // super-blocks: 4-byte words; 84-byte: 4-byte; 110 / 210-byte: 2-byte)
+    const uint32_t wal = (fmt == kQ3K || fmt == kQ6K) ? 2u : 4u;
+    ANE_ARG_CHECK(((uintptr_t)x & 7) == 0 && ((uintptr_t)W & (wal - 1)) == 0,
+                  "kquant_gemv: x must be 8-byte aligned, W 4-byte (2-byte for q3_k / q6_k)");
+    const uint32_t nsb = K / 256;  // the handlers run floor(K / 256) super-blocks (lsr #8)
+    if (nsb == 0) {
+        ANE_CUDA_TRY(cudaMemsetAsync(out, 0, (size_t)M * 4, s));
+        return ANE_OK;
+    }
+    const dim3 grid((M + 31) / 32), block(256);
+    switch (fmt) {
+        case kQ4K: kquant_gemv_kernel<kQ4K><<<grid, block, 0, s>>>(x, W, out, M, nsb); break;
+        case kQ2K: kquant_gemv_kernel<kQ2K><<<grid, block, 0, s>>>(x, W, out, M, nsb); break;
+        case kQ3K: kquant_gemv_kernel<kQ3K><<<grid, block, 0, s>>>(x, W, out, M, nsb); break;
+        case kQ5K: kquant_gemv_kernel<kQ5K><<<grid, block, 0, s>>>(x, W, out, M, nsb); break;
+        default: kquant_gemv_kernel<kQ6K><<<grid, block, 0, s>>>(x, W, out, M, nsb); break;
+    }
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
+
+int launch_get_rows_q4_0(uint32_t n_rows, uint32_t dim, const uint8_t* table, const uint32_t* idx, float* out,
+                         cudaStream_t s) {
+    const uint32_t nb = dim / 32;
+    if (n_rows == 0 || nb == 0) return ANE_OK;
+    const size_t n = (size_t)n_rows * nb * 16;
+    size_t g = (n + 255) / 256;
+    const size_t cap = (size_t)num_sms() * 16;
+    if (g > cap) g = cap;
+    get_rows_q4_0_kernel<<<(unsigned)g, 256, 0, s>>>(n_rows, nb, table, idx, out);
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
+
+}  // namespace ane_b200

@@ -57,7 +57,13 @@ int payload_size(uint8_t op) {
         case 0x63: return 1 + 12 + 12 + 8 + 24;
         case 0x57: return 8 + 24;           // q8_0_gemv: M K in W out
         case 0x58: return 8 + 24;           // q4_0_gemv: M K in W out
+        case 0x75:                          // q4_k_gemv: M K in W out
+        case 0x76:                          // q2_k_gemv
+        case 0x77:                          // q3_k_gemv
+        case 0x78:                          // q5_k_gemv
+        case 0x79: return 8 + 24;           // q6_k_gemv
         case 0x7C: return 8 + 24;           // get_rows_q8_0: n_rows dim table indices out
+        case 0x7D: return 8 + 24;           // get_rows_q4_0: n_rows dim table indices out
         case 0x80: return 12 + 4 + 1 + 24;  // dense_fused_i8: M N K scale relu A B C
         default: return -1;
     }
@@ -140,6 +146,30 @@ int exec_one(uint8_t op, Reader& r) {
             const void* W = r.ptr<const void>();
             float* out = r.ptr<float>();
             return ane_q4_0_gemv(M, K, in, W, out);
+        }
+        case 0x75:
+        case 0x76:
+        case 0x77:
+        case 0x78:
+        case 0x79: {
+            uint32_t M = r.get<uint32_t>(), K = r.get<uint32_t>();
+            const float* in = r.ptr<const float>();
+            const void* W = r.ptr<const void>();
+            float* out = r.ptr<float>();
+            switch (op) {
+                case 0x75: return ane_q4_k_gemv(M, K, in, W, out);
+                case 0x76: return ane_q2_k_gemv(M, K, in, W, out);
+                case 0x77: return ane_q3_k_gemv(M, K, in, W, out);
+                case 0x78: return ane_q5_k_gemv(M, K, in, W, out);
+                default: return ane_q6_k_gemv(M, K, in, W, out);
+            }
+        }
+        case 0x7D: {
+            uint32_t n_rows = r.get<uint32_t>(), dim = r.get<uint32_t>();
+            const void* table = r.ptr<const void>();
+            const uint32_t* indices = r.ptr<const uint32_t>();
+            float* out = r.ptr<float>();
+            return ane_get_rows_q4_0(n_rows, dim, table, indices, out);
         }
         case 0x7C: {
             uint32_t n_rows = r.get<uint32_t>(), dim = r.get<uint32_t>();

@@ -120,6 +120,25 @@ int ane_q4_0_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float*
  * block b of table row indices[r] (u32 indices; dim % 32 == 0).  With a host
  * table the rows up to the largest index are copied to the device. */
 int ane_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out);
+/* get_rows_q4_0 (0x7D; :12419-12466): out[r][32b+i] = (low nibble of byte i - 8)
+ * * float(d), out[r][32b+16+i] = (high nibble - 8) * float(d), block b of table
+ * row indices[r] (18-byte Q4_0 blocks; dim % 32 == 0). */
+int ane_get_rows_q4_0(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out);
+/* K-quant matvecs, out[M] = W x in for rows of floor(K/256) super-blocks:
+ *   q4_k_gemv (0x75; :11024-11133) 144 B {fp16 d, fp16 dmin, scales[12], qs[128]}
+ *   q2_k_gemv (0x76; :11146-11224)  84 B {scales[16], qs[64], fp16 d, fp16 dmin}
+ *   q3_k_gemv (0x77; :11236-11360) 110 B {hmask[32], qs[64], scales[12], fp16 d}
+ *   q5_k_gemv (0x78; :11372-11486) 176 B {fp16 d, fp16 dmin, scales[12], qh[32], qs[128]}
+ *   q6_k_gemv (0x79; :11498-11606) 210 B {ql[128], qh[64], int8 scales[16], fp16 d}
+ * Bit-exact with the handlers: their element layouts and value arithmetic
+ * (including q3_k's shift of its second-half codes by the first half's x bits),
+ * 16-lane FMA order and FADDV tree.  x 8-byte aligned; W 4-byte aligned (2-byte
+ * for q3_k and q6_k). */
+int ane_q4_k_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out);
+int ane_q2_k_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out);
+int ane_q3_k_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out);
+int ane_q5_k_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out);
+int ane_q6_k_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out);
 /* dense_fused_i8 (0x80, new; README.md:87-97 usage).  fp32 A (M x K, stride K)
  * and B (K x N, stride N) quantized per tensor to int8 (absmax/127), int8 x int8
  * -> exact int32, y = float(acc)*(sa*sb), y = y*scale, optional ReLU; C is
@@ -177,6 +196,13 @@ int ane_q8_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, fl
 int ane_get_rows_q8_0_dev(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out,
                           void* stream);
 int ane_q4_0_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream);
+int ane_get_rows_q4_0_dev(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out,
+                          void* stream);
+int ane_q4_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream);
+int ane_q2_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream);
+int ane_q3_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream);
+int ane_q5_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream);
+int ane_q6_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream);
 int ane_elementwise_scaled_add_fp32_dev(uint32_t count, float scale, const float* a, const float* b, float* out,
                                         void* stream);
 int ane_relu_backward_fp32_dev(uint32_t count, const float* act, const float* grad, float* out, void* stream);

@@ -60,6 +60,12 @@ def lib():
             "ane_ref_dense_fused_epilogue": (None, [_u32, _u32, _i32p, _f, _f, _f, ctypes.c_int, _f32p]),
             "ane_ref_q8_0_gemv": (None, [_u32, _u32, _f32p, _u8p, _f32p]),
             "ane_ref_q4_0_gemv": (None, [_u32, _u32, _f32p, _u8p, _f32p]),
+            "ane_ref_q4_k_gemv": (None, [_u32, _u32, _f32p, _u8p, _f32p]),
+            "ane_ref_q2_k_gemv": (None, [_u32, _u32, _f32p, _u8p, _f32p]),
+            "ane_ref_q3_k_gemv": (None, [_u32, _u32, _f32p, _u8p, _f32p]),
+            "ane_ref_q5_k_gemv": (None, [_u32, _u32, _f32p, _u8p, _f32p]),
+            "ane_ref_q6_k_gemv": (None, [_u32, _u32, _f32p, _u8p, _f32p]),
+            "ane_ref_get_rows_q4_0": (None, [_u32, _u32, _u8p, _u32p, _f32p]),
             "ane_ref_quantize_q8_0": (None, [_f32p, _u8p, _sz, _sz]),
             "ane_ref_q8_0_gemv_q8": (None, [_u32, _u32, _u8p, _u8p, _f32p, _vp]),
             "ane_ref_get_rows_q8_0": (None, [_u32, _u32, _u8p, _u32p, _f32p]),
@@ -223,6 +229,18 @@ def q4_0_gemv(W_blocks, x, M: int, K: int):
     return out
 
 
+# K-quant super-block sizes (bytes per 256 weights), by format name
+KQUANT_BLOCK_BYTES = {"q2_k": 84, "q3_k": 110, "q4_k": 144, "q5_k": 176, "q6_k": 210}
+
+
+def kquant_gemv(fmt: str, W_blocks, x, M: int, K: int):
+    """out[M] = K-quant matrix W (M rows of K/256 super-blocks) times fp32 x[K],
+    the reference handler's arithmetic (fmt in KQUANT_BLOCK_BYTES)."""
+    out = np.empty(M, np.float32)
+    getattr(lib(), "ane_ref_%s_gemv" % fmt)(M, K, _c(x, np.float32).ravel(), _c(W_blocks, np.uint8).ravel(), out)
+    return out
+
+
 def q8_0_gemv_omp(W_blocks, x, M: int, K: int, threads=0):
     out = np.empty(M, np.float32)
     lib().ane_ref_q8_0_gemv_omp(M, K, _c(x, np.float32).ravel(), _c(W_blocks, np.uint8).ravel(), out,
@@ -328,6 +346,13 @@ def get_rows_q8_0(table, indices, dim: int):
     idx = _c(indices, np.uint32).ravel()
     out = np.empty(idx.size * dim, np.float32)
     lib().ane_ref_get_rows_q8_0(idx.size, dim, _c(table, np.uint8).ravel(), idx, out)
+    return out.reshape(idx.size, dim)
+
+
+def get_rows_q4_0(table, indices, dim: int):
+    idx = _c(indices, np.uint32).ravel()
+    out = np.empty(idx.size * dim, np.float32)
+    lib().ane_ref_get_rows_q4_0(idx.size, dim, _c(table, np.uint8).ravel(), idx, out)
     return out.reshape(idx.size, dim)
 
 

@@ -487,6 +487,201 @@ void ane_ref_q4_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W,
     }
 }
 
+/* ------------------------------------------------------ K-quant matvecs
+ * q4_k / q2_k / q3_k / q5_k / q6_k _gemv (bytecode_interpreter.s:11024-11620):
+ * rows of K/256 super-blocks; 16 accumulator lanes, lane l taking every
+ * 16-element chunk's element l in row order with one fused multiply-add
+ * (fmla), the row = the FADDV tree.  Each element's value is computed with
+ * separately rounded operations exactly as the handlers do (ucvtf/scvtf exact,
+ * then fmul, then fadd where the format has a min term).  The layouts are the
+ * handlers' own (their comments name the ggml formats; the byte layouts below
+ * are what the code reads), including two of their quirks: q3_k's second half
+ * of every 32-element sub-block shifts its packed 2-bit codes right first by
+ * the bit pattern of the x values the first half loaded (a clobbered shift
+ * vector; SVE clamps shifts >= 32 to a zero result), and q6_k's value lanes
+ * 8..15 carry garbage that zip1 discards. */
+
+static inline uint32_t le16(const uint8_t* p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
+static inline uint32_t bits_of(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    return u;
+}
+static inline uint32_t le32(const uint8_t* p) { return le16(p) | (le16(p + 2) << 16); }
+
+/* 6-bit scale and min of sub-block j from the 12 packed bytes (q4_k :11052-11085,
+ * q5_k :11402-11423) */
+static inline void k_scale_min(const uint8_t* s, int j, uint32_t* sc, uint32_t* m) {
+    if (j < 4) {
+        *sc = s[j] & 0x3Fu;
+        *m = s[j + 4] & 0x3Fu;
+    } else {
+        *sc = (s[j + 4] & 0x0Fu) | ((uint32_t)(s[j - 4] >> 6) << 4);
+        *m = (uint32_t)(s[j + 4] >> 4) | ((uint32_t)(s[j] >> 6) << 4);
+    }
+}
+
+/* q4_k (:11024-11133): 144-byte super-blocks {fp16 d, fp16 dmin, scales[12], qs[128]};
+ * 8 sub-blocks of 32: element i < 16 = low nibble of qs[16j+i], 16+i = its high
+ * nibble; value RN(RN(q * RN(d*sc)) + RN(-dmin*m)). */
+void ane_ref_q4_k_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out) {
+    uint32_t nsb = K / 256;
+    for (uint32_t r = 0; r < M; r++) {
+        float acc[16] = {0};
+        for (uint32_t b = 0; b < nsb; b++) {
+            const uint8_t* blk = W + ((size_t)r * nsb + b) * 144;
+            float d = ane_ref_fp16_to_fp32((uint16_t)le16(blk));
+            float nd = -ane_ref_fp16_to_fp32((uint16_t)le16(blk + 2));  /* fneg */
+            const uint8_t* qs = blk + 16;
+            const float* xb = x + (size_t)b * 256;
+            for (int j = 0; j < 8; j++) {
+                uint32_t sc, mn;
+                k_scale_min(blk + 4, j, &sc, &mn);
+                float dsc = d * (float)sc, dmm = nd * (float)mn;
+                for (int l = 0; l < 16; l++) {
+                    float t = (float)(qs[16 * j + l] & 0x0F) * dsc;
+                    float v = t + dmm;
+                    acc[l] = fmaf(v, xb[32 * j + l], acc[l]);
+                }
+                for (int l = 0; l < 16; l++) {
+                    float t = (float)(qs[16 * j + l] >> 4) * dsc;
+                    float v = t + dmm;
+                    acc[l] = fmaf(v, xb[32 * j + 16 + l], acc[l]);
+                }
+            }
+        }
+        out[r] = faddv16(acc);
+    }
+}
+
+/* q2_k (:11146-11224): 84-byte super-blocks {scales[16], qs[64], fp16 d, fp16 dmin};
+ * 16 sub-blocks of 16: sc = scales[j] & 15, m = scales[j] >> 4, element l = bits
+ * 2l..2l+1 of the little-endian word qs[4j..4j+3]. */
+void ane_ref_q2_k_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out) {
+    uint32_t nsb = K / 256;
+    for (uint32_t r = 0; r < M; r++) {
+        float acc[16] = {0};
+        for (uint32_t b = 0; b < nsb; b++) {
+            const uint8_t* blk = W + ((size_t)r * nsb + b) * 84;
+            float d = ane_ref_fp16_to_fp32((uint16_t)le16(blk + 80));
+            float nd = -ane_ref_fp16_to_fp32((uint16_t)le16(blk + 82));
+            const float* xb = x + (size_t)b * 256;
+            for (int j = 0; j < 16; j++) {
+                float dsc = d * (float)(blk[j] & 0x0F), dmm = nd * (float)(blk[j] >> 4);
+                uint32_t w = le32(blk + 16 + 4 * j);
+                for (int l = 0; l < 16; l++) {
+                    float t = (float)((w >> (2 * l)) & 3u) * dsc;
+                    float v = t + dmm;
+                    acc[l] = fmaf(v, xb[16 * j + l], acc[l]);
+                }
+            }
+        }
+        out[r] = faddv16(acc);
+    }
+}
+
+/* q3_k (:11236-11360): 110-byte super-blocks {hmask[32], qs[64], scales[12], fp16 d};
+ * 8 sub-blocks of 32; scale s6 (the q4_k 6-bit scale rule) - 32, signed; code
+ * q = 2 low bits | hmask bit << 2, value RN((q - 4) * RN(d * (s6 - 32))). */
+void ane_ref_q3_k_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out) {
+    uint32_t nsb = K / 256;
+    for (uint32_t r = 0; r < M; r++) {
+        float acc[16] = {0};
+        for (uint32_t b = 0; b < nsb; b++) {
+            const uint8_t* blk = W + ((size_t)r * nsb + b) * 110;
+            const uint8_t *hm = blk, *qs = blk + 32, *sc = blk + 96;
+            float d = ane_ref_fp16_to_fp32((uint16_t)le16(blk + 108));
+            const float* xb = x + (size_t)b * 256;
+            for (int j = 0; j < 8; j++) {
+                uint32_t s6 = j < 4 ? (sc[j] & 0x3Fu) : ((sc[j + 4] & 0x0Fu) | ((uint32_t)(sc[j - 4] >> 6) << 4));
+                float dsc = d * (float)((int32_t)s6 - 32);
+                uint32_t w0 = le32(qs + 8 * j), h0 = le16(hm + 4 * j);
+                for (int l = 0; l < 16; l++) {
+                    uint32_t q = ((w0 >> (2 * l)) & 3u) | (((h0 >> l) & 1u) << 2);
+                    float v = (float)((int32_t)q - 4) * dsc;
+                    acc[l] = fmaf(v, xb[32 * j + l], acc[l]);
+                }
+                uint32_t w1 = le32(qs + 8 * j + 4), h1 = le16(hm + 4 * j + 2);
+                for (int l = 0; l < 16; l++) {
+                    /* lsr by the first half's x bits (the stale z1), then by 2l */
+                    uint32_t xs = bits_of(xb[32 * j + l]);
+                    uint32_t t = xs >= 32u ? 0u : (w1 >> xs);
+                    uint32_t q = ((t >> (2 * l)) & 3u) | (((h1 >> l) & 1u) << 2);
+                    float v = (float)((int32_t)q - 4) * dsc;
+                    acc[l] = fmaf(v, xb[32 * j + 16 + l], acc[l]);
+                }
+            }
+        }
+        out[r] = faddv16(acc);
+    }
+}
+
+/* q5_k (:11372-11486): 176-byte super-blocks {fp16 d, fp16 dmin, scales[12], qh[32],
+ * qs[128]}; q4_k's scales and nibbles, plus bit l (first half) or 16+l (second
+ * half) of the little-endian word qh[4j..4j+3] as bit 4. */
+void ane_ref_q5_k_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out) {
+    uint32_t nsb = K / 256;
+    for (uint32_t r = 0; r < M; r++) {
+        float acc[16] = {0};
+        for (uint32_t b = 0; b < nsb; b++) {
+            const uint8_t* blk = W + ((size_t)r * nsb + b) * 176;
+            float d = ane_ref_fp16_to_fp32((uint16_t)le16(blk));
+            float nd = -ane_ref_fp16_to_fp32((uint16_t)le16(blk + 2));
+            const uint8_t *qh = blk + 16, *qs = blk + 48;
+            const float* xb = x + (size_t)b * 256;
+            for (int j = 0; j < 8; j++) {
+                uint32_t sc, mn;
+                k_scale_min(blk + 4, j, &sc, &mn);
+                float dsc = d * (float)sc, dmm = nd * (float)mn;
+                uint32_t h = le32(qh + 4 * j);
+                for (int l = 0; l < 16; l++) {
+                    uint32_t q = (qs[16 * j + l] & 0x0Fu) | (((h >> l) & 1u) << 4);
+                    float t = (float)q * dsc;
+                    float v = t + dmm;
+                    acc[l] = fmaf(v, xb[32 * j + l], acc[l]);
+                }
+                for (int l = 0; l < 16; l++) {
+                    uint32_t q = (uint32_t)(qs[16 * j + l] >> 4) | (((h >> (16 + l)) & 1u) << 4);
+                    float t = (float)q * dsc;
+                    float v = t + dmm;
+                    acc[l] = fmaf(v, xb[32 * j + 16 + l], acc[l]);
+                }
+            }
+        }
+        out[r] = faddv16(acc);
+    }
+}
+
+/* q6_k (:11498-11606): 210-byte super-blocks {ql[128], qh[64], int8 scales[16],
+ * fp16 d}; 16 sub-blocks of 16: element n = nibble (low for even n, high for
+ * odd) of ql[8j + n/2] | bits 2n..2n+1 of the little-endian word qh[4j..4j+3]
+ * << 4; value RN((q - 32) * RN(d * scale)). */
+void ane_ref_q6_k_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out) {
+    uint32_t nsb = K / 256;
+    for (uint32_t r = 0; r < M; r++) {
+        float acc[16] = {0};
+        for (uint32_t b = 0; b < nsb; b++) {
+            const uint8_t* blk = W + ((size_t)r * nsb + b) * 210;
+            const uint8_t *ql = blk, *qh = blk + 128;
+            const int8_t* sc = (const int8_t*)(blk + 192);
+            float d = ane_ref_fp16_to_fp32((uint16_t)le16(blk + 208));
+            const float* xb = x + (size_t)b * 256;
+            for (int j = 0; j < 16; j++) {
+                float dsc = d * (float)sc[j];
+                uint32_t h = le32(qh + 4 * j);
+                for (int n = 0; n < 16; n++) {
+                    uint32_t byte = ql[8 * j + n / 2];
+                    uint32_t nib = (n & 1) ? (byte >> 4) : (byte & 0x0Fu);
+                    uint32_t q = nib | (((h >> (2 * n)) & 3u) << 4);
+                    float v = (float)((int32_t)q - 32) * dsc;
+                    acc[n] = fmaf(v, xb[16 * j + n], acc[n]);
+                }
+            }
+        }
+        out[r] = faddv16(acc);
+    }
+}
+
 void ane_ref_quantize_q8_0(const float* x, uint8_t* blocks, size_t n_rows, size_t K) {
     size_t nb = K / 32;
     for (size_t r = 0; r < n_rows; r++)
@@ -566,6 +761,25 @@ void ane_ref_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const uint8_t* table,
             float d = ane_ref_fp16_to_fp32((uint16_t)(blk[0] | (blk[1] << 8)));
             for (int j = 0; j < 32; j++)
                 out[(size_t)r * dim + b * 32 + j] = (float)(int8_t)blk[2 + j] * d;
+        }
+    }
+}
+
+void ane_ref_get_rows_q4_0(uint32_t n_rows, uint32_t dim, const uint8_t* table,
+                           const uint32_t* indices, float* out) {
+    /* bytecode_interpreter.s:12419-12466: 18-byte Q4_0 blocks; element i < 16 =
+     * (low nibble of byte i) - 8, element 16+i = (high nibble) - 8, times d
+     * (scvtf exact, one RN multiply). */
+    uint32_t nb = dim / 32;
+    for (uint32_t r = 0; r < n_rows; r++) {
+        const uint8_t* row = table + (size_t)indices[r] * nb * 18;
+        for (uint32_t b = 0; b < nb; b++) {
+            const uint8_t* blk = row + (size_t)b * 18;
+            float d = ane_ref_fp16_to_fp32((uint16_t)(blk[0] | (blk[1] << 8)));
+            for (int i = 0; i < 16; i++) {
+                out[(size_t)r * dim + b * 32 + i] = (float)((int32_t)(blk[2 + i] & 0x0F) - 8) * d;
+                out[(size_t)r * dim + b * 32 + 16 + i] = (float)((int32_t)(blk[2 + i] >> 4) - 8) * d;
+            }
         }
     }
 }

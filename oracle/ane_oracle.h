@@ -98,6 +98,12 @@ void ane_ref_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W,
  * byte i, element 16+i = high nibble, value (nibble - 8) * d; q8_0_gemv's lane
  * order and FADDV tree. */
 void ane_ref_q4_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out);
+/* K-quant matvecs (bytecode_interpreter.s:11024-11620), K % 256 == 0 */
+void ane_ref_q4_k_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out);
+void ane_ref_q2_k_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out);
+void ane_ref_q3_k_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out);
+void ane_ref_q5_k_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out);
+void ane_ref_q6_k_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out);
 
 /* ---- Q8_0 helpers ---------------------------------------------------------------
  * Quantize fp32 rows into Q8_0 blocks with the ggml rule: d = absmax/127,
@@ -142,6 +148,8 @@ void ane_ref_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const uint8
 
 /* ---- get_rows_q8_0 (0x7C) -------------------------------------------------------- */
 void ane_ref_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const uint8_t* table,
+                           const uint32_t* indices, float* out);
+void ane_ref_get_rows_q4_0(uint32_t n_rows, uint32_t dim, const uint8_t* table,
                            const uint32_t* indices, float* out);
 
 /* ---- OpenMP variants (CPU baseline; identical results) ---------------------------- */

@@ -55,7 +55,8 @@ def test_payload_size_table_matches_encoding():
     L = ane_b200.lib
     for op, n in [(0x18, 53), (0x19, 28), (0x1A, 24), (0x1B, 24), (0x1C, 32), (0x57, 32), (0x80, 41),
                   (0x1E, 53), (0x58, 32), (0x61, 57), (0x62, 57), (0x63, 57), (0x7C, 32),
-                  (0x0D, 32), (0x0F, 28), (0x11, 24), (0x12, 48), (0x15, 49), (0x16, 28)]:
+                  (0x0D, 32), (0x0F, 28), (0x11, 24), (0x12, 48), (0x15, 49), (0x16, 28),
+                  (0x75, 32), (0x76, 32), (0x77, 32), (0x78, 32), (0x79, 32), (0x7D, 32)]:
         assert L.ane_opcode_payload_size(op) == n, hex(op)
         assert L.ane_opcode_supported(op) == 1
     for op in (0x01, 0x14, 0x4D, 0x7A, 0x7F, 0xFF):

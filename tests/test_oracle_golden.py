@@ -344,3 +344,46 @@ def test_mnist_fp32_ops_oracle_sanity():
     onehot = np.zeros_like(probs)
     onehot[np.arange(50), labels] = 1
     assert np.array_equal(gout, (probs - onehot).astype(F32))
+
+
+# ------------------------------------------------ K-quant matvecs, get_rows_q4_0
+from kquant_util import BLOCK_BYTES, dequant_row, get_rows_q4_0_kat_tables, random_blocks  # noqa: E402
+
+
+def test_get_rows_q4_0_oracle_kat():
+    """The reference's get_rows_q4_0 test tables and expectations."""
+    for table, idx, dim, ref in get_rows_q4_0_kat_tables():
+        got = oracle.get_rows_q4_0(table, idx, dim)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("fmt", sorted(BLOCK_BYTES))
+def test_kquant_oracle_decoding_matches_numpy(fmt):
+    """The C oracle's layouts against an independent numpy dequantizer (float64
+    dot products, so a tolerance: the oracle's FMA order is checked on the GPU
+    side, bit for bit, and by the lane-order test below)."""
+    rng = np.random.default_rng(7)
+    M, K = 6, 512
+    W = random_blocks(fmt, M, K, rng)
+    x = rng.standard_normal(K).astype(np.float32)
+    x[3] = 0.0                                   # q3_k: a stale shift of 0 keeps the codes
+    x[40] = np.uint32(5).view(np.float32)        # a tiny denormal: shift by 5
+    got = oracle.kquant_gemv(fmt, W, x, M, K)
+    rows = W.reshape(M, -1)
+    for m in range(M):
+        ref = float(np.dot(dequant_row(fmt, rows[m], x), x.astype(np.float64)))
+        scale = float(np.abs(dequant_row(fmt, rows[m], x)).dot(np.abs(x.astype(np.float64)))) + 1e-30
+        assert abs(float(got[m]) - ref) <= 1e-5 * scale, (fmt, m, got[m], ref)
+
+
+def test_kquant_oracle_lane_order():
+    """One nonzero lane of the 16: the FADDV tree and lane FMA chains reduce to
+    that lane's fused chain; a q4_k row with a single 1.0 weight at element e
+    returns x[e] exactly."""
+    K = 256
+    W = np.zeros(144, np.uint8)
+    W[0:2] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)   # d = 1, dmin = 0
+    W[4] = 1                                                      # sub-block 0: sc = 1, m = 0
+    W[16 + 5] = 0x01                                              # element 5 = 1 (low nibble)
+    x = np.arange(K, dtype=np.float32) * 0.5 + 1.0
+    assert oracle.kquant_gemv("q4_k", W, x, 1, K)[0] == x[5]
