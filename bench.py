@@ -282,6 +282,27 @@ def q8_bench(ane, torch, dev, steps=50):
         res["q4_0_static_us"] = ms * 1e3
         res["q4_0_static_gbs"] = (q4bytes + 4 * cols + 4 * rows) / (ms * 1e-3) / 1e9
         del W4s
+        # K-quant matvecs (q2_k .. q6_k): random super-blocks with small fp16 scales
+        for fmt, bb in sorted(ane.KQUANT_BLOCK_BYTES.items()):
+            kbytes = rows * (cols // 256) * bb
+            kcopies = max(4, -(-512_000_000 // kbytes))
+            Wks = [torch.randint(0, 256, (kbytes,), dtype=torch.uint8, device=dev, generator=g) for _ in range(kcopies)]
+            for Wk in Wks:  # d (and dmin) = small positive fp16: high byte 0x1C
+                v = Wk.view(-1, bb)
+                for off in {"q2_k": (81, 83), "q3_k": (109,), "q4_k": (1, 3), "q5_k": (1, 3), "q6_k": (209,)}[fmt]:
+                    v[:, off] = 0x1C
+            itk = [0]
+
+            def step_k():
+                ane.kquant_gemv(fmt, Wks[itk[0] % kcopies], x, rows, cols, out=y)
+                itk[0] += 1
+
+            for _ in range(3):
+                step_k()
+            ms = time_graph(step_k, steps, stream)
+            res[f"{fmt}_us"] = ms * 1e3
+            res[f"{fmt}_gbs"] = (kbytes + 4 * cols + 4 * rows) / (ms * 1e-3) / 1e9
+            del Wks
         # decode at batch 16: ggml MUL_MAT over 16 fp32 activation rows, weights read once
         xb = torch.randn((16, cols), device=dev, generator=g)
         yb = torch.empty((16, rows), device=dev)

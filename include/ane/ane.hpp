@@ -149,15 +149,15 @@ enum class Op : uint8_t {
     rope_backward_fp32 = 0x72,
     cross_entropy_fp32 = 0x73,
     elementwise_sub_fp32 = 0x74,
-    q4_k_gemv = 0x75,
-    q2_k_gemv = 0x76,
-    q3_k_gemv = 0x77,
-    q5_k_gemv = 0x78,
-    q6_k_gemv = 0x79,
+    q4_k_gemv = 0x75,                     // executed on the GPU
+    q2_k_gemv = 0x76,                     // executed on the GPU
+    q3_k_gemv = 0x77,                     // executed on the GPU
+    q5_k_gemv = 0x78,                     // executed on the GPU
+    q6_k_gemv = 0x79,                     // executed on the GPU
     flash_attention_fp32 = 0x7A,
     get_rows_fp32 = 0x7B,
     get_rows_q8_0 = 0x7C,                 // executed on the GPU
-    get_rows_q4_0 = 0x7D,
+    get_rows_q4_0 = 0x7D,                 // executed on the GPU
     dense_strided_fp32 = 0x7E,
     advance_param_stride = 0x7F,
     dense_fused_i8 = 0x80,  // new: quantize(A), quantize(B), int8 GEMM, rescale, ReLU
