@@ -15,12 +15,21 @@
 //
 // Threads: 8 per row, thread t holding lanes 2t and 2t+1 (the first FADDV level
 // in-thread, the other three by xor shuffles 1, 2, 4) -- the q4_0 / q8_0 mode-R
-// lane mapping; 4 rows per warp.  Loads follow each format's alignment (144-
-// and 176-byte super-blocks keep 16-byte alignment, 84-byte ones 4-byte,
-// 110- and 210-byte ones only 2-byte).
+// lane mapping, 4 rows per compute warp.  Streamed kernel (rows whose byte
+// length is a multiple of 16): the mode-R ring -- one producer warp per CTA,
+// each stage = C super-blocks of every compute warp's 4 rows (one 2-D TMA box
+// per warp; C = 4 for q4_k / q5_k, 8 for q2_k / q3_k / q6_k, so a box row is a
+// multiple of 16 bytes) plus the matching slice of x (bulk copy); the decoders
+// read shared memory.  Otherwise a direct-load kernel with the same decoders
+// and lane mapping.  Loads follow each layout's alignment (144- and 176-byte
+// super-blocks keep 16-byte alignment, 84-byte ones 4-byte, 110- and 210-byte
+// ones only 2-byte).
 #include <cuda_fp16.h>
 
+#include <cuda.h>
+
 #include "ane_internal.cuh"
+#include "q8_stream.cuh"
 #include "sm100_ptx.cuh"
 
 namespace ane_b200 {
@@ -32,23 +41,23 @@ template <int F>
 struct KBlock;
 template <>
 struct KBlock<kQ4K> {
-    static constexpr uint32_t bytes = 144;
+    static constexpr uint32_t bytes = 144, chunk = 4, elem = 4;  // super-blocks per stage, TMA element bytes
 };
 template <>
 struct KBlock<kQ2K> {
-    static constexpr uint32_t bytes = 84;
+    static constexpr uint32_t bytes = 84, chunk = 8, elem = 4;  // super-blocks per stage, TMA element bytes
 };
 template <>
 struct KBlock<kQ3K> {
-    static constexpr uint32_t bytes = 110;
+    static constexpr uint32_t bytes = 110, chunk = 8, elem = 4;  // super-blocks per stage, TMA element bytes
 };
 template <>
 struct KBlock<kQ5K> {
-    static constexpr uint32_t bytes = 176;
+    static constexpr uint32_t bytes = 176, chunk = 4, elem = 4;  // super-blocks per stage, TMA element bytes
 };
 template <>
 struct KBlock<kQ6K> {
-    static constexpr uint32_t bytes = 210;
+    static constexpr uint32_t bytes = 210, chunk = 8, elem = 8;  // super-blocks per stage, TMA element bytes
 };
 
 __device__ __forceinline__ float h2f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }
@@ -202,6 +211,119 @@ __global__ void __launch_bounds__(256) kquant_gemv_kernel(const float* __restric
     if (row < M && t == 0) out[row] = s;
 }
 
+// The streamed matvec: stage t = chunk t % nchunks of pass t / nchunks.
+template <int F>
+__global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
+    kquant_stream_kernel(const __grid_constant__ CUtensorMap wmap, const float* __restrict__ x,
+                         float* __restrict__ out, uint32_t M, uint32_t nsb, uint32_t groups, uint32_t nw,
+                         uint32_t nslots, int* err) {
+    constexpr uint32_t BB = KBlock<F>::bytes, C = KBlock<F>::chunk, CB = C * BB;
+    constexpr uint32_t TILE = (kQ8RowsPerWarp * CB + 127) / 128 * 128;  // one warp's 4 rows, 128-byte pitch
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t nchunks = (nsb + C - 1) / C;
+    const uint32_t w_bytes = nw * TILE, slot_bytes = w_bytes + C * 1024;
+    auto chunk_sbs = [&](uint32_t c) { return min(C, nsb - c * C); };
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // nslots
+    uint64_t* empty = full + nslots;                     // nslots
+    uint8_t* ring = smem + 128;
+    const uint32_t g0 = (uint32_t)((uint64_t)groups * blockIdx.x / gridDim.x);
+    const uint32_t g1 = (uint32_t)((uint64_t)groups * (blockIdx.x + 1) / gridDim.x);
+    const uint32_t npass = (g1 - g0 + nw - 1) / nw, ntiles = npass * nchunks;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t i = 0; i < nslots; i++) {
+            ptx::mbar_init(&full[i], 1);
+            ptx::mbar_init(&empty[i], nw);
+        }
+        ptx::fence_mbarrier_init();
+    }
+    __syncthreads();
+    ptx::griddep_launch_dependents();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            ptx::prefetch_tmap(&wmap);
+            ptx::griddep_wait();  // x may be written by the previous kernel
+            for (uint32_t t = 0; t < ntiles; t++) {
+                const uint32_t slot = t % nslots, pass = t / nchunks, c = t - pass * nchunks;
+                if (!ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err)) break;
+                const uint32_t gp = g0 + pass * nw, nwp = min(nw, g1 - gp);
+                uint8_t* dst = ring + (size_t)slot * slot_bytes;
+                // full boxes: the part past the row end (a short last chunk) is zero fill
+                ptx::mbar_arrive_expect_tx(&full[slot], nwp * kQ8RowsPerWarp * CB + chunk_sbs(c) * 1024);
+                for (uint32_t w = 0; w < nwp; w++)
+                    ptx::tma_load_2d(dst + w * TILE, &wmap, &full[slot], (int)(c * (CB / KBlock<F>::elem)),
+                                     (int)((gp + w) * kQ8RowsPerWarp));
+                ptx::bulk_load(dst + w_bytes, x + (size_t)c * C * 256, chunk_sbs(c) * 1024, &full[slot]);
+            }
+        }
+        return;
+    }
+    // ------------------------------------------------------------ compute
+    ptx::griddep_wait();  // out may belong to the previous kernel
+    const uint32_t cw = warp - 1, rr = lane >> 3, t8 = lane & 7;
+    bool alive = true;
+    for (uint32_t pass = 0; pass < npass && alive; pass++) {
+        const uint32_t gp = g0 + pass * nw;
+        const uint32_t row = (gp + cw) * kQ8RowsPerWarp + rr;
+        const bool active = gp + cw < g1 && row < M;
+        float a0 = 0.0f, a1 = 0.0f;
+        for (uint32_t c = 0; c < nchunks; c++) {
+            const uint32_t t = pass * nchunks + c, slot = t % nslots;
+            if (!ptx::mbar_wait(&full[slot], (t / nslots) & 1, err)) {
+                alive = false;
+                break;
+            }
+            if (active) {
+                const uint8_t* st = ring + (size_t)slot * slot_bytes;
+                const uint8_t* rp = st + cw * TILE + rr * CB;
+                const float* xc = reinterpret_cast<const float*>(st + w_bytes);
+                const uint32_t n = chunk_sbs(c);
+                for (uint32_t k = 0; k < n; k++) kq_superblock<F>(rp + k * BB, xc + 256 * k, t8, a0, a1);
+            }
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&empty[slot]);
+        }
+        float sum = __fadd_rn(a0, a1);
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 4));
+        if (active && alive && t8 == 0) out[row] = sum;
+    }
+}
+
+template <int F>
+int launch_kquant_stream(uint32_t M, uint32_t nsb, const float* x, const uint8_t* W, float* out, cudaStream_t s) {
+    constexpr uint32_t BB = KBlock<F>::bytes, C = KBlock<F>::chunk, CB = C * BB;
+    constexpr uint32_t TILE = (kQ8RowsPerWarp * CB + 127) / 128 * 128;
+    const Q8Plan p = plan_q8_stream(M, nsb * 256, C * 1024, 128, (BB + 7) / 8, TILE);
+    static const cudaError_t attr_err =
+        cudaFuncSetAttribute(kquant_stream_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    ANE_CUDA_TRY(attr_err);
+    ANE_ARG_CHECK(p.smem <= 200 * 1024, "kquant_gemv: shared-memory plan too large");
+    const uint64_t row_bytes = (uint64_t)nsb * BB;
+    CUtensorMap wmap;
+    const uint32_t E = KBlock<F>::elem;
+    int rc = encode_tensor_map_2d(&wmap, E == 8 ? CU_TENSOR_MAP_DATA_TYPE_INT64 : CU_TENSOR_MAP_DATA_TYPE_UINT32, W,
+                                  row_bytes / E, M, row_bytes, CB / E, kQ8RowsPerWarp, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    return launch_q8_stream(kquant_stream_kernel<F>, p, s, wmap, x, out, M, nsb, p.groups, p.warps, p.slots,
+                            device_timeout_flag());
+}
+
+template <int F>
+int launch_kquant(uint32_t M, uint32_t nsb, const float* x, const uint8_t* W, float* out, cudaStream_t s) {
+    // streamed when a row is a whole number of 16-byte units (the TMA row stride)
+    // and W, x are 16-byte aligned (TMA base, bulk copies of x)
+    const uint64_t row_bytes = (uint64_t)nsb * KBlock<F>::bytes;
+    if (row_bytes % 16 == 0 && ((uintptr_t)W & 15) == 0 && ((uintptr_t)x & 15) == 0)
+        return launch_kquant_stream<F>(M, nsb, x, W, out, s);
+    kquant_gemv_kernel<F><<<(M + 31) / 32, 256, 0, s>>>(x, W, out, M, nsb);
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
+}
+
 // get_rows_q4_0: one thread per (row, block, i < 16): elements i and 16 + i.
 __global__ void get_rows_q4_0_kernel(uint32_t n_rows, uint32_t nb, const uint8_t* __restrict__ table,
                                      const uint32_t* __restrict__ idx, float* __restrict__ out) {
@@ -246,16 +368,13 @@ int launch_kquant_gemv(uint32_t fmt, uint32_t M, uint32_t K, const float* x, con
         ANE_CUDA_TRY(cudaMemsetAsync(out, 0, (size_t)M * 4, s));
         return ANE_OK;
     }
-    const dim3 grid((M + 31) / 32), block(256);
     switch (fmt) {
-        case kQ4K: kquant_gemv_kernel<kQ4K><<<grid, block, 0, s>>>(x, W, out, M, nsb); break;
-        case kQ2K: kquant_gemv_kernel<kQ2K><<<grid, block, 0, s>>>(x, W, out, M, nsb); break;
-        case kQ3K: kquant_gemv_kernel<kQ3K><<<grid, block, 0, s>>>(x, W, out, M, nsb); break;
-        case kQ5K: kquant_gemv_kernel<kQ5K><<<grid, block, 0, s>>>(x, W, out, M, nsb); break;
-        default: kquant_gemv_kernel<kQ6K><<<grid, block, 0, s>>>(x, W, out, M, nsb); break;
+        case kQ4K: return launch_kquant<kQ4K>(M, nsb, x, W, out, s);
+        case kQ2K: return launch_kquant<kQ2K>(M, nsb, x, W, out, s);
+        case kQ3K: return launch_kquant<kQ3K>(M, nsb, x, W, out, s);
+        case kQ5K: return launch_kquant<kQ5K>(M, nsb, x, W, out, s);
+        default: return launch_kquant<kQ6K>(M, nsb, x, W, out, s);
     }
-    ANE_CHECK_LAUNCH();
-    return ANE_OK;
 }
 
 int launch_get_rows_q4_0(uint32_t n_rows, uint32_t dim, const uint8_t* table, const uint32_t* idx, float* out,
