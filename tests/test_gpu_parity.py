@@ -253,6 +253,32 @@ def test_dense_fused_i8_stages_bit_exact(ane):
     assert K16 % 16 == 0
 
 
+@pytest.mark.parametrize("M,N,K", [
+    (1024, 1028, 4096),   # cooperative prologue, N % 256 != 0: B codes read with plain loads
+    (1024, 1280, 4112),   # cooperative prologue with TMA refills: last column unit half outside N,
+                          # last row unit 16 rows (the boxes' zero fill)
+])
+def test_dense_fused_i8_coop_prologue_edges(ane, M, N, K):
+    """Shapes the one-launch cooperative prologue takes (M*K, K*N >= 2^22),
+    away from 4096^3: quantized operands, scales and C against the oracle."""
+    import torch
+
+    rng = np.random.default_rng(M + N + K)
+    A = rng.standard_normal((M, K)).astype(F32)
+    B = rng.standard_normal((K, N)).astype(F32)
+    Ad, Bd = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    Aq, Bt, scales = ane.quantize_pair(Ad, Bd)
+    C = ane.dense_fused_i8(Ad, Bd, 0.75, True)
+    torch.cuda.synchronize()
+    C_r, Aq_r, Bq_r, _, sa, sb = oracle.dense_fused_i8(A, B, 0.75, True, full=True)
+    s = scales.cpu().numpy()
+    assert s[0] == sa and s[1] == sb
+    Aqn, Btn = Aq.cpu().numpy(), Bt.cpu().numpy()
+    assert np.array_equal(Aqn[:, :K], Aq_r)
+    assert np.array_equal(Btn[:N, :K], Bq_r.T)
+    assert bits_equal(C.cpu().numpy(), C_r)
+
+
 def test_dense_fused_i8_device_4096_properties(ane):
     """Config 2 at full size: quantized operands and sampled accumulator rows exact."""
     import torch
