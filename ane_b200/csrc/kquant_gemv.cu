@@ -85,20 +85,40 @@ __device__ __forceinline__ float kq_term(float acc, int32_t q, float dsc, float 
 }
 
 // One super-block of a row for thread t's lanes 2t (a0) and 2t+1 (a1).
+// sh (a constant at every call site): the row's 8 threads are converged (all
+// 32 lanes of the warp call together); thread t decodes sub-block t's scale (and
+// t + 8's in the 16-sub-block formats) and the others take it by a width-8
+// shuffle -- the same values, decoded once per row instead of in every thread.
 template <int F>
 __device__ __forceinline__ void kq_superblock(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
-                                              uint32_t t, float& a0, float& a1);
+                                              uint32_t t, float& a0, float& a1, bool sh);
+
+__device__ __forceinline__ float row_bcast(float v, uint32_t j) { return __shfl_sync(0xffffffffu, v, (int)j, 8); }
 
 template <>
 __device__ __forceinline__ void kq_superblock<kQ4K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
-                                                    uint32_t t, float& a0, float& a1) {
+                                                    uint32_t t, float& a0, float& a1, bool sh) {
     const float d = h2f(ld_u16(blk)), nd = -h2f(ld_u16(blk + 2));
     const uint8_t* qs = blk + 16;
+    float tdsc = 0.0f, tdmm = 0.0f;  // sub-block t's, when shared
+    if (sh) {
+        uint32_t sc, mn;
+        k_scale_min(blk + 4, t, sc, mn);
+        tdsc = __fmul_rn(d, (float)sc);
+        tdmm = __fmul_rn(nd, (float)mn);
+    }
 #pragma unroll
     for (uint32_t j = 0; j < 8; j++) {
-        uint32_t sc, mn;
-        k_scale_min(blk + 4, j, sc, mn);
-        const float dsc = __fmul_rn(d, (float)sc), dmm = __fmul_rn(nd, (float)mn);
+        float dsc, dmm;
+        if (sh) {
+            dsc = row_bcast(tdsc, j);
+            dmm = row_bcast(tdmm, j);
+        } else {
+            uint32_t sc, mn;
+            k_scale_min(blk + 4, j, sc, mn);
+            dsc = __fmul_rn(d, (float)sc);
+            dmm = __fmul_rn(nd, (float)mn);
+        }
         const uint32_t b = ld_u16(qs + 16 * j + 2 * t);  // bytes of lanes 2t, 2t+1
         const float2 xl = *reinterpret_cast<const float2*>(xb + 32 * j + 2 * t);
         const float2 xh = *reinterpret_cast<const float2*>(xb + 32 * j + 16 + 2 * t);
@@ -111,13 +131,27 @@ __device__ __forceinline__ void kq_superblock<kQ4K>(const uint8_t* __restrict__ 
 
 template <>
 __device__ __forceinline__ void kq_superblock<kQ2K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
-                                                    uint32_t t, float& a0, float& a1) {
+                                                    uint32_t t, float& a0, float& a1, bool sh) {
     const uint32_t dd = *reinterpret_cast<const uint32_t*>(blk + 80);
     const float d = h2f(dd & 0xFFFFu), nd = -h2f(dd >> 16);
+    float tdsc0 = 0.0f, tdmm0 = 0.0f, tdsc1 = 0.0f, tdmm1 = 0.0f;  // sub-blocks t and t + 8, when shared
+    if (sh) {
+        tdsc0 = __fmul_rn(d, (float)(blk[t] & 0x0Fu));
+        tdmm0 = __fmul_rn(nd, (float)(blk[t] >> 4));
+        tdsc1 = __fmul_rn(d, (float)(blk[t + 8] & 0x0Fu));
+        tdmm1 = __fmul_rn(nd, (float)(blk[t + 8] >> 4));
+    }
 #pragma unroll
     for (uint32_t j = 0; j < 16; j++) {
-        const uint32_t s = blk[j];
-        const float dsc = __fmul_rn(d, (float)(s & 0x0Fu)), dmm = __fmul_rn(nd, (float)(s >> 4));
+        float dsc, dmm;
+        if (sh) {
+            dsc = row_bcast(j < 8 ? tdsc0 : tdsc1, j & 7);
+            dmm = row_bcast(j < 8 ? tdmm0 : tdmm1, j & 7);
+        } else {
+            const uint32_t s = blk[j];
+            dsc = __fmul_rn(d, (float)(s & 0x0Fu));
+            dmm = __fmul_rn(nd, (float)(s >> 4));
+        }
         const uint32_t w = *reinterpret_cast<const uint32_t*>(blk + 16 + 4 * j);
         const float2 xv = *reinterpret_cast<const float2*>(xb + 16 * j + 2 * t);
         a0 = kq_min_term(a0, (w >> (4 * t)) & 3u, dsc, dmm, xv.x);
@@ -127,14 +161,18 @@ __device__ __forceinline__ void kq_superblock<kQ2K>(const uint8_t* __restrict__ 
 
 template <>
 __device__ __forceinline__ void kq_superblock<kQ3K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
-                                                    uint32_t t, float& a0, float& a1) {
+                                                    uint32_t t, float& a0, float& a1, bool sh) {
     const uint8_t *hm = blk, *qs = blk + 32, *sc = blk + 96;
     const float d = h2f(ld_u16(blk + 108));
     const uint32_t l0 = 2 * t, l1 = 2 * t + 1;
+    auto scale_of = [&](uint32_t j) {
+        const uint32_t s6 = j < 4 ? (sc[j] & 0x3Fu) : ((sc[j + 4] & 0x0Fu) | ((uint32_t)(sc[j - 4] >> 6) << 4));
+        return __fmul_rn(d, (float)((int32_t)s6 - 32));
+    };
+    const float tdsc = sh ? scale_of(t) : 0.0f;
 #pragma unroll
     for (uint32_t j = 0; j < 8; j++) {
-        const uint32_t s6 = j < 4 ? (sc[j] & 0x3Fu) : ((sc[j + 4] & 0x0Fu) | ((uint32_t)(sc[j - 4] >> 6) << 4));
-        const float dsc = __fmul_rn(d, (float)((int32_t)s6 - 32));
+        const float dsc = sh ? row_bcast(tdsc, j) : scale_of(j);
         const uint32_t w0 = ld_u32_a2(qs + 8 * j), h0 = ld_u16(hm + 4 * j);
         const float2 xl = *reinterpret_cast<const float2*>(xb + 32 * j + 2 * t);
         const float2 xh = *reinterpret_cast<const float2*>(xb + 32 * j + 16 + 2 * t);
@@ -155,15 +193,29 @@ __device__ __forceinline__ void kq_superblock<kQ3K>(const uint8_t* __restrict__ 
 
 template <>
 __device__ __forceinline__ void kq_superblock<kQ5K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
-                                                    uint32_t t, float& a0, float& a1) {
+                                                    uint32_t t, float& a0, float& a1, bool sh) {
     const float d = h2f(ld_u16(blk)), nd = -h2f(ld_u16(blk + 2));
     const uint8_t *qh = blk + 16, *qs = blk + 48;
     const uint32_t l0 = 2 * t, l1 = 2 * t + 1;
+    float tdsc = 0.0f, tdmm = 0.0f;
+    if (sh) {
+        uint32_t sc, mn;
+        k_scale_min(blk + 4, t, sc, mn);
+        tdsc = __fmul_rn(d, (float)sc);
+        tdmm = __fmul_rn(nd, (float)mn);
+    }
 #pragma unroll
     for (uint32_t j = 0; j < 8; j++) {
-        uint32_t sc, mn;
-        k_scale_min(blk + 4, j, sc, mn);
-        const float dsc = __fmul_rn(d, (float)sc), dmm = __fmul_rn(nd, (float)mn);
+        float dsc, dmm;
+        if (sh) {
+            dsc = row_bcast(tdsc, j);
+            dmm = row_bcast(tdmm, j);
+        } else {
+            uint32_t sc, mn;
+            k_scale_min(blk + 4, j, sc, mn);
+            dsc = __fmul_rn(d, (float)sc);
+            dmm = __fmul_rn(nd, (float)mn);
+        }
         const uint32_t h = *reinterpret_cast<const uint32_t*>(qh + 4 * j);
         const uint32_t b = ld_u16(qs + 16 * j + 2 * t);
         const float2 xl = *reinterpret_cast<const float2*>(xb + 32 * j + 2 * t);
@@ -177,13 +229,14 @@ __device__ __forceinline__ void kq_superblock<kQ5K>(const uint8_t* __restrict__ 
 
 template <>
 __device__ __forceinline__ void kq_superblock<kQ6K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
-                                                    uint32_t t, float& a0, float& a1) {
+                                                    uint32_t t, float& a0, float& a1, bool sh) {
     const uint8_t *ql = blk, *qh = blk + 128;
     const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
     const float d = h2f(ld_u16(blk + 208));
+    const float tdsc0 = sh ? __fmul_rn(d, (float)sc[t]) : 0.0f, tdsc1 = sh ? __fmul_rn(d, (float)sc[t + 8]) : 0.0f;
 #pragma unroll
     for (uint32_t j = 0; j < 16; j++) {
-        const float dsc = __fmul_rn(d, (float)sc[j]);
+        const float dsc = sh ? row_bcast(j < 8 ? tdsc0 : tdsc1, j & 7) : __fmul_rn(d, (float)sc[j]);
         const uint32_t h = ld_u32_a2(qh + 4 * j);
         const uint32_t b = ql[8 * j + t];  // element 2t: low nibble, 2t+1: high nibble
         const float2 xv = *reinterpret_cast<const float2*>(xb + 16 * j + 2 * t);
@@ -201,7 +254,8 @@ __global__ void __launch_bounds__(256) kquant_gemv_kernel(const float* __restric
     float a0 = 0.0f, a1 = 0.0f;
     if (row < M) {
         const uint8_t* rp = W + (size_t)row * nsb * KBlock<F>::bytes;
-        for (uint32_t b = 0; b < nsb; b++) kq_superblock<F>(rp + (size_t)b * KBlock<F>::bytes, x + 256 * b, t, a0, a1);
+        for (uint32_t b = 0; b < nsb; b++)
+            kq_superblock<F>(rp + (size_t)b * KBlock<F>::bytes, x + 256 * b, t, a0, a1, false);
     }
     // FADDV: level 1 in-thread (lanes 2t, 2t+1), levels 2-4 across the row's 8 threads
     float s = __fadd_rn(a0, a1);
@@ -267,20 +321,23 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
     for (uint32_t pass = 0; pass < npass && alive; pass++) {
         const uint32_t gp = g0 + pass * nw;
         const uint32_t row = (gp + cw) * kQ8RowsPerWarp + rr;
-        const bool active = gp + cw < g1 && row < M;
+        // the whole warp computes (rows past M read the box's zero fill), so the
+        // decoders' width-8 shuffles see all 32 lanes; only the store is per row
+        const bool warp_on = gp + cw < g1, active = warp_on && row < M;
         float a0 = 0.0f, a1 = 0.0f;
         for (uint32_t c = 0; c < nchunks; c++) {
             const uint32_t t = pass * nchunks + c, slot = t % nslots;
-            if (!ptx::mbar_wait(&full[slot], (t / nslots) & 1, err)) {
+            // one verdict per warp, so no lane is left behind at a shuffle
+            if (!__all_sync(0xffffffffu, ptx::mbar_wait(&full[slot], (t / nslots) & 1, err))) {
                 alive = false;
                 break;
             }
-            if (active) {
+            if (warp_on) {
                 const uint8_t* st = ring + (size_t)slot * slot_bytes;
                 const uint8_t* rp = st + cw * TILE + rr * CB;
                 const float* xc = reinterpret_cast<const float*>(st + w_bytes);
                 const uint32_t n = chunk_sbs(c);
-                for (uint32_t k = 0; k < n; k++) kq_superblock<F>(rp + k * BB, xc + 256 * k, t8, a0, a1);
+                for (uint32_t k = 0; k < n; k++) kq_superblock<F>(rp + k * BB, xc + 256 * k, t8, a0, a1, true);
             }
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&empty[slot]);
