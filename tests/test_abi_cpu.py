@@ -105,6 +105,18 @@ def test_no_gpu_means_loud_failure():
     rc = ane_b200.lib.ane_quantize_fp32_i8(16, x.ctypes.data, q.ctypes.data, s.ctypes.data)
     assert rc == 5  # ANE_ERR_NO_DEVICE
     assert not q.any() and s[0] == 0
+    # the K-quant matvecs and get_rows_q4_0 likewise: no CPU fallback
+    xk = np.ones(256, np.float32)
+    W = np.zeros(210, np.uint8)
+    out = np.full(1, 7.0, np.float32)
+    for fmt in ("q2_k", "q3_k", "q4_k", "q5_k", "q6_k"):
+        fn = getattr(ane_b200.lib, "ane_%s_gemv" % fmt)
+        assert fn(1, 256, xk.ctypes.data, W.ctypes.data, out.ctypes.data) == 5, fmt
+        assert out[0] == 7.0
+    idx = np.zeros(1, np.uint32)
+    rows = np.full(32, 7.0, np.float32)
+    assert ane_b200.lib.ane_get_rows_q4_0(1, 32, W.ctypes.data, idx.ctypes.data, rows.ctypes.data) == 5
+    assert (rows == 7.0).all()
 
 
 def test_cpp_header_compiles_on_linux(tmp_path):
