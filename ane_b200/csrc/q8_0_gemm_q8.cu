@@ -332,7 +332,9 @@ __global__ void __launch_bounds__(32 * (kMaxTiles * kMaxGroups + 1), 1)
         const uint32_t pass = t / nseg, s = t - pass * nseg, slot = t % nslots;
         const uint32_t qa = q0 + 2 * (pass * T + ti);
         const bool active = qa < q1;  // once false, false for every later pass
-        if (!ptx::mbar_wait(&full[slot], (t / nslots) & 1, err)) break;
+        // one verdict per warp: no lane may reach the warp-wide MMAs or shuffles
+        // without the others after a timed-out wait
+        if (!__all_sync(0xffffffffu, ptx::mbar_wait(&full[slot], (t / nslots) & 1, err))) break;
         if (!active) {
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&empty[slot]);
@@ -347,7 +349,7 @@ __global__ void __launch_bounds__(32 * (kMaxTiles * kMaxGroups + 1), 1)
         if (lane == 0) ptx::mbar_arrive(&empty[slot]);
         // the row totals, in segment order: wait for stage t - 1's phase of this
         // tile's baton, add this segment, pass the baton on
-        if (t > 0 && !ptx::mbar_wait(&baton[ti], (t - 1) & 1, err)) break;
+        if (t > 0 && !__all_sync(0xffffffffu, ptx::mbar_wait(&baton[ti], (t - 1) & 1, err))) break;
         float4 acc = s == 0 ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : *reinterpret_cast<const float4*>(tot);
         const float2 lo = fadd2_rn(make_float2(acc.x, acc.y), seg01);
         const float2 hi = fadd2_rn(make_float2(acc.z, acc.w), seg23);
