@@ -314,7 +314,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             const uint32_t m0 = (t / p.tiles_n) * S_BM, n0 = (t % p.tiles_n) * S_BN;
-            if (!ptx::mbar_wait(&bars->tmem_full[acc], acc_phase, p.err)) break;
+            // one verdict per warp: no lane reaches the warp-wide tcgen05.ld alone
+            if (!__all_sync(0xffffffffu, ptx::mbar_wait(&bars->tmem_full[acc], acc_phase, p.err))) break;
             ptx::tc_fence_after();
             const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + acc * ACC_COLS;
             uint64_t* empty_bar = &bars->tmem_empty[acc];
@@ -443,7 +444,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const PairUnit un = pair_unit(p, u);
             if (un.n0 >= p.N) continue;
             const uint32_t m0 = un.m0 + rank * P_HM;
-            if (!ptx::mbar_wait(&bars->tmem_full[acc], acc_phase, p.err)) break;
+            // one verdict per warp: no lane reaches the warp-wide tcgen05.ld alone
+            if (!__all_sync(0xffffffffu, ptx::mbar_wait(&bars->tmem_full[acc], acc_phase, p.err))) break;
             ptx::tc_fence_after();
             const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + acc * ACC_COLS;
             const uint32_t empty_leader = ptx::mapa_shared(ptx::smem_u32(&bars->tmem_empty[acc]), 0);

@@ -226,7 +226,8 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
         float2 acc = make_float2(0.f, 0.f);
         for (uint32_t c = 0; c < nchunks; c++) {
             const uint32_t t = pass * nchunks + c, slot = t % nslots;
-            if (!ptx::mbar_wait(&full[slot], (t / nslots) & 1, err)) { alive = false; break; }
+            // one verdict per warp: after a timed-out wait every lane leaves together
+            if (!__all_sync(0xffffffffu, ptx::mbar_wait(&full[slot], (t / nslots) & 1, err))) { alive = false; break; }
             if (active) {
                 const uint8_t* st = ring + (size_t)slot * slot_bytes;
                 const uint8_t* rp = st + cw * kQ8WarpTileBytes + rr * kQ8ChunkBytes;

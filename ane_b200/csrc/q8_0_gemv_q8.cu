@@ -137,7 +137,7 @@ __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, co
     // ------------------------------------------------------------ compute
     ptx::griddep_wait();  // out / block_dots may belong to the previous kernel
     const uint32_t cw = warp - 1;
-    bool alive = ptx::mbar_wait(xbar, 0, err);
+    bool alive = __all_sync(0xffffffffu, ptx::mbar_wait(xbar, 0, err));  // one verdict per warp
     if (alive && XF32) {  // quantize: one thread per 32-element block
         for (uint32_t b = cw * 32 + lane; b < nb; b += nw * 32)
             q8_quantize_block<false>(reinterpret_cast<const float*>(xraw) + (size_t)b * 32, xs, xd, b);
@@ -159,7 +159,8 @@ __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, co
         float sum = 0.f;
         for (uint32_t c = 0; c < nchunks; c++) {
             const uint32_t t = pass * nchunks + c, slot = t % nslots;
-            if (!ptx::mbar_wait(&full[slot], (t / nslots) & 1, err)) { alive = false; break; }
+            // one verdict per warp: after a timed-out wait every lane leaves together
+            if (!__all_sync(0xffffffffu, ptx::mbar_wait(&full[slot], (t / nslots) & 1, err))) { alive = false; break; }
             const uint32_t b = c * kQ8ChunkBlocks + 2 * pp;  // first block of the pair
             if (active && b < nb) {
                 const uint32_t* pw = reinterpret_cast<const uint32_t*>(ring + (size_t)slot * slot_bytes +
