@@ -2,7 +2,7 @@
 
 * libane_b200.so loads and exports every function include/ane_b200.h declares;
 * the Python `encode` packs opcodes byte-for-byte like ane::dispatch
-  (include/ane/ane.hpp:206-220) -- payload sizes of SURVEY-listed calls;
+  (include/ane/ane.hpp:206-220) -- payload sizes of the hot-path opcodes;
 * stream_exec rejects unsupported opcodes and truncated payloads before any
   device work, and a supported opcode without a GPU fails loudly (no fallback).
 """
