@@ -387,3 +387,32 @@ def test_kquant_oracle_lane_order():
     W[16 + 5] = 0x01                                              # element 5 = 1 (low nibble)
     x = np.arange(K, dtype=np.float32) * 0.5 + 1.0
     assert oracle.kquant_gemv("q4_k", W, x, 1, K)[0] == x[5]
+
+
+def test_mul_mat_q8_0_batch_oracle_matches_numpy_segments():
+    """The batched Q8_0 MUL_MAT oracle against a numpy restatement of its
+    contract: per (token, row) the terms float(sumi) * (dw * dx) (separate fp32
+    roundings), summed from +0 in block order within segments of 32 blocks, the
+    segment sums added from +0 in segment order -- exact, float32 numpy."""
+    rng = np.random.default_rng(17)
+    for M, K, NT in [(24, 4096, 5), (9, 11008, 3), (16, 256, 2)]:
+        W = oracle.quantize_q8_0((rng.standard_normal((M, K)) * 0.02).astype(np.float32), M, K)
+        x = rng.standard_normal((NT, K)).astype(np.float32)
+        xq = oracle.quantize_q8_0(x, NT, K)
+        nb = K // 32
+        Wb = W.reshape(M, nb, 34)
+        Xb = xq.reshape(NT, nb, 34)
+        dw = Wb[:, :, 0:2].copy().view(np.float16).reshape(M, nb).astype(np.float32)
+        dx = Xb[:, :, 0:2].copy().view(np.float16).reshape(NT, nb).astype(np.float32)
+        qw = Wb[:, :, 2:].view(np.int8).astype(np.int32)
+        qx = Xb[:, :, 2:].view(np.int8).astype(np.int32)
+        sumi = np.einsum("mbk,tbk->tmb", qw, qx)          # exact int32 block dots
+        total = np.zeros((NT, M), np.float32)
+        for s0 in range(0, nb, 32):
+            seg = np.zeros((NT, M), np.float32)
+            for b in range(s0, min(s0 + 32, nb)):
+                p = (dw[None, :, b] * dx[:, None, b]).astype(np.float32)
+                seg = (seg + sumi[:, :, b].astype(np.float32) * p).astype(np.float32)
+            total = (total + seg).astype(np.float32)
+        got = oracle.mul_mat_q8_0_batch(W, xq, M, K, NT)
+        assert np.array_equal(got.view(np.uint32), total.view(np.uint32)), (M, K, NT)
