@@ -416,3 +416,29 @@ def test_mul_mat_q8_0_batch_oracle_matches_numpy_segments():
             total = (total + seg).astype(np.float32)
         got = oracle.mul_mat_q8_0_batch(W, xq, M, K, NT)
         assert np.array_equal(got.view(np.uint32), total.view(np.uint32)), (M, K, NT)
+
+
+def test_q4_0_gemv_oracle_layout():
+    """q4_0_gemv oracle: element i < 16 of a block is the low nibble of byte i,
+    element 16 + i its high nibble, value (nibble - 8) * d -- a numpy dequant
+    dotted in float64 (a tolerance: the lane FMA order is checked on the GPU bit
+    for bit), and a single nonzero weight returning x[e] * d exactly."""
+    rng = np.random.default_rng(23)
+    M, K = 5, 512
+    nb = K // 32
+    W = rng.integers(0, 256, size=(M, nb, 18), dtype=np.uint8)
+    W[:, :, 0:2] = (rng.random((M, nb)) * 0.05 + 0.01).astype(np.float16).view(np.uint8).reshape(M, nb, 2)
+    x = rng.standard_normal(K).astype(np.float32)
+    got = oracle.q4_0_gemv(W.reshape(-1), x, M, K)
+    d = W[:, :, 0:2].copy().view(np.float16).reshape(M, nb).astype(np.float64)
+    q = W[:, :, 2:].astype(np.int64)
+    vals = np.concatenate([(q & 15) - 8, (q >> 4) - 8], axis=2) * d[:, :, None]   # [M, nb, 32]
+    ref = vals.reshape(M, K) @ x.astype(np.float64)
+    scale = np.abs(vals.reshape(M, K)) @ np.abs(x.astype(np.float64))
+    assert np.all(np.abs(got - ref) <= 1e-5 * scale)
+    # one nonzero weight: element 21 of block 1 (high nibble of byte 5) = 9 - 8 = 1
+    W1 = np.zeros((1, nb, 18), np.uint8)
+    W1[:, :, 2:] = 0x88                                          # every code 8 -> value 0
+    W1[0, 1, 0:2] = np.frombuffer(np.float16(0.5).tobytes(), np.uint8)
+    W1[0, 1, 2 + 5] = 0x98                                       # high nibble 9 -> element 16 + 5
+    assert oracle.q4_0_gemv(W1.reshape(-1), x, 1, K)[0] == np.float32(x[32 + 21] * np.float32(0.5))
