@@ -75,6 +75,12 @@ def test_stream_exec_rejects_unsupported_and_truncated():
     with pytest.raises(ane_b200.AneError) as e:
         ane_b200.stream_exec(full[:-1])
     assert e.value.code == 3
+    for op in (Op.q4_k_gemv, Op.q2_k_gemv, Op.q3_k_gemv, Op.q5_k_gemv, Op.q6_k_gemv, Op.get_rows_q4_0):
+        full = encode(op, U32(32), U32(256), Ptr(1), Ptr(2), Ptr(3))
+        assert len(full) == 33
+        with pytest.raises(ane_b200.AneError) as e:
+            ane_b200.stream_exec(full[:-3])
+        assert e.value.code == 3, op
     # 0x00 ends the stream (jump-table slot 0 = exit) and an empty stream is a no-op
     ane_b200.stream_exec(bytes([0x00]) + bytes([0x14]))
     ane_b200.stream_exec(b"")
