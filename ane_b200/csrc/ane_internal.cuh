@@ -52,6 +52,16 @@ inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_o
 // Device properties of the current device (cached per device).
 int num_sms();
 
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
+// device.  The attribute belongs to one device context, so a process that
+// drives several GPUs must set it on each: `done` is the caller's per-kernel
+// bitmask of devices already set (devices >= 64 are set on every call).
+int set_max_dynamic_smem_impl(const void* kernel, int bytes, std::atomic<uint64_t>& done);
+template <typename F>
+inline int set_max_dynamic_smem(F* kernel, int bytes, std::atomic<uint64_t>& done) {
+    return set_max_dynamic_smem_impl(reinterpret_cast<const void*>(kernel), bytes, done);
+}
+
 // Integer tuning override from the environment (0 / unset = automatic choice).
 inline int env_int(const char* name) {
     const char* v = getenv(name);
@@ -94,6 +104,8 @@ int require_sm100();
 // Device-side bounded-wait failure counter (incremented by kernels that give up).
 int read_and_reset_device_timeouts(cudaStream_t s);
 int* device_timeout_flag();  // device address of the counter
+// Same for the allocation-free dense_fused_i8 path's own counter (noalloc.cu).
+int noalloc_read_and_reset_timeouts(cudaStream_t s);
 
 // While a ScopedLaunchOverride is alive on a thread, num_sms() and
 // device_timeout_flag() return its values instead of touching the lazily

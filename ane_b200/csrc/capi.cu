@@ -229,6 +229,15 @@ int num_sms() {
     int s = device_info().sms;
     return s > 0 ? s : 148;
 }
+int set_max_dynamic_smem_impl(const void* kernel, int bytes, std::atomic<uint64_t>& done) {
+    int dev = 0;
+    ANE_CUDA_TRY(cudaGetDevice(&dev));
+    const uint64_t bit = (dev >= 0 && dev < 64) ? (uint64_t)1 << dev : 0;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return ANE_OK;
+    ANE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.fetch_or(bit, std::memory_order_release);  // a racing second set is harmless
+    return ANE_OK;
+}
 int require_sm100() {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
@@ -275,7 +284,7 @@ const char* ane_version(void) { return "ane_b200 0.1 (sm_100a)"; }
 uint64_t ane_kernel_launch_count(void) { return g_launches.load(); }
 int ane_device_timeouts(void) {
     if (require_sm100()) return 0;
-    return read_and_reset_device_timeouts(nullptr);
+    return read_and_reset_device_timeouts(nullptr) + noalloc_read_and_reset_timeouts(nullptr);
 }
 
 size_t ane_absmax_partials_count(size_t count_a, size_t count_b) {

@@ -349,9 +349,8 @@ int stack_plan_create(const ane_q8_stack_proj* projs, uint32_t nproj, uint32_t w
 int stack_plan_run(void* plan_ptr, cudaStream_t s) {
     ANE_ARG_CHECK(plan_ptr, "q8_stack: NULL plan");
     auto* plan = static_cast<StackPlan*>(plan_ptr);
-    static const cudaError_t attr_err = cudaFuncSetAttribute(
-        decode_stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024);
-    ANE_CUDA_TRY(attr_err);
+    static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
+    if (int arc = set_max_dynamic_smem(decode_stack_kernel, 226 * 1024, smem_set)) return arc;
     ANE_ARG_CHECK(num_sms() <= 256, "q8_stack: the guard words assume at most 256 SMs");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)num_sms(), 1, 1);

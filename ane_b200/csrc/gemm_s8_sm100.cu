@@ -507,11 +507,6 @@ int make_kmajor_map(CUtensorMap* map, const int8_t* base, uint32_t rows, uint32_
                                 CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-int set_smem_attr_once(const void* fn, size_t bytes, std::once_flag& flag, cudaError_t& err) {
-    std::call_once(flag, [&] { err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes); });
-    ANE_CUDA_TRY(err);
-    return ANE_OK;
-}
 
 }  // namespace
 
@@ -558,9 +553,8 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
     rc = make_kmajor_map(&tb, Bt, N, K, pair ? P_HN : S_BN);
     if (rc) return rc;
     if (!pair) {
-        static std::once_flag f;
-        static cudaError_t e;
-        rc = set_smem_attr_once((const void*)gemm_s8_single_kernel, S_SMEM, f, e);
+        static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
+        rc = set_max_dynamic_smem(gemm_s8_single_kernel, (int)S_SMEM, smem_set);
         if (rc) return rc;
         p.tiles_m = (M + S_BM - 1) / S_BM;
         p.tiles_n = (N + S_BN - 1) / S_BN;
@@ -569,9 +563,8 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
         if (grid_out) *grid_out = grid;
         return launch_pdl(gemm_s8_single_kernel, dim3(grid), dim3(NUM_THREADS), S_SMEM, s, ta, tb, p);
     }
-    static std::once_flag f2;
-    static cudaError_t e2;
-    rc = set_smem_attr_once((const void*)gemm_s8_pair_kernel, P_SMEM, f2, e2);
+    static std::atomic<uint64_t> smem_set2{0};
+    rc = set_max_dynamic_smem(gemm_s8_pair_kernel, (int)P_SMEM, smem_set2);
     if (rc) return rc;
     p.tiles_m = (M + P_BM - 1) / P_BM;
     p.tiles_n = (N + P_BN - 1) / P_BN;

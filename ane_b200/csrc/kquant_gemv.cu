@@ -355,9 +355,8 @@ int launch_kquant_stream(uint32_t M, uint32_t nsb, const float* x, const uint8_t
     constexpr uint32_t BB = KBlock<F>::bytes, C = KBlock<F>::chunk, CB = C * BB;
     constexpr uint32_t TILE = (kQ8RowsPerWarp * CB + 127) / 128 * 128;
     const Q8Plan p = plan_q8_stream(M, nsb * 256, C * 1024, 128, (BB + 7) / 8, TILE);
-    static const cudaError_t attr_err =
-        cudaFuncSetAttribute(kquant_stream_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    ANE_CUDA_TRY(attr_err);
+    static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
+    if (int arc = set_max_dynamic_smem(kquant_stream_kernel<F>, 200 * 1024, smem_set)) return arc;
     ANE_ARG_CHECK(p.smem <= 200 * 1024, "kquant_gemv: shared-memory plan too large");
     const uint64_t row_bytes = (uint64_t)nsb * BB;
     CUtensorMap wmap;

@@ -25,6 +25,11 @@
 //  * The first call on a device looks the array's device address up with
 //    cudaGetSymbolAddress (once per device, that device current).  Make that
 //    first call before any stream capture.
+//  * The call returns once its kernels are enqueued.  A bounded device-side
+//    wait that gives up inside them is counted in a counter of this path;
+//    ane_device_timeouts() reads and resets it together with the library's
+//    main counter, so check it after synchronising the stream.
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -41,6 +46,7 @@ static __device__ int g_noalloc_timeouts;  // target of the kernels' bounded wai
 
 struct DeviceScratch {
     std::once_flag once;
+    std::atomic<bool> ready{false};  // set-up done: scratch and timeouts hold device addresses
     cudaError_t err = cudaSuccess;
     void* scratch = nullptr;
     int* timeouts = nullptr;
@@ -50,6 +56,29 @@ struct DeviceScratch {
 DeviceScratch g_scratch[kMaxDevices];
 
 }  // namespace
+
+// Bounded-wait failures of kernels launched by the allocation-free entry point
+// on the current device since the last read, and resets the count (0 if that
+// entry point never ran on this device).  ane_device_timeouts() adds this to the
+// library's main counter, so one call reports every timed-out wait.
+int noalloc_read_and_reset_timeouts(cudaStream_t s) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return 0;
+    }
+    DeviceScratch& d = g_scratch[dev];
+    if (!d.ready.load(std::memory_order_acquire) || !d.timeouts) return 0;
+    int v = 0;
+    if (cudaMemcpyAsync(&v, d.timeouts, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    cudaStreamSynchronize(s);
+    if (v) cudaMemsetAsync(d.timeouts, 0, sizeof(int), s);
+    return v;
+}
+
 }  // namespace ane_b200
 
 using namespace ane_b200;
@@ -81,6 +110,7 @@ extern "C" int ane_dense_fused_i8_noalloc_dev(uint32_t M, uint32_t N, uint32_t K
         if (d.err == cudaSuccess) d.err = cudaGetSymbolAddress((void**)&d.timeouts, g_noalloc_timeouts);
         if (d.err == cudaSuccess) d.err = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
         if (d.err == cudaSuccess) d.err = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+        if (d.err == cudaSuccess) d.ready.store(true, std::memory_order_release);
     });
     if (d.err != cudaSuccess || !d.scratch) {
         set_status(ANE_ERR_CUDA, std::string("dense_fused_i8_noalloc: scratch set-up failed: ") + cudaGetErrorString(d.err));

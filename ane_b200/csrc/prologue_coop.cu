@@ -550,9 +550,8 @@ int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, con
         xr.slots = static_cast<const uint64_t*>(x->slots);
         xr.ctl = x->ctl;
     }
-    static const cudaError_t attr_err = cudaFuncSetAttribute(
-        prologue_coop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCoopSmem);
-    ANE_CUDA_TRY(attr_err);
+    static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
+    if (int arc = set_max_dynamic_smem(prologue_coop_kernel, (int)kCoopSmem, smem_set)) return arc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)num_sms(), 1, 1);
     cfg.blockDim = dim3(kCoopThreads, 1, 1);

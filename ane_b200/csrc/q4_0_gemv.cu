@@ -224,9 +224,8 @@ int launch_q4_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, f
     ANE_ARG_CHECK(K % 32 == 0, "q4_0_gemv: K must be a multiple of 32");
     if (K % 256 == 0 && ((uintptr_t)W & 15) == 0 && ((uintptr_t)x & 15) == 0) {
         const Q8Plan p = plan_q8_stream(M, K, kQ4ChunkXBytes, 128, kQ4BlockBytes, kQ4WarpTileBytes);
-        static const cudaError_t attr_err = cudaFuncSetAttribute(
-            q4_0_gemv_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        ANE_CUDA_TRY(attr_err);
+        static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
+        if (int arc = set_max_dynamic_smem(q4_0_gemv_stream_kernel, 200 * 1024, smem_set)) return arc;
         ANE_ARG_CHECK(p.smem <= 200 * 1024, "q4_0_gemv: shared-memory plan too large");
         const uint64_t row_bytes = (uint64_t)(K / 32) * kQ4BlockBytes;
         CUtensorMap wmap;

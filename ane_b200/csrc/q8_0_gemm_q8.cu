@@ -432,9 +432,8 @@ int launch_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const float* 
     const uint32_t nthreads = nb * kTok;
     rc = launch_pdl(quantize_x_segments_kernel, dim3((nthreads + 255) / 256), dim3(256), 0, s, x, ldx, NT, nb, records);
     if (rc) return rc;
-    static const cudaError_t attr_err =
-        cudaFuncSetAttribute(q8_0_gemm_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    ANE_CUDA_TRY(attr_err);
+    static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
+    if (int arc = set_max_dynamic_smem(q8_0_gemm_q8_kernel, 227 * 1024, smem_set)) return arc;
     return launch_pdl(q8_0_gemm_q8_kernel, dim3(ctas), dim3(32 * (1 + a.ntiles * a.ngroups)), smem, s, wmap8, wmap4,
                       (const uint8_t*)records, a, device_timeout_flag());
 }

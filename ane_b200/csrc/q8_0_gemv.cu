@@ -298,9 +298,8 @@ int launch_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, f
     ANE_ARG_CHECK(((uintptr_t)W & 1) == 0, "q8_0_gemv: W must be 2-byte aligned");
     if (K % 256 == 0 && ((uintptr_t)W & 15) == 0 && ((uintptr_t)x & 15) == 0) {
         const Q8Plan p = plan_q8_stream(M, K, kChunkXBytes, 128);
-        static const cudaError_t attr_err = cudaFuncSetAttribute(
-            q8_0_gemv_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        ANE_CUDA_TRY(attr_err);
+        static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
+        if (int arc = set_max_dynamic_smem(q8_0_gemv_stream_kernel, 200 * 1024, smem_set)) return arc;
         ANE_ARG_CHECK(p.smem <= 200 * 1024, "q8_0_gemv: shared-memory plan too large");
         const uint64_t row_bytes = (uint64_t)(K / 32) * 34;
         CUtensorMap wmap;

@@ -230,9 +230,8 @@ static int launch_gemv_q8(uint32_t M, uint32_t K, const uint8_t* x, const uint8_
                          round_up(K, 128);
     const Q8Plan p = plan_q8_stream(M, K, 0, fixed);
     ANE_ARG_CHECK(p.smem <= 200 * 1024, "q8_0_gemv_q8: K too large for the shared activation buffer");
-    static const cudaError_t attr_err =
-        cudaFuncSetAttribute(q8_0_gemv_q8_kernel<XF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    ANE_CUDA_TRY(attr_err);
+    static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
+    if (int arc = set_max_dynamic_smem(q8_0_gemv_q8_kernel<XF32>, 200 * 1024, smem_set)) return arc;
     const uint64_t row_bytes = (uint64_t)nb * 34;
     CUtensorMap wmap;
     int rc = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, row_bytes / 4, M, row_bytes,

@@ -1,8 +1,11 @@
 """Q8_0 decode stack: a 7B-shaped stack of Q8_0 matvecs, N-sharded by rows.
 
 Per layer four projections run back to back (ggml MUL_MAT at batch 1 with
-Q8_0 weights, src/ggml-backend/ggml-ane.cpp:142-177; the activation of each
-matvec is first quantized to Q8_0, the ggml CPU convention for Q8_0 weights):
+Q8_0 weights, src/ggml-backend/ggml-ane.cpp:142-177), in one of two
+arithmetics: mode "q" quantizes each matvec's activation to Q8_0 first (the
+ggml CPU convention for Q8_0 weights); mode "r" keeps the
+activation in fp32 and runs the reference's q8_0_gemv, as its ggml backend
+does:
 
     QKV      12288 x 4096
     O         4096 x 4096
@@ -127,16 +130,28 @@ class DecodeStack:
 # ------------------------------------------------------------------ GPU binding
 def gpu_stack(layers: int, device, world: int = 1, rank: int = 0, group=None, seed: int = 5,
               shapes: Sequence = LAYER_SHAPES, static_weights: bool = True, batch: int = 1,
-              weights: list | None = None) -> DecodeStack:
+              weights: list | None = None, first_layer: int = 0, mode: str = "q") -> DecodeStack:
     """DecodeStack on libane_b200 with an NCCL all-gather.  batch 1: one launch
     per projection (Q8_0 activation quantization fused into the Q8_0 x Q8_0
-    matvec); batch > 1: the batched MUL_MAT (weights read once for all tokens)."""
+    matvec); batch > 1: the batched MUL_MAT (weights read once for all tokens).
+    first_layer: the stack holds layers first_layer .. first_layer+layers-1 of
+    the seeded model (same weights and inputs as those layers of a taller stack),
+    so one GPU can recompute the last layer of a sharded run.
+    mode "q": the activation is quantized to Q8_0 and multiplied block by block
+    in int32 (ggml's CPU convention for Q8_0 weights); mode "r": the
+    reference's own arithmetic -- q8_0_gemv on the fp32 activation
+    (src/ggml-backend/ggml-ane.cpp:160-166 hands src1 to q8_0_gemv, whose
+    handler keeps x in fp32, src/bytecode_interpreter.s:7010-7063), batch 1."""
+    if mode not in ("q", "r"):
+        raise ValueError("mode is 'q' (Q8_0 activation) or 'r' (fp32 activation, reference arithmetic)")
+    if mode == "r" and batch != 1:
+        raise ValueError("mode 'r' runs one token per step: the reference's MUL_MAT computes column 0 only")
     import ane_b200 as ane
 
     workspaces, gather_bufs = {}, {}
 
     def make_rows(layer, p, blk, K):
-        g = torch.Generator(device=device).manual_seed(block_seed(seed, layer, p, blk))
+        g = torch.Generator(device=device).manual_seed(block_seed(seed, first_layer + layer, p, blk))
         w = torch.randn(ROW_BLOCK * K, device=device, generator=g) * 0.02
         return ane.quantize_q8_0(w)
 
@@ -145,6 +160,8 @@ def gpu_stack(layers: int, device, world: int = 1, rank: int = 0, group=None, se
         return x
 
     def matvec(W, x, rows, K, out):
+        if mode == "r":
+            return ane.q8_0_gemv(W, x, rows, K, out=out, static_weights=static_weights)
         if batch == 1:
             return ane.mul_mat_q8_0(W, x, rows, K, out=out, static_weights=static_weights)
         if (rows, K) not in workspaces:
@@ -166,7 +183,8 @@ def gpu_stack(layers: int, device, world: int = 1, rank: int = 0, group=None, se
 
     def make_inputs(n, K):
         g = torch.Generator(device=device).manual_seed(seed + 17)
-        return torch.randn(n, K, device=device, generator=g)
+        skip = first_layer * batch  # rows of the layers below first_layer
+        return torch.randn(skip + n, K, device=device, generator=g)[skip:]
 
     alloc = lambda n, dtype: torch.empty(n, dtype=dtype, device=device)  # noqa: E731
     return DecodeStack(layers, world, rank, make_rows, quantize, matvec, gather, shapes, alloc, make_inputs, batch,

@@ -43,8 +43,8 @@ sys.path.insert(0, ROOT)
 METRIC = "int8 GEMM TOPS (4096³) & Q8_0 matvec GB/s at 1/2/4/8 B200"
 M = N = K = 4096
 SCALE, RELU = 1.0, False
-# DRAM read + write of one gemm_s8_pair_kernel launch at 4096^3, from the ncu
-# capture summarised in profiles/gemm_s8_pair_dense_fused_4096.md
+# DRAM read + write of one gemm_s8_pair_kernel launch at 4096^3 (ncu,
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel).
 GEMM_TRAFFIC_BYTES = 33_807_616 + 17_284_352
 
 
@@ -60,7 +60,67 @@ def parse():
     p.add_argument("--no-configs", action="store_true", help="skip the config 1 / 2-sweep / 4 legs")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (profiling runs)")
     p.add_argument("--no-clocks", action="store_true", help="skip nvidia-smi sampling and its soak (profiling runs)")
+    p.add_argument("--profile-case", default=None,
+                   help="profiling aid: run one kernel on one small case --steps times and exit, no JSON line. "
+                        "dense:<n> (dense_fused_i8 n^3), q8r:<M>x<K> (q8_0_gemv, fp32 x), q8q:<M>x<K> "
+                        "(MUL_MAT, Q8_0 x), kq:<fmt>:<M>x<K> (K-quant matvec), b16:<M>x<K> (batched MUL_MAT)")
     return p.parse_args()
+
+
+def run_profile_case(args):
+    """One kernel on one case, `steps` times after `warmup` calls: a small,
+    self-ending workload for ncu captures (no timing, no JSON)."""
+    import torch
+
+    import ane_b200 as ane
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    kind, _, rest = args.profile_case.partition(":")
+    g = torch.Generator(device=dev).manual_seed(7)
+    if kind == "dense":
+        n = int(rest)
+        A = torch.randn((n, n), device=dev, generator=g)
+        B = torch.randn((n, n), device=dev, generator=g)
+        C = torch.empty((n, n), device=dev)
+        ws = ane.dense_fused_i8_workspace(n, n, n, dev)
+        fn = lambda: ane.dense_fused_i8(A, B, 1.0, False, out=C, workspace=ws)  # noqa: E731
+    else:
+        fmt = None
+        if kind == "kq":
+            fmt, _, rest = rest.partition(":")
+        rows, cols = (int(v) for v in rest.split("x"))
+        if kind == "kq":
+            bb = ane.KQUANT_BLOCK_BYTES[fmt]
+            W = torch.randint(0, 256, (rows * (cols // 256) * bb,), dtype=torch.uint8, device=dev, generator=g)
+            for off in {"q2_k": (81, 83), "q3_k": (109,), "q4_k": (1, 3), "q5_k": (1, 3), "q6_k": (209,)}[fmt]:
+                W.view(-1, bb)[:, off] = 0x1C  # small positive fp16 scales
+        else:
+            W = torch.randint(0, 256, (rows * (cols // 32) * 34,), dtype=torch.uint8, device=dev, generator=g)
+            W.view(-1, 34)[:, 1] = 0x1C  # fp16 scales in [2^-8, 2^-7)
+        x = torch.randn(cols, device=dev, generator=g)
+        y = torch.empty(rows, device=dev)
+        if kind == "q8r":
+            fn = lambda: ane.q8_0_gemv(W, x, rows, cols, out=y, static_weights=True)  # noqa: E731
+        elif kind == "q8q":
+            fn = lambda: ane.mul_mat_q8_0(W, x, rows, cols, out=y, static_weights=True)  # noqa: E731
+        elif kind == "kq":
+            fn = lambda: ane.kquant_gemv(fmt, W, x, rows, cols, out=y)  # noqa: E731
+        elif kind == "b16":
+            xb = torch.randn((16, cols), device=dev, generator=g)
+            yb = torch.empty((16, rows), device=dev)
+            wsb = ane.mul_mat_q8_0_batch_workspace(rows, cols, dev)
+            fn = lambda: ane.mul_mat_q8_0_batch(W, xb, rows, cols, out=yb, workspace=wsb,  # noqa: E731
+                                                static_weights=True)
+        else:
+            raise SystemExit(f"unknown --profile-case {args.profile_case}")
+    for _ in range(args.warmup):
+        fn()
+    for _ in range(args.steps):
+        fn()
+    torch.cuda.synchronize()
+    assert ane.lib.ane_device_timeouts() == 0
+    print(f"profile case {args.profile_case}: {args.warmup} + {args.steps} calls done", flush=True)
 
 
 def load_peaks():
@@ -132,56 +192,82 @@ def dist_env():
     return world, rank, local
 
 
+def host_cores() -> int:
+    """Host threads this process may run on (all of them, whatever OMP_NUM_THREADS says)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def workload_config(world: int) -> dict:
+    """The `config` of the headline line; both arms print the same one."""
+    return {"workload": "dense_fused_i8 M=N=K=4096 scale=1.0 relu=off, fp32 N(0,1) A and B in HBM"
+                        + ("" if world == 1 else f"; A/C row-sharded, {M} rows per rank, B replicated, "
+                           "absmax exchanged between GPUs inside the cooperative prologue (tagged NVLink "
+                           "peer words), all-gather of C fused into the GEMM epilogue (NVLink peer stores); "
+                           "no NCCL call in the step"),
+            "M_per_rank": M, "N": N, "K": K,
+            "l2": ("inputs larger than L2: two (A, B) fp32 pairs of 128 MiB alternate between steps, no flush; "
+                   "within a step each fp32 tensor's second read (quantize after absmax) is served from "
+                   "L2 by design"),
+            "parallelism": f"n-shard{world}" if world > 1 else "single"}
+
+
+def cpu_dense_sample(rows: int, threads: int, reps: int):
+    """The oracle's OpenMP dense_fused_i8 (the reference's semantics restated in
+    C) on `rows` rows of A against the full 4096 x 4096 B: (TOPS, s per rep)."""
+    import numpy as np
+
+    import oracle
+
+    rng = np.random.default_rng(1234)
+    A = rng.standard_normal((rows, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    oracle.dense_fused_i8_omp(A[:16], B, SCALE, RELU, threads)  # warm (pages, threads)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        oracle.dense_fused_i8_omp(A, B, SCALE, RELU, threads)
+    dt = (time.perf_counter() - t0) / reps
+    return 2.0 * rows * N * K / dt / 1e12, dt
+
+
+def cpu_baseline_record(all_cores: int, rows_all: int, reps_all: int, tops_all: float):
+    """cpu_baseline object: the all-cores figure plus a single-thread one."""
+    rows_1 = 16
+    tops_1, _ = cpu_dense_sample(rows_1, 1, 1)
+    return {"value": tops_all, "unit": "TOPS", "cores": all_cores, "kind": "port",
+            "sample": (f"oracle OpenMP dense_fused_i8 on {all_cores} host threads: rows 0..{rows_all - 1} of A "
+                       f"(of {M}) x the full {K}x{N} B per rep, quantize of the full B included, {reps_all} reps"),
+            "single_thread": {"value": tops_1, "unit": "TOPS", "cores": 1,
+                              "sample": f"rows 0..{rows_1 - 1} of A x the full B, 1 rep"}}
+
+
 # --------------------------------------------------------------------------- reference arm
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    import numpy as np
-
-    import oracle
-
-    threads = oracle.max_threads()
-    rows = 256  # bounded sample: first 256 rows of A against the full 4096 x 4096 B
-    rng = np.random.default_rng(1234)
-    A = rng.standard_normal((rows, K)).astype(np.float32)
-    B = rng.standard_normal((K, N)).astype(np.float32)
+    threads = host_cores()
+    rows = 256  # bounded sample: the first 256 rows of A against the full B per step
     for _ in range(max(1, min(args.warmup, 1))):
-        oracle.dense_fused_i8_omp(A[:16], B, SCALE, RELU, threads)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        oracle.dense_fused_i8_omp(A, B, SCALE, RELU, threads)
-    dt = (time.perf_counter() - t0) / args.steps
-    tops = 2.0 * rows * N * K / dt / 1e12
-    sample = f"rows 0..{rows - 1} of A (of {M}) x full B {K}x{N} per step, quantize of full B included"
+        cpu_dense_sample(16, threads, 1)
+    tops, dt = cpu_dense_sample(rows, threads, args.steps)
+    cpu = cpu_baseline_record(threads, rows, args.steps, tops)
     line = {"impl": "reference", "metric": METRIC, "value": tops, "unit": "TOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "dense_fused_i8 M=N=K=4096 scale=1.0 relu=off (CPU sample)", "sample": sample},
-            "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample},
+            "config": workload_config(world), "cpu_baseline": cpu,
             "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 # --------------------------------------------------------------------------- our arm
 def cpu_baseline_sample():
-    import numpy as np
-
-    import oracle
-
-    threads = oracle.max_threads()
-    rows = 256
-    rng = np.random.default_rng(1234)
-    A = rng.standard_normal((rows, K)).astype(np.float32)
-    B = rng.standard_normal((K, N)).astype(np.float32)
-    oracle.dense_fused_i8_omp(A[:16], B, SCALE, RELU, threads)
-    reps = 3
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        oracle.dense_fused_i8_omp(A, B, SCALE, RELU, threads)
-    dt = (time.perf_counter() - t0) / reps
-    return {"value": 2.0 * rows * N * K / dt / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
-            "sample": f"oracle OpenMP dense_fused_i8, rows 0..{rows - 1} of A x full 4096x4096 B, {reps} reps"}
+    threads = host_cores()
+    rows, reps = 256, 3
+    tops, _ = cpu_dense_sample(rows, threads, reps)
+    return cpu_baseline_record(threads, rows, reps, tops)
 
 
 def time_events(fn, steps, stream):
@@ -393,6 +479,14 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
             torch.distributed.barrier(group)
     finally:
         fused.close()
+    # mode R: the reference's arithmetic (q8_0_gemv on the fp32 activation), same weights
+    stack_r = decode.gpu_stack(layers, dev, world=world, rank=rank, group=group, weights=stack.weights, mode="r")
+    stack_r.forward()
+    torch.cuda.synchronize()
+    gr = capture(stack_r.forward)
+    r_graph = gr is not None
+    r_ms = timed(gr.replay if r_graph else stack_r.forward)
+    del gr
     # batch 16: the same weights, 16 tokens per step through the batched MUL_MAT
     batch = 16
     stack16 = decode.gpu_stack(layers, dev, world=world, rank=rank, group=group, batch=batch,
@@ -402,7 +496,31 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
     g16 = capture(stack16.forward)
     b16_graph = g16 is not None
     b16_ms = timed(g16.replay if b16_graph else stack16.forward)
-    del g16, stack16
+    del g16
+    parity = None
+    if world > 1:
+        # the last layer's outputs of the sharded run against one GPU computing
+        # that layer alone (each layer starts from its own seeded input)
+        outs = {"chain_q": stack.forward().clone(), "mode_r": stack_r.forward().clone(),
+                "batch16": stack16.forward().clone()}
+        fused2 = decode.FusedDecodeStack(stack, dev, group=group)
+        try:
+            outs["fused_q"] = fused2.forward().clone()
+            torch.cuda.synchronize()
+            torch.distributed.barrier(group)
+        finally:
+            fused2.close()
+        if rank == 0:
+            one = decode.gpu_stack(1, dev, first_layer=layers - 1)
+            one_r = decode.gpu_stack(1, dev, first_layer=layers - 1, weights=one.weights, mode="r")
+            one16 = decode.gpu_stack(1, dev, first_layer=layers - 1, weights=one.weights, batch=batch)
+            refs = {"chain_q": one.forward(), "fused_q": one.forward(), "mode_r": one_r.forward(),
+                    "batch16": one16.forward()}
+            torch.cuda.synchronize()
+            parity = {k: bool(torch.equal(outs[k].view(torch.int32), refs[k].view(torch.int32))) for k in outs}
+            del one, one_r, one16, refs
+        torch.distributed.barrier(group)
+    del stack16, stack_r
     wbytes = decode.stack_weight_bytes(layers)
     peaks = load_peaks()
     fused_path = "one persistent launch per token" + (", all-gather by NVLink peer stores" if world > 1 else "")
@@ -414,6 +532,13 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
             "gbs": gbs, "per_gpu_hbm_frac": gbs / world / peaks["hbm_gbs"], "path": best_path,
             "fused_ms_per_token": fused_ms, "fused_gbs": wbytes / (fused_ms * 1e-3) / 1e9, "fused_path": fused_path,
             "chain_ms_per_token": chain_ms, "chain_gbs": wbytes / (chain_ms * 1e-3) / 1e9, "chain_path": chain_path,
+            "mode": "q (Q8_0 activation, ggml convention) for ms_per_token, fused and chain",
+            "mode_r": {"ms_per_token": r_ms, "gbs": wbytes / (r_ms * 1e-3) / 1e9,
+                       "per_gpu_hbm_frac": wbytes / (r_ms * 1e-3) / 1e9 / world / peaks["hbm_gbs"],
+                       "path": (f"{4 * layers} q8_0_gemv launches on the fp32 activation (the reference's "
+                                "arithmetic)" + ("" if world == 1 else " + NCCL all-gather each")
+                                + (" in a CUDA graph" if r_graph else " (eager)"))},
+            "parity_ok_vs_1gpu": parity,
             "batch16": {"ms_per_step": b16_ms, "tokens_per_s": batch / (b16_ms * 1e-3),
                         "weight_gbs": wbytes / (b16_ms * 1e-3) / 1e9,
                         "per_gpu_hbm_frac": wbytes / (b16_ms * 1e-3) / 1e9 / world / peaks["hbm_gbs"],
@@ -535,8 +660,8 @@ def config4_sharded(ane, torch, dev, world, group, steps=20):
     g = torch.Generator(device=dev).manual_seed(4)
     B = torch.randn((4096, 14336), device=dev, generator=g)
     B_local = B[:, rank * n_local:(rank + 1) * n_local].contiguous()
-    del B
     out = {}
+    parity = {}
     for m in (1, 8, 64, 512):
         A = torch.randn((m, 4096), device=dev, generator=g)
         A = torch.where(torch.rand(A.shape, device=dev, generator=g) < 0.01, A * 20, A)
@@ -552,10 +677,37 @@ def config4_sharded(ane, torch, dev, world, group, steps=20):
         ms = float(t.item())
         torch.cuda.synchronize()
         torch.distributed.barrier(group)
+        # the gathered C against one GPU running the whole projection (A is the
+        # same on every rank, B regenerated from its seed)
+        C_gathered = ctx.forward(A, B_local, 0.125, True).clone()
+        torch.cuda.synchronize()
+        torch.distributed.barrier(group)
+        if rank == 0:
+            C_one = ane.dense_fused_i8(A, B, 0.125, True)
+            torch.cuda.synchronize()
+            parity[str(m)] = bool(torch.equal(C_gathered.view(torch.int32), C_one.view(torch.int32)))
+            del C_one
+        del C_gathered
+        torch.distributed.barrier(group)
         ctx.close()
         out[str(m)] = {"tops": 2.0 * m * 14336 * 4096 / (ms * 1e-3) / 1e12, "ms": ms}
-    del flush, B_local
-    return {"config4_projection_sharded": {"n_gpus": world, "shard": f"cols, 14336/{world} per rank", **out}}
+    del flush, B_local, B
+    return {"config4_projection_sharded": {"n_gpus": world, "shard": f"cols, 14336/{world} per rank", **out,
+                                           "parity_ok_vs_1gpu": parity if rank == 0 else None}}
+
+
+def parity_summary(world, headline, legs, dec):
+    """N > 1: every sharded result that rank 0 checked against one GPU, bit for
+    bit (headline C, config 4 at each M, the decode stack's last layer in each
+    path); True only if all of them matched.  N = 1: None (the single-GPU path
+    is checked against the oracle by the test suite)."""
+    if world == 1:
+        return None
+    checks = {"headline_c": headline}
+    c4 = (legs or {}).get("config4_projection_sharded", {}).get("parity_ok_vs_1gpu") or {}
+    checks.update({f"config4_m{m}": v for m, v in c4.items()})
+    checks.update({f"decode_{k}": v for k, v in ((dec or {}).get("parity_ok_vs_1gpu") or {}).items()})
+    return {"all": all(v is True for v in checks.values()), "checks": checks}
 
 
 def run_ours(args):
@@ -648,7 +800,7 @@ def run_ours(args):
     ops_per_rank = 2.0 * M * N * K
     value = world * ops_per_rank / (ms * 1e-3) / 1e12
     launches_per_step = launches / float(args.steps) if args.steps else 0
-    no_gather_ms = nccl_gather_ms = None
+    no_gather_ms = nccl_gather_ms = parity_headline = None
     if world > 1:
         def max_ranks(v):
             t = torch.tensor([v], device=dev)
@@ -663,6 +815,20 @@ def run_ours(args):
             ctx_nccl.forward(A, B, SCALE, RELU)
         nccl_gather_ms = max_ranks(time_events(lambda: ctx_nccl.forward(A, B, SCALE, RELU), args.steps, stream))
         torch.cuda.synchronize()
+        torch.distributed.barrier()
+        # rank 0's gathered C against one GPU computing the whole (N*4096) x 4096 x 4096
+        # problem on the same inputs (every rank's A block regenerated from its seed)
+        C_gathered = ctx.forward(A, B, SCALE, RELU).clone()
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        if rank == 0:
+            A_all = torch.cat([torch.randn((M, K), device=dev, generator=torch.Generator(device=dev).manual_seed(1234 + r))
+                               for r in range(world)])
+            C_one = ane.dense_fused_i8(A_all, B, SCALE, RELU)
+            torch.cuda.synchronize()
+            parity_headline = bool(torch.equal(C_gathered.view(torch.int32), C_one.view(torch.int32)))
+            del A_all, C_one
+        del C_gathered
         torch.distributed.barrier()
 
     # ---- dominant kernel alone: tcgen05 GEMM on resident quantized operands
@@ -750,24 +916,16 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "dense_fused_i8 M=N=K=4096 scale=1.0 relu=off, fp32 N(0,1) A and B in HBM"
-                               + ("" if world == 1 else f"; A/C row-sharded, {M} rows per rank, B replicated, "
-                                  "absmax exchanged between GPUs inside the cooperative prologue (tagged NVLink "
-                                  "peer words), all-gather of C fused into the GEMM epilogue (NVLink peer stores); "
-                                  "no NCCL call in the step"),
-                   "M_per_rank": M, "N": N, "K": K,
-                   "l2": ("inputs larger than L2: two (A, B) fp32 pairs of 128 MiB alternate between steps, no flush; "
-                          "within a step each fp32 tensor's second read (quantize after absmax) is served from "
-                          "L2 by design"),
-                   "parallelism": f"n-shard{world}" if world > 1 else "single"},
+        "config": workload_config(world),
         "roofline": {"bound": "tensor", "kernel": "gemm_s8_pair_kernel (tcgen05 kind::i8, cta_group::2)",
                      "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS", "frac": gemm_tops / int8_peak,
                      "peak_source": f"2 x {peaks['source']} bf16 burst ({peaks['bf16_tflops']} TFLOP/s)",
                      "traffic": GEMM_TRAFFIC_BYTES, "traffic_unit": "bytes per launch (DRAM read + write)",
-                     "traffic_source": "ncu capture, profiles/gemm_s8_pair_dense_fused_4096.md",
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch",
                      "algorithmic_bytes": M * K + N * K + 4 * M * N, "gemm_ms": gemm_ms},
         "stages_ms": {"quantize_pair": q_ms, "gemm": gemm_ms, "step": ms, "step_nccl_path_without_all_gather": no_gather_ms,
                       "step_with_nccl_all_gather": nccl_gather_ms},
+        "parity_ok": parity_summary(world, parity_headline, legs, dec),
         "e2e": e2e, "gpu_launches": int(launches), "gpu_launches_per_step": launches_per_step,
         "clocks": clocks, "q8_0_gemv": q8, "decode_stack": dec, "configs": legs, "cpu_baseline": cpu,
     }
@@ -778,7 +936,9 @@ def run_ours(args):
 
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.profile_case:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -338,12 +338,19 @@ int ane_ipc_close_handle(void* base);
  * Every GPU that loads this part of the library keeps the 40 MiB until exit.
  * All calls on a device share the array: calls whose kernels overlap on the
  * GPU race, so serialise them.  The first call on each device looks the array
- * up (cudaGetSymbolAddress); make it before any stream capture. */
+ * up (cudaGetSymbolAddress); make it before any stream capture.  A timed-out
+ * device wait inside the call is reported by ane_device_timeouts(). */
 int ane_dense_fused_i8_noalloc_dev(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t relu,
                                    const float* A, const float* B, float* C, void* stream);
 
 /* ------------------------------------------------------------ diagnostics */
-/* Device-side bounded-wait failures since the last call (and reset). */
+/* Device-side bounded-wait failures on the current device since the last call
+ * (and reset): every kernel wait is bounded (about 2 s) and, when it gives up,
+ * counts here and unwinds instead of hanging.  Covers every entry point,
+ * ane_dense_fused_i8_noalloc_dev included; the synchronous entry points also
+ * return ANE_ERR_DEVICE_TIMEOUT themselves.  Call it after synchronising the
+ * stream of an asynchronous (*_dev) call.  After a timeout, treat the device as
+ * failed: copies that the kernel had in flight may still land. */
 int ane_device_timeouts(void);
 /* Kernel launches this library issued since process start (all threads). */
 uint64_t ane_kernel_launch_count(void);

@@ -108,3 +108,28 @@ def test_fused_stack_equals_per_projection_chain(ane, shapes, layers):
         assert ane.lib.ane_device_timeouts() == 0
     finally:
         fused.close()
+
+
+@pytest.mark.parametrize("shapes,layers", [("small", 2), ("config5", 1)])
+def test_decode_stack_mode_r_steps_exact(ane, shapes, layers):
+    """Config 5 with the reference's arithmetic (mode R): each projection is
+    q8_0_gemv on the fp32 activation -- what the reference's ggml MUL_MAT Q8_0
+    branch dispatches (src/ggml-backend/ggml-ane.cpp:160-166) -- and equals
+    the oracle's q8_0_gemv of that step's input bit for bit (the handler's
+    16-lane FMA order and FADDV tree, src/bytecode_interpreter.s:7010-7063)."""
+    import torch
+
+    from ane_b200.decode import LAYER_SHAPES, gpu_stack
+
+    sh = LAYER_SHAPES if shapes == "config5" else (("qkv", 512, 256), ("o", 256, 256), ("gate_up", 512, 256),
+                                                   ("down", 256, 256))
+    stack = gpu_stack(layers, torch.device("cuda", 0), shapes=sh, seed=13, mode="r")
+    trace = []
+    out = stack.forward(trace)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    assert len(trace) == layers * len(sh)
+    for (l, p, x, y) in trace:
+        _, M, K = sh[p]
+        ref = oracle.q8_0_gemv(stack.weights[l][p].cpu().numpy(), x.contiguous().cpu().numpy(), M, K)
+        assert np.array_equal(ref.view(np.uint32), y.contiguous().cpu().numpy().view(np.uint32)), (l, p)
