@@ -176,7 +176,7 @@ struct CoopXRank {
     uint32_t* ctl;       // this GPU's 2 control words
 };
 int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq, int8_t* Bt,
-                         float* scales, float* partials, cudaStream_t s, const CoopXRank* x = nullptr);
+                         float* scales, cudaStream_t s, const CoopXRank* x = nullptr);
 // dense_fused_i8 prologue in three programmatic-dependent launches with each fp32
 // tensor kept L2-resident between its absmax read and its quantize read;
 // partials must hold 2 x 1024 floats.

@@ -189,7 +189,7 @@ static int launch_prologue(uint32_t M, uint32_t N, uint32_t K, const float* A, c
     static const char* force = getenv("ANE_PROLOGUE");
     const bool staged = force && !strcmp(force, "staged");
     if (!staged && prologue_coop_supported(M, N, K, A, B, Aq, Bt))
-        return launch_prologue_coop(M, N, K, A, B, Aq, Bt, scales, partials, s);
+        return launch_prologue_coop(M, N, K, A, B, Aq, Bt, scales, s);
     return launch_quantize_staged(M, N, K, (uint32_t)round_up(K, 16), A, B, Aq, Bt, scales, partials, s);
 }
 
@@ -589,7 +589,8 @@ int ane_quantize_pair_xrank_dev(uint32_t M, uint32_t N, uint32_t K, const float*
     for (uint32_t q = 0; q < world && world > 1; q++) x.slot_peer[q] = slot_peer[q];
     x.slots = slots;
     x.ctl = ctl;
-    int rc = launch_prologue_coop(M, N, K, A, B, Aq, Bt, scales, partials, static_cast<cudaStream_t>(stream), &x);
+    (void)partials;  // the cooperative prologue reduces through its own control block
+    int rc = launch_prologue_coop(M, N, K, A, B, Aq, Bt, scales, static_cast<cudaStream_t>(stream), &x);
     return rc ? rc : ok();
 }
 

@@ -5,27 +5,39 @@
 // (quantize_fp32_i8, src/bytecode_interpreter.s:1876-1950) must be complete
 // before the first code can be produced.  At M=N=K=4096 each fp32 tensor is
 // 64 MB, more than the part of the 126 MB L2 that keeps a re-read tensor, so a
-// second pass streams it from HBM again.  Here every CTA (one per SM) owns a
-// contiguous slice of the tensor; during the absmax pass it keeps the first
-// 192 KB of its slice in shared memory (~28 MB over 148 SMs) and marks the rest
-// evict_last in L2 (~36 MB); after a grid-wide barrier it quantizes from shared
-// memory and L2.  HBM traffic per call: A and B once (fp32) plus Aq and Bt
-// (int8) -- 160 MB at 4096^3 instead of 288 MB.
+// second pass would stream it from HBM again.  Here each tensor is split into
+//   * a RESIDENT part: CTA c (one per SM) owns a fixed 192 KB slice that
+//     bulk copies bring into its shared memory during the absmax pass
+//     (~28 MB over 148 SMs); the quantize pass reads it from there;
+//   * a REMAINDER, handed out in 64 KB chunks (A) or 64 KB units (B) through
+//     per-phase work counters, so CTAs that stream faster take more and all
+//     finish together; the absmax pass marks it evict_last in L2 and the
+//     quantize pass reads it back from L2.
+// HBM traffic per call: A and B once (fp32) plus Aq and Bt (int8).
 //
-//   phase A1  absmax of the CTA's A slice (cache it), partials[c]      | barrier
-//   phase A2  global absmax of A -> scales[0]; codes of the slice -> Aq
-//   phase B1  absmax of the CTA's B units (32 rows x 512 columns; cache the
-//             first three), partials[G+c]                            | barrier
-//   phase B2  global absmax of B -> scales[1]; per unit, codes transposed
-//             through shared memory -> one aligned 32-byte run per Bt row
+//   A1  resident A slice -> smem (bulk copies); remainder chunks: absmax;
+//       absmax of the smem slice; atomicMax into the launch's abs_a  | barrier
+//   A2  codes of the smem slice -> Aq; then B's resident units are requested
+//       into the freed shared memory (TMA) while the A remainder is quantized
+//       from L2 -> Aq
+//   B1  remainder units of B: absmax; then the resident units in smem;
+//       atomicMax into abs_b                                          | barrier
+//   B2  per unit (32 rows x 512 columns), codes transposed through shared
+//       memory -> one aligned 32-byte run per Bt row; resident units first,
+//       then remainder units refilled into the freed slots by TMA from L2,
+//       two units ahead of the arithmetic
 //
-// The grid barrier is a self-resetting sense-reversal barrier on two words of a
-// per-device __device__ array (zero at module load); its waits are bounded and
-// record a device timeout instead of hanging.  Two launches of this kernel can
-// never be resident at once (each CTA takes more than half of an SM's shared
-// memory), so one barrier per device suffices.
+// Each launch takes one of kSlots per-device control blocks (round robin on
+// the host), so launches that overlap on the GPU from different streams never
+// share counters.  Every word of a block is zero between launches: after each
+// grid barrier CTA 0 zeroes the counters of the phases that just ended, the
+// last CTA to finish zeroes the rest.  Every wait is bounded and records a
+// device timeout instead of hanging; after a timeout the block may be left
+// mid-count and the device must be treated as failed.
 #include <cuda.h>
 #include <string.h>
+
+#include <atomic>
 
 #include "ane_internal.cuh"
 #include "sm100_ptx.cuh"
@@ -37,14 +49,34 @@ constexpr int kCoopThreads = 512;
 // B is handled in units of 32 rows x 512 columns (64 KB of fp32); a unit's codes
 // form one aligned 32-byte run in each of 512 rows of Bt.
 constexpr uint32_t kUnitRows = 32, kUnitCols = 512, kUnitF4 = kUnitRows * kUnitCols / 4;
-constexpr uint32_t kCacheSlots = 3;                      // units of B kept in shared memory
-constexpr uint32_t kCacheF4 = kCacheSlots * kUnitF4;    // 192 KB, also the A cache
-constexpr size_t kCoopSmem = (size_t)kCacheF4 * 16;     // dynamic; + 18 KB static staging
-constexpr uint32_t kStageRow = kUnitCols + 4;           // staged words per 4-row group (16-byte rows)
-static_assert(kCoopSmem > 114 * 1024, "more than half of an SM: one resident launch per SM");
+constexpr uint32_t kCacheSlots = 3;                    // resident B units per CTA
+constexpr uint32_t kCacheF4 = kCacheSlots * kUnitF4;  // 192 KB: also A's resident slice
+constexpr size_t kCoopSmem = (size_t)kCacheF4 * 16;   // dynamic; + ~17 KB static staging
+constexpr uint32_t kStageRow = kUnitCols + 4;         // staged words per 4-row group (16-byte rows)
+constexpr uint32_t kChunkF4 = kCoopThreads * 8;       // remainder chunk of A: 8 float4 per thread (64 KB)
+constexpr uint32_t kBulkPieceF4 = kCacheF4 / 4;       // resident A slice in 4 bulk copies of 48 KB
+constexpr uint32_t kNone = 0xffffffffu;
+constexpr uint32_t kSlots = 16;  // control blocks per device
+static_assert(kCoopSmem > 114 * 1024, "more than half of an SM: one resident CTA per SM");
 static_assert(kUnitCols == kCoopThreads, "one column of a unit per thread");
 
-__device__ unsigned int g_coop_barrier[2];  // {arrivals, generation}
+constexpr uint32_t kOwnMax = 64;  // remainder chunks / units a CTA records in phase 1
+
+// Control block of one launch (all zero between launches).  Every word has a
+// 128-byte line of its own: the barrier's arrival count, the absmax words and
+// the work counters each see a different stream of atomics.
+struct alignas(128) CtlWord {
+    unsigned int v;
+    unsigned int pad[31];
+};
+struct CoopCtl {
+    CtlWord bar_count;                  // grid barrier arrivals (barrier k completes at k x CTAs)
+    CtlWord ctr_a1, ctr_a2, ctr_b1, ctr_b2;  // remainder work counters, one per phase
+    CtlWord abs_a, abs_b;               // tensor-wide |max| as magnitude bits
+    CtlWord ovf_a, ovf_b;               // some CTA took more than kOwnMax chunks / units in phase 1
+    CtlWord done;                       // CTAs that finished the launch
+};
+__device__ CoopCtl g_coop_ctl[kSlots];
 
 // m is a running magnitude (>= 0 or NaN); every element enters through its |.|
 __device__ __forceinline__ float absmax4(float m, float4 v) {
@@ -68,6 +100,14 @@ __device__ __forceinline__ float4 ld4(const float4* ptr, uint64_t pol) {
                  : "l"(ptr), "l"(pol));
     return v;
 }
+__device__ __forceinline__ unsigned int ld_gpu(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_gpu(unsigned int* p, unsigned int v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 __device__ uint32_t block_max(uint32_t v) {
     __shared__ uint32_t red[kCoopThreads / 32];
@@ -81,32 +121,40 @@ __device__ uint32_t block_max(uint32_t v) {
     return v;
 }
 
-// Sense-reversal grid barrier.  Returns false (and bumps *err) if the wait
-// gave up after ~2 s.
-__device__ bool grid_barrier(unsigned int nblocks, int* err) {
+// Grid barrier number `which` (1, 2) of the launch: every CTA adds one to the
+// arrival count with a release reduction (no reply to wait for) and polls the
+// count with acquire loads until it reaches which * nblocks -- one trip to L2
+// per arrival and no second hop through a releasing CTA.  The count is zeroed
+// by the last CTA to finish the launch.  Afterwards CTA 0 zeroes the work
+// counters of the phases every CTA has now left (barrier 1: A1's; barrier 2:
+// A2's, B1's, abs_a and ovf_a, which every CTA read after barrier 1).
+// Returns false (and bumps *err) if the wait gave up.
+__device__ bool grid_barrier(CoopCtl* ctl, unsigned int nblocks, int which, int* err) {
     __shared__ int ok_s;
-    unsigned int* bar = g_coop_barrier;
     __syncthreads();
     if (threadIdx.x == 0) {
         int ok = 1;
-        unsigned int gen, prev;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(bar + 1) : "memory");
-        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(bar) : "memory");
-        if (prev == nblocks - 1) {
-            asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(bar) : "memory");
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar + 1) : "memory");
-        } else {
-            const long long t0 = clock64();
-            while (true) {
-                unsigned int g;
-                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(bar + 1) : "memory");
-                if (g != gen) break;
-                if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
-                    atomicAdd(err, 1);
-                    ok = 0;
-                    break;
-                }
-                __nanosleep(32);
+        const unsigned int target = (unsigned int)which * nblocks;
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&ctl->bar_count.v) : "memory");
+        const long long t0 = clock64();
+        while (true) {
+            unsigned int n;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(n) : "l"(&ctl->bar_count.v) : "memory");
+            if (n >= target) break;
+            if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
+                atomicAdd(err, 1);
+                ok = 0;
+                break;
+            }
+        }
+        if (ok && blockIdx.x == 0) {
+            if (which == 1) {
+                st_gpu(&ctl->ctr_a1.v, 0u);
+            } else {
+                st_gpu(&ctl->ctr_a2.v, 0u);
+                st_gpu(&ctl->ctr_b1.v, 0u);
+                st_gpu(&ctl->abs_a.v, 0u);
+                st_gpu(&ctl->ovf_a.v, 0u);
             }
         }
         ok_s = ok;
@@ -114,6 +162,17 @@ __device__ bool grid_barrier(unsigned int nblocks, int* err) {
     __syncwarp();  // warp 0 reconverges after lane 0's spin
     __syncthreads();
     return ok_s != 0;
+}
+
+// Next index of a work counter, the same value in every thread of the CTA.
+// Consecutive grabs alternate between two broadcast words, so one
+// __syncthreads per grab suffices (a word is rewritten two grabs later, after
+// every thread passed the barrier of the grab in between).
+__device__ __forceinline__ uint32_t grab(unsigned int* ctr, uint32_t* bcast, uint32_t& k) {
+    uint32_t* w = bcast + (k++ & 1u);
+    if (threadIdx.x == 0) *w = atomicAdd(ctr, 1u);
+    __syncthreads();
+    return *w;
 }
 
 __device__ __forceinline__ void scale_from_absmax(float absmax, float* scale, float* inv) {
@@ -155,70 +214,100 @@ __device__ __forceinline__ uint32_t pack4(float4 v, float inv) {
 }
 __device__ __forceinline__ bool fast_inv(float inv) { return inv > 0.0f && inv < __int_as_float(0x7f800000); }
 
-// ----------------------------------------------------------------- phases
-// Batches of 8 float4 per thread (64 KB per CTA); the streaming loops
-// are ping-pong pipelined: batch k+1 is requested before batch k is consumed.
-constexpr size_t kBatch = (size_t)kCoopThreads * 8;
+// ------------------------------------------------------------ A (flat)
+// Geometry of A's split (float4 indices): CTA c's resident slice [res0,
+// res0 + nres), remainder [rem0, n) in chunks of kChunkF4.
+struct ASplit {
+    size_t n, res0, nres, rem0;
+    uint32_t nchunks;
+};
+__device__ __forceinline__ ASplit a_split(size_t n, unsigned int c, unsigned int G) {
+    ASplit s;
+    s.n = n;
+    s.res0 = min(n, (size_t)c * kCacheF4);
+    s.nres = min(n, (size_t)(c + 1) * kCacheF4) - s.res0;
+    s.rem0 = min(n, (size_t)G * kCacheF4);
+    s.nchunks = (uint32_t)ceil_div(n - s.rem0, kChunkF4);
+    return s;
+}
 
-__device__ __forceinline__ void load_batch(float4 (&v)[8], const float4* __restrict__ x4, size_t base, size_t n,
-                                           uint64_t pol_lo, uint64_t pol_hi, size_t split) {
+// The thread's eight float4 of remainder chunk ch (zero past the end).
+__device__ __forceinline__ void load_chunk(float4 (&v)[8], const float4* __restrict__ x4, const ASplit& s,
+                                           uint32_t ch, uint64_t pol) {
+    const size_t base = s.rem0 + (size_t)ch * kChunkF4 + threadIdx.x;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-        const size_t i = base + threadIdx.x + (size_t)j * kCoopThreads;
-        v[j] = i < n ? ld4(x4 + i, i < split ? pol_lo : pol_hi) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const size_t i = base + (size_t)j * kCoopThreads;
+        v[j] = i < s.n ? ld4(x4 + i, pol) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 }
 
-// Absmax (as a float magnitude) of x4[0..n); the first min(n, kCacheF4) float4
-// are copied to `cache` (read once: evict_first), the rest stay in L2 (evict_last).
-__device__ float absmax_and_cache(const float4* __restrict__ x4, size_t n, float4* cache) {
-    const uint64_t keep = policy_evict_last(), once = policy_evict_first();
-    float m = 0.0f;
-    auto consume = [&](const float4 (&v)[8], size_t base) {
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const size_t i = base + threadIdx.x + (size_t)j * kCoopThreads;
-            m = absmax4(m, v[j]);
-            if (i < kCacheF4 && i < n) cache[i] = v[j];
-        }
-    };
+// Notes remainder item `idx` as taken by this CTA in phase 1 (the leader
+// thread writes the list; every calling thread counts).  Past kOwnMax items
+// the list is incomplete and the launch-wide overflow flag sends phase 2 back
+// to a work counter.
+__device__ __forceinline__ void record_own(uint32_t idx, uint32_t* own, uint32_t& nown, unsigned int* ovf,
+                                           bool leader = threadIdx.x == 0) {
+    if (leader) {
+        if (nown < kOwnMax)
+            own[nown] = idx;
+        else if (nown == kOwnMax)
+            atomicExch(ovf, 1u);
+    }
+    nown++;
+}
+
+// Runs body(v, ch) over the remainder chunks this CTA takes from `ctr`; chunk
+// k+1 is requested before chunk k is consumed.  With `own`, the chunks taken
+// are recorded (record_own) so that phase 2 can revisit the same chunks on the
+// same SM, next to the L2 slice that cached them.
+template <class Body>
+__device__ __forceinline__ void for_each_chunk(const float4* __restrict__ x4, const ASplit& s, unsigned int* ctr,
+                                               uint32_t* bcast, uint32_t& gk, uint64_t pol, uint32_t* own,
+                                               uint32_t& nown, unsigned int* ovf, Body body) {
     float4 a[8], b[8];
-    load_batch(a, x4, 0, n, once, keep, kCacheF4);
-    for (size_t base = 0; base < n; base += 2 * kBatch) {
-        if (base + kBatch < n) load_batch(b, x4, base + kBatch, n, once, keep, kCacheF4);
-        consume(a, base);
-        if (base + kBatch >= n) break;
-        if (base + 2 * kBatch < n) load_batch(a, x4, base + 2 * kBatch, n, once, keep, kCacheF4);
-        consume(b, base + kBatch);
+    uint32_t cur = grab(ctr, bcast, gk);
+    if (cur < s.nchunks) load_chunk(a, x4, s, cur, pol);
+    while (cur < s.nchunks) {
+        if (own) record_own(cur, own, nown, ovf);
+        const uint32_t nxt = grab(ctr, bcast, gk);
+        if (nxt < s.nchunks) load_chunk(b, x4, s, nxt, pol);
+        body(a, cur);
+        if (nxt >= s.nchunks) break;
+        if (own) record_own(nxt, own, nown, ovf);
+        cur = grab(ctr, bcast, gk);
+        if (cur < s.nchunks) load_chunk(a, x4, s, cur, pol);
+        body(b, nxt);
     }
-    return m;
 }
 
-// Codes of the CTA's A slice: shared-memory part, then the L2 part (pipelined).
+// Phase 2 over the chunks recorded in phase 1 (no counter, no barrier).
+template <class Body>
+__device__ __forceinline__ void for_own_chunks(const float4* __restrict__ x4, const ASplit& s, const uint32_t* own,
+                                               uint32_t nown, uint64_t pol, Body body) {
+    float4 a[8], b[8];
+    if (nown) load_chunk(a, x4, s, own[0], pol);
+    for (uint32_t k = 0; k < nown; k += 2) {
+        if (k + 1 < nown) load_chunk(b, x4, s, own[k + 1], pol);
+        body(a, own[k]);
+        if (k + 1 >= nown) break;
+        if (k + 2 < nown) load_chunk(a, x4, s, own[k + 2], pol);
+        body(b, own[k + 1]);
+    }
+}
+
 template <bool FAST>
-__device__ void quantize_slice(const float4* __restrict__ A4, size_t n, const float4* cache, uint32_t* out,
-                               float inv) {
-    const uint64_t once = policy_evict_first();
-    const size_t nc = n < kCacheF4 ? n : kCacheF4;
-    float4 a[8], b[8];
-    if (nc < n) load_batch(a, A4, nc, n, once, once, 0);  // first L2 batch in flight during the smem part
-    for (size_t i = threadIdx.x; i < nc; i += kCoopThreads) out[i] = pack4<FAST>(cache[i], inv);
-    auto consume = [&](const float4 (&v)[8], size_t base) {
+__device__ __forceinline__ void codes_of_chunk(const float4 (&v)[8], uint32_t ch, const ASplit& s, uint32_t* out,
+                                               float inv) {
+    const size_t base = s.rem0 + (size_t)ch * kChunkF4 + threadIdx.x;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const size_t i = base + threadIdx.x + (size_t)j * kCoopThreads;
-            if (i < n) out[i] = pack4<FAST>(v[j], inv);
-        }
-    };
-    for (size_t base = nc; base < n; base += 2 * kBatch) {
-        if (base + kBatch < n) load_batch(b, A4, base + kBatch, n, once, once, 0);
-        consume(a, base);
-        if (base + kBatch >= n) break;
-        if (base + 2 * kBatch < n) load_batch(a, A4, base + 2 * kBatch, n, once, once, 0);
-        consume(b, base + kBatch);
+    for (int j = 0; j < 8; j++) {
+        const size_t i = base + (size_t)j * kCoopThreads;
+        if (i < s.n) out[i] = pack4<FAST>(v[j], inv);
     }
 }
 
+// ------------------------------------------------------------ B (units)
 // Geometry of B unit u: rows [r0, r0+rows), columns [c0, c0+4*cols4).
 struct BUnit {
     uint32_t r0, rows, c0, cols4;
@@ -231,6 +320,129 @@ __device__ __forceinline__ BUnit b_unit(uint32_t u, uint32_t nch, uint32_t K, ui
     g.c0 = nc * kUnitCols;
     g.cols4 = min(kUnitCols, N - g.c0) / 4;
     return g;
+}
+
+// Units of B: CTA c's resident units [first, first + nres), remainder [rem0, U).
+struct BSplit {
+    uint32_t U, nch, first, nres, rem0;
+};
+__device__ __forceinline__ BSplit b_split(uint32_t K, uint32_t N, unsigned int c, unsigned int G) {
+    BSplit s;
+    s.nch = (N + kUnitCols - 1) / kUnitCols;
+    s.U = ((K + kUnitRows - 1) / kUnitRows) * s.nch;
+    s.first = kCacheSlots * c;
+    s.nres = s.U > s.first ? min(kCacheSlots, s.U - s.first) : 0u;
+    s.rem0 = min(s.U, kCacheSlots * G);
+    return s;
+}
+
+// Absmax layout: thread (c4 = t % 128, r = t / 128) reads rows r + 4j (j < 8)
+// of column quad c4; zero outside the unit.
+__device__ __forceinline__ void load_unit_rows(float4 (&v)[kUnitRows / 4], const float4* __restrict__ B4, uint32_t N4,
+                                               const BUnit& g, uint64_t pol) {
+    const uint32_t c4 = threadIdx.x % (kUnitCols / 4), r = threadIdx.x / (kUnitCols / 4);
+#pragma unroll
+    for (uint32_t j = 0; j < kUnitRows / 4; j++) {
+        const uint32_t rr = r + 4 * j;
+        v[j] = (c4 < g.cols4 && rr < g.rows) ? ld4(B4 + (size_t)(g.r0 + rr) * N4 + g.c0 / 4 + c4, pol)
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+// ------------------------------------------------ A2 and B1 side by side
+// While A's remainder is quantized from L2 (warps 0-7), B's remainder streams
+// from HBM for its absmax (warps 8-15): the two halves of the CTA keep L2 and
+// HBM busy at the same time.  Each half has kHalf threads; `lt` is the
+// thread's index within its half.
+constexpr uint32_t kHalf = kCoopThreads / 2;
+constexpr uint32_t kBarB = 1;  // named barrier of the B half (barrier 0 is __syncthreads)
+
+// Pass p (0, 1) of A chunk ch for a half: eight float4 per thread.
+__device__ __forceinline__ void load_chunk_half(float4 (&v)[8], const float4* __restrict__ x4, const ASplit& s,
+                                                uint32_t ch, uint32_t p, uint32_t lt, uint64_t pol) {
+    const size_t base = s.rem0 + (size_t)ch * kChunkF4 + p * (kChunkF4 / 2) + lt;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const size_t i = base + (size_t)j * kHalf;
+        v[j] = i < s.n ? ld4(x4 + i, pol) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+template <bool FAST>
+__device__ __forceinline__ void codes_of_chunk_half(const float4 (&v)[8], uint32_t ch, uint32_t p, uint32_t lt,
+                                                    const ASplit& s, uint32_t* out, float inv) {
+    const size_t base = s.rem0 + (size_t)ch * kChunkF4 + p * (kChunkF4 / 2) + lt;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const size_t i = base + (size_t)j * kHalf;
+        if (i < s.n) out[i] = pack4<FAST>(v[j], inv);
+    }
+}
+// Codes of the A chunks recorded in A1, by one half: steps (chunk, pass) with
+// step t+1 requested before step t is consumed; no barrier.
+template <bool FAST>
+__device__ void quantize_own_chunks_half(const float4* __restrict__ x4, const ASplit& s, const uint32_t* own,
+                                         uint32_t nown, uint32_t lt, uint32_t* out, float inv, uint64_t pol) {
+    const uint32_t steps = 2 * nown;
+    float4 a[8], b[8];
+    if (steps) load_chunk_half(a, x4, s, own[0], 0, lt, pol);
+    for (uint32_t t = 0; t < steps; t += 2) {
+        load_chunk_half(b, x4, s, own[t / 2], 1, lt, pol);
+        codes_of_chunk_half<FAST>(a, own[t / 2], 0, lt, s, out, inv);
+        if (t + 2 < steps) load_chunk_half(a, x4, s, own[t / 2 + 1], 0, lt, pol);
+        codes_of_chunk_half<FAST>(b, own[t / 2], 1, lt, s, out, inv);
+    }
+}
+
+// Half h (rows 16h .. 16h+15) of B unit g for a half of the CTA: thread
+// (c4 = lt % 128, r = lt / 128) reads rows 16h + r + 2j (j < 8) of column quad
+// c4; zero outside the unit.
+__device__ __forceinline__ void load_unit_half(float4 (&v)[8], const float4* __restrict__ B4, uint32_t N4,
+                                               const BUnit& g, uint32_t h, uint32_t lt, uint64_t pol) {
+    const uint32_t c4 = lt % (kUnitCols / 4), r = lt / (kUnitCols / 4);
+#pragma unroll
+    for (uint32_t j = 0; j < 8; j++) {
+        const uint32_t rr = 16 * h + r + 2 * j;
+        v[j] = (c4 < g.cols4 && rr < g.rows) ? ld4(B4 + (size_t)(g.r0 + rr) * N4 + g.c0 / 4 + c4, pol)
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+// Next index of a work counter for the B half (its own named barrier and
+// broadcast words; the same one-barrier-per-grab argument as grab()).
+__device__ __forceinline__ uint32_t grab_half(unsigned int* ctr, uint32_t* bcast, uint32_t& k, uint32_t lt) {
+    uint32_t* w = bcast + (k++ & 1u);
+    if (lt == 0) *w = atomicAdd(ctr, 1u);
+    ptx::named_barrier_sync(kBarB, kHalf);
+    return *w;
+}
+
+// Codes layout: thread (c4 = t % 128, rg = t / 128) takes 4-row groups rg and
+// rg + 4 of column quad c4, from a shared-memory copy of the unit (32 rows x
+// 512 columns, row pitch 128 float4; zero outside the unit) ...
+__device__ __forceinline__ void unit_from_smem(float4 (&v)[2][4], const float4* cu, const BUnit& g, uint32_t c4,
+                                               uint32_t rg) {
+    const uint32_t groups = g.rows / 4;
+#pragma unroll
+    for (uint32_t h = 0; h < 2; h++) {
+        const uint32_t gi = rg + 4 * h;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            v[h][i] = (c4 >= g.cols4 || gi >= groups) ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                                       : cu[(4 * gi + i) * (kUnitCols / 4) + c4];
+    }
+}
+// ... or straight from global memory (L2).
+__device__ __forceinline__ void unit_from_global(float4 (&v)[2][4], const float4* __restrict__ B4, uint32_t N4,
+                                                 const BUnit& g, uint32_t c4, uint32_t rg, uint64_t pol) {
+    const uint32_t groups = g.rows / 4;
+#pragma unroll
+    for (uint32_t h = 0; h < 2; h++) {
+        const uint32_t gi = rg + 4 * h;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            v[h][i] = (c4 >= g.cols4 || gi >= groups)
+                          ? make_float4(0.f, 0.f, 0.f, 0.f)
+                          : ld4(B4 + (size_t)(g.r0 + 4 * gi + i) * N4 + g.c0 / 4 + c4, pol);
+    }
 }
 
 // Pack, transpose and write one unit of B codes from the thread's eight float4
@@ -272,97 +484,79 @@ __device__ __forceinline__ void unit_codes_out(const float4 (&cur)[2][4], const 
     __syncthreads();  // stage is rewritten by the next unit
 }
 
-// The thread's eight float4 of unit g from a shared-memory copy of the unit
-// (32 rows x 512 columns, row pitch 128 float4); zero outside the unit.
-__device__ __forceinline__ void unit_from_smem(float4 (&v)[2][4], const float4* cu, const BUnit& g, uint32_t c4,
-                                               uint32_t rg) {
-    const uint32_t groups = g.rows / 4;
-#pragma unroll
-    for (uint32_t h = 0; h < 2; h++) {
-        const uint32_t gi = rg + 4 * h;
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-            v[h][i] = (c4 >= g.cols4 || gi >= groups) ? make_float4(0.f, 0.f, 0.f, 0.f)
-                                                       : cu[(4 * gi + i) * (kUnitCols / 4) + c4];
-    }
-}
-
-// Codes of B units [ub0, ub1), transposed: thread (c4 = t % 128, rg = t / 128)
-// takes 4-row groups g = rg, rg + 4 of column quad c4.
-// With a tensor map (bmap): unit k of the CTA is read from shared-memory slot
-// k % kCacheSlots -- units 0..2 are still there from the absmax phase; unit
-// k + 3 is brought into slot k % 3 by one 3-D TMA box (from L2, where the
-// absmax phase left it) as soon as unit k's values are in registers, so the
-// copies run two units ahead of the arithmetic.  Returns false if a copy did
-// not arrive in time (device timeout recorded).
-// Without: the next unit's eight float4 are requested (shared memory or L2)
-// before the current unit is processed.
+// Phase B2: codes of this CTA's resident units and of its remainder units,
+// transposed into Bt.  The remainder units are the ones this CTA streamed in
+// B1 (own[0..nown), so they come from the L2 slice next to this SM), or, if
+// some CTA's list overflowed (use_own false), units taken from ctr_b2.  With
+// the tensor map, the slots form a ring: after slot s's values are in
+// registers, the next remainder unit is requested into slot s (one 3-D TMA
+// box, from L2 where B1 left it), so copies run two units ahead of the
+// arithmetic.  Without it (N % 256 != 0), remainder units are read from L2
+// directly.  Returns false if a copy did not arrive in time (device timeout
+// recorded).
 template <bool FAST>
-__device__ bool quantize_units_transposed(const float4* __restrict__ B4, uint32_t N4, uint32_t K, uint32_t N,
-                                          uint32_t nch, uint32_t ub0, uint32_t ub1, float4* cache,
-                                          uint32_t* stage, int8_t* __restrict__ Bt, float inv,
-                                          const CUtensorMap* bmap, uint64_t* tbar, int* err) {
+__device__ bool quantize_b_units(const float4* __restrict__ B4, uint32_t N4, uint32_t K, uint32_t N, const BSplit& s,
+                                 float4* cache, uint32_t* stage, int8_t* __restrict__ Bt, float inv,
+                                 const CUtensorMap* bmap, uint64_t* tbar, CoopCtl* ctl, uint32_t* bcast,
+                                 uint32_t& gk, const uint32_t* own, uint32_t nown, bool use_own, int* err) {
+    __shared__ uint32_t slot_unit[kCacheSlots];
     const uint64_t once = policy_evict_first();
     const uint32_t c4 = threadIdx.x % (kUnitCols / 4), rg = threadIdx.x / (kUnitCols / 4);
-    if (bmap) {
-        const uint32_t n = ub1 - ub0;
-        for (uint32_t k = 0; k < n; k++) {
-            const uint32_t slot = k % kCacheSlots;
-            if (k >= kCacheSlots) {
-                const bool ok = ptx::mbar_wait(&tbar[slot], (k / kCacheSlots - 1) & 1, err);
-                if (__syncthreads_or(!ok)) return false;
-            }
-            const BUnit g = b_unit(ub0 + k, nch, K, N);
+    if (!bmap) {
+        for (uint32_t k = 0; k < s.nres; k++) {
+            const BUnit g = b_unit(s.first + k, s.nch, K, N);
             float4 cur[2][4];
-            unit_from_smem(cur, cache + slot * kUnitF4, g, c4, rg);
-            __syncthreads();  // every thread holds its values: the slot may be refilled
-            if (threadIdx.x == 0 && k + kCacheSlots < n) {
-                const BUnit gn = b_unit(ub0 + k + kCacheSlots, nch, K, N);
-                ptx::fence_proxy_async_smem();  // the slot's generic accesses before the async-proxy write
-                ptx::mbar_arrive_expect_tx(&tbar[slot], kUnitF4 * 16);
-                ptx::tma_load_3d(cache + slot * kUnitF4, bmap, &tbar[slot], 0, (int)(gn.c0 / 256), (int)gn.r0);
-            }
+            unit_from_smem(cur, cache + k * kUnitF4, g, c4, rg);
+            unit_codes_out<FAST>(cur, g, c4, rg, stage, Bt, K, inv);
+        }
+        for (uint32_t k = 0;; k++) {
+            const uint32_t u = use_own ? (k < nown ? own[k] : kNone) : s.rem0 + grab(&ctl->ctr_b2.v, bcast, gk);
+            if (u >= s.U) break;
+            const BUnit g = b_unit(u, s.nch, K, N);
+            float4 cur[2][4];
+            unit_from_global(cur, B4, N4, g, c4, rg, once);
             unit_codes_out<FAST>(cur, g, c4, rg, stage, Bt, K, inv);
         }
         return true;
     }
-    auto load_unit = [&](float4 (&v)[2][4], uint32_t u) {
-        const BUnit g = b_unit(u, nch, K, N);
-        const uint32_t slot = u - ub0, groups = g.rows / 4;
-        if (slot < kCacheSlots) {
-            unit_from_smem(v, cache + slot * kUnitF4, g, c4, rg);
-            return;
+    // the resident units fill the slots first; when this CTA has fewer than
+    // kCacheSlots of them (a small B), it has no remainder units either
+    if (threadIdx.x == 0)
+        for (uint32_t k = 0; k < kCacheSlots; k++) slot_unit[k] = k < s.nres ? s.first + k : kNone;
+    __syncthreads();
+    uint32_t next_own = 0;  // thread 0: next entry of own[] to request
+    for (uint32_t k = 0;; k++) {
+        const uint32_t slot = k % kCacheSlots;
+        const uint32_t u = slot_unit[slot];  // written three iterations ago, barriers in between
+        if (u == kNone) break;               // CTA-uniform; the work counter only grows, so no later slot is full
+        if (k >= kCacheSlots) {
+            const bool ok = ptx::mbar_wait(&tbar[slot], (k / kCacheSlots - 1) & 1, err);
+            if (__syncthreads_or(!ok)) return false;
         }
-#pragma unroll
-        for (uint32_t h = 0; h < 2; h++) {
-            const uint32_t gi = rg + 4 * h;
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const uint32_t r = 4 * gi + i;
-                v[h][i] = (c4 >= g.cols4 || gi >= groups)
-                              ? make_float4(0.f, 0.f, 0.f, 0.f)
-                              : ld4(B4 + (size_t)(g.r0 + r) * N4 + g.c0 / 4 + c4, once);
+        const BUnit g = b_unit(u, s.nch, K, N);
+        float4 cur[2][4];
+        unit_from_smem(cur, cache + slot * kUnitF4, g, c4, rg);
+        __syncthreads();  // every thread holds its values: the slot may be refilled
+        if (threadIdx.x == 0) {
+            uint32_t nu = kNone;
+            if (use_own)
+                nu = next_own < nown ? own[next_own++] : kNone;
+            else if (s.rem0 < s.U)
+                nu = s.rem0 + atomicAdd(&ctl->ctr_b2.v, 1u);
+            if (nu < s.U) {
+                const BUnit gn = b_unit(nu, s.nch, K, N);
+                ptx::fence_proxy_async_smem();  // the slot's generic reads before the async-proxy write
+                ptx::mbar_arrive_expect_tx(&tbar[slot], kUnitF4 * 16);
+                ptx::tma_load_3d_hint(cache + slot * kUnitF4, bmap, &tbar[slot], 0, (int)(gn.c0 / 256), (int)gn.r0,
+                                      once);
+                slot_unit[slot] = nu;
+            } else {
+                slot_unit[slot] = kNone;
             }
         }
-    };
-    float4 cur[2][4], nxt[2][4];
-    if (ub0 < ub1) load_unit(cur, ub0);
-    for (uint32_t u = ub0; u < ub1; u++) {
-        if (u + 1 < ub1) load_unit(nxt, u + 1);
-        unit_codes_out<FAST>(cur, b_unit(u, nch, K, N), c4, rg, stage, Bt, K, inv);
-#pragma unroll
-        for (int h = 0; h < 2; h++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) cur[h][i] = nxt[h][i];
+        unit_codes_out<FAST>(cur, g, c4, rg, stage, Bt, K, inv);  // its barriers publish slot_unit
     }
     return true;
-}
-
-__device__ float global_absmax(const float* __restrict__ partials, unsigned int n) {
-    uint32_t m = 0;
-    // __ldcg: written by other CTAs before the barrier; read at L2, never a stale L1 line
-    for (unsigned int i = threadIdx.x; i < n; i += kCoopThreads) m = max(m, __float_as_uint(__ldcg(partials + i)));
-    return __uint_as_float(block_max(m));
 }
 
 // Cross-GPU absmax (N-sharded dense_fused_i8): every rank publishes its
@@ -415,17 +609,26 @@ __device__ __forceinline__ uint32_t exchange_absmax(const CoopRanks& xr, uint32_
 __global__ void __launch_bounds__(kCoopThreads, 1)
     prologue_coop_kernel(const float* __restrict__ A, const float* __restrict__ B, int8_t* __restrict__ Aq,
                          int8_t* __restrict__ Bt, uint32_t M, uint32_t N, uint32_t K, float* __restrict__ scales,
-                         float* __restrict__ partials, CoopRanks xr, const __grid_constant__ CUtensorMap bmap,
-                         uint32_t use_tma, int* err) {
-    extern __shared__ __align__(128) float4 cache[];  // 128-byte aligned: TMA destination
+                         CoopRanks xr, const __grid_constant__ CUtensorMap bmap, uint32_t use_tma, uint32_t slot,
+                         int* err) {
+    extern __shared__ __align__(128) float4 cache[];  // 128-byte aligned: bulk-copy / TMA destination
     __shared__ __align__(16) uint32_t stage[kUnitRows / 4 * kStageRow];
-    __shared__ uint64_t tbar[kCacheSlots];  // B units refilled into the cache slots
-    __shared__ uint32_t tag_s;
+    __shared__ uint64_t rbar[2];            // resident slice of A / resident units of B arrived
+    __shared__ uint64_t tbar[kCacheSlots];  // remainder units of B refilled into the slots
+    __shared__ uint32_t bcast[2], bcast_b[2];
+    __shared__ uint32_t own_a[kOwnMax], own_b[kOwnMax];  // remainder items this CTA streamed in phase 1
+    __shared__ uint32_t tag_s, abs_s, ovf_s, nown_b_s;
     __shared__ int fail_s;
     const unsigned int G = gridDim.x, c = blockIdx.x;
+    CoopCtl* ctl = &g_coop_ctl[slot];
+    const uint64_t keep = policy_evict_last(), once = policy_evict_first();
+    uint32_t gk = 0;                 // grabs so far (the same in every thread)
+    uint32_t nown_a = 0, nown_b = 0;  // items taken in phase 1 (the same in every thread)
     if (threadIdx.x == 0) {
         tag_s = xr.world > 1 ? *reinterpret_cast<volatile uint32_t*>(xr.ctl) + 1u : 0u;
         fail_s = 0;
+        ptx::mbar_init(&rbar[0], 1);
+        ptx::mbar_init(&rbar[1], 1);
         for (uint32_t i = 0; i < kCacheSlots; i++) ptx::mbar_init(&tbar[i], 1);
         ptx::fence_mbarrier_init();
     }
@@ -439,87 +642,192 @@ __global__ void __launch_bounds__(kCoopThreads, 1)
         return __uint_as_float(m);
     };
 
-    // ------------------------------------------------------------------ A
-    const size_t na4 = (size_t)M * K / 4;
-    const size_t a0 = na4 * c / G, a1 = na4 * (c + 1) / G;
-    const float4* A4 = reinterpret_cast<const float4*>(A) + a0;
+    // ------------------------------------------------------------------ A1
+    const float4* A4 = reinterpret_cast<const float4*>(A);
+    const ASplit sa = a_split((size_t)M * K / 4, c, G);
+    if (threadIdx.x == 0 && sa.nres) {
+        ptx::mbar_arrive_expect_tx(&rbar[0], (uint32_t)(sa.nres * 16));
+        for (size_t off = 0; off < sa.nres; off += kBulkPieceF4) {
+            const size_t n = min((size_t)kBulkPieceF4, sa.nres - off);
+            ptx::bulk_load_hint(cache + off, A4 + sa.res0 + off, (uint32_t)(n * 16), &rbar[0], once);
+        }
+    }
+    float m = 0.0f;
+    for_each_chunk(A4, sa, &ctl->ctr_a1.v, bcast, gk, keep, own_a, nown_a, &ctl->ovf_a.v,
+                   [&](const float4(&v)[8], uint32_t) {
+#pragma unroll
+                       for (int j = 0; j < 8; j++) m = absmax4(m, v[j]);  // zero-filled past the end
+                   });
+    if (sa.nres) {
+        const bool ok = ptx::mbar_wait(&rbar[0], 0, err);
+        if (__syncthreads_or(!ok)) return;
+        for (size_t i = threadIdx.x; i < sa.nres; i += kCoopThreads) m = absmax4(m, cache[i]);
+    }
     // magnitudes are non-negative or NaN: their bit patterns order like the values
-    uint32_t m = block_max(__float_as_uint(absmax_and_cache(A4, a1 - a0, cache)));
-    if (threadIdx.x == 0) partials[c] = __uint_as_float(m);
-    if (!grid_barrier(G, err)) return;
+    uint32_t mb = block_max(__float_as_uint(m));
+    if (threadIdx.x == 0) atomicMax(&ctl->abs_a.v, mb);
+    if (!grid_barrier(ctl, G, 1, err)) return;
+
+    // ------------------------------------------------------------------ A2
+    if (threadIdx.x == 0) {
+        abs_s = ld_gpu(&ctl->abs_a.v);
+        ovf_s = ld_gpu(&ctl->ovf_a.v);
+    }
+    __syncthreads();
+    const bool own_ok_a = ovf_s == 0;  // every CTA's chunk list is complete: revisit them
     float scale, inv;
-    scale_from_absmax(rank_absmax(0, global_absmax(partials, G)), &scale, &inv);
+    scale_from_absmax(rank_absmax(0, __uint_as_float(abs_s)), &scale, &inv);
     __syncthreads();
     if (fail_s) return;
     if (c == 0 && threadIdx.x == 0) scales[0] = scale;
-    uint32_t* outA = reinterpret_cast<uint32_t*>(Aq) + a0;  // K % 16 == 0: Aq row stride is K
-    if (fast_inv(inv))
-        quantize_slice<true>(A4, a1 - a0, cache, outA, inv);
-    else
-        quantize_slice<false>(A4, a1 - a0, cache, outA, inv);
-    __syncthreads();  // the cache is reused for B
-
-    // ------------------------------------------------------------------ B
-    // Units u = ks * nch + nc (rows 32ks.., columns 512nc..); CTA c owns units
-    // [U*c/G, U*(c+1)/G); the first kCacheSlots of them stay in shared memory.
-    const uint32_t nks = (K + kUnitRows - 1) / kUnitRows, nch = (N + kUnitCols - 1) / kUnitCols;
-    const uint32_t U = nks * nch;
-    const uint32_t ub0 = (uint32_t)((uint64_t)U * c / G), ub1 = (uint32_t)((uint64_t)U * (c + 1) / G);
-    const float4* B4 = reinterpret_cast<const float4*>(B);
+    uint32_t* outA = reinterpret_cast<uint32_t*>(Aq);  // K % 16 == 0: Aq row stride is K, codes flat like A
+    const bool fa = fast_inv(inv);
+    for (size_t i = threadIdx.x; i < sa.nres; i += kCoopThreads)
+        outA[sa.res0 + i] = fa ? pack4<true>(cache[i], inv) : pack4<false>(cache[i], inv);
+    __syncthreads();  // the slice is read: B's resident units may land in shared memory
     const uint32_t N4 = N / 4;
-    {
-        const uint64_t keep = policy_evict_last(), once = policy_evict_first();
-        const uint32_t c4 = threadIdx.x % (kUnitCols / 4), r = threadIdx.x / (kUnitCols / 4);
-        float mf = 0.0f;
-        // unit u: rows r + 4j (j < 8) of column quad c4; the first kCacheSlots
-        // units are read once (evict_first) into shared memory, the rest stay in
-        // L2 (evict_last).  Unit u+1 is requested before unit u is consumed.
-        auto load_unit = [&](float4 (&v)[kUnitRows / 4], uint32_t u) {
-            const BUnit g = b_unit(u, nch, K, N);
-            const uint64_t pol = u - ub0 < kCacheSlots ? once : keep;
-#pragma unroll
-            for (uint32_t j = 0; j < kUnitRows / 4; j++) {
-                const uint32_t rr = r + 4 * j;
-                v[j] = (c4 < g.cols4 && rr < g.rows) ? ld4(B4 + (size_t)(g.r0 + rr) * N4 + g.c0 / 4 + c4, pol)
-                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        };
-        float4 cur[kUnitRows / 4], nxt[kUnitRows / 4];
-        if (ub0 < ub1) load_unit(cur, ub0);
-        for (uint32_t u = ub0; u < ub1; u++) {
-            if (u + 1 < ub1) load_unit(nxt, u + 1);
-            const BUnit g = b_unit(u, nch, K, N);
-            const uint32_t slot = u - ub0;
-            float4* dst = slot < kCacheSlots ? cache + slot * kUnitF4 : nullptr;
-#pragma unroll
-            for (uint32_t j = 0; j < kUnitRows / 4; j++) {
-                const uint32_t rr = r + 4 * j;
-                mf = absmax4(mf, cur[j]);  // zero-filled outside the unit
-                if (dst && c4 < g.cols4 && rr < g.rows) dst[rr * (kUnitCols / 4) + c4] = cur[j];  // pitch 128 float4
-            }
-#pragma unroll
-            for (uint32_t j = 0; j < kUnitRows / 4; j++) cur[j] = nxt[j];
+    const float4* B4 = reinterpret_cast<const float4*>(B);
+    const BSplit sb = b_split(K, N, c, G);
+    if (use_tma && threadIdx.x == 0 && sb.nres) {
+        ptx::fence_proxy_async_smem();  // the generic reads above before the async-proxy writes
+        ptx::mbar_arrive_expect_tx(&rbar[1], sb.nres * kUnitF4 * 16);
+        for (uint32_t k = 0; k < sb.nres; k++) {
+            const BUnit g = b_unit(sb.first + k, sb.nch, K, N);
+            ptx::tma_load_3d_hint(cache + k * kUnitF4, &bmap, &rbar[1], 0, (int)(g.c0 / 256), (int)g.r0, once);
         }
-        m = block_max(__float_as_uint(mf));
     }
-    if (threadIdx.x == 0) partials[G + c] = __uint_as_float(m);
-    if (!grid_barrier(G, err)) return;
-    scale_from_absmax(rank_absmax(1, global_absmax(partials + G, G)), &scale, &inv);
+    // ------------------------------------------------- A2 remainder | B1
+    float mf = 0.0f;  // this thread's running |max| of B
+    if (own_ok_a) {
+        // the two halves of the CTA side by side: A's recorded chunks from L2
+        // (warps 0-7) while B's remainder units stream from HBM (warps 8-15)
+        if (threadIdx.x < kHalf) {
+            if (fa)
+                quantize_own_chunks_half<true>(A4, sa, own_a, nown_a, threadIdx.x, outA, inv, once);
+            else
+                quantize_own_chunks_half<false>(A4, sa, own_a, nown_a, threadIdx.x, outA, inv, once);
+        } else {
+            // remainder units (evict_last: B2 reads them back from L2); half 1
+            // of a unit and half 0 of the next are requested before the
+            // current half is consumed
+            const uint32_t lt = threadIdx.x - kHalf;
+            uint32_t k2 = 0, nb = 0;
+            float4 h0[8], h1[8];
+            uint32_t u = sb.rem0 + grab_half(&ctl->ctr_b1.v, bcast_b, k2, lt);
+            if (u < sb.U) load_unit_half(h0, B4, N4, b_unit(u, sb.nch, K, N), 0, lt, keep);
+            while (u < sb.U) {
+                record_own(u, own_b, nb, &ctl->ovf_b.v, lt == 0);
+                const BUnit g = b_unit(u, sb.nch, K, N);
+                load_unit_half(h1, B4, N4, g, 1, lt, keep);
+#pragma unroll
+                for (int j = 0; j < 8; j++) mf = absmax4(mf, h0[j]);  // zero-filled outside the unit
+                u = sb.rem0 + grab_half(&ctl->ctr_b1.v, bcast_b, k2, lt);
+                if (u < sb.U) load_unit_half(h0, B4, N4, b_unit(u, sb.nch, K, N), 0, lt, keep);
+#pragma unroll
+                for (int j = 0; j < 8; j++) mf = absmax4(mf, h1[j]);
+            }
+            if (lt == 0) nown_b_s = nb;
+        }
+        __syncthreads();
+        nown_b = nown_b_s;
+    } else {
+        // some CTA's chunk list overflowed: the whole CTA quantizes chunks
+        // from a work counter, then streams B's remainder units
+        auto codes_a = [&](const float4(&v)[8], uint32_t ch) {
+            if (fa)
+                codes_of_chunk<true>(v, ch, sa, outA, inv);
+            else
+                codes_of_chunk<false>(v, ch, sa, outA, inv);
+        };
+        uint32_t unused = 0;
+        for_each_chunk(A4, sa, &ctl->ctr_a2.v, bcast, gk, once, nullptr, unused, nullptr, codes_a);
+        float4 cur[kUnitRows / 4], nxt[kUnitRows / 4];
+        auto absmax_unit = [&](const float4(&v)[kUnitRows / 4]) {
+#pragma unroll
+            for (uint32_t j = 0; j < kUnitRows / 4; j++) mf = absmax4(mf, v[j]);
+        };
+        uint32_t u = sb.rem0 + grab(&ctl->ctr_b1.v, bcast, gk);
+        if (u < sb.U) load_unit_rows(cur, B4, N4, b_unit(u, sb.nch, K, N), keep);
+        while (u < sb.U) {
+            record_own(u, own_b, nown_b, &ctl->ovf_b.v);
+            const uint32_t un = sb.rem0 + grab(&ctl->ctr_b1.v, bcast, gk);
+            if (un < sb.U) load_unit_rows(nxt, B4, N4, b_unit(un, sb.nch, K, N), keep);
+            absmax_unit(cur);
+            if (un >= sb.U) break;
+            record_own(un, own_b, nown_b, &ctl->ovf_b.v);
+            u = sb.rem0 + grab(&ctl->ctr_b1.v, bcast, gk);
+            if (u < sb.U) load_unit_rows(cur, B4, N4, b_unit(u, sb.nch, K, N), keep);
+            absmax_unit(nxt);
+        }
+    }
+
+    // ------------------------------------------------------------------ B1
+    {
+        float4 cur[kUnitRows / 4];
+        auto absmax_unit = [&](const float4(&v)[kUnitRows / 4]) {
+#pragma unroll
+            for (uint32_t j = 0; j < kUnitRows / 4; j++) mf = absmax4(mf, v[j]);  // zero-filled outside the unit
+        };
+        // resident units: landed by TMA during A2, or read here into the slots
+        if (use_tma) {
+            if (sb.nres) {
+                const bool ok = ptx::mbar_wait(&rbar[1], 0, err);
+                if (__syncthreads_or(!ok)) return;
+                for (uint32_t i = threadIdx.x; i < sb.nres * kUnitF4; i += kCoopThreads) mf = absmax4(mf, cache[i]);
+            }
+        } else {
+            const uint32_t c4 = threadIdx.x % (kUnitCols / 4), r = threadIdx.x / (kUnitCols / 4);
+            for (uint32_t k = 0; k < sb.nres; k++) {
+                const BUnit g = b_unit(sb.first + k, sb.nch, K, N);
+                load_unit_rows(cur, B4, N4, g, once);
+                absmax_unit(cur);
+                float4* dst = cache + k * kUnitF4;
+#pragma unroll
+                for (uint32_t j = 0; j < kUnitRows / 4; j++)
+                    dst[(r + 4 * j) * (kUnitCols / 4) + c4] = cur[j];  // pitch 128 float4; zeros outside
+            }
+        }
+        mb = block_max(__float_as_uint(mf));
+    }
+    if (threadIdx.x == 0) atomicMax(&ctl->abs_b.v, mb);
+    if (!grid_barrier(ctl, G, 2, err)) return;
+
+    // ------------------------------------------------------------------ B2
+    if (threadIdx.x == 0) {
+        abs_s = ld_gpu(&ctl->abs_b.v);
+        ovf_s = ld_gpu(&ctl->ovf_b.v);
+    }
+    __syncthreads();
+    const bool own_ok_b = ovf_s == 0;
+    scale_from_absmax(rank_absmax(1, __uint_as_float(abs_s)), &scale, &inv);
     __syncthreads();
     if (fail_s) return;
     if (c == 0 && threadIdx.x == 0) scales[1] = scale;
     const CUtensorMap* bm = use_tma ? &bmap : nullptr;
-    const bool done = fast_inv(inv)
-                          ? quantize_units_transposed<true>(B4, N4, K, N, nch, ub0, ub1, cache, stage, Bt, inv, bm, tbar, err)
-                          : quantize_units_transposed<false>(B4, N4, K, N, nch, ub0, ub1, cache, stage, Bt, inv, bm, tbar, err);
+    const bool done = fast_inv(inv) ? quantize_b_units<true>(B4, N4, K, N, sb, cache, stage, Bt, inv, bm, tbar, ctl,
+                                                             bcast, gk, own_b, nown_b, own_ok_b, err)
+                                    : quantize_b_units<false>(B4, N4, K, N, sb, cache, stage, Bt, inv, bm, tbar, ctl,
+                                                              bcast, gk, own_b, nown_b, own_ok_b, err);
     if (!done) return;
-    // this call is finished on this CTA; the last CTA of this GPU bumps the call count
-    if (xr.world > 1 && threadIdx.x == 0) {
-        const uint32_t prev = atomicAdd(xr.ctl + 1, 1u);
+    if (threadIdx.x == 0) {
+        // the last CTA to finish zeroes what was used after barrier 2
+        unsigned int prev;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&ctl->done.v) : "memory");
         if (prev == G - 1) {
-            xr.ctl[1] = 0;
-            __threadfence();
-            atomicAdd(xr.ctl, 1u);
+            st_gpu(&ctl->bar_count.v, 0u);
+            st_gpu(&ctl->ctr_b2.v, 0u);
+            st_gpu(&ctl->abs_b.v, 0u);
+            st_gpu(&ctl->ovf_b.v, 0u);
+            st_gpu(&ctl->done.v, 0u);
+        }
+        // N-sharded calls: the last CTA of this GPU bumps the call count (the exchange tag)
+        if (xr.world > 1) {
+            const uint32_t p2 = atomicAdd(xr.ctl + 1, 1u);
+            if (p2 == G - 1) {
+                xr.ctl[1] = 0;
+                __threadfence();
+                atomicAdd(xr.ctl, 1u);
+            }
         }
     }
 }
@@ -536,7 +844,7 @@ bool prologue_coop_supported(uint32_t M, uint32_t N, uint32_t K, const float* A,
 }
 
 int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq, int8_t* Bt,
-                         float* scales, float* partials, cudaStream_t s, const CoopXRank* x) {
+                         float* scales, cudaStream_t s, const CoopXRank* x) {
     CoopRanks xr{};
     xr.world = 1;
     if (x && x->world > 1) {
@@ -552,6 +860,10 @@ int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, con
     }
     static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
     if (int arc = set_max_dynamic_smem(prologue_coop_kernel, (int)kCoopSmem, smem_set)) return arc;
+    // a control block per launch, round robin: launches that overlap on the GPU
+    // (other streams) use different blocks
+    static std::atomic<uint32_t> next_slot{0};
+    const uint32_t slot = next_slot.fetch_add(1, std::memory_order_relaxed) % kSlots;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)num_sms(), 1, 1);
     cfg.blockDim = dim3(kCoopThreads, 1, 1);
@@ -563,7 +875,7 @@ int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, con
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     // B as (256 columns, N / 256 column halves, K rows): one 256 x 2 x 32 box is a
-    // whole B unit (32 rows x 512 columns) in the shared-memory layout of the cache
+    // whole B unit (32 rows x 512 columns) in the shared-memory layout of the slots
     CUtensorMap bmap;
     memset(&bmap, 0, sizeof(bmap));
     uint32_t use_tma = 0;
@@ -574,8 +886,8 @@ int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, con
         if (rc) return rc;
         use_tma = 1;
     }
-    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, prologue_coop_kernel, A, B, Aq, Bt, M, N, K, scales, partials, xr, bmap,
-                                    use_tma, device_timeout_flag()));
+    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, prologue_coop_kernel, A, B, Aq, Bt, M, N, K, scales, xr, bmap, use_tma, slot,
+                                    device_timeout_flag()));
     ANE_CHECK_LAUNCH();
     return ANE_OK;
 }

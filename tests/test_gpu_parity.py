@@ -484,6 +484,8 @@ def test_q8_chain_in_cuda_graph(ane):
     (2048, 2052, 2048, None),       # smallest shapes that take the cooperative prologue
     (4100, 1024, 4096, "inf"),      # ragged per-CTA slices; +-inf in A
     (1024, 4096, 4112, "nan"),      # K not a multiple of 64; NaN in B
+    (1024, 2052, 8192, None),       # N % 256 != 0 with remainder units of B (read from L2 directly)
+    (8192, 4096, 1024, "nanA"),     # NaN in a remainder chunk of A (the last rows)
 ])
 def test_quantize_prologue_single_read(ane, M, N, K, special):
     """Aq, Bt and both scales from the one-kernel prologue, each bit-exact."""
@@ -497,6 +499,8 @@ def test_quantize_prologue_single_read(ane, M, N, K, special):
         A[3, 5], A[M - 1, K - 1] = np.inf, -np.inf
     if special == "nan":
         B[K // 2, N - 3] = np.nan
+    if special == "nanA":
+        A[M - 1, K - 2] = np.nan
     Aq, Bt, scales = ane.quantize_pair(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
     qa, sa = oracle.quantize_fp32_i8(A)
     qb, sb = oracle.quantize_fp32_i8(B)
