@@ -93,6 +93,7 @@ SIGNATURES = {
     "ane_absmax_pair_dev": (_i32, [_vp, _sz, _vp, _sz, _vp, _vp, _vp]),
     "ane_quantize_pair_absmax_dev": (_i32, [_u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ane_gemm_s8_dev": (_i32, [_u32, _u32, _u32, _vp, _vp, _vp, _f, _u8, _i32, _vp, _vp]),
+    "ane_gemm_s8_kn_dev": (_i32, [_u32, _u32, _u32, _vp, _vp, _u32, _vp, _f, _u8, _i32, _vp, _vp]),
     "ane_quantize_fp32_i8_dev": (_i32, [_u32, _vp, _vp, _vp, _vp]),
     "ane_pack_b_i8_dev": (_i32, [_u32, _u32, _vp, _vp, _vp]),
     "ane_dense_i8_dev": (_i32, [_u32, _u32, _u32, _f, _f, _u8, _vp, _vp, _vp, _vp, _vp]),
@@ -294,18 +295,23 @@ def dense_fused_i8_workspace(M: int, N: int, K: int, device="cuda"):
 
 
 def quantize_pair(A, B, stream=None):
-    """Stage 1 of dense_fused_i8: returns (Aq [M x K16], Bt [N x K16], scales[2])."""
+    """Stage 1 of dense_fused_i8: returns (Aq [M x K16], Bq [K16 x N16], scales[2]).
+
+    Bq holds the codes of B in B's own layout (row k = codes of B[k, :], pad
+    columns zero); its rows K..K16-1 are not written (they meet Aq's zero pad
+    columns in the GEMM)."""
     torch = _torch()
     M, K = A.shape
     N = B.shape[1]
     K16 = (K + 15) // 16 * 16
+    N16 = (N + 15) // 16 * 16
     Aq = torch.empty((M, K16), dtype=torch.int8, device=A.device)
-    Bt = torch.empty((N, K16), dtype=torch.int8, device=A.device)
+    Bq = torch.empty((K16, N16), dtype=torch.int8, device=A.device)
     scales = torch.empty(2, dtype=torch.float32, device=A.device)
     partials = torch.empty(int(_lib.ane_absmax_partials_count(M * K, K * N)), dtype=torch.float32, device=A.device)
     check(_lib.ane_quantize_pair_dev(M, N, K, A.contiguous().data_ptr(), B.contiguous().data_ptr(), Aq.data_ptr(),
-                                     Bt.data_ptr(), scales.data_ptr(), partials.data_ptr(), _stream_ptr(stream)))
-    return Aq, Bt, scales
+                                     Bq.data_ptr(), scales.data_ptr(), partials.data_ptr(), _stream_ptr(stream)))
+    return Aq, Bq, scales
 
 
 INT_GEMM_KINDS = {"igemm": 0, "ugemm": 1, "usgemm": 2}
@@ -332,6 +338,21 @@ def gemm_s8(Aq, Bt, scales=None, scale: float = 1.0, relu: bool = False, raw_i32
     check(_lib.ane_gemm_s8_dev(M, N, K16, Aq.data_ptr(), Bt.data_ptr(),
                                scales.data_ptr() if scales is not None else None, float(scale), int(bool(relu)),
                                1 if raw_i32 else 0, out.data_ptr(), _stream_ptr(stream)))
+    return out
+
+
+def gemm_s8_kn(Aq, Bq, N: int, scales=None, scale: float = 1.0, relu: bool = False, raw_i32: bool = False,
+               out=None, stream=None):
+    """Tensor-core int8 GEMM with B stored K x N: Aq [M x K16], Bq [K16 x ldb] (the
+    layout quantize_pair returns), N <= ldb output columns."""
+    torch = _torch()
+    M, K16 = Aq.shape
+    assert Bq.shape[0] >= K16 and Bq.shape[1] >= N
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.int32 if raw_i32 else torch.float32, device=Aq.device)
+    check(_lib.ane_gemm_s8_kn_dev(M, N, K16, Aq.data_ptr(), Bq.data_ptr(), Bq.stride(0),
+                                  scales.data_ptr() if scales is not None else None, float(scale), int(bool(relu)),
+                                  1 if raw_i32 else 0, out.data_ptr(), _stream_ptr(stream)))
     return out
 
 

@@ -124,9 +124,12 @@ private:
 };
 
 // dense_fused_i8 on a stream with a caller-provided workspace (layout below).
+// Aq: codes of A, M x K16 (pad columns 0).  Bq: codes of B in B's own layout,
+// K16 x N16 (row stride N16; rows past K are never written: they meet the zero
+// pad columns of Aq).
 struct FusedWs {
     int8_t* Aq;
-    int8_t* Bt;
+    int8_t* Bq;
     float* scales;
     float* partials;
 };
@@ -167,7 +170,7 @@ int launch_reduce_partials(const float* partials, int pblocks_a, int pblocks_b, 
 // dense_fused_i8 prologue as one cooperative kernel reading A and B from HBM
 // once (prologue_coop.cu); partials must hold 2 x num_sms() floats.
 bool prologue_coop_supported(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, const int8_t* Aq,
-                             const int8_t* Bt);
+                             const int8_t* Bq);
 // Cross-GPU absmax exchange of the cooperative prologue (N-sharded dense_fused_i8).
 struct CoopXRank {
     uint32_t world, rank;
@@ -175,15 +178,17 @@ struct CoopXRank {
     const void* slots;   // this GPU's exchange area (2 words per rank)
     uint32_t* ctl;       // this GPU's 2 control words
 };
-int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq, int8_t* Bt,
+// Writes Aq (M x K) and Bq (K x N), both in their tensor's own layout.
+int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq, int8_t* Bq,
                          float* scales, cudaStream_t s, const CoopXRank* x = nullptr);
 // dense_fused_i8 prologue in three programmatic-dependent launches with each fp32
 // tensor kept L2-resident between its absmax read and its quantize read;
 // partials must hold 2 x 1024 floats.
+// Aq: M x K16 (pad columns 0); Bq: K x N16 (B's layout, pad columns 0).
 int launch_quantize_staged(uint32_t M, uint32_t N, uint32_t K, uint32_t K16, const float* A, const float* B,
-                           int8_t* Aq, int8_t* Bt, float* scales, float* partials, cudaStream_t s);
+                           int8_t* Aq, int8_t* Bq, float* scales, float* partials, cudaStream_t s);
 int launch_quantize_pair(uint32_t M, uint32_t N, uint32_t K, uint32_t K16, const float* A,
-                         const float* B, int8_t* Aq, int8_t* Bt, float* scales, const float* partials,
+                         const float* B, int8_t* Aq, int8_t* Bq, float* scales, const float* partials,
                          int blocks_a, int blocks_b, cudaStream_t s);
 int launch_quantize_flat(size_t count, const float* src, int8_t* dst, float* scale_out,
                          float* partials, int blocks, cudaStream_t s);
@@ -229,6 +234,12 @@ struct GatherArgs {
 int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const int8_t* Bt, void* C, size_t ldc,
                       const GemmEpilogue& ep, cudaStream_t s, const GatherArgs* gather = nullptr,
                       uint32_t* grid_out = nullptr);
+// The same with B given as codes stored K x N (row stride ldb bytes, a multiple
+// of 16; the buffer holds K rows, K a multiple of 16): B is read as an
+// MN-major tcgen05 operand.
+int launch_gemm_s8_tc_kn(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const int8_t* Bq, size_t ldb,
+                         void* C, size_t ldc, const GemmEpilogue& ep, cudaStream_t s,
+                         const GatherArgs* gather = nullptr, uint32_t* grid_out = nullptr);
 int launch_gather_wait(const uint32_t* ctr, uint32_t* epoch, uint32_t per_call, cudaStream_t s);
 int launch_fill_epilogue_zero_k(uint32_t M, uint32_t N, void* C, size_t ldc, const GemmEpilogue& ep,
                                 cudaStream_t s);

@@ -169,12 +169,13 @@ size_t fused_ws_layout(uint32_t M, uint32_t N, uint32_t K, FusedWs* w, void* bas
         off += a256(bytes);
         return o;
     };
-    size_t oa = take((size_t)M * K16), ob = take((size_t)N * K16), os = take(2 * sizeof(float)),
+    const size_t N16 = round_up(N, 16);
+    size_t oa = take((size_t)M * K16), ob = take(K16 * N16), os = take(2 * sizeof(float)),
            op = take(pcount * sizeof(float));
     if (w && base) {
         uint8_t* b = static_cast<uint8_t*>(base);
         w->Aq = reinterpret_cast<int8_t*>(b + oa);
-        w->Bt = reinterpret_cast<int8_t*>(b + ob);
+        w->Bq = reinterpret_cast<int8_t*>(b + ob);
         w->scales = reinterpret_cast<float*>(b + os);
         w->partials = reinterpret_cast<float*>(b + op);
     }
@@ -182,15 +183,16 @@ size_t fused_ws_layout(uint32_t M, uint32_t N, uint32_t K, FusedWs* w, void* bas
 }
 
 // The quantize prologue: one cooperative kernel when the shape allows it
-// (prologue_coop.cu), else three programmatic-dependent launches.
+// (prologue_coop.cu), else three programmatic-dependent launches.  Either way
+// Aq is M x K16 and Bq is B's codes in B's layout, row stride N16.
 // ANE_PROLOGUE=staged forces the latter (tuning aid).
 static int launch_prologue(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
-                           int8_t* Bt, float* scales, float* partials, cudaStream_t s) {
+                           int8_t* Bq, float* scales, float* partials, cudaStream_t s) {
     static const char* force = getenv("ANE_PROLOGUE");
     const bool staged = force && !strcmp(force, "staged");
-    if (!staged && prologue_coop_supported(M, N, K, A, B, Aq, Bt))
-        return launch_prologue_coop(M, N, K, A, B, Aq, Bt, scales, s);
-    return launch_quantize_staged(M, N, K, (uint32_t)round_up(K, 16), A, B, Aq, Bt, scales, partials, s);
+    if (!staged && prologue_coop_supported(M, N, K, A, B, Aq, Bq))
+        return launch_prologue_coop(M, N, K, A, B, Aq, Bq, scales, s);
+    return launch_quantize_staged(M, N, K, (uint32_t)round_up(K, 16), A, B, Aq, Bq, scales, partials, s);
 }
 
 int dense_fused_on_stream(uint32_t M, uint32_t N, uint32_t K, float scale, uint8_t relu, const float* A,
@@ -198,10 +200,10 @@ int dense_fused_on_stream(uint32_t M, uint32_t N, uint32_t K, float scale, uint8
     FusedWs w{};
     fused_ws_layout(M, N, K, &w, ws);
     const uint32_t K16 = (uint32_t)round_up(K, 16);
-    int rc = launch_prologue(M, N, K, A, B, w.Aq, w.Bt, w.scales, w.partials, s);
+    int rc = launch_prologue(M, N, K, A, B, w.Aq, w.Bq, w.scales, w.partials, s);
     if (rc) return rc;
     GemmEpilogue ep{kOutFusedF32, w.scales, 0.f, 0.f, scale, relu ? 1 : 0, nullptr};
-    return launch_gemm_s8_tc(M, N, K16, w.Aq, w.Bt, C, N, ep, s);
+    return launch_gemm_s8_tc_kn(M, N, K16, w.Aq, w.Bq, round_up(N, 16), C, N, ep, s);
 }
 
 namespace {
@@ -322,10 +324,10 @@ int ane_dense_fused_i8_dev(uint32_t M, uint32_t N, uint32_t K, float scale, uint
 }
 
 int ane_quantize_pair_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
-                          int8_t* Bt, float* scales, float* partials, void* stream) {
+                          int8_t* Bq, float* scales, float* partials, void* stream) {
     ANE_REQUIRE_GPU();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    int rc = launch_prologue(M, N, K, A, B, Aq, Bt, scales, partials, s);
+    int rc = launch_prologue(M, N, K, A, B, Aq, Bq, scales, partials, s);
     return rc ? rc : ok();
 }
 
@@ -341,11 +343,20 @@ int ane_absmax_pair_dev(const float* A, size_t count_a, const float* B, size_t c
 }
 
 int ane_quantize_pair_absmax_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
-                                 int8_t* Bt, const float* absmax2, float* scales, void* stream) {
+                                 int8_t* Bq, const float* absmax2, float* scales, void* stream) {
     ANE_REQUIRE_GPU();
     // absmax2 stands in for a one-entry partials list per tensor
-    int rc = launch_quantize_pair(M, N, K, (uint32_t)round_up(K, 16), A, B, Aq, Bt, scales, absmax2, 1, 1,
+    int rc = launch_quantize_pair(M, N, K, (uint32_t)round_up(K, 16), A, B, Aq, Bq, scales, absmax2, 1, 1,
                                   static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+int ane_gemm_s8_kn_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* Aq, const int8_t* Bq, uint32_t ldb,
+                       const float* scales, float scale, uint8_t relu, int out_mode, void* C, void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(out_mode == 0 || out_mode == 1, "gemm_s8_kn: out_mode must be 0 (fp32) or 1 (int32)");
+    GemmEpilogue ep{out_mode == 0 ? kOutFusedF32 : kOutRawI32, scales, 1.f, 1.f, scale, relu ? 1 : 0, nullptr};
+    int rc = launch_gemm_s8_tc_kn(M, N, K16, Aq, Bq, ldb, C, N, ep, static_cast<cudaStream_t>(stream));
     return rc ? rc : ok();
 }
 
@@ -576,12 +587,12 @@ int ane_mul_mat_q8_0_batch_dev(uint32_t M, uint32_t K, uint32_t NT, const float*
 }
 
 int ane_quantize_pair_xrank_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
-                                int8_t* Bt, float* scales, float* partials, uint32_t world, uint32_t rank,
+                                int8_t* Bq, float* scales, float* partials, uint32_t world, uint32_t rank,
                                 void* const* slot_peer, const void* slots, uint32_t* ctl, void* stream) {
     ANE_REQUIRE_GPU();
     ANE_ARG_CHECK(world >= 1 && world <= 8 && rank < world, "quantize xrank: world must be 1..8, rank < world");
-    ANE_ARG_CHECK(prologue_coop_supported(M, N, K, A, B, Aq, Bt),
-                  "quantize xrank: needs K % 16 == 0, N % 4 == 0, 16-byte alignment and M*K, K*N >= 2^22");
+    ANE_ARG_CHECK(prologue_coop_supported(M, N, K, A, B, Aq, Bq),
+                  "quantize xrank: needs K % 16 == 0, N % 16 == 0, 16-byte alignment and M*K, K*N >= 2^22");
     ANE_ARG_CHECK(world == 1 || (slot_peer && slots && ctl), "quantize xrank: NULL exchange pointer");
     CoopXRank x{};
     x.world = world;
@@ -590,11 +601,11 @@ int ane_quantize_pair_xrank_dev(uint32_t M, uint32_t N, uint32_t K, const float*
     x.slots = slots;
     x.ctl = ctl;
     (void)partials;  // the cooperative prologue reduces through its own control block
-    int rc = launch_prologue_coop(M, N, K, A, B, Aq, Bt, scales, static_cast<cudaStream_t>(stream), &x);
+    int rc = launch_prologue_coop(M, N, K, A, B, Aq, Bq, scales, static_cast<cudaStream_t>(stream), &x);
     return rc ? rc : ok();
 }
 
-int ane_gemm_s8_gather_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* Aq, const int8_t* Bt,
+int ane_gemm_s8_gather_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* Aq, const int8_t* Bq,
                            const float* scales, float scale, uint8_t relu, uint32_t world, uint32_t rank,
                            void* const* C_ranks, uint32_t ldc, uint32_t* const* ctr_ranks, uint32_t* epoch,
                            void* stream) {
@@ -611,7 +622,7 @@ int ane_gemm_s8_gather_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* A
     }
     GemmEpilogue ep{kOutFusedF32, scales, 0.f, 0.f, scale, relu ? 1 : 0, nullptr};
     uint32_t grid = 0;
-    int rc = launch_gemm_s8_tc(M, N, K16, Aq, Bt, C_ranks[rank], ldc, ep, s, &g, &grid);
+    int rc = launch_gemm_s8_tc_kn(M, N, K16, Aq, Bq, round_up(N, 16), C_ranks[rank], ldc, ep, s, &g, &grid);
     if (rc) return rc;
     rc = launch_gather_wait(ctr_ranks[rank], epoch, world * grid, s);
     return rc ? rc : ok();

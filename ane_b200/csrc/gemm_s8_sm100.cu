@@ -65,6 +65,9 @@ constexpr size_t P_SMEM = (size_t)P_STAGES * P_STAGE + EPI_BYTES + sizeof(Barrie
 static_assert(S_SMEM <= 232448 && P_SMEM <= 232448, "shared memory budget");
 
 constexpr uint32_t kGatherMaxRanks = 8;
+// MN-major B: bytes between two 128-column SWIZZLE_128B atoms of one stage
+// (the single-CTA kernel's 256-column tile is two such boxes)
+constexpr uint32_t kMnAtomBytes = 128 * BK;
 constexpr uint32_t P_BN_COLS = 256;  // pair tile width (= P_BN)
 
 struct Params {
@@ -227,6 +230,8 @@ __device__ __forceinline__ void drain_accumulator(const Params& p, uint32_t tadd
 }
 
 // ------------------------------------------------------------ 1-CTA kernel
+// BKN: B is given as the codes stored K x N (MN-major operand) instead of N x K.
+template <bool BKN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_s8_single_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const Params p) {
@@ -276,14 +281,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     if (!ptx::mbar_wait(&bars->empty[stage], phase ^ 1, p.err)) { alive = false; break; }
                     ptx::mbar_arrive_expect_tx(&bars->full[stage], S_STAGE);
                     ptx::tma_load_2d(sa + (size_t)stage * S_A, &tmap_a, &bars->full[stage], (int)(kb * BK), m0);
-                    ptx::tma_load_2d(sb + (size_t)stage * S_B, &tmap_b, &bars->full[stage], (int)(kb * BK), n0);
+                    if constexpr (BKN) {
+                        // two 128-column SWIZZLE_128B boxes, one N atom each (16 KB apart)
+                        ptx::tma_load_2d(sb + (size_t)stage * S_B, &tmap_b, &bars->full[stage], n0, (int)(kb * BK));
+                        ptx::tma_load_2d(sb + (size_t)stage * S_B + kMnAtomBytes, &tmap_b, &bars->full[stage],
+                                         n0 + 128, (int)(kb * BK));
+                    } else {
+                        ptx::tma_load_2d(sb + (size_t)stage * S_B, &tmap_b, &bars->full[stage], (int)(kb * BK), n0);
+                    }
                     if (++stage == S_STAGES) { stage = 0; phase ^= 1; }
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = ptx::idesc_i8(S_BM, S_BN, !p.ep.a_unsigned, !p.ep.b_unsigned);
+            const uint32_t idesc = ptx::idesc_i8(S_BM, S_BN, !p.ep.a_unsigned, !p.ep.b_unsigned) |
+                                   (BKN ? ptx::kIdescBMnMajor : 0u);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool alive = true;
             for (uint32_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
@@ -296,9 +309,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t a_addr = ptx::smem_u32(sa + (size_t)stage * S_A);
                     const uint32_t b_addr = ptx::smem_u32(sb + (size_t)stage * S_B);
 #pragma unroll
-                    for (int k = 0; k < BK / UMMA_K; k++)
-                        ptx::umma_i8(d_tmem, ptx::sdesc_kmajor_sw128(a_addr + k * UMMA_K),
-                                     ptx::sdesc_kmajor_sw128(b_addr + k * UMMA_K), idesc, (kb | k) != 0);
+                    for (int k = 0; k < BK / UMMA_K; k++) {
+                        const uint64_t bdesc = BKN ? ptx::sdesc_mn(b_addr + k * UMMA_K * 128, 128, kMnAtomBytes)
+                                                   : ptx::sdesc_kmajor_sw128(b_addr + k * UMMA_K);
+                        ptx::umma_i8(d_tmem, ptx::sdesc_kmajor_sw128(a_addr + k * UMMA_K), bdesc, idesc,
+                                     (kb | k) != 0);
+                    }
                     ptx::umma_commit(&bars->empty[stage]);
                     if (++stage == S_STAGES) { stage = 0; phase ^= 1; }
                 }
@@ -337,9 +353,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 // --------------------------------------------------------- CTA-pair kernel
+// BKN: B is given as the codes stored K x N (MN-major operand).  Then each CTA's
+// B half of a unit (`half` = 128, 64 or 32 columns) is one TMA box of `half`
+// columns x BK rows with the swizzle of that width: tmap_b, tmap_b64, tmap_b32.
+// Without BKN, tmap_b holds 128-row K-major boxes and tmap_b32 32-row ones.
+template <bool BKN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_s8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                        const __grid_constant__ CUtensorMap tmap_b32, const Params p) {
+                        const __grid_constant__ CUtensorMap tmap_b64, const __grid_constant__ CUtensorMap tmap_b32,
+                        const Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sa = smem;
@@ -365,6 +387,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ptx::prefetch_tmap(&tmap_a);
         ptx::prefetch_tmap(&tmap_b);
         if (p.split > 1) ptx::prefetch_tmap(&tmap_b32);
+        if (BKN && p.split > 1) ptx::prefetch_tmap(&tmap_b64);
     }
     if (warp == 1) {
         ptx::tmem_alloc_cg2(&bars->tmem_base, TMEM_COLS);
@@ -395,7 +418,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     if (rank == 0) ptx::mbar_arrive_expect_tx(&bars->full[stage], tx);
                     const uint32_t full_leader = ptx::mapa_shared(ptx::smem_u32(&bars->full[stage]), 0);
                     ptx::tma_load_2d_cg2(sa + (size_t)stage * P_A, &tmap_a, full_leader, (int)(kb * BK), m0);
-                    if (half == P_HN) {
+                    if constexpr (BKN) {
+                        const CUtensorMap* bm = half == P_HN ? &tmap_b : half == 64 ? &tmap_b64 : &tmap_b32;
+                        ptx::tma_load_2d_cg2(sb + (size_t)stage * P_B, bm, full_leader, n0, (int)(kb * BK));
+                    } else if (half == P_HN) {
                         ptx::tma_load_2d_cg2(sb + (size_t)stage * P_B, &tmap_b, full_leader, (int)(kb * BK), n0);
                     } else {
                         // 32-row boxes, each 4 KB apart: the same SWIZZLE_128B image as one taller box
@@ -414,7 +440,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (uint32_t u = pair; u < num_units && alive; u += num_pairs) {
                 const PairUnit un = pair_unit(p, u);
                 if (un.n0 >= p.N) continue;
-                const uint32_t idesc = ptx::idesc_i8(P_BM, (int)un.ncols, !p.ep.a_unsigned, !p.ep.b_unsigned);
+                const uint32_t idesc = ptx::idesc_i8(P_BM, (int)un.ncols, !p.ep.a_unsigned, !p.ep.b_unsigned) |
+                                       (BKN ? ptx::kIdescBMnMajor : 0u);
+                const uint32_t half = un.ncols / 2;  // B columns (MN-major row bytes) per CTA
                 if (!ptx::mbar_wait(&bars->tmem_empty[acc], acc_phase ^ 1, p.err)) break;
                 ptx::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
@@ -424,9 +452,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t a_addr = ptx::smem_u32(sa + (size_t)stage * P_A);
                     const uint32_t b_addr = ptx::smem_u32(sb + (size_t)stage * P_B);
 #pragma unroll
-                    for (int k = 0; k < BK / UMMA_K; k++)
-                        ptx::umma_i8_cg2(d_tmem, ptx::sdesc_kmajor_sw128(a_addr + k * UMMA_K),
-                                         ptx::sdesc_kmajor_sw128(b_addr + k * UMMA_K), idesc, (kb | k) != 0);
+                    for (int k = 0; k < BK / UMMA_K; k++) {
+                        const uint64_t bdesc = BKN ? ptx::sdesc_mn(b_addr + k * UMMA_K * half, half, kMnAtomBytes)
+                                                   : ptx::sdesc_kmajor_sw128(b_addr + k * UMMA_K);
+                        ptx::umma_i8_cg2(d_tmem, ptx::sdesc_kmajor_sw128(a_addr + k * UMMA_K), bdesc, idesc,
+                                         (kb | k) != 0);
+                    }
                     ptx::umma_commit_cg2_mc(&bars->empty[stage], 0x3);  // frees the stage in both CTAs
                     if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
                 }
@@ -506,17 +537,33 @@ int make_kmajor_map(CUtensorMap* map, const int8_t* base, uint32_t rows, uint32_
     return encode_tensor_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, K, rows, K, BK, box_rows,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
 }
+// MN-major int8 operand (B codes K x N, row stride ldb bytes), box = `cols`
+// (128, 64 or 32) x BK rows with the swizzle of that width.  Rows past `rows`
+// and columns past N read as zero.
+int make_mn_map(CUtensorMap* map, const int8_t* base, uint32_t N, uint32_t rows, size_t ldb, uint32_t cols) {
+    const CUtensorMapSwizzle sw = cols == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : cols == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                               : CU_TENSOR_MAP_SWIZZLE_32B;
+    return encode_tensor_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, N, rows, ldb, cols, BK, sw);
+}
 
+// B operand of one launch: Bt (N x K, K-major) or Bq (K x N, row stride ldb).
+struct BOperand {
+    const int8_t* ptr;
+    size_t ldb;      // Bq: row stride in bytes (multiple of 16)
+};
 
-}  // namespace
-
-int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const int8_t* Bt, void* C, size_t ldc,
-                      const GemmEpilogue& ep, cudaStream_t s, const GatherArgs* gather, uint32_t* grid_out) {
+template <bool BKN>
+int launch_gemm_impl(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const BOperand& bop, void* C, size_t ldc,
+                     const GemmEpilogue& ep, cudaStream_t s, const GatherArgs* gather, uint32_t* grid_out) {
+    const int8_t* Bt = bop.ptr;
     if (M == 0 || N == 0) return ANE_OK;
     if (K == 0) return launch_fill_epilogue_zero_k(M, N, C, ldc, ep, s);
     ANE_ARG_CHECK(K % 16 == 0, "gemm: K must be a multiple of 16 (TMA row stride)");
     ANE_ARG_CHECK((reinterpret_cast<uintptr_t>(Aq) & 15) == 0 && (reinterpret_cast<uintptr_t>(Bt) & 15) == 0,
                   "gemm: int8 operands must be 16-byte aligned");
+    ANE_ARG_CHECK(!BKN || (bop.ldb % 16 == 0 && bop.ldb >= N),
+                  "gemm: B stored K x N needs a row stride that is a multiple of 16 and >= N");
     Params p;
     p.M = M;
     p.N = N;
@@ -550,21 +597,21 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
     CUtensorMap ta, tb;
     int rc = make_kmajor_map(&ta, Aq, M, K, pair ? P_HM : S_BM);
     if (rc) return rc;
-    rc = make_kmajor_map(&tb, Bt, N, K, pair ? P_HN : S_BN);
+    rc = BKN ? make_mn_map(&tb, Bt, N, K, bop.ldb, 128) : make_kmajor_map(&tb, Bt, N, K, pair ? P_HN : S_BN);
     if (rc) return rc;
     if (!pair) {
         static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
-        rc = set_max_dynamic_smem(gemm_s8_single_kernel, (int)S_SMEM, smem_set);
+        rc = set_max_dynamic_smem(gemm_s8_single_kernel<BKN>, (int)S_SMEM, smem_set);
         if (rc) return rc;
         p.tiles_m = (M + S_BM - 1) / S_BM;
         p.tiles_n = (N + S_BN - 1) / S_BN;
         const uint32_t tiles = p.tiles_m * p.tiles_n;
         const uint32_t grid = tiles < (uint32_t)sms ? tiles : (uint32_t)sms;
         if (grid_out) *grid_out = grid;
-        return launch_pdl(gemm_s8_single_kernel, dim3(grid), dim3(NUM_THREADS), S_SMEM, s, ta, tb, p);
+        return launch_pdl(gemm_s8_single_kernel<BKN>, dim3(grid), dim3(NUM_THREADS), S_SMEM, s, ta, tb, p);
     }
     static std::atomic<uint64_t> smem_set2{0};
-    rc = set_max_dynamic_smem(gemm_s8_pair_kernel, (int)P_SMEM, smem_set2);
+    rc = set_max_dynamic_smem(gemm_s8_pair_kernel<BKN>, (int)P_SMEM, smem_set2);
     if (rc) return rc;
     p.tiles_m = (M + P_BM - 1) / P_BM;
     p.tiles_n = (N + P_BN - 1) / P_BN;
@@ -591,12 +638,16 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
     p.num_units = p.tail_start + p.split * (tiles - p.tail_start);
     if (pairs > p.num_units) pairs = p.num_units;
     if (grid_out) *grid_out = 2 * pairs;
-    CUtensorMap tb32;
+    CUtensorMap tb64 = tb, tb32 = tb;  // unused unless the tail is split
     if (p.split > 1) {
-        rc = make_kmajor_map(&tb32, Bt, N, K, 32);
+        if (BKN) {
+            rc = make_mn_map(&tb64, Bt, N, K, bop.ldb, 64);
+            if (rc) return rc;
+            rc = make_mn_map(&tb32, Bt, N, K, bop.ldb, 32);
+        } else {
+            rc = make_kmajor_map(&tb32, Bt, N, K, 32);
+        }
         if (rc) return rc;
-    } else {
-        tb32 = tb;  // unused
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
@@ -612,9 +663,24 @@ int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, cons
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_s8_pair_kernel, ta, tb, tb32, p));
+    ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_s8_pair_kernel<BKN>, ta, tb, tb64, tb32, p));
     ANE_CHECK_LAUNCH();
     return ANE_OK;
+}
+
+}  // namespace
+
+int launch_gemm_s8_tc(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const int8_t* Bt, void* C, size_t ldc,
+                      const GemmEpilogue& ep, cudaStream_t s, const GatherArgs* gather, uint32_t* grid_out) {
+    const BOperand b{Bt, 0};
+    return launch_gemm_impl<false>(M, N, K, Aq, b, C, ldc, ep, s, gather, grid_out);
+}
+
+int launch_gemm_s8_tc_kn(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const int8_t* Bq, size_t ldb,
+                         void* C, size_t ldc, const GemmEpilogue& ep, cudaStream_t s, const GatherArgs* gather,
+                         uint32_t* grid_out) {
+    const BOperand b{Bq, ldb};
+    return launch_gemm_impl<true>(M, N, K, Aq, b, C, ldc, ep, s, gather, grid_out);
 }
 
 // Fused all-gather, receiving side: one thread waits (bounded) until every CTA

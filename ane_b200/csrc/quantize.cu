@@ -184,75 +184,13 @@ __device__ void quantize_rows(const float* __restrict__ src, int8_t* __restrict_
     }
 }
 
-// ------------------------------------------------ transposing quantize of B
-// B is K x N fp32 row-major; Bt is N x ld int8 (ld = K16), Bt[n][k] = q(B[k][n]),
-// zero for K <= k < ld.  Tiles of 128 (k) x 32 (n) through shared memory:
-// each thread issues its four 16-byte loads (rows k, k+32, k+64, k+96; 4-column
-// group) back to back, quantizes, scatters the bytes into a transposed tile
-// (pitch 132 B = 33 words: conflict-free both ways), then each n-row of the tile
-// leaves as one full 128-byte line.  Tiles are walked from the highest k down,
-// the reverse of the absmax pass, to hit its L2-resident tail first.
-static constexpr int kTK = 128, kTN = 32;
-static constexpr int kTPitch = kTK + 4;
-
-__device__ void quantize_transpose(const float* __restrict__ B, int8_t* __restrict__ Bt, uint32_t K,
-                                   uint32_t N, uint32_t ld, float inv, int bid, int nblk) {
-    __shared__ __align__(16) uint8_t tile[kTN * kTPitch];
-    const uint32_t tiles_k = (ld + kTK - 1) / kTK, tiles_n = (N + kTN - 1) / kTN;
-    const uint32_t num_tiles = tiles_k * tiles_n;
-    const uint32_t t8 = threadIdx.x & 7, r0 = threadIdx.x >> 3;  // 4-column group, first row
-    const bool vec = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(B) & 15) == 0);
-    const uint64_t pol = l2_policy_evict_first();  // last read of B
-    for (uint32_t it = bid; it < num_tiles; it += nblk) {
-        const uint32_t t = num_tiles - 1 - it;
-        const uint32_t k0 = (t / tiles_n) * kTK, n0 = (t % tiles_n) * kTN;
-        const uint32_t n = n0 + 4 * t8;
-        float4 v[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint32_t k = k0 + r0 + 32 * i;
-            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (k < K) {
-                const float* src = B + (size_t)k * N + n;
-                if (vec && n + 4 <= N) {
-                    v[i] = ld_policy(reinterpret_cast<const float4*>(src), pol);
-                } else {
-                    if (n + 0 < N) v[i].x = __ldcs(src + 0);
-                    if (n + 1 < N) v[i].y = __ldcs(src + 1);
-                    if (n + 2 < N) v[i].z = __ldcs(src + 2);
-                    if (n + 3 < N) v[i].w = __ldcs(src + 3);
-                }
-            }
-        }
-        __syncthreads();  // previous tile's reads of `tile` are done
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint32_t kl = r0 + 32 * i;
-            const bool kin = k0 + kl < K;  // zero padding K <= k < ld
-            uint8_t* col = tile + (4 * t8) * kTPitch + kl;
-            col[0 * kTPitch] = kin ? (uint8_t)quantize_one(v[i].x, inv) : 0;
-            col[1 * kTPitch] = kin ? (uint8_t)quantize_one(v[i].y, inv) : 0;
-            col[2 * kTPitch] = kin ? (uint8_t)quantize_one(v[i].z, inv) : 0;
-            col[3 * kTPitch] = kin ? (uint8_t)quantize_one(v[i].w, inv) : 0;
-        }
-        __syncthreads();
-        const uint32_t nl = threadIdx.x >> 3, kc = (threadIdx.x & 7) * 16;
-        const uint32_t nn = n0 + nl, k = k0 + kc;
-        if (nn < N && k < ld) {
-            const uint32_t* src = reinterpret_cast<const uint32_t*>(tile + nl * kTPitch + kc);
-            const uint4 o = make_uint4(src[0], src[1], src[2], src[3]);
-            // ld is a multiple of 16, so a 16-byte chunk is either all in or all out
-            *reinterpret_cast<uint4*>(Bt + (size_t)nn * ld + k) = o;
-        }
-    }
-}
-
-// Quantize A (row-major -> Aq, row stride ld) and B (-> Bt transposed, row stride
-// ld) in one launch: blocks [0, blocks_a) take A, the rest take B.
+// Quantize A (row-major -> Aq, row stride lda) and B (row-major -> Bq, row
+// stride ldb: B's own layout) in one launch: blocks [0, blocks_a) take A, the
+// rest take B.
 __global__ void __launch_bounds__(kThreads) quantize_pair_kernel(
     const float* __restrict__ A, const float* __restrict__ B, int8_t* __restrict__ Aq,
-    int8_t* __restrict__ Bt, float* __restrict__ scales, const float* __restrict__ partials,
-    uint32_t M, uint32_t N, uint32_t K, uint32_t ld, int pblocks_a, int pblocks_b, int blocks_a) {
+    int8_t* __restrict__ Bq, float* __restrict__ scales, const float* __restrict__ partials,
+    uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb, int pblocks_a, int pblocks_b, int blocks_a) {
     const bool seg_b = (int)blockIdx.x >= blocks_a;
     const float absmax = seg_b ? reduce_partials(partials + pblocks_a, pblocks_b)
                                : reduce_partials(partials, pblocks_a);
@@ -262,9 +200,9 @@ __global__ void __launch_bounds__(kThreads) quantize_pair_kernel(
     const int nblk = seg_b ? (int)gridDim.x - blocks_a : blocks_a;
     if (bid == 0 && threadIdx.x == 0) scales[seg_b ? 1 : 0] = scale;
     if (!seg_b)
-        quantize_rows(A, Aq, M, K, ld, inv, bid, nblk);
+        quantize_rows(A, Aq, M, K, lda, inv, bid, nblk);
     else
-        quantize_transpose(B, Bt, K, N, ld, inv, bid, nblk);
+        quantize_rows(B, Bq, K, N, ldb, inv, bid, nblk);
 }
 
 // ------------------------------------------ staged dense_fused_i8 prologue
@@ -272,7 +210,7 @@ __global__ void __launch_bounds__(kThreads) quantize_pair_kernel(
 //   absmax_keep_kernel          absmax partials of A (A marked evict_last)
 //   quantize_a_absmax_b_kernel  quantize A (its last read)  +  absmax partials of
 //                               B (B marked evict_last), in one grid
-//   quantize_b_kernel           transposing quantize of B (its last read)
+//   quantize_b_kernel           quantize of B into its own layout (its last read)
 // All three are launched with programmatic dependent launch: they signal the
 // next launch at entry and wait for the previous one before touching memory.
 __global__ void __launch_bounds__(kThreads) absmax_keep_kernel(const float* __restrict__ x, size_t n,
@@ -301,8 +239,8 @@ __global__ void __launch_bounds__(kThreads) quantize_a_absmax_b_kernel(
     }
 }
 
-__global__ void __launch_bounds__(kThreads) quantize_b_kernel(const float* __restrict__ B, int8_t* __restrict__ Bt,
-                                                              uint32_t K, uint32_t N, uint32_t ld,
+__global__ void __launch_bounds__(kThreads) quantize_b_kernel(const float* __restrict__ B, int8_t* __restrict__ Bq,
+                                                              uint32_t K, uint32_t N, uint32_t ldb,
                                                               float* __restrict__ scales,
                                                               const float* __restrict__ partials_b, int pb) {
     ptx::griddep_launch_dependents();
@@ -310,7 +248,7 @@ __global__ void __launch_bounds__(kThreads) quantize_b_kernel(const float* __res
     float scale, inv;
     scale_from_absmax(reduce_partials(partials_b, pb), &scale, &inv);
     if (blockIdx.x == 0 && threadIdx.x == 0) scales[1] = scale;
-    quantize_transpose(B, Bt, K, N, ld, inv, blockIdx.x, gridDim.x);
+    quantize_rows(B, Bq, K, N, ldb, inv, blockIdx.x, gridDim.x);
 }
 
 // Flat quantize of one tensor (opcode 0x19).
@@ -389,9 +327,10 @@ int launch_absmax_partials(const float* a, size_t na, const float* b, size_t nb,
 }
 
 int launch_quantize_pair(uint32_t M, uint32_t N, uint32_t K, uint32_t K16, const float* A,
-                         const float* B, int8_t* Aq, int8_t* Bt, float* scales, const float* partials,
+                         const float* B, int8_t* Aq, int8_t* Bq, float* scales, const float* partials,
                          int pblocks_a, int pblocks_b, cudaStream_t s) {
-    const size_t work_a = (size_t)M * K16, work_b = (size_t)N * K16;
+    const uint32_t N16 = (uint32_t)round_up(N, 16);
+    const size_t work_a = (size_t)M * K16, work_b = (size_t)K * N16;
     const int sms = num_sms();
     // split ~4 waves of blocks between the two tensors in proportion to their size
     int total = sms * 8;  // 8 resident 256-thread blocks per SM
@@ -399,17 +338,14 @@ int launch_quantize_pair(uint32_t M, uint32_t N, uint32_t K, uint32_t K16, const
     if (ba < 1) ba = 1;
     int bb = total - ba;
     if (bb < 1) bb = 1;
-    size_t tiles_b = ceil_div(K16, kTK) * ceil_div(N, kTN);
-    if ((size_t)bb > tiles_b) bb = (int)tiles_b;
-    if (bb < 1) bb = 1;
-    quantize_pair_kernel<<<ba + bb, kThreads, 0, s>>>(A, B, Aq, Bt, scales, partials, M, N, K, K16,
+    quantize_pair_kernel<<<ba + bb, kThreads, 0, s>>>(A, B, Aq, Bq, scales, partials, M, N, K, K16, N16,
                                                       pblocks_a, pblocks_b, ba);
     ANE_CHECK_LAUNCH();
     return ANE_OK;
 }
 
 int launch_quantize_staged(uint32_t M, uint32_t N, uint32_t K, uint32_t K16, const float* A, const float* B,
-                           int8_t* Aq, int8_t* Bt, float* scales, float* partials, cudaStream_t s) {
+                           int8_t* Aq, int8_t* Bq, float* scales, float* partials, cudaStream_t s) {
     const size_t na = (size_t)M * K, nb = (size_t)K * N;
     const int pa = absmax_blocks_for(na), pb = absmax_blocks_for(nb);
     const int sms = num_sms();
@@ -422,11 +358,12 @@ int launch_quantize_staged(uint32_t M, uint32_t N, uint32_t K, uint32_t K16, con
     rc = launch_pdl(quantize_a_absmax_b_kernel, dim3(qa + pb), dim3(kThreads), 0, s, A, Aq, M, K, K16, B, nb,
                     scales, partials, pa, qa);
     if (rc) return rc;
+    const uint32_t N16 = (uint32_t)round_up(N, 16);
     int qb = sms * 8;
-    const size_t tiles_b = ceil_div(K16, kTK) * ceil_div(N, kTN);
-    if ((size_t)qb > tiles_b) qb = (int)tiles_b;
+    const size_t chunks_b = (size_t)K * N16 / 16;
+    if ((size_t)qb * kThreads > chunks_b) qb = (int)ceil_div(chunks_b, (size_t)kThreads);
     if (qb < 1) qb = 1;
-    return launch_pdl(quantize_b_kernel, dim3(qb), dim3(kThreads), 0, s, B, Bt, K, N, K16, scales,
+    return launch_pdl(quantize_b_kernel, dim3(qb), dim3(kThreads), 0, s, B, Bq, K, N, N16, scales,
                       (const float*)partials + pa, pb);
 }
 

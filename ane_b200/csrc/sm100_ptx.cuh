@@ -28,6 +28,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// Arrive without release semantics: the thread's earlier memory operations
+// (global stores in flight) are not waited for.  For consumers that free a
+// buffer whose shared-memory reads have already returned their values.
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -267,6 +273,25 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
     d |= (uint64_t)2u << 61;
     return d;
 }
+
+// Shared-memory matrix descriptor for an MN-major operand tile (the B codes
+// stored K x N, N contiguous) laid out by a TMA box of `row_bytes` (128, 64 or
+// 32) columns x K rows with the matching swizzle (SWIZZLE_128B / 64B / 32B):
+// K row r sits at r * row_bytes, one swizzle atom = row_bytes columns x 8 K
+// rows.  Stride byte offset = 8 * row_bytes (next 8 K rows); leading byte
+// offset = `lbo` (next atom along N, used when the tile is wider than one atom).
+// Layout codes (bits 61-63): 2 = 128B, 4 = 64B, 6 = 32B swizzle.
+__device__ __forceinline__ uint64_t sdesc_mn(uint32_t saddr, uint32_t row_bytes, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)(((8u * row_bytes) >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)(row_bytes == 128 ? 2u : row_bytes == 64 ? 4u : 6u) << 61;
+    return d;
+}
+// Instruction-descriptor bit that marks B as MN-major ("transpose B").
+constexpr uint32_t kIdescBMnMajor = 1u << 16;
 
 // Instruction descriptor for kind::i8: s8 x s8 -> s32, both operands K-major.
 __host__ __device__ constexpr uint32_t idesc_s8s8s32(int M, int N) {

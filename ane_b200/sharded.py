@@ -135,7 +135,8 @@ class ShardedDense:
         self.partials = torch.empty(int(ane.lib.ane_absmax_partials_count(M * K, K * N_local)),
                                     dtype=torch.float32, device=device)
         self.Aq = torch.empty((M, K16), dtype=torch.int8, device=device)
-        self.Bt = torch.empty((N_local, K16), dtype=torch.int8, device=device)
+        # codes of this rank's B block in B's layout (K16 rows of N16 bytes)
+        self.Bq = torch.empty((K16, (N_local + 15) // 16 * 16), dtype=torch.int8, device=device)
         self.scales = torch.empty(2, dtype=torch.float32, device=device)
         self.C_local = torch.empty((M, N_local), dtype=torch.float32, device=device)
         self.gathered = torch.empty((world, M, N_local), dtype=torch.float32, device=device)
@@ -165,7 +166,7 @@ class ShardedDense:
             self._slots = self.fused.ptrs[rank] + c_bytes + 256
             self._xctl = self.fused.ptrs[rank] + c_bytes + 512
             K16 = (K + 15) // 16 * 16
-            self._coop = (K % 16 == 0 and N_local % 4 == 0 and M * K >= (1 << 22) and K * N_local >= (1 << 22)
+            self._coop = (K % 16 == 0 and N_local % 16 == 0 and M * K >= (1 << 22) and K * N_local >= (1 << 22)
                           and K16 == K)
             self._rank = rank
             self.C_gathered = self.fused.tensor[:c_bytes].view(torch.float32).view(*shape)
@@ -189,16 +190,16 @@ class ShardedDense:
                 # with the peers through tagged words (also the handshake)
                 ane.check(ane.lib.ane_quantize_pair_xrank_dev(
                     self.M, self.N_local, self.K, A.data_ptr(), B_local.data_ptr(), self.Aq.data_ptr(),
-                    self.Bt.data_ptr(), self.scales.data_ptr(), self.partials.data_ptr(), self.world, self._rank,
+                    self.Bq.data_ptr(), self.scales.data_ptr(), self.partials.data_ptr(), self.world, self._rank,
                     self._slot_peer, self._slots, self._xctl, ane._stream_ptr()))
             else:
                 absmax2 = global_absmax(self._absmax2(A, B_local), self.group)
                 ane.check(ane.lib.ane_quantize_pair_absmax_dev(self.M, self.N_local, self.K, A.data_ptr(),
                                                                B_local.data_ptr(), self.Aq.data_ptr(),
-                                                               self.Bt.data_ptr(), absmax2.data_ptr(),
+                                                               self.Bq.data_ptr(), absmax2.data_ptr(),
                                                                self.scales.data_ptr(), ane._stream_ptr()))
             ane.check(ane.lib.ane_gemm_s8_gather_dev(self.M, self.N_local, self.Aq.shape[1], self.Aq.data_ptr(),
-                                                     self.Bt.data_ptr(), self.scales.data_ptr(), float(scale),
+                                                     self.Bq.data_ptr(), self.scales.data_ptr(), float(scale),
                                                      int(bool(relu)), self.world, self._rank, self._c_ranks,
                                                      self.ldc, self._ctr_ranks, self._epoch, ane._stream_ptr()))
             return self.C_gathered
@@ -206,9 +207,9 @@ class ShardedDense:
         def quantize_gemm(A, B_local, absmax2):
             ane.check(ane.lib.ane_quantize_pair_absmax_dev(self.M, self.N_local, self.K, A.data_ptr(),
                                                            B_local.data_ptr(), self.Aq.data_ptr(),
-                                                           self.Bt.data_ptr(), absmax2.data_ptr(),
+                                                           self.Bq.data_ptr(), absmax2.data_ptr(),
                                                            self.scales.data_ptr(), ane._stream_ptr()))
-            return ane.gemm_s8(self.Aq, self.Bt, self.scales, scale, relu, out=self.C_local)
+            return ane.gemm_s8_kn(self.Aq, self.Bq, self.N_local, self.scales, scale, relu, out=self.C_local)
 
         return self.plan.run(A, B_local, self._absmax2, quantize_gemm, gather, self.gathered)
 

@@ -160,24 +160,33 @@ int ane_dense_fused_i8_dev(uint32_t M, uint32_t N, uint32_t K, float scale, uint
                            size_t workspace_bytes, void* stream);
 /* Quantize-only stages of dense_fused_i8 (for staged timing and tests):
  * Aq = M x K16 int8 (row stride K16 = ceil(K/16)*16, pad columns zero),
- * Bt = N x K16 int8 (B quantized AND transposed, pad zero), scales[0]=sa,
- * scales[1]=sb.  `partials` holds ane_absmax_partials_count(M*K, K*N) floats. */
+ * Bq = the codes of B in B's own layout, K rows of N16 = ceil(N/16)*16 bytes
+ * (pad columns zero; allocate K16 rows: the GEMM reads rows up to K16, which
+ * meet Aq's zero pad columns), scales[0]=sa, scales[1]=sb.  `partials` holds
+ * ane_absmax_partials_count(M*K, K*N) floats. */
 size_t ane_absmax_partials_count(size_t count_a, size_t count_b);
 int ane_quantize_pair_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B,
-                          int8_t* Aq, int8_t* Bt, float* scales, float* partials, void* stream);
+                          int8_t* Aq, int8_t* Bq, float* scales, float* partials, void* stream);
 /* Multi-GPU building blocks (N-sharded dense_fused_i8): absmax of both tensors
  * into device absmax2[2] (reduce across ranks with MAX, then quantize with the
  * global values, so every shard uses the single-GPU scales). */
 int ane_absmax_pair_dev(const float* A, size_t count_a, const float* B, size_t count_b, float* absmax2,
                         float* partials, void* stream);
 int ane_quantize_pair_absmax_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
-                                 int8_t* Bt, const float* absmax2, float* scales, void* stream);
+                                 int8_t* Bq, const float* absmax2, float* scales, void* stream);
 /* int8 tensor-core GEMM with the dense_fused_i8 epilogue, operands resident:
  * Aq M x K16 (K-major), Bt N x K16 (K-major), scales device float[2].
  * out_mode 0: fp32 C = relu?(float(acc)*(s0*s1)*scale);  1: raw int32 acc. */
 int ane_gemm_s8_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* Aq, const int8_t* Bt,
                     const float* scales, float scale, uint8_t relu, int out_mode, void* C,
                     void* stream);
+/* The same GEMM with B as dense_fused_i8's prologue leaves it: Bq = codes of B
+ * stored K x N, row stride ldb bytes (a multiple of 16, >= N), K16 rows
+ * readable (rows past the true K meet Aq's zero pad columns).  The tensor
+ * cores read Bq as an MN-major operand, so B is never transposed.  No
+ * counterpart in the reference (its B operand is the packed panel layout). */
+int ane_gemm_s8_kn_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* Aq, const int8_t* Bq, uint32_t ldb,
+                       const float* scales, float scale, uint8_t relu, int out_mode, void* C, void* stream);
 int ane_quantize_fp32_i8_dev(uint32_t count, const float* src, int8_t* dst, float* scale_out,
                              void* stream);
 int ane_pack_b_i8_dev(uint32_t K, uint32_t N, const int8_t* src, int8_t* dst, void* stream);
@@ -300,13 +309,13 @@ void ane_q8_stack_plan_free(void* plan);
  * ctl = this GPU's 2 control words.  Exchange area and ctl start zeroed and
  * are never reset; every rank makes the same calls.  The exchange also acts as
  * the call's entry handshake (a rank leaves it only after all ranks entered).
- * Needs K % 16 == 0, N % 4 == 0, 16-byte aligned A, B, Aq, Bt, and
- * M*K, K*N >= 2^22 (else ANE_ERR_INVALID_ARGUMENT).  Aq is M x K, Bt N x K.
+ * Needs K % 16 == 0, N % 16 == 0, 16-byte aligned A, B, Aq, Bq, and
+ * M*K, K*N >= 2^22 (else ANE_ERR_INVALID_ARGUMENT).  Aq is M x K, Bq K x N.
  * No counterpart in the reference. */
 int ane_quantize_pair_xrank_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
-                                int8_t* Bt, float* scales, float* partials, uint32_t world, uint32_t rank,
+                                int8_t* Bq, float* scales, float* partials, uint32_t world, uint32_t rank,
                                 void* const* slot_peer, const void* slots, uint32_t* ctl, void* stream);
-/* int8 GEMM (as ane_gemm_s8_dev, out_mode 0) fused with an all-gather of C over
+/* int8 GEMM (as ane_gemm_s8_kn_dev with ldb = N16, out_mode 0) fused with an all-gather of C over
  * `world` GPUs: every C tile is stored into each rank's gathered output from the
  * epilogue (C_ranks[q] = rank q's buffer at this rank's first element, row
  * stride ldc floats; CUDA-IPC peer pointers, C_ranks[rank] local), then every
@@ -316,7 +325,7 @@ int ane_quantize_pair_xrank_dev(uint32_t M, uint32_t N, uint32_t K, const float*
  * calls.  A stream-ordered collective before the call (the absmax all-reduce
  * of the sharded dense_fused_i8) must separate it from the previous call's
  * readers.  No counterpart in the reference. */
-int ane_gemm_s8_gather_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* Aq, const int8_t* Bt,
+int ane_gemm_s8_gather_dev(uint32_t M, uint32_t N, uint32_t K16, const int8_t* Aq, const int8_t* Bq,
                            const float* scales, float scale, uint8_t relu, uint32_t world, uint32_t rank,
                            void* const* C_ranks, uint32_t ldc, uint32_t* const* ctr_ranks, uint32_t* epoch,
                            void* stream);

@@ -68,15 +68,15 @@ def check_dense_fused(ane, torch, A, B, C, scale, relu, parts=None, check_stages
     M, K = Aq_r.shape
     N = Bq_r.shape[1]
     if check_stages:
-        Aq, Bt, scales = ane.quantize_pair(A, B)
-        acc = ane.gemm_s8(Aq, Bt, scales, raw_i32=True)
+        Aq, Bq, scales = ane.quantize_pair(A, B)
+        acc = ane.gemm_s8_kn(Aq, Bq, N, scales, raw_i32=True)
         torch.cuda.synchronize()
         s = scales.cpu().numpy()
         assert s[0] == sa and s[1] == sb, (s, sa, sb)
         assert np.array_equal(Aq.cpu().numpy()[:, :K], Aq_r)
-        assert np.array_equal(Bt.cpu().numpy()[:N, :K], Bq_r.T)
+        assert np.array_equal(Bq.cpu().numpy()[:K, :N], Bq_r)
         assert np.array_equal(acc.cpu().numpy(), acc_r)
-        del Aq, Bt, acc
+        del Aq, Bq, acc
     Cn = C.cpu().numpy()
     assert bits_equal(Cn, C_r)
     ref = C_r.astype(np.float64)

@@ -23,19 +23,19 @@ def _setup(torch, ane, dev, M=512, N=512, K=512):
     g = torch.Generator(device=dev).manual_seed(7)
     A = torch.randn((M, K), device=dev, generator=g)
     B = torch.randn((K, N), device=dev, generator=g)
-    Aq, Bt, scales = ane.quantize_pair(A, B)
+    Aq, Bq, scales = ane.quantize_pair(A, B)
     ref = ane.dense_fused_i8(A, B, 1.0, False)
-    return Aq, Bt, scales, ref
+    return Aq, Bq, scales, ref
 
 
-def _gather(ane, torch, Aq, Bt, scales, C_ranks, ctr_ranks, epoch):
+def _gather(ane, torch, Aq, Bq, scales, C_ranks, ctr_ranks, epoch):
     import ctypes
 
     M, K16 = Aq.shape
-    N = Bt.shape[0]
+    N = C_ranks[0].shape[1]
     c_arr = (ctypes.c_void_p * 2)(*[c.data_ptr() for c in C_ranks])
     k_arr = (ctypes.c_void_p * 2)(*[c.data_ptr() for c in ctr_ranks])
-    return ane.lib.ane_gemm_s8_gather_dev(M, N, K16, Aq.data_ptr(), Bt.data_ptr(), scales.data_ptr(), 1.0, 0, 2, 0,
+    return ane.lib.ane_gemm_s8_gather_dev(M, N, K16, Aq.data_ptr(), Bq.data_ptr(), scales.data_ptr(), 1.0, 0, 2, 0,
                                           c_arr, N, k_arr, epoch.data_ptr(), ane._stream_ptr())
 
 
@@ -46,13 +46,13 @@ def test_gather_wait_times_out_when_a_rank_never_arrives():
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    Aq, Bt, scales, ref = _setup(torch, ane, dev)
+    Aq, Bq, scales, ref = _setup(torch, ane, dev)
     assert ane.lib.ane_device_timeouts() == 0
     C0, C1 = torch.zeros_like(ref), torch.zeros_like(ref)
     ctr0 = torch.zeros(1, dtype=torch.int32, device=dev)
     ctr1 = torch.zeros(1, dtype=torch.int32, device=dev)
     epoch = torch.zeros(1, dtype=torch.int32, device=dev)
-    ane.check(_gather(ane, torch, Aq, Bt, scales, [C0, C1], [ctr0, ctr1], epoch))
+    ane.check(_gather(ane, torch, Aq, Bq, scales, [C0, C1], [ctr0, ctr1], epoch))
     torch.cuda.synchronize()  # returns after the bounded wait gave up (about 2 s)
     assert ane.lib.ane_device_timeouts() == 1
     assert ane.lib.ane_device_timeouts() == 0  # read and reset
@@ -72,12 +72,12 @@ def test_gather_wait_completes_when_every_rank_arrives():
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    Aq, Bt, scales, ref = _setup(torch, ane, dev)
+    Aq, Bq, scales, ref = _setup(torch, ane, dev)
     C0, C1 = torch.zeros_like(ref), torch.zeros_like(ref)
     ctr = torch.zeros(1, dtype=torch.int32, device=dev)
     epoch = torch.zeros(1, dtype=torch.int32, device=dev)
     for step in range(3):  # counters only grow; each call waits for its own arrivals
-        ane.check(_gather(ane, torch, Aq, Bt, scales, [C0, C1], [ctr, ctr], epoch))
+        ane.check(_gather(ane, torch, Aq, Bq, scales, [C0, C1], [ctr, ctr], epoch))
         torch.cuda.synchronize()
         assert ane.lib.ane_device_timeouts() == 0
         assert int(epoch.item()) == step + 1

@@ -193,6 +193,55 @@ def test_gemm_s8_tail_split_exact(ane, M, N, K):
     assert torch.equal(acc, ref)
 
 
+def _kn_operands(torch, M, N, K, seed, pad_rows_garbage=True):
+    """Random int8 Aq [M x K16] (zero pad columns) and Bq [K16 x N16] in the
+    layout dense_fused_i8's prologue writes.  Bq's rows K..K16 are filled with
+    nonzero codes: the GEMM must cancel them through Aq's zero pad columns."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    K16, N16 = (K + 15) // 16 * 16, (N + 15) // 16 * 16
+    Aq = torch.randint(-127, 128, (M, K16), generator=g, device="cuda", dtype=torch.int8)
+    Aq[:, K:] = 0
+    Bq = torch.randint(-127, 128, (K16, N16), generator=g, device="cuda", dtype=torch.int8)
+    if not pad_rows_garbage:
+        Bq[K:] = 0
+    return Aq, Bq
+
+
+@pytest.mark.parametrize("M,N,K", [
+    (4096, 4096, 256),   # pair kernel, 256 tiles on 74 pairs: the last 34 cut in 2 (64-column halves, SWIZZLE_64B)
+    (1000, 1000, 256),   # every tile cut in 4: 32-column halves (SWIZZLE_32B), ragged N
+    (4096, 1104, 512),   # 80 tiles: last 6 cut in 4, parts past N
+    (3000, 2000, 392),   # ragged M, K % 128 != 0 (last K block partly outside Bq)
+    (512, 512, 4096),    # pair kernel, whole tiles only
+    (128, 256, 128),     # single-CTA kernel (M <= 128): two 128-column atoms per B stage
+    (7, 10, 48),         # single-CTA kernel, N inside one atom, K16 pad rows
+    (64, 14336, 4096),   # config 4 shape (single-CTA kernel)
+])
+def test_gemm_s8_kn_int32_exact(ane, M, N, K):
+    """The GEMM with B stored K x N (MN-major tcgen05 operand, the layout the
+    dense_fused_i8 prologue writes): raw int32 accumulators exact against an
+    fp64 product, for every tile width the kernels use."""
+    import torch
+
+    Aq, Bq = _kn_operands(torch, M, N, K, M * 5 + N * 3 + K)
+    acc = ane.gemm_s8_kn(Aq, Bq, N, raw_i32=True)
+    K16 = Aq.shape[1]
+    ref = (Aq.double() @ Bq[:K16, :N].double()).to(torch.int32)
+    assert torch.equal(acc, ref)
+
+
+def test_gemm_s8_kn_equals_kmajor(ane):
+    """The same codes through both B layouts give the same fp32 C, bit for bit."""
+    import torch
+
+    M, N, K = 1024, 768, 1040
+    Aq, Bq = _kn_operands(torch, M, N, K, 99, pad_rows_garbage=False)
+    scales = torch.tensor([0.0123, 0.0456], device="cuda")
+    c_kn = ane.gemm_s8_kn(Aq, Bq, N, scales, scale=0.5, relu=True)
+    c_km = ane.gemm_s8(Aq, Bq[:, :N].t().contiguous(), scales, scale=0.5, relu=True)
+    assert torch.equal(c_kn.view(torch.int32), c_km.view(torch.int32))
+
+
 def test_gemm_s8_extreme_values(ane):
     """All -127 / +127 operands: the largest |acc| K allows, exact."""
     import torch
@@ -231,7 +280,7 @@ def test_dense_fused_i8_host_entry(ane, M, N, K, scale, relu):
 
 
 def test_dense_fused_i8_stages_bit_exact(ane):
-    """Aq, Bt, both scales and the int32 accumulators, each against the oracle."""
+    """Aq, Bq, both scales and the int32 accumulators, each against the oracle."""
     import torch
 
     M, N, K = 300, 520, 784
@@ -239,24 +288,24 @@ def test_dense_fused_i8_stages_bit_exact(ane):
     A = rng.random((M, K)).astype(F32)                      # MNIST-like U[0,1)
     B = (rng.standard_normal((K, N)) * np.sqrt(2 / K)).astype(F32)
     C, Aq_r, Bq_r, acc_r, sa_r, sb_r = oracle.dense_fused_i8(A, B, 1.0, True, full=True)
-    Aq, Bt, scales = ane.quantize_pair(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
+    Aq, Bq, scales = ane.quantize_pair(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
     K16 = Aq.shape[1]
     s = scales.cpu().numpy()
     assert s[0] == sa_r and s[1] == sb_r
-    Aqn, Btn = Aq.cpu().numpy(), Bt.cpu().numpy()
+    Aqn, Bqn = Aq.cpu().numpy(), Bq.cpu().numpy()
     assert np.array_equal(Aqn[:, :K], Aq_r) and not Aqn[:, K:].any()
-    assert np.array_equal(Btn[:, :K], Bq_r.T) and not Btn[:, K:].any()
-    acc = ane.gemm_s8(Aq, Bt, raw_i32=True).cpu().numpy()
+    assert np.array_equal(Bqn[:K, :N], Bq_r) and not Bqn[:K, N:].any()
+    acc = ane.gemm_s8_kn(Aq, Bq, N, raw_i32=True).cpu().numpy()
     assert np.array_equal(acc, acc_r)
-    Cg = ane.gemm_s8(Aq, Bt, scales, scale=1.0, relu=True).cpu().numpy()
+    Cg = ane.gemm_s8_kn(Aq, Bq, N, scales, scale=1.0, relu=True).cpu().numpy()
     assert bits_equal(Cg, C)
     assert K16 % 16 == 0
 
 
 @pytest.mark.parametrize("M,N,K", [
-    (1024, 1028, 4096),   # cooperative prologue, N % 256 != 0: B codes read with plain loads
-    (1024, 1280, 4112),   # cooperative prologue with TMA refills: last column unit half outside N,
-                          # last row unit 16 rows (the boxes' zero fill)
+    (1024, 1040, 4096),   # cooperative prologue, N % 256 != 0 (ragged last B chunk rows)
+    (1024, 1280, 4112),   # cooperative prologue, K % 128 != 0 (the GEMM's last K block partly outside)
+    (1024, 1028, 4096),   # N % 16 != 0: the staged prologue (B codes with 16-byte padded rows)
 ])
 def test_dense_fused_i8_coop_prologue_edges(ane, M, N, K):
     """Shapes the one-launch cooperative prologue takes (M*K, K*N >= 2^22),
@@ -267,15 +316,15 @@ def test_dense_fused_i8_coop_prologue_edges(ane, M, N, K):
     A = rng.standard_normal((M, K)).astype(F32)
     B = rng.standard_normal((K, N)).astype(F32)
     Ad, Bd = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
-    Aq, Bt, scales = ane.quantize_pair(Ad, Bd)
+    Aq, Bq, scales = ane.quantize_pair(Ad, Bd)
     C = ane.dense_fused_i8(Ad, Bd, 0.75, True)
     torch.cuda.synchronize()
     C_r, Aq_r, Bq_r, _, sa, sb = oracle.dense_fused_i8(A, B, 0.75, True, full=True)
     s = scales.cpu().numpy()
     assert s[0] == sa and s[1] == sb
-    Aqn, Btn = Aq.cpu().numpy(), Bt.cpu().numpy()
+    Aqn, Bqn = Aq.cpu().numpy(), Bq.cpu().numpy()
     assert np.array_equal(Aqn[:, :K], Aq_r)
-    assert np.array_equal(Btn[:N, :K], Bq_r.T)
+    assert np.array_equal(Bqn[:K, :N], Bq_r) and not Bqn[:K, N:].any()
     assert bits_equal(C.cpu().numpy(), C_r)
 
 
@@ -481,14 +530,15 @@ def test_q8_chain_in_cuda_graph(ane):
 
 # ------------------------------------- cooperative single-read quantize prologue
 @pytest.mark.parametrize("M,N,K,special", [
-    (2048, 2052, 2048, None),       # smallest shapes that take the cooperative prologue
-    (4100, 1024, 4096, "inf"),      # ragged per-CTA slices; +-inf in A
+    (2048, 2064, 2048, None),       # smallest shapes that take the cooperative prologue (all chunks resident)
+    (4100, 1024, 4096, "inf"),      # ragged last chunk of A; +-inf in A (general quantize rule)
     (1024, 4096, 4112, "nan"),      # K not a multiple of 64; NaN in B
-    (1024, 2052, 8192, None),       # N % 256 != 0 with remainder units of B (read from L2 directly)
+    (1024, 2064, 8192, None),       # remainder chunks of B read back from L2
     (8192, 4096, 1024, "nanA"),     # NaN in a remainder chunk of A (the last rows)
+    (4096, 4096, 4096, "zeroB"),    # the benchmark shape; B all zero (absmax 0: scale 1)
 ])
 def test_quantize_prologue_single_read(ane, M, N, K, special):
-    """Aq, Bt and both scales from the one-kernel prologue, each bit-exact."""
+    """Aq, Bq and both scales from the one-kernel prologue, each bit-exact."""
     import torch
 
     rng = np.random.default_rng(M + 3 * N + 7 * K)
@@ -501,13 +551,15 @@ def test_quantize_prologue_single_read(ane, M, N, K, special):
         B[K // 2, N - 3] = np.nan
     if special == "nanA":
         A[M - 1, K - 2] = np.nan
-    Aq, Bt, scales = ane.quantize_pair(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
+    if special == "zeroB":
+        B[:] = 0.0
+    Aq, Bq, scales = ane.quantize_pair(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
     qa, sa = oracle.quantize_fp32_i8(A)
     qb, sb = oracle.quantize_fp32_i8(B)
     s = scales.cpu().numpy()
     assert bits_equal(s, np.array([sa, sb], F32))
     assert np.array_equal(Aq.cpu().numpy(), qa.reshape(M, K))
-    assert np.array_equal(Bt.cpu().numpy(), qb.reshape(K, N).T)
+    assert np.array_equal(Bq.cpu().numpy()[:K, :N], qb.reshape(K, N))
 
 
 # ----------------------------------- ggml MUL_MAT: activation quantized in-kernel
