@@ -393,7 +393,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const Flat fa = make_flat(A, Aq, (size_t)M * K, c, G);
     const Flat fb = make_flat(B, Bq, (size_t)K * N, c, G);
     if (threadIdx.x == 0) {
-        tag_s = xr.world > 1 ? *reinterpret_cast<volatile uint32_t*>(xr.ctl) + 1u : 0u;
         fail_s = 0;
         for (uint32_t i = 0; i < kStages; i++) {
             ptx::mbar_init(&full[i], 1);                  // the producer's arrive (+ the copy's bytes)
@@ -401,6 +400,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::fence_mbarrier_init();
     }
+    // Programmatic dependent launch: the next kernel (the GEMM) may be scheduled
+    // now -- its CTAs take an SM only when a CTA of this grid leaves it -- and
+    // this grid's set-up above overlapped the previous kernel; nothing in global
+    // memory is touched before that kernel has finished.
+    ptx::griddep_launch_dependents();
+    ptx::griddep_wait();
+    if (threadIdx.x == 0) tag_s = xr.world > 1 ? *reinterpret_cast<volatile uint32_t*>(xr.ctl) + 1u : 0u;
     __syncthreads();
 
     if (threadIdx.x >= kConsumers) {
@@ -610,11 +616,13 @@ int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, con
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = kCoopSmem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident: the grid barrier cannot wait on an unscheduled CTA
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     ANE_CUDA_TRY(cudaLaunchKernelEx(&cfg, prologue_coop_kernel, A, B, Aq, Bq, M, N, K, scales, xr, slot,
                                     device_timeout_flag()));
     ANE_CHECK_LAUNCH();
