@@ -43,9 +43,10 @@ sys.path.insert(0, ROOT)
 METRIC = "int8 GEMM TOPS (4096³) & Q8_0 matvec GB/s at 1/2/4/8 B200"
 M = N = K = 4096
 SCALE, RELU = 1.0, False
-# DRAM read + write of one gemm_s8_pair_kernel launch at 4096^3 (ncu,
-# dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel).
-GEMM_TRAFFIC_BYTES = 33_807_616 + 17_284_352
+# DRAM read + write of one gemm_s8_pair_kernel launch at 4096^3 (B read as an
+# MN-major operand): ncu dram__bytes_read.sum + dram__bytes_write.sum of one
+# launch of this kernel.
+GEMM_TRAFFIC_BYTES = 34_032_640 + 16_945_408
 
 
 def parse():
