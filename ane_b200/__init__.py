@@ -106,6 +106,10 @@ SIGNATURES = {
     "ane_q8_0_gemv_q8_ex_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _u32, _vp]),
     "ane_mul_mat_q8_0_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp, _u32, _vp]),
     "ane_mul_mat_q8_0_batch_workspace_size": (_sz, [_u32, _u32]),
+    "ane_mul_mat_q8_0_ctas": (_u32, [_u32, _u32]),
+    "ane_mul_mat_q8_0_gather_dev": (_i32, [_u32, _u32, _vp, _vp, _u32, _vp, _vp, _u32, _u32, _u32, _vp, _u32, _u32,
+                                           _u32, _vp]),
+    "ane_q8_chain_token_end_dev": (_i32, [_vp, _u32, _u32, _vp, _vp]),
     "ane_mul_mat_q8_0_batch_dev": (_i32, [_u32, _u32, _u32, _vp, _sz, _vp, _vp, _sz, _vp, _u32, _vp]),
     "ane_q8_stack_plan_create": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp]),
     "ane_q8_stack_run": (_i32, [_vp, _vp]),

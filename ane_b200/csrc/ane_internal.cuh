@@ -279,6 +279,33 @@ int launch_softmax_argmax_f32(uint32_t batch, uint32_t cols, const float* logits
                               const uint8_t* labels, float* g_out, int32_t* argmax, cudaStream_t s);
 int launch_mul_mat_q8_0(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, int32_t* block_dots,
                         uint32_t flags, cudaStream_t s);
+// A row-sharded chain of MUL_MATs (the decode stack on `world` GPUs) with the
+// all-gather fused into each matvec (q8_0_gemv_q8.cu).  Vectors are TAGGED:
+// element i is one 8-byte word {fp32 value, u32 tag}, written by one store, so
+// a reader that sees the expected tag has the value -- no fence, flag or
+// counter.  Projection j of token t writes tag t*nproj + j + 1 into every
+// rank's vector (out[q] = rank q's vector at this rank's first row; CUDA-IPC
+// peer pointers) and reads tag t*nproj + j from this GPU's copy of the
+// previous projection's vector `prev`: its input x (x_from_prev) and, always,
+// one guard word per (rank, CTA) of that projection (the CTA's first row,
+// stored after the CTA read its own input), so no rank overwrites a vector
+// another rank still reads.
+struct Q8ChainGather {
+    uint32_t world;
+    uint64_t* out[8];
+    const uint64_t* prev;      // this GPU's vector of the previous projection (all ranks' rows)
+    uint32_t x_from_prev;      // 1: x = prev[0..K); 0: x is the fp32 input
+    uint32_t prev_rows, prev_groups, prev_ctas;  // the previous projection's per-rank split
+    const uint32_t* tok;       // this GPU's count of finished tokens
+    uint32_t nproj, j;         // projections per token, this projection
+};
+int launch_mul_mat_q8_0_gather(uint32_t M, uint32_t K, const float* x, const uint8_t* W, const Q8ChainGather& g,
+                               uint32_t flags, cudaStream_t s);
+uint32_t mul_mat_q8_0_ctas(uint32_t M, uint32_t K);
+// Ends a token of such a chain: waits (bounded) until every word of the last
+// projection's vector (`len` words, this GPU's copy) carries that projection's
+// tag, then bumps *tok.
+int launch_q8_chain_token_end(const uint64_t* last, uint32_t len, uint32_t nproj, uint32_t* tok, cudaStream_t s);
 // ggml MUL_MAT for NT <= 16 activation rows (q8_0_gemm_q8.cu); the workspace
 // (mul_mat_q8_0_batch_workspace_size bytes, 256-byte aligned) receives the
 // quantized activation.

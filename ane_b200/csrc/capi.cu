@@ -573,6 +573,42 @@ int ane_mul_mat_q8_0_dev(uint32_t M, uint32_t K, const float* x, const void* W, 
     return rc ? rc : ok();
 }
 
+uint32_t ane_mul_mat_q8_0_ctas(uint32_t rows_local, uint32_t K) {
+    if (require_sm100()) return 0;
+    return mul_mat_q8_0_ctas(rows_local, K);
+}
+
+int ane_mul_mat_q8_0_gather_dev(uint32_t rows_local, uint32_t K, const float* x, const void* W, uint32_t world,
+                                void* const* out_ranks, const void* prev, uint32_t x_from_prev, uint32_t prev_rows,
+                                uint32_t prev_ctas, const uint32_t* tok, uint32_t nproj, uint32_t j, uint32_t flags,
+                                void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK((flags & ~ANE_Q8_WEIGHTS_STATIC) == 0, "mul_mat_q8_0_gather: unknown flag bits");
+    ANE_ARG_CHECK(world >= 1 && world <= 8 && out_ranks, "mul_mat_q8_0_gather: world must be 1..8");
+    Q8ChainGather g{};
+    g.world = world;
+    for (uint32_t q = 0; q < world; q++) g.out[q] = static_cast<uint64_t*>(out_ranks[q]);
+    g.prev = static_cast<const uint64_t*>(prev);
+    g.x_from_prev = x_from_prev ? 1u : 0u;
+    g.prev_rows = prev_rows;
+    g.prev_groups = (prev_rows + 3) / 4;
+    g.prev_ctas = prev_ctas;
+    g.tok = tok;
+    g.nproj = nproj;
+    g.j = j;
+    int rc = launch_mul_mat_q8_0_gather(rows_local, K, x, static_cast<const uint8_t*>(W), g, flags,
+                                        static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+int ane_q8_chain_token_end_dev(const void* last, uint32_t len, uint32_t nproj, uint32_t* tok, void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(last && tok && nproj > 0, "q8_chain_token_end: bad arguments");
+    int rc = launch_q8_chain_token_end(static_cast<const uint64_t*>(last), len, nproj, tok,
+                                       static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
 size_t ane_mul_mat_q8_0_batch_workspace_size(uint32_t M, uint32_t K) {
     return mul_mat_q8_0_batch_workspace_size(M, K);
 }

@@ -72,14 +72,56 @@ __global__ void quantize_q8_0_kernel(const float* __restrict__ x, uint8_t* __res
 // when the kernel quantizes the activation itself (XF32).
 __host__ __device__ constexpr uint32_t x_raw_bytes(bool xf32, uint32_t K) { return xf32 ? K * 4 : K / 32 * 34; }
 
+// Tagged words: one 64-bit access each (value low, tag high), so a reader never
+// sees a half-written word, even from a peer GPU over NVLink.
+__device__ __forceinline__ uint64_t ld_tagged(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_tagged(uint64_t* p, float value, uint32_t tag) {
+    const uint64_t w = (uint64_t)__float_as_uint(value) | ((uint64_t)tag << 32);
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint4 ld_tagged2(const uint64_t* p) {
+    uint64_t a, b;
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+    return make_uint4((uint32_t)a, (uint32_t)(a >> 32), (uint32_t)b, (uint32_t)(b >> 32));
+}
+// Bounded wait until *p carries `tag`; returns the word's value (or false on timeout).
+__device__ bool wait_tagged(const uint64_t* p, uint32_t tag, float* value, int* err) {
+    uint64_t w = ld_tagged(p);
+    if ((uint32_t)(w >> 32) != tag) {
+        const long long t0 = clock64();
+        while (true) {
+            __nanosleep(32);
+            w = ld_tagged(p);
+            if ((uint32_t)(w >> 32) == tag) break;
+            if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
+                atomicAdd(err, 1);
+                return false;
+            }
+        }
+    }
+    *value = __uint_as_float((uint32_t)w);
+    return true;
+}
+
 // XF32 = false: xq holds K/32 Q8_0 blocks.  XF32 = true: xq holds fp32 x[K] and
 // every CTA quantizes it with the ggml rule (the quantize_q8_0_kernel
 // arithmetic above, block by block) into the same shared-memory codes + scales,
 // so the result equals quantize_q8_0 followed by the XF32 = false kernel.
-template <bool XF32>
-__global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ xq,
+// GATHER (with XF32): one projection of a row-sharded chain (Q8ChainGather,
+// tagged vectors): the compute warps fill x themselves -- from the previous
+// projection's tagged vector, or the fp32 input -- after the guard words of the
+// previous projection carry its tag, and the rows go to every rank's vector as
+// tagged words.  The producer streams weights only, so the weight tiles of the
+// first ring stages load while the compute warps wait for their input.
+template <bool XF32, bool GATHER>
+__global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1)) q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ xq,
                                     float* __restrict__ out, int32_t* __restrict__ block_dots, uint32_t M, uint32_t K,
-                                    uint32_t groups, uint32_t nw, uint32_t nslots, uint32_t flags, int* err) {
+                                    uint32_t groups, uint32_t nw, uint32_t nslots, uint32_t flags, int* err,
+                                    const __grid_constant__ Q8ChainGather pg) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t nb = K / 32, nchunks = (nb + kQ8ChunkBlocks - 1) / kQ8ChunkBlocks;
     const uint32_t slot_bytes = nw * kQ8WarpTileBytes;
@@ -124,8 +166,10 @@ __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, co
             const uint32_t pre = (flags & ANE_Q8_WEIGHTS_STATIC) ? min(nslots, ntiles) : 0;
             for (uint32_t t = 0; t < pre; t++) issue_weights(t, t);
             ptx::griddep_wait();  // xq may be written by the previous kernel
-            ptx::mbar_arrive_expect_tx(xbar, xbytes);
-            ptx::bulk_load(xraw, xq, xbytes, xbar);
+            if constexpr (!GATHER) {  // (with GATHER the compute warps fill x)
+                ptx::mbar_arrive_expect_tx(xbar, xbytes);
+                ptx::bulk_load(xraw, xq, xbytes, xbar);
+            }
             for (uint32_t t = pre; t < ntiles; t++) {
                 const uint32_t slot = t % nslots;
                 if (!ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err)) break;
@@ -135,9 +179,79 @@ __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, co
         return;
     }
     // ------------------------------------------------------------ compute
+    // the token count: only the token-end kernel writes it, which precedes
+    // projection 0 of a token, so later projections read it before the wait
+    uint32_t tok_early = 0;
+    if constexpr (GATHER) {
+        if (pg.j != 0) tok_early = *reinterpret_cast<const volatile uint32_t*>(pg.tok);
+    }
     ptx::griddep_wait();  // out / block_dots may belong to the previous kernel
     const uint32_t cw = warp - 1;
-    bool alive = __all_sync(0xffffffffu, ptx::mbar_wait(xbar, 0, err));  // one verdict per warp
+    uint32_t tag_out = 0;
+    bool alive = true;
+    if constexpr (GATHER) {
+        // Every compute thread takes a share of the guard words and of x's word
+        // pairs; one round issues kXU loads per thread back to back, then checks
+        // their tags, and polls (bounded) only the words not there yet.
+        // Cross-GPU waits only: the previous kernel on this GPU has finished.
+        const uint32_t tokv = pg.j != 0 ? tok_early : *reinterpret_cast<const volatile uint32_t*>(pg.tok);
+        const uint32_t tag_in = tokv * pg.nproj + pg.j;
+        tag_out = tag_in + 1u;
+        const uint32_t tid = cw * 32 + lane, nthr = nw * 32;
+        const uint32_t nguard = pg.world * pg.prev_ctas;
+        const uint32_t npairs = pg.x_from_prev ? K / 2 : 0;
+        float* xf = reinterpret_cast<float*>(xraw);
+        bool ok = true;
+        float v;
+        constexpr uint32_t kXU = 8;
+        for (uint32_t base = tid; base < nguard + npairs && ok; base += nthr * kXU) {
+            uint4 w[kXU];
+#pragma unroll
+            for (uint32_t u = 0; u < kXU; u++) {
+                const uint32_t i = base + u * nthr;
+                if (i < nguard) {
+                    const uint32_t r = i / pg.prev_ctas, c = i - r * pg.prev_ctas;
+                    const uint32_t g = (uint32_t)((uint64_t)pg.prev_groups * c / pg.prev_ctas);
+                    const uint64_t* p = pg.prev + (size_t)r * pg.prev_rows + g * kQ8RowsPerWarp;
+                    const uint64_t gw = ld_tagged(p);
+                    w[u] = make_uint4((uint32_t)gw, (uint32_t)(gw >> 32), 0u, tag_in);
+                } else if (i < nguard + npairs) {
+                    w[u] = ld_tagged2(pg.prev + 2 * (i - nguard));
+                }
+            }
+#pragma unroll
+            for (uint32_t u = 0; u < kXU; u++) {
+                const uint32_t i = base + u * nthr;
+                if (i < nguard) {
+                    if (w[u].y != tag_in) {
+                        const uint32_t r = i / pg.prev_ctas, c = i - r * pg.prev_ctas;
+                        const uint32_t g = (uint32_t)((uint64_t)pg.prev_groups * c / pg.prev_ctas);
+                        ok = ok && wait_tagged(pg.prev + (size_t)r * pg.prev_rows + g * kQ8RowsPerWarp, tag_in, &v,
+                                               err);
+                    }
+                } else if (i < nguard + npairs) {
+                    const uint32_t pi = i - nguard;
+                    if (w[u].y != tag_in) {
+                        ok = ok && wait_tagged(pg.prev + 2 * pi, tag_in, &v, err);
+                        w[u].x = __float_as_uint(v);
+                    }
+                    if (w[u].w != tag_in) {
+                        ok = ok && wait_tagged(pg.prev + 2 * pi + 1, tag_in, &v, err);
+                        w[u].z = __float_as_uint(v);
+                    }
+                    reinterpret_cast<float2*>(xf)[pi] = make_float2(__uint_as_float(w[u].x), __uint_as_float(w[u].z));
+                }
+            }
+        }
+        if (!pg.x_from_prev) {
+            const float4* x4 = reinterpret_cast<const float4*>(xq);
+            for (uint32_t i = tid; i < K / 4; i += nthr) reinterpret_cast<float4*>(xf)[i] = x4[i];
+        }
+        alive = __all_sync(0xffffffffu, ok);
+        ptx::named_barrier_sync(1, nw * 32);  // x complete in shared memory
+    } else {
+        alive = __all_sync(0xffffffffu, ptx::mbar_wait(xbar, 0, err));  // one verdict per warp
+    }
     if (alive && XF32) {  // quantize: one thread per 32-element block
         for (uint32_t b = cw * 32 + lane; b < nb; b += nw * 32)
             q8_quantize_block<false>(reinterpret_cast<const float*>(xraw) + (size_t)b * 32, xs, xd, b);
@@ -177,8 +291,31 @@ __global__ void q8_0_gemv_q8_kernel(const __grid_constant__ CUtensorMap wmap, co
             if (lane == 0) ptx::mbar_arrive(&empty[slot]);
         }
         sum = q8_row_total(sum);
-        if (active && alive && pp == 0) out[row] = sum;
+        if (active && alive && pp == 0) {
+            if constexpr (GATHER) {
+                for (uint32_t q = 0; q < pg.world; q++) st_tagged(pg.out[q] + row, sum, tag_out);
+            } else {
+                out[row] = sum;
+            }
+        }
     }
+}
+
+// Ends a token of a row-sharded chain: waits (bounded) until every word of the
+// last projection's vector on this GPU carries its tag (the gathered output is
+// complete here), then counts the token.  Launched in plain stream order: only
+// peers' words can still be missing.
+__global__ void q8_chain_token_end_kernel(const uint64_t* last, uint32_t len, uint32_t nproj, uint32_t* tok,
+                                          int* err) {
+    __shared__ uint32_t t_s;
+    if (threadIdx.x == 0) t_s = *reinterpret_cast<volatile uint32_t*>(tok);
+    __syncthreads();
+    const uint32_t tag = t_s * nproj + nproj;
+    float v;
+    bool ok = true;  // a timed-out wait is counted; the token still ends
+    for (uint32_t i = threadIdx.x; i < len && ok; i += blockDim.x) ok = wait_tagged(last + i, tag, &v, err);
+    __syncthreads();
+    if (threadIdx.x == 0) *tok = t_s + 1u;
 }
 
 }  // namespace
@@ -218,27 +355,35 @@ int launch_quantize_q8_0(uint32_t K, const float* x, uint8_t* out, cudaStream_t 
 }
 
 template <bool XF32>
+static Q8Plan gemv_q8_plan(uint32_t M, uint32_t K) {
+    const uint32_t nb = K / 32;
+    // barriers (256) + the raw activation + scales + aligned codes
+    const size_t fixed = 256 + round_up((size_t)x_raw_bytes(XF32, K), 128) + round_up((size_t)nb * 4, 128) +
+                         round_up(K, 128);
+    return plan_q8_stream(M, K, 0, fixed);
+}
+
+template <bool XF32, bool GATHER = false>
 static int launch_gemv_q8(uint32_t M, uint32_t K, const uint8_t* x, const uint8_t* W, float* out, int32_t* block_dots,
-                          uint32_t flags, cudaStream_t s) {
+                          uint32_t flags, cudaStream_t s, const Q8ChainGather* gather = nullptr) {
     if (M == 0) return ANE_OK;
     ANE_ARG_CHECK(K % 256 == 0, "q8_0_gemv_q8: K must be a multiple of 256");
     ANE_ARG_CHECK(((uintptr_t)W & 15) == 0, "q8_0_gemv_q8: W must be 16-byte aligned");
     ANE_ARG_CHECK(((uintptr_t)x & 15) == 0, "q8_0_gemv_q8: the activation must be 16-byte aligned");
     const uint32_t nb = K / 32;
-    // barriers (256) + the raw activation + scales + aligned codes
-    const size_t fixed = 256 + round_up((size_t)x_raw_bytes(XF32, K), 128) + round_up((size_t)nb * 4, 128) +
-                         round_up(K, 128);
-    const Q8Plan p = plan_q8_stream(M, K, 0, fixed);
+    const Q8Plan p = gemv_q8_plan<XF32>(M, K);
     ANE_ARG_CHECK(p.smem <= 200 * 1024, "q8_0_gemv_q8: K too large for the shared activation buffer");
     static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
-    if (int arc = set_max_dynamic_smem(q8_0_gemv_q8_kernel<XF32>, 200 * 1024, smem_set)) return arc;
+    if (int arc = set_max_dynamic_smem(q8_0_gemv_q8_kernel<XF32, GATHER>, 200 * 1024, smem_set)) return arc;
     const uint64_t row_bytes = (uint64_t)nb * 34;
     CUtensorMap wmap;
     int rc = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, row_bytes / 4, M, row_bytes,
                                   kQ8ChunkBytes / 4, kQ8RowsPerWarp, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    return launch_q8_stream(q8_0_gemv_q8_kernel<XF32>, p, s, wmap, x, out, block_dots, M, K, p.groups, p.warps,
-                            p.slots, flags, device_timeout_flag());
+    Q8ChainGather pg{};
+    if (gather) pg = *gather;
+    return launch_q8_stream(q8_0_gemv_q8_kernel<XF32, GATHER>, p, s, wmap, x, out, block_dots, M, K, p.groups,
+                            p.warps, p.slots, flags, device_timeout_flag(), pg);
 }
 
 int launch_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8_t* W, float* out, int32_t* block_dots,
@@ -249,6 +394,27 @@ int launch_q8_0_gemv_q8(uint32_t M, uint32_t K, const uint8_t* xq, const uint8_t
 int launch_mul_mat_q8_0(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, int32_t* block_dots,
                         uint32_t flags, cudaStream_t s) {
     return launch_gemv_q8<true>(M, K, reinterpret_cast<const uint8_t*>(x), W, out, block_dots, flags, s);
+}
+
+uint32_t mul_mat_q8_0_ctas(uint32_t M, uint32_t K) { return M ? gemv_q8_plan<true>(M, K).ctas : 0; }
+
+int launch_mul_mat_q8_0_gather(uint32_t M, uint32_t K, const float* x, const uint8_t* W, const Q8ChainGather& g,
+                               uint32_t flags, cudaStream_t s) {
+    ANE_ARG_CHECK(M > 0 && g.world >= 1 && g.world <= 8 && g.prev && g.tok && g.nproj > 0 && g.j < g.nproj,
+                  "mul_mat gather: bad arguments");
+    ANE_ARG_CHECK(g.prev_ctas > 0 && g.prev_groups >= g.prev_ctas && g.prev_rows > 0,
+                  "mul_mat gather: bad previous-projection split");
+    ANE_ARG_CHECK(g.x_from_prev || (x && ((uintptr_t)x & 15) == 0), "mul_mat gather: fp32 input must be 16-byte aligned");
+    ANE_ARG_CHECK(!g.x_from_prev || K <= g.world * g.prev_rows, "mul_mat gather: x longer than the previous output");
+    for (uint32_t q = 0; q < g.world; q++) ANE_ARG_CHECK(g.out[q], "mul_mat gather: NULL rank pointer");
+    const float* xs = g.x_from_prev ? reinterpret_cast<const float*>(g.prev) : x;  // 16-byte aligned either way
+    return launch_gemv_q8<true, true>(M, K, reinterpret_cast<const uint8_t*>(xs), W, nullptr, nullptr, flags, s, &g);
+}
+
+int launch_q8_chain_token_end(const uint64_t* last, uint32_t len, uint32_t nproj, uint32_t* tok, cudaStream_t s) {
+    q8_chain_token_end_kernel<<<1, 256, 0, s>>>(last, len, nproj, tok, device_timeout_flag());
+    ANE_CHECK_LAUNCH();
+    return ANE_OK;
 }
 
 }  // namespace ane_b200

@@ -268,3 +268,85 @@ class FusedDecodeStack:
         for b in self._opened:
             self._ane.lib.ane_ipc_close_handle(b)
         self._opened = []
+
+
+# ------------------------------------------- per-projection launches, fused gather
+class PeerChainDecodeStack:
+    """The weights and inputs of a batch-1 mode-Q DecodeStack run as one
+    MUL_MAT launch per projection (ane_mul_mat_q8_0_gather_dev) whose rows go
+    straight into every rank's next input vector over NVLink -- no NCCL call --
+    plus one token-end launch; the whole token captures into a CUDA graph.
+
+    Per rank one zeroed buffer holds two TAGGED vectors (8-byte {fp32 value,
+    u32 tag} words; projection j writes vector j % 2) and the token count; the
+    other ranks' buffers are mapped with CUDA IPC.  Projection j reads the
+    previous projection's vector: as its input x (when it chains), and always
+    one guard word per (rank, CTA) of that projection, so a fast rank never
+    overwrites a vector a slow one still reads.
+    """
+
+    def __init__(self, stack: DecodeStack, device, group=None):
+        import ctypes
+
+        import ane_b200 as ane
+
+        if stack.batch != 1:
+            raise ValueError("the fused-gather chain runs one token per step")
+        self._ane, self.stack = ane, stack
+        world, rank = stack.world, stack.rank
+        width = stack.h[0].numel()
+        vec_bytes = (width * 8 + 255) // 256 * 256
+        tok_off = 2 * vec_bytes
+        self.block = torch.zeros(tok_off + 256, dtype=torch.uint8, device=device)
+        base = self.block.data_ptr()
+        self._opened = []
+        peer = [0] * world
+        peer[rank] = base
+        if world > 1:
+            handle = (ctypes.c_uint8 * 64)()
+            off = ctypes.c_uint64()
+            ane.check(ane.lib.ane_ipc_get_handle(base, handle, ctypes.byref(off)))
+            everyone = [None] * world
+            dist.all_gather_object(everyone, (bytes(handle), off.value), group=group)
+            for r in range(world):
+                if r == rank:
+                    continue
+                h = (ctypes.c_uint8 * 64).from_buffer_copy(everyone[r][0])
+                b = ctypes.c_void_p()
+                ane.check(ane.lib.ane_ipc_open_handle(h, ctypes.byref(b)))
+                self._opened.append(b.value)
+                peer[r] = b.value + everyone[r][1]
+        self._tok = base + tok_off
+        projs = [(layer, p, M, K) for layer in range(stack.layers) for p, (_, M, K) in enumerate(stack.shapes)]
+        self.nproj = len(projs)
+        split = [(M // world, int(ane.lib.ane_mul_mat_q8_0_ctas(M // world, K))) for _, _, M, K in projs]
+        self._calls = []
+        for j, (layer, p, M, K) in enumerate(projs):
+            rows = M // world
+            jp = (j - 1) % self.nproj  # the previous projection (of the previous token for j = 0)
+            prev = base + (jp % 2) * vec_bytes
+            chained = p != 0
+            x = 0 if chained else stack.inputs[layer].data_ptr()
+            outs = (ctypes.c_void_p * world)(*[q + (j % 2) * vec_bytes + 8 * rank * rows for q in peer])
+            self._calls.append((rows, K, x, stack.weights[layer][p].data_ptr(), outs, prev, int(chained),
+                                split[jp][0], split[jp][1], j))
+        last_M = stack.shapes[-1][1]
+        self._last = base + ((self.nproj - 1) % 2) * vec_bytes
+        self._last_len = last_M
+        words = self.block[:tok_off].view(torch.float32).view(2, vec_bytes // 8, 2)
+        self.out = words[(self.nproj - 1) % 2, :last_M, 0]  # values of the last output
+
+    def forward(self, stream=None) -> torch.Tensor:
+        ane, world = self._ane, self.stack.world
+        s = ane._stream_ptr(stream)
+        for rows, K, x, W, outs, prev, chained, prev_rows, prev_ctas, j in self._calls:
+            ane.check(ane.lib.ane_mul_mat_q8_0_gather_dev(rows, K, x or None, W, world, outs, prev, chained,
+                                                          prev_rows, prev_ctas, self._tok, self.nproj, j,
+                                                          ane.WEIGHTS_STATIC, s))
+        ane.check(ane.lib.ane_q8_chain_token_end_dev(self._last, self._last_len, self.nproj, self._tok, s))
+        return self.out
+
+    def close(self):
+        for b in self._opened:
+            self._ane.lib.ane_ipc_close_handle(b)
+        self._opened = []

@@ -420,7 +420,10 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
       fused     -- ONE persistent launch per token (ane_q8_stack_run); with N > 1
                    each rank's rows go to every rank by NVLink peer stores;
       chain     -- one MUL_MAT launch per projection (a CUDA graph on 1 GPU), NCCL
-                   all-gather per projection with N > 1."""
+                   all-gather per projection with N > 1;
+      peer      -- one MUL_MAT launch per projection whose rows go to every rank
+                   by NVLink peer stores (arrival counters, no NCCL), a CUDA graph
+                   per token."""
     from ane_b200 import decode
 
     t0 = time.perf_counter()
@@ -480,6 +483,14 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
             torch.distributed.barrier(group)
     finally:
         fused.close()
+    peer = decode.PeerChainDecodeStack(stack, dev, group=group)
+    peer.forward()
+    torch.cuda.synchronize()
+    gp = capture(peer.forward)
+    peer_graph = gp is not None
+    peer_ms = timed(gp.replay if peer_graph else peer.forward)
+    del gp
+    torch.cuda.synchronize()
     # mode R: the reference's arithmetic (q8_0_gemv on the fp32 activation), same weights
     stack_r = decode.gpu_stack(layers, dev, world=world, rank=rank, group=group, weights=stack.weights, mode="r")
     stack_r.forward()
@@ -503,7 +514,7 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
         # the last layer's outputs of the sharded run against one GPU computing
         # that layer alone (each layer starts from its own seeded input)
         outs = {"chain_q": stack.forward().clone(), "mode_r": stack_r.forward().clone(),
-                "batch16": stack16.forward().clone()}
+                "batch16": stack16.forward().clone(), "peer_q": peer.forward().clone()}
         fused2 = decode.FusedDecodeStack(stack, dev, group=group)
         try:
             outs["fused_q"] = fused2.forward().clone()
@@ -516,24 +527,32 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
             one_r = decode.gpu_stack(1, dev, first_layer=layers - 1, weights=one.weights, mode="r")
             one16 = decode.gpu_stack(1, dev, first_layer=layers - 1, weights=one.weights, batch=batch)
             refs = {"chain_q": one.forward(), "fused_q": one.forward(), "mode_r": one_r.forward(),
-                    "batch16": one16.forward()}
+                    "batch16": one16.forward(), "peer_q": one.forward()}
             torch.cuda.synchronize()
             parity = {k: bool(torch.equal(outs[k].view(torch.int32), refs[k].view(torch.int32))) for k in outs}
             del one, one_r, one16, refs
         torch.distributed.barrier(group)
+    torch.cuda.synchronize()
+    if group is not None:
+        torch.distributed.barrier(group)  # no rank unmaps a peer buffer while a peer still writes it
+    peer.close()
     del stack16, stack_r
     wbytes = decode.stack_weight_bytes(layers)
     peaks = load_peaks()
     fused_path = "one persistent launch per token" + (", all-gather by NVLink peer stores" if world > 1 else "")
     chain_path = (f"{4 * layers} MUL_MAT launches" + ("" if world == 1 else " + NCCL all-gather each")
                   + (" in a CUDA graph" if chain_graph else " (eager)"))
-    best_ms, best_path = (fused_ms, fused_path) if fused_ms <= chain_ms else (chain_ms, chain_path)
+    peer_path = (f"{4 * layers} MUL_MAT launches, rows to every rank by NVLink peer stores + arrival counters"
+                 if world > 1 else f"{4 * layers} MUL_MAT launches with arrival counters") + (
+                     ", a CUDA graph per token" if peer_graph else " (eager)")
+    best_ms, best_path = min([(fused_ms, fused_path), (chain_ms, chain_path), (peer_ms, peer_path)])
     gbs = wbytes / (best_ms * 1e-3) / 1e9
     return {"layers": layers, "batch": 1, "n_gpus": world, "weight_bytes": wbytes, "ms_per_token": best_ms,
             "gbs": gbs, "per_gpu_hbm_frac": gbs / world / peaks["hbm_gbs"], "path": best_path,
             "fused_ms_per_token": fused_ms, "fused_gbs": wbytes / (fused_ms * 1e-3) / 1e9, "fused_path": fused_path,
             "chain_ms_per_token": chain_ms, "chain_gbs": wbytes / (chain_ms * 1e-3) / 1e9, "chain_path": chain_path,
-            "mode": "q (Q8_0 activation, ggml convention) for ms_per_token, fused and chain",
+            "peer_ms_per_token": peer_ms, "peer_gbs": wbytes / (peer_ms * 1e-3) / 1e9, "peer_path": peer_path,
+            "mode": "q (Q8_0 activation, ggml convention) for ms_per_token, fused, chain and peer",
             "mode_r": {"ms_per_token": r_ms, "gbs": wbytes / (r_ms * 1e-3) / 1e9,
                        "per_gpu_hbm_frac": wbytes / (r_ms * 1e-3) / 1e9 / world / peaks["hbm_gbs"],
                        "path": (f"{4 * layers} q8_0_gemv launches on the fp32 activation (the reference's "

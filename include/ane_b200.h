@@ -274,7 +274,37 @@ int ane_mul_mat_q8_0_batch_dev(uint32_t M, uint32_t K, uint32_t NT, const float*
                                float* y, size_t ldy, void* workspace, uint32_t flags, void* stream);
 
 /* ------------------------------------------------ decode stack (config 5)
- * A chain of Q8_0 MUL_MATs (batch 1, Q8_0 activation, as ane_mul_mat_q8_0_dev)
+ * A row-sharded chain of Q8_0 MUL_MATs with the all-gather fused into each
+ * matvec, one launch per projection (capturable in a CUDA graph).  Rank r of
+ * `world` owns rows_local rows of every projection and computes them as
+ * ane_mul_mat_q8_0_dev does (bit for bit).  Vectors are TAGGED: element i is
+ * one 8-byte word {fp32 value, u32 tag} written by one store, so a reader that
+ * sees the expected tag has the value -- no fence, flag or counter (a
+ * system-scope fence per projection would cost several microseconds).
+ * Projection j of token t (t = *tok, this GPU's count of finished tokens,
+ * nproj projections per token) stores tag t*nproj + j + 1 into every rank's
+ * vector (out_ranks[q] = rank q's vector at this rank's first row, 16-byte
+ * aligned CUDA-IPC peer pointers; out_ranks[rank] local) and waits (bounded,
+ * ~2 s) for tag t*nproj + j in `prev`, this GPU's copy of the previous
+ * projection's vector: in the words it reads as x (x_from_prev: x = prev[0..K),
+ * else x is the fp32 input) and in one guard word per (rank, CTA) of that
+ * projection (prev_rows rows per rank, prev_ctas = ane_mul_mat_q8_0_ctas of
+ * it), which that CTA stored after reading its own input -- so with two vectors
+ * per rank alternating, no rank overwrites a vector another still reads.  For
+ * j = 0, `prev` is the previous token's last vector (tag t*nproj; all zero
+ * before the first token).  ane_q8_chain_token_end_dev waits until the `len`
+ * words of the last vector carry tag t*nproj + nproj (the gathered output is
+ * then complete on this GPU) and bumps *tok.  Vectors and tok start zeroed;
+ * every rank makes the same calls.  No counterpart in the reference (its ggml
+ * backend issues one synchronous q8_0_gemv per MUL_MAT). */
+uint32_t ane_mul_mat_q8_0_ctas(uint32_t rows_local, uint32_t K);
+int ane_mul_mat_q8_0_gather_dev(uint32_t rows_local, uint32_t K, const float* x, const void* W, uint32_t world,
+                                void* const* out_ranks, const void* prev, uint32_t x_from_prev, uint32_t prev_rows,
+                                uint32_t prev_ctas, const uint32_t* tok, uint32_t nproj, uint32_t j, uint32_t flags,
+                                void* stream);
+int ane_q8_chain_token_end_dev(const void* last, uint32_t len, uint32_t nproj, uint32_t* tok, void* stream);
+
+/* The same chain (batch 1, Q8_0 activation, as ane_mul_mat_q8_0_dev)
  * in ONE persistent cooperative launch, row-sharded over `world` GPUs.
  * Outputs are TAGGED vectors: element i is one 8-byte word {fp32 value, u32
  * tag}, written with a single store, so a reader that sees the expected tag

@@ -79,6 +79,40 @@ def test_decode_stack_graph_replay_matches_eager(ane):
 
 
 @pytest.mark.parametrize("shapes,layers", [("small", 3), ("config5", 2)])
+def test_peer_chain_equals_per_projection_chain(ane, shapes, layers):
+    """The fused-gather chain (one MUL_MAT launch per projection writing every
+    rank's next input, arrival counters, a token-end launch) == the plain chain
+    of MUL_MAT launches, bit for bit, on repeated tokens (counters and token
+    count only grow) and under graph replay."""
+    import torch
+
+    from ane_b200.decode import LAYER_SHAPES, PeerChainDecodeStack, gpu_stack
+
+    sh = LAYER_SHAPES if shapes == "config5" else (("qkv", 512, 256), ("o", 256, 256), ("gate_up", 512, 256),
+                                                   ("down", 256, 256))
+    stack = gpu_stack(layers, torch.device("cuda", 0), shapes=sh, seed=23)
+    ref = stack.forward().clone()
+    peer = PeerChainDecodeStack(stack, torch.device("cuda", 0))
+    try:
+        for _ in range(3):
+            out = peer.forward()
+            torch.cuda.synchronize()
+            assert torch.equal(out.view(torch.int32), ref.view(torch.int32))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            peer.forward()
+        for _ in range(2):
+            peer.out.fill_(float("nan"))
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(peer.out.view(torch.int32), ref.view(torch.int32))
+        del g
+        assert ane.lib.ane_device_timeouts() == 0
+    finally:
+        peer.close()
+
+
+@pytest.mark.parametrize("shapes,layers", [("small", 3), ("config5", 2)])
 def test_fused_stack_equals_per_projection_chain(ane, shapes, layers):
     """One persistent launch per token == the chain of MUL_MAT launches, bit for
     bit, on repeated tokens (the counters only grow) and under graph replay."""

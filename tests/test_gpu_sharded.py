@@ -103,15 +103,17 @@ def _stack_worker(rank, world, port, layers, result_q):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
-    fused = None
+    fused = peer = None
     try:
         import ane_b200 as ane
-        from ane_b200.decode import FusedDecodeStack, gpu_stack
+        from ane_b200.decode import FusedDecodeStack, PeerChainDecodeStack, gpu_stack
 
         sharded = gpu_stack(layers, dev, world=world, rank=rank, seed=33)
         nccl_out = sharded.forward().clone()            # NCCL all-gather per projection
         fused = FusedDecodeStack(sharded, dev)           # peer stores + counters, one launch
         outs = [fused.forward().clone() for _ in range(3)]
+        peer = PeerChainDecodeStack(sharded, dev)        # peer stores + counters, a launch per projection
+        outs += [peer.forward().clone() for _ in range(3)]
         single = gpu_stack(layers, dev, world=1, rank=0, seed=33).forward()  # one GPU, all rows
         torch.cuda.synchronize()
         ok = torch.equal(nccl_out.view(torch.int32), single.view(torch.int32)) and all(
@@ -122,17 +124,20 @@ def _stack_worker(rank, world, port, layers, result_q):
         if rank == 0:
             result_q.put(int(flags.item()))
     finally:
-        if fused is not None:
+        if fused is not None or peer is not None:
             torch.cuda.synchronize()
             dist.barrier()  # no rank unmaps a peer buffer while a peer still writes it
-            fused.close()
+            for s in (fused, peer):
+                if s is not None:
+                    s.close()
         dist.destroy_process_group()
 
 
 def test_decode_stack_two_gpus_fused_and_nccl_equal_one_gpu():
     """Config-5 decode stack (2 layers) row-sharded over 2 GPUs: the NCCL
-    all-gather version and the one-launch peer-store version both give the
-    1-GPU vector bit for bit, on repeated tokens."""
+    all-gather version, the one-launch peer-store version and the
+    launch-per-projection peer-store chain all give the 1-GPU vector bit for
+    bit, on repeated tokens."""
     import torch
 
     if torch.cuda.device_count() < 2:
