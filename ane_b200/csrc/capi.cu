@@ -628,7 +628,7 @@ int ane_quantize_pair_xrank_dev(uint32_t M, uint32_t N, uint32_t K, const float*
     ANE_REQUIRE_GPU();
     ANE_ARG_CHECK(world >= 1 && world <= 8 && rank < world, "quantize xrank: world must be 1..8, rank < world");
     ANE_ARG_CHECK(prologue_coop_supported(M, N, K, A, B, Aq, Bq),
-                  "quantize xrank: needs K % 16 == 0, N % 16 == 0, 16-byte alignment and M*K, K*N >= 2^22");
+                  "quantize xrank: needs K % 16 == 0, N % 16 == 0, 16-byte alignment and M*K + K*N >= 2^22");
     ANE_ARG_CHECK(world == 1 || (slot_peer && slots && ctl), "quantize xrank: NULL exchange pointer");
     CoopXRank x{};
     x.world = world;

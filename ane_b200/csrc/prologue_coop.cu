@@ -582,12 +582,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 bool prologue_coop_supported(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, const int8_t* Aq,
                              const int8_t* Bq) {
-    // large enough that two HBM passes would cost more than the barriers; both
-    // tensors flat with 16-byte rows (K and N multiples of 16: the code arrays
-    // are the operands' own layouts) and 16-byte aligned
+    // large enough that a second HBM pass would cost more than the grid
+    // barriers (one small tensor is fine: its chunks simply sit with the first
+    // CTAs); both tensors flat with 16-byte rows (K and N multiples of 16: the
+    // code arrays are the operands' own layouts) and 16-byte aligned
     const uintptr_t align = (uintptr_t)A | (uintptr_t)B | (uintptr_t)Aq | (uintptr_t)Bq;
-    return K % 16 == 0 && N % 16 == 0 && (align & 15) == 0 && (size_t)M * K >= ((size_t)1 << 22) &&
-           (size_t)K * N >= ((size_t)1 << 22);
+    return K % 16 == 0 && N % 16 == 0 && (align & 15) == 0 && M > 0 && K > 0 && N > 0 &&
+           (size_t)M * K + (size_t)K * N >= ((size_t)1 << 22);
 }
 
 int launch_prologue_coop(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq, int8_t* Bq,

@@ -166,7 +166,7 @@ class ShardedDense:
             self._slots = self.fused.ptrs[rank] + c_bytes + 256
             self._xctl = self.fused.ptrs[rank] + c_bytes + 512
             K16 = (K + 15) // 16 * 16
-            self._coop = (K % 16 == 0 and N_local % 16 == 0 and M * K >= (1 << 22) and K * N_local >= (1 << 22)
+            self._coop = (K % 16 == 0 and N_local % 16 == 0 and M * K + K * N_local >= (1 << 22)
                           and K16 == K)
             self._rank = rank
             self.C_gathered = self.fused.tensor[:c_bytes].view(torch.float32).view(*shape)

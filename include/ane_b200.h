@@ -340,7 +340,7 @@ void ane_q8_stack_plan_free(void* plan);
  * are never reset; every rank makes the same calls.  The exchange also acts as
  * the call's entry handshake (a rank leaves it only after all ranks entered).
  * Needs K % 16 == 0, N % 16 == 0, 16-byte aligned A, B, Aq, Bq, and
- * M*K, K*N >= 2^22 (else ANE_ERR_INVALID_ARGUMENT).  Aq is M x K, Bq K x N.
+ * M*K + K*N >= 2^22 (else ANE_ERR_INVALID_ARGUMENT).  Aq is M x K, Bq K x N.
  * No counterpart in the reference. */
 int ane_quantize_pair_xrank_dev(uint32_t M, uint32_t N, uint32_t K, const float* A, const float* B, int8_t* Aq,
                                 int8_t* Bq, float* scales, float* partials, uint32_t world, uint32_t rank,

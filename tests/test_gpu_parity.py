@@ -308,7 +308,7 @@ def test_dense_fused_i8_stages_bit_exact(ane):
     (1024, 1028, 4096),   # N % 16 != 0: the staged prologue (B codes with 16-byte padded rows)
 ])
 def test_dense_fused_i8_coop_prologue_edges(ane, M, N, K):
-    """Shapes the one-launch cooperative prologue takes (M*K, K*N >= 2^22),
+    """Shapes the one-launch cooperative prologue takes (M*K + K*N >= 2^22),
     away from 4096^3: quantized operands, scales and C against the oracle."""
     import torch
 
