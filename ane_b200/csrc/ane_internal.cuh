@@ -98,6 +98,9 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
     ANE_CHECK_LAUNCH();
     return ANE_OK;
 }
+// Bytes of the device allocation that holds p, counted from p (0 when p is not
+// device memory or the driver cannot tell).
+size_t device_bytes_from(const void* p);
 // Verifies that the current device is sm_100 (the only target of this library).
 int require_sm100();
 

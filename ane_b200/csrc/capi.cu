@@ -695,6 +695,22 @@ MemGetAddressRangeFn address_range_fn() {
 }
 }  // namespace
 
+extern "C++" {
+namespace ane_b200 {
+size_t device_bytes_from(const void* p) {
+    auto fn = address_range_fn();
+    if (!fn || !p) return 0;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (fn(&base, &size, (CUdeviceptr)p) != CUDA_SUCCESS) {
+        cudaGetLastError();
+        return 0;
+    }
+    return (size_t)(base + size - (CUdeviceptr)p);
+}
+}  // namespace ane_b200
+}
+
 int ane_ipc_get_handle(const void* dev_ptr, void* handle64, uint64_t* offset) {
     ANE_REQUIRE_GPU();
     ANE_ARG_CHECK(dev_ptr && handle64 && offset, "ipc: NULL argument");

@@ -27,6 +27,7 @@
 #include <cuda_fp16.h>
 
 #include <cuda.h>
+#include <string.h>
 
 #include "ane_internal.cuh"
 #include "q8_stream.cuh"
@@ -265,14 +266,32 @@ __global__ void __launch_bounds__(256) kquant_gemv_kernel(const float* __restric
     if (row < M && t == 0) out[row] = s;
 }
 
-// The streamed matvec: stage t = chunk t % nchunks of pass t / nchunks.
+// Row segments of the bulk-copy variant: a row's chunk (up to CB bytes from a
+// 2-byte-aligned address) is copied as the 16-byte-aligned span around it, so a
+// segment slot holds CB + 30 bytes rounded up to 16.
 template <int F>
+struct KSeg {
+    static constexpr uint32_t CB = KBlock<F>::chunk * KBlock<F>::bytes;
+    static constexpr uint32_t seg = (CB + 30 + 15) / 16 * 16;
+    static constexpr uint32_t tile = kQ8RowsPerWarp * seg;
+};
+
+// The streamed matvec: stage t = chunk t % nchunks of pass t / nchunks.
+// BULK = false: one 2-D TMA box per warp (rows a whole number of 16-byte units).
+// BULK = true (any row length): every row's chunk arrives by one 1-D bulk copy
+// of the 16-byte-aligned span around it; the producer warp's 32 lanes share the
+// copies, and readers start at the chunk's offset in its span (its address mod
+// 16), so every load keeps the alignment it has in global memory.
+template <int F, bool BULK>
 __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
-    kquant_stream_kernel(const __grid_constant__ CUtensorMap wmap, const float* __restrict__ x,
-                         float* __restrict__ out, uint32_t M, uint32_t nsb, uint32_t groups, uint32_t nw,
-                         uint32_t nslots, int* err) {
+    kquant_stream_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ W,
+                         const float* __restrict__ x, float* __restrict__ out, uint32_t M, uint32_t nsb,
+                         uint32_t groups, uint32_t nw, uint32_t nslots, int* err) {
     constexpr uint32_t BB = KBlock<F>::bytes, C = KBlock<F>::chunk, CB = C * BB;
-    constexpr uint32_t TILE = (kQ8RowsPerWarp * CB + 127) / 128 * 128;  // one warp's 4 rows, 128-byte pitch
+    // one warp's 4 rows: a 128-byte-pitch TMA box, or 4 bulk-copy segments
+    constexpr uint32_t TILE = BULK ? KSeg<F>::tile : (kQ8RowsPerWarp * CB + 127) / 128 * 128;
+    constexpr uint32_t RPITCH = BULK ? KSeg<F>::seg : CB;
+    const size_t row_bytes = (size_t)nsb * BB;
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t nchunks = (nsb + C - 1) / C;
     const uint32_t w_bytes = nw * TILE, slot_bytes = w_bytes + C * 1024;
@@ -295,6 +314,44 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
     __syncthreads();
     ptx::griddep_launch_dependents();
 
+    if (warp == 0 && BULK) {
+        ptx::griddep_wait();  // x (and W) may be written by the previous kernel
+        for (uint32_t t = 0; t < ntiles; t++) {
+            const uint32_t slot = t % nslots, pass = t / nchunks, c = t - pass * nchunks;
+            bool ok = true;
+            if (lane == 0) ok = ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            const uint32_t gp = g0 + pass * nw, nwp = min(nw, g1 - gp);
+            const uint32_t nbytes = chunk_sbs(c) * BB;
+            uint8_t* dst = ring + (size_t)slot * slot_bytes;
+            // copy i = (warp w, row rr); rows past M are not copied (never stored)
+            auto span = [&](uint32_t i, uintptr_t& a0) -> uint32_t {
+                const uint32_t row = (gp + i / kQ8RowsPerWarp) * kQ8RowsPerWarp + i % kQ8RowsPerWarp;
+                if (row >= M) return 0u;
+                const uintptr_t a = reinterpret_cast<uintptr_t>(W) + (size_t)row * row_bytes + (size_t)c * CB;
+                a0 = a & ~(uintptr_t)15;
+                return (uint32_t)(((a + nbytes + 15) & ~(uintptr_t)15) - a0);
+            };
+            uint32_t mine = 0;
+            for (uint32_t i = lane; i < nwp * kQ8RowsPerWarp; i += 32) {
+                uintptr_t a0;
+                mine += span(i, a0);
+            }
+            for (int o = 16; o > 0; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
+            if (lane == 0) ptx::mbar_arrive_expect_tx(&full[slot], mine + chunk_sbs(c) * 1024);
+            __syncwarp();
+            for (uint32_t i = lane; i < nwp * kQ8RowsPerWarp; i += 32) {
+                uintptr_t a0 = 0;
+                const uint32_t len = span(i, a0);
+                if (len)
+                    ptx::bulk_load(dst + (i / kQ8RowsPerWarp) * TILE + (i % kQ8RowsPerWarp) * RPITCH,
+                                   reinterpret_cast<const void*>(a0), len, &full[slot]);
+            }
+            if (lane == 0)
+                ptx::bulk_load(dst + w_bytes, x + (size_t)c * C * 256, chunk_sbs(c) * 1024, &full[slot]);
+        }
+        return;
+    }
     if (warp == 0) {
         if (lane == 0) {
             ptx::prefetch_tmap(&wmap);
@@ -334,7 +391,9 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
             }
             if (warp_on) {
                 const uint8_t* st = ring + (size_t)slot * slot_bytes;
-                const uint8_t* rp = st + cw * TILE + rr * CB;
+                const uint8_t* rp = st + cw * TILE + rr * RPITCH;
+                if (BULK)  // the chunk's offset within its copied span
+                    rp += (reinterpret_cast<uintptr_t>(W) + (size_t)row * row_bytes + (size_t)c * CB) & 15;
                 const float* xc = reinterpret_cast<const float*>(st + w_bytes);
                 const uint32_t n = chunk_sbs(c);
                 for (uint32_t k = 0; k < n; k++) kq_superblock<F>(rp + k * BB, xc + 256 * k, t8, a0, a1, true);
@@ -350,22 +409,26 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
     }
 }
 
-template <int F>
+template <int F, bool BULK>
 int launch_kquant_stream(uint32_t M, uint32_t nsb, const float* x, const uint8_t* W, float* out, cudaStream_t s) {
     constexpr uint32_t BB = KBlock<F>::bytes, C = KBlock<F>::chunk, CB = C * BB;
-    constexpr uint32_t TILE = (kQ8RowsPerWarp * CB + 127) / 128 * 128;
+    constexpr uint32_t TILE = BULK ? KSeg<F>::tile : (kQ8RowsPerWarp * CB + 127) / 128 * 128;
     const Q8Plan p = plan_q8_stream(M, nsb * 256, C * 1024, 128, (BB + 7) / 8, TILE);
     static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
-    if (int arc = set_max_dynamic_smem(kquant_stream_kernel<F>, 200 * 1024, smem_set)) return arc;
+    if (int arc = set_max_dynamic_smem(kquant_stream_kernel<F, BULK>, 200 * 1024, smem_set)) return arc;
     ANE_ARG_CHECK(p.smem <= 200 * 1024, "kquant_gemv: shared-memory plan too large");
     const uint64_t row_bytes = (uint64_t)nsb * BB;
     CUtensorMap wmap;
-    const uint32_t E = KBlock<F>::elem;
-    int rc = encode_tensor_map_2d(&wmap, E == 8 ? CU_TENSOR_MAP_DATA_TYPE_INT64 : CU_TENSOR_MAP_DATA_TYPE_UINT32, W,
-                                  row_bytes / E, M, row_bytes, CB / E, kQ8RowsPerWarp, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc) return rc;
-    return launch_q8_stream(kquant_stream_kernel<F>, p, s, wmap, x, out, M, nsb, p.groups, p.warps, p.slots,
-                            device_timeout_flag());
+    memset(&wmap, 0, sizeof(wmap));
+    if (!BULK) {
+        const uint32_t E = KBlock<F>::elem;
+        int rc = encode_tensor_map_2d(&wmap, E == 8 ? CU_TENSOR_MAP_DATA_TYPE_INT64 : CU_TENSOR_MAP_DATA_TYPE_UINT32,
+                                      W, row_bytes / E, M, row_bytes, CB / E, kQ8RowsPerWarp,
+                                      CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+    }
+    return launch_q8_stream(kquant_stream_kernel<F, BULK>, p, s, wmap, W, x, out, M, nsb, p.groups, p.warps,
+                            p.slots, device_timeout_flag());
 }
 
 template <int F>
@@ -374,7 +437,14 @@ int launch_kquant(uint32_t M, uint32_t nsb, const float* x, const uint8_t* W, fl
     // and W, x are 16-byte aligned (TMA base, bulk copies of x)
     const uint64_t row_bytes = (uint64_t)nsb * KBlock<F>::bytes;
     if (row_bytes % 16 == 0 && ((uintptr_t)W & 15) == 0 && ((uintptr_t)x & 15) == 0)
-        return launch_kquant_stream<F>(M, nsb, x, W, out, s);
+        return launch_kquant_stream<F, false>(M, nsb, x, W, out, s);
+    // any row length: bulk copies of 16-byte-aligned spans, as long as the last
+    // span (up to 15 bytes past the matrix) stays inside W's allocation
+    const uint64_t total = (uint64_t)M * row_bytes;
+    const uint64_t tail = ((reinterpret_cast<uintptr_t>(W) + total + 15) & ~(uint64_t)15) -
+                          reinterpret_cast<uintptr_t>(W);
+    if (((uintptr_t)x & 15) == 0 && device_bytes_from(W) >= tail)
+        return launch_kquant_stream<F, true>(M, nsb, x, W, out, s);
     kquant_gemv_kernel<F><<<(M + 31) / 32, 256, 0, s>>>(x, W, out, M, nsb);
     ANE_CHECK_LAUNCH();
     return ANE_OK;

@@ -47,6 +47,25 @@ def test_kquant_gemv_exact(ane, fmt, M, K):
     _same_bits(y.cpu().numpy(), ref)
 
 
+@pytest.mark.parametrize("fmt", ["q3_k", "q6_k"])
+@pytest.mark.parametrize("offset", [2, 6])
+def test_kquant_gemv_unaligned_base(ane, fmt, offset):
+    """Rows of 110- / 210-byte super-blocks at a W base that is only 2-byte
+    aligned: the bulk-copy path copies 16-byte-aligned spans and reads each row
+    from its offset inside its span, bit-exact with the oracle."""
+    import torch
+
+    M, K = 100, 11008
+    rng = np.random.default_rng(offset * 31 + len(fmt))
+    W = random_blocks(fmt, M, K, rng)
+    x = _x(K, rng)
+    ref = oracle.kquant_gemv(fmt, W, x, M, K)
+    buf = torch.zeros(W.size + 64, dtype=torch.uint8, device="cuda")
+    buf[offset:offset + W.size] = torch.from_numpy(W).cuda()
+    y = ane.kquant_gemv(fmt, buf[offset:offset + W.size], torch.from_numpy(x).cuda(), M, K)
+    _same_bits(y.cpu().numpy(), ref)
+
+
 @pytest.mark.parametrize("fmt", FMTS)
 def test_kquant_gemv_special_scales(ane, fmt):
     """Zero, subnormal, inf and NaN super-block scales (d and, where the format
