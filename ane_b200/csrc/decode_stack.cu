@@ -196,19 +196,38 @@ __global__ void __launch_bounds__(32 * (kStackWarps + 1), 1)
                 const uint2* xw = reinterpret_cast<const uint2*>(P->x);
                 const uint32_t want = tag_of(epoch, j - 1);
                 for (uint32_t b = ct; b < nb && !dead; b += nw * 32) {
-                    // all 16 loads of the block in flight at once; words not yet
-                    // published are polled again one by one (bounded)
+                    // all 16 loads of the block in flight at once; the pairs not yet
+                    // published are read again together, one round trip per round
+                    // (a CTA that finished the last projection early reads words
+                    // other CTAs are still computing), bounded
                     const uint2* blk = xw + (size_t)b * 32;
-                    uint4 raw[16];
-#pragma unroll
-                    for (int k = 0; k < 16; k++) raw[k] = ld_word2(blk + 2 * k);
                     float v[32];
+                    uint32_t miss = 0;
 #pragma unroll
                     for (int k = 0; k < 16; k++) {
-                        v[2 * k] = raw[k].y == want ? __uint_as_float(raw[k].x)
-                                                    : wait_word(blk + 2 * k, want, &dead, err);
-                        v[2 * k + 1] = raw[k].w == want ? __uint_as_float(raw[k].z)
-                                                        : wait_word(blk + 2 * k + 1, want, &dead, err);
+                        const uint4 w = ld_word2(blk + 2 * k);
+                        v[2 * k] = __uint_as_float(w.x);
+                        v[2 * k + 1] = __uint_as_float(w.z);
+                        miss |= (w.y != want || w.w != want) ? 1u << k : 0u;
+                    }
+                    const long long t0 = miss ? clock64() : 0;
+                    while (miss) {
+                        if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
+                            atomicAdd(err, 1);
+                            dead = true;
+                            break;
+                        }
+                        __nanosleep(64);
+#pragma unroll
+                        for (int k = 0; k < 16; k++) {
+                            if (!((miss >> k) & 1u)) continue;
+                            const uint4 w = ld_word2(blk + 2 * k);
+                            if (w.y == want && w.w == want) {
+                                v[2 * k] = __uint_as_float(w.x);
+                                v[2 * k + 1] = __uint_as_float(w.z);
+                                miss &= ~(1u << k);
+                            }
+                        }
                     }
                     if (!dead) q8_quantize_regs(v, xs, xd, b);
                 }

@@ -327,26 +327,29 @@ __global__ void __launch_bounds__(32 * (kMaxTiles * kMaxGroups + 1), 1)
     float* tot = totals + ti * (kTotBytes / 4) + lane * 4;
     // stage t goes to group t % ngroups, so with two groups stage t - 2 is always
     // this warp's own: when it waits on phase t - 1 of the baton, phase t - 2 is
-    // complete and the parity test is exact
+    // complete and the parity test is exact.  A full-barrier parity wait is exact
+    // too: by the baton, every stage before t - 2 of this tile has been consumed,
+    // so slot t % nslots is at most one phase behind.  That argument needs the
+    // baton, so a warp whose tile has no rows in a pass leaves (a tile without
+    // rows has none in every later pass): out of step with the other group, an
+    // odd ring could show it a slot two phases behind, its parity wait would pass
+    // at once, and its early arrival would free a slot still being read.  Tile
+    // 0's warp, which has rows in every pass, arrives for the ones that left.
     for (uint32_t t = grp; t < nstages; t += a.ngroups) {
         const uint32_t pass = t / nseg, s = t - pass * nseg, slot = t % nslots;
         const uint32_t qa = q0 + 2 * (pass * T + ti);
-        const bool active = qa < q1;  // once false, false for every later pass
+        if (qa >= q1) break;
+        const uint32_t absent = T - min(T, tiles - pass * T);  // warps of this group that have left
         // one verdict per warp: no lane may reach the warp-wide MMAs or shuffles
         // without the others after a timed-out wait
         if (!__all_sync(0xffffffffu, ptx::mbar_wait(&full[slot], (t / nslots) & 1, err))) break;
-        if (!active) {
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&empty[slot]);
-            continue;
-        }
         const uint32_t rows = qa + 1 < q1 ? 8u : 4u;  // real rows of this tile
         const uint8_t* xs = ring + (size_t)slot * slot_bytes;
         const uint32_t nblk = min(kSegBlocks, a.nb - s * kSegBlocks);
         float2 seg01, seg23;
         segment_sums(xs, xs + kXSegBytes + (size_t)ti * kTileBytes, nblk, rows, g, q, seg01, seg23);
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&empty[slot]);
+        if (lane == 0) ptx::mbar_arrive_cnt(&empty[slot], ti == 0 ? 1u + absent : 1u);
         // the row totals, in segment order: wait for stage t - 1's phase of this
         // tile's baton, add this segment, pass the baton on
         if (t > 0 && !__all_sync(0xffffffffu, ptx::mbar_wait(&baton[ti], (t - 1) & 1, err))) break;
