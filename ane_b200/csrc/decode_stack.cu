@@ -169,7 +169,8 @@ __global__ void __launch_bounds__(32 * (kStackWarps + 1), 1)
         //    launch, or the last one of the previous launch) read.  Every (rank, CTA)
         //    with rows in j-1 read its input before publishing its first row, so
         //    one word per such row range with j-1's tag proves the vector is free.
-        //    Loads are issued now and checked after the activation read.
+        //    Loads are issued now; words not there yet are read again in the same
+        //    rounds as the activation's (one round trip per round for both).
         const bool guard = npass > 0 && (j > 0 || epoch > 0);
         const StackProj* Q = projs + (j ? j - 1 : nproj - 1);
         const uint32_t qtag = j ? tag_of(epoch, j - 1) : tag_of(epoch - 1, nproj - 1);
@@ -189,6 +190,22 @@ __global__ void __launch_bounds__(32 * (kStackWarps + 1), 1)
                 }
             }
         }
+        bool gchecked = false;
+        uint32_t gmiss = 0;  // guard words still without j-1's tag
+        auto guard_miss = [&]() {
+            uint32_t m = 0;
+#pragma unroll
+            for (uint32_t k = 0; k < kGuards; k++)
+                if (gptr[k] && gval[k].y != qtag) m |= 1u << k;
+            return m;
+        };
+        auto guard_round = [&](uint32_t m) {
+#pragma unroll
+            for (uint32_t k = 0; k < kGuards; k++)
+                if ((m >> k) & 1u)
+                    if (ld_word(gptr[k]).y == qtag) m &= ~(1u << k);
+            return m;
+        };
         // 1. activation -> Q8_0 codes + scales in shared memory (one thread per
         //    block); a CTA without rows in this projection does not read it
         if (!dead && npass > 0) {
@@ -210,8 +227,12 @@ __global__ void __launch_bounds__(32 * (kStackWarps + 1), 1)
                         v[2 * k + 1] = __uint_as_float(w.z);
                         miss |= (w.y != want || w.w != want) ? 1u << k : 0u;
                     }
-                    const long long t0 = miss ? clock64() : 0;
-                    while (miss) {
+                    if (!gchecked) {
+                        gmiss = guard_miss();
+                        gchecked = true;
+                    }
+                    const long long t0 = (miss | gmiss) ? clock64() : 0;
+                    while (miss | gmiss) {
                         if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
                             atomicAdd(err, 1);
                             dead = true;
@@ -228,6 +249,7 @@ __global__ void __launch_bounds__(32 * (kStackWarps + 1), 1)
                                 miss &= ~(1u << k);
                             }
                         }
+                        gmiss = guard_round(gmiss);
                     }
                     if (!dead) q8_quantize_regs(v, xs, xd, b);
                 }
@@ -236,9 +258,20 @@ __global__ void __launch_bounds__(32 * (kStackWarps + 1), 1)
                     q8_quantize_block<true>(reinterpret_cast<const float*>(P->x) + (size_t)b * 32, xs, xd, b);
             }
         }
-#pragma unroll
-        for (uint32_t k = 0; k < kGuards; k++)
-            if (!dead && gptr[k] && gval[k].y != qtag) wait_word(gptr[k], qtag, &dead, err);
+        // threads without an activation block: their guard words alone
+        if (!gchecked) gmiss = guard_miss();
+        if (!dead && gmiss) {
+            const long long t0 = clock64();
+            while (gmiss) {
+                if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
+                    atomicAdd(err, 1);
+                    dead = true;
+                    break;
+                }
+                __nanosleep(64);
+                gmiss = guard_round(gmiss);
+            }
+        }
         if (dead) dead_s = 1;
         __syncwarp();
         ptx::named_barrier_sync(1, nw * 32);
@@ -249,18 +282,40 @@ __global__ void __launch_bounds__(32 * (kStackWarps + 1), 1)
             const uint32_t row = (gp + cw) * kQ8RowsPerWarp + r;
             const bool active = gp + cw < g1 && row < rows;
             float sum = 0.f;
-            for (uint32_t ch = 0; ch < nchunks; ch++, t++) {
-                const uint32_t slot = t % nslots;
-                if (!dead && !ptx::mbar_wait(&full[slot], (t / nslots) & 1, err)) dead = true;
+            // two ring stages per step: the second pair's loads and block dots run
+            // alongside the first's (each lane still adds its terms in block order)
+            uint32_t slot = t % nslots, phase = (t / nslots) & 1u;
+            const uint32_t lane_off = cw * kQ8WarpTileBytes + r * kQ8ChunkBytes + pp * 68;
+            for (uint32_t ch = 0; ch < nchunks; ch += 2) {
+                const bool two = ch + 1 < nchunks;
+                const uint32_t slot2 = slot + 1 == nslots ? 0u : slot + 1;
+                const uint32_t phase2 = slot + 1 == nslots ? phase ^ 1u : phase;
+                if (!dead && !ptx::mbar_wait(&full[slot], phase, err)) dead = true;
+                if (two && !dead && !ptx::mbar_wait(&full[slot2], phase2, err)) dead = true;
                 const uint32_t b = ch * kQ8ChunkBlocks + 2 * pp;
-                if (!dead && active && b < nb) {
-                    const uint32_t* pw = reinterpret_cast<const uint32_t*>(
-                        ring + (size_t)slot * slot_bytes + cw * kQ8WarpTileBytes + r * kQ8ChunkBytes + pp * 68);
+                if (!dead && active) {
                     int32_t s0, s1;
-                    q8_pair(pw, xs, xd, b, s0, s1, sum);
+                    if (b < nb)
+                        q8_pair(reinterpret_cast<const uint32_t*>(ring + (size_t)slot * slot_bytes + lane_off), xs, xd,
+                                b, s0, s1, sum);
+                    if (two && b + kQ8ChunkBlocks < nb)
+                        q8_pair(reinterpret_cast<const uint32_t*>(ring + (size_t)slot2 * slot_bytes + lane_off), xs,
+                                xd, b + kQ8ChunkBlocks, s0, s1, sum);
                 }
-                __syncwarp();
-                if (lane == 0 && !dead) ptx::mbar_arrive(&empty[slot]);
+                // the vote consumes every lane's sum, so all of this step's ring reads
+                // have returned: the stages can be freed without release semantics
+                __all_sync(0xffffffffu, sum == sum);
+                if (lane == 0 && !dead) {
+                    ptx::mbar_arrive_relaxed(&empty[slot]);
+                    if (two) ptx::mbar_arrive_relaxed(&empty[slot2]);
+                }
+                const uint32_t adv = two ? 2u : 1u;
+                t += adv;
+                slot += adv;
+                if (slot >= nslots) {
+                    slot -= nslots;
+                    phase ^= 1u;
+                }
             }
             sum = q8_row_total(sum);
             // 3. publish: one tagged word per row and rank
