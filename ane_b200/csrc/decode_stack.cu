@@ -134,17 +134,23 @@ __global__ void __launch_bounds__(32 * (kStackWarps + 1), 1)
                 const uint32_t nchunks = (P->K / 32 + kQ8ChunkBlocks - 1) / kQ8ChunkBlocks;
                 for (uint32_t pass = 0; pass < npass && alive; pass++) {
                     const uint32_t gp = g0 + pass * nw, nwp = min(nw, g1 - gp);
-                    for (uint32_t ch = 0; ch < nchunks; ch++, t++) {
+                    // a stage holds U consecutive chunks of each of the pass's nwp
+                    // groups: with few groups per CTA, fewer and longer steps
+                    const uint32_t U = nw / nwp, nst = (nchunks + U - 1) / U;
+                    for (uint32_t st = 0; st < nst; st++, t++) {
                         const uint32_t slot = t % nslots;
                         if (!ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err)) {
                             alive = false;
                             break;
                         }
+                        const uint32_t c0 = st * U, nc = min(U, nchunks - c0);
                         uint8_t* dst = ring + (size_t)slot * slot_bytes;
-                        ptx::mbar_arrive_expect_tx(&full[slot], nwp * kQ8WarpTileBytes);
+                        ptx::mbar_arrive_expect_tx(&full[slot], nwp * nc * kQ8WarpTileBytes);
                         for (uint32_t w = 0; w < nwp; w++)
-                            ptx::tma_load_2d(dst + w * kQ8WarpTileBytes, &P->wmap, &full[slot],
-                                             (int)(ch * (kQ8ChunkBytes / 4)), (int)((gp + w) * kQ8RowsPerWarp));
+                            for (uint32_t u = 0; u < nc; u++)
+                                ptx::tma_load_2d(dst + (w * U + u) * kQ8WarpTileBytes, &P->wmap, &full[slot],
+                                                 (int)((c0 + u) * (kQ8ChunkBytes / 4)),
+                                                 (int)((gp + w) * kQ8RowsPerWarp));
                     }
                 }
             }
@@ -278,29 +284,32 @@ __global__ void __launch_bounds__(32 * (kStackWarps + 1), 1)
         if (dead_s) dead = true;
         // 2. this CTA's rows: ring stages in the producer's order
         for (uint32_t pass = 0; pass < npass; pass++) {
-            const uint32_t gp = g0 + pass * nw;
+            const uint32_t gp = g0 + pass * nw, nwp = min(nw, g1 - gp);
+            const uint32_t U = nw / nwp, nst = (nchunks + U - 1) / U;  // the producer's stages
             const uint32_t row = (gp + cw) * kQ8RowsPerWarp + r;
-            const bool active = gp + cw < g1 && row < rows;
+            const bool active = cw < nwp && row < rows;
             float sum = 0.f;
-            // two ring stages per step: the second pair's loads and block dots run
+            // two ring stages per step: the second's loads and block dots run
             // alongside the first's (each lane still adds its terms in block order)
             uint32_t slot = t % nslots, phase = (t / nslots) & 1u;
-            const uint32_t lane_off = cw * kQ8WarpTileBytes + r * kQ8ChunkBytes + pp * 68;
-            for (uint32_t ch = 0; ch < nchunks; ch += 2) {
-                const bool two = ch + 1 < nchunks;
+            const uint32_t lane_off = cw * U * kQ8WarpTileBytes + r * kQ8ChunkBytes + pp * 68;
+            for (uint32_t st = 0; st < nst; st += 2) {
+                const bool two = st + 1 < nst;
                 const uint32_t slot2 = slot + 1 == nslots ? 0u : slot + 1;
                 const uint32_t phase2 = slot + 1 == nslots ? phase ^ 1u : phase;
                 if (!dead && !ptx::mbar_wait(&full[slot], phase, err)) dead = true;
                 if (two && !dead && !ptx::mbar_wait(&full[slot2], phase2, err)) dead = true;
-                const uint32_t b = ch * kQ8ChunkBlocks + 2 * pp;
                 if (!dead && active) {
-                    int32_t s0, s1;
-                    if (b < nb)
-                        q8_pair(reinterpret_cast<const uint32_t*>(ring + (size_t)slot * slot_bytes + lane_off), xs, xd,
-                                b, s0, s1, sum);
-                    if (two && b + kQ8ChunkBlocks < nb)
-                        q8_pair(reinterpret_cast<const uint32_t*>(ring + (size_t)slot2 * slot_bytes + lane_off), xs,
-                                xd, b + kQ8ChunkBlocks, s0, s1, sum);
+                    const uint32_t nc = min(2 * U, nchunks - st * U);  // chunks of this step
+#pragma unroll 2
+                    for (uint32_t u = 0; u < nc; u++) {
+                        const uint32_t b = (st * U + u) * kQ8ChunkBlocks + 2 * pp;
+                        if (b >= nb) break;
+                        const uint8_t* base = ring + (size_t)(u < U ? slot : slot2) * slot_bytes;
+                        int32_t s0, s1;
+                        q8_pair(reinterpret_cast<const uint32_t*>(base + lane_off + (u < U ? u : u - U) * kQ8WarpTileBytes),
+                                xs, xd, b, s0, s1, sum);
+                    }
                 }
                 // the vote consumes every lane's sum, so all of this step's ring reads
                 // have returned: the stages can be freed without release semantics
