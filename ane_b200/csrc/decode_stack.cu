@@ -133,24 +133,26 @@ __global__ void __launch_bounds__(32 * (kStackWarps + 1), 1)
                 const uint32_t npass = (g1 - g0 + nw - 1) / nw;
                 const uint32_t nchunks = (P->K / 32 + kQ8ChunkBlocks - 1) / kQ8ChunkBlocks;
                 for (uint32_t pass = 0; pass < npass && alive; pass++) {
+                    // the pass's (chunk, group) tiles in chunk-major order, nw tiles
+                    // per stage: every stage is full whatever the pass's group count
                     const uint32_t gp = g0 + pass * nw, nwp = min(nw, g1 - gp);
-                    // a stage holds U consecutive chunks of each of the pass's nwp
-                    // groups: with few groups per CTA, fewer and longer steps
-                    const uint32_t U = nw / nwp, nst = (nchunks + U - 1) / U;
+                    const uint32_t ntiles = nwp * nchunks, nst = (ntiles + nw - 1) / nw;
                     for (uint32_t st = 0; st < nst; st++, t++) {
                         const uint32_t slot = t % nslots;
                         if (!ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err)) {
                             alive = false;
                             break;
                         }
-                        const uint32_t c0 = st * U, nc = min(U, nchunks - c0);
+                        const uint32_t i0 = st * nw, n = min(nw, ntiles - i0);
                         uint8_t* dst = ring + (size_t)slot * slot_bytes;
-                        ptx::mbar_arrive_expect_tx(&full[slot], nwp * nc * kQ8WarpTileBytes);
-                        for (uint32_t w = 0; w < nwp; w++)
-                            for (uint32_t u = 0; u < nc; u++)
-                                ptx::tma_load_2d(dst + (w * U + u) * kQ8WarpTileBytes, &P->wmap, &full[slot],
-                                                 (int)((c0 + u) * (kQ8ChunkBytes / 4)),
-                                                 (int)((gp + w) * kQ8RowsPerWarp));
+                        ptx::mbar_arrive_expect_tx(&full[slot], n * kQ8WarpTileBytes);
+                        for (uint32_t k = 0; k < n; k++) {
+                            const uint32_t ch = (i0 + k) / nwp, w = i0 + k - ch * nwp;
+                            ptx::tma_load_2d(dst + k * kQ8WarpTileBytes, &P->wmap, &full[slot],
+                                             (int)(ch * (kQ8ChunkBytes / 4)), (int)((gp + w) * kQ8RowsPerWarp));
+                        }
+                        // a stage is freed by one arrival per tile: those it does not hold
+                        if (n < nw) ptx::mbar_arrive_cnt(&empty[slot], nw - n);
                     }
                 }
             }
@@ -285,50 +287,71 @@ __global__ void __launch_bounds__(32 * (kStackWarps + 1), 1)
         // 2. this CTA's rows: ring stages in the producer's order
         for (uint32_t pass = 0; pass < npass; pass++) {
             const uint32_t gp = g0 + pass * nw, nwp = min(nw, g1 - gp);
-            const uint32_t U = nw / nwp, nst = (nchunks + U - 1) / U;  // the producer's stages
+            const uint32_t nst = (nwp * nchunks + nw - 1) / nw;  // the producer's stages
             const uint32_t row = (gp + cw) * kQ8RowsPerWarp + r;
-            const bool active = cw < nwp && row < rows;
             float sum = 0.f;
-            // two ring stages per step: the second's loads and block dots run
-            // alongside the first's (each lane still adds its terms in block order)
-            uint32_t slot = t % nslots, phase = (t / nslots) & 1u;
-            const uint32_t lane_off = cw * U * kQ8WarpTileBytes + r * kQ8ChunkBytes + pp * 68;
-            for (uint32_t st = 0; st < nst; st += 2) {
-                const bool two = st + 1 < nst;
-                const uint32_t slot2 = slot + 1 == nslots ? 0u : slot + 1;
-                const uint32_t phase2 = slot + 1 == nslots ? phase ^ 1u : phase;
-                if (!dead && !ptx::mbar_wait(&full[slot], phase, err)) dead = true;
-                if (two && !dead && !ptx::mbar_wait(&full[slot2], phase2, err)) dead = true;
-                if (!dead && active) {
-                    const uint32_t nc = min(2 * U, nchunks - st * U);  // chunks of this step
-#pragma unroll 2
-                    for (uint32_t u = 0; u < nc; u++) {
-                        const uint32_t b = (st * U + u) * kQ8ChunkBlocks + 2 * pp;
-                        if (b >= nb) break;
-                        const uint8_t* base = ring + (size_t)(u < U ? slot : slot2) * slot_bytes;
-                        int32_t s0, s1;
-                        q8_pair(reinterpret_cast<const uint32_t*>(base + lane_off + (u < U ? u : u - U) * kQ8WarpTileBytes),
-                                xs, xd, b, s0, s1, sum);
+            if (cw < nwp && !dead) {
+                // this warp's tiles are cw, cw + nwp, cw + 2 nwp, ... (its chunks in
+                // order); two per step, so the second's loads and block dots run
+                // alongside the first's (each lane still adds its terms in block order)
+                uint32_t wslot = t % nslots, wphase = (t / nslots) & 1u;  // next stage to wait for
+                uint32_t waited = 0, aslot = wslot, astage = 0;           // aslot: slot of stage astage
+                const uint32_t lane_off = r * kQ8ChunkBytes + pp * 68;
+                for (uint32_t ch = 0; ch < nchunks; ch += 2) {
+                    const bool two = ch + 1 < nchunks;
+                    const uint32_t i0 = ch * nwp + cw, i1 = i0 + nwp;
+                    const uint32_t s0 = i0 / nw, s1 = two ? i1 / nw : s0;
+                    while (waited <= s1 && !dead) {
+                        if (!ptx::mbar_wait(&full[wslot], wphase, err)) dead = true;
+                        waited++;
+                        if (++wslot == nslots) {
+                            wslot = 0;
+                            wphase ^= 1u;
+                        }
+                    }
+                    if (dead) break;
+                    while (astage < s0) {
+                        astage++;
+                        aslot = aslot + 1 == nslots ? 0u : aslot + 1;
+                    }
+                    const uint32_t bslot = s1 == s0 ? aslot : (aslot + 1 == nslots ? 0u : aslot + 1);
+                    const uint32_t b = ch * kQ8ChunkBlocks + 2 * pp;
+                    if (row < rows) {
+                        int32_t d0, d1;
+                        if (b < nb)
+                            q8_pair(reinterpret_cast<const uint32_t*>(ring + (size_t)aslot * slot_bytes +
+                                                                      (i0 % nw) * kQ8WarpTileBytes + lane_off),
+                                    xs, xd, b, d0, d1, sum);
+                        if (two && b + kQ8ChunkBlocks < nb)
+                            q8_pair(reinterpret_cast<const uint32_t*>(ring + (size_t)bslot * slot_bytes +
+                                                                      (i1 % nw) * kQ8WarpTileBytes + lane_off),
+                                    xs, xd, b + kQ8ChunkBlocks, d0, d1, sum);
+                    }
+                    // the vote consumes every lane's sum, so all of this step's ring reads
+                    // have returned: the tiles can be freed without release semantics
+                    __all_sync(0xffffffffu, sum == sum);
+                    if (lane == 0) {
+                        ptx::mbar_arrive_relaxed(&empty[aslot]);
+                        if (two) ptx::mbar_arrive_relaxed(&empty[bslot]);
                     }
                 }
-                // the vote consumes every lane's sum, so all of this step's ring reads
-                // have returned: the stages can be freed without release semantics
-                __all_sync(0xffffffffu, sum == sum);
-                if (lane == 0 && !dead) {
-                    ptx::mbar_arrive_relaxed(&empty[slot]);
-                    if (two) ptx::mbar_arrive_relaxed(&empty[slot2]);
-                }
-                const uint32_t adv = two ? 2u : 1u;
-                t += adv;
-                slot += adv;
-                if (slot >= nslots) {
-                    slot -= nslots;
-                    phase ^= 1u;
+                // A warp's last tile may sit in the stage before the last.  It still
+                // waits for every stage of the pass: a parity wait is exact only while
+                // the slot is at most one phase away, and a warp that skipped a stage
+                // could otherwise meet that slot two phases on in a later pass.
+                while (waited < nst && !dead) {
+                    if (!ptx::mbar_wait(&full[wslot], wphase, err)) dead = true;
+                    waited++;
+                    if (++wslot == nslots) {
+                        wslot = 0;
+                        wphase ^= 1u;
+                    }
                 }
             }
+            t += nst;
             sum = q8_row_total(sum);
             // 3. publish: one tagged word per row and rank
-            if (!dead && active && pp == 0)
+            if (!dead && cw < nwp && row < rows && pp == 0)
                 for (uint32_t q = 0; q < world; q++) st_word(P->out[q] + row, sum, tag);
         }
         // every compute warp is done with xs / xd before the next projection rewrites them
