@@ -305,15 +305,33 @@ struct Q8ChainGather {
 int launch_mul_mat_q8_0_gather(uint32_t M, uint32_t K, const float* x, const uint8_t* W, const Q8ChainGather& g,
                                uint32_t flags, cudaStream_t s);
 uint32_t mul_mat_q8_0_ctas(uint32_t M, uint32_t K);
-// Ends a token of such a chain: waits (bounded) until every word of the last
-// projection's vector (`len` words, this GPU's copy) carries that projection's
-// tag, then bumps *tok.
-int launch_q8_chain_token_end(const uint64_t* last, uint32_t len, uint32_t nproj, uint32_t* tok, cudaStream_t s);
+// Ends a step of such a chain: waits (bounded) until every word of the last
+// projection's output on this GPU (`ntok` token rows of `rows` words, row
+// stride `ld` words) carries that projection's tag, then bumps *tok.
+int launch_q8_chain_token_end(const uint64_t* last, uint32_t rows, size_t ld, uint32_t ntok, uint32_t nproj,
+                              uint32_t* tok, cudaStream_t s);
 // ggml MUL_MAT for NT <= 16 activation rows (q8_0_gemm_q8.cu); the workspace
 // (mul_mat_q8_0_batch_workspace_size bytes, 256-byte aligned) receives the
 // quantized activation.
 size_t mul_mat_q8_0_batch_workspace_size(uint32_t M, uint32_t K);
 int launch_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const float* x, size_t ldx, const uint8_t* W,
                               float* y, size_t ldy, void* workspace, uint32_t flags, cudaStream_t s);
+// The same MUL_MAT as one link of a row-sharded chain (decode at batch NT): the
+// activation rows come from the previous projection's TAGGED output (or the
+// plain fp32 x), and each output (token t, row r) leaves as one {value, tag}
+// word stored into every rank's next vector at out[q] + t * ldw + r.
+struct Q8BatchGather {
+    uint32_t world;
+    uint64_t* out[8];      // per rank: this rank's first row of that rank's vector
+    size_t ldw;            // words per token row of every vector
+    const uint64_t* prev;  // this GPU's vector of the previous projection
+    uint32_t x_from_prev;  // 1: token t's x = prev[t * ldw + 0..K); 0: x is the fp32 input
+    uint32_t prev_rows;    // the previous projection's rows per rank (guard words)
+    const uint32_t* tok;   // this GPU's count of finished steps
+    uint32_t nproj, j;     // projections per step, this projection
+};
+int launch_mul_mat_q8_0_batch_gather(uint32_t M, uint32_t K, uint32_t NT, const float* x, size_t ldx,
+                                     const uint8_t* W, void* workspace, const Q8BatchGather& g, uint32_t flags,
+                                     cudaStream_t s);
 
 }  // namespace ane_b200

@@ -604,7 +604,45 @@ int ane_mul_mat_q8_0_gather_dev(uint32_t rows_local, uint32_t K, const float* x,
 int ane_q8_chain_token_end_dev(const void* last, uint32_t len, uint32_t nproj, uint32_t* tok, void* stream) {
     ANE_REQUIRE_GPU();
     ANE_ARG_CHECK(last && tok && nproj > 0, "q8_chain_token_end: bad arguments");
-    int rc = launch_q8_chain_token_end(static_cast<const uint64_t*>(last), len, nproj, tok,
+    int rc = launch_q8_chain_token_end(static_cast<const uint64_t*>(last), len, len, 1, nproj, tok,
+                                       static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+int ane_mul_mat_q8_0_batch_gather_dev(uint32_t rows_local, uint32_t K, uint32_t NT, const float* x, size_t ldx,
+                                      const void* W, void* workspace, uint32_t world, void* const* out_ranks,
+                                      size_t ldw, const void* prev, uint32_t x_from_prev, uint32_t prev_rows,
+                                      const uint32_t* tok, uint32_t nproj, uint32_t j, uint32_t flags, void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK((flags & ~ANE_Q8_WEIGHTS_STATIC) == 0, "mul_mat_q8_0_batch_gather: unknown flag bits");
+    ANE_ARG_CHECK(world >= 1 && world <= 8 && out_ranks, "mul_mat_q8_0_batch_gather: world must be 1..8");
+    ANE_ARG_CHECK(prev && tok && nproj > 0 && j < nproj && prev_rows > 0, "mul_mat_q8_0_batch_gather: bad chain");
+    ANE_ARG_CHECK(ldw >= (size_t)rows_local * world && ldw >= K && (ldw % 2) == 0 && ((uintptr_t)prev & 15) == 0,
+                  "mul_mat_q8_0_batch_gather: ldw must hold every rank's rows and K, be even, prev 16-byte aligned");
+    Q8BatchGather g{};
+    g.world = world;
+    for (uint32_t q = 0; q < world; q++) {
+        ANE_ARG_CHECK(out_ranks[q] && ((uintptr_t)out_ranks[q] & 7) == 0,
+                      "mul_mat_q8_0_batch_gather: 8-byte-aligned output pointer per rank");
+        g.out[q] = static_cast<uint64_t*>(out_ranks[q]);
+    }
+    g.ldw = ldw;
+    g.prev = static_cast<const uint64_t*>(prev);
+    g.x_from_prev = x_from_prev ? 1u : 0u;
+    g.prev_rows = prev_rows;
+    g.tok = tok;
+    g.nproj = nproj;
+    g.j = j;
+    int rc = launch_mul_mat_q8_0_batch_gather(rows_local, K, NT, x, ldx, static_cast<const uint8_t*>(W), workspace,
+                                              g, flags, static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
+int ane_q8_batch_step_end_dev(const void* last, uint32_t rows, size_t ld, uint32_t ntok, uint32_t nproj,
+                              uint32_t* tok, void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK(last && tok && nproj > 0 && ld >= rows, "q8_batch_step_end: bad arguments");
+    int rc = launch_q8_chain_token_end(static_cast<const uint64_t*>(last), rows, ld, ntok, nproj, tok,
                                        static_cast<cudaStream_t>(stream));
     return rc ? rc : ok();
 }

@@ -66,10 +66,44 @@ __host__ __device__ constexpr size_t round_up256(size_t v) { return (v + 255) / 
 // Thread i = (block b, token t): ggml Q8_0 quantization of x[t][32b..32b+31]
 // (q8_quantize_words, the arithmetic of every other Q8_0 activation path here).
 // Blocks past nb in the last segment's record are never written nor read.
+//
+// GATHER (one link of a row-sharded chain, decode at batch NT): x is either the
+// plain fp32 input or, with x_from_prev, the previous projection's TAGGED output
+// on this GPU (token t's words at prev + t * ldw): all 16 two-word loads of a
+// block in flight, then the pairs without the previous projection's tag read
+// again together each round (bounded).  Block 0 also waits for one word per
+// rank of the previous projection's output: a rank's word proves that rank
+// has finished reading the vector the GEMM after this kernel overwrites.
+__device__ __forceinline__ uint4 ld_word2(const uint64_t* p) {
+    uint64_t a, b;
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+    return make_uint4((uint32_t)a, (uint32_t)(a >> 32), (uint32_t)b, (uint32_t)(b >> 32));
+}
+__device__ __forceinline__ bool wait_word(const uint64_t* p, uint32_t tag, int* err) {
+    const long long t0 = clock64();
+    while (true) {
+        uint64_t w;
+        asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+        if ((uint32_t)(w >> 32) == tag) return true;
+        if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
+            atomicAdd(err, 1);
+            return false;
+        }
+        __nanosleep(64);
+    }
+}
+
+template <bool GATHER>
 __global__ void quantize_x_segments_kernel(const float* __restrict__ x, size_t ldx, uint32_t NT, uint32_t nb,
-                                           uint8_t* __restrict__ records) {
+                                           uint8_t* __restrict__ records, const __grid_constant__ Q8BatchGather bg,
+                                           int* err) {
     ptx::griddep_launch_dependents();
     ptx::griddep_wait();  // x may come from the previous kernel; the records may still be read by it
+    uint32_t tag_in = 0;  // the previous projection's tag
+    if constexpr (GATHER) {
+        tag_in = *reinterpret_cast<const volatile uint32_t*>(bg.tok) * bg.nproj + bg.j;
+        if (blockIdx.x == 0 && threadIdx.x < bg.world) wait_word(bg.prev + (size_t)threadIdx.x * bg.prev_rows, tag_in, err);
+    }
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= nb * kTok) return;
     const uint32_t b = i / kTok, t = i % kTok;
@@ -85,14 +119,44 @@ __global__ void quantize_x_segments_kernel(const float* __restrict__ x, size_t l
         return;
     }
     float v[32];
-    const float4* xb = reinterpret_cast<const float4*>(x + (size_t)t * ldx + (size_t)b * 32);
+    if (GATHER && bg.x_from_prev) {
+        const uint64_t* blk = bg.prev + (size_t)t * bg.ldw + (size_t)b * 32;
+        uint32_t miss = 0;
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const float4 f = xb[k];
-        v[4 * k] = f.x;
-        v[4 * k + 1] = f.y;
-        v[4 * k + 2] = f.z;
-        v[4 * k + 3] = f.w;
+        for (int k = 0; k < 16; k++) {
+            const uint4 w = ld_word2(blk + 2 * k);
+            v[2 * k] = __uint_as_float(w.x);
+            v[2 * k + 1] = __uint_as_float(w.z);
+            miss |= (w.y != tag_in || w.w != tag_in) ? 1u << k : 0u;
+        }
+        const long long t0 = miss ? clock64() : 0;
+        while (miss) {
+            if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
+                atomicAdd(err, 1);
+                break;  // counted; the values are whatever was there
+            }
+            __nanosleep(64);
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                if (!((miss >> k) & 1u)) continue;
+                const uint4 w = ld_word2(blk + 2 * k);
+                if (w.y == tag_in && w.w == tag_in) {
+                    v[2 * k] = __uint_as_float(w.x);
+                    v[2 * k + 1] = __uint_as_float(w.z);
+                    miss &= ~(1u << k);
+                }
+            }
+        }
+    } else {
+        const float4* xb = reinterpret_cast<const float4*>(x + (size_t)t * ldx + (size_t)b * 32);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const float4 f = xb[k];
+            v[4 * k] = f.x;
+            v[4 * k + 1] = f.y;
+            v[4 * k + 2] = f.z;
+            v[4 * k + 3] = f.w;
+        }
     }
     uint32_t w[8];
     *scale = q8_quantize_words(v, w);
@@ -239,9 +303,11 @@ struct GemmQ8Args {
     uint32_t ngroups, nslots, flags;
 };
 
+template <bool GATHER>
 __global__ void __launch_bounds__(32 * (kMaxTiles * kMaxGroups + 1), 1)
     q8_0_gemm_q8_kernel(const __grid_constant__ CUtensorMap wmap8, const __grid_constant__ CUtensorMap wmap4,
-                        const uint8_t* __restrict__ records, const GemmQ8Args a, int* err) {
+                        const uint8_t* __restrict__ records, const GemmQ8Args a,
+                        const __grid_constant__ Q8BatchGather bg, int* err) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t T = a.ntiles, nslots = a.nslots, nseg = (a.nb + kSegBlocks - 1) / kSegBlocks;
     const uint32_t slot_bytes = kXSegBytes + T * kTileBytes;
@@ -321,6 +387,9 @@ __global__ void __launch_bounds__(32 * (kMaxTiles * kMaxGroups + 1), 1)
     }
     // ------------------------------------------------------------ compute
     ptx::griddep_wait();  // y may still be read by the kernel before this one
+    // GATHER: this projection's tag (the step count is final once the kernels
+    // before this one have ended)
+    const uint32_t tag_out = GATHER ? *reinterpret_cast<const volatile uint32_t*>(bg.tok) * bg.nproj + bg.j + 1u : 0u;
     const uint32_t cw = warp - 1, grp = cw / T, ti = cw % T;
     if (tiles == 0 || grp >= a.ngroups) return;
     const uint32_t g = lane >> 2, q = lane & 3;
@@ -364,7 +433,18 @@ __global__ void __launch_bounds__(32 * (kMaxTiles * kMaxGroups + 1), 1)
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 const uint32_t row = row0 + (k & 1), tok = g + 8 * (k >> 1);
-                if (2 * q + (k & 1) < rows && row < a.M && tok < a.NT) a.y[(size_t)tok * a.ldy + row] = v[k];
+                if (2 * q + (k & 1) < rows && row < a.M && tok < a.NT) {
+                    if constexpr (GATHER) {
+                        // one 8-byte {value, tag} word per rank: seen whole or not at all
+                        const uint64_t w = (uint64_t)__float_as_uint(v[k]) | ((uint64_t)tag_out << 32);
+                        for (uint32_t q8 = 0; q8 < bg.world; q8++)
+                            asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(bg.out[q8] + (size_t)tok * bg.ldw + row),
+                                         "l"(w)
+                                         : "memory");
+                    } else {
+                        a.y[(size_t)tok * a.ldy + row] = v[k];
+                    }
+                }
             }
         }
         __syncwarp();
@@ -379,15 +459,19 @@ size_t mul_mat_q8_0_batch_workspace_size(uint32_t M, uint32_t K) {
     return round_up256((size_t)((K / 32 + kSegBlocks - 1) / kSegBlocks) * kXSegBytes);
 }
 
-int launch_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const float* x, size_t ldx, const uint8_t* W,
-                              float* y, size_t ldy, void* workspace, uint32_t flags, cudaStream_t s) {
+namespace {
+
+// bg == nullptr: the plain MUL_MAT (x fp32, y fp32); else one chain link.
+int launch_batch_impl(uint32_t M, uint32_t K, uint32_t NT, const float* x, size_t ldx, const uint8_t* W, float* y,
+                      size_t ldy, void* workspace, uint32_t flags, cudaStream_t s, const Q8BatchGather* bg) {
     if (M == 0 || NT == 0) return ANE_OK;
     ANE_ARG_CHECK(NT <= kTok, "mul_mat_q8_0_batch: at most 16 activation rows");
     ANE_ARG_CHECK(K % 256 == 0 && K > 0, "mul_mat_q8_0_batch: K must be a positive multiple of 256");
     ANE_ARG_CHECK(((uintptr_t)W & 15) == 0, "mul_mat_q8_0_batch: W must be 16-byte aligned");
-    ANE_ARG_CHECK(((uintptr_t)x & 15) == 0 && (NT == 1 || ldx % 4 == 0) && ldx >= K,
-                  "mul_mat_q8_0_batch: x rows must be 16-byte aligned (ldx % 4 == 0, ldx >= K)");
-    ANE_ARG_CHECK(ldy >= M || NT == 1, "mul_mat_q8_0_batch: ldy < M");
+    if (!bg || !bg->x_from_prev)
+        ANE_ARG_CHECK(x && ((uintptr_t)x & 15) == 0 && (NT == 1 || ldx % 4 == 0) && ldx >= K,
+                      "mul_mat_q8_0_batch: x rows must be 16-byte aligned (ldx % 4 == 0, ldx >= K)");
+    if (!bg) ANE_ARG_CHECK(ldy >= M || NT == 1, "mul_mat_q8_0_batch: ldy < M");
     ANE_ARG_CHECK(workspace && ((uintptr_t)workspace & 255) == 0, "mul_mat_q8_0_batch: workspace must be 256-byte aligned");
     const uint32_t sms = (uint32_t)num_sms(), nb = K / 32, nseg = (nb + kSegBlocks - 1) / kSegBlocks;
     GemmQ8Args a;
@@ -432,13 +516,37 @@ int launch_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const float* 
                               kRows / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     uint8_t* records = static_cast<uint8_t*>(workspace);
-    const uint32_t nthreads = nb * kTok;
-    rc = launch_pdl(quantize_x_segments_kernel, dim3((nthreads + 255) / 256), dim3(256), 0, s, x, ldx, NT, nb, records);
+    const uint32_t nthreads = nb * kTok;  // blocks of 64: the activation spreads over more SMs
+    const Q8BatchGather none{};
+    if (!bg) {
+        rc = launch_pdl(quantize_x_segments_kernel<false>, dim3((nthreads + 63) / 64), dim3(64), 0, s, x, ldx, NT,
+                        nb, records, none, device_timeout_flag());
+        if (rc) return rc;
+        static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
+        if (int arc = set_max_dynamic_smem(q8_0_gemm_q8_kernel<false>, 227 * 1024, smem_set)) return arc;
+        return launch_pdl(q8_0_gemm_q8_kernel<false>, dim3(ctas), dim3(32 * (1 + a.ntiles * a.ngroups)), smem, s,
+                          wmap8, wmap4, (const uint8_t*)records, a, none, device_timeout_flag());
+    }
+    rc = launch_pdl(quantize_x_segments_kernel<true>, dim3((nthreads + 63) / 64), dim3(64), 0, s, x, ldx, NT, nb,
+                    records, *bg, device_timeout_flag());
     if (rc) return rc;
-    static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
-    if (int arc = set_max_dynamic_smem(q8_0_gemm_q8_kernel, 227 * 1024, smem_set)) return arc;
-    return launch_pdl(q8_0_gemm_q8_kernel, dim3(ctas), dim3(32 * (1 + a.ntiles * a.ngroups)), smem, s, wmap8, wmap4,
-                      (const uint8_t*)records, a, device_timeout_flag());
+    static std::atomic<uint64_t> smem_set_g{0};
+    if (int arc = set_max_dynamic_smem(q8_0_gemm_q8_kernel<true>, 227 * 1024, smem_set_g)) return arc;
+    return launch_pdl(q8_0_gemm_q8_kernel<true>, dim3(ctas), dim3(32 * (1 + a.ntiles * a.ngroups)), smem, s, wmap8,
+                      wmap4, (const uint8_t*)records, a, *bg, device_timeout_flag());
+}
+
+}  // namespace
+
+int launch_mul_mat_q8_0_batch(uint32_t M, uint32_t K, uint32_t NT, const float* x, size_t ldx, const uint8_t* W,
+                              float* y, size_t ldy, void* workspace, uint32_t flags, cudaStream_t s) {
+    return launch_batch_impl(M, K, NT, x, ldx, W, y, ldy, workspace, flags, s, nullptr);
+}
+
+int launch_mul_mat_q8_0_batch_gather(uint32_t M, uint32_t K, uint32_t NT, const float* x, size_t ldx,
+                                     const uint8_t* W, void* workspace, const Q8BatchGather& g, uint32_t flags,
+                                     cudaStream_t s) {
+    return launch_batch_impl(M, K, NT, x, ldx, W, nullptr, 0, workspace, flags, s, &g);
 }
 
 }  // namespace ane_b200

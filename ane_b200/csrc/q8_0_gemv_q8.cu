@@ -301,21 +301,51 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1)) q8_0_gemv_q8_kernel(co
     }
 }
 
-// Ends a token of a row-sharded chain: waits (bounded) until every word of the
-// last projection's vector on this GPU carries its tag (the gathered output is
-// complete here), then counts the token.  Launched in plain stream order: only
-// peers' words can still be missing.
-__global__ void q8_chain_token_end_kernel(const uint64_t* last, uint32_t len, uint32_t nproj, uint32_t* tok,
-                                          int* err) {
+// Ends a step of a row-sharded chain: waits (bounded) until every word of the
+// last projection's output on this GPU (ntok token rows of `rows` words, `ld`
+// apart) carries its tag (the gathered output is complete here), then counts
+// the step.  Launched in plain stream order: only peers' words can still be
+// missing.  Each of the grid's CTAs checks a slice (eight loads in flight per
+// thread, the words not there yet read again together each round); tok[1]
+// counts CTA arrivals over all steps, and the CTA that completes this step's
+// count bumps tok[0].
+constexpr uint32_t kEndThreads = 1024, kEndUnroll = 8, kEndMaxCtas = 32;
+__global__ void __launch_bounds__(kEndThreads) q8_chain_token_end_kernel(const uint64_t* last, uint32_t rows, size_t ld,
+                                                                         uint32_t ntok, uint32_t nproj, uint32_t* tok,
+                                                                         int* err) {
     __shared__ uint32_t t_s;
     if (threadIdx.x == 0) t_s = *reinterpret_cast<volatile uint32_t*>(tok);
     __syncthreads();
-    const uint32_t tag = t_s * nproj + nproj;
-    float v;
-    bool ok = true;  // a timed-out wait is counted; the token still ends
-    for (uint32_t i = threadIdx.x; i < len && ok; i += blockDim.x) ok = wait_tagged(last + i, tag, &v, err);
+    const uint32_t tag = t_s * nproj + nproj, n = rows * ntok;
+    const uint32_t stride = gridDim.x * kEndThreads;
+    for (uint32_t base = blockIdx.x * kEndThreads + threadIdx.x; base < n; base += stride * kEndUnroll) {
+        uint32_t miss = 0;
+#pragma unroll
+        for (uint32_t u = 0; u < kEndUnroll; u++) {
+            const uint32_t i = base + u * stride;
+            if (i < n && (uint32_t)(ld_tagged(last + (size_t)(i / rows) * ld + i % rows) >> 32) != tag) miss |= 1u << u;
+        }
+        const long long t0 = miss ? clock64() : 0;
+        while (miss) {
+            if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
+                atomicAdd(err, 1);  // counted; the step still ends
+                break;
+            }
+            __nanosleep(64);
+#pragma unroll
+            for (uint32_t u = 0; u < kEndUnroll; u++) {
+                const uint32_t i = base + u * stride;
+                if (((miss >> u) & 1u) &&
+                    (uint32_t)(ld_tagged(last + (size_t)(i / rows) * ld + i % rows) >> 32) == tag)
+                    miss &= ~(1u << u);
+            }
+        }
+    }
     __syncthreads();
-    if (threadIdx.x == 0) *tok = t_s + 1u;
+    if (threadIdx.x == 0) {
+        const uint32_t prev = atomicAdd(tok + 1, 1u);
+        if (prev + 1u == (t_s + 1u) * gridDim.x) *reinterpret_cast<volatile uint32_t*>(tok) = t_s + 1u;
+    }
 }
 
 }  // namespace
@@ -411,8 +441,13 @@ int launch_mul_mat_q8_0_gather(uint32_t M, uint32_t K, const float* x, const uin
     return launch_gemv_q8<true, true>(M, K, reinterpret_cast<const uint8_t*>(xs), W, nullptr, nullptr, flags, s, &g);
 }
 
-int launch_q8_chain_token_end(const uint64_t* last, uint32_t len, uint32_t nproj, uint32_t* tok, cudaStream_t s) {
-    q8_chain_token_end_kernel<<<1, 256, 0, s>>>(last, len, nproj, tok, device_timeout_flag());
+int launch_q8_chain_token_end(const uint64_t* last, uint32_t rows, size_t ld, uint32_t ntok, uint32_t nproj,
+                              uint32_t* tok, cudaStream_t s) {
+    // one grid size per chain (the arrival count assumes it): set by the words to check
+    const uint32_t n = rows * ntok, per = kEndThreads * kEndUnroll;
+    const uint32_t ctas = (n + per - 1) / per < kEndMaxCtas ? (n + per - 1) / per : kEndMaxCtas;
+    q8_chain_token_end_kernel<<<ctas ? ctas : 1, kEndThreads, 0, s>>>(last, rows, ld, ntok, nproj, tok,
+                                                                      device_timeout_flag());
     ANE_CHECK_LAUNCH();
     return ANE_OK;
 }

@@ -350,3 +350,91 @@ class PeerChainDecodeStack:
         for b in self._opened:
             self._ane.lib.ane_ipc_close_handle(b)
         self._opened = []
+
+
+# ------------------------------------------- batch > 1: the same chain, batched
+class PeerBatchDecodeStack:
+    """The weights and inputs of a batch-NT (NT <= 16) mode-Q DecodeStack run
+    as one batched MUL_MAT per projection (ane_mul_mat_q8_0_batch_gather_dev:
+    the activation quantize launch and the GEMM launch) whose outputs go
+    straight into every rank's next vector over NVLink -- no NCCL call -- plus
+    one step-end launch; the whole step captures into a CUDA graph.
+
+    Per rank one zeroed buffer holds two TAGGED vectors of NT token rows
+    (8-byte {fp32 value, u32 tag} words, row stride ldw; projection j writes
+    vector j % 2) and the step count; the other ranks' buffers are mapped with
+    CUDA IPC.  Each projection also waits for one word per rank of the
+    previous projection, so a fast rank never overwrites a vector a slow one
+    still reads.
+    """
+
+    def __init__(self, stack: DecodeStack, device, group=None):
+        import ctypes
+
+        import ane_b200 as ane
+
+        if stack.batch == 1:
+            raise ValueError("batch 1 runs as PeerChainDecodeStack or FusedDecodeStack")
+        self._ane, self.stack = ane, stack
+        world, rank, NT = stack.world, stack.rank, stack.batch
+        ldw = (stack.h[0].shape[1] + 1) // 2 * 2
+        vec_bytes = (NT * ldw * 8 + 255) // 256 * 256
+        tok_off = 2 * vec_bytes
+        self.block = torch.zeros(tok_off + 256, dtype=torch.uint8, device=device)
+        base = self.block.data_ptr()
+        self._opened = []
+        peer = [0] * world
+        peer[rank] = base
+        if world > 1:
+            handle = (ctypes.c_uint8 * 64)()
+            off = ctypes.c_uint64()
+            ane.check(ane.lib.ane_ipc_get_handle(base, handle, ctypes.byref(off)))
+            everyone = [None] * world
+            dist.all_gather_object(everyone, (bytes(handle), off.value), group=group)
+            for r in range(world):
+                if r == rank:
+                    continue
+                h = (ctypes.c_uint8 * 64).from_buffer_copy(everyone[r][0])
+                b = ctypes.c_void_p()
+                ane.check(ane.lib.ane_ipc_open_handle(h, ctypes.byref(b)))
+                self._opened.append(b.value)
+                peer[r] = b.value + everyone[r][1]
+        self._tok = base + tok_off
+        projs = [(layer, p, M, K) for layer in range(stack.layers) for p, (_, M, K) in enumerate(stack.shapes)]
+        self.nproj = len(projs)
+        self._ws = {}
+        self._calls = []
+        for j, (layer, p, M, K) in enumerate(projs):
+            rows = M // world
+            jp = (j - 1) % self.nproj  # the previous projection (of the previous step for j = 0)
+            prev = base + (jp % 2) * vec_bytes
+            chained = p != 0
+            x = stack.inputs[layer]
+            if (rows, K) not in self._ws:
+                self._ws[(rows, K)] = ane.mul_mat_q8_0_batch_workspace(rows, K, device)
+            outs = (ctypes.c_void_p * world)(*[q + (j % 2) * vec_bytes + 8 * rank * rows for q in peer])
+            self._calls.append((rows, K, 0 if chained else x.data_ptr(), x.stride(0), stack.weights[layer][p].data_ptr(),
+                                self._ws[(rows, K)].data_ptr(), outs, prev, int(chained), projs[jp][2] // world, j))
+        self._ldw, self._NT = ldw, NT
+        last_M = stack.shapes[-1][1]
+        self._last = base + ((self.nproj - 1) % 2) * vec_bytes
+        self._last_rows = last_M
+        words = self.block[:tok_off].view(torch.float32).view(2, vec_bytes // 8, 2)
+        # values of the last output, [NT, last_M]
+        self.out = words[(self.nproj - 1) % 2, :NT * ldw, 0].view(NT, ldw)[:, :last_M]
+
+    def forward(self, stream=None) -> torch.Tensor:
+        ane, world = self._ane, self.stack.world
+        s = ane._stream_ptr(stream)
+        for rows, K, x, ldx, W, ws, outs, prev, chained, prev_rows, j in self._calls:
+            ane.check(ane.lib.ane_mul_mat_q8_0_batch_gather_dev(rows, K, self._NT, x or None, ldx, W, ws, world, outs,
+                                                                self._ldw, prev, chained, prev_rows, self._tok,
+                                                                self.nproj, j, ane.WEIGHTS_STATIC, s))
+        ane.check(ane.lib.ane_q8_batch_step_end_dev(self._last, self._last_rows, self._ldw, self._NT, self.nproj,
+                                                    self._tok, s))
+        return self.out
+
+    def close(self):
+        for b in self._opened:
+            self._ane.lib.ane_ipc_close_handle(b)
+        self._opened = []

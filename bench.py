@@ -509,12 +509,22 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
     b16_graph = g16 is not None
     b16_ms = timed(g16.replay if b16_graph else stack16.forward)
     del g16
+    # batch 16 with the outputs going straight into every rank's next vector
+    peer16 = decode.PeerBatchDecodeStack(stack16, dev, group=group)
+    peer16.forward()
+    torch.cuda.synchronize()
+    gp16 = capture(peer16.forward)
+    p16_graph = gp16 is not None
+    p16_ms = timed(gp16.replay if p16_graph else peer16.forward)
+    del gp16
+    torch.cuda.synchronize()
     parity = None
     if world > 1:
         # the last layer's outputs of the sharded run against one GPU computing
         # that layer alone (each layer starts from its own seeded input)
         outs = {"chain_q": stack.forward().clone(), "mode_r": stack_r.forward().clone(),
-                "batch16": stack16.forward().clone(), "peer_q": peer.forward().clone()}
+                "batch16": stack16.forward().clone(), "peer_q": peer.forward().clone(),
+                "batch16_peer": peer16.forward().clone()}
         fused2 = decode.FusedDecodeStack(stack, dev, group=group)
         try:
             outs["fused_q"] = fused2.forward().clone()
@@ -526,8 +536,9 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
             one = decode.gpu_stack(1, dev, first_layer=layers - 1)
             one_r = decode.gpu_stack(1, dev, first_layer=layers - 1, weights=one.weights, mode="r")
             one16 = decode.gpu_stack(1, dev, first_layer=layers - 1, weights=one.weights, batch=batch)
+            ref16 = one16.forward()
             refs = {"chain_q": one.forward(), "fused_q": one.forward(), "mode_r": one_r.forward(),
-                    "batch16": one16.forward(), "peer_q": one.forward()}
+                    "batch16": ref16, "peer_q": one.forward(), "batch16_peer": ref16}
             torch.cuda.synchronize()
             parity = {k: bool(torch.equal(outs[k].view(torch.int32), refs[k].view(torch.int32))) for k in outs}
             del one, one_r, one16, refs
@@ -536,6 +547,7 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
     if group is not None:
         torch.distributed.barrier(group)  # no rank unmaps a peer buffer while a peer still writes it
     peer.close()
+    peer16.close()
     del stack16, stack_r
     wbytes = decode.stack_weight_bytes(layers)
     peaks = load_peaks()
@@ -559,15 +571,26 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
                                 "arithmetic)" + ("" if world == 1 else " + NCCL all-gather each")
                                 + (" in a CUDA graph" if r_graph else " (eager)"))},
             "parity_ok_vs_1gpu": parity,
-            "batch16": {"ms_per_step": b16_ms, "tokens_per_s": batch / (b16_ms * 1e-3),
-                        "weight_gbs": wbytes / (b16_ms * 1e-3) / 1e9,
-                        "per_gpu_hbm_frac": wbytes / (b16_ms * 1e-3) / 1e9 / world / peaks["hbm_gbs"],
-                        "path": (f"{4 * layers} x (activation quantize + batched MUL_MAT) launches"
-                                 + ("" if world == 1 else " + NCCL all-gather each")
-                                 + (" in a CUDA graph" if b16_graph else " (eager)"))},
+            "batch16": batch16_line(batch, wbytes, world, peaks, layers, b16_ms, b16_graph, p16_ms, p16_graph),
             "activation": "Q8_0 (ggml convention), static weights",
             "timing": f"{reps} tokens each path, CUDA events" + ("" if world == 1 else ", max over ranks"),
             "build_s": build_s}
+
+
+def batch16_line(batch, wbytes, world, peaks, layers, nccl_ms, nccl_graph, peer_ms, peer_graph):
+    """The batch-16 decode numbers: the better of the NCCL-gathered chain and
+    the chain whose outputs go to every rank by peer stores, with both times."""
+    nccl_path = (f"{4 * layers} x (activation quantize + batched MUL_MAT) launches"
+                 + ("" if world == 1 else " + NCCL all-gather each")
+                 + (" in a CUDA graph" if nccl_graph else " (eager)"))
+    peer_path = (f"{4 * layers} x (activation quantize from the tagged vector + batched MUL_MAT storing "
+                 + ("every rank's next vector by NVLink peer stores" if world > 1 else "the next tagged vector")
+                 + ") launches + a step-end launch" + (", a CUDA graph per step" if peer_graph else " (eager)"))
+    ms, path = min((nccl_ms, nccl_path), (peer_ms, peer_path))
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    return {"ms_per_step": ms, "tokens_per_s": batch / (ms * 1e-3), "weight_gbs": gbs,
+            "per_gpu_hbm_frac": gbs / world / peaks["hbm_gbs"], "path": path,
+            "nccl_ms_per_step": nccl_ms, "peer_ms_per_step": peer_ms}
 
 
 def as_graph(torch, fn, keep):

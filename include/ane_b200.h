@@ -294,8 +294,10 @@ int ane_mul_mat_q8_0_batch_dev(uint32_t M, uint32_t K, uint32_t NT, const float*
  * j = 0, `prev` is the previous token's last vector (tag t*nproj; all zero
  * before the first token).  ane_q8_chain_token_end_dev waits until the `len`
  * words of the last vector carry tag t*nproj + nproj (the gathered output is
- * then complete on this GPU) and bumps *tok.  Vectors and tok start zeroed;
- * every rank makes the same calls.  No counterpart in the reference (its ggml
+ * then complete on this GPU) and bumps *tok.  tok points at two uint32 words
+ * (the count, then the token-end launch's arrival count); vectors and both
+ * words start zeroed; every rank makes the same calls, with the same `len`
+ * every token.  No counterpart in the reference (its ggml
  * backend issues one synchronous q8_0_gemv per MUL_MAT). */
 uint32_t ane_mul_mat_q8_0_ctas(uint32_t rows_local, uint32_t K);
 int ane_mul_mat_q8_0_gather_dev(uint32_t rows_local, uint32_t K, const float* x, const void* W, uint32_t world,
@@ -303,6 +305,30 @@ int ane_mul_mat_q8_0_gather_dev(uint32_t rows_local, uint32_t K, const float* x,
                                 uint32_t prev_ctas, const uint32_t* tok, uint32_t nproj, uint32_t j, uint32_t flags,
                                 void* stream);
 int ane_q8_chain_token_end_dev(const void* last, uint32_t len, uint32_t nproj, uint32_t* tok, void* stream);
+
+/* The same chain at batch NT <= 16 (decode of NT tokens per step), each link
+ * being ane_mul_mat_q8_0_batch_dev's MUL_MAT (bit for bit): a vector holds NT
+ * token rows of ldw tagged words (ldw even, >= every rank's rows and every K).
+ * Output (token t, local row r) goes to out_ranks[q] + t*ldw + r on every rank
+ * q (out_ranks[q] = rank q's vector at this rank's first row).  x_from_prev:
+ * token t's activation is prev[t*ldw + 0..K) (prev = this GPU's vector of the
+ * previous projection, 16-byte aligned), else the fp32 rows x (row stride
+ * ldx).  Before any output is stored, the word prev[q * prev_rows] (rank q's
+ * first row of the previous projection, token 0) must carry the previous
+ * projection's tag for every rank q: a rank that has stored it has finished
+ * reading the vector this call overwrites.  Tags: projection j of step s
+ * (s = *tok) stores s*nproj + j + 1.  ane_q8_batch_step_end_dev waits until
+ * the last projection's `rows` words of each of `ntok` token rows (`ld` words
+ * apart) carry tag s*nproj + nproj, then bumps *tok (two zeroed uint32 words,
+ * as for the batch-1 chain; the same rows and ntok every step).  workspace as for
+ * ane_mul_mat_q8_0_batch_dev; flags: ANE_Q8_WEIGHTS_STATIC.  No counterpart
+ * in the reference. */
+int ane_mul_mat_q8_0_batch_gather_dev(uint32_t rows_local, uint32_t K, uint32_t NT, const float* x, size_t ldx,
+                                      const void* W, void* workspace, uint32_t world, void* const* out_ranks,
+                                      size_t ldw, const void* prev, uint32_t x_from_prev, uint32_t prev_rows,
+                                      const uint32_t* tok, uint32_t nproj, uint32_t j, uint32_t flags, void* stream);
+int ane_q8_batch_step_end_dev(const void* last, uint32_t rows, size_t ld, uint32_t ntok, uint32_t nproj,
+                              uint32_t* tok, void* stream);
 
 /* The same chain (batch 1, Q8_0 activation, as ane_mul_mat_q8_0_dev)
  * in ONE persistent cooperative launch, row-sharded over `world` GPUs.

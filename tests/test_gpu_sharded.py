@@ -103,10 +103,10 @@ def _stack_worker(rank, world, port, layers, result_q):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
-    fused = peer = None
+    fused = peer = peer16 = None
     try:
         import ane_b200 as ane
-        from ane_b200.decode import FusedDecodeStack, PeerChainDecodeStack, gpu_stack
+        from ane_b200.decode import FusedDecodeStack, PeerBatchDecodeStack, PeerChainDecodeStack, gpu_stack
 
         sharded = gpu_stack(layers, dev, world=world, rank=rank, seed=33)
         nccl_out = sharded.forward().clone()            # NCCL all-gather per projection
@@ -118,16 +118,23 @@ def _stack_worker(rank, world, port, layers, result_q):
         torch.cuda.synchronize()
         ok = torch.equal(nccl_out.view(torch.int32), single.view(torch.int32)) and all(
             torch.equal(o.view(torch.int32), single.view(torch.int32)) for o in outs)
+        # batch 16: the batched chain with peer stores == the 1-GPU batched stack
+        sharded16 = gpu_stack(layers, dev, world=world, rank=rank, seed=33, batch=16)
+        peer16 = PeerBatchDecodeStack(sharded16, dev)
+        outs16 = [peer16.forward().clone() for _ in range(3)]
+        single16 = gpu_stack(layers, dev, world=1, rank=0, seed=33, batch=16).forward()
+        torch.cuda.synchronize()
+        ok = ok and all(torch.equal(o.view(torch.int32), single16.view(torch.int32)) for o in outs16)
         ok = ok and ane.lib.ane_device_timeouts() == 0
         flags = torch.tensor([1 if ok else 0], device=dev)
         dist.all_reduce(flags, op=dist.ReduceOp.MIN)
         if rank == 0:
             result_q.put(int(flags.item()))
     finally:
-        if fused is not None or peer is not None:
+        if fused is not None or peer is not None or peer16 is not None:
             torch.cuda.synchronize()
             dist.barrier()  # no rank unmaps a peer buffer while a peer still writes it
-            for s in (fused, peer):
+            for s in (fused, peer, peer16):
                 if s is not None:
                     s.close()
         dist.destroy_process_group()
@@ -137,7 +144,8 @@ def test_decode_stack_two_gpus_fused_and_nccl_equal_one_gpu():
     """Config-5 decode stack (2 layers) row-sharded over 2 GPUs: the NCCL
     all-gather version, the one-launch peer-store version and the
     launch-per-projection peer-store chain all give the 1-GPU vector bit for
-    bit, on repeated tokens."""
+    bit, on repeated tokens; so does the batch-16 chain of batched MUL_MATs
+    with peer stores."""
     import torch
 
     if torch.cuda.device_count() < 2:
