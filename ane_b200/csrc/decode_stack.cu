@@ -42,7 +42,7 @@
 namespace ane_b200 {
 
 constexpr uint32_t kStackMaxRanks = 8;
-constexpr uint32_t kStackWarps = 16;  // compute warps per CTA
+constexpr uint32_t kStackWarps = 15;  // compute warps per CTA: 16 warps in all, so 128 registers each
 
 struct alignas(64) StackProj {
     CUtensorMap wmap;               // this rank's rows of W as a 2-D uint32 tensor

@@ -64,7 +64,8 @@ def parse():
     p.add_argument("--profile-case", default=None,
                    help="profiling aid: run one kernel on one small case --steps times and exit, no JSON line. "
                         "dense:<n> (dense_fused_i8 n^3), q8r:<M>x<K> (q8_0_gemv, fp32 x), q8q:<M>x<K> "
-                        "(MUL_MAT, Q8_0 x), kq:<fmt>:<M>x<K> (K-quant matvec), b16:<M>x<K> (batched MUL_MAT)")
+                        "(MUL_MAT, Q8_0 x), kq:<fmt>:<M>x<K> (K-quant matvec), b16:<M>x<K> (batched MUL_MAT), "
+                        "stack:<layers> (config-5 decode stack as the persistent megakernel)")
     return p.parse_args()
 
 
@@ -79,6 +80,7 @@ def run_profile_case(args):
     torch.cuda.set_device(dev)
     kind, _, rest = args.profile_case.partition(":")
     g = torch.Generator(device=dev).manual_seed(7)
+    closer = None
     if kind == "dense":
         n = int(rest)
         A = torch.randn((n, n), device=dev, generator=g)
@@ -86,6 +88,12 @@ def run_profile_case(args):
         C = torch.empty((n, n), device=dev)
         ws = ane.dense_fused_i8_workspace(n, n, n, dev)
         fn = lambda: ane.dense_fused_i8(A, B, 1.0, False, out=C, workspace=ws)  # noqa: E731
+    elif kind == "stack":
+        # config-5 decode stack of `rest` layers as the persistent megakernel (1 GPU)
+        from ane_b200 import decode
+
+        fused = decode.FusedDecodeStack(decode.gpu_stack(int(rest), dev), dev)
+        fn, closer = fused.forward, fused.close
     else:
         fmt = None
         if kind == "kq":
@@ -121,6 +129,8 @@ def run_profile_case(args):
         fn()
     torch.cuda.synchronize()
     assert ane.lib.ane_device_timeouts() == 0
+    if closer is not None:
+        closer()
     print(f"profile case {args.profile_case}: {args.warmup} + {args.steps} calls done", flush=True)
 
 
@@ -610,12 +620,22 @@ def as_graph(torch, fn, keep):
     return g.replay
 
 
+def make_flush(torch, dev):
+    """L2 flush buffers: 256 MiB written, then another 256 MiB read, before every
+    timed step.  The read evicts the dirty lines the write leaves (their write-back
+    happens before the step, not inside it) and leaves L2 holding clean lines
+    the step does not use."""
+    return torch.empty(2 * 64 * 1024 * 1024, dtype=torch.float32, device=dev)
+
+
 def timed_steps_flushed(torch, fn, steps, stream, flush):
-    """Mean device ms of fn() with the L2 flushed (a 256 MiB write) before every
-    step; only fn() sits between the events."""
+    """Mean device ms of fn() with the L2 flushed (make_flush) before every step;
+    only fn() sits between the events."""
     total = 0.0
+    half = flush.numel() // 2
     for _ in range(steps):
-        flush.zero_()
+        flush[:half].zero_()
+        flush[half:].sum()
         s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s_ev.record(stream)
         fn()
@@ -629,7 +649,7 @@ def config_legs(ane, torch, dev, steps=20):
     """Configs 1, 2 (size sweep) and 4 of BASELINE.json at 1 GPU, each step with
     the L2 flushed first (small inputs would otherwise be served from L2)."""
     stream = torch.cuda.current_stream()
-    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    flush = make_flush(torch, dev)
     out = {}
     # ---- config 1: MNIST-MLP forward (784 -> 128 ReLU -> 10), batch 50
     g = torch.Generator(device=dev).manual_seed(1)
@@ -665,7 +685,7 @@ def config_legs(ane, torch, dev, steps=20):
     host_ms = (time.perf_counter() - t0) * 1e3 / steps
     out["config1_mnist_forward"] = {"us_device": ms * 1e3, "samples_per_s_device": 50 / (ms * 1e-3),
                                     "us_host_entry": host_ms * 1e3, "ops": ops,
-                                    "timing": "two dense_fused_i8 calls per forward, L2 flushed before each "
+                                    "timing": "two dense_fused_i8 calls per forward, L2 flushed (256 MiB write, then 256 MiB read) before each "
                                               "forward; host entry = wall clock of the synchronous C calls on pinned "
                                               "host buffers"}
     del A, W1, W2, h, y
@@ -703,7 +723,8 @@ def config_legs(ane, torch, dev, steps=20):
         cfg4[str(m)] = {"tops": 2.0 * m * 14336 * 4096 / (ms * 1e-3) / 1e12, "ms": ms,
                         "gbs": nbytes / (ms * 1e-3) / 1e9, "bytes": nbytes}
         del A, C, ws
-    cfg4["timing"] = "one step = a CUDA graph replay of the dense_fused_i8 call, L2 flushed before each"
+    cfg4["timing"] = ("one step = a CUDA graph replay of the dense_fused_i8 call, L2 flushed (256 MiB write, then "
+                      "256 MiB read) before each")
     out["config4_projection"] = cfg4
     del B, flush
     return out
@@ -717,7 +738,7 @@ def config4_sharded(ane, torch, dev, world, group, steps=20):
     from ane_b200 import sharded
 
     stream = torch.cuda.current_stream()
-    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    flush = make_flush(torch, dev)
     rank = torch.distributed.get_rank(group)
     n_local = 14336 // world
     g = torch.Generator(device=dev).manual_seed(4)
@@ -762,7 +783,7 @@ def config4_sharded(ane, torch, dev, world, group, steps=20):
     del flush, B_local, B
     return {"config4_projection_sharded": {"n_gpus": world, "shard": f"cols, 14336/{world} per rank", **out,
                                            "timing": "one step = a CUDA graph replay (no NCCL call in the "
-                                                     "step), L2 flushed before each, max over ranks",
+                                                     "step), L2 flushed (256 MiB write, then 256 MiB read) before each, max over ranks",
                                            "parity_ok_vs_1gpu": parity if rank == 0 else None}}
 
 
