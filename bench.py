@@ -628,14 +628,19 @@ def make_flush(torch, dev):
     return torch.empty(2 * 64 * 1024 * 1024, dtype=torch.float32, device=dev)
 
 
-def timed_steps_flushed(torch, fn, steps, stream, flush):
+def timed_steps_flushed(torch, fn, steps, stream, flush, group=None):
     """Mean device ms of fn() with the L2 flushed (make_flush) before every step;
-    only fn() sits between the events."""
+    only fn() sits between the events.  With a process group, a one-element
+    all-reduce after the flush lines the ranks' streams up, so a step that waits
+    for the other ranks does not also time how far apart their flushes ended."""
     total = 0.0
     half = flush.numel() // 2
+    align = torch.zeros(1, device=flush.device) if group is not None else None
     for _ in range(steps):
         flush[:half].zero_()
         flush[half:].sum()
+        if align is not None:
+            torch.distributed.all_reduce(align, group=group)
         s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s_ev.record(stream)
         fn()
@@ -717,7 +722,10 @@ def config_legs(ane, torch, dev, steps=20):
         for _ in range(3):
             f()
         graphs = []
-        ms = timed_steps_flushed(torch, as_graph(torch, f, graphs), steps, stream, flush)
+        step = as_graph(torch, f, graphs)
+        step()  # the graph's first launch (uploads it) stays out of the timed steps
+        torch.cuda.synchronize()
+        ms = timed_steps_flushed(torch, step, steps, stream, flush)
         del graphs
         nbytes = 9 * (4096 * m + 4096 * 14336) + 4 * m * 14336
         cfg4[str(m)] = {"tops": 2.0 * m * 14336 * 4096 / (ms * 1e-3) / 1e12, "ms": ms,
@@ -758,8 +766,10 @@ def config4_sharded(ane, torch, dev, world, group, steps=20):
         # the fused path makes no NCCL call: the step captures into a CUDA graph
         graphs = []
         step = as_graph(torch, f, graphs) if ctx.fused is not None and ctx._coop else f
+        step()  # the graph's first launch (uploads it) stays out of the timed steps
+        torch.cuda.synchronize()
         torch.distributed.barrier(group)
-        ms = timed_steps_flushed(torch, step, steps, stream, flush)
+        ms = timed_steps_flushed(torch, step, steps, stream, flush, group)
         del graphs
         t = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=group)
@@ -783,7 +793,9 @@ def config4_sharded(ane, torch, dev, world, group, steps=20):
     del flush, B_local, B
     return {"config4_projection_sharded": {"n_gpus": world, "shard": f"cols, 14336/{world} per rank", **out,
                                            "timing": "one step = a CUDA graph replay (no NCCL call in the "
-                                                     "step), L2 flushed (256 MiB write, then 256 MiB read) before each, max over ranks",
+                                                     "step), L2 flushed (256 MiB write, then 256 MiB read) and the "
+                                                     "ranks lined up (a one-element all-reduce) before each, max "
+                                                     "over ranks",
                                            "parity_ok_vs_1gpu": parity if rank == 0 else None}}
 
 
