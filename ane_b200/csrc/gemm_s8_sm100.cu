@@ -60,7 +60,10 @@ struct Barriers {
     uint64_t tmem_empty[2];
     uint32_t tmem_base;
 };
-constexpr size_t S_SMEM = (size_t)S_STAGES * S_STAGE + EPI_BYTES + sizeof(Barriers<S_STAGES>) + 1024;
+// The 1-CTA kernel's operand region holds S_STAGES full stages; with a small M
+// its stages are smaller (A tiles of round_up(M, 8) rows) and more of them fit.
+constexpr int S_OPS = S_STAGES * S_STAGE, S_MAX_STAGES = 16;
+constexpr size_t S_SMEM = (size_t)S_OPS + EPI_BYTES + sizeof(Barriers<S_MAX_STAGES>) + 1024;
 constexpr size_t P_SMEM = (size_t)P_STAGES * P_STAGE + EPI_BYTES + sizeof(Barriers<P_STAGES>) + 1024;
 static_assert(S_SMEM <= 232448 && P_SMEM <= 232448, "shared memory budget");
 
@@ -73,6 +76,10 @@ constexpr uint32_t P_BN_COLS = 256;  // pair tile width (= P_BN)
 struct Params {
     uint32_t M, N, K;
     uint32_t tiles_m, tiles_n, num_kb;
+    uint32_t s_bn;  // 1-CTA kernel: columns per tile (256; 128 or 64 for an MN-major B when few tiles)
+    // 1-CTA kernel ring: A tile rows loaded per stage (128, or round_up(M, 8) for
+    // M < 128), stages, bytes of an A and a B tile, offset of the B tiles
+    uint32_t s_am, s_stages, s_a_bytes, s_b_bytes, s_b_base;
     void* C;
     size_t ldc;
     int vec_ok;  // C rows allow 16-byte stores
@@ -231,22 +238,32 @@ __device__ __forceinline__ void drain_accumulator(const Params& p, uint32_t tadd
 
 // ------------------------------------------------------------ 1-CTA kernel
 // BKN: B is given as the codes stored K x N (MN-major operand) instead of N x K.
+// With an MN-major B a tile may be 128 or 64 columns wide (p.s_bn): for small
+// M the 256-column tiles would leave most SMs idle, each busy one streaming the
+// whole K alone.  128 columns: one SWIZZLE_128B box; 64: one SWIZZLE_64B box
+// (tmap_b64).
 template <bool BKN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_s8_single_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                          const Params p) {
+                          const __grid_constant__ CUtensorMap tmap_b64, const Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // All A tiles first (stage i at i * s_a_bytes), then the B tiles.  The MMA
+    // reads 128 A rows from each A tile; with fewer rows loaded the rest are
+    // other stages' (or not yet written) bytes that only reach accumulator
+    // rows >= M, which are never stored.  s_b_base leaves 16 KB after the last A
+    // tile, so those reads stay inside the operand region.
     uint8_t* sa = smem;
-    uint8_t* sb = smem + (size_t)S_STAGES * S_A;
-    uint32_t* epi = reinterpret_cast<uint32_t*>(smem + (size_t)S_STAGES * S_STAGE);
-    auto* bars = reinterpret_cast<Barriers<S_STAGES>*>(smem + (size_t)S_STAGES * S_STAGE + EPI_BYTES);
+    uint8_t* sb = smem + p.s_b_base;
+    uint32_t* epi = reinterpret_cast<uint32_t*>(smem + (size_t)S_OPS);
+    auto* bars = reinterpret_cast<Barriers<S_MAX_STAGES>*>(smem + (size_t)S_OPS + EPI_BYTES);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t num_tiles = p.tiles_m * p.tiles_n;
+    const uint32_t nstages = p.s_stages;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S_STAGES; s++) {
+        for (uint32_t s = 0; s < nstages; s++) {
             ptx::mbar_init(&bars->full[s], 1);
             ptx::mbar_init(&bars->empty[s], 1);
         }
@@ -256,7 +273,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         ptx::fence_mbarrier_init();
         ptx::prefetch_tmap(&tmap_a);
-        ptx::prefetch_tmap(&tmap_b);
+        ptx::prefetch_tmap(BKN && p.s_bn == 64 ? &tmap_b64 : &tmap_b);
     }
     if (warp == 1) {
         ptx::tmem_alloc(&bars->tmem_base, TMEM_COLS);
@@ -275,27 +292,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) {
             uint32_t stage = 0, phase = 0;
             bool alive = true;
+            const uint32_t bn = BKN ? p.s_bn : (uint32_t)S_BN;
             for (uint32_t t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
-                const int m0 = (int)((t / p.tiles_n) * S_BM), n0 = (int)((t % p.tiles_n) * S_BN);
+                const int m0 = (int)((t / p.tiles_n) * S_BM), n0 = (int)((t % p.tiles_n) * bn);
                 for (uint32_t kb = 0; kb < p.num_kb; kb++) {
                     if (!ptx::mbar_wait(&bars->empty[stage], phase ^ 1, p.err)) { alive = false; break; }
-                    ptx::mbar_arrive_expect_tx(&bars->full[stage], S_STAGE);
-                    ptx::tma_load_2d(sa + (size_t)stage * S_A, &tmap_a, &bars->full[stage], (int)(kb * BK), m0);
+                    ptx::mbar_arrive_expect_tx(&bars->full[stage], p.s_a_bytes + p.s_b_bytes);
+                    ptx::tma_load_2d(sa + (size_t)stage * p.s_a_bytes, &tmap_a, &bars->full[stage], (int)(kb * BK), m0);
                     if constexpr (BKN) {
-                        // two 128-column SWIZZLE_128B boxes, one N atom each (16 KB apart)
-                        ptx::tma_load_2d(sb + (size_t)stage * S_B, &tmap_b, &bars->full[stage], n0, (int)(kb * BK));
-                        ptx::tma_load_2d(sb + (size_t)stage * S_B + kMnAtomBytes, &tmap_b, &bars->full[stage],
-                                         n0 + 128, (int)(kb * BK));
+                        if (bn == 64) {
+                            ptx::tma_load_2d(sb + (size_t)stage * p.s_b_bytes, &tmap_b64, &bars->full[stage], n0,
+                                             (int)(kb * BK));
+                        } else {
+                            // 128-column SWIZZLE_128B boxes, one N atom each (16 KB apart)
+                            ptx::tma_load_2d(sb + (size_t)stage * p.s_b_bytes, &tmap_b, &bars->full[stage], n0,
+                                             (int)(kb * BK));
+                            if (bn == 256)
+                                ptx::tma_load_2d(sb + (size_t)stage * p.s_b_bytes + kMnAtomBytes, &tmap_b, &bars->full[stage],
+                                                 n0 + 128, (int)(kb * BK));
+                        }
                     } else {
-                        ptx::tma_load_2d(sb + (size_t)stage * S_B, &tmap_b, &bars->full[stage], (int)(kb * BK), n0);
+                        ptx::tma_load_2d(sb + (size_t)stage * p.s_b_bytes, &tmap_b, &bars->full[stage], (int)(kb * BK), n0);
                     }
-                    if (++stage == S_STAGES) { stage = 0; phase ^= 1; }
+                    if (++stage == nstages) { stage = 0; phase ^= 1; }
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = ptx::idesc_i8(S_BM, S_BN, !p.ep.a_unsigned, !p.ep.b_unsigned) |
+            const uint32_t bn = BKN ? p.s_bn : (uint32_t)S_BN;
+            const uint32_t brow = bn < 128 ? bn : 128u;  // bytes per K row of a B atom
+            const uint32_t idesc = ptx::idesc_i8(S_BM, (int)bn, !p.ep.a_unsigned, !p.ep.b_unsigned) |
                                    (BKN ? ptx::kIdescBMnMajor : 0u);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool alive = true;
@@ -306,17 +333,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (uint32_t kb = 0; kb < p.num_kb; kb++) {
                     if (!ptx::mbar_wait(&bars->full[stage], phase, p.err)) { alive = false; break; }
                     ptx::tc_fence_after();
-                    const uint32_t a_addr = ptx::smem_u32(sa + (size_t)stage * S_A);
-                    const uint32_t b_addr = ptx::smem_u32(sb + (size_t)stage * S_B);
+                    const uint32_t a_addr = ptx::smem_u32(sa + (size_t)stage * p.s_a_bytes);
+                    const uint32_t b_addr = ptx::smem_u32(sb + (size_t)stage * p.s_b_bytes);
 #pragma unroll
                     for (int k = 0; k < BK / UMMA_K; k++) {
-                        const uint64_t bdesc = BKN ? ptx::sdesc_mn(b_addr + k * UMMA_K * 128, 128, kMnAtomBytes)
+                        const uint64_t bdesc = BKN ? ptx::sdesc_mn(b_addr + k * UMMA_K * brow, brow, kMnAtomBytes)
                                                    : ptx::sdesc_kmajor_sw128(b_addr + k * UMMA_K);
                         ptx::umma_i8(d_tmem, ptx::sdesc_kmajor_sw128(a_addr + k * UMMA_K), bdesc, idesc,
                                      (kb | k) != 0);
                     }
                     ptx::umma_commit(&bars->empty[stage]);
-                    if (++stage == S_STAGES) { stage = 0; phase ^= 1; }
+                    if (++stage == nstages) { stage = 0; phase ^= 1; }
                 }
                 if (!alive) break;
                 ptx::umma_commit(&bars->tmem_full[acc]);
@@ -328,14 +355,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t quarter = (uint32_t)(warp & 3);
         uint32_t* stage = epi + (warp - 2) * EPI_STAGE_WORDS;
         uint32_t acc = 0, acc_phase = 0;
+        const uint32_t bn = BKN ? p.s_bn : (uint32_t)S_BN;
         for (uint32_t t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-            const uint32_t m0 = (t / p.tiles_n) * S_BM, n0 = (t % p.tiles_n) * S_BN;
+            const uint32_t m0 = (t / p.tiles_n) * S_BM, n0 = (t % p.tiles_n) * bn;
             // one verdict per warp: no lane reaches the warp-wide tcgen05.ld alone
             if (!__all_sync(0xffffffffu, ptx::mbar_wait(&bars->tmem_full[acc], acc_phase, p.err))) break;
             ptx::tc_fence_after();
             const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + acc * ACC_COLS;
             uint64_t* empty_bar = &bars->tmem_empty[acc];
-            drain_accumulator(p, taddr, m0 + quarter * 32, n0, ACC_COLS, stage, lane, [&] {
+            drain_accumulator(p, taddr, m0 + quarter * 32, n0, bn, stage, lane, [&] {
                 if (lane == 0) ptx::mbar_arrive(empty_bar);
             });
             acc ^= 1;
@@ -595,7 +623,8 @@ int launch_gemm_impl(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const
     if (force && !strcmp(force, "single")) pair = false;
     if (force && !strcmp(force, "pair")) pair = true;
     CUtensorMap ta, tb;
-    int rc = make_kmajor_map(&ta, Aq, M, K, pair ? P_HM : S_BM);
+    const uint32_t s_am = M >= (uint32_t)S_BM ? (uint32_t)S_BM : (M + 7) / 8 * 8;  // 1-CTA kernel: A rows per stage
+    int rc = make_kmajor_map(&ta, Aq, M, K, pair ? P_HM : s_am);
     if (rc) return rc;
     rc = BKN ? make_mn_map(&tb, Bt, N, K, bop.ldb, 128) : make_kmajor_map(&tb, Bt, N, K, pair ? P_HN : S_BN);
     if (rc) return rc;
@@ -604,11 +633,46 @@ int launch_gemm_impl(uint32_t M, uint32_t N, uint32_t K, const int8_t* Aq, const
         rc = set_max_dynamic_smem(gemm_s8_single_kernel<BKN>, (int)S_SMEM, smem_set);
         if (rc) return rc;
         p.tiles_m = (M + S_BM - 1) / S_BM;
-        p.tiles_n = (N + S_BN - 1) / S_BN;
+        // MN-major B: the tile width (256, 128 or 64 columns) with the fewest
+        // waves x width, ties to the wider tile (fewer tiles)
+        p.s_bn = S_BN;
+        if (BKN) {
+            uint64_t best = ~0ull;
+            for (uint32_t bn : {256u, 128u, 64u}) {
+                const uint64_t tiles = (uint64_t)p.tiles_m * ((N + bn - 1) / bn);
+                const uint64_t cost = (tiles + sms - 1) / sms * bn;
+                if (cost < best) {
+                    best = cost;
+                    p.s_bn = bn;
+                }
+            }
+        }
+        p.tiles_n = (N + p.s_bn - 1) / p.s_bn;
+        // the ring: as many stages (<= S_MAX_STAGES) as the operand region holds
+        // with the A tiles first and 16 KB of room after the last one
+        p.s_am = s_am;
+        p.s_a_bytes = s_am * BK;
+        p.s_b_bytes = p.s_bn * BK;
+        p.s_stages = S_STAGES;  // the full-size plan, which always fits
+        p.s_b_base = S_STAGES * S_A;
+        for (uint32_t st = S_MAX_STAGES; st >= 2; st--) {
+            const uint32_t a_end = (st - 1) * p.s_a_bytes + (uint32_t)S_A;
+            const uint32_t base = ((a_end > st * p.s_a_bytes ? a_end : st * p.s_a_bytes) + 1023) / 1024 * 1024;
+            if (base + st * p.s_b_bytes <= (uint32_t)S_OPS) {
+                p.s_stages = st;
+                p.s_b_base = base;
+                break;
+            }
+        }
+        CUtensorMap tb64 = tb;
+        if (BKN && p.s_bn == 64) {
+            rc = make_mn_map(&tb64, Bt, N, K, bop.ldb, 64);
+            if (rc) return rc;
+        }
         const uint32_t tiles = p.tiles_m * p.tiles_n;
         const uint32_t grid = tiles < (uint32_t)sms ? tiles : (uint32_t)sms;
         if (grid_out) *grid_out = grid;
-        return launch_pdl(gemm_s8_single_kernel<BKN>, dim3(grid), dim3(NUM_THREADS), S_SMEM, s, ta, tb, p);
+        return launch_pdl(gemm_s8_single_kernel<BKN>, dim3(grid), dim3(NUM_THREADS), S_SMEM, s, ta, tb, tb64, p);
     }
     static std::atomic<uint64_t> smem_set2{0};
     rc = set_max_dynamic_smem(gemm_s8_pair_kernel<BKN>, (int)P_SMEM, smem_set2);

@@ -213,9 +213,13 @@ def _kn_operands(torch, M, N, K, seed, pad_rows_garbage=True):
     (4096, 1104, 512),   # 80 tiles: last 6 cut in 4, parts past N
     (3000, 2000, 392),   # ragged M, K % 128 != 0 (last K block partly outside Bq)
     (512, 512, 4096),    # pair kernel, whole tiles only
-    (128, 256, 128),     # single-CTA kernel (M <= 128): two 128-column atoms per B stage
-    (7, 10, 48),         # single-CTA kernel, N inside one atom, K16 pad rows
-    (64, 14336, 4096),   # config 4 shape (single-CTA kernel)
+    (128, 256, 128),     # single-CTA kernel (M <= 128), 64-column tiles (fewest waves x width)
+    (7, 10, 48),         # single-CTA kernel, N inside one 64-column tile, K16 pad rows
+    (64, 14336, 4096),   # config 4 shape (single-CTA kernel, 128-column tiles)
+    (1, 7168, 4096),     # config 4 at 2 GPUs, M = 1: 112 tiles of 64 columns (SWIZZLE_64B)
+    (1, 14336, 4096),    # config 4 at 1 GPU, M = 1: 112 tiles of 128 columns
+    (100, 37888, 256),   # 148 tiles of 256 columns: two 128-column atoms per B stage
+    (33, 200, 1040),     # 64-column tiles, ragged N, K % 128 != 0
 ])
 def test_gemm_s8_kn_int32_exact(ane, M, N, K):
     """The GEMM with B stored K x N (MN-major tcgen05 operand, the layout the
