@@ -65,7 +65,8 @@ def parse():
                    help="profiling aid: run one kernel on one small case --steps times and exit, no JSON line. "
                         "dense:<n> (dense_fused_i8 n^3), q8r:<M>x<K> (q8_0_gemv, fp32 x), q8q:<M>x<K> "
                         "(MUL_MAT, Q8_0 x), kq:<fmt>:<M>x<K> (K-quant matvec), b16:<M>x<K> (batched MUL_MAT), "
-                        "stack:<layers> (config-5 decode stack as the persistent megakernel)")
+                        "stack:<layers> (config-5 decode stack as the persistent megakernel), b16stack:<layers> (the batch-16 "
+                        "stack: plain chain, then the tagged-output chain)")
     return p.parse_args()
 
 
@@ -94,6 +95,19 @@ def run_profile_case(args):
 
         fused = decode.FusedDecodeStack(decode.gpu_stack(int(rest), dev), dev)
         fn, closer = fused.forward, fused.close
+    elif kind == "b16stack":
+        # config-5 decode stack of `rest` layers at batch 16: the plain batched chain,
+        # then the chain with tagged outputs (1 GPU), one step of each per call
+        from ane_b200 import decode
+
+        st16 = decode.gpu_stack(int(rest), dev, batch=16)
+        peer16 = decode.PeerBatchDecodeStack(st16, dev)
+
+        def fn():
+            st16.forward()
+            peer16.forward()
+
+        closer = peer16.close
     else:
         fmt = None
         if kind == "kq":
