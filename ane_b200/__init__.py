@@ -110,6 +110,8 @@ SIGNATURES = {
     "ane_mul_mat_q8_0_gather_dev": (_i32, [_u32, _u32, _vp, _vp, _u32, _vp, _vp, _u32, _u32, _u32, _vp, _u32, _u32,
                                            _u32, _vp]),
     "ane_q8_chain_token_end_dev": (_i32, [_vp, _u32, _u32, _vp, _vp]),
+    "ane_q8_0_gemv_gather_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _u32, _vp, _vp, _u32, _u32, _vp, _u32, _u32, _u32,
+                                        _vp]),
     "ane_mul_mat_q8_0_batch_dev": (_i32, [_u32, _u32, _u32, _vp, _sz, _vp, _vp, _sz, _vp, _u32, _vp]),
     "ane_mul_mat_q8_0_batch_gather_dev": (_i32, [_u32, _u32, _u32, _vp, _sz, _vp, _vp, _u32, _vp, _sz, _vp, _u32,
                                                  _u32, _vp, _u32, _u32, _u32, _vp]),

@@ -305,6 +305,13 @@ struct Q8ChainGather {
 int launch_mul_mat_q8_0_gather(uint32_t M, uint32_t K, const float* x, const uint8_t* W, const Q8ChainGather& g,
                                uint32_t flags, cudaStream_t s);
 uint32_t mul_mat_q8_0_ctas(uint32_t M, uint32_t K);
+// The same chain link in mode R (q8_0_gemv on the fp32 activation): a kernel
+// writes x as fp32 into xbuf from the previous projection's tagged vector (and
+// waits for one guard word per rank), then the q8_0_gemv stream kernel stores
+// its rows as tagged words into every rank's vector.  Uses world, out, prev,
+// x_from_prev, prev_rows, tok, nproj, j of g.
+int launch_q8_0_gemv_gather(uint32_t M, uint32_t K, const float* x, float* xbuf, const uint8_t* W,
+                            const Q8ChainGather& g, uint32_t flags, cudaStream_t s);
 // Ends a step of such a chain: waits (bounded) until every word of the last
 // projection's output on this GPU (`ntok` token rows of `rows` words, row
 // stride `ld` words) carries that projection's tag, then bumps *tok.

@@ -601,6 +601,32 @@ int ane_mul_mat_q8_0_gather_dev(uint32_t rows_local, uint32_t K, const float* x,
     return rc ? rc : ok();
 }
 
+int ane_q8_0_gemv_gather_dev(uint32_t rows_local, uint32_t K, const float* x, float* xbuf, const void* W,
+                             uint32_t world, void* const* out_ranks, const void* prev, uint32_t x_from_prev,
+                             uint32_t prev_rows, const uint32_t* tok, uint32_t nproj, uint32_t j, uint32_t flags,
+                             void* stream) {
+    ANE_REQUIRE_GPU();
+    ANE_ARG_CHECK((flags & ~ANE_Q8_WEIGHTS_STATIC) == 0, "q8_0_gemv_gather: unknown flag bits");
+    ANE_ARG_CHECK(world >= 1 && world <= 8 && out_ranks, "q8_0_gemv_gather: world must be 1..8");
+    ANE_ARG_CHECK(!x_from_prev || xbuf, "q8_0_gemv_gather: a chained input needs xbuf");
+    Q8ChainGather g{};
+    g.world = world;
+    for (uint32_t q = 0; q < world; q++) {
+        ANE_ARG_CHECK(out_ranks[q] && ((uintptr_t)out_ranks[q] & 7) == 0,
+                      "q8_0_gemv_gather: 8-byte-aligned output pointer per rank");
+        g.out[q] = static_cast<uint64_t*>(out_ranks[q]);
+    }
+    g.prev = static_cast<const uint64_t*>(prev);
+    g.x_from_prev = x_from_prev ? 1u : 0u;
+    g.prev_rows = prev_rows;
+    g.tok = tok;
+    g.nproj = nproj;
+    g.j = j;
+    int rc = launch_q8_0_gemv_gather(rows_local, K, x, xbuf, static_cast<const uint8_t*>(W), g, flags,
+                                     static_cast<cudaStream_t>(stream));
+    return rc ? rc : ok();
+}
+
 int ane_q8_chain_token_end_dev(const void* last, uint32_t len, uint32_t nproj, uint32_t* tok, void* stream) {
     ANE_REQUIRE_GPU();
     ANE_ARG_CHECK(last && tok && nproj > 0, "q8_chain_token_end: bad arguments");

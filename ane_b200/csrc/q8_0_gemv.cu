@@ -154,10 +154,15 @@ __device__ __forceinline__ float2 q8_block_fast(float2 acc, uint32_t w, float d,
 // one 4-row x 544-byte TMA box per compute warp with rows in the pass and one
 // bulk copy of the x slice, after the consumers have released the stage.
 // (The launch bound lets ptxas keep a whole 8-block load phase in registers.)
+// GATHER (one link of a row-sharded decode chain): each row result leaves as
+// one 8-byte {value, tag} word stored into every rank's next vector instead of
+// out[row]; x is then the fp32 vector q8_unpack_tagged_kernel wrote.
+template <bool GATHER>
 __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
     q8_0_gemv_stream_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ W,
                             const float* __restrict__ x, float* __restrict__ out, uint32_t M, uint32_t K,
-                            uint32_t groups, uint32_t nw, uint32_t nslots, uint32_t flags, int* err) {
+                            uint32_t groups, uint32_t nw, uint32_t nslots, uint32_t flags, int* err,
+                            const __grid_constant__ Q8ChainGather pg) {
     extern __shared__ __align__(128) uint8_t smem[];
     // the last chunk may hold 8 blocks (K % 512 == 256): the TMA box then runs
     // past the row end and zero-fills, and the transaction counts the full box
@@ -217,6 +222,9 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
     }
     // ------------------------------------------------------------ compute
     ptx::griddep_wait();  // out (and x, on the replay path) may belong to the previous kernel
+    // GATHER: this projection's tag (the count is final once the kernels before
+    // this one have ended)
+    const uint32_t tag_out = GATHER ? *reinterpret_cast<const volatile uint32_t*>(pg.tok) * pg.nproj + pg.j + 1u : 0u;
     const uint32_t cw = warp - 1, rr = lane >> 3, j = lane & 7;
     bool alive = true;
     for (uint32_t pass = 0; pass < npass && alive; pass++) {
@@ -287,7 +295,89 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
             const float t = faddv(a0, a1);
             if (redo) s = t;
         }
-        if (active && j == 0 && alive) out[row] = s;
+        if (active && j == 0 && alive) {
+            if constexpr (GATHER) {
+                const uint64_t w = (uint64_t)__float_as_uint(s) | ((uint64_t)tag_out << 32);
+                for (uint32_t q = 0; q < pg.world; q++)
+                    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(pg.out[q] + row), "l"(w) : "memory");
+            } else {
+                out[row] = s;
+            }
+        }
+    }
+}
+
+// The fp32 input of a mode-R chain link: waits (bounded) until each of the K
+// words of the previous projection's tagged vector on this GPU carries that
+// projection's tag and writes its value to x (16-byte loads, eight per thread
+// in flight, the missing ones read again together each round).  Block 0 also
+// waits for one word per rank of the previous projection (that rank's first
+// row): a rank that stored it has finished reading the vector the matvec after
+// this kernel overwrites.  K = 0: the guard alone (a layer's first projection,
+// whose x is the fp32 layer input).
+constexpr uint32_t kUnpackThreads = 256, kUnpackPairs = 8;
+__global__ void __launch_bounds__(kUnpackThreads) q8_unpack_tagged_kernel(const uint64_t* __restrict__ prev,
+                                                                          uint32_t K, float* __restrict__ x,
+                                                                          uint32_t world, uint32_t prev_rows,
+                                                                          const uint32_t* tok, uint32_t nproj,
+                                                                          uint32_t jproj, int* err) {
+    ptx::griddep_launch_dependents();
+    ptx::griddep_wait();  // x may still be read by the kernel before this one
+    const uint32_t tag = *reinterpret_cast<const volatile uint32_t*>(tok) * nproj + jproj;
+    auto ld_word = [](const uint64_t* p) {
+        uint64_t w;
+        asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+        return w;
+    };
+    if (blockIdx.x == 0 && threadIdx.x < world) {
+        const uint64_t* g = prev + (size_t)threadIdx.x * prev_rows;
+        const long long t0 = clock64();
+        while ((uint32_t)(ld_word(g) >> 32) != tag) {
+            if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
+                atomicAdd(err, 1);
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    const uint32_t npairs = K / 2, stride = gridDim.x * kUnpackThreads;
+    for (uint32_t base = blockIdx.x * kUnpackThreads + threadIdx.x; base < npairs; base += stride * kUnpackPairs) {
+        uint2 v[kUnpackPairs];
+        uint32_t miss = 0;
+#pragma unroll
+        for (uint32_t u = 0; u < kUnpackPairs; u++) {
+            const uint32_t i = base + u * stride;
+            if (i < npairs) {
+                uint64_t a, b;
+                asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(prev + 2 * i) : "memory");
+                v[u] = make_uint2((uint32_t)a, (uint32_t)b);
+                if ((uint32_t)(a >> 32) != tag || (uint32_t)(b >> 32) != tag) miss |= 1u << u;
+            }
+        }
+        const long long t0 = miss ? clock64() : 0;
+        while (miss) {
+            if (clock64() - t0 > ptx::kWaitTimeoutCycles) {
+                atomicAdd(err, 1);
+                break;
+            }
+            __nanosleep(64);
+#pragma unroll
+            for (uint32_t u = 0; u < kUnpackPairs; u++) {
+                if (!((miss >> u) & 1u)) continue;
+                const uint32_t i = base + u * stride;
+                uint64_t a, b;
+                asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(prev + 2 * i) : "memory");
+                if ((uint32_t)(a >> 32) == tag && (uint32_t)(b >> 32) == tag) {
+                    v[u] = make_uint2((uint32_t)a, (uint32_t)b);
+                    miss &= ~(1u << u);
+                }
+            }
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < kUnpackPairs; u++) {
+            const uint32_t i = base + u * stride;
+            if (i < npairs) reinterpret_cast<float2*>(x)[i] = make_float2(__uint_as_float(v[u].x), __uint_as_float(v[u].y));
+        }
     }
 }
 
@@ -299,15 +389,16 @@ int launch_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, f
     if (K % 256 == 0 && ((uintptr_t)W & 15) == 0 && ((uintptr_t)x & 15) == 0) {
         const Q8Plan p = plan_q8_stream(M, K, kChunkXBytes, 128);
         static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
-        if (int arc = set_max_dynamic_smem(q8_0_gemv_stream_kernel, 200 * 1024, smem_set)) return arc;
+        if (int arc = set_max_dynamic_smem(q8_0_gemv_stream_kernel<false>, 200 * 1024, smem_set)) return arc;
         ANE_ARG_CHECK(p.smem <= 200 * 1024, "q8_0_gemv: shared-memory plan too large");
         const uint64_t row_bytes = (uint64_t)(K / 32) * 34;
         CUtensorMap wmap;
         int rc = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, row_bytes / 4, M, row_bytes,
                                       kQ8ChunkBytes / 4, kQ8RowsPerWarp, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
-        return launch_q8_stream(q8_0_gemv_stream_kernel, p, s, wmap, W, x, out, M, K, p.groups, p.warps, p.slots,
-                                flags, device_timeout_flag());
+        const Q8ChainGather none{};
+        return launch_q8_stream(q8_0_gemv_stream_kernel<false>, p, s, wmap, W, x, out, M, K, p.groups, p.warps,
+                                p.slots, flags, device_timeout_flag(), none);
     }
     const size_t smem = (size_t)K * sizeof(float);
     ANE_ARG_CHECK(smem <= 200 * 1024, "q8_0_gemv: K too large for the shared activation buffer");
@@ -318,6 +409,34 @@ int launch_q8_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, f
     q8_0_gemv_kernel<<<blocks, kQThreads, smem, s>>>(x, W, out, M, K);
     ANE_CHECK_LAUNCH();
     return ANE_OK;
+}
+
+int launch_q8_0_gemv_gather(uint32_t M, uint32_t K, const float* x, float* xbuf, const uint8_t* W,
+                            const Q8ChainGather& g, uint32_t flags, cudaStream_t s) {
+    ANE_ARG_CHECK(M > 0 && K % 256 == 0 && K > 0, "q8_0_gemv gather: K must be a positive multiple of 256");
+    ANE_ARG_CHECK(g.world >= 1 && g.world <= 8 && g.prev && g.tok && g.nproj > 0 && g.j < g.nproj && g.prev_rows > 0,
+                  "q8_0_gemv gather: bad chain arguments");
+    ANE_ARG_CHECK(((uintptr_t)W & 15) == 0 && ((uintptr_t)g.prev & 15) == 0, "q8_0_gemv gather: W and prev must be 16-byte aligned");
+    const float* xin = g.x_from_prev ? xbuf : x;
+    ANE_ARG_CHECK(xin && ((uintptr_t)xin & 15) == 0, "q8_0_gemv gather: x must be 16-byte aligned");
+    // the input (or the guard alone): one kernel, then the matvec
+    const uint32_t kx = g.x_from_prev ? K : 0u;
+    const uint32_t per = kUnpackThreads * kUnpackPairs * 2;
+    const uint32_t blocks = kx ? (kx + per - 1) / per : 1u;
+    int rc = launch_pdl(q8_unpack_tagged_kernel, dim3(blocks), dim3(kUnpackThreads), 0, s, g.prev, kx, xbuf, g.world,
+                        g.prev_rows, g.tok, g.nproj, g.j, device_timeout_flag());
+    if (rc) return rc;
+    const Q8Plan p = plan_q8_stream(M, K, kChunkXBytes, 128);
+    static std::atomic<uint64_t> smem_set{0};
+    if (int arc = set_max_dynamic_smem(q8_0_gemv_stream_kernel<true>, 200 * 1024, smem_set)) return arc;
+    ANE_ARG_CHECK(p.smem <= 200 * 1024, "q8_0_gemv gather: shared-memory plan too large");
+    const uint64_t row_bytes = (uint64_t)(K / 32) * 34;
+    CUtensorMap wmap;
+    rc = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, row_bytes / 4, M, row_bytes,
+                              kQ8ChunkBytes / 4, kQ8RowsPerWarp, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    return launch_q8_stream(q8_0_gemv_stream_kernel<true>, p, s, wmap, W, xin, (float*)nullptr, M, K, p.groups,
+                            p.warps, p.slots, flags, device_timeout_flag(), g);
 }
 
 }  // namespace ane_b200

@@ -272,10 +272,12 @@ class FusedDecodeStack:
 
 # ------------------------------------------- per-projection launches, fused gather
 class PeerChainDecodeStack:
-    """The weights and inputs of a batch-1 mode-Q DecodeStack run as one
-    MUL_MAT launch per projection (ane_mul_mat_q8_0_gather_dev) whose rows go
-    straight into every rank's next input vector over NVLink -- no NCCL call --
-    plus one token-end launch; the whole token captures into a CUDA graph.
+    """The weights and inputs of a batch-1 DecodeStack run as one MUL_MAT
+    launch per projection (mode q: ane_mul_mat_q8_0_gather_dev; mode r:
+    ane_q8_0_gemv_gather_dev, the reference's q8_0_gemv arithmetic) whose rows
+    go straight into every rank's next input vector over NVLink -- no NCCL
+    call -- plus one token-end launch; the whole token captures into a CUDA
+    graph.
 
     Per rank one zeroed buffer holds two TAGGED vectors (8-byte {fp32 value,
     u32 tag} words; projection j writes vector j % 2) and the token count; the
@@ -285,14 +287,19 @@ class PeerChainDecodeStack:
     overwrites a vector a slow one still reads.
     """
 
-    def __init__(self, stack: DecodeStack, device, group=None):
+    def __init__(self, stack: DecodeStack, device, group=None, mode: str = "q"):
+        """mode "q": each link is the Q8_0-activation MUL_MAT; mode "r": the
+        reference's arithmetic, q8_0_gemv on the fp32 activation (an extra launch
+        per projection writes the previous vector's values as fp32 first)."""
         import ctypes
 
         import ane_b200 as ane
 
         if stack.batch != 1:
             raise ValueError("the fused-gather chain runs one token per step")
-        self._ane, self.stack = ane, stack
+        if mode not in ("q", "r"):
+            raise ValueError("mode is 'q' or 'r'")
+        self._ane, self.stack, self.mode = ane, stack, mode
         world, rank = stack.world, stack.rank
         width = stack.h[0].numel()
         vec_bytes = (width * 8 + 255) // 256 * 256
@@ -320,6 +327,8 @@ class PeerChainDecodeStack:
         projs = [(layer, p, M, K) for layer in range(stack.layers) for p, (_, M, K) in enumerate(stack.shapes)]
         self.nproj = len(projs)
         split = [(M // world, int(ane.lib.ane_mul_mat_q8_0_ctas(M // world, K))) for _, _, M, K in projs]
+        # mode r: the fp32 input of a chained projection, written from the tagged vector
+        self._xbuf = torch.empty(max(K for _, _, _, K in projs), dtype=torch.float32, device=device)
         self._calls = []
         for j, (layer, p, M, K) in enumerate(projs):
             rows = M // world
@@ -339,10 +348,17 @@ class PeerChainDecodeStack:
     def forward(self, stream=None) -> torch.Tensor:
         ane, world = self._ane, self.stack.world
         s = ane._stream_ptr(stream)
-        for rows, K, x, W, outs, prev, chained, prev_rows, prev_ctas, j in self._calls:
-            ane.check(ane.lib.ane_mul_mat_q8_0_gather_dev(rows, K, x or None, W, world, outs, prev, chained,
-                                                          prev_rows, prev_ctas, self._tok, self.nproj, j,
-                                                          ane.WEIGHTS_STATIC, s))
+        if self.mode == "r":
+            xbuf = self._xbuf.data_ptr()
+            for rows, K, x, W, outs, prev, chained, prev_rows, _, j in self._calls:
+                ane.check(ane.lib.ane_q8_0_gemv_gather_dev(rows, K, x or None, xbuf, W, world, outs, prev, chained,
+                                                           prev_rows, self._tok, self.nproj, j, ane.WEIGHTS_STATIC,
+                                                           s))
+        else:
+            for rows, K, x, W, outs, prev, chained, prev_rows, prev_ctas, j in self._calls:
+                ane.check(ane.lib.ane_mul_mat_q8_0_gather_dev(rows, K, x or None, W, world, outs, prev, chained,
+                                                              prev_rows, prev_ctas, self._tok, self.nproj, j,
+                                                              ane.WEIGHTS_STATIC, s))
         ane.check(ane.lib.ane_q8_chain_token_end_dev(self._last, self._last_len, self.nproj, self._tok, s))
         return self.out
 

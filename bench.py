@@ -523,6 +523,15 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
     r_graph = gr is not None
     r_ms = timed(gr.replay if r_graph else stack_r.forward)
     del gr
+    # mode R as the chain whose rows go to every rank by peer stores
+    peer_r = decode.PeerChainDecodeStack(stack_r, dev, group=group, mode="r")
+    peer_r.forward()
+    torch.cuda.synchronize()
+    gpr = capture(peer_r.forward)
+    pr_graph = gpr is not None
+    pr_ms = timed(gpr.replay if pr_graph else peer_r.forward)
+    del gpr
+    torch.cuda.synchronize()
     # batch 16: the same weights, 16 tokens per step through the batched MUL_MAT
     batch = 16
     stack16 = decode.gpu_stack(layers, dev, world=world, rank=rank, group=group, batch=batch,
@@ -548,7 +557,7 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
         # that layer alone (each layer starts from its own seeded input)
         outs = {"chain_q": stack.forward().clone(), "mode_r": stack_r.forward().clone(),
                 "batch16": stack16.forward().clone(), "peer_q": peer.forward().clone(),
-                "batch16_peer": peer16.forward().clone()}
+                "batch16_peer": peer16.forward().clone(), "mode_r_peer": peer_r.forward().clone()}
         fused2 = decode.FusedDecodeStack(stack, dev, group=group)
         try:
             outs["fused_q"] = fused2.forward().clone()
@@ -561,8 +570,9 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
             one_r = decode.gpu_stack(1, dev, first_layer=layers - 1, weights=one.weights, mode="r")
             one16 = decode.gpu_stack(1, dev, first_layer=layers - 1, weights=one.weights, batch=batch)
             ref16 = one16.forward()
-            refs = {"chain_q": one.forward(), "fused_q": one.forward(), "mode_r": one_r.forward(),
-                    "batch16": ref16, "peer_q": one.forward(), "batch16_peer": ref16}
+            ref_r = one_r.forward()
+            refs = {"chain_q": one.forward(), "fused_q": one.forward(), "mode_r": ref_r,
+                    "batch16": ref16, "peer_q": one.forward(), "batch16_peer": ref16, "mode_r_peer": ref_r}
             torch.cuda.synchronize()
             parity = {k: bool(torch.equal(outs[k].view(torch.int32), refs[k].view(torch.int32))) for k in outs}
             del one, one_r, one16, refs
@@ -572,6 +582,7 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
         torch.distributed.barrier(group)  # no rank unmaps a peer buffer while a peer still writes it
     peer.close()
     peer16.close()
+    peer_r.close()
     del stack16, stack_r
     wbytes = decode.stack_weight_bytes(layers)
     peaks = load_peaks()
@@ -589,16 +600,27 @@ def decode_bench(torch, dev, layers=32, reps=20, world=1, rank=0, group=None):
             "chain_ms_per_token": chain_ms, "chain_gbs": wbytes / (chain_ms * 1e-3) / 1e9, "chain_path": chain_path,
             "peer_ms_per_token": peer_ms, "peer_gbs": wbytes / (peer_ms * 1e-3) / 1e9, "peer_path": peer_path,
             "mode": "q (Q8_0 activation, ggml convention) for ms_per_token, fused, chain and peer",
-            "mode_r": {"ms_per_token": r_ms, "gbs": wbytes / (r_ms * 1e-3) / 1e9,
-                       "per_gpu_hbm_frac": wbytes / (r_ms * 1e-3) / 1e9 / world / peaks["hbm_gbs"],
-                       "path": (f"{4 * layers} q8_0_gemv launches on the fp32 activation (the reference's "
-                                "arithmetic)" + ("" if world == 1 else " + NCCL all-gather each")
-                                + (" in a CUDA graph" if r_graph else " (eager)"))},
+            "mode_r": mode_r_line(layers, wbytes, world, peaks, r_ms, r_graph, pr_ms, pr_graph),
             "parity_ok_vs_1gpu": parity,
             "batch16": batch16_line(batch, wbytes, world, peaks, layers, b16_ms, b16_graph, p16_ms, p16_graph),
             "activation": "Q8_0 (ggml convention), static weights",
             "timing": f"{reps} tokens each path, CUDA events" + ("" if world == 1 else ", max over ranks"),
             "build_s": build_s}
+
+
+def mode_r_line(layers, wbytes, world, peaks, chain_ms, chain_graph, peer_ms, peer_graph):
+    """The mode-R decode numbers (the reference's q8_0_gemv arithmetic): the better
+    of the plain chain (NCCL all-gathers from 2 GPUs) and the peer-store chain."""
+    chain_path = (f"{4 * layers} q8_0_gemv launches on the fp32 activation (the reference's arithmetic)"
+                  + ("" if world == 1 else " + NCCL all-gather each")
+                  + (" in a CUDA graph" if chain_graph else " (eager)"))
+    peer_path = (f"{4 * layers} x (fp32 input from the tagged vector + q8_0_gemv storing "
+                 + ("every rank's next vector by NVLink peer stores" if world > 1 else "the next tagged vector")
+                 + ") launches + a token-end launch" + (", a CUDA graph per token" if peer_graph else " (eager)"))
+    ms, path = min((chain_ms, chain_path), (peer_ms, peer_path))
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    return {"ms_per_token": ms, "gbs": gbs, "per_gpu_hbm_frac": gbs / world / peaks["hbm_gbs"], "path": path,
+            "chain_ms_per_token": chain_ms, "peer_ms_per_token": peer_ms}
 
 
 def batch16_line(batch, wbytes, world, peaks, layers, nccl_ms, nccl_graph, peer_ms, peer_graph):

@@ -305,6 +305,21 @@ int ane_mul_mat_q8_0_gather_dev(uint32_t rows_local, uint32_t K, const float* x,
                                 uint32_t prev_ctas, const uint32_t* tok, uint32_t nproj, uint32_t j, uint32_t flags,
                                 void* stream);
 int ane_q8_chain_token_end_dev(const void* last, uint32_t len, uint32_t nproj, uint32_t* tok, void* stream);
+/* The same chain in mode R: each link is q8_0_gemv (bit for bit: the
+ * reference's fp32-activation arithmetic) on x, or -- x_from_prev -- on the
+ * previous projection's tagged vector prev (16-byte aligned), whose values a
+ * first launch writes as fp32 into xbuf (K floats, 16-byte aligned) after
+ * waiting (bounded) for their tags.  That launch also waits, before anything is
+ * stored, for prev[q * prev_rows] (rank q's first row of the previous
+ * projection) to carry the previous projection's tag for every rank q.  Rows
+ * go to out_ranks[q] + r as tagged words, tags and tok as for
+ * ane_mul_mat_q8_0_gather_dev; ane_q8_chain_token_end_dev ends a token.  K is
+ * a positive multiple of 256, W 16-byte aligned.  No counterpart in the
+ * reference. */
+int ane_q8_0_gemv_gather_dev(uint32_t rows_local, uint32_t K, const float* x, float* xbuf, const void* W,
+                             uint32_t world, void* const* out_ranks, const void* prev, uint32_t x_from_prev,
+                             uint32_t prev_rows, const uint32_t* tok, uint32_t nproj, uint32_t j, uint32_t flags,
+                             void* stream);
 
 /* The same chain at batch NT <= 16 (decode of NT tokens per step), each link
  * being ane_mul_mat_q8_0_batch_dev's MUL_MAT (bit for bit): a vector holds NT

@@ -78,6 +78,41 @@ def test_decode_stack_graph_replay_matches_eager(ane):
     del g
 
 
+@pytest.mark.parametrize("shapes,layers", [("small", 3), ("config5", 2)])
+def test_peer_chain_mode_r_equals_q8_0_gemv_chain(ane, shapes, layers):
+    """Mode R (the reference's q8_0_gemv on the fp32 activation) as a chain whose
+    rows go into the next projection's tagged vector (ane_q8_0_gemv_gather_dev)
+    == the plain chain of q8_0_gemv launches, bit for bit, on repeated tokens and
+    under graph replay."""
+    import torch
+
+    from ane_b200.decode import LAYER_SHAPES, PeerChainDecodeStack, gpu_stack
+
+    sh = LAYER_SHAPES if shapes == "config5" else (("qkv", 512, 256), ("o", 256, 256), ("gate_up", 512, 256),
+                                                   ("down", 256, 256))
+    dev = torch.device("cuda", 0)
+    stack = gpu_stack(layers, dev, shapes=sh, seed=31, mode="r")
+    ref = stack.forward().clone()
+    peer = PeerChainDecodeStack(stack, dev, mode="r")
+    try:
+        for _ in range(3):
+            out = peer.forward()
+            torch.cuda.synchronize()
+            assert torch.equal(out.view(torch.int32), ref.view(torch.int32))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            peer.forward()
+        for _ in range(2):
+            peer.out.fill_(float("nan"))
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(peer.out.view(torch.int32), ref.view(torch.int32))
+        del g
+        assert ane.lib.ane_device_timeouts() == 0
+    finally:
+        peer.close()
+
+
 @pytest.mark.parametrize("shapes,layers,batch", [("small", 3, 16), ("small", 2, 5), ("config5", 1, 16)])
 def test_peer_batch_equals_batched_stack(ane, shapes, layers, batch):
     """Decode at batch > 1 as a chain of batched MUL_MATs whose outputs go

@@ -103,7 +103,7 @@ def _stack_worker(rank, world, port, layers, result_q):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
-    fused = peer = peer16 = None
+    fused = peer = peer16 = peer_r = None
     try:
         import ane_b200 as ane
         from ane_b200.decode import FusedDecodeStack, PeerBatchDecodeStack, PeerChainDecodeStack, gpu_stack
@@ -118,6 +118,13 @@ def _stack_worker(rank, world, port, layers, result_q):
         torch.cuda.synchronize()
         ok = torch.equal(nccl_out.view(torch.int32), single.view(torch.int32)) and all(
             torch.equal(o.view(torch.int32), single.view(torch.int32)) for o in outs)
+        # mode R (the reference's q8_0_gemv arithmetic) as the peer-store chain
+        sharded_r = gpu_stack(layers, dev, world=world, rank=rank, seed=33, mode="r", weights=sharded.weights)
+        peer_r = PeerChainDecodeStack(sharded_r, dev, mode="r")
+        outs_r = [peer_r.forward().clone() for _ in range(3)]
+        single_r = gpu_stack(layers, dev, world=1, rank=0, seed=33, mode="r").forward()
+        torch.cuda.synchronize()
+        ok = ok and all(torch.equal(o.view(torch.int32), single_r.view(torch.int32)) for o in outs_r)
         # batch 16: the batched chain with peer stores == the 1-GPU batched stack
         sharded16 = gpu_stack(layers, dev, world=world, rank=rank, seed=33, batch=16)
         peer16 = PeerBatchDecodeStack(sharded16, dev)
@@ -131,10 +138,10 @@ def _stack_worker(rank, world, port, layers, result_q):
         if rank == 0:
             result_q.put(int(flags.item()))
     finally:
-        if fused is not None or peer is not None or peer16 is not None:
+        if fused is not None or peer is not None or peer16 is not None or peer_r is not None:
             torch.cuda.synchronize()
             dist.barrier()  # no rank unmaps a peer buffer while a peer still writes it
-            for s in (fused, peer, peer16):
+            for s in (fused, peer, peer16, peer_r):
                 if s is not None:
                     s.close()
         dist.destroy_process_group()
