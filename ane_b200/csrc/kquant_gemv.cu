@@ -5,10 +5,11 @@
 // Arithmetic of every matvec handler: rows of K/256 super-blocks; 16
 // accumulator lanes, lane l taking element l of every 16-element chunk of the
 // row in order with one fused multiply-add; the row result is the FADDV tree
-// ((a0+a1)+(a2+a3))+... over the 16 lanes.  Element values are computed with the
-// handler's separately rounded operations (integer -> float exact, one multiply
-// by the sub-block scale, one add of the sub-block min where the format has
-// one).  The byte layouts are the handlers' own, including q3_k's stale shift
+// ((a0+a1)+(a2+a3))+... over the 16 lanes.  Element values are the handler's
+// separately rounded operations (integer -> float exact, one multiply by the
+// sub-block scale, one add of the sub-block min where the format has one),
+// computed without the conversion unit and two lanes per packed instruction
+// (the identities are stated at the decoders).  The byte layouts are the handlers' own, including q3_k's stale shift
 // vector: its second 16 elements of every 32-element sub-block shift the packed
 // 2-bit codes right first by the bit pattern of the x values the first half
 // loaded (shifts >= 32 give 0, as SVE LSR does), then by 2l.
@@ -76,29 +77,49 @@ __device__ __forceinline__ void k_scale_min(const uint8_t* s, uint32_t j, uint32
     }
 }
 
-// value = RN(RN(q * dsc) + dmm), accumulated with one fma
-__device__ __forceinline__ float kq_min_term(float acc, uint32_t q, float dsc, float dmm, float x) {
-    return __fmaf_rn(__fadd_rn(__fmul_rn((float)q, dsc), dmm), x, acc);
+// Element values without the conversion unit.  For an integer v < 2^23 the
+// float with bit pattern 0x4B000000 | v is 2^23 + v exactly, so subtracting
+// 2^23 (plus the format's code offset) gives the code as a float exactly -- the
+// handlers' int -> float conversion.  A code left at bit position p (v = q·2^p)
+// is paired with the scale times 2^-p, which is exact (a nonzero scale is at
+// least 2^-24 in magnitude; 0, inf and NaN stay what they are), so every
+// product is the handler's.
+//
+// Formats with a min compute RN(RN(q·dsc) + dmm).  dsc is an fp16 d times a
+// code of at most 6 bits (<= 17 significant bits) and q has at most 5 bits, so
+// q·dsc is exact and RN(RN(q·dsc) + dmm) = fma(q, dsc, dmm) for every input,
+// inf and NaN included.  Formats without one compute RN((q - off)·dsc), one
+// multiply.  A thread's two lanes (2t, 2t+1) share each packed operation.
+constexpr uint32_t kMag = 0x4B000000u;  // 2^23
+constexpr float kMagF = 8388608.0f;
+__device__ __forceinline__ float mag(uint32_t v) { return __uint_as_float(kMag | v); }
+// 2^23 + byte k of v
+__device__ __forceinline__ float mag_byte(uint32_t v, uint32_t k) {
+    return __uint_as_float(__byte_perm(v, kMag, 0x7440u + k));
 }
-// value = RN(q * dsc) (signed q), accumulated with one fma
-__device__ __forceinline__ float kq_term(float acc, int32_t q, float dsc, float x) {
-    return __fmaf_rn(__fmul_rn((float)q, dsc), x, acc);
+// {fma(q0, s.x, m.x), fma(q1, s.y, m.y)} from f = {2^23 + q0, 2^23 + q1}
+__device__ __forceinline__ float2 kq_min_pair(float2 f, float2 s, float2 m) {
+    return ptx::ffma2(ptx::fadd2(f, make_float2(-kMagF, -kMagF)), s, m);
+}
+// {RN((f.x - o.x)·s.x), RN((f.y - o.y)·s.y)}, no = -o (o = 2^23 + the code offset)
+__device__ __forceinline__ float2 kq_off_pair(float2 f, float2 no, float2 s) {
+    return ptx::fmul2(ptx::fadd2(f, no), s);
 }
 
-// One super-block of a row for thread t's lanes 2t (a0) and 2t+1 (a1).
+// One super-block of a row for thread t's lanes 2t (acc.x) and 2t+1 (acc.y).
 // sh (a constant at every call site): the row's 8 threads are converged (all
 // 32 lanes of the warp call together); thread t decodes sub-block t's scale (and
 // t + 8's in the 16-sub-block formats) and the others take it by a width-8
 // shuffle -- the same values, decoded once per row instead of in every thread.
 template <int F>
 __device__ __forceinline__ void kq_superblock(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
-                                              uint32_t t, float& a0, float& a1, bool sh);
+                                              uint32_t t, float2& acc, bool sh);
 
 __device__ __forceinline__ float row_bcast(float v, uint32_t j) { return __shfl_sync(0xffffffffu, v, (int)j, 8); }
 
 template <>
 __device__ __forceinline__ void kq_superblock<kQ4K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
-                                                    uint32_t t, float& a0, float& a1, bool sh) {
+                                                    uint32_t t, float2& acc, bool sh) {
     const float d = h2f(ld_u16(blk)), nd = -h2f(ld_u16(blk + 2));
     const uint8_t* qs = blk + 16;
     float tdsc = 0.0f, tdmm = 0.0f;  // sub-block t's, when shared
@@ -123,16 +144,18 @@ __device__ __forceinline__ void kq_superblock<kQ4K>(const uint8_t* __restrict__ 
         const uint32_t b = ld_u16(qs + 16 * j + 2 * t);  // bytes of lanes 2t, 2t+1
         const float2 xl = *reinterpret_cast<const float2*>(xb + 32 * j + 2 * t);
         const float2 xh = *reinterpret_cast<const float2*>(xb + 32 * j + 16 + 2 * t);
-        a0 = kq_min_term(a0, b & 0x0Fu, dsc, dmm, xl.x);
-        a1 = kq_min_term(a1, (b >> 8) & 0x0Fu, dsc, dmm, xl.y);
-        a0 = kq_min_term(a0, (b >> 4) & 0x0Fu, dsc, dmm, xh.x);
-        a1 = kq_min_term(a1, (b >> 12) & 0x0Fu, dsc, dmm, xh.y);
+        const float2 m = make_float2(dmm, dmm);
+        // low nibbles at bits 0 and 8 (codes x 1, x 256), high ones at 4 and 12 (x 16, x 4096)
+        const float2 slo = make_float2(dsc, __fmul_rn(dsc, 0.00390625f));
+        const float2 shi = make_float2(__fmul_rn(dsc, 0.0625f), __fmul_rn(dsc, 0.000244140625f));
+        acc = ptx::ffma2(kq_min_pair(make_float2(mag(b & 0x000Fu), mag(b & 0x0F00u)), slo, m), xl, acc);
+        acc = ptx::ffma2(kq_min_pair(make_float2(mag(b & 0x00F0u), mag(b & 0xF000u)), shi, m), xh, acc);
     }
 }
 
 template <>
 __device__ __forceinline__ void kq_superblock<kQ2K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
-                                                    uint32_t t, float& a0, float& a1, bool sh) {
+                                                    uint32_t t, float2& acc, bool sh) {
     const uint32_t dd = *reinterpret_cast<const uint32_t*>(blk + 80);
     const float d = h2f(dd & 0xFFFFu), nd = -h2f(dd >> 16);
     float tdsc0 = 0.0f, tdmm0 = 0.0f, tdsc1 = 0.0f, tdmm1 = 0.0f;  // sub-blocks t and t + 8, when shared
@@ -153,16 +176,18 @@ __device__ __forceinline__ void kq_superblock<kQ2K>(const uint8_t* __restrict__ 
             dsc = __fmul_rn(d, (float)(s & 0x0Fu));
             dmm = __fmul_rn(nd, (float)(s >> 4));
         }
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(blk + 16 + 4 * j);
+        // lane 2t's code at bits 0-1 (x 1), lane 2t+1's at bits 2-3 (x 4)
+        const uint32_t ws = *reinterpret_cast<const uint32_t*>(blk + 16 + 4 * j) >> (4 * t);
         const float2 xv = *reinterpret_cast<const float2*>(xb + 16 * j + 2 * t);
-        a0 = kq_min_term(a0, (w >> (4 * t)) & 3u, dsc, dmm, xv.x);
-        a1 = kq_min_term(a1, (w >> (4 * t + 2)) & 3u, dsc, dmm, xv.y);
+        const float2 sp = make_float2(dsc, __fmul_rn(dsc, 0.25f));
+        acc = ptx::ffma2(kq_min_pair(make_float2(mag(ws & 3u), mag(ws & 0xCu)), sp, make_float2(dmm, dmm)), xv,
+                         acc);
     }
 }
 
 template <>
 __device__ __forceinline__ void kq_superblock<kQ3K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
-                                                    uint32_t t, float& a0, float& a1, bool sh) {
+                                                    uint32_t t, float2& acc, bool sh) {
     const uint8_t *hm = blk, *qs = blk + 32, *sc = blk + 96;
     const float d = h2f(ld_u16(blk + 108));
     const uint32_t l0 = 2 * t, l1 = 2 * t + 1;
@@ -171,33 +196,34 @@ __device__ __forceinline__ void kq_superblock<kQ3K>(const uint8_t* __restrict__ 
         return __fmul_rn(d, (float)((int32_t)s6 - 32));
     };
     const float tdsc = sh ? scale_of(t) : 0.0f;
+    // lane 2t's 3-bit code at bits 0-2 (x 1), lane 2t+1's at bits 2-4 (x 4); offset 4
+    const float2 no = make_float2(-(kMagF + 4.0f), -(kMagF + 16.0f));
 #pragma unroll
     for (uint32_t j = 0; j < 8; j++) {
         const float dsc = sh ? row_bcast(tdsc, j) : scale_of(j);
+        const float2 sp = make_float2(dsc, __fmul_rn(dsc, 0.25f));
         const uint32_t w0 = ld_u32_a2(qs + 8 * j), h0 = ld_u16(hm + 4 * j);
         const float2 xl = *reinterpret_cast<const float2*>(xb + 32 * j + 2 * t);
         const float2 xh = *reinterpret_cast<const float2*>(xb + 32 * j + 16 + 2 * t);
-        const uint32_t q00 = ((w0 >> (2 * l0)) & 3u) | (((h0 >> l0) & 1u) << 2);
-        const uint32_t q01 = ((w0 >> (2 * l1)) & 3u) | (((h0 >> l1) & 1u) << 2);
-        a0 = kq_term(a0, (int32_t)q00 - 4, dsc, xl.x);
-        a1 = kq_term(a1, (int32_t)q01 - 4, dsc, xl.y);
+        const uint32_t ws = w0 >> (4 * t);
+        const uint32_t e00 = (ws & 3u) | (((h0 >> l0) & 1u) << 2);
+        const uint32_t e01 = (ws & 0xCu) | (((h0 >> l1) & 1u) << 4);
+        acc = ptx::ffma2(kq_off_pair(make_float2(mag(e00), mag(e01)), no, sp), xl, acc);
         // second half: the stale shift by the first half's x bits, then by 2l
         const uint32_t w1 = ld_u32_a2(qs + 8 * j + 4), h1 = ld_u16(hm + 4 * j + 2);
-        const uint32_t s0 = __float_as_uint(xl.x), s1 = __float_as_uint(xl.y);
-        const uint32_t t0 = s0 >= 32u ? 0u : (w1 >> s0), t1 = s1 >= 32u ? 0u : (w1 >> s1);
-        const uint32_t q10 = ((t0 >> (2 * l0)) & 3u) | (((h1 >> l0) & 1u) << 2);
-        const uint32_t q11 = ((t1 >> (2 * l1)) & 3u) | (((h1 >> l1) & 1u) << 2);
-        a0 = kq_term(a0, (int32_t)q10 - 4, dsc, xh.x);
-        a1 = kq_term(a1, (int32_t)q11 - 4, dsc, xh.y);
+        const uint32_t t0 = ptx::shr_clamp(w1, __float_as_uint(xl.x)) >> (4 * t);
+        const uint32_t t1 = ptx::shr_clamp(w1, __float_as_uint(xl.y)) >> (4 * t);
+        const uint32_t e10 = (t0 & 3u) | (((h1 >> l0) & 1u) << 2);
+        const uint32_t e11 = (t1 & 0xCu) | (((h1 >> l1) & 1u) << 4);
+        acc = ptx::ffma2(kq_off_pair(make_float2(mag(e10), mag(e11)), no, sp), xh, acc);
     }
 }
 
 template <>
 __device__ __forceinline__ void kq_superblock<kQ5K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
-                                                    uint32_t t, float& a0, float& a1, bool sh) {
+                                                    uint32_t t, float2& acc, bool sh) {
     const float d = h2f(ld_u16(blk)), nd = -h2f(ld_u16(blk + 2));
     const uint8_t *qh = blk + 16, *qs = blk + 48;
-    const uint32_t l0 = 2 * t, l1 = 2 * t + 1;
     float tdsc = 0.0f, tdmm = 0.0f;
     if (sh) {
         uint32_t sc, mn;
@@ -221,30 +247,35 @@ __device__ __forceinline__ void kq_superblock<kQ5K>(const uint8_t* __restrict__ 
         const uint32_t b = ld_u16(qs + 16 * j + 2 * t);
         const float2 xl = *reinterpret_cast<const float2*>(xb + 32 * j + 2 * t);
         const float2 xh = *reinterpret_cast<const float2*>(xb + 32 * j + 16 + 2 * t);
-        a0 = kq_min_term(a0, (b & 0x0Fu) | (((h >> l0) & 1u) << 4), dsc, dmm, xl.x);
-        a1 = kq_min_term(a1, ((b >> 8) & 0x0Fu) | (((h >> l1) & 1u) << 4), dsc, dmm, xl.y);
-        a0 = kq_min_term(a0, ((b >> 4) & 0x0Fu) | (((h >> (16 + l0)) & 1u) << 4), dsc, dmm, xh.x);
-        a1 = kq_min_term(a1, ((b >> 12) & 0x0Fu) | (((h >> (16 + l1)) & 1u) << 4), dsc, dmm, xh.y);
+        // the four 5-bit codes as bytes: nibble | high bit << 4, high bits h[2t], h[2t+1],
+        // h[16+2t], h[16+2t+1] moved to bits 4, 12, 20, 28 by one multiply (no carries)
+        const uint32_t hb = (h >> (2 * t)) & 0x00030003u;
+        const uint32_t v = ((b | (b << 12)) & 0x0F0F0F0Fu) | ((hb * 0x810u) & 0x10101010u);
+        const float2 sp = make_float2(dsc, dsc), m = make_float2(dmm, dmm);
+        acc = ptx::ffma2(kq_min_pair(make_float2(mag_byte(v, 0), mag_byte(v, 1)), sp, m), xl, acc);
+        acc = ptx::ffma2(kq_min_pair(make_float2(mag_byte(v, 2), mag_byte(v, 3)), sp, m), xh, acc);
     }
 }
 
 template <>
 __device__ __forceinline__ void kq_superblock<kQ6K>(const uint8_t* __restrict__ blk, const float* __restrict__ xb,
-                                                    uint32_t t, float& a0, float& a1, bool sh) {
+                                                    uint32_t t, float2& acc, bool sh) {
     const uint8_t *ql = blk, *qh = blk + 128;
     const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
     const float d = h2f(ld_u16(blk + 208));
     const float tdsc0 = sh ? __fmul_rn(d, (float)sc[t]) : 0.0f, tdsc1 = sh ? __fmul_rn(d, (float)sc[t + 8]) : 0.0f;
+    // lane 2t's 6-bit code at bits 0-5 (x 1), lane 2t+1's at bits 4-9 (x 16); offset 32
+    const float2 no = make_float2(-(kMagF + 32.0f), -(kMagF + 512.0f));
 #pragma unroll
     for (uint32_t j = 0; j < 16; j++) {
         const float dsc = sh ? row_bcast(j < 8 ? tdsc0 : tdsc1, j & 7) : __fmul_rn(d, (float)sc[j]);
-        const uint32_t h = ld_u32_a2(qh + 4 * j);
-        const uint32_t b = ql[8 * j + t];  // element 2t: low nibble, 2t+1: high nibble
+        const uint32_t hs = ld_u32_a2(qh + 4 * j) >> (4 * t);  // bits 0-1: lane 2t's high bits, 2-3: lane 2t+1's
+        const uint32_t b = ql[8 * j + t];                      // element 2t: low nibble, 2t+1: high nibble
         const float2 xv = *reinterpret_cast<const float2*>(xb + 16 * j + 2 * t);
-        const uint32_t q0 = (b & 0x0Fu) | (((h >> (4 * t)) & 3u) << 4);
-        const uint32_t q1 = (b >> 4) | (((h >> (4 * t + 2)) & 3u) << 4);
-        a0 = kq_term(a0, (int32_t)q0 - 32, dsc, xv.x);
-        a1 = kq_term(a1, (int32_t)q1 - 32, dsc, xv.y);
+        const uint32_t e0 = (b & 0x0Fu) | ((hs << 4) & 0x30u);
+        const uint32_t e1 = (b & 0xF0u) | ((hs << 6) & 0x300u);
+        acc = ptx::ffma2(kq_off_pair(make_float2(mag(e0), mag(e1)), no, make_float2(dsc, __fmul_rn(dsc, 0.0625f))),
+                         xv, acc);
     }
 }
 
@@ -252,14 +283,14 @@ template <int F>
 __global__ void __launch_bounds__(256) kquant_gemv_kernel(const float* __restrict__ x, const uint8_t* __restrict__ W,
                                                           float* __restrict__ out, uint32_t M, uint32_t nsb) {
     const uint32_t row = blockIdx.x * (blockDim.x / 8) + threadIdx.x / 8, t = threadIdx.x % 8;
-    float a0 = 0.0f, a1 = 0.0f;
+    float2 acc = make_float2(0.0f, 0.0f);
     if (row < M) {
         const uint8_t* rp = W + (size_t)row * nsb * KBlock<F>::bytes;
         for (uint32_t b = 0; b < nsb; b++)
-            kq_superblock<F>(rp + (size_t)b * KBlock<F>::bytes, x + 256 * b, t, a0, a1, false);
+            kq_superblock<F>(rp + (size_t)b * KBlock<F>::bytes, x + 256 * b, t, acc, false);
     }
     // FADDV: level 1 in-thread (lanes 2t, 2t+1), levels 2-4 across the row's 8 threads
-    float s = __fadd_rn(a0, a1);
+    float s = __fadd_rn(acc.x, acc.y);
     s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
     s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 2));
     s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 4));
@@ -381,7 +412,7 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
         // the whole warp computes (rows past M read the box's zero fill), so the
         // decoders' width-8 shuffles see all 32 lanes; only the store is per row
         const bool warp_on = gp + cw < g1, active = warp_on && row < M;
-        float a0 = 0.0f, a1 = 0.0f;
+        float2 acc = make_float2(0.0f, 0.0f);
         for (uint32_t c = 0; c < nchunks; c++) {
             const uint32_t t = pass * nchunks + c, slot = t % nslots;
             // one verdict per warp, so no lane is left behind at a shuffle
@@ -396,12 +427,12 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
                     rp += (reinterpret_cast<uintptr_t>(W) + (size_t)row * row_bytes + (size_t)c * CB) & 15;
                 const float* xc = reinterpret_cast<const float*>(st + w_bytes);
                 const uint32_t n = chunk_sbs(c);
-                for (uint32_t k = 0; k < n; k++) kq_superblock<F>(rp + k * BB, xc + 256 * k, t8, a0, a1, true);
+                for (uint32_t k = 0; k < n; k++) kq_superblock<F>(rp + k * BB, xc + 256 * k, t8, acc, true);
             }
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&empty[slot]);
         }
-        float sum = __fadd_rn(a0, a1);
+        float sum = __fadd_rn(acc.x, acc.y);
         sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
         sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
         sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 4));

@@ -94,6 +94,40 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     return d;
 }
 
+// Two IEEE fp32 adds / multiplies (round to nearest even, no flush to zero) in
+// one packed instruction.  A product of fmul2 must not feed an add (the
+// compiler may fuse the pair into one rounding); feeding an fma's multiplicand
+// is fine.
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+// Logical right shift whose amount is clamped to 32 (amounts >= 32 give 0).
+__device__ __forceinline__ uint32_t shr_clamp(uint32_t a, uint32_t s) {
+    uint32_t d;
+    asm("shr.b32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(s));
+    return d;
+}
+
 // max that propagates NaN (IEEE maximum), on magnitudes: the absmax step.
 __device__ __forceinline__ float absmax_nan(float m, float a) {
     float d;
