@@ -444,7 +444,13 @@ template <int F, bool BULK>
 int launch_kquant_stream(uint32_t M, uint32_t nsb, const float* x, const uint8_t* W, float* out, cudaStream_t s) {
     constexpr uint32_t BB = KBlock<F>::bytes, C = KBlock<F>::chunk, CB = C * BB;
     constexpr uint32_t TILE = BULK ? KSeg<F>::tile : (kQ8RowsPerWarp * CB + 127) / 128 * 128;
-    const Q8Plan p = plan_q8_stream(M, nsb * 256, C * 1024, 128, (BB + 7) / 8, TILE);
+    // many rows of short K can ask for more groups per CTA than two ring slots
+    // of 200 KB hold: halve the groups per CTA (more CTAs) until they fit
+    Q8Plan p;
+    for (uint32_t mw = kQ8MaxWarps; mw >= 1; mw /= 2) {
+        p = plan_q8_stream(M, nsb * 256, C * 1024, 128, (BB + 7) / 8, TILE, mw);
+        if (p.smem <= 200 * 1024) break;
+    }
     static std::atomic<uint64_t> smem_set{0};  // devices whose limit is raised
     if (int arc = set_max_dynamic_smem(kquant_stream_kernel<F, BULK>, 200 * 1024, smem_set)) return arc;
     ANE_ARG_CHECK(p.smem <= 200 * 1024, "kquant_gemv: shared-memory plan too large");

@@ -38,9 +38,11 @@ struct Q8Plan {
 // prologue while this grid drains (see the budget below).  ANE_Q8_WARPS /
 // ANE_Q8_SLOTS / ANE_Q8_CPS (CTAs per SM) override the choice (tuning aids).
 // block_bytes / warp_tile_bytes: 34 / 2176 for Q8_0; 18 / 1152 for Q4_0 (same
-// 4 rows x 16 blocks per warp tile).
+// 4 rows x 16 blocks per warp tile).  max_warps: the most 4-row groups one CTA
+// takes per pass.
 inline Q8Plan plan_q8_stream(uint32_t M, uint32_t K, size_t extra_slot_bytes, size_t fixed_bytes,
-                             uint32_t block_bytes = 34, uint32_t warp_tile_bytes = kQ8WarpTileBytes) {
+                             uint32_t block_bytes = 34, uint32_t warp_tile_bytes = kQ8WarpTileBytes,
+                             uint32_t max_warps = kQ8MaxWarps) {
     static const int force_warps = env_int("ANE_Q8_WARPS"), force_slots = env_int("ANE_Q8_SLOTS"),
                      force_cps = env_int("ANE_Q8_CPS");
     const uint32_t sms = (uint32_t)num_sms();
@@ -52,11 +54,11 @@ inline Q8Plan plan_q8_stream(uint32_t M, uint32_t K, size_t extra_slot_bytes, si
     // (finer-grained hand-over between grids) and the whole shared memory for
     // the rings (more bytes in flight per SM).
     const double sm_bytes = (double)M * (K / 32) * block_bytes / sms;
-    uint32_t cps = (per_sm + kQ8MaxWarps - 1) / kQ8MaxWarps;
+    uint32_t cps = (per_sm + max_warps - 1) / max_warps;
     if (sm_bytes > 160.0 * 1024 && cps < 2 && per_sm >= 2) cps = 2;
     if (force_cps > 0) cps = (uint32_t)force_cps;
     if (force_warps > 0) {
-        const uint32_t w = force_warps > (int)kQ8MaxWarps ? kQ8MaxWarps : (uint32_t)force_warps;
+        const uint32_t w = force_warps > (int)max_warps ? max_warps : (uint32_t)force_warps;
         p.ctas = (p.groups + w - 1) / w;
     } else {
         p.ctas = sms * cps;
@@ -64,7 +66,7 @@ inline Q8Plan plan_q8_stream(uint32_t M, uint32_t K, size_t extra_slot_bytes, si
     if (p.ctas > p.groups) p.ctas = p.groups;
     if (p.ctas == 0) p.ctas = 1;
     p.warps = (p.groups + p.ctas - 1) / p.ctas;
-    if (p.warps > kQ8MaxWarps) p.warps = kQ8MaxWarps;  // the CTA then streams several passes
+    if (p.warps > max_warps) p.warps = max_warps;  // the CTA then streams several passes
     p.slot_bytes = (size_t)p.warps * warp_tile_bytes + extra_slot_bytes;
     // With one CTA per SM, the next grid's CTAs fit beside this grid's, one per
     // SM, so they are placed evenly; with more, a reserved spare would be filled

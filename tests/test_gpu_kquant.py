@@ -35,8 +35,10 @@ def _x(K, rng):
 
 
 @pytest.mark.parametrize("fmt", FMTS)
-@pytest.mark.parametrize("M,K", [(1, 256), (37, 512), (4096, 4096), (1000, 11008), (64, 300)])
+@pytest.mark.parametrize("M,K", [(1, 256), (37, 512), (4096, 4096), (1000, 11008), (64, 300), (8192, 512)])
 def test_kquant_gemv_exact(ane, fmt, M, K):
+    """8192 rows of K = 512: more four-row groups per CTA than two ring slots
+    hold, so the plan spreads them over more CTAs."""
     import torch
 
     rng = np.random.default_rng(M * 7 + K + len(fmt))
