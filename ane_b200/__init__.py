@@ -80,6 +80,7 @@ SIGNATURES = {
     "ane_q3_k_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
     "ane_q5_k_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
     "ane_q6_k_gemv_dev": (_i32, [_u32, _u32, _vp, _vp, _vp, _vp]),
+    "ane_kquant_gemv_ex_dev": (_i32, [_u8, _u32, _u32, _vp, _vp, _vp, _u32, _vp]),
     "ane_cblas_igemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
     "ane_cblas_ugemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
     "ane_cblas_usgemm": (_i32, [_u8, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f, _vp, _vp, _vp]),
@@ -448,14 +449,23 @@ def q4_0_gemv(W, x, M: int, K: int, out=None, stream=None, static_weights=False)
 KQUANT_BLOCK_BYTES = {"q2_k": 84, "q3_k": 110, "q4_k": 144, "q5_k": 176, "q6_k": 210}
 
 
-def kquant_gemv(fmt: str, W, x, M: int, K: int, out=None, stream=None):
+KQUANT_OPCODES = {"q4_k": 0x75, "q2_k": 0x76, "q3_k": 0x77, "q5_k": 0x78, "q6_k": 0x79}
+
+
+def kquant_gemv(fmt: str, W, x, M: int, K: int, out=None, stream=None, static_weights=False):
     """out[M] = K-quant matrix W (M rows of K/256 super-blocks of format `fmt`,
-    a key of KQUANT_BLOCK_BYTES; uint8 tensor) times fp32 x[K]."""
+    a key of KQUANT_BLOCK_BYTES; uint8 tensor) times fp32 x[K].
+    static_weights: W is not written by the kernel before this call on the
+    stream, so the matvec may start reading it early (ANE_Q8_WEIGHTS_STATIC)."""
     torch = _torch()
     if fmt not in KQUANT_BLOCK_BYTES:
         raise ValueError("unknown K-quant format %r" % (fmt,))
     if out is None:
         out = torch.empty(M, dtype=torch.float32, device=x.device)
+    if static_weights:
+        check(_lib.ane_kquant_gemv_ex_dev(KQUANT_OPCODES[fmt], M, K, x.data_ptr(), W.data_ptr(), out.data_ptr(),
+                                          WEIGHTS_STATIC, _stream_ptr(stream)))
+        return out
     fn = getattr(_lib, "ane_%s_gemv_dev" % fmt)
     check(fn(M, K, x.data_ptr(), W.data_ptr(), out.data_ptr(), _stream_ptr(stream)))
     return out

@@ -263,10 +263,10 @@ void stack_plan_free(void* plan);
 int launch_get_rows_q8_0(uint32_t n_rows, uint32_t dim, const uint8_t* table, const uint32_t* indices, float* out,
                          cudaStream_t s);
 // K-quant matvecs (kquant_gemv.cu): fmt 0 = q4_k, 1 = q2_k, 2 = q3_k, 3 = q5_k,
-// 4 = q6_k; floor(K / 256) super-blocks per row.
+// 4 = q6_k; floor(K / 256) super-blocks per row; flags: ANE_Q8_WEIGHTS_STATIC.
 uint32_t kquant_block_bytes(uint32_t fmt);
 int launch_kquant_gemv(uint32_t fmt, uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out,
-                       cudaStream_t s);
+                       uint32_t flags, cudaStream_t s);
 int launch_get_rows_q4_0(uint32_t n_rows, uint32_t dim, const uint8_t* table, const uint32_t* idx, float* out,
                          cudaStream_t s);
 int launch_q4_0_gemv(uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out, uint32_t flags,

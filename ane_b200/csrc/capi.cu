@@ -489,26 +489,33 @@ int ane_get_rows_q8_0_dev(uint32_t n_rows, uint32_t dim, const void* table, cons
 }
 
 static int kquant_dev(uint32_t fmt, uint32_t M, uint32_t K, const float* in, const void* W, float* out,
-                      void* stream) {
+                      uint32_t flags, void* stream) {
     ANE_REQUIRE_GPU();
     ANE_ARG_CHECK(M == 0 || (in && W && out), "k-quant gemv: NULL pointer");
-    int rc = launch_kquant_gemv(fmt, M, K, in, static_cast<const uint8_t*>(W), out, static_cast<cudaStream_t>(stream));
+    ANE_ARG_CHECK((flags & ~ANE_Q8_WEIGHTS_STATIC) == 0, "k-quant gemv: unknown flag bits");
+    int rc = launch_kquant_gemv(fmt, M, K, in, static_cast<const uint8_t*>(W), out, flags,
+                                static_cast<cudaStream_t>(stream));
     return rc ? rc : ok();
 }
+int ane_kquant_gemv_ex_dev(uint8_t op, uint32_t M, uint32_t K, const float* in, const void* W, float* out,
+                           uint32_t flags, void* stream) {
+    ANE_ARG_CHECK(op >= 0x75 && op <= 0x79, "k-quant gemv: op must be one of 0x75-0x79");
+    return kquant_dev(op - 0x75u, M, K, in, W, out, flags, stream);
+}
 int ane_q4_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
-    return kquant_dev(0, M, K, in, W, out, stream);
+    return kquant_dev(0, M, K, in, W, out, 0, stream);
 }
 int ane_q2_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
-    return kquant_dev(1, M, K, in, W, out, stream);
+    return kquant_dev(1, M, K, in, W, out, 0, stream);
 }
 int ane_q3_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
-    return kquant_dev(2, M, K, in, W, out, stream);
+    return kquant_dev(2, M, K, in, W, out, 0, stream);
 }
 int ane_q5_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
-    return kquant_dev(3, M, K, in, W, out, stream);
+    return kquant_dev(3, M, K, in, W, out, 0, stream);
 }
 int ane_q6_k_gemv_dev(uint32_t M, uint32_t K, const float* in, const void* W, float* out, void* stream) {
-    return kquant_dev(4, M, K, in, W, out, stream);
+    return kquant_dev(4, M, K, in, W, out, 0, stream);
 }
 
 int ane_get_rows_q4_0_dev(uint32_t n_rows, uint32_t dim, const void* table, const uint32_t* indices, float* out,
@@ -1069,7 +1076,7 @@ static int kquant_host(uint32_t fmt, uint32_t M, uint32_t K, const float* in, co
                              {out, (size_t)M * 4, false, true}};
     return run_staged(args, 0, [&](cudaStream_t s, void*) {
         return launch_kquant_gemv(fmt, M, K, (const float*)args[0].dev, (const uint8_t*)args[1].dev,
-                                  (float*)args[2].dev, s);
+                                  (float*)args[2].dev, 0, s);
     });
 }
 int ane_q4_k_gemv(uint32_t M, uint32_t K, const float* in, const void* W, float* out) {

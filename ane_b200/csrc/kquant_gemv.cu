@@ -317,7 +317,7 @@ template <int F, bool BULK>
 __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
     kquant_stream_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ W,
                          const float* __restrict__ x, float* __restrict__ out, uint32_t M, uint32_t nsb,
-                         uint32_t groups, uint32_t nw, uint32_t nslots, int* err) {
+                         uint32_t groups, uint32_t nw, uint32_t nslots, uint32_t flags, int* err) {
     constexpr uint32_t BB = KBlock<F>::bytes, C = KBlock<F>::chunk, CB = C * BB;
     // one warp's 4 rows: a 128-byte-pitch TMA box, or 4 bulk-copy segments
     constexpr uint32_t TILE = BULK ? KSeg<F>::tile : (kQ8RowsPerWarp * CB + 127) / 128 * 128;
@@ -345,13 +345,20 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
     __syncthreads();
     ptx::griddep_launch_dependents();
 
+    // ANE_Q8_WEIGHTS_STATIC: the first stages' weights are requested before the
+    // previous kernel on the stream has finished (it does not write W); x is
+    // always requested after it has
+    const uint32_t pre = (flags & ANE_Q8_WEIGHTS_STATIC) ? min(nslots, ntiles) : 0;
+    auto issue_x = [&](uint32_t t, uint32_t slot) {
+        const uint32_t c = t % nchunks;
+        ptx::bulk_load(ring + (size_t)slot * slot_bytes + w_bytes, x + (size_t)c * C * 256, chunk_sbs(c) * 1024,
+                       &full[slot]);
+    };
     if (warp == 0 && BULK) {
-        ptx::griddep_wait();  // x (and W) may be written by the previous kernel
-        for (uint32_t t = 0; t < ntiles; t++) {
-            const uint32_t slot = t % nslots, pass = t / nchunks, c = t - pass * nchunks;
-            bool ok = true;
-            if (lane == 0) ok = ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err);
-            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        // stage t's weights: the warp's 32 lanes share the row copies; lane 0
+        // arms the stage with the bytes of the copies and of the x slice
+        auto issue_weights = [&](uint32_t t, uint32_t slot) {
+            const uint32_t pass = t / nchunks, c = t - pass * nchunks;
             const uint32_t gp = g0 + pass * nw, nwp = min(nw, g1 - gp);
             const uint32_t nbytes = chunk_sbs(c) * BB;
             uint8_t* dst = ring + (size_t)slot * slot_bytes;
@@ -378,26 +385,41 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
                     ptx::bulk_load(dst + (i / kQ8RowsPerWarp) * TILE + (i % kQ8RowsPerWarp) * RPITCH,
                                    reinterpret_cast<const void*>(a0), len, &full[slot]);
             }
-            if (lane == 0)
-                ptx::bulk_load(dst + w_bytes, x + (size_t)c * C * 256, chunk_sbs(c) * 1024, &full[slot]);
+        };
+        for (uint32_t t = 0; t < pre; t++) issue_weights(t, t);  // fresh slots: no wait
+        ptx::griddep_wait();  // x (and W, without the flag) may be written by the previous kernel
+        for (uint32_t t = 0; t < pre && lane == 0; t++) issue_x(t, t);
+        for (uint32_t t = pre; t < ntiles; t++) {
+            const uint32_t slot = t % nslots;
+            bool ok = true;
+            if (lane == 0) ok = ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+            issue_weights(t, slot);
+            if (lane == 0) issue_x(t, slot);
         }
         return;
     }
     if (warp == 0) {
         if (lane == 0) {
-            ptx::prefetch_tmap(&wmap);
-            ptx::griddep_wait();  // x may be written by the previous kernel
-            for (uint32_t t = 0; t < ntiles; t++) {
-                const uint32_t slot = t % nslots, pass = t / nchunks, c = t - pass * nchunks;
-                if (!ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err)) break;
+            // full boxes: the part past the row end (a short last chunk) is zero fill
+            auto issue_weights = [&](uint32_t t, uint32_t slot) {
+                const uint32_t pass = t / nchunks, c = t - pass * nchunks;
                 const uint32_t gp = g0 + pass * nw, nwp = min(nw, g1 - gp);
                 uint8_t* dst = ring + (size_t)slot * slot_bytes;
-                // full boxes: the part past the row end (a short last chunk) is zero fill
                 ptx::mbar_arrive_expect_tx(&full[slot], nwp * kQ8RowsPerWarp * CB + chunk_sbs(c) * 1024);
                 for (uint32_t w = 0; w < nwp; w++)
                     ptx::tma_load_2d(dst + w * TILE, &wmap, &full[slot], (int)(c * (CB / KBlock<F>::elem)),
                                      (int)((gp + w) * kQ8RowsPerWarp));
-                ptx::bulk_load(dst + w_bytes, x + (size_t)c * C * 256, chunk_sbs(c) * 1024, &full[slot]);
+            };
+            ptx::prefetch_tmap(&wmap);
+            for (uint32_t t = 0; t < pre; t++) issue_weights(t, t);  // fresh slots: no wait
+            ptx::griddep_wait();  // x (and W, without the flag) may be written by the previous kernel
+            for (uint32_t t = 0; t < pre; t++) issue_x(t, t);
+            for (uint32_t t = pre; t < ntiles; t++) {
+                const uint32_t slot = t % nslots;
+                if (!ptx::mbar_wait(&empty[slot], ((t / nslots) & 1) ^ 1, err)) break;
+                issue_weights(t, slot);
+                issue_x(t, slot);
             }
         }
         return;
@@ -441,7 +463,8 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1), 1)
 }
 
 template <int F, bool BULK>
-int launch_kquant_stream(uint32_t M, uint32_t nsb, const float* x, const uint8_t* W, float* out, cudaStream_t s) {
+int launch_kquant_stream(uint32_t M, uint32_t nsb, const float* x, const uint8_t* W, float* out, uint32_t flags,
+                         cudaStream_t s) {
     constexpr uint32_t BB = KBlock<F>::bytes, C = KBlock<F>::chunk, CB = C * BB;
     constexpr uint32_t TILE = BULK ? KSeg<F>::tile : (kQ8RowsPerWarp * CB + 127) / 128 * 128;
     // many rows of short K can ask for more groups per CTA than two ring slots
@@ -465,23 +488,24 @@ int launch_kquant_stream(uint32_t M, uint32_t nsb, const float* x, const uint8_t
         if (rc) return rc;
     }
     return launch_q8_stream(kquant_stream_kernel<F, BULK>, p, s, wmap, W, x, out, M, nsb, p.groups, p.warps,
-                            p.slots, device_timeout_flag());
+                            p.slots, flags, device_timeout_flag());
 }
 
 template <int F>
-int launch_kquant(uint32_t M, uint32_t nsb, const float* x, const uint8_t* W, float* out, cudaStream_t s) {
+int launch_kquant(uint32_t M, uint32_t nsb, const float* x, const uint8_t* W, float* out, uint32_t flags,
+                  cudaStream_t s) {
     // streamed when a row is a whole number of 16-byte units (the TMA row stride)
     // and W, x are 16-byte aligned (TMA base, bulk copies of x)
     const uint64_t row_bytes = (uint64_t)nsb * KBlock<F>::bytes;
     if (row_bytes % 16 == 0 && ((uintptr_t)W & 15) == 0 && ((uintptr_t)x & 15) == 0)
-        return launch_kquant_stream<F, false>(M, nsb, x, W, out, s);
+        return launch_kquant_stream<F, false>(M, nsb, x, W, out, flags, s);
     // any row length: bulk copies of 16-byte-aligned spans, as long as the last
     // span (up to 15 bytes past the matrix) stays inside W's allocation
     const uint64_t total = (uint64_t)M * row_bytes;
     const uint64_t tail = ((reinterpret_cast<uintptr_t>(W) + total + 15) & ~(uint64_t)15) -
                           reinterpret_cast<uintptr_t>(W);
     if (((uintptr_t)x & 15) == 0 && device_bytes_from(W) >= tail)
-        return launch_kquant_stream<F, true>(M, nsb, x, W, out, s);
+        return launch_kquant_stream<F, true>(M, nsb, x, W, out, flags, s);
     kquant_gemv_kernel<F><<<(M + 31) / 32, 256, 0, s>>>(x, W, out, M, nsb);
     ANE_CHECK_LAUNCH();
     return ANE_OK;
@@ -518,7 +542,7 @@ uint32_t kquant_block_bytes(uint32_t fmt) {
 }
 
 int launch_kquant_gemv(uint32_t fmt, uint32_t M, uint32_t K, const float* x, const uint8_t* W, float* out,
-                       cudaStream_t s) {
+                       uint32_t flags, cudaStream_t s) {
     ANE_ARG_CHECK(fmt <= kQ6K, "kquant_gemv: unknown format");
     if (M == 0) return ANE_OK;
     // float2 loads of x; the widest aligned weight load per format (16-byte
@@ -532,11 +556,11 @@ int launch_kquant_gemv(uint32_t fmt, uint32_t M, uint32_t K, const float* x, con
         return ANE_OK;
     }
     switch (fmt) {
-        case kQ4K: return launch_kquant<kQ4K>(M, nsb, x, W, out, s);
-        case kQ2K: return launch_kquant<kQ2K>(M, nsb, x, W, out, s);
-        case kQ3K: return launch_kquant<kQ3K>(M, nsb, x, W, out, s);
-        case kQ5K: return launch_kquant<kQ5K>(M, nsb, x, W, out, s);
-        default: return launch_kquant<kQ6K>(M, nsb, x, W, out, s);
+        case kQ4K: return launch_kquant<kQ4K>(M, nsb, x, W, out, flags, s);
+        case kQ2K: return launch_kquant<kQ2K>(M, nsb, x, W, out, flags, s);
+        case kQ3K: return launch_kquant<kQ3K>(M, nsb, x, W, out, flags, s);
+        case kQ5K: return launch_kquant<kQ5K>(M, nsb, x, W, out, flags, s);
+        default: return launch_kquant<kQ6K>(M, nsb, x, W, out, flags, s);
     }
 }
 

@@ -403,16 +403,17 @@ def q8_bench(ane, torch, dev, steps=50):
                 for off in {"q2_k": (81, 83), "q3_k": (109,), "q4_k": (1, 3), "q5_k": (1, 3), "q6_k": (209,)}[fmt]:
                     v[:, off] = 0x1C
             itk = [0]
+            for tag, stat in (("", False), ("_static", True)):  # plain, and with the static-weights flag
 
-            def step_k():
-                ane.kquant_gemv(fmt, Wks[itk[0] % kcopies], x, rows, cols, out=y)
-                itk[0] += 1
+                def step_k():
+                    ane.kquant_gemv(fmt, Wks[itk[0] % kcopies], x, rows, cols, out=y, static_weights=stat)
+                    itk[0] += 1
 
-            for _ in range(3):
-                step_k()
-            ms = time_graph(step_k, steps, stream)
-            res[f"{fmt}_us"] = ms * 1e3
-            res[f"{fmt}_gbs"] = (kbytes + 4 * cols + 4 * rows) / (ms * 1e-3) / 1e9
+                for _ in range(3):
+                    step_k()
+                ms = time_graph(step_k, steps, stream)
+                res[f"{fmt}{tag}_us"] = ms * 1e3
+                res[f"{fmt}{tag}_gbs"] = (kbytes + 4 * cols + 4 * rows) / (ms * 1e-3) / 1e9
             del Wks
         # decode at batch 16: ggml MUL_MAT over 16 fp32 activation rows, weights read once
         xb = torch.randn((16, cols), device=dev, generator=g)

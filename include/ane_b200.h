@@ -256,6 +256,13 @@ int ane_q8_0_gemv_ex_dev(uint32_t M, uint32_t K, const float* in, const void* W,
                          uint32_t flags, void* stream);
 int ane_q8_0_gemv_q8_ex_dev(uint32_t M, uint32_t K, const void* xq_blocks, const void* W, float* out,
                             int32_t* block_dots, uint32_t flags, void* stream);
+/* The K-quant matvecs ane_q4_k_gemv_dev .. ane_q6_k_gemv_dev with a flags word
+ * (ANE_Q8_WEIGHTS_STATIC, as above); op selects the format by its reference
+ * opcode: 0x75 q4_k, 0x76 q2_k, 0x77 q3_k, 0x78 q5_k, 0x79 q6_k.  Results are
+ * the same as without the flag.  No counterpart in the reference (its calls
+ * are synchronous). */
+int ane_kquant_gemv_ex_dev(uint8_t op, uint32_t M, uint32_t K, const float* in, const void* W, float* out,
+                           uint32_t flags, void* stream);
 
 /* ggml MUL_MAT with Q8_0 weights W[M rows x K] and NT (1..16) fp32 activation
  * rows x[t * ldx + k] (a decode step over NT tokens): y[t * ldy + m].  The

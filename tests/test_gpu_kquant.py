@@ -92,6 +92,37 @@ def test_kquant_gemv_special_scales(ane, fmt):
 
 
 @pytest.mark.parametrize("fmt", FMTS)
+def test_kquant_gemv_static_weights_chain(ane, fmt):
+    """With the static-weights flag the next matvec streams its weights while
+    the previous one still runs, and reads its activation only after that one
+    has finished: a chain of three square matvecs, each output the next input,
+    equals the plain calls bit for bit (and its first step the oracle)."""
+    import torch
+
+    M = K = 4096
+    rng = np.random.default_rng(17 + len(fmt))
+    Ws = [random_blocks(fmt, M, K, rng) for _ in range(3)]
+    x = _x(K, rng)
+    dWs = [torch.from_numpy(W).cuda() for W in Ws]
+    dx = torch.from_numpy(x).cuda()
+
+    def chain(static):
+        v, outs = dx, []
+        for W in dWs:
+            v = ane.kquant_gemv(fmt, W, v, M, K, static_weights=static)
+            outs.append(v)
+        return [o.cpu().numpy() for o in outs]
+
+    plain, static = chain(False), chain(True)
+    for a, b in zip(plain, static):
+        _same_bits(b, a)
+    _same_bits(static[0], oracle.kquant_gemv(fmt, Ws[0], x, M, K))
+    with pytest.raises(ane.AneError):
+        ane.check(ane.lib.ane_kquant_gemv_ex_dev(0x74, M, K, dx.data_ptr(), dWs[0].data_ptr(),
+                                                 dx.data_ptr(), 1, None))
+
+
+@pytest.mark.parametrize("fmt", FMTS)
 def test_kquant_gemv_host_and_stream_exec(ane, fmt):
     """Host buffers through ane_<fmt>_gemv and through a stream_exec byte stream."""
     from ane_b200 import Op, Ptr, U32, dispatch
