@@ -92,23 +92,25 @@ def test_kquant_gemv_special_scales(ane, fmt):
 
 
 @pytest.mark.parametrize("fmt", FMTS)
-def test_kquant_gemv_static_weights_chain(ane, fmt):
+@pytest.mark.parametrize("shapes", [((4096, 4096),) * 3, ((11008, 4096), (4096, 11008))], ids=["square", "ffn"])
+def test_kquant_gemv_static_weights_chain(ane, fmt, shapes):
     """With the static-weights flag the next matvec streams its weights while
     the previous one still runs, and reads its activation only after that one
-    has finished: a chain of three square matvecs, each output the next input,
-    equals the plain calls bit for bit (and its first step the oracle)."""
+    has finished: a chain of matvecs, each output the next input, equals the
+    plain calls bit for bit (and its first step the oracle).  The 7B FFN pair
+    (11008 x 4096, then 4096 x 11008) also runs the bulk-copy producer, whose
+    rows of 43 super-blocks of 84 / 110 / 210 bytes are not 16-byte multiples."""
     import torch
 
-    M = K = 4096
-    rng = np.random.default_rng(17 + len(fmt))
-    Ws = [random_blocks(fmt, M, K, rng) for _ in range(3)]
-    x = _x(K, rng)
+    rng = np.random.default_rng(17 + len(fmt) + len(shapes))
+    Ws = [random_blocks(fmt, M, K, rng) for M, K in shapes]
+    x = _x(shapes[0][1], rng)
     dWs = [torch.from_numpy(W).cuda() for W in Ws]
     dx = torch.from_numpy(x).cuda()
 
     def chain(static):
         v, outs = dx, []
-        for W in dWs:
+        for W, (M, K) in zip(dWs, shapes):
             v = ane.kquant_gemv(fmt, W, v, M, K, static_weights=static)
             outs.append(v)
         return [o.cpu().numpy() for o in outs]
@@ -116,9 +118,10 @@ def test_kquant_gemv_static_weights_chain(ane, fmt):
     plain, static = chain(False), chain(True)
     for a, b in zip(plain, static):
         _same_bits(b, a)
-    _same_bits(static[0], oracle.kquant_gemv(fmt, Ws[0], x, M, K))
+    M0, K0 = shapes[0]
+    _same_bits(static[0], oracle.kquant_gemv(fmt, Ws[0], x, M0, K0))
     with pytest.raises(ane.AneError):
-        ane.check(ane.lib.ane_kquant_gemv_ex_dev(0x74, M, K, dx.data_ptr(), dWs[0].data_ptr(),
+        ane.check(ane.lib.ane_kquant_gemv_ex_dev(0x74, M0, K0, dx.data_ptr(), dWs[0].data_ptr(),
                                                  dx.data_ptr(), 1, None))
 
 
