@@ -252,9 +252,16 @@ __global__ void __launch_bounds__(32 * (kQ8MaxWarps + 1)) q8_0_gemv_q8_kernel(co
     } else {
         alive = __all_sync(0xffffffffu, ptx::mbar_wait(xbar, 0, err));  // one verdict per warp
     }
-    if (alive && XF32) {  // quantize: one thread per 32-element block
-        for (uint32_t b = cw * 32 + lane; b < nb; b += nw * 32)
-            q8_quantize_block<false>(reinterpret_cast<const float*>(xraw) + (size_t)b * 32, xs, xd, b);
+    if (alive && XF32) {
+        // quantize: 4 lanes per 32-element block (8 blocks per warp step), a
+        // quarter of the dependent chain per lane and no 32-value array in
+        // registers (the kernel then fits 32 registers, so two CTAs of up to
+        // 24 warps share an SM)
+        for (uint32_t b0 = cw * 8; b0 < nb; b0 += nw * 8) {
+            const uint32_t b = b0 + (lane >> 2), bb = b < nb ? b : nb - 1;
+            q8_quantize_quarter(reinterpret_cast<const float*>(xraw) + (size_t)bb * 32 + (lane & 3) * 8, xs, xd, bb,
+                                lane & 3, b < nb);
+        }
     } else if (alive) {  // activation blocks -> aligned codes + fp32 scales (compute warps only)
         for (uint32_t i = cw * 32 + lane; i < nb * 8; i += nw * 32) {
             const unsigned short* src = reinterpret_cast<const unsigned short*>(xraw + (i >> 3) * 34 + 2 + (i & 7) * 4);

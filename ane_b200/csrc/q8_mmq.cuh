@@ -61,6 +61,50 @@ __device__ __forceinline__ void q8_quantize_block(const float* xb, int8_t* xs, f
     q8_quantize_regs(v, xs, xd, b);
 }
 
+// One block quantized by 4 lanes (lanes 4k .. 4k+3 of a warp, quarter i = lane
+// & 3 holding elements 8i .. 8i+7): the same operations as q8_quantize_words,
+// with the absmax fold split into 4 in-order segments.  The fold
+// acc = acc > a ? acc : a (a = |x|) restarts at a NaN (NaN > a and a > NaN are
+// false), so a segment holding a NaN yields its own fold from 0 whatever came
+// before, and any other segment yields the fold step applied to (acc, its own
+// maximum); combining the 4 segment results in order that way gives the
+// sequential 32-element fold bit for bit.  All 32 lanes of the warp call
+// together (width-4 shuffles); store = false lanes compute but write nothing.
+__device__ __forceinline__ void q8_quantize_quarter(const float* xq8, int8_t* xs, float* xd, uint32_t b,
+                                                    uint32_t i, bool store) {
+    const float4 t0 = reinterpret_cast<const float4*>(xq8)[0], t1 = reinterpret_cast<const float4*>(xq8)[1];
+    const float v[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+    float r = 0.0f;
+    bool nan = false;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float a = fabsf(v[j]);
+        nan |= a != a;
+        r = r > a ? r : a;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float rk = __shfl_sync(0xffffffffu, r, k, 4);
+        const bool nk = __shfl_sync(0xffffffffu, (int)nan, k, 4) != 0;
+        amax = nk ? rk : (amax > rk ? amax : rk);
+    }
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t w[2];
+#pragma unroll
+    for (int j = 0; j < 8; j += 4) {
+        uint32_t x = 0;
+#pragma unroll
+        for (int q = 0; q < 4; q++) x |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[j + q], id)) << (8 * q);
+        w[j / 4] = x;
+    }
+    if (store) {
+        reinterpret_cast<uint2*>(xs + (size_t)b * 32)[i] = make_uint2(w[0], w[1]);
+        if (i == 0) xd[b] = __half2float(__float2half_rn(d));
+    }
+}
+
 // Block pair (b, b+1) of one weight row against the activation: pw = the 68
 // bytes of the pair (4-byte aligned: the even block's codes straddle words 0..8,
 // the odd block's codes are words 9..16).  Adds the two terms to `sum` in block
