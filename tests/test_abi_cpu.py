@@ -119,6 +119,13 @@ def test_no_gpu_means_loud_failure():
         fn = getattr(ane_b200.lib, "ane_%s_gemv" % fmt)
         assert fn(1, 256, xk.ctypes.data, W.ctypes.data, out.ctypes.data) == 5, fmt
         assert out[0] == 7.0
+    # the flags entry: an opcode outside 0x75-0x79 is an argument error before
+    # any device work; a valid one fails loudly without a GPU
+    ex = ane_b200.lib.ane_kquant_gemv_ex_dev
+    assert ex(0x74, 1, 256, xk.ctypes.data, W.ctypes.data, out.ctypes.data, 1, None) == 1
+    assert ex(0x7A, 1, 256, xk.ctypes.data, W.ctypes.data, out.ctypes.data, 1, None) == 1
+    assert ex(0x79, 1, 256, xk.ctypes.data, W.ctypes.data, out.ctypes.data, 1, None) == 5
+    assert out[0] == 7.0
     idx = np.zeros(1, np.uint32)
     rows = np.full(32, 7.0, np.float32)
     assert ane_b200.lib.ane_get_rows_q4_0(1, 32, W.ctypes.data, idx.ctypes.data, rows.ctypes.data) == 5
